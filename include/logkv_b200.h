@@ -1,0 +1,124 @@
+/*
+ * C ABI of the B200-native SemanticLogKV flush-and-attend path.
+ *
+ * Plain pointers and sizes only.  Every device pointer is caller-owned CUDA
+ * memory laid out exactly like the corresponding buffer of the reference's
+ * LogStructuredKVCache (litgpt/log_kv_cache.py:907-1122): contiguous,
+ * row-major, same shapes and dtypes.  All work is enqueued on the stream the
+ * caller passes (a cudaStream_t as void*; NULL = legacy default stream); no
+ * call allocates device memory, synchronizes, or reads device data back,
+ * except the explicitly named *_read_status helper.  Scratch comes from a
+ * caller-provided workspace sized by the matching *_workspace_bytes call.
+ *
+ * Return value: 0 on success, a negative LOGKV_E* code for invalid
+ * arguments (nothing is launched then), or a CUDA error code > 0 when a
+ * launch fails.
+ */
+#ifndef LOGKV_B200_H
+#define LOGKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LOGKV_API __attribute__((visibility("default")))
+#else
+#define LOGKV_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LOGKV_OK 0
+#define LOGKV_E_SHAPE (-1)      /* a size is out of the supported range      */
+#define LOGKV_E_DTYPE (-2)      /* unsupported storage dtype code            */
+#define LOGKV_E_WORKSPACE (-3)  /* workspace missing or too small            */
+#define LOGKV_E_POINTER (-4)    /* a required pointer is NULL or misaligned  */
+#define LOGKV_E_SMEM (-5)       /* the shape needs more shared memory        */
+
+#define LOGKV_DTYPE_F32 0
+#define LOGKV_DTYPE_BF16 1
+
+/* Static geometry of one layer's cache (LogStructuredKVCache.__init__, log_kv_cache.py:681-1133). */
+typedef struct logkv_layout {
+  int32_t batch;           /* B  : batch rows                                  */
+  int32_t groups;          /* G  : KV groups (n_query_groups)                  */
+  int32_t dim;             /* D  : head dim of K (pre-RoPE) and V              */
+  int32_t clusters;        /* K  : cluster_k_max (<= 32)                       */
+  int32_t levels;          /* L  : L_alloc                                     */
+  int32_t slots;           /* B' : B_prime, slots per level                    */
+  int32_t recent_capacity; /* 2 * recent_size                                  */
+  int32_t exact;           /* P  : alpha_exact_tokens (> 0)                    */
+  int32_t span_cap;        /* alpha_span_max_tokens                            */
+  int32_t beta;            /* beta_novelty and beta_adaptive_merge (both on)   */
+  int32_t dtype;           /* LOGKV_DTYPE_*: storage dtype of K/V buffers      */
+  float eta;               /* seg_eta                                          */
+  float g0;                /* seg_g0                                           */
+  float lam;               /* cluster_lambda_rel                               */
+} logkv_layout_t;
+
+/*
+ * Device state of one layer.  The first block are the reference's
+ * named_buffers (log_kv_cache.py:907-1122); the alpha_span_* block is the
+ * device form of the host lists _alpha_spans / _alpha_positions / alpha_count
+ * (log_kv_cache.py:925-941), which this implementation keeps on the device so
+ * a flush never waits for the host.
+ */
+typedef struct logkv_state {
+  void* level_k;            /* [B,G,K,L,B',D] dtype */
+  void* level_v;            /* [B,G,K,L,B',D] dtype */
+  float* level_w;           /* [B,G,K,L,B']         */
+  int64_t* level_p_lo;      /* [B,G,K,L,B']         */
+  int64_t* level_p_hi;
+  int64_t* level_sum_wp;
+  int64_t* level_order;
+  uint8_t* pad_mask;        /* bool                 */
+  int16_t* level_count;     /* [B,G,K,L]            */
+  float* centroid;          /* [B,G,K,D]            */
+  float* n_eff;             /* [B,G,K]              */
+  int32_t* n_total;         /* [B,G,K]              */
+  int64_t* p_hi_c;          /* [B,G,K]              */
+  int32_t* level0_phase;    /* [B,G,K]              */
+  uint8_t* alive;           /* [B,G,K] bool         */
+  float* s_h;               /* [B,G]                */
+  void* recent_k;           /* [B,G,2R,D] dtype (post-RoPE)  */
+  void* recent_k_raw;       /* [B,G,2R,D] dtype (pre-RoPE)   */
+  void* recent_v;           /* [B,G,2R,D] dtype              */
+  int64_t* recent_pos;      /* [B,2R]                        */
+  uint8_t* recent_ends;     /* [B,2R] span-end flags (host list _recent_span_ends) */
+  void* alpha_k_raw;        /* [B,G,P,D] dtype      */
+  void* alpha_v;            /* [B,G,P,D] dtype      */
+  int64_t* alpha_pos;       /* [B,P]                */
+  uint8_t* alpha_valid;     /* [B,P] bool           */
+  int32_t* alpha_span_len;  /* [B,P] lengths of the pool's spans, pool order */
+  uint8_t* alpha_span_closed; /* [B,P]              */
+  int32_t* alpha_nspans;    /* [B]                  */
+  int32_t* alpha_rowcount;  /* [B] kept tokens per row                       */
+  int32_t* alpha_count;     /* [1] max over rows (the reference's alpha_count) */
+} logkv_state_t;
+
+/* Bytes of scratch one logkv_flush call needs for this layout and flush size. */
+LOGKV_API size_t logkv_flush_workspace_bytes(const logkv_layout_t* layout, int32_t flush_tokens);
+
+/*
+ * One flush of the `flush_tokens` oldest window tokens of every batch row, then
+ * the window shift.  Replaces LogStructuredKVCache._route_and_flush_batch for
+ * the Alpha + attach route (log_kv_cache.py:5033-5128 -> _alpha_route_flush
+ * :3903-4003) followed by the window shift of _semantic_flush_tokens
+ * (:5640-5661): Alpha span cut/score/greedy choice and pool rewrite, attach
+ * decisions with farthest-point seeding, new clusters, ordinary and delayed
+ * joins, the per-cluster ladder append with pairwise or Beta merges, and the
+ * ordered centroid update.  `recent_count` is the window fill before the flush.
+ */
+LOGKV_API int logkv_flush(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                          int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Copy the workspace status word to *out (synchronizes `stream`); nonzero = a capacity was exceeded. */
+LOGKV_API int logkv_read_status(const void* workspace, int32_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LOGKV_B200_H */

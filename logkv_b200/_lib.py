@@ -1,0 +1,79 @@
+"""ctypes binding of the in-tree C-ABI library ``liblogkv_b200.so``.
+
+The library is the product: there is no CPU or PyTorch fallback.  Loading
+fails loudly when the shared object is missing (build it with
+``python -m logkv_b200.build``) and every call's return code is checked.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liblogkv_b200.so")
+
+ERRORS = {-1: "shape out of the supported range", -2: "unsupported storage dtype",
+          -3: "workspace missing or too small", -4: "null or misaligned pointer",
+          -5: "shape needs more shared memory than one SM has"}
+
+DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1}
+
+
+class Layout(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int32), ("groups", ctypes.c_int32), ("dim", ctypes.c_int32),
+                ("clusters", ctypes.c_int32), ("levels", ctypes.c_int32), ("slots", ctypes.c_int32),
+                ("recent_capacity", ctypes.c_int32), ("exact", ctypes.c_int32), ("span_cap", ctypes.c_int32),
+                ("beta", ctypes.c_int32), ("dtype", ctypes.c_int32), ("eta", ctypes.c_float),
+                ("g0", ctypes.c_float), ("lam", ctypes.c_float)]
+
+
+STATE_FIELDS = ["level_k", "level_v", "level_w", "level_p_lo", "level_p_hi", "level_sum_wp", "level_order",
+                "pad_mask", "level_count", "centroid", "n_eff", "n_total", "p_hi_c", "level0_phase", "alive",
+                "s_h", "recent_k", "recent_k_raw", "recent_v", "recent_pos", "recent_ends", "alpha_k_raw",
+                "alpha_v", "alpha_pos", "alpha_valid", "alpha_span_len", "alpha_span_closed", "alpha_nspans",
+                "alpha_rowcount", "alpha_count"]
+
+
+class State(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_void_p) for name in STATE_FIELDS]
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load the library once; raise if it was not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"logkv_b200 CUDA library missing at {LIB_PATH}; run `python -m logkv_b200.build`")
+        handle = ctypes.CDLL(LIB_PATH)
+        handle.logkv_flush_workspace_bytes.restype = ctypes.c_size_t
+        handle.logkv_flush_workspace_bytes.argtypes = [ctypes.POINTER(Layout), ctypes.c_int32]
+        handle.logkv_flush.restype = ctypes.c_int
+        handle.logkv_flush.argtypes = [ctypes.POINTER(Layout), ctypes.POINTER(State), ctypes.c_int32,
+                                       ctypes.c_int32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+        handle.logkv_read_status.restype = ctypes.c_int
+        handle.logkv_read_status.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), ctypes.c_void_p]
+        _lib = handle
+    return _lib
+
+
+def check(code: int, what: str) -> None:
+    if code != 0:
+        reason = ERRORS.get(code, f"CUDA error {code}")
+        raise RuntimeError(f"{what} failed: {reason}")
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t: torch.Tensor) -> int:
+    if not t.is_cuda:
+        raise ValueError("logkv_b200 kernels need CUDA tensors")
+    if not t.is_contiguous():
+        raise ValueError("logkv_b200 kernels need contiguous tensors")
+    return t.data_ptr()

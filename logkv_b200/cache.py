@@ -1,0 +1,345 @@
+"""B200 LogStructuredKVCache for the in-scope SemanticLogKV configuration.
+
+Drop-in for the reference's ``LogStructuredKVCache`` (litgpt/log_kv_cache.py:640)
+when it runs the default flush-and-attend route: semantic clusters with
+K > 1, mid anchors, attach routing, the Alpha exact-span pool with or without
+Beta, first-order entries.  The constructor takes the reference's keyword
+arguments, registers the same buffers (same names, shapes, dtypes and
+layout, so ``named_buffers()`` compares one-to-one), and ``add_recent`` keeps
+the reference's window/flush contract (:5668-5718, :5609-5666).  Every flush
+runs on the device through ``logkv_flush`` of the C-ABI library without a
+host synchronization; the reference's host mirrors (``_semantic_counts``,
+``_alpha_spans`` ...) are materialized from the device on attribute access.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import torch
+import torch.nn as nn
+
+from . import _lib
+
+UNSUPPORTED = "logkv_b200 implements the attach + Alpha (+ Beta) mid-anchor flush path only"
+
+
+def ladder_geometry(max_seq_length: int, k_dim: int, v_dim: int, n_groups: int, B: int, clusters: int,
+                    exact: int, element_size: int) -> tuple[int, int]:
+    """(B', L): slots per level after paying for the exact pool, and the level count.
+
+    Same byte budget as the reference constructor (log_kv_cache.py:855-899):
+    the largest B' < B whose ladder plus the exact pool fits in the ladder of B.
+    """
+    levels = max(2, math.ceil(math.log2(max_seq_length / max(clusters * B, 1) + 1.0)) + 2)
+    if not exact:
+        return B, levels
+    packed_dim = ((max(k_dim + 1, v_dim) + 7) // 8) * 8
+    entry = (k_dim + v_dim + 2 * packed_dim) * element_size + 41
+    exact_bytes = exact * (n_groups * (k_dim + v_dim + 2 * packed_dim) * element_size + 9)
+    baseline = n_groups * clusters * levels * (B * entry + 2)
+    for cand in range(B - 1, 1, -1):
+        lv = max(2, math.ceil(math.log2(max_seq_length / (clusters * cand) + 1.0)) + 2)
+        if n_groups * clusters * lv * (cand * entry + 2) + exact_bytes <= baseline:
+            return cand, lv
+    raise ValueError("compressed ladder budget is too small for alpha_exact_tokens; increase B or reduce exact capacity")
+
+
+class LogStructuredKVCache(nn.Module):
+    def __init__(self, k_shape, v_shape, B: int = 512, recent_size: int = 0, device=None, dtype=None, *,
+                 semantic_clusters: bool = True, cluster_k_max: int = 12, cluster_lambda_rel: float = 1.0,
+                 seg_eta: float = 1.0, seg_g0: float = 2048.0, seg_gap_max=None, seg_block_level: int = 0,
+                 seg_forget: float = 0.5, semantic_s_h=None, semantic_flush_granularity: int = 2,
+                 semantic_cluster_chunk_size: int = 0, semantic_capacity_beta: float = 0.0,
+                 semantic_capacity_hard_cap_mult: float = 0.0, semantic_legacy_route: bool = False,
+                 semantic_unified_route: bool = False, semantic_merge_passes: int = 1,
+                 semantic_anchor_mode: str = "mid", semantic_pack_backend: str = "auto",
+                 semantic_centroid_backend: str = "sequential", semantic_replay_updates: bool = False,
+                 cos_cache=None, sin_cache=None, rope_n_elem=None, allocate_second_order: bool = False,
+                 alpha_exact_tokens: int = 256, alpha_span_max_tokens: int = 64, beta_novelty: bool = False,
+                 beta_adaptive_merge: bool = False, importance_pooling: bool = False, **unused) -> None:
+        super().__init__()
+        batch, groups, max_seq, k_dim = k_shape
+        v_dim = v_shape[3]
+        device = torch.device(device) if device is not None else torch.device("cuda")
+        dtype = dtype or torch.float32
+        if dtype not in _lib.DTYPE_CODES:
+            raise ValueError(f"storage dtype {dtype} is not supported (float32 or bfloat16)")
+        if not semantic_clusters or semantic_anchor_mode != "mid" or allocate_second_order:
+            raise NotImplementedError(UNSUPPORTED)
+        if semantic_unified_route or semantic_legacy_route or semantic_cluster_chunk_size:
+            raise NotImplementedError(UNSUPPORTED + " (attach route)")
+        if semantic_capacity_hard_cap_mult or semantic_capacity_beta or importance_pooling:
+            raise NotImplementedError(UNSUPPORTED + " (no capacity terms)")
+        if (seg_gap_max is not None and math.isfinite(seg_gap_max)) or seg_block_level:
+            raise ValueError("AlphaLogKV requires disabled segment gaps/padding for delayed archival")
+        if beta_novelty != beta_adaptive_merge:
+            raise NotImplementedError(UNSUPPORTED + " (Beta novelty and 4->2 merge together)")
+        if not alpha_exact_tokens:
+            raise NotImplementedError(UNSUPPORTED + " (alpha_exact_tokens > 0)")
+        if cluster_k_max <= 1 or cluster_k_max > 32:
+            raise ValueError("cluster_k_max must be in [2, 32]")
+        if k_dim != v_dim:
+            raise NotImplementedError(UNSUPPORTED + " (k_dim == v_dim)")
+        if not 1 <= alpha_span_max_tokens <= alpha_exact_tokens:
+            raise ValueError("alpha_span_max_tokens must be in [1, alpha_exact_tokens]")
+        if cos_cache is None or sin_cache is None or rope_n_elem is None:
+            raise ValueError("semantic LogKV requires cos_cache, sin_cache, and rope_n_elem")
+        if semantic_centroid_backend not in ("sequential", "parallel"):
+            raise ValueError("semantic_centroid_backend must be sequential or parallel")
+        self.recent_size = recent_size if recent_size > 0 else 2
+        if not 1 <= semantic_flush_granularity <= self.recent_size:
+            raise ValueError("semantic_flush_granularity must be in [1, recent_size]")
+        if not (math.isfinite(cluster_lambda_rel) and cluster_lambda_rel > 0):
+            raise ValueError("cluster_lambda_rel must be finite and > 0")
+        if not (math.isfinite(seg_g0) and seg_g0 > 0):
+            raise ValueError("seg_g0 must be finite and > 0")
+        self.batch_size, self.n_groups, self.max_seq_length = batch, groups, max_seq
+        self.k_dim, self.v_dim, self.B = k_dim, v_dim, B
+        self.semantic_clusters = True
+        self.semantic_anchor_mode = "mid"
+        self.semantic_pack_backend = semantic_pack_backend
+        self.semantic_centroid_backend = semantic_centroid_backend
+        self.semantic_replay_updates = bool(semantic_replay_updates)
+        self.K_max = int(cluster_k_max)
+        self.cluster_lambda_rel, self.seg_eta, self.seg_g0 = float(cluster_lambda_rel), float(seg_eta), float(seg_g0)
+        self.seg_forget = float(seg_forget)
+        self.semantic_flush_granularity = int(semantic_flush_granularity)
+        self.alpha_exact_tokens, self.alpha_span_max_tokens = int(alpha_exact_tokens), int(alpha_span_max_tokens)
+        self.beta_novelty, self.beta_adaptive_merge = bool(beta_novelty), bool(beta_adaptive_merge)
+        self.rope_n_elem = int(rope_n_elem)
+        self.allocate_second_order = False
+        esize = torch.empty((), dtype=dtype).element_size()
+        self.B_prime, self.L_alloc = ladder_geometry(max_seq, k_dim, v_dim, groups, B, self.K_max,
+                                                     self.alpha_exact_tokens, esize)
+        self.max_levels = self.L_alloc
+        self.B = self.B_prime
+        self.recent_capacity = 2 * self.recent_size
+        self.slot_k_dim = int(cos_cache.size(1)) + k_dim - self.rope_n_elem
+        self.token_count = 0
+        self.recent_count = 0
+        P, R, K, L, Bs = self.alpha_exact_tokens, self.recent_capacity, self.K_max, self.L_alloc, self.B_prime
+        z = dict(device=device)
+        reg = lambda name, t: self.register_buffer(name, t, persistent=False)  # noqa: E731
+        reg("cos_cache", cos_cache.to(device=device))
+        reg("sin_cache", sin_cache.to(device=device))
+        reg("recent_k", torch.zeros(batch, groups, R, self.slot_k_dim, dtype=dtype, **z))
+        reg("recent_v", torch.zeros(batch, groups, R, v_dim, dtype=dtype, **z))
+        reg("recent_k_raw", torch.zeros(batch, groups, R, k_dim, dtype=dtype, **z))
+        reg("recent_pos", torch.zeros(batch, R, dtype=torch.int64, **z))
+        reg("alpha_k_raw", torch.zeros(batch, groups, P, k_dim, dtype=dtype, **z))
+        reg("alpha_v", torch.zeros(batch, groups, P, v_dim, dtype=dtype, **z))
+        reg("alpha_pos", torch.zeros(batch, P, dtype=torch.int64, **z))
+        reg("alpha_valid", torch.zeros(batch, P, dtype=torch.bool, **z))
+        shape = (batch, groups, K, L, Bs)
+        reg("level_k", torch.zeros(*shape, k_dim, dtype=dtype, **z))
+        reg("level_v", torch.zeros(*shape, v_dim, dtype=dtype, **z))
+        reg("level_w", torch.zeros(*shape, dtype=torch.float32, **z))
+        reg("level_imp", torch.zeros(*shape, dtype=torch.float32, **z))
+        for name in ("level_sigma_u", "level_sigma2", "level_gamma_a", "level_gamma_b", "level_gamma"):
+            reg(name, None)
+        reg("level_count", torch.zeros(batch, groups, K, L, dtype=torch.int16, **z))
+        reg("pad_mask", torch.zeros(*shape, dtype=torch.bool, **z))
+        i64max = torch.iinfo(torch.int64).max
+        reg("level_p_lo", torch.full(shape, i64max, dtype=torch.int64, **z))
+        reg("level_p_hi", torch.full(shape, -1, dtype=torch.int64, **z))
+        reg("level_sum_wp", torch.zeros(shape, dtype=torch.int64, **z))
+        reg("level_order", torch.zeros(shape, dtype=torch.int64, **z))
+        reg("centroid", torch.zeros(batch, groups, K, k_dim, dtype=torch.float32, **z))
+        reg("n_eff", torch.zeros(batch, groups, K, dtype=torch.float32, **z))
+        reg("n_total", torch.zeros(batch, groups, K, dtype=torch.int32, **z))
+        reg("p_hi_c", torch.full((batch, groups, K), -1, dtype=torch.int64, **z))
+        reg("current_segment", torch.zeros(batch, groups, K, dtype=torch.int32, **z))
+        reg("level0_phase", torch.zeros(batch, groups, K, dtype=torch.int32, **z))
+        reg("alive", torch.zeros(batch, groups, K, dtype=torch.bool, **z))
+        reg("ward_cost", torch.full((batch, groups, K, K), float("inf"), dtype=torch.float32, **z))
+        if semantic_s_h is None:
+            s_h = torch.ones(batch, groups, dtype=torch.float32, **z)
+        elif isinstance(semantic_s_h, torch.Tensor):
+            s_h = semantic_s_h.to(device=device, dtype=torch.float32)
+            if s_h.shape == (groups,):
+                s_h = s_h.unsqueeze(0).expand(batch, -1).contiguous()
+            elif s_h.shape != (batch, groups):
+                raise ValueError(f"semantic_s_h must have shape ({groups},) or ({batch},{groups})")
+        else:
+            s_h = torch.full((batch, groups), float(semantic_s_h), dtype=torch.float32, **z)
+        if not bool(torch.isfinite(s_h).all()) or not bool((s_h > 0).all()):
+            raise ValueError("semantic_s_h must be finite and > 0")
+        reg("s_h", s_h)
+        # Device form of the reference's host-side pool lists (not registered buffers).
+        self._recent_ends = torch.zeros(batch, R, dtype=torch.uint8, **z)
+        self._span_len = torch.zeros(batch, P, dtype=torch.int32, **z)
+        self._span_closed = torch.zeros(batch, P, dtype=torch.uint8, **z)
+        self._span_count = torch.zeros(batch, dtype=torch.int32, **z)
+        self._row_count = torch.zeros(batch, dtype=torch.int32, **z)
+        self._alpha_count_dev = torch.zeros(1, dtype=torch.int32, **z)
+        self._recent_pos_host = [[0] * R for _ in range(batch)]
+        self._recent_span_ends = [[False] * R for _ in range(batch)]
+        self.op_log = None
+        self.op_log_len = None
+        self._layout = _lib.Layout(batch, groups, k_dim, K, L, Bs, R, P, self.alpha_span_max_tokens,
+                                   int(self.beta_adaptive_merge), _lib.DTYPE_CODES[dtype], self.seg_eta,
+                                   self.seg_g0, self.cluster_lambda_rel)
+        nbytes = _lib.lib().logkv_flush_workspace_bytes(ctypes.byref(self._layout), self.semantic_flush_granularity)
+        if not nbytes:
+            raise ValueError("cache geometry is outside the supported range of the flush kernels")
+        self._workspace = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        self._state = None
+
+    # ------------------------------------------------------------------ C-ABI state
+    def _state_struct(self) -> _lib.State:
+        views = dict(level_k=self.level_k, level_v=self.level_v, level_w=self.level_w,
+                     level_p_lo=self.level_p_lo, level_p_hi=self.level_p_hi, level_sum_wp=self.level_sum_wp,
+                     level_order=self.level_order, pad_mask=self.pad_mask, level_count=self.level_count,
+                     centroid=self.centroid, n_eff=self.n_eff, n_total=self.n_total, p_hi_c=self.p_hi_c,
+                     level0_phase=self.level0_phase, alive=self.alive, s_h=self.s_h, recent_k=self.recent_k,
+                     recent_k_raw=self.recent_k_raw, recent_v=self.recent_v, recent_pos=self.recent_pos,
+                     recent_ends=self._recent_ends, alpha_k_raw=self.alpha_k_raw, alpha_v=self.alpha_v,
+                     alpha_pos=self.alpha_pos, alpha_valid=self.alpha_valid, alpha_span_len=self._span_len,
+                     alpha_span_closed=self._span_closed, alpha_nspans=self._span_count,
+                     alpha_rowcount=self._row_count, alpha_count=self._alpha_count_dev)
+        return _lib.State(**{name: _lib.ptr(t) for name, t in views.items()})
+
+    def flush_device(self, take: int) -> None:
+        """One device flush of the ``take`` oldest window tokens plus the window shift."""
+        state = self._state_struct()
+        code = _lib.lib().logkv_flush(ctypes.byref(self._layout), ctypes.byref(state), int(take),
+                                      int(self.recent_count), ctypes.c_void_p(self._workspace.data_ptr()),
+                                      self._workspace.numel(), ctypes.c_void_p(_lib.stream_ptr(self.level_k.device)))
+        _lib.check(code, "logkv_flush")
+
+    def read_status(self) -> int:
+        out = ctypes.c_int32(0)
+        _lib.check(_lib.lib().logkv_read_status(ctypes.c_void_p(self._workspace.data_ptr()), ctypes.byref(out),
+                                                ctypes.c_void_p(_lib.stream_ptr(self.level_k.device))),
+                   "logkv_read_status")
+        return int(out.value)
+
+    # ------------------------------------------------------------------ window
+    def _positions(self, n: int, input_pos):
+        dev = self.recent_pos.device
+        if input_pos is None:
+            host = [list(range(self.token_count, self.token_count + n)) for _ in range(self.batch_size)]
+            return torch.arange(self.token_count, self.token_count + n, device=dev).unsqueeze(0).expand(
+                self.batch_size, -1), host
+        if input_pos.dim() == 1:
+            if input_pos.numel() != n:
+                raise ValueError(f"input_pos length {input_pos.numel()} != chunk size {n}")
+            row = [int(x) for x in input_pos.detach().cpu().tolist()]
+            return input_pos.to(device=dev, dtype=torch.int64).unsqueeze(0).expand(self.batch_size, -1), \
+                [row[:] for _ in range(self.batch_size)]
+        if input_pos.dim() == 2:
+            if input_pos.shape != (self.batch_size, n):
+                raise ValueError(f"input_pos shape {tuple(input_pos.shape)} != ({self.batch_size}, {n})")
+            return input_pos.to(device=dev, dtype=torch.int64), [[int(x) for x in r] for r in input_pos.tolist()]
+        raise ValueError(f"input_pos must be 1-D or 2-D, got shape {tuple(input_pos.shape)}")
+
+    def add_recent(self, k, v, *, k_raw=None, input_pos=None, record_op_log=False, span_ends=None, **replay):
+        """Append a chunk to the window; flush ``semantic_flush_granularity`` blocks on overflow."""
+        if k_raw is None:
+            raise ValueError("semantic LogKV add_recent requires pre-RoPE k_raw")
+        if record_op_log or any(v_ is not None for v_ in replay.values()):
+            raise NotImplementedError("op-log recording and replay are not implemented by logkv_b200")
+        n = k.size(2)
+        if n > self.recent_size:
+            raise ValueError(f"chunk size {n} exceeds recent_size {self.recent_size}")
+        if k_raw.shape[:3] != k.shape[:3] or k_raw.size(-1) != self.k_dim:
+            raise ValueError(f"k_raw shape {tuple(k_raw.shape)} does not match semantic cache shape")
+        if span_ends is None or len(span_ends) != self.batch_size or any(len(r) != n for r in span_ends):
+            raise ValueError("AlphaLogKV span boundaries must match the input batch and token count")
+        positions, positions_host = self._positions(n, input_pos)
+        if self.token_count + n > self.max_seq_length:
+            raise RuntimeError(f"LogStructuredKVCache: token overflow! token_count={self.token_count}, n={n}, "
+                               f"max_seq_length={self.max_seq_length}.")
+        if self.recent_count + n > self.recent_capacity:
+            raise RuntimeError(f"semantic LogKV recent buffer overflow: recent_count={self.recent_count}, n={n}, "
+                               f"capacity={self.recent_capacity}")
+        self.token_count += n
+        dst = slice(self.recent_count, self.recent_count + n)
+        self.recent_k[:, :, dst] = k
+        self.recent_k_raw[:, :, dst] = k_raw
+        self.recent_v[:, :, dst] = v
+        self.recent_pos[:, dst] = positions
+        ends = torch.tensor(span_ends, dtype=torch.uint8)
+        self._recent_ends[:, dst].copy_(ends.pin_memory() if self.recent_pos.is_cuda else ends, non_blocking=True)
+        for b in range(self.batch_size):
+            self._recent_pos_host[b][dst] = positions_host[b]
+            self._recent_span_ends[b][dst] = [bool(x) for x in span_ends[b]]
+        self.recent_count += n
+        overflow = self.recent_count - self.recent_size
+        if overflow > 0:
+            gran = self.semantic_flush_granularity
+            pending = gran * ((overflow + gran - 1) // gran)
+            while pending > 0:
+                take = min(gran, pending)
+                if take > self.recent_count:
+                    raise RuntimeError(f"semantic LogKV cannot flush {take} tokens from recent_count={self.recent_count}")
+                self.flush_device(take)
+                remaining = self.recent_count - take
+                for b in range(self.batch_size):
+                    self._recent_pos_host[b][:remaining] = self._recent_pos_host[b][take:self.recent_count]
+                    self._recent_pos_host[b][remaining:self.recent_count] = [0] * take
+                    self._recent_span_ends[b][:remaining] = self._recent_span_ends[b][take:self.recent_count]
+                    self._recent_span_ends[b][remaining:self.recent_count] = [False] * take
+                self.recent_count = remaining
+                pending -= take
+
+    # ------------------------------------------------------------------ host mirrors (lazy, synchronizing)
+    @property
+    def alpha_count(self) -> int:
+        return int(self._alpha_count_dev.item())
+
+    @property
+    def _semantic_counts(self):
+        return self.level_count.long().tolist()
+
+    @property
+    def _semantic_alive(self):
+        return self.alive.tolist()
+
+    @property
+    def _semantic_p_hi_c(self):
+        return self.p_hi_c.tolist()
+
+    @property
+    def _semantic_n_total(self):
+        return self.n_total.long().tolist()
+
+    @property
+    def _semantic_level0_phase(self):
+        return self.level0_phase.long().tolist()
+
+    @property
+    def _semantic_current_segment(self):
+        return self.current_segment.long().tolist()
+
+    @property
+    def _alpha_spans(self):
+        lens, closed, count = self._span_len.tolist(), self._span_closed.tolist(), self._span_count.tolist()
+        return [[(lens[b][i], bool(closed[b][i])) for i in range(count[b])] for b in range(self.batch_size)]
+
+    @property
+    def _alpha_positions(self):
+        pos, rows = self.alpha_pos.tolist(), self._row_count.tolist()
+        return [pos[b][:rows[b]] for b in range(self.batch_size)]
+
+    def reset_parameters(self) -> None:
+        """Empty cache: every buffer and mirror back to its constructor value."""
+        i64max = torch.iinfo(torch.int64).max
+        for name in ("recent_k", "recent_v", "recent_k_raw", "recent_pos", "alpha_k_raw", "alpha_v", "alpha_pos",
+                     "alpha_valid", "level_k", "level_v", "level_w", "level_imp", "level_count", "pad_mask",
+                     "level_sum_wp", "level_order", "centroid", "n_eff", "n_total", "current_segment",
+                     "level0_phase", "alive"):
+            getattr(self, name).zero_()
+        self.level_p_lo.fill_(i64max)
+        self.level_p_hi.fill_(-1)
+        self.p_hi_c.fill_(-1)
+        self.ward_cost.fill_(float("inf"))
+        for t in (self._recent_ends, self._span_len, self._span_closed, self._span_count, self._row_count,
+                  self._alpha_count_dev):
+            t.zero_()
+        R = self.recent_capacity
+        self._recent_pos_host = [[0] * R for _ in range(self.batch_size)]
+        self._recent_span_ends = [[False] * R for _ in range(self.batch_size)]
+        self.token_count = 0
+        self.recent_count = 0

@@ -1,0 +1,289 @@
+// Host side of the device-resident flush: workspace carving, launch sequence
+// and the C ABI entry points declared in include/logkv_b200.h.
+//
+// Launch sequence of one flush (all on the caller's stream, no host sync):
+//   K0 snapshot   old exact pool -> workspace
+//   K1 cut        candidate spans per batch row
+//   K2 score      Alpha / Beta span scores
+//   K3 choose     bounded greedy, keep / archive lists, new span table
+//   K4 attach     frozen-centroid decisions per archived token
+//   K5 plan       farthest-point seeds, per-cluster grouping and jobs
+//   K6a prepare   centroids, scalars, new / delayed cluster staging
+//   K6b cascade   ladder append with pairwise or Beta merges
+//   K7 pool       exact pool rewrite
+//   K8 window     window shift by the flushed tokens
+#include <algorithm>
+#include <cstdio>
+
+#include "flush_alpha.cuh"
+#include "flush_ladder.cuh"
+#include "flush_route.cuh"
+
+namespace logkv {
+
+// ---------------------------------------------------------------- K8: window shift
+template <typename T>
+__global__ void window_stage_kernel(Geo g, logkv_state_t s, Work w, int rem) {
+  // copy [F, F+rem) -> staging [0, rem) when source and destination overlap
+  const int b = blockIdx.z, grp = blockIdx.y;
+  const size_t base = ((size_t)b * g.G + grp) * g.cap2R * g.D;
+  const size_t n = (size_t)rem * g.D;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t src = base + (size_t)g.F * g.D + i;
+    static_cast<T*>(w.wk)[base + i] = static_cast<const T*>(s.recent_k)[src];
+    static_cast<T*>(w.wkr)[base + i] = static_cast<const T*>(s.recent_k_raw)[src];
+    static_cast<T*>(w.wv)[base + i] = static_cast<const T*>(s.recent_v)[src];
+  }
+  if (grp == 0 && blockIdx.x == 0)
+    for (int i = threadIdx.x; i < rem; i += blockDim.x) {
+      w.wpos[(size_t)b * g.cap2R + i] = s.recent_pos[(size_t)b * g.cap2R + g.F + i];
+      w.wends[(size_t)b * g.cap2R + i] = s.recent_ends[(size_t)b * g.cap2R + g.F + i];
+    }
+}
+
+template <typename T>
+__global__ void window_shift_kernel(Geo g, logkv_state_t s, Work w, int rem, int staged) {
+  const int b = blockIdx.z, grp = blockIdx.y;
+  const size_t base = ((size_t)b * g.G + grp) * g.cap2R * g.D;
+  const size_t n = (size_t)g.recent_count * g.D;
+  T* rk = static_cast<T*>(s.recent_k);
+  T* rkr = static_cast<T*>(s.recent_k_raw);
+  T* rv = static_cast<T*>(s.recent_v);
+  const T* sk = staged ? static_cast<const T*>(w.wk) : rk;
+  const T* skr = staged ? static_cast<const T*>(w.wkr) : rkr;
+  const T* sv = staged ? static_cast<const T*>(w.wv) : rv;
+  const size_t F = (size_t)g.F * g.D, R = (size_t)rem * g.D;
+  // Without staging (rem <= F) element j of [F, count) is read and then zeroed by
+  // the same thread; [rem, F) is never read.  With staging every source is a copy.
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    if (staged) {
+      if (i < R) {
+        rk[base + i] = sk[base + i];
+        rkr[base + i] = skr[base + i];
+        rv[base + i] = sv[base + i];
+      } else {
+        rk[base + i] = Elem<T>::zero();
+        rkr[base + i] = Elem<T>::zero();
+        rv[base + i] = Elem<T>::zero();
+      }
+    } else if (i >= F) {
+      const T a = rk[base + i], c = rkr[base + i], e = rv[base + i];
+      rk[base + i - F] = a;
+      rkr[base + i - F] = c;
+      rv[base + i - F] = e;
+      rk[base + i] = Elem<T>::zero();
+      rkr[base + i] = Elem<T>::zero();
+      rv[base + i] = Elem<T>::zero();
+    } else if (i >= R) {
+      rk[base + i] = Elem<T>::zero();
+      rkr[base + i] = Elem<T>::zero();
+      rv[base + i] = Elem<T>::zero();
+    }
+  }
+  if (grp == 0 && blockIdx.x == 0) {
+    const size_t r = (size_t)b * g.cap2R;
+    for (int i = threadIdx.x; i < g.recent_count; i += blockDim.x) {
+      if (staged) {
+        s.recent_pos[r + i] = i < rem ? w.wpos[r + i] : 0;
+        s.recent_ends[r + i] = i < rem ? w.wends[r + i] : 0;
+      } else if (i >= g.F) {
+        const int64_t p = s.recent_pos[r + i];
+        const uint8_t e = s.recent_ends[r + i];
+        s.recent_pos[r + i - g.F] = p;
+        s.recent_ends[r + i - g.F] = e;
+        s.recent_pos[r + i] = 0;
+        s.recent_ends[r + i] = 0;
+      } else if (i >= rem) {
+        s.recent_pos[r + i] = 0;
+        s.recent_ends[r + i] = 0;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- workspace
+struct Carver {
+  char* base;
+  size_t off = 0;
+  template <typename P>
+  P* take(size_t count, size_t elem) {
+    off = (off + 255) & ~size_t(255);
+    P* p = reinterpret_cast<P*>(base ? base + off : nullptr);
+    off += count * elem;
+    return p;
+  }
+};
+
+static int next_pow2(int v) {
+  int p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+static Geo make_geo(const logkv_layout_t& L, int F, int recent_count) {
+  Geo g{};
+  g.B = L.batch;
+  g.G = L.groups;
+  g.D = L.dim;
+  g.K = L.clusters;
+  g.L = L.levels;
+  g.Bs = L.slots;
+  g.cap2R = L.recent_capacity;
+  g.P = L.exact;
+  g.span_cap = L.span_cap;
+  g.beta = L.beta;
+  g.F = F;
+  g.NW = g.P + F;
+  g.NC = g.P + F;
+  g.recent_count = recent_count;
+  g.S = g.NW + g.K * g.L * g.Bs + 2 * g.K;
+  g.sort_cap = next_pow2(g.L * g.Bs + g.NW);
+  g.eta = L.eta;
+  g.g0 = L.g0;
+  g.lam = L.lam;
+  return g;
+}
+
+static size_t carve(const Geo& g, size_t esize, char* base, Work* w) {
+  Carver c{base};
+  const size_t B = g.B, G = g.G, D = g.D, K = g.K, P = g.P, NC = g.NC, NW = g.NW, S = g.S;
+  w->status = c.take<int32_t>(1, 4);
+  w->snap_k = c.take<char>(B * G * P * D, esize);
+  w->snap_v = c.take<char>(B * G * P * D, esize);
+  w->snap_pos = c.take<int64_t>(B * P, 8);
+  w->snap_rowcount = c.take<int32_t>(B, 4);
+  w->cand_s0 = c.take<int32_t>(B * NC, 4);
+  w->cand_n0 = c.take<int32_t>(B * NC, 4);
+  w->cand_s1 = c.take<int32_t>(B * NC, 4);
+  w->cand_n1 = c.take<int32_t>(B * NC, 4);
+  w->cand_flags = c.take<uint8_t>(B * NC, 1);
+  w->n_cand = c.take<int32_t>(B, 4);
+  w->scores = c.take<float>(B * NC, 4);
+  w->keep_idx = c.take<int32_t>(B * P, 4);
+  w->nkeep = c.take<int32_t>(B, 4);
+  w->arch_idx = c.take<int32_t>(B * NW, 4);
+  w->narch = c.take<int32_t>(B, 4);
+  w->assign = c.take<int8_t>(B * G * NW, 1);
+  w->orphan = c.take<uint8_t>(B * G * NW, 1);
+  w->s_winner = c.take<float>(B * G * NW, 4);
+  w->tok_list = c.take<int32_t>(B * G * NW, 4);
+  w->plan_off = c.take<int32_t>(B * G * K, 4);
+  w->plan_n = c.take<int32_t>(B * G * K, 4);
+  w->plan_type = c.take<int32_t>(B * G * K, 4);
+  w->plan_m0 = c.take<int32_t>(B * G * K, 4);
+  w->plan_scr = c.take<int32_t>(B * G * K, 4);
+  w->plan_base = c.take<int64_t>(B * G * K, 8);
+  w->sk = c.take<char>(B * G * 2 * S * D, esize);
+  w->sv = c.take<char>(B * G * 2 * S * D, esize);
+  w->sw = c.take<float>(B * G * 2 * S, 4);
+  w->slo = c.take<int64_t>(B * G * 2 * S, 8);
+  w->shi = c.take<int64_t>(B * G * 2 * S, 8);
+  w->sswp = c.take<int64_t>(B * G * 2 * S, 8);
+  w->sord = c.take<int64_t>(B * G * 2 * S, 8);
+  w->spad = c.take<uint8_t>(B * G * 2 * S, 1);
+  const size_t R = g.cap2R;
+  w->wk = c.take<char>(B * G * R * D, esize);
+  w->wkr = c.take<char>(B * G * R * D, esize);
+  w->wv = c.take<char>(B * G * R * D, esize);
+  w->wpos = c.take<int64_t>(B * R, 8);
+  w->wends = c.take<uint8_t>(B * R, 1);
+  return (c.off + 255) & ~size_t(255);
+}
+
+static int validate(const logkv_layout_t* L, int F) {
+  if (!L) return LOGKV_E_POINTER;
+  if (L->dtype != LOGKV_DTYPE_F32 && L->dtype != LOGKV_DTYPE_BF16) return LOGKV_E_DTYPE;
+  if (L->batch < 1 || L->groups < 1 || L->dim < 2 || L->dim > 1024 || L->dim % 2) return LOGKV_E_SHAPE;
+  if (L->clusters < 2 || L->clusters > kMaxClusters || L->levels < 2 || L->levels > kMaxLevels) return LOGKV_E_SHAPE;
+  if (L->slots < 2 || L->exact < 1 || L->span_cap < 1 || L->span_cap > L->exact) return LOGKV_E_SHAPE;
+  if (F < 1 || F > L->recent_capacity || L->exact + F > 8192) return LOGKV_E_SHAPE;
+  if (L->levels * L->slots + L->exact + F > (1 << 14)) return LOGKV_E_SHAPE;
+  return LOGKV_OK;
+}
+
+template <typename T>
+static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st) {
+  const dim3 rows3(1, g.G, g.B);
+  const int sm_count = 148;
+  const int per_bg = std::max(1, std::min(64, (g.P * g.D + 255) / 256));
+  snapshot_kernel<T><<<dim3(per_bg, g.G, g.B), 256, 0, st>>>(g, s, w);
+  const size_t cut_smem = 2 * (size_t)g.F * sizeof(int);
+  if (cut_smem > 48 * 1024) cudaFuncSetAttribute(alpha_cut_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cut_smem);
+  alpha_cut_kernel<<<g.B, 1024, cut_smem, st>>>(g, s, w);
+  const size_t score_smem = (2 * (size_t)g.G * g.D + (size_t)g.G * 256 + 6 * (size_t)g.G) * sizeof(float);
+  if (score_smem > 48 * 1024)
+    cudaFuncSetAttribute(alpha_score_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)score_smem);
+  const int score_blocks = std::max(1, std::min(g.NC, 2 * sm_count / std::max(1, g.B) + 1));
+  alpha_score_kernel<T><<<dim3(score_blocks, g.B), 256, score_smem, st>>>(g, s, w);
+  const size_t choose_smem = (size_t)g.NC * (8 + 4 * 4 + 2);
+  if (choose_smem > 48 * 1024)
+    cudaFuncSetAttribute(alpha_choose_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)choose_smem);
+  alpha_choose_kernel<<<g.B, 1024, choose_smem, st>>>(g, s, w);
+  const size_t attach_smem = ((size_t)g.K * g.D + 128 * (size_t)(g.D + 1)) * sizeof(float);
+  if (attach_smem > 48 * 1024)
+    cudaFuncSetAttribute(attach_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attach_smem);
+  attach_kernel<T><<<dim3((g.NW + 127) / 128, g.G, g.B), 128, attach_smem, st>>>(g, s, w);
+  const size_t plan_smem = (size_t)g.NW * sizeof(float);
+  if (plan_smem > 48 * 1024)
+    cudaFuncSetAttribute(plan_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan_smem);
+  plan_kernel<T><<<dim3(g.G, g.B), 1024, plan_smem, st>>>(g, s, w);
+  const size_t prep_smem = (size_t)g.sort_cap * sizeof(unsigned long long);
+  if (prep_smem > 48 * 1024)
+    cudaFuncSetAttribute(prepare_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
+  prepare_kernel<T><<<dim3(g.K, g.G, g.B), 256, prep_smem, st>>>(g, s, w);
+  const size_t casc_smem = 2 * (size_t)g.Bs * g.D * sizeof(T) + (size_t)g.Bs * sizeof(Meta) + 16;
+  if (g.beta) {
+    if (casc_smem > 48 * 1024)
+      cudaFuncSetAttribute(cascade_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)casc_smem);
+    cascade_kernel<T, true><<<dim3(g.K, g.G, g.B), 256, casc_smem, st>>>(g, s, w);
+  } else {
+    if (casc_smem > 48 * 1024)
+      cudaFuncSetAttribute(cascade_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)casc_smem);
+    cascade_kernel<T, false><<<dim3(g.K, g.G, g.B), 256, casc_smem, st>>>(g, s, w);
+  }
+  pool_rewrite_kernel<T><<<dim3(per_bg, g.G, g.B), 256, 0, st>>>(g, s, w);
+  const int rem = g.recent_count - g.F;
+  const int per_win = std::max(1, std::min(128, (g.recent_count * g.D + 255) / 256));
+  const int staged = rem > g.F ? 1 : 0;
+  if (staged) window_stage_kernel<T><<<dim3(per_win, g.G, g.B), 256, 0, st>>>(g, s, w, rem);
+  window_shift_kernel<T><<<dim3(per_win, g.G, g.B), 256, 0, st>>>(g, s, w, rem, staged);
+  (void)rows3;
+  return (int)cudaGetLastError();
+}
+
+}  // namespace logkv
+
+using namespace logkv;
+
+extern "C" size_t logkv_flush_workspace_bytes(const logkv_layout_t* layout, int32_t flush_tokens) {
+  if (validate(layout, flush_tokens) != LOGKV_OK) return 0;
+  const Geo g = make_geo(*layout, flush_tokens, layout->recent_capacity);
+  Work w{};
+  return carve(g, layout->dtype == LOGKV_DTYPE_BF16 ? 2 : 4, nullptr, &w);
+}
+
+extern "C" int logkv_flush(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                           int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream) {
+  const int v = validate(layout, flush_tokens);
+  if (v != LOGKV_OK) return v;
+  if (!state || !workspace) return LOGKV_E_POINTER;
+  if (recent_count < flush_tokens || recent_count > layout->recent_capacity) return LOGKV_E_SHAPE;
+  const size_t esize = layout->dtype == LOGKV_DTYPE_BF16 ? 2 : 4;
+  const Geo g = make_geo(*layout, flush_tokens, recent_count);
+  Work w{};
+  const size_t need = carve(g, esize, static_cast<char*>(workspace), &w);
+  if (workspace_bytes < need) return LOGKV_E_WORKSPACE;
+  const size_t casc_smem = 2 * (size_t)g.Bs * g.D * esize + (size_t)g.Bs * sizeof(Meta) + 16;
+  if (casc_smem > 227 * 1024 || (size_t)g.sort_cap * 8 > 227 * 1024) return LOGKV_E_SMEM;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (layout->dtype == LOGKV_DTYPE_BF16) return launch_flush<__nv_bfloat16>(g, *state, w, st);
+  return launch_flush<float>(g, *state, w, st);
+}
+
+extern "C" int logkv_read_status(const void* workspace, int32_t* out, void* stream) {
+  if (!workspace || !out) return LOGKV_E_POINTER;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(out, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  return (int)e;
+}

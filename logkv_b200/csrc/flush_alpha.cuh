@@ -1,0 +1,570 @@
+// Alpha exact-span pool on the device: snapshot, span cut, span scores, greedy choice.
+//
+// Follows litgpt/alpha_log_kv.py (_new_runs :16-53, cut_spans :84-122,
+// score_spans :125-174, choose_spans :177-226) and the pool rewrite of
+// _alpha_route_flush (litgpt/log_kv_cache.py:3903-4003).  Token index space of
+// one batch row: [0, P) = old pool rows (compacted, kept spans in pool order),
+// [P, P + F) = the flushed window tokens.
+#pragma once
+
+#include "flush_common.cuh"
+
+namespace logkv {
+
+// ---------------------------------------------------------------- K0: snapshot
+// Copies the old exact pool so the pool can be rewritten in place later, and
+// resets the status word and the device alpha_count.
+template <typename T>
+__global__ void snapshot_kernel(Geo g, logkv_state_t s, Work w) {
+  const int b = blockIdx.z, grp = blockIdx.y;
+  const size_t n = (size_t)g.P * g.D;
+  const T* ksrc = static_cast<const T*>(s.alpha_k_raw) + ((size_t)b * g.G + grp) * n;
+  const T* vsrc = static_cast<const T*>(s.alpha_v) + ((size_t)b * g.G + grp) * n;
+  T* kdst = static_cast<T*>(w.snap_k) + ((size_t)b * g.G + grp) * n;
+  T* vdst = static_cast<T*>(w.snap_v) + ((size_t)b * g.G + grp) * n;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    kdst[i] = ksrc[i];
+    vdst[i] = vsrc[i];
+  }
+  if (grp == 0 && blockIdx.x == 0) {
+    for (int i = threadIdx.x; i < g.P; i += blockDim.x) w.snap_pos[(size_t)b * g.P + i] = s.alpha_pos[(size_t)b * g.P + i];
+    if (threadIdx.x == 0) {
+      w.snap_rowcount[b] = s.alpha_rowcount[b];
+      if (b == 0) {
+        *w.status = 0;
+        *s.alpha_count = 0;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- K1: span cut
+// One block (1024 threads) per batch row.  Candidates, in the reference's
+// order: closed old spans (pool order), the old unfinished span if a
+// position jump closed it, then the runs of the new tokens (the first one
+// continuing the unfinished span), or the unfinished span alone when no new
+// token arrived.
+__global__ void __launch_bounds__(1024) alpha_cut_kernel(Geo g, logkv_state_t s, Work w) {
+  const int b = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+  const int P = g.P, F = g.F, cap = g.span_cap;
+  __shared__ int wsum[32];
+  __shared__ int sh_pend_idx, sh_n_closed, sh_nruns;
+  extern __shared__ int run_end[];  // [F]
+  const int nsp = s.alpha_nspans[b];
+  if (tid == 0) sh_pend_idx = -1;
+  __syncthreads();
+  // Old spans: offsets and closed-candidate slots via block scans (chunked over P).
+  int carry_off = 0, carry_closed = 0;
+  for (int base = 0; base < nsp; base += nt) {
+    const int i = base + tid;
+    const int len = i < nsp ? s.alpha_span_len[(size_t)b * P + i] : 0;
+    const int closed = i < nsp ? (int)s.alpha_span_closed[(size_t)b * P + i] : 0;
+    const int off_incl = block_inclusive_scan(len, wsum);
+    const int cl_incl = block_inclusive_scan(i < nsp && closed ? 1 : 0, wsum);
+    if (i < nsp) {
+      const int off = carry_off + off_incl - len;
+      if (closed) {
+        const int c = carry_closed + cl_incl - 1;
+        w.cand_s0[(size_t)b * g.NC + c] = off;
+        w.cand_n0[(size_t)b * g.NC + c] = len;
+        w.cand_s1[(size_t)b * g.NC + c] = 0;
+        w.cand_n1[(size_t)b * g.NC + c] = 0;
+        w.cand_flags[(size_t)b * g.NC + c] = 3;  // old | closed
+      } else {
+        atomicMax(&sh_pend_idx, i);
+      }
+    }
+    // broadcast the chunk totals
+    __shared__ int tot_off, tot_cl;
+    if (tid == nt - 1) {
+      tot_off = off_incl;
+      tot_cl = cl_incl;
+    }
+    __syncthreads();
+    carry_off += tot_off;
+    carry_closed += tot_cl;
+    __syncthreads();
+  }
+  if (tid == 0) sh_n_closed = carry_closed;
+  // Pending (unfinished) span: its offset is the sum of lengths before it.
+  __shared__ int sh_pend_off, sh_pend_len;
+  __shared__ long long sh_pend_pos;
+  if (tid == 0) {
+    sh_pend_off = 0;
+    sh_pend_len = 0;
+    sh_pend_pos = 0;
+    const int pi = sh_pend_idx;
+    if (pi >= 0) {
+      int off = 0;
+      for (int i = 0; i < pi; ++i) off += s.alpha_span_len[(size_t)b * P + i];
+      sh_pend_off = off;
+      sh_pend_len = s.alpha_span_len[(size_t)b * P + pi];
+      if (sh_pend_len > 0) sh_pend_pos = w.snap_pos[(size_t)b * P + off + sh_pend_len - 1];
+    }
+  }
+  __syncthreads();
+  const int pend_len = sh_pend_len, pend_off = sh_pend_off;
+  const int64_t* pos = s.recent_pos + (size_t)b * g.cap2R;
+  const uint8_t* ends = s.recent_ends + (size_t)b * g.cap2R;
+  const bool pclosed = pend_len > 0 && F > 0 && pos[0] != (int64_t)sh_pend_pos + 1;
+  const int prefix = pclosed ? 0 : pend_len;
+  // New runs: each thread owns a contiguous chunk of tokens.
+  const int per = (F + nt - 1) / nt;
+  const int lo = tid * per, hi = min(F, lo + per);
+  // segment start = last token <= i that starts a segment (jump or boundary before it).
+  int local_start = -1;
+  for (int i = lo; i < hi; ++i) {
+    const bool first = i == 0 || pos[i] != pos[i - 1] + 1 || ends[i - 1];
+    if (first) local_start = i;
+  }
+  // inclusive max-scan over threads of local_start
+  __shared__ int seg_carry[1024];
+  seg_carry[tid] = local_start;
+  __syncthreads();
+  for (int off = 1; off < nt; off <<= 1) {
+    int v = seg_carry[tid];
+    if (tid >= off) v = max(v, seg_carry[tid - off]);
+    __syncthreads();
+    seg_carry[tid] = v;
+    __syncthreads();
+  }
+  int seg_start = tid > 0 ? seg_carry[tid - 1] : -1;
+  int nstops = 0;
+  uint32_t stop_mask = 0, closed_mask = 0;
+  for (int i = lo; i < hi; ++i) {
+    const bool first = i == 0 || pos[i] != pos[i - 1] + 1 || ends[i - 1];
+    if (first) seg_start = i;
+    const bool seg0 = seg_start == 0;
+    const int filled = i - seg_start + (seg0 ? prefix : 0) + 1;
+    bool capc = filled % cap == 0;
+    if (prefix >= cap && seg0) capc = false;
+    const bool close = ends[i] != 0 || capc;
+    const bool jump_next = i + 1 < F && pos[i + 1] != pos[i] + 1;
+    const bool stop = close || jump_next || i == F - 1;
+    if (stop) {
+      stop_mask |= 1u << (i - lo);
+      if (close || jump_next) closed_mask |= 1u << (i - lo);
+      ++nstops;
+    }
+  }
+  const int incl = block_inclusive_scan(nstops, wsum);
+  int r = incl - nstops;
+  int* run_closed = run_end + F;
+  for (int i = lo; i < hi; ++i)
+    if (stop_mask & (1u << (i - lo))) {
+      run_closed[r] = (closed_mask >> (i - lo)) & 1u;
+      run_end[r++] = i + 1;
+    }
+  if (tid == nt - 1) sh_nruns = incl;
+  __syncthreads();
+  const int nruns = sh_nruns;
+  const int base = sh_n_closed + (pclosed ? 1 : 0);
+  if (tid == 0 && pclosed) {
+    const size_t c = (size_t)b * g.NC + sh_n_closed;
+    w.cand_s0[c] = pend_off;
+    w.cand_n0[c] = pend_len;
+    w.cand_s1[c] = 0;
+    w.cand_n1[c] = 0;
+    w.cand_flags[c] = 2;  // closed, not old
+  }
+  // run -> candidate
+  for (int rr = tid; rr < nruns; rr += nt) {
+    const int stop = run_end[rr];
+    const int start = rr == 0 ? 0 : run_end[rr - 1];
+    const size_t c = (size_t)b * g.NC + base + rr;
+    if (rr == 0 && pend_len > 0 && !pclosed) {
+      w.cand_s0[c] = pend_off;
+      w.cand_n0[c] = pend_len;
+      w.cand_s1[c] = P + start;
+      w.cand_n1[c] = stop - start;
+    } else {
+      w.cand_s0[c] = P + start;
+      w.cand_n0[c] = stop - start;
+      w.cand_s1[c] = 0;
+      w.cand_n1[c] = 0;
+    }
+    w.cand_flags[c] = run_closed[rr] ? 2 : 0;
+  }
+  if (tid == 0) {
+    int total = base + nruns;
+    if (pend_len > 0 && !pclosed && nruns == 0) {
+      const size_t c = (size_t)b * g.NC + base;
+      w.cand_s0[c] = pend_off;
+      w.cand_n0[c] = pend_len;
+      w.cand_s1[c] = 0;
+      w.cand_n1[c] = 0;
+      w.cand_flags[c] = 0;
+      total += 1;
+    }
+    w.n_cand[b] = total;
+  }
+}
+
+// ---------------------------------------------------------------- K2: span scores
+template <typename T>
+__device__ __forceinline__ const T* cand_row(const Geo& g, const logkv_state_t& s, const Work& w, const T* snap,
+                                             const T* recent, int b, int grp, int src) {
+  if (src < g.P) return snap + (((size_t)b * g.G + grp) * g.P + src) * g.D;
+  return recent + (((size_t)b * g.G + grp) * g.cap2R + (src - g.P)) * g.D;
+}
+
+// Per candidate and group: mean vector, energy E, residual part
+// R = max(E - mean(mean^2), 0) / max(E, 1e-12); Beta adds the novelty term.
+template <typename T>
+__global__ void __launch_bounds__(256) alpha_score_kernel(Geo g, logkv_state_t s, Work w) {
+  const int b = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
+  const int G = g.G, D = g.D, K = g.K;
+  extern __shared__ float sm[];
+  float* kmean = sm;                 // [G][D]
+  float* vmean = kmean + G * D;      // [G][D]
+  float* etok = vmean + G * D;       // [G][256]
+  float* part = etok + G * 256;      // [2][G]
+  float* kener = part + 2 * G;       // [G]
+  float* kms = kener + G;            // [G]
+  float* gscore = kms + G;           // [G]
+  float* nearest = gscore + G;       // [G]
+  const T* snapk = static_cast<const T*>(w.snap_k);
+  const T* snapv = static_cast<const T*>(w.snap_v);
+  const T* reck = static_cast<const T*>(s.recent_k_raw);
+  const T* recv = static_cast<const T*>(s.recent_v);
+  const int ncand = w.n_cand[b];
+  for (int ci = blockIdx.x; ci < ncand; ci += gridDim.x) {
+    const size_t cix = (size_t)b * g.NC + ci;
+    const int s0 = w.cand_s0[cix], n0 = w.cand_n0[cix], s1 = w.cand_s1[cix], n1 = w.cand_n1[cix];
+    const int n = n0 + n1;
+    const float fn = (float)n;
+    for (int comp = 0; comp < 2; ++comp) {
+      const T* snap = comp == 0 ? snapk : snapv;
+      const T* rec = comp == 0 ? reck : recv;
+      float* mean = comp == 0 ? kmean : vmean;
+      // mean over tokens (sequential per feature)
+      for (int item = tid; item < G * D; item += nt) {
+        const int grp = item / D, d = item % D;
+        float acc = 0.f;
+        for (int t = 0; t < n; ++t) {
+          const int src = t < n0 ? s0 + t : s1 + (t - n0);
+          acc = fadd(acc, Elem<T>::load(cand_row<T>(g, s, w, snap, rec, b, grp, src) + d));
+        }
+        mean[item] = fdiv(acc, fn);
+      }
+      // energy: per token sum(x^2)/D sequential, then sequential mean over tokens
+      float eacc = 0.f;  // owned by thread grp < G
+      for (int c0 = 0; c0 < n; c0 += 256) {
+        const int cn = min(256, n - c0);
+        __syncthreads();
+        for (int item = tid; item < G * cn; item += nt) {
+          const int grp = item / cn, tt = item % cn, t = c0 + tt;
+          const int src = t < n0 ? s0 + t : s1 + (t - n0);
+          const T* row = cand_row<T>(g, s, w, snap, rec, b, grp, src);
+          float acc = 0.f;
+          for (int d = 0; d < D; ++d) {
+            const float x = Elem<T>::load(row + d);
+            acc = fadd(acc, fmul(x, x));
+          }
+          etok[grp * 256 + tt] = fdiv(acc, (float)D);
+        }
+        __syncthreads();
+        if (tid < G)
+          for (int tt = 0; tt < cn; ++tt) eacc = fadd(eacc, etok[tid * 256 + tt]);
+      }
+      __syncthreads();
+      if (tid < G) {
+        const float energy = fdiv(eacc, fn);
+        float ms = 0.f;
+        for (int d = 0; d < D; ++d) ms = fadd(ms, fmul(mean[tid * D + d], mean[tid * D + d]));
+        ms = fdiv(ms, (float)D);
+        const float resid = fmaxf(fsub(energy, ms), 0.f);
+        part[comp * G + tid] = fdiv(resid, fmaxf(energy, 1e-12f));
+        if (comp == 0) {
+          kener[tid] = energy;
+          kms[tid] = ms;
+        }
+      }
+      __syncthreads();
+    }
+    if (!g.beta) {
+      if (tid == 0) {
+        float a = 0.f, c = 0.f;
+        for (int grp = 0; grp < G; ++grp) a = fadd(a, part[grp]);
+        for (int grp = 0; grp < G; ++grp) c = fadd(c, part[G + grp]);
+        w.scores[cix] = fadd(fdiv(a, (float)G), fdiv(c, (float)G));
+      }
+      __syncthreads();
+      continue;
+    }
+    // Beta novelty: nearest live centre by mean-square distance of the key mean.
+    if (tid < G) nearest[tid] = INFINITY;
+    __syncthreads();
+    for (int item = tid; item < G * K; item += nt) {
+      const int grp = item / K, c = item % K;
+      const size_t lane = ((size_t)b * G + grp) * K + c;
+      if (!s.alive[lane]) continue;
+      const float* mu = s.centroid + lane * D;
+      float dot = 0.f, mm = 0.f;
+      for (int d = 0; d < D; ++d) {
+        dot = fadd(dot, fmul(kmean[grp * D + d], mu[d]));
+        mm = fadd(mm, fmul(mu[d], mu[d]));
+      }
+      dot = fdiv(dot, (float)D);
+      mm = fdiv(mm, (float)D);
+      const float dist = fmaxf(fsub(fadd(kms[grp], mm), fmul(2.f, dot)), 0.f);
+      atomicMin(reinterpret_cast<int*>(&nearest[grp]), __float_as_int(dist));  // dist >= 0: int order == float order
+    }
+    __syncthreads();
+    if (tid < G) {
+      bool any = false;
+      for (int c = 0; c < K; ++c) any |= s.alive[((size_t)b * G + tid) * K + c] != 0;
+      const float nr = any ? nearest[tid] : 0.f;
+      const float nov = fdiv(nr, fmaxf(kener[tid], 1e-12f));
+      gscore[tid] = fadd(fmul(fadd(part[tid], part[G + tid]), 0.5f), fdiv(nov, fadd(1.f, nov)));
+    }
+    __syncthreads();
+    if (tid == 0) {
+      float v1 = -INFINITY, v2 = -INFINITY;
+      for (int grp = 0; grp < G; ++grp) {
+        const float x = gscore[grp];
+        if (x > v1) {
+          v2 = v1;
+          v1 = x;
+        } else if (x > v2) {
+          v2 = x;
+        }
+      }
+      const int top = G < 2 ? G : 2;
+      float acc = fadd(0.f, v1);
+      if (top == 2) acc = fadd(acc, v2);
+      w.scores[cix] = fdiv(acc, (float)top);
+    }
+    __syncthreads();
+  }
+}
+
+// ---------------------------------------------------------------- K3: greedy choice
+// Sort helpers: the reference sorts Python tuples; ties are impossible because
+// the index is part of every key.
+__device__ __forceinline__ bool victim_less(double da, int ia, double db, int ib) {
+  return da < db || (da == db && ia > ib);  // (density, -i) ascending
+}
+__device__ __forceinline__ bool ranked_less(double da, int ia, double db, int ib) {
+  return da > db || (da == db && ia < ib);  // (-density, i) ascending
+}
+
+__global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t s, Work w) {
+  const int b = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+  const int NC = g.NC, P = g.P;
+  extern __shared__ unsigned char smraw[];
+  double* dens = reinterpret_cast<double*>(smraw);          // [NC]
+  int* size = reinterpret_cast<int*>(dens + NC);             // [NC]
+  int* vict = size + NC;                                     // [NC] sorted victims
+  int* ranked = vict + NC;                                   // [NC]
+  int* keep_off = ranked + NC;                               // [NC]
+  unsigned char* flags = reinterpret_cast<unsigned char*>(keep_off + NC);  // [NC]
+  unsigned char* chosen = flags + NC;                        // [NC]
+  __shared__ int wsum[32];
+  __shared__ int sh_nv, sh_nr, sh_room;
+  const int n = w.n_cand[b];
+  for (int i = tid; i < n; i += nt) {
+    const size_t c = (size_t)b * NC + i;
+    flags[i] = w.cand_flags[c];
+    size[i] = w.cand_n0[c] + w.cand_n1[c];
+    const double sc = (double)w.scores[c];
+    dens[i] = (flags[i] & 1) ? sc * 1.1 : sc * 1.0;
+    chosen[i] = (!(flags[i] & 2)) || (flags[i] & 1);  // mandatory (open) or old
+  }
+  __syncthreads();
+  // room = budget - sizes of mandatory and old spans (integer, any order)
+  if (tid == 0) {
+    int room = P;
+    for (int i = 0; i < n; ++i)
+      if (chosen[i]) room -= size[i];
+    sh_room = room;
+  }
+  __syncthreads();
+  // victims = chosen and not mandatory, sorted by (density, -i): rank-based placement
+  for (int i = tid; i < n; i += nt) {
+    if (!(chosen[i] && (flags[i] & 2))) continue;
+    int rank = 0;
+    for (int j = 0; j < n; ++j)
+      if (j != i && chosen[j] && (flags[j] & 2) && victim_less(dens[j], j, dens[i], i)) ++rank;
+    vict[rank] = i;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int nv = 0;
+    for (int i = 0; i < n; ++i) nv += (chosen[i] && (flags[i] & 2)) ? 1 : 0;
+    // make room for the bounded unfinished tail first (victims in order)
+    int room = sh_room, k = 0;
+    while (k < nv && room < 0) {
+      chosen[vict[k]] = 0;
+      room += size[vict[k]];
+      ++k;
+    }
+    for (int i = k; i < nv; ++i) vict[i - k] = vict[i];
+    sh_nv = nv - k;
+    sh_room = room;
+  }
+  __syncthreads();
+  // ranked = not chosen, sorted by (-density, i)
+  for (int i = tid; i < n; i += nt) {
+    if (chosen[i]) continue;
+    int rank = 0;
+    for (int j = 0; j < n; ++j)
+      if (j != i && !chosen[j] && ranked_less(dens[j], j, dens[i], i)) ++rank;
+    ranked[rank] = i;
+  }
+  if (tid == 0) {
+    int nr = 0;
+    for (int i = 0; i < n; ++i) nr += chosen[i] ? 0 : 1;
+    sh_nr = nr;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int room = sh_room, nv = sh_nv;
+    const int nr = sh_nr;
+    for (int q = 0; q < nr; ++q) {
+      const int i = ranked[q];
+      const int length = size[i];
+      int available = room, nrem = 0;
+      double loss = 0.0;
+      if (available < length) {
+        for (int j = 0; j < nv; ++j) {
+          const int v = vict[j];
+          ++nrem;
+          available += size[v];
+          loss += dens[v] * (double)size[v];
+          if (available >= length) break;
+        }
+      }
+      if (available >= length && (nrem == 0 || dens[i] * (double)length > loss)) {
+        for (int j = 0; j < nrem; ++j) chosen[vict[j]] = 0;
+        // victims: drop the removed prefix, insert i at its sorted place
+        int m = 0;
+        for (int j = nrem; j < nv; ++j) vict[m++] = vict[j];
+        int at = m;
+        while (at > 0 && victim_less(dens[i], i, dens[vict[at - 1]], vict[at - 1])) {
+          vict[at] = vict[at - 1];
+          --at;
+        }
+        vict[at] = i;
+        nv = m + 1;
+        chosen[i] = 1;
+        room = available - length;
+      }
+    }
+  }
+  __syncthreads();
+  // Emit keep/archive token lists in candidate order and the new span table.
+  int carry_keep = 0, carry_arch = 0, carry_sp = 0;
+  __shared__ int tot_k, tot_a, tot_s;
+  for (int base = 0; base < n; base += nt) {
+    const int i = base + tid;
+    const bool in = i < n;
+    const int sz = in ? size[i] : 0;
+    const bool ch = in && chosen[i];
+    const int kincl = block_inclusive_scan(ch ? sz : 0, wsum);
+    const int aincl = block_inclusive_scan(in && !ch ? sz : 0, wsum);
+    const int sincl = block_inclusive_scan(ch ? 1 : 0, wsum);
+    if (in) {
+      const size_t c = (size_t)b * NC + i;
+      const int s0 = w.cand_s0[c], n0 = w.cand_n0[c], s1 = w.cand_s1[c];
+      if (ch) {
+        const int at = carry_keep + kincl - sz;
+        for (int t = 0; t < sz; ++t) {
+          const int src = t < n0 ? s0 + t : s1 + (t - n0);
+          if (at + t < P) w.keep_idx[(size_t)b * P + at + t] = src;
+        }
+        const int sp = carry_sp + sincl - 1;
+        if (sp < P) {
+          s.alpha_span_len[(size_t)b * P + sp] = sz;
+          s.alpha_span_closed[(size_t)b * P + sp] = (flags[i] & 2) ? 1 : 0;
+        }
+      } else {
+        const int at = carry_arch + aincl - sz;
+        for (int t = 0; t < sz; ++t) {
+          const int src = t < n0 ? s0 + t : s1 + (t - n0);
+          w.arch_idx[(size_t)b * g.NW + at + t] = src;
+        }
+      }
+    }
+    if (tid == nt - 1) {
+      tot_k = kincl;
+      tot_a = aincl;
+      tot_s = sincl;
+    }
+    __syncthreads();
+    carry_keep += tot_k;
+    carry_arch += tot_a;
+    carry_sp += tot_s;
+    __syncthreads();
+  }
+  if (tid == 0) {
+    int nkeep = carry_keep;
+    if (nkeep > P) {
+      set_status(w.status, kStatusListOverflow);
+      nkeep = P;
+    }
+    w.nkeep[b] = nkeep;
+    w.narch[b] = carry_arch;
+    s.alpha_nspans[b] = carry_sp < P ? carry_sp : P;
+    s.alpha_rowcount[b] = nkeep;
+    atomicMax(s.alpha_count, nkeep);
+  }
+  __syncthreads();
+  // Archive rows in position order (stable).  Usually already sorted.
+  const int na = carry_arch;
+  int* arch = w.arch_idx + (size_t)b * g.NW;
+  __shared__ int unsorted;
+  if (tid == 0) unsorted = 0;
+  __syncthreads();
+  for (int i = tid + 1; i < na; i += nt)
+    if (token_position(g, s, w, b, arch[i - 1]) > token_position(g, s, w, b, arch[i])) unsorted = 1;
+  __syncthreads();
+  if (unsorted) {
+    int* tmp = ranked;  // reuse [NC] >= NW scratch in shared memory
+    for (int i = tid; i < na; i += nt) tmp[i] = arch[i];
+    __syncthreads();
+    for (int i = tid; i < na; i += nt) {
+      const int64_t pi = token_position(g, s, w, b, tmp[i]);
+      int rank = 0;
+      for (int j = 0; j < na; ++j) {
+        const int64_t pj = token_position(g, s, w, b, tmp[j]);
+        if (pj < pi || (pj == pi && j < i)) ++rank;
+      }
+      arch[rank] = tmp[i];
+    }
+  }
+}
+
+// ---------------------------------------------------------------- K7: pool rewrite
+template <typename T>
+__global__ void pool_rewrite_kernel(Geo g, logkv_state_t s, Work w) {
+  const int b = blockIdx.z, grp = blockIdx.y;
+  const int nkeep = w.nkeep[b];
+  T* kdst = static_cast<T*>(s.alpha_k_raw) + ((size_t)b * g.G + grp) * g.P * g.D;
+  T* vdst = static_cast<T*>(s.alpha_v) + ((size_t)b * g.G + grp) * g.P * g.D;
+  const T* snapk = static_cast<const T*>(w.snap_k);
+  const T* snapv = static_cast<const T*>(w.snap_v);
+  const T* reck = static_cast<const T*>(s.recent_k_raw);
+  const T* recv = static_cast<const T*>(s.recent_v);
+  const size_t total = (size_t)g.P * g.D;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int row = (int)(i / g.D), d = (int)(i % g.D);
+    if (row < nkeep) {
+      const int src = w.keep_idx[(size_t)b * g.P + row];
+      kdst[i] = cand_row<T>(g, s, w, snapk, reck, b, grp, src)[d];
+      vdst[i] = cand_row<T>(g, s, w, snapv, recv, b, grp, src)[d];
+    } else {
+      kdst[i] = Elem<T>::zero();
+      vdst[i] = Elem<T>::zero();
+    }
+  }
+  if (grp == 0 && blockIdx.x == 0) {
+    for (int row = threadIdx.x; row < g.P; row += blockDim.x) {
+      const bool kept = row < nkeep;
+      s.alpha_pos[(size_t)b * g.P + row] = kept ? token_position(g, s, w, b, w.keep_idx[(size_t)b * g.P + row]) : 0;
+      s.alpha_valid[(size_t)b * g.P + row] = kept ? 1 : 0;
+    }
+  }
+}
+
+}  // namespace logkv

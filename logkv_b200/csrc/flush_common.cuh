@@ -1,0 +1,85 @@
+// Geometry and workspace views shared by the flush kernels.
+#pragma once
+
+#include "common.cuh"
+
+namespace logkv {
+
+// Per-call constants (by value into every kernel).
+struct Geo {
+  int B, G, D, K, L, Bs;  // batch, KV groups, head dim, clusters, levels, slots per level
+  int cap2R;              // recent capacity (2 * recent_size)
+  int P;                  // exact pool capacity
+  int span_cap;           // alpha_span_max_tokens
+  int beta;               // Beta novelty + 4->2 merge
+  int F;                  // tokens flushed now
+  int NW;                 // token index space per batch row: P + F
+  int NC;                 // candidate capacity per row: P + F
+  int recent_count;       // window fill before the flush
+  int S;                  // ladder scratch rows per buffer per (b, g)
+  int sort_cap;           // power of two >= L * Bs + NW (delayed re-insert sort)
+  float eta, g0, lam;
+};
+
+enum JobType : int32_t { kJobNone = 0, kJobOrdinary = 1, kJobNew = 2, kJobLate = 3 };
+
+// Views into the caller's workspace (carved by the host in flush.cu).
+struct Work {
+  int32_t* status;
+  void* snap_k;            // [B,G,P,D] T  old pool snapshot
+  void* snap_v;
+  int64_t* snap_pos;       // [B,P]
+  int32_t* snap_rowcount;  // [B]
+  int32_t* cand_s0;        // [B,NC] first token range (start, count) of a candidate
+  int32_t* cand_n0;
+  int32_t* cand_s1;        // second range (old unfinished span continued by new tokens)
+  int32_t* cand_n1;
+  uint8_t* cand_flags;     // bit0 old, bit1 closed
+  int32_t* n_cand;         // [B]
+  float* scores;           // [B,NC]
+  int32_t* keep_idx;       // [B,P]  token indices kept in the pool, candidate order
+  int32_t* nkeep;          // [B]
+  int32_t* arch_idx;       // [B,NW] archived token indices, position order
+  int32_t* narch;          // [B]
+  int8_t* assign;          // [B,G,NW] cluster per archived token (position rank)
+  uint8_t* orphan;         // [B,G,NW]
+  float* s_winner;         // [B,G,NW]
+  int32_t* tok_list;       // [B,G,NW] archive ranks grouped by cluster (stable)
+  int32_t* plan_off;       // [B,G,K] offset into tok_list
+  int32_t* plan_n;         // [B,G,K] tokens joining the cluster
+  int32_t* plan_type;      // [B,G,K] JobType
+  int32_t* plan_m0;        // [B,G,K] level-0 stage rows
+  int32_t* plan_scr;       // [B,G,K] first scratch row of the cluster in its (b,g) region
+  int64_t* plan_base;      // [B,G,K] order of the first token row (level0_phase before the flush)
+  // Ladder scratch: [B*G][2][S] rows, structure of arrays.
+  void* sk;
+  void* sv;
+  float* sw;
+  int64_t* slo;
+  int64_t* shi;
+  int64_t* sswp;
+  int64_t* sord;
+  uint8_t* spad;
+  // Window staging for overlapping shifts: [B,G,2R,D] x3 + [B,2R] x2.
+  void* wk;
+  void* wkr;
+  void* wv;
+  int64_t* wpos;
+  uint8_t* wends;
+};
+
+// Position of token `src` of row b in [old pool | flush] index space.
+__device__ __forceinline__ int64_t token_position(const Geo& g, const logkv_state_t& s, const Work& w, int b,
+                                                  int src) {
+  return src < g.P ? w.snap_pos[(size_t)b * g.P + src] : s.recent_pos[(size_t)b * g.cap2R + (src - g.P)];
+}
+
+// Pointer to the D features of token `src` of (b, group) for a [pool | window] pair of sources.
+template <typename T>
+__device__ __forceinline__ const T* token_row(const Geo& g, const T* snap, const T* recent, int b, int grp,
+                                              int src) {
+  if (src < g.P) return snap + (((size_t)b * g.G + grp) * g.P + src) * g.D;
+  return recent + (((size_t)b * g.G + grp) * g.cap2R + (src - g.P)) * g.D;
+}
+
+}  // namespace logkv
