@@ -1,0 +1,363 @@
+"""Benchmark of the SemanticLogKV flush path on B200 (driver contract: one JSON line on rank 0).
+
+Workload (Qwen3-0.6B-shaped streaming prefill): 28 layer
+caches of 8 KV groups x head dim 128 (bf16), a 32768-token stream in 2048-token
+chunks, K=12 clusters, B=128 slots (B'=125 after the exact pool), recent window
+2048, flush granularity 2048, exact pool 256 tokens with 64-token spans, Beta on,
+mid anchors.  One step = the whole stream through all 28 layers: 16 add_recent
+calls per layer, 15 of which flush 2048 tokens (420 flushes per step), starting
+from empty caches.  Keys are synthetic (a seeded 12-component Gaussian mixture
+per layer and group with 5% far orphans; the model's projections are not part of
+the path); span boundaries every 23rd token.
+
+value     = device time per flush (chunk x layer), us, CUDA-graph replay of whole
+            steps with inputs resident in HBM (each step's 5.6 GB of chunk inputs is
+            larger than L2).
+e2e       = the same metric through the public API: add_recent called eagerly per
+            chunk and layer, with every chunk's K, pre-RoPE K and V copied from pinned
+            host memory inside the timed region and the cache's alpha_count read back.
+roofline  = the ladder cascade kernel (the dominant flush stage): algorithmic
+            bytes of its rows (549 B per bf16 row: K and V 256 B each, w 4 B,
+            p_lo/p_hi/sum_wp/order 8 B each, pad 1 B) over its CUDA-event time,
+            against the measured HBM copy bandwidth.
+--impl reference times the CPU oracle port (a numpy restatement of the
+reference's flush, single-threaded) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOAD = dict(workload="qwen3-0.6b streaming prefill flush (28 layers, 32K tokens, 2048-token flushes)",
+                layers=28, groups=8, head_dim=128, clusters=12, B=128, recent=2048, granularity=2048,
+                exact=256, span_cap=64, beta=True, tokens=32768, chunk=2048, batch_per_rank=1, dtype="bf16")
+ROW_BYTES = 256 + 256 + 4 + 4 * 8 + 1   # one bf16 ladder entry (13 fields, first-order subset)
+METRIC = "flush us per 2048-tok chunk/layer"
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            d = json.load(fh)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    def __init__(self, index: int):
+        self.index, self.samples, self.proc = index, [], None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 6:
+                self.samples.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[2 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------------------------- inputs
+def make_inputs(torch, cfg, device, seed):
+    """Per layer and chunk: k_raw, post-RoPE k and v (bf16, on device), plus the span-end table."""
+    from logkv_b200.workload import rope_tables
+    G, D, K, T, n_chunks = cfg["groups"], cfg["head_dim"], cfg["clusters"], cfg["chunk"], cfg["tokens"] // cfg["chunk"]
+    gen = torch.Generator(device=device).manual_seed(seed)
+    cos_np, sin_np = rope_tables(cfg["tokens"], D, base=1e6)
+    cos = torch.from_numpy(cos_np).to(device)
+    sin = torch.from_numpy(sin_np).to(device)
+    ends_row = [(i % 23) == 22 for i in range(T)]
+    ends_dev = torch.tensor([ends_row], dtype=torch.uint8, device=device)
+    layers = []
+    for layer in range(cfg["layers"]):
+        centres = torch.randn(G, K, D, generator=gen, device=device)
+        chunks = []
+        for c in range(n_chunks):
+            z = torch.randint(0, K, (G, T), generator=gen, device=device)
+            base = torch.gather(centres, 1, z[..., None].expand(-1, -1, D))
+            noise = torch.randn(G, T, D, generator=gen, device=device) * 0.3
+            orphan = torch.rand(G, T, generator=gen, device=device) < 0.05
+            u = torch.randn(G, T, D, generator=gen, device=device)
+            u = u / u.norm(dim=-1, keepdim=True) * (4 * 0.3 * D ** 0.5)
+            kr = torch.where(orphan[..., None], base + u, base + noise)[None]
+            pos = torch.arange(c * T, (c + 1) * T, device=device)
+            half = D // 2
+            rot = torch.cat([-kr[..., half:], kr[..., :half]], dim=-1)
+            k = kr * cos[pos] + rot * sin[pos]
+            v = torch.randn(1, G, T, D, generator=gen, device=device)
+            chunks.append((k.bfloat16().contiguous(), kr.bfloat16().contiguous(), v.bfloat16().contiguous()))
+        layers.append(chunks)
+    return layers, cos, sin, [ends_row], ends_dev
+
+
+def make_caches(torch, cfg, device, cos, sin):
+    from logkv_b200.cache import LogStructuredKVCache
+    caches = []
+    for _ in range(cfg["layers"]):
+        caches.append(LogStructuredKVCache(
+            (cfg["batch_per_rank"], cfg["groups"], cfg["tokens"], cfg["head_dim"]),
+            (cfg["batch_per_rank"], cfg["groups"], cfg["tokens"], cfg["head_dim"]),
+            B=cfg["B"], recent_size=cfg["recent"], device=device, dtype=torch.bfloat16,
+            cluster_k_max=cfg["clusters"], semantic_flush_granularity=cfg["granularity"],
+            semantic_centroid_backend="parallel", semantic_replay_updates=True,
+            alpha_exact_tokens=cfg["exact"], alpha_span_max_tokens=cfg["span_cap"],
+            beta_novelty=cfg["beta"], beta_adaptive_merge=cfg["beta"], cos_cache=cos, sin_cache=sin,
+            rope_n_elem=cfg["head_dim"]))
+    return caches
+
+
+def run_step(caches, layers, ends_host, ends_dev=None):
+    for cache in caches:
+        cache.reset_parameters()
+    n_chunks = len(layers[0])
+    for c in range(n_chunks):
+        for cache, chunks in zip(caches, layers):
+            k, kr, v = chunks[c]
+            cache.add_recent(k, v, k_raw=kr, span_ends=ends_host, span_ends_device=ends_dev)
+
+
+# ---------------------------------------------------------------------------------------------- our arm
+def bench_ours(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    cfg = dict(WORKLOAD)
+    layers, cos, sin, ends_host, ends_dev = make_inputs(torch, cfg, device, seed=1234 + rank)
+    caches = make_caches(torch, cfg, device, cos, sin)
+    flushes_per_step = cfg["layers"] * (cfg["tokens"] // cfg["chunk"] - cfg["recent"] // cfg["chunk"])
+    stream = torch.cuda.Stream(device)
+    # Warm-up (eager), then one CUDA graph per step.
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            run_step(caches, layers, ends_host, ends_dev)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        run_step(caches, layers, ends_host, ends_dev)
+    for _ in range(max(1, args.warmup)):
+        graph.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        stop.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(stop)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    us_per_flush = ms * 1000.0 / (args.steps * flushes_per_step)
+    ms_per_step = ms / args.steps
+
+    # Per-stage profile (eager, one step): stage events around every flush.
+    nstage = 10
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(nstage + 1)] for _ in range(flushes_per_step)]
+    for evs in events:
+        for e in evs:
+            e.record(stream)
+    torch.cuda.synchronize()
+    before = [c.read_counters() for c in caches]
+    stage_ms = [0.0] * nstage
+    with torch.cuda.stream(stream):
+        for cache in caches:
+            cache.reset_parameters()
+        idx = 0
+        for c in range(len(layers[0])):
+            for cache, chunks in zip(caches, layers):
+                k, kr, v = chunks[c]
+                will_flush = cache.recent_count + k.size(2) > cache.recent_size
+                cache.profile_events = events[idx] if will_flush else None
+                cache.add_recent(k, v, k_raw=kr, span_ends=ends_host, span_ends_device=ends_dev)
+                idx += 1 if will_flush else 0
+                cache.profile_events = None
+    torch.cuda.synchronize()
+    for evs in events:
+        for i in range(nstage):
+            stage_ms[i] += evs[i].elapsed_time(evs[i + 1])
+    after = [c.read_counters() for c in caches]
+    delta = {k: sum(a[k] - b[k] for a, b in zip(after, before)) for k in after[0]}
+    from logkv_b200._lib import FLUSH_STAGES
+    stages_us = {name: round(stage_ms[i] * 1000.0 / flushes_per_step, 2) for i, name in enumerate(FLUSH_STAGES)}
+    casc_rows = delta["storage_read"] + delta["stage_read"] + delta["survivor"] + delta["fill"] + delta["clear"] \
+        + delta["carry"]
+    casc_bytes_per_launch = casc_rows * ROW_BYTES / flushes_per_step
+    casc_s = stage_ms[FLUSH_STAGES.index("cascade")] / 1000.0 / flushes_per_step
+    peak, peak_kind = measured_peaks()
+    achieved = casc_bytes_per_launch / casc_s / 1e9
+    # Whole-flush algorithmic bytes (ladder rows + Alpha/route reads of [pool|flush] K,V + pool rewrite).
+    e = 2
+    P, F, G, D = cfg["exact"], cfg["granularity"], cfg["groups"], cfg["head_dim"]
+    flush_rows = delta["storage_read"] + delta["stage_read"] + delta["survivor"] + delta["fill"] + delta["clear"]
+    flush_bytes = flush_rows * ROW_BYTES / flushes_per_step + (P + F) * G * D * 2 * e + P * G * D * 2 * e
+    flush_achieved = flush_bytes / (us_per_flush * 1e-6) / 1e9
+
+    # e2e: public API, eager, host inputs copied each chunk.
+    host = []
+    for chunks in layers:
+        host.append([tuple(t[:, :, :].cpu().pin_memory() for t in chunks[c]) for c in range(2)])
+    dev_buf = [tuple(torch.empty_like(t) for t in layers[0][0]) for _ in range(2)]
+    h2d_per_step = sum(t.numel() * t.element_size() for t in layers[0][0]) * len(layers) * len(layers[0])
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e_start.record(stream)
+        for _ in range(args.steps):
+            for cache in caches:
+                cache.reset_parameters()
+            for c in range(len(layers[0])):
+                for li, cache in enumerate(caches):
+                    buf = dev_buf[c % 2]
+                    for d, h in zip(buf, host[li][c % 2]):
+                        d.copy_(h, non_blocking=True)
+                    cache.add_recent(buf[0], buf[2], k_raw=buf[1], span_ends=ends_host)
+            readback = caches[-1]._alpha_count_dev.to("cpu", non_blocking=False)
+        e_stop.record(stream)
+    torch.cuda.synchronize()
+    e_ms = e_start.elapsed_time(e_stop)
+    if world > 1:
+        t = torch.tensor([e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+    e2e_us = e_ms * 1000.0 / (args.steps * flushes_per_step)
+    del readback
+    n_launch = flushes_per_step * 10 * args.steps
+    return dict(value=us_per_flush * 1.0 / world, ms_per_step=ms_per_step, e2e_us=e2e_us / world,
+                h2d=h2d_per_step * world, stages=stages_us, counters=delta, flushes_per_step=flushes_per_step,
+                roofline={"bound": "hbm", "kernel": "cascade_kernel", "achieved": round(achieved, 1),
+                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                          "traffic": None, "bytes_per_launch": round(casc_bytes_per_launch)},
+                flush_roofline={"achieved": round(flush_achieved, 1), "unit": "GB/s",
+                                "frac": round(flush_achieved / peak, 4), "bytes_per_flush": round(flush_bytes)},
+                clocks=clocks.summary(), launches=n_launch)
+
+
+# ---------------------------------------------------------------------------------------------- CPU leg
+def cpu_flush_sample(n_flushes: int = 3, seed: int = 7):
+    """Time the oracle port on flushes of one layer of the same shape (single thread)."""
+    from logkv_b200.workload import MixtureKeys, boundary_pattern
+    from oracle.cache import OracleCache
+    cfg = WORKLOAD
+    rng = np.random.default_rng(seed)
+    G, D, T = cfg["groups"], cfg["head_dim"], cfg["chunk"]
+    mix = MixtureKeys(rng, G, D, cfg["clusters"])
+    oc = OracleCache(batch=1, groups=G, max_seq=cfg["tokens"], dim=D, B=cfg["B"], recent=cfg["recent"],
+                     clusters=cfg["clusters"], granularity=cfg["granularity"], exact=cfg["exact"],
+                     span_cap=cfg["span_cap"], beta=cfg["beta"], dtype="bf16")
+    times = []
+    for c in range(n_flushes + 1):
+        kr = mix.draw(1, T)
+        v = rng.standard_normal((1, G, T, D)).astype(np.float32)
+        pos = np.arange(c * T, (c + 1) * T)[None]
+        ends = boundary_pattern(rng, 1, T, "mod23")
+        t = time.perf_counter()
+        oc.add_recent(kr, v, kr, pos, ends)
+        if c:
+            times.append(time.perf_counter() - t)
+    return statistics.median(times) * 1e6, n_flushes
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-flushes", type=int, default=3)
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    config = {k: WORKLOAD[k] for k in ("workload", "layers", "groups", "head_dim", "clusters", "B", "recent",
+                                        "granularity", "exact", "span_cap", "tokens", "batch_per_rank")}
+    config.update(parallelism=f"batch-sharded streams x{world}", l2="inputs larger than L2 (5.6 GB per step)")
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        us, n = cpu_flush_sample(args.cpu_flushes)
+        line = dict(metric=METRIC, value=round(us, 1), unit="us", n_gpus=args.gpus, steps=args.steps,
+                    warmup=args.warmup, ms_per_step=round(us * 420 / 1000.0, 1), higher_is_better=False,
+                    scaling="weak", vs_baseline=None, dtype="bf16", data="synthetic", config=config,
+                    impl="reference",
+                    cpu_baseline={"value": round(us, 1), "unit": "us", "cores": 1, "kind": "port",
+                                  "sample": f"median of {n} flushes of one 0.6B-shaped layer (oracle/, numpy)"},
+                    e2e={"value": round(us, 1), "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
+        print(json.dumps(line), flush=True)
+        return
+    import torch
+    import torch.distributed as dist
+    from logkv_b200 import build as _build
+    if rank == 0 and not os.path.exists(os.path.join(ROOT, "logkv_b200", "liblogkv_b200.so")):
+        _build.build()
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    res = bench_ours(args, rank, world, local_rank)
+    cpu = None
+    if rank == 0 and world == 1:
+        us, n = cpu_flush_sample(args.cpu_flushes)
+        cpu = {"value": round(us, 1), "unit": "us", "cores": 1, "kind": "port",
+               "sample": f"median of {n} flushes of one 0.6B-shaped layer (oracle/, numpy, 1 thread)"}
+    if rank == 0:
+        line = dict(metric=METRIC, value=round(res["value"], 2), unit="us", n_gpus=world, steps=args.steps,
+                    warmup=args.warmup, ms_per_step=round(res["ms_per_step"], 3), higher_is_better=False,
+                    scaling="weak", vs_baseline=None, dtype="bf16", data="synthetic", config=config,
+                    e2e={"value": round(res["e2e_us"], 2), "unit": "us", "h2d_bytes_per_step": res["h2d"],
+                         "d2h_bytes_per_step": 4},
+                    roofline=res["roofline"], flush_roofline=res["flush_roofline"], cpu_baseline=cpu,
+                    clocks=res["clocks"], gpu_launches=res["launches"], stages_us=res["stages"],
+                    flushes_per_step=res["flushes_per_step"])
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

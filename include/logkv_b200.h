@@ -117,6 +117,29 @@ LOGKV_API int logkv_flush(const logkv_layout_t* layout, const logkv_state_t* sta
 /* Copy the workspace status word to *out (synchronizes `stream`); nonzero = a capacity was exceeded. */
 LOGKV_API int logkv_read_status(const void* workspace, int32_t* out, void* stream);
 
+/*
+ * Measurement helpers (no reference counterpart; the reference times stages
+ * with host counters and optional CUDA events, litgpt/log_kv_timing.py:15-50).
+ * logkv_flush_profiled is logkv_flush plus one cudaEventRecord (events are
+ * cudaEvent_t as void*) before the first and after each of the
+ * LOGKV_FLUSH_STAGES kernels stages: snapshot, span cut, span score, choose,
+ * attach, plan, prepare, cascade, pool rewrite, window shift.
+ */
+#define LOGKV_FLUSH_STAGES 10
+LOGKV_API int logkv_flush_profiled(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                   int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream,
+                                   void** events, int32_t n_events);
+
+/*
+ * Copy up to n of the workspace's row counters (accumulated over every flush
+ * since the workspace was zeroed) to out, synchronizing `stream`: [0] stored
+ * level rows read, [1] incoming rows read, [2] survivor rows written, [3] rows
+ * appended, [4] rows zeroed, [5] merged rows carried up, [6] rows gathered for
+ * delayed re-inserts, [7] flushes.  The workspace must be zero-filled once
+ * when it is allocated.
+ */
+LOGKV_API int logkv_read_counters(const void* workspace, uint64_t* out, int32_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

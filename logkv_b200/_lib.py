@@ -20,6 +20,10 @@ ERRORS = {-1: "shape out of the supported range", -2: "unsupported storage dtype
 
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1}
 
+FLUSH_STAGES = ("snapshot", "span_cut", "span_score", "choose", "attach", "plan", "prepare", "cascade",
+                "pool_rewrite", "window_shift")
+COUNTERS = ("storage_read", "stage_read", "survivor", "fill", "clear", "carry", "gather", "flushes")
+
 
 class Layout(ctypes.Structure):
     _fields_ = [("batch", ctypes.c_int32), ("groups", ctypes.c_int32), ("dim", ctypes.c_int32),
@@ -57,6 +61,13 @@ def lib() -> ctypes.CDLL:
                                        ctypes.c_int32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
         handle.logkv_read_status.restype = ctypes.c_int
         handle.logkv_read_status.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), ctypes.c_void_p]
+        handle.logkv_flush_profiled.restype = ctypes.c_int
+        handle.logkv_flush_profiled.argtypes = [ctypes.POINTER(Layout), ctypes.POINTER(State), ctypes.c_int32,
+                                                ctypes.c_int32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                                                ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32]
+        handle.logkv_read_counters.restype = ctypes.c_int
+        handle.logkv_read_counters.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int32,
+                                               ctypes.c_void_p]
         _lib = handle
     return _lib
 

@@ -183,8 +183,9 @@ class LogStructuredKVCache(nn.Module):
         nbytes = _lib.lib().logkv_flush_workspace_bytes(ctypes.byref(self._layout), self.semantic_flush_granularity)
         if not nbytes:
             raise ValueError("cache geometry is outside the supported range of the flush kernels")
-        self._workspace = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        self._workspace = torch.zeros(nbytes, dtype=torch.uint8, device=device)
         self._state = None
+        self.profile_events = None   # set to a list of LOGKV_FLUSH_STAGES+1 torch.cuda.Event to time stages
 
     # ------------------------------------------------------------------ C-ABI state
     def _state_struct(self) -> _lib.State:
@@ -203,10 +204,23 @@ class LogStructuredKVCache(nn.Module):
     def flush_device(self, take: int) -> None:
         """One device flush of the ``take`` oldest window tokens plus the window shift."""
         state = self._state_struct()
-        code = _lib.lib().logkv_flush(ctypes.byref(self._layout), ctypes.byref(state), int(take),
-                                      int(self.recent_count), ctypes.c_void_p(self._workspace.data_ptr()),
-                                      self._workspace.numel(), ctypes.c_void_p(_lib.stream_ptr(self.level_k.device)))
-        _lib.check(code, "logkv_flush")
+        args = (ctypes.byref(self._layout), ctypes.byref(state), int(take), int(self.recent_count),
+                ctypes.c_void_p(self._workspace.data_ptr()), self._workspace.numel(),
+                ctypes.c_void_p(_lib.stream_ptr(self.level_k.device)))
+        if self.profile_events is None:
+            _lib.check(_lib.lib().logkv_flush(*args), "logkv_flush")
+            return
+        events = (ctypes.c_void_p * len(self.profile_events))(*[e.cuda_event for e in self.profile_events])
+        _lib.check(_lib.lib().logkv_flush_profiled(*args, events, len(self.profile_events)), "logkv_flush_profiled")
+
+    def read_counters(self) -> dict:
+        """Row counters accumulated by every flush of this cache (synchronizes)."""
+        out = (ctypes.c_uint64 * len(_lib.COUNTERS))()
+        _lib.check(_lib.lib().logkv_read_counters(ctypes.c_void_p(self._workspace.data_ptr()), out,
+                                                  len(_lib.COUNTERS),
+                                                  ctypes.c_void_p(_lib.stream_ptr(self.level_k.device))),
+                   "logkv_read_counters")
+        return dict(zip(_lib.COUNTERS, (int(x) for x in out)))
 
     def read_status(self) -> int:
         out = ctypes.c_int32(0)
@@ -234,8 +248,15 @@ class LogStructuredKVCache(nn.Module):
             return input_pos.to(device=dev, dtype=torch.int64), [[int(x) for x in r] for r in input_pos.tolist()]
         raise ValueError(f"input_pos must be 1-D or 2-D, got shape {tuple(input_pos.shape)}")
 
-    def add_recent(self, k, v, *, k_raw=None, input_pos=None, record_op_log=False, span_ends=None, **replay):
-        """Append a chunk to the window; flush ``semantic_flush_granularity`` blocks on overflow."""
+    def add_recent(self, k, v, *, k_raw=None, input_pos=None, record_op_log=False, span_ends=None,
+                   span_ends_device=None, **replay):
+        """Append a chunk to the window; flush ``semantic_flush_granularity`` blocks on overflow.
+
+        ``span_ends`` is the reference's host list of per-row boundary flags.
+        ``span_ends_device`` (optional, uint8 [B, n] on the cache device) holds
+        the same flags already on the device, so the call issues no host-to-device
+        copy and can be captured in a CUDA graph.
+        """
         if k_raw is None:
             raise ValueError("semantic LogKV add_recent requires pre-RoPE k_raw")
         if record_op_log or any(v_ is not None for v_ in replay.values()):
@@ -260,8 +281,11 @@ class LogStructuredKVCache(nn.Module):
         self.recent_k_raw[:, :, dst] = k_raw
         self.recent_v[:, :, dst] = v
         self.recent_pos[:, dst] = positions
-        ends = torch.tensor(span_ends, dtype=torch.uint8)
-        self._recent_ends[:, dst].copy_(ends.pin_memory() if self.recent_pos.is_cuda else ends, non_blocking=True)
+        if span_ends_device is not None:
+            self._recent_ends[:, dst].copy_(span_ends_device)
+        else:
+            ends = torch.tensor(span_ends, dtype=torch.uint8)
+            self._recent_ends[:, dst].copy_(ends.pin_memory() if self.recent_pos.is_cuda else ends, non_blocking=True)
         for b in range(self.batch_size):
             self._recent_pos_host[b][dst] = positions_host[b]
             self._recent_span_ends[b][dst] = [bool(x) for x in span_ends[b]]

@@ -148,6 +148,7 @@ static size_t carve(const Geo& g, size_t esize, char* base, Work* w) {
   Carver c{base};
   const size_t B = g.B, G = g.G, D = g.D, K = g.K, P = g.P, NC = g.NC, NW = g.NW, S = g.S;
   w->status = c.take<int32_t>(1, 4);
+  w->counters = c.take<unsigned long long>(kNumCounters, 8);
   w->snap_k = c.take<char>(B * G * P * D, esize);
   w->snap_v = c.take<char>(B * G * P * D, esize);
   w->snap_pos = c.take<int64_t>(B * P, 8);
@@ -202,35 +203,47 @@ static int validate(const logkv_layout_t* L, int F) {
 }
 
 template <typename T>
-static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st) {
-  const dim3 rows3(1, g.G, g.B);
+static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st, cudaEvent_t* ev) {
+  int stage = 0;
+  auto mark = [&]() {
+    if (ev) cudaEventRecord(ev[stage], st);
+    ++stage;
+  };
   const int sm_count = 148;
   const int per_bg = std::max(1, std::min(64, (g.P * g.D + 255) / 256));
+  mark();
   snapshot_kernel<T><<<dim3(per_bg, g.G, g.B), 256, 0, st>>>(g, s, w);
+  mark();
   const size_t cut_smem = 2 * (size_t)g.F * sizeof(int);
   if (cut_smem > 48 * 1024) cudaFuncSetAttribute(alpha_cut_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cut_smem);
   alpha_cut_kernel<<<g.B, 1024, cut_smem, st>>>(g, s, w);
+  mark();
   const size_t score_smem = (2 * (size_t)g.G * g.D + (size_t)g.G * 256 + 6 * (size_t)g.G) * sizeof(float);
   if (score_smem > 48 * 1024)
     cudaFuncSetAttribute(alpha_score_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)score_smem);
   const int score_blocks = std::max(1, std::min(g.NC, 2 * sm_count / std::max(1, g.B) + 1));
   alpha_score_kernel<T><<<dim3(score_blocks, g.B), 256, score_smem, st>>>(g, s, w);
+  mark();
   const size_t choose_smem = (size_t)g.NC * (8 + 4 * 4 + 2);
   if (choose_smem > 48 * 1024)
     cudaFuncSetAttribute(alpha_choose_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)choose_smem);
   alpha_choose_kernel<<<g.B, 1024, choose_smem, st>>>(g, s, w);
+  mark();
   const size_t attach_smem = ((size_t)g.K * g.D + 128 * (size_t)(g.D + 1)) * sizeof(float);
   if (attach_smem > 48 * 1024)
     cudaFuncSetAttribute(attach_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attach_smem);
   attach_kernel<T><<<dim3((g.NW + 127) / 128, g.G, g.B), 128, attach_smem, st>>>(g, s, w);
+  mark();
   const size_t plan_smem = (size_t)g.NW * sizeof(float);
   if (plan_smem > 48 * 1024)
     cudaFuncSetAttribute(plan_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan_smem);
   plan_kernel<T><<<dim3(g.G, g.B), 1024, plan_smem, st>>>(g, s, w);
+  mark();
   const size_t prep_smem = (size_t)g.sort_cap * sizeof(unsigned long long);
   if (prep_smem > 48 * 1024)
     cudaFuncSetAttribute(prepare_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
   prepare_kernel<T><<<dim3(g.K, g.G, g.B), 256, prep_smem, st>>>(g, s, w);
+  mark();
   const size_t casc_smem = 2 * (size_t)g.Bs * g.D * sizeof(T) + (size_t)g.Bs * sizeof(Meta) + 16;
   if (g.beta) {
     if (casc_smem > 48 * 1024)
@@ -241,14 +254,34 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
       cudaFuncSetAttribute(cascade_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)casc_smem);
     cascade_kernel<T, false><<<dim3(g.K, g.G, g.B), 256, casc_smem, st>>>(g, s, w);
   }
+  mark();
   pool_rewrite_kernel<T><<<dim3(per_bg, g.G, g.B), 256, 0, st>>>(g, s, w);
+  mark();
   const int rem = g.recent_count - g.F;
   const int per_win = std::max(1, std::min(128, (g.recent_count * g.D + 255) / 256));
   const int staged = rem > g.F ? 1 : 0;
   if (staged) window_stage_kernel<T><<<dim3(per_win, g.G, g.B), 256, 0, st>>>(g, s, w, rem);
   window_shift_kernel<T><<<dim3(per_win, g.G, g.B), 256, 0, st>>>(g, s, w, rem, staged);
-  (void)rows3;
+  mark();
   return (int)cudaGetLastError();
+}
+
+static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                     int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream, cudaEvent_t* ev) {
+  const int v = validate(layout, flush_tokens);
+  if (v != LOGKV_OK) return v;
+  if (!state || !workspace) return LOGKV_E_POINTER;
+  if (recent_count < flush_tokens || recent_count > layout->recent_capacity) return LOGKV_E_SHAPE;
+  const size_t esize = layout->dtype == LOGKV_DTYPE_BF16 ? 2 : 4;
+  const Geo g = make_geo(*layout, flush_tokens, recent_count);
+  Work w{};
+  const size_t need = carve(g, esize, static_cast<char*>(workspace), &w);
+  if (workspace_bytes < need) return LOGKV_E_WORKSPACE;
+  const size_t casc_smem = 2 * (size_t)g.Bs * g.D * esize + (size_t)g.Bs * sizeof(Meta) + 16;
+  if (casc_smem > 227 * 1024 || (size_t)g.sort_cap * 8 > 227 * 1024) return LOGKV_E_SMEM;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (layout->dtype == LOGKV_DTYPE_BF16) return launch_flush<__nv_bfloat16>(g, *state, w, st, ev);
+  return launch_flush<float>(g, *state, w, st, ev);
 }
 
 }  // namespace logkv
@@ -264,26 +297,31 @@ extern "C" size_t logkv_flush_workspace_bytes(const logkv_layout_t* layout, int3
 
 extern "C" int logkv_flush(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
                            int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream) {
-  const int v = validate(layout, flush_tokens);
-  if (v != LOGKV_OK) return v;
-  if (!state || !workspace) return LOGKV_E_POINTER;
-  if (recent_count < flush_tokens || recent_count > layout->recent_capacity) return LOGKV_E_SHAPE;
-  const size_t esize = layout->dtype == LOGKV_DTYPE_BF16 ? 2 : 4;
-  const Geo g = make_geo(*layout, flush_tokens, recent_count);
-  Work w{};
-  const size_t need = carve(g, esize, static_cast<char*>(workspace), &w);
-  if (workspace_bytes < need) return LOGKV_E_WORKSPACE;
-  const size_t casc_smem = 2 * (size_t)g.Bs * g.D * esize + (size_t)g.Bs * sizeof(Meta) + 16;
-  if (casc_smem > 227 * 1024 || (size_t)g.sort_cap * 8 > 227 * 1024) return LOGKV_E_SMEM;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (layout->dtype == LOGKV_DTYPE_BF16) return launch_flush<__nv_bfloat16>(g, *state, w, st);
-  return launch_flush<float>(g, *state, w, st);
+  return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream, nullptr);
+}
+
+extern "C" int logkv_flush_profiled(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                    int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream,
+                                    void** events, int32_t n_events) {
+  if (!events || n_events < LOGKV_FLUSH_STAGES + 1) return LOGKV_E_POINTER;
+  return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream,
+                   reinterpret_cast<cudaEvent_t*>(events));
 }
 
 extern "C" int logkv_read_status(const void* workspace, int32_t* out, void* stream) {
   if (!workspace || !out) return LOGKV_E_POINTER;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaMemcpyAsync(out, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  return (int)e;
+}
+
+extern "C" int logkv_read_counters(const void* workspace, uint64_t* out, int32_t n, void* stream) {
+  if (!workspace || !out || n < 1) return LOGKV_E_POINTER;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int m = n < kNumCounters ? n : kNumCounters;
+  cudaError_t e = cudaMemcpyAsync(out, static_cast<const char*>(workspace) + 256, m * sizeof(uint64_t),
+                                  cudaMemcpyDeviceToHost, st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   return (int)e;
 }

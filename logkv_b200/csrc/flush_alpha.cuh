@@ -33,6 +33,7 @@ __global__ void snapshot_kernel(Geo g, logkv_state_t s, Work w) {
       if (b == 0) {
         *w.status = 0;
         *s.alpha_count = 0;
+        w.counters[kCntFlushes] += 1ull;
       }
     }
   }

@@ -23,9 +23,23 @@ struct Geo {
 
 enum JobType : int32_t { kJobNone = 0, kJobOrdinary = 1, kJobNew = 2, kJobLate = 3 };
 
+// Traffic counters (rows) accumulated across flushes in the workspace.
+enum Counter : int {
+  kCntStorageRead = 0,   // stored level rows loaded for an overflowing level
+  kCntStageRead = 1,     // incoming rows read (tokens, carries, staged re-inserts)
+  kCntSurvivor = 2,      // survivor rows written
+  kCntFill = 3,          // rows appended without overflow
+  kCntClear = 4,         // rows zeroed (level tails, cleared clusters)
+  kCntCarry = 5,         // merged rows written for the next level
+  kCntGather = 6,        // rows gathered for delayed re-inserts
+  kCntFlushes = 7,       // flush calls
+  kNumCounters = 8,
+};
+
 // Views into the caller's workspace (carved by the host in flush.cu).
 struct Work {
   int32_t* status;
+  unsigned long long* counters;  // [kNumCounters]
   void* snap_k;            // [B,G,P,D] T  old pool snapshot
   void* snap_v;
   int64_t* snap_pos;       // [B,P]

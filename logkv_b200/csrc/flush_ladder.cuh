@@ -289,6 +289,10 @@ __global__ void __launch_bounds__(256) prepare_kernel(Geo g, logkv_state_t s, Wo
     s.pad_mask[row] = 0;
   }
   for (int l = tid; l < g.L; l += nt) s.level_count[x.lane * g.L + l] = 0;
+  if (tid == 0) {
+    atomicAdd(&w.counters[kCntClear], (unsigned long long)rows);
+    if (type == kJobLate) atomicAdd(&w.counters[kCntGather], (unsigned long long)(e + n));
+  }
 }
 
 // ---------------------------------------------------------------- K6b: cascade
@@ -328,7 +332,11 @@ __global__ void __launch_bounds__(256) cascade_kernel(Geo g, logkv_state_t s, Wo
         LV[row * D + d] = x.stage_v(st, i)[d];
       }
       for (int i = tid; i < m; i += nt) x.put_level_meta(x.level_row(ell, cnt + i), x.stage_meta(st, i));
-      if (tid == 0) s.level_count[x.lane * g.L + ell] = (int16_t)(cnt + m);
+      if (tid == 0) {
+        s.level_count[x.lane * g.L + ell] = (int16_t)(cnt + m);
+        atomicAdd(&w.counters[kCntStageRead], (unsigned long long)m);
+        atomicAdd(&w.counters[kCntFill], (unsigned long long)m);
+      }
       break;
     }
     // Overflow: stage the stored rows, then rewrite the whole level.
@@ -371,6 +379,9 @@ __global__ void __launch_bounds__(256) cascade_kernel(Geo g, logkv_state_t s, Wo
         for (int t = 1; t <= rem; ++t) acc = merge_meta(acc, pool_m(t));
         x.put_level_meta(lrow0, acc);
         s.level_count[x.lane * g.L + ell] = (int16_t)Bs;
+        atomicAdd(&w.counters[kCntStorageRead], (unsigned long long)cnt);
+        atomicAdd(&w.counters[kCntStageRead], (unsigned long long)m);
+        atomicAdd(&w.counters[kCntSurvivor], (unsigned long long)Bs);
       }
       for (int item = tid; item < (Bs - 1) * D; item += nt) {
         const int slot = 1 + item / D, d = item % D;
@@ -553,7 +564,14 @@ __global__ void __launch_bounds__(256) cascade_kernel(Geo g, logkv_state_t s, Wo
         x.put_level_meta(lrow0 + slot, Meta{0.f, 0, 0, 0, 0, 0});
       }
     }
-    if (tid == 0) s.level_count[x.lane * g.L + ell] = (int16_t)nsurv;
+    if (tid == 0) {
+      s.level_count[x.lane * g.L + ell] = (int16_t)nsurv;
+      atomicAdd(&w.counters[kCntStorageRead], (unsigned long long)cnt);
+      atomicAdd(&w.counters[kCntStageRead], (unsigned long long)m);
+      atomicAdd(&w.counters[kCntSurvivor], (unsigned long long)nsurv);
+      atomicAdd(&w.counters[kCntClear], (unsigned long long)(Bs - nsurv));
+      atomicAdd(&w.counters[kCntCarry], (unsigned long long)ncarry);
+    }
     __syncthreads();
     st.kind = 1;
     st.buf = nb;

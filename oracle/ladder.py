@@ -187,20 +187,89 @@ def beta_apply(g: Rows, width: int, cut: int) -> Rows:
                 np.asarray([o[6] for o in outs], np.int64), np.asarray([o[7] for o in outs], bool))
 
 
+def _grouped(x: np.ndarray, n: int, fill=0):
+    """Pad a per-row array of one lane to [ceil(n/4), 4, ...] groups."""
+    ng = (n + 3) // 4
+    out = np.full((ng * 4,) + x.shape[1:], fill, dtype=x.dtype)
+    out[:n] = x[:n]
+    return out.reshape((ng, 4) + x.shape[1:])
+
+
+def beta_costs_all(rows: Rows) -> np.ndarray:
+    """Costs [groups, 3] for cuts (2, 1, 3) of every group of one lane (vectorised beta_cost_cut)."""
+    n = len(rows)
+    w = _grouped(rows.w, n)                                   # [NG, 4]
+    width = np.minimum(4, n - 4 * np.arange(w.shape[0]))
+    valid = np.arange(4)[None, :] < width[:, None]
+    total = np.maximum(seq_sum(w.T), F32(1e-12))             # [NG]
+    costs = np.zeros((w.shape[0], 3), F32)
+    offs = np.arange(4)[None, :]
+    for xr in (rows.k, rows.v):
+        x = _grouped(xr, n)                                   # [NG, 4, D]
+        energy = np.maximum((seq_sum((dsum(x * x) * w).T) / total).astype(F32), F32(1e-12))
+        for j, cut in enumerate((2, 1, 3)):
+            left = valid & (offs < cut)
+            for mask in (left, valid & ~left):
+                om = (w * mask).astype(F32)                   # [NG, 4]
+                den = np.maximum(seq_sum(om.T), F32(1e-12))   # [NG]
+                mean = (seq_sum(np.moveaxis(x * om[..., None], 1, 0)) / den[:, None]).astype(F32)   # [NG, D]
+                loss = seq_sum((dsum((x - mean[:, None, :]) ** 2) * om).T)                        # [NG]
+                costs[:, j] = (costs[:, j] + (loss / energy).astype(F32)).astype(F32)
+    return costs
+
+
 def beta_merge(rows: Rows, cuts=None) -> tuple[Rows, np.ndarray]:
-    """One lane's pair rows -> half as many entries via Beta groups (merge_blocks, :95-105)."""
-    layout = beta_layout([len(rows)])
-    chosen = np.zeros(len(layout), np.uint8)
-    parts = []
-    for gi, (start, width, _dst) in enumerate(layout):
-        group = rows.take(slice(int(start), int(start + width)))
-        cut = int(cuts[gi]) if cuts is not None else beta_cost_cut(group, int(width))[0]
-        chosen[gi] = cut
-        parts.append(beta_apply(group, int(width), cut))
-    out = parts[0] if parts else Rows.empty(rows.k.shape[1], rows.v.shape[1])
-    for p in parts[1:]:
-        out = Rows.cat(out, p)
-    return out, chosen
+    """One lane's pair rows -> half as many entries via Beta groups (merge_blocks, :95-105).
+
+    All groups are evaluated at once with the same left-to-right sums as
+    ``beta_cost_cut`` / ``beta_apply``.
+    """
+    n = len(rows)
+    if n == 0:
+        return Rows.empty(rows.k.shape[1], rows.v.shape[1]), np.zeros(0, np.uint8)
+    ng = (n + 3) // 4
+    width = np.minimum(4, n - 4 * np.arange(ng))
+    if cuts is None:
+        costs = beta_costs_all(rows)
+        chosen = np.asarray((2, 1, 3), np.uint8)[np.argmin(costs, axis=1)]
+        chosen = np.where(width == 2, np.uint8(1), chosen).astype(np.uint8)
+    else:
+        chosen = np.asarray(cuts, np.uint8)
+    w = _grouped(rows.w, n)
+    k4, v4 = _grouped(rows.k, n), _grouped(rows.v, n)
+    lo4, hi4 = _grouped(rows.lo, n), _grouped(rows.hi, n)
+    swp4, ord4 = _grouped(rows.swp, n), _grouped(rows.order, n)
+    pad4 = _grouped(rows.pad, n, fill=True)
+    valid = np.arange(4)[None, :] < width[:, None]
+    offs = np.arange(4)[None, :]
+    cut = chosen.astype(np.int64)[:, None]
+    sides = []
+    for side in (0, 1):
+        if side == 0:
+            mask = np.where((width == 2)[:, None], valid, valid & (offs < cut))
+        else:
+            mask = np.where((width == 2)[:, None], False, valid & (offs >= cut))
+        om = (w * mask).astype(F32)
+        mass = seq_sum(om.T)
+        den = np.maximum(mass, F32(1e-12))
+        kk = (seq_sum(np.moveaxis(k4 * om[..., None], 1, 0)) / den[:, None]).astype(F32)
+        vv = (seq_sum(np.moveaxis(v4 * om[..., None], 1, 0)) / den[:, None]).astype(F32)
+        live = mask & (w > 0)
+        lo = np.where(mass > 0, np.min(np.where(live, lo4, I64MAX), axis=1), 0)
+        hi = np.where(mass > 0, np.max(np.where(live, hi4, I64MIN), axis=1), 0)
+        swp = np.sum(np.where(mask, swp4, 0), axis=1)
+        order = np.min(np.where(mask, ord4, I64MAX), axis=1)
+        pad = np.all(pad4 | ~mask, axis=1)
+        sides.append((kk, vv, mass, lo, hi, swp, order, pad))
+    # Interleave left/right per group; width-2 groups emit only the left entry.
+    keep_right = width == 4
+    fields = []
+    for f in range(8):
+        left, right = sides[0][f], sides[1][f]
+        inter = np.stack([left, right], axis=1).reshape((2 * ng,) + left.shape[1:])
+        sel = np.stack([np.ones(ng, bool), keep_right], axis=1).reshape(-1)
+        fields.append(inter[sel])
+    return Rows(*fields), chosen
 
 
 class Ladder:

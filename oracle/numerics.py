@@ -49,10 +49,11 @@ def dsum(x: np.ndarray) -> np.ndarray:
     agree bit for bit on every distance, energy and cost.
     """
     x = np.asarray(x, dtype=np.float32)
-    acc = np.zeros(x.shape[:-1], dtype=np.float32)
-    for d in range(x.shape[-1]):
-        acc = (acc + x[..., d]).astype(np.float32)
-    return acc
+    if x.shape[-1] == 0:
+        return np.zeros(x.shape[:-1], dtype=np.float32)
+    # ufunc.accumulate is evaluated strictly left to right in float32; +0.0 added
+    # first changes nothing but the sign of an all-negative-zero sum.
+    return (np.add.accumulate(x, axis=-1, dtype=np.float32)[..., -1] + np.float32(0.0)).astype(np.float32)
 
 
 def ddot(a: np.ndarray, b: np.ndarray) -> np.ndarray:
@@ -66,7 +67,7 @@ def seq_sum(rows: np.ndarray) -> np.ndarray:
     Matches ``torch.segment_reduce(..., 'sum')`` and reductions over a short
     non-innermost axis on CPU, both of which accumulate in index order.
     """
-    acc = np.zeros(rows.shape[1:], dtype=np.float32)
-    for r in rows:
-        acc = (acc + r).astype(np.float32)
-    return acc
+    rows = np.asarray(rows, dtype=np.float32)
+    if rows.shape[0] == 0:
+        return np.zeros(rows.shape[1:], dtype=np.float32)
+    return (np.float32(0.0) + np.add.accumulate(rows, axis=0, dtype=np.float32)[-1]).astype(np.float32)
