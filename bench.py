@@ -162,6 +162,7 @@ def bench_ours(args, rank, world, local_rank):
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     cfg = dict(WORKLOAD)
+    cfg["layers"] = args.layers
     layers, cos, sin, ends_host, ends_dev = make_inputs(torch, cfg, device, seed=1234 + rank)
     caches = make_caches(torch, cfg, device, cos, sin)
     flushes_per_step = cfg["layers"] * (cfg["tokens"] // cfg["chunk"] - cfg["recent"] // cfg["chunk"])
@@ -174,18 +175,20 @@ def bench_ours(args, rank, world, local_rank):
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         run_step(caches, layers, ends_host, ends_dev)
-    for _ in range(max(1, args.warmup)):
-        graph.replay()
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup)):
+            graph.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clocks:
         torch.cuda.synchronize()
-        start.record(stream)
-        for _ in range(args.steps):
-            graph.replay()
-        stop.record(stream)
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            stop.record(stream)
         torch.cuda.synchronize()
     ms = start.elapsed_time(stop)
     if world > 1:
@@ -310,14 +313,16 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--cpu-flushes", type=int, default=3)
+    ap.add_argument("--cpu-flushes", type=int, default=3, help="oracle flushes timed for cpu_baseline (0: skip)")
+    ap.add_argument("--layers", type=int, default=WORKLOAD["layers"], help="layer caches (profiling runs only)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     config = {k: WORKLOAD[k] for k in ("workload", "layers", "groups", "head_dim", "clusters", "B", "recent",
                                         "granularity", "exact", "span_cap", "tokens", "batch_per_rank")}
-    config.update(parallelism=f"batch-sharded streams x{world}", l2="inputs larger than L2 (5.6 GB per step)")
+    config.update(layers=args.layers, parallelism=f"batch-sharded streams x{world}",
+                  l2="inputs larger than L2 (5.6 GB per step at 28 layers)")
     if args.impl == "reference":
         if rank != 0:
             return
@@ -340,7 +345,7 @@ def main():
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     res = bench_ours(args, rank, world, local_rank)
     cpu = None
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and args.cpu_flushes > 0:
         us, n = cpu_flush_sample(args.cpu_flushes)
         cpu = {"value": round(us, 1), "unit": "us", "cores": 1, "kind": "port",
                "sample": f"median of {n} flushes of one 0.6B-shaped layer (oracle/, numpy, 1 thread)"}
