@@ -16,10 +16,15 @@
 #include <cstdio>
 
 #include "flush_alpha.cuh"
+#include "flush_cascade.cuh"
 #include "flush_ladder.cuh"
 #include "flush_route.cuh"
 
 namespace logkv {
+
+static size_t cascade_smem(const Geo& g, size_t esize) {
+  return 2 * (size_t)kTileRows * g.D * esize + (size_t)kTileRows * sizeof(Meta) + (size_t)g.NW * sizeof(int) + 16;
+}
 
 // ---------------------------------------------------------------- K8: window shift
 template <typename T>
@@ -194,7 +199,8 @@ static size_t carve(const Geo& g, size_t esize, char* base, Work* w) {
 static int validate(const logkv_layout_t* L, int F) {
   if (!L) return LOGKV_E_POINTER;
   if (L->dtype != LOGKV_DTYPE_F32 && L->dtype != LOGKV_DTYPE_BF16) return LOGKV_E_DTYPE;
-  if (L->batch < 1 || L->groups < 1 || L->dim < 2 || L->dim > 1024 || L->dim % 2) return LOGKV_E_SHAPE;
+  if (L->batch < 1 || L->groups < 1 || L->dim < 4 || L->dim > 1024) return LOGKV_E_SHAPE;
+  if (L->dim % (L->dtype == LOGKV_DTYPE_BF16 ? 8 : 4)) return LOGKV_E_SHAPE;  // 16-byte rows
   if (L->clusters < 2 || L->clusters > kMaxClusters || L->levels < 2 || L->levels > kMaxLevels) return LOGKV_E_SHAPE;
   if (L->slots < 2 || L->exact < 1 || L->span_cap < 1 || L->span_cap > L->exact) return LOGKV_E_SHAPE;
   if (F < 1 || F > L->recent_capacity || L->exact + F > 8192) return LOGKV_E_SHAPE;
@@ -244,15 +250,15 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
     cudaFuncSetAttribute(prepare_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
   prepare_kernel<T><<<dim3(g.K, g.G, g.B), 256, prep_smem, st>>>(g, s, w);
   mark();
-  const size_t casc_smem = 2 * (size_t)g.Bs * g.D * sizeof(T) + (size_t)g.Bs * sizeof(Meta) + 16;
+  const size_t casc_smem = cascade_smem(g, sizeof(T));
   if (g.beta) {
     if (casc_smem > 48 * 1024)
       cudaFuncSetAttribute(cascade_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)casc_smem);
-    cascade_kernel<T, true><<<dim3(g.K, g.G, g.B), 256, casc_smem, st>>>(g, s, w);
+    cascade_kernel<T, true><<<dim3(g.K, g.G, g.B), 512, casc_smem, st>>>(g, s, w);
   } else {
     if (casc_smem > 48 * 1024)
       cudaFuncSetAttribute(cascade_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)casc_smem);
-    cascade_kernel<T, false><<<dim3(g.K, g.G, g.B), 256, casc_smem, st>>>(g, s, w);
+    cascade_kernel<T, false><<<dim3(g.K, g.G, g.B), 512, casc_smem, st>>>(g, s, w);
   }
   mark();
   pool_rewrite_kernel<T><<<dim3(per_bg, g.G, g.B), 256, 0, st>>>(g, s, w);
@@ -277,8 +283,7 @@ static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, i
   Work w{};
   const size_t need = carve(g, esize, static_cast<char*>(workspace), &w);
   if (workspace_bytes < need) return LOGKV_E_WORKSPACE;
-  const size_t casc_smem = 2 * (size_t)g.Bs * g.D * esize + (size_t)g.Bs * sizeof(Meta) + 16;
-  if (casc_smem > 227 * 1024 || (size_t)g.sort_cap * 8 > 227 * 1024) return LOGKV_E_SMEM;
+  if (cascade_smem(g, esize) > 227 * 1024 || (size_t)g.sort_cap * 8 > 227 * 1024) return LOGKV_E_SMEM;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (layout->dtype == LOGKV_DTYPE_BF16) return launch_flush<__nv_bfloat16>(g, *state, w, st, ev);
   return launch_flush<float>(g, *state, w, st, ev);

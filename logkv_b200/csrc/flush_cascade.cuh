@@ -1,0 +1,389 @@
+// Ladder cascade (K6b): one CTA per (batch, group, cluster) lane walks the
+// levels; each overflowing level streams its pool through shared memory in
+// tiles of kTileRows rows with 16-byte vector loads/stores.
+//
+// Hazard-free in place: tile t is fully staged before any of its outputs are
+// written, and survivors land in slots below the tile's first row, all of
+// which are already staged; merged rows go to the other scratch buffer.
+#pragma once
+
+#include "flush_ladder.cuh"
+
+namespace logkv {
+
+constexpr int kTileRows = 64;                 // multiple of 4 (Beta groups never straddle tiles)
+constexpr int kTileGroups = kTileRows / 4;
+
+template <typename T>
+struct Vec {
+  static constexpr int N = 16 / sizeof(T);
+};
+
+__device__ __forceinline__ void unpack(const uint4& u, float* out, const float*) {
+  const float* f = reinterpret_cast<const float*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) out[i] = f[i];
+}
+__device__ __forceinline__ void unpack(const uint4& u, float* out, const __nv_bfloat16*) {
+  const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) out[i] = __bfloat162float(h[i]);
+}
+__device__ __forceinline__ uint4 pack(const float* in, const float*) {
+  uint4 u;
+  float* f = reinterpret_cast<float*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) f[i] = in[i];
+  return u;
+}
+__device__ __forceinline__ uint4 pack(const float* in, const __nv_bfloat16*) {
+  uint4 u;
+  __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) h[i] = __float2bfloat16_rn(in[i]);
+  return u;
+}
+
+template <typename T, bool BETA>
+__global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Work w) {
+  LaneCtx<T> x = make_ctx<T>(g, s, w);
+  const int type = w.plan_type[x.lane];
+  if (type == kJobNone) return;
+  constexpr int VN = Vec<T>::N;
+  const int tid = threadIdx.x, nt = blockDim.x, D = g.D, Bs = g.Bs, DV = g.D / VN;
+  extern __shared__ uint4 smem4[];
+  T* tk = reinterpret_cast<T*>(smem4);                 // [kTileRows][D]
+  T* tv = tk + (size_t)kTileRows * D;                  // [kTileRows][D]
+  Meta* tm = reinterpret_cast<Meta*>(tv + (size_t)kTileRows * D);  // [kTileRows]
+  int* srcs = reinterpret_cast<int*>(tm + kTileRows);  // [NW] token sources
+  __shared__ float bloss[kTileGroups][12];
+  __shared__ float bener[kTileGroups][2];
+  __shared__ int bcut[kTileGroups];
+  T* LK = static_cast<T*>(s.level_k);
+  T* LV = static_cast<T*>(s.level_v);
+  T* SK = static_cast<T*>(w.sk);
+  T* SV = static_cast<T*>(w.sv);
+  const int ntok = type == kJobLate ? 0 : w.plan_n[x.lane];
+  for (int i = tid; i < ntok; i += nt) srcs[i] = x.arch[x.toks[x.toff + i]];
+  __syncthreads();
+  Stage st;
+  st.kind = type == kJobLate ? 1 : 0;
+  st.buf = 0;
+  st.m = w.plan_m0[x.lane];
+  int nb = 1;
+  // Row pointers of incoming rows (tokens through the source table, else scratch).
+  auto stage_k = [&](int i) -> const T* {
+    if (st.kind == 0) return token_row<T>(g, x.snapk, x.reck, x.b, x.grp, srcs[i]);
+    return SK + x.scr_row(st.buf, i) * D;
+  };
+  auto stage_v = [&](int i) -> const T* {
+    if (st.kind == 0) return token_row<T>(g, x.snapv, x.recv, x.b, x.grp, srcs[i]);
+    return SV + x.scr_row(st.buf, i) * D;
+  };
+  auto stage_meta = [&](int i) -> Meta {
+    if (st.kind == 0) {
+      const int64_t p = token_position(g, s, w, x.b, srcs[i]);
+      return Meta{1.f, p, p, p, x.base_order + i, 0};
+    }
+    const size_t r = x.scr_row(st.buf, i);
+    return Meta{w.sw[r], w.slo[r], w.shi[r], w.sswp[r], w.sord[r], w.spad[r]};
+  };
+  for (int ell = 0; ell < g.L; ++ell) {
+    const int m = st.m;
+    if (m == 0) break;
+    const int cnt = s.level_count[x.lane * g.L + ell];
+    const size_t lrow0 = x.level_row(ell, 0);
+    auto pool_k = [&](int p) -> const T* { return p < cnt ? LK + (lrow0 + p) * D : stage_k(p - cnt); };
+    auto pool_v = [&](int p) -> const T* { return p < cnt ? LV + (lrow0 + p) * D : stage_v(p - cnt); };
+    auto pool_m = [&](int p) -> Meta {
+      if (p < cnt) {
+        const size_t r = lrow0 + p;
+        return Meta{s.level_w[r], s.level_p_lo[r], s.level_p_hi[r], s.level_sum_wp[r], s.level_order[r],
+                    s.pad_mask[r]};
+      }
+      return stage_meta(p - cnt);
+    };
+    if (cnt + m <= Bs) {
+      // Fill: incoming rows become slots cnt.. (already in the storage dtype).
+      for (int item = tid; item < m * DV * 2; item += nt) {
+        const int i = item / (2 * DV), f = (item / DV) & 1, v = item % DV;
+        const T* src = (f ? stage_v(i) : stage_k(i)) + v * VN;
+        T* dst = (f ? LV : LK) + (lrow0 + cnt + i) * D + v * VN;
+        *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(src);
+      }
+      for (int i = tid; i < m; i += nt) x.put_level_meta(lrow0 + cnt + i, stage_meta(i));
+      if (tid == 0) {
+        s.level_count[x.lane * g.L + ell] = (int16_t)(cnt + m);
+        atomicAdd(&w.counters[kCntStageRead], (unsigned long long)m);
+        atomicAdd(&w.counters[kCntFill], (unsigned long long)m);
+      }
+      break;
+    }
+    const int rem = cnt + m - Bs;
+    if (ell == g.L - 1) {
+      // Saturated top level (rare): slot 0 = left fold of pool[0..rem], rounded each step;
+      // slots 1.. = pool[rem+1..].  Pool rows are read straight from their sources; the
+      // shifted rows are staged through registers in two passes to avoid overlap.
+      for (int d = tid; d < D; d += nt) {
+        float ak = Elem<T>::load(pool_k(0) + d), av = Elem<T>::load(pool_v(0) + d);
+        float aw = pool_m(0).w;
+        for (int t = 1; t <= rem; ++t) {
+          const float bw = pool_m(t).w;
+          const float alpha = fdiv(aw, fmaxf(fadd(aw, bw), 1e-8f));
+          const float beta = fsub(1.f, alpha);
+          ak = Elem<T>::round(fadd(fmul(alpha, ak), fmul(beta, Elem<T>::load(pool_k(t) + d))));
+          av = Elem<T>::round(fadd(fmul(alpha, av), fmul(beta, Elem<T>::load(pool_v(t) + d))));
+          aw = fadd(aw, bw);
+        }
+        // The folded entry waits in tile row 0 until every shifted source row is staged.
+        Elem<T>::store(tk + d, ak);
+        Elem<T>::store(tv + d, av);
+      }
+      if (tid == 0) {
+        Meta acc = pool_m(0);
+        for (int t = 1; t <= rem; ++t) acc = merge_meta(acc, pool_m(t));
+        tm[0] = acc;
+      }
+      __syncthreads();
+      // Shift: slot j (1 <= j < Bs) <- pool[rem + j].  Sources at p = rem + j > j, processed
+      // in tiles of ascending j, staged before written.
+      for (int j0 = 1; j0 < Bs; j0 += kTileRows - 1) {
+        const int jn = min(kTileRows - 1, Bs - j0);
+        for (int item = tid; item < jn * D; item += nt) {
+          const int r = item / D, d = item % D;
+          tk[(1 + r) * D + d] = pool_k(rem + j0 + r)[d];
+          tv[(1 + r) * D + d] = pool_v(rem + j0 + r)[d];
+        }
+        for (int r = tid; r < jn; r += nt) tm[1 + r] = pool_m(rem + j0 + r);
+        __syncthreads();
+        for (int item = tid; item < jn * D; item += nt) {
+          const int r = item / D, d = item % D;
+          LK[(lrow0 + j0 + r) * D + d] = tk[(1 + r) * D + d];
+          LV[(lrow0 + j0 + r) * D + d] = tv[(1 + r) * D + d];
+        }
+        for (int r = tid; r < jn; r += nt) x.put_level_meta(lrow0 + j0 + r, tm[1 + r]);
+        __syncthreads();
+      }
+      for (int d = tid; d < D; d += nt) {
+        LK[lrow0 * D + d] = tk[d];
+        LV[lrow0 * D + d] = tv[d];
+      }
+      if (tid == 0) {
+        x.put_level_meta(lrow0, tm[0]);
+        s.level_count[x.lane * g.L + ell] = (int16_t)Bs;
+        atomicAdd(&w.counters[kCntStorageRead], (unsigned long long)cnt);
+        atomicAdd(&w.counters[kCntStageRead], (unsigned long long)m);
+        atomicAdd(&w.counters[kCntSurvivor], (unsigned long long)Bs);
+      }
+      break;
+    }
+    const int npair = 2 * ((rem + 1) / 2);
+    const int ncarry = npair / 2;
+    const int nsurv = cnt + m - npair;
+    const int total = cnt + m;
+    for (int t0 = 0; t0 < total; t0 += kTileRows) {
+      const int tn = min(kTileRows, total - t0);
+      // Stage the tile (K and V rows, 16 B per access) and its metadata.
+      for (int item = tid; item < tn * DV * 2; item += nt) {
+        const int r = item / (2 * DV), f = (item / DV) & 1, v = item % DV;
+        const T* src = (f ? pool_v(t0 + r) : pool_k(t0 + r)) + v * VN;
+        *reinterpret_cast<uint4*>((f ? tv : tk) + r * D + v * VN) = *reinterpret_cast<const uint4*>(src);
+      }
+      for (int r = tid; r < tn; r += nt) tm[r] = pool_m(t0 + r);
+      __syncthreads();
+      const int mend = min(t0 + tn, npair);  // merge rows of this tile: [t0, mend)
+      if (mend > t0) {
+        if (!BETA) {
+          const int j0 = t0 / 2, jn = (mend - t0) / 2;
+          for (int item = tid; item < jn * DV * 2; item += nt) {
+            const int j = item / (2 * DV), f = (item / DV) & 1, v = item % DV;
+            const int ra = 2 * j, rb = 2 * j + 1;
+            const float wa = tm[ra].w, wb = tm[rb].w;
+            const float alpha = fdiv(wa, fmaxf(fadd(wa, wb), 1e-8f));
+            const float beta = fsub(1.f, alpha);
+            const T* base = f ? tv : tk;
+            float a[VN], b[VN], o[VN];
+            unpack(*reinterpret_cast<const uint4*>(base + ra * D + v * VN), a, (const T*)nullptr);
+            unpack(*reinterpret_cast<const uint4*>(base + rb * D + v * VN), b, (const T*)nullptr);
+#pragma unroll
+            for (int e = 0; e < VN; ++e) o[e] = fadd(fmul(alpha, a[e]), fmul(beta, b[e]));
+            *reinterpret_cast<uint4*>((f ? SV : SK) + x.scr_row(nb, j0 + j) * D + v * VN) = pack(o, (const T*)nullptr);
+          }
+          for (int j = tid; j < jn; j += nt) x.put_scratch(nb, j0 + j, merge_meta(tm[2 * j], tm[2 * j + 1]));
+        } else {
+          const int qn = (mend - t0 + 3) / 4;  // groups of this tile (tile rows 4q..4q+3)
+          for (int item = tid; item < qn * 14; item += nt) {
+            const int q = item / 14, k = item % 14;
+            const int start = 4 * q;                       // tile row of the group
+            const int width = min(4, npair - (t0 + start));
+            if (width != 4) continue;
+            float wv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) wv[i] = tm[start + i].w;
+            const int comp = k < 12 ? k / 6 : k - 12;
+            const T* base = comp == 0 ? tk : tv;
+            if (k >= 12) {
+              float e[4] = {0.f, 0.f, 0.f, 0.f};
+              for (int d = 0; d < D; ++d)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const float xv = Elem<T>::load(base + (start + i) * D + d);
+                  e[i] = fadd(e[i], fmul(xv, xv));
+                }
+              float tot = 0.f, acc = 0.f;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) tot = fadd(tot, wv[i]);
+              tot = fmaxf(tot, 1e-12f);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) acc = fadd(acc, fmul(e[i], wv[i]));
+              bener[q][comp] = fmaxf(fdiv(acc, tot), 1e-12f);
+            } else {
+              const int j = (k % 6) / 2, side = k % 2;
+              const int cut = j == 0 ? 2 : (j == 1 ? 1 : 3);
+              float om[4];
+              float ws = 0.f;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const bool in = side == 0 ? (i < cut) : (i >= cut);
+                om[i] = fmul(wv[i], in ? 1.f : 0.f);
+                ws = fadd(ws, om[i]);
+              }
+              const float den = fmaxf(ws, 1e-12f);
+              float r[4] = {0.f, 0.f, 0.f, 0.f};
+              for (int d = 0; d < D; ++d) {
+                float xv[4];
+                float sacc = 0.f;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  xv[i] = Elem<T>::load(base + (start + i) * D + d);
+                  sacc = fadd(sacc, fmul(xv[i], om[i]));
+                }
+                const float mean = fdiv(sacc, den);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                  const float df = fsub(xv[i], mean);
+                  r[i] = fadd(r[i], fmul(df, df));
+                }
+              }
+              float loss = 0.f;
+#pragma unroll
+              for (int i = 0; i < 4; ++i) loss = fadd(loss, fmul(r[i], om[i]));
+              bloss[q][k] = loss;
+            }
+          }
+          __syncthreads();
+          for (int q = tid; q < qn; q += nt) {
+            const int width = min(4, npair - (t0 + 4 * q));
+            if (width != 4) {
+              bcut[q] = 1;
+              continue;
+            }
+            float costs[3] = {0.f, 0.f, 0.f};
+            for (int comp = 0; comp < 2; ++comp)
+              for (int j = 0; j < 3; ++j)
+                for (int side = 0; side < 2; ++side)
+                  costs[j] = fadd(costs[j], fdiv(bloss[q][comp * 6 + j * 2 + side], bener[q][comp]));
+            int best = 0;
+            if (costs[1] < costs[best]) best = 1;
+            if (costs[2] < costs[best]) best = 2;
+            bcut[q] = best == 0 ? 2 : (best == 1 ? 1 : 3);
+          }
+          __syncthreads();
+          // Apply: per output side, sum over member rows (row order) of w*x / max(mass, 1e-12).
+          for (int item = tid; item < qn * 2 * 2 * DV; item += nt) {
+            const int q = item / (4 * DV), side = (item / (2 * DV)) & 1, f = (item / DV) & 1, v = item % DV;
+            const int start = 4 * q;
+            const int width = min(4, npair - (t0 + start));
+            if (side == 1 && width != 4) continue;
+            const int cut = bcut[q];
+            const T* base = f ? tv : tk;
+            float acc[VN], mass = 0.f;
+#pragma unroll
+            for (int e = 0; e < VN; ++e) acc[e] = 0.f;
+            for (int i = 0; i < 4; ++i) {
+              const bool valid = i < width;
+              const bool in = valid && (width == 2 ? side == 0 : (side == 0 ? i < cut : i >= cut));
+              const float om = fmul(valid ? tm[start + i].w : 0.f, in ? 1.f : 0.f);
+              float xr[VN];
+              if (valid) {
+                unpack(*reinterpret_cast<const uint4*>(base + (start + i) * D + v * VN), xr, (const T*)nullptr);
+              } else {
+#pragma unroll
+                for (int e = 0; e < VN; ++e) xr[e] = 0.f;
+              }
+              mass = fadd(mass, om);
+#pragma unroll
+              for (int e = 0; e < VN; ++e) acc[e] = fadd(acc[e], fmul(xr[e], om));
+            }
+            const float den = fmaxf(mass, 1e-12f);
+#pragma unroll
+            for (int e = 0; e < VN; ++e) acc[e] = fdiv(acc[e], den);
+            const int outrow = (t0 + start) / 2 + side;
+            *reinterpret_cast<uint4*>((f ? SV : SK) + x.scr_row(nb, outrow) * D + v * VN) = pack(acc, (const T*)nullptr);
+          }
+          for (int item = tid; item < qn * 2; item += nt) {
+            const int q = item / 2, side = item % 2;
+            const int start = 4 * q;
+            const int width = min(4, npair - (t0 + start));
+            if (side == 1 && width != 4) continue;
+            const int cut = bcut[q];
+            float mass = 0.f;
+            int64_t lo = INT64_MAX, hi = INT64_MIN, swp = 0, ord = INT64_MAX;
+            uint8_t pad = 1;
+            for (int i = 0; i < width; ++i) {
+              const bool in = width == 2 ? side == 0 : (side == 0 ? i < cut : i >= cut);
+              const Meta& r = tm[start + i];
+              mass = fadd(mass, fmul(r.w, in ? 1.f : 0.f));
+              if (!in) continue;
+              if (r.w > 0.f) {
+                lo = min(lo, r.lo);
+                hi = max(hi, r.hi);
+              }
+              swp += r.swp;
+              ord = min(ord, r.ord);
+              pad &= r.pad;
+            }
+            x.put_scratch(nb, (t0 + start) / 2 + side,
+                          Meta{mass, mass > 0.f ? lo : 0, mass > 0.f ? hi : 0, swp, ord, pad});
+          }
+        }
+      }
+      // Survivors of this tile: pool row p >= npair -> slot p - npair.
+      const int sbeg = max(t0, npair);
+      const int sn = t0 + tn - sbeg;
+      if (sn > 0) {
+        for (int item = tid; item < sn * DV * 2; item += nt) {
+          const int r = item / (2 * DV), f = (item / DV) & 1, v = item % DV;
+          const int p = sbeg + r;
+          *reinterpret_cast<uint4*>((f ? LV : LK) + (lrow0 + p - npair) * D + v * VN) =
+              *reinterpret_cast<const uint4*>((f ? tv : tk) + (p - t0) * D + v * VN);
+        }
+        for (int r = tid; r < sn; r += nt) x.put_level_meta(lrow0 + sbeg + r - npair, tm[sbeg + r - t0]);
+      }
+      __syncthreads();
+    }
+    // Tail slots are zeroed.
+    const int nclr = Bs - nsurv;
+    const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+    for (int item = tid; item < nclr * DV * 2; item += nt) {
+      const int r = item / (2 * DV), f = (item / DV) & 1, v = item % DV;
+      *reinterpret_cast<uint4*>((f ? LV : LK) + (lrow0 + nsurv + r) * D + v * VN) = zero;
+    }
+    for (int r = tid; r < nclr; r += nt) x.put_level_meta(lrow0 + nsurv + r, Meta{0.f, 0, 0, 0, 0, 0});
+    if (tid == 0) {
+      s.level_count[x.lane * g.L + ell] = (int16_t)nsurv;
+      atomicAdd(&w.counters[kCntStorageRead], (unsigned long long)cnt);
+      atomicAdd(&w.counters[kCntStageRead], (unsigned long long)m);
+      atomicAdd(&w.counters[kCntSurvivor], (unsigned long long)nsurv);
+      atomicAdd(&w.counters[kCntClear], (unsigned long long)nclr);
+      atomicAdd(&w.counters[kCntCarry], (unsigned long long)ncarry);
+    }
+    __syncthreads();
+    st.kind = 1;
+    st.buf = nb;
+    st.m = ncarry;
+    nb = 1 - nb;
+  }
+}
+
+}  // namespace logkv
