@@ -108,24 +108,25 @@ def make_inputs(torch, cfg, device, seed):
     ends_row = [(i % 23) == 22 for i in range(T)]
     ends_dev = torch.tensor([ends_row], dtype=torch.uint8, device=device)
     layers = []
+    N = n_chunks
+    pos = torch.arange(N * T, device=device).view(N, 1, T)
     for layer in range(cfg["layers"]):
+        # All chunks of one layer at once (few launches); chunk c is the view [c:c+1].
         centres = torch.randn(G, K, D, generator=gen, device=device)
-        chunks = []
-        for c in range(n_chunks):
-            z = torch.randint(0, K, (G, T), generator=gen, device=device)
-            base = torch.gather(centres, 1, z[..., None].expand(-1, -1, D))
-            noise = torch.randn(G, T, D, generator=gen, device=device) * 0.3
-            orphan = torch.rand(G, T, generator=gen, device=device) < 0.05
-            u = torch.randn(G, T, D, generator=gen, device=device)
-            u = u / u.norm(dim=-1, keepdim=True) * (4 * 0.3 * D ** 0.5)
-            kr = torch.where(orphan[..., None], base + u, base + noise)[None]
-            pos = torch.arange(c * T, (c + 1) * T, device=device)
-            half = D // 2
-            rot = torch.cat([-kr[..., half:], kr[..., :half]], dim=-1)
-            k = kr * cos[pos] + rot * sin[pos]
-            v = torch.randn(1, G, T, D, generator=gen, device=device)
-            chunks.append((k.bfloat16().contiguous(), kr.bfloat16().contiguous(), v.bfloat16().contiguous()))
-        layers.append(chunks)
+        z = torch.randint(0, K, (N, G, T), generator=gen, device=device)
+        base = centres[torch.arange(G, device=device)[None, :, None], z]
+        noise = torch.randn(N, G, T, D, generator=gen, device=device) * 0.3
+        orphan = torch.rand(N, G, T, generator=gen, device=device) < 0.05
+        u = torch.randn(N, G, T, D, generator=gen, device=device)
+        u = u / u.norm(dim=-1, keepdim=True) * (4 * 0.3 * D ** 0.5)
+        kr = torch.where(orphan[..., None], base + u, base + noise)
+        half = D // 2
+        rot = torch.cat([-kr[..., half:], kr[..., :half]], dim=-1)
+        k = (kr * cos[pos] + rot * sin[pos]).bfloat16()
+        v = torch.randn(N, G, T, D, generator=gen, device=device).bfloat16()
+        kr = kr.bfloat16()
+        del base, noise, u, rot
+        layers.append([(k[c:c + 1], kr[c:c + 1], v[c:c + 1]) for c in range(N)])
     return layers, cos, sin, [ends_row], ends_dev
 
 
@@ -220,13 +221,18 @@ def bench_ours(args, rank, world, local_rank):
                 idx += 1 if will_flush else 0
                 cache.profile_events = None
     torch.cuda.synchronize()
+    per_flush = [[] for _ in range(nstage)]
     for evs in events:
         for i in range(nstage):
-            stage_ms[i] += evs[i].elapsed_time(evs[i + 1])
+            t = evs[i].elapsed_time(evs[i + 1])
+            stage_ms[i] += t
+            per_flush[i].append(t)
     after = [c.read_counters() for c in caches]
     delta = {k: sum(a[k] - b[k] for a, b in zip(after, before)) for k in after[0]}
     from logkv_b200._lib import FLUSH_STAGES
     stages_us = {name: round(stage_ms[i] * 1000.0 / flushes_per_step, 2) for i, name in enumerate(FLUSH_STAGES)}
+    stages_med = {name: round(statistics.median(per_flush[i]) * 1000.0, 2) for i, name in enumerate(FLUSH_STAGES)}
+    stages_max = {name: round(max(per_flush[i]) * 1000.0, 2) for i, name in enumerate(FLUSH_STAGES)}
     casc_rows = delta["storage_read"] + delta["stage_read"] + delta["survivor"] + delta["fill"] + delta["clear"] \
         + delta["carry"]
     casc_bytes_per_launch = casc_rows * ROW_BYTES / flushes_per_step
@@ -273,7 +279,8 @@ def bench_ours(args, rank, world, local_rank):
     del readback
     n_launch = flushes_per_step * 10 * args.steps
     return dict(value=us_per_flush * 1.0 / world, ms_per_step=ms_per_step, e2e_us=e2e_us / world,
-                h2d=h2d_per_step * world, stages=stages_us, counters=delta, flushes_per_step=flushes_per_step,
+                h2d=h2d_per_step * world, stages=stages_us, stages_med=stages_med, stages_max=stages_max,
+                counters=delta, flushes_per_step=flushes_per_step,
                 roofline={"bound": "hbm", "kernel": "cascade_kernel", "achieved": round(achieved, 1),
                           "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
                           "traffic": None, "bytes_per_launch": round(casc_bytes_per_launch)},
@@ -357,6 +364,7 @@ def main():
                          "d2h_bytes_per_step": 4},
                     roofline=res["roofline"], flush_roofline=res["flush_roofline"], cpu_baseline=cpu,
                     clocks=res["clocks"], gpu_launches=res["launches"], stages_us=res["stages"],
+                    stages_us_median=res["stages_med"], stages_us_max=res["stages_max"],
                     flushes_per_step=res["flushes_per_step"])
         print(json.dumps(line), flush=True)
     if world > 1:

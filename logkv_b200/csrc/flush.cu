@@ -165,6 +165,7 @@ static size_t carve(const Geo& g, size_t esize, char* base, Work* w) {
   w->cand_flags = c.take<uint8_t>(B * NC, 1);
   w->n_cand = c.take<int32_t>(B, 4);
   w->scores = c.take<float>(B * NC, 4);
+  w->gpart = c.take<float>(B * NC * G * 2, 4);
   w->keep_idx = c.take<int32_t>(B * P, 4);
   w->nkeep = c.take<int32_t>(B, 4);
   w->arch_idx = c.take<int32_t>(B * NW, 4);
@@ -224,11 +225,11 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   if (cut_smem > 48 * 1024) cudaFuncSetAttribute(alpha_cut_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cut_smem);
   alpha_cut_kernel<<<g.B, 1024, cut_smem, st>>>(g, s, w);
   mark();
-  const size_t score_smem = (2 * (size_t)g.G * g.D + (size_t)g.G * 256 + 6 * (size_t)g.G) * sizeof(float);
+  const size_t score_smem = (64 * (size_t)(g.D + 1) + 2 * (size_t)g.D + 64 + (size_t)g.K) * sizeof(float);
   if (score_smem > 48 * 1024)
     cudaFuncSetAttribute(alpha_score_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)score_smem);
-  const int score_blocks = std::max(1, std::min(g.NC, 2 * sm_count / std::max(1, g.B) + 1));
-  alpha_score_kernel<T><<<dim3(score_blocks, g.B), 256, score_smem, st>>>(g, s, w);
+  const int score_blocks = std::max(1, std::min(g.NC, 8 * sm_count / std::max(1, g.B * g.G) + 1));
+  alpha_score_kernel<T><<<dim3(score_blocks, g.G, g.B), 256, score_smem, st>>>(g, s, w);
   mark();
   const size_t choose_smem = (size_t)g.NC * (8 + 4 * 4 + 2);
   if (choose_smem > 48 * 1024)
@@ -240,12 +241,12 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
     cudaFuncSetAttribute(attach_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attach_smem);
   attach_kernel<T><<<dim3((g.NW + 127) / 128, g.G, g.B), 128, attach_smem, st>>>(g, s, w);
   mark();
-  const size_t plan_smem = (size_t)g.NW * sizeof(float);
+  const size_t plan_smem = ((size_t)((g.NW + 3) & ~3) + (size_t)g.K * g.D) * sizeof(float);
   if (plan_smem > 48 * 1024)
     cudaFuncSetAttribute(plan_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan_smem);
   plan_kernel<T><<<dim3(g.G, g.B), 1024, plan_smem, st>>>(g, s, w);
   mark();
-  const size_t prep_smem = (size_t)g.sort_cap * sizeof(unsigned long long);
+  const size_t prep_smem = (size_t)g.sort_cap * sizeof(unsigned long long) + (size_t)g.NW * sizeof(int);
   if (prep_smem > 48 * 1024)
     cudaFuncSetAttribute(prepare_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
   prepare_kernel<T><<<dim3(g.K, g.G, g.B), 256, prep_smem, st>>>(g, s, w);
@@ -283,7 +284,8 @@ static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, i
   Work w{};
   const size_t need = carve(g, esize, static_cast<char*>(workspace), &w);
   if (workspace_bytes < need) return LOGKV_E_WORKSPACE;
-  if (cascade_smem(g, esize) > 227 * 1024 || (size_t)g.sort_cap * 8 > 227 * 1024) return LOGKV_E_SMEM;
+  if (cascade_smem(g, esize) > 227 * 1024 || (size_t)g.sort_cap * 8 + (size_t)g.NW * 4 > 227 * 1024)
+    return LOGKV_E_SMEM;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (layout->dtype == LOGKV_DTYPE_BF16) return launch_flush<__nv_bfloat16>(g, *state, w, st, ev);
   return launch_flush<float>(g, *state, w, st, ev);

@@ -202,32 +202,25 @@ __global__ void __launch_bounds__(1024) alpha_cut_kernel(Geo g, logkv_state_t s,
 }
 
 // ---------------------------------------------------------------- K2: span scores
-template <typename T>
-__device__ __forceinline__ const T* cand_row(const Geo& g, const logkv_state_t& s, const Work& w, const T* snap,
-                                             const T* recent, int b, int grp, int src) {
-  if (src < g.P) return snap + (((size_t)b * g.G + grp) * g.P + src) * g.D;
-  return recent + (((size_t)b * g.G + grp) * g.cap2R + (src - g.P)) * g.D;
-}
-
-// Per candidate and group: mean vector, energy E, residual part
-// R = max(E - mean(mean^2), 0) / max(E, 1e-12); Beta adds the novelty term.
+// One block per (candidate, group) in a grid-stride over candidates: the span's
+// rows are staged in shared memory (64 tokens at a time, 16-byte loads); mean
+// per feature and energy per token are left-to-right sums.  Output per
+// (row, candidate, group): Alpha parts (R_K, R_V) or Beta's per-group score.
 template <typename T>
 __global__ void __launch_bounds__(256) alpha_score_kernel(Geo g, logkv_state_t s, Work w) {
-  const int b = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
+  const int b = blockIdx.z, grp = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
   const int G = g.G, D = g.D, K = g.K;
+  constexpr int VN = Vec<T>::N;
+  const int DV = D / VN;
   extern __shared__ float sm[];
-  float* kmean = sm;                 // [G][D]
-  float* vmean = kmean + G * D;      // [G][D]
-  float* etok = vmean + G * D;       // [G][256]
-  float* part = etok + G * 256;      // [2][G]
-  float* kener = part + 2 * G;       // [G]
-  float* kms = kener + G;            // [G]
-  float* gscore = kms + G;           // [G]
-  float* nearest = gscore + G;       // [G]
-  const T* snapk = static_cast<const T*>(w.snap_k);
-  const T* snapv = static_cast<const T*>(w.snap_v);
-  const T* reck = static_cast<const T*>(s.recent_k_raw);
-  const T* recv = static_cast<const T*>(s.recent_v);
+  float* rows = sm;                          // [64][D + 1]
+  float* kmean = rows + 64 * (D + 1);        // [D]
+  float* mean = kmean + D;                   // [D]
+  float* etok = mean + D;                    // [64]
+  float* cdist = etok + 64;                  // [K]
+  __shared__ float sh_part[2], sh_kener, sh_kms;
+  const T* snap[2] = {static_cast<const T*>(w.snap_k), static_cast<const T*>(w.snap_v)};
+  const T* rec[2] = {static_cast<const T*>(s.recent_k_raw), static_cast<const T*>(s.recent_v)};
   const int ncand = w.n_cand[b];
   for (int ci = blockIdx.x; ci < ncand; ci += gridDim.x) {
     const size_t cix = (size_t)b * g.NC + ci;
@@ -235,106 +228,87 @@ __global__ void __launch_bounds__(256) alpha_score_kernel(Geo g, logkv_state_t s
     const int n = n0 + n1;
     const float fn = (float)n;
     for (int comp = 0; comp < 2; ++comp) {
-      const T* snap = comp == 0 ? snapk : snapv;
-      const T* rec = comp == 0 ? reck : recv;
-      float* mean = comp == 0 ? kmean : vmean;
-      // mean over tokens (sequential per feature)
-      for (int item = tid; item < G * D; item += nt) {
-        const int grp = item / D, d = item % D;
-        float acc = 0.f;
-        for (int t = 0; t < n; ++t) {
-          const int src = t < n0 ? s0 + t : s1 + (t - n0);
-          acc = fadd(acc, Elem<T>::load(cand_row<T>(g, s, w, snap, rec, b, grp, src) + d));
+      float acc = 0.f, eacc = 0.f;
+      for (int c0 = 0; c0 < n; c0 += 64) {
+        const int cn = min(64, n - c0);
+        for (int item = tid; item < cn * DV; item += nt) {
+          const int t = item / DV, v = item % DV;
+          const int tt = c0 + t;
+          const int src = tt < n0 ? s0 + tt : s1 + (tt - n0);
+          float xv[VN];
+          unpack(*reinterpret_cast<const uint4*>(token_row<T>(g, snap[comp], rec[comp], b, grp, src) + v * VN), xv,
+                 (const T*)nullptr);
+#pragma unroll
+          for (int e = 0; e < VN; ++e) rows[t * (D + 1) + v * VN + e] = xv[e];
         }
-        mean[item] = fdiv(acc, fn);
+        __syncthreads();
+        if (tid < D)
+          for (int t = 0; t < cn; ++t) acc = fadd(acc, rows[t * (D + 1) + tid]);
+        for (int t = tid; t < cn; t += nt) {
+          float e = 0.f;
+          for (int d = 0; d < D; ++d) e = fadd(e, fmul(rows[t * (D + 1) + d], rows[t * (D + 1) + d]));
+          etok[t] = fdiv(e, (float)D);
+        }
+        __syncthreads();
+        if (tid == 0)
+          for (int t = 0; t < cn; ++t) eacc = fadd(eacc, etok[t]);
+        __syncthreads();
       }
-      // energy: per token sum(x^2)/D sequential, then sequential mean over tokens
-      float eacc = 0.f;  // owned by thread grp < G
-      for (int c0 = 0; c0 < n; c0 += 256) {
-        const int cn = min(256, n - c0);
-        __syncthreads();
-        for (int item = tid; item < G * cn; item += nt) {
-          const int grp = item / cn, tt = item % cn, t = c0 + tt;
-          const int src = t < n0 ? s0 + t : s1 + (t - n0);
-          const T* row = cand_row<T>(g, s, w, snap, rec, b, grp, src);
-          float acc = 0.f;
-          for (int d = 0; d < D; ++d) {
-            const float x = Elem<T>::load(row + d);
-            acc = fadd(acc, fmul(x, x));
-          }
-          etok[grp * 256 + tt] = fdiv(acc, (float)D);
-        }
-        __syncthreads();
-        if (tid < G)
-          for (int tt = 0; tt < cn; ++tt) eacc = fadd(eacc, etok[tid * 256 + tt]);
+      if (tid < D) {
+        mean[tid] = fdiv(acc, fn);
+        if (comp == 0) kmean[tid] = mean[tid];
       }
       __syncthreads();
-      if (tid < G) {
+      if (tid == 0) {
         const float energy = fdiv(eacc, fn);
         float ms = 0.f;
-        for (int d = 0; d < D; ++d) ms = fadd(ms, fmul(mean[tid * D + d], mean[tid * D + d]));
+        for (int d = 0; d < D; ++d) ms = fadd(ms, fmul(mean[d], mean[d]));
         ms = fdiv(ms, (float)D);
-        const float resid = fmaxf(fsub(energy, ms), 0.f);
-        part[comp * G + tid] = fdiv(resid, fmaxf(energy, 1e-12f));
+        sh_part[comp] = fdiv(fmaxf(fsub(energy, ms), 0.f), fmaxf(energy, 1e-12f));
         if (comp == 0) {
-          kener[tid] = energy;
-          kms[tid] = ms;
+          sh_kener = energy;
+          sh_kms = ms;
         }
       }
       __syncthreads();
     }
+    float* out = w.gpart + (cix * G + grp) * 2;
     if (!g.beta) {
       if (tid == 0) {
-        float a = 0.f, c = 0.f;
-        for (int grp = 0; grp < G; ++grp) a = fadd(a, part[grp]);
-        for (int grp = 0; grp < G; ++grp) c = fadd(c, part[G + grp]);
-        w.scores[cix] = fadd(fdiv(a, (float)G), fdiv(c, (float)G));
+        out[0] = sh_part[0];
+        out[1] = sh_part[1];
       }
       __syncthreads();
       continue;
     }
-    // Beta novelty: nearest live centre by mean-square distance of the key mean.
-    if (tid < G) nearest[tid] = INFINITY;
-    __syncthreads();
-    for (int item = tid; item < G * K; item += nt) {
-      const int grp = item / K, c = item % K;
-      const size_t lane = ((size_t)b * G + grp) * K + c;
-      if (!s.alive[lane]) continue;
-      const float* mu = s.centroid + lane * D;
-      float dot = 0.f, mm = 0.f;
-      for (int d = 0; d < D; ++d) {
-        dot = fadd(dot, fmul(kmean[grp * D + d], mu[d]));
-        mm = fadd(mm, fmul(mu[d], mu[d]));
+    // Beta novelty: mean-square distance of the key mean to every live centre.
+    const size_t lane0 = ((size_t)b * G + grp) * K;
+    for (int c = tid; c < K; c += nt) {
+      float dist = INFINITY;
+      if (s.alive[lane0 + c]) {
+        const float* mu = s.centroid + (lane0 + c) * D;
+        float dot = 0.f, mm = 0.f;
+        for (int d = 0; d < D; ++d) {
+          dot = fadd(dot, fmul(kmean[d], mu[d]));
+          mm = fadd(mm, fmul(mu[d], mu[d]));
+        }
+        dot = fdiv(dot, (float)D);
+        mm = fdiv(mm, (float)D);
+        dist = fmaxf(fsub(fadd(sh_kms, mm), fmul(2.f, dot)), 0.f);
       }
-      dot = fdiv(dot, (float)D);
-      mm = fdiv(mm, (float)D);
-      const float dist = fmaxf(fsub(fadd(kms[grp], mm), fmul(2.f, dot)), 0.f);
-      atomicMin(reinterpret_cast<int*>(&nearest[grp]), __float_as_int(dist));  // dist >= 0: int order == float order
-    }
-    __syncthreads();
-    if (tid < G) {
-      bool any = false;
-      for (int c = 0; c < K; ++c) any |= s.alive[((size_t)b * G + tid) * K + c] != 0;
-      const float nr = any ? nearest[tid] : 0.f;
-      const float nov = fdiv(nr, fmaxf(kener[tid], 1e-12f));
-      gscore[tid] = fadd(fmul(fadd(part[tid], part[G + tid]), 0.5f), fdiv(nov, fadd(1.f, nov)));
+      cdist[c] = dist;
     }
     __syncthreads();
     if (tid == 0) {
-      float v1 = -INFINITY, v2 = -INFINITY;
-      for (int grp = 0; grp < G; ++grp) {
-        const float x = gscore[grp];
-        if (x > v1) {
-          v2 = v1;
-          v1 = x;
-        } else if (x > v2) {
-          v2 = x;
-        }
+      bool any = false;
+      float nr = INFINITY;
+      for (int c = 0; c < K; ++c) {
+        any |= s.alive[lane0 + c] != 0;
+        nr = fminf(nr, cdist[c]);
       }
-      const int top = G < 2 ? G : 2;
-      float acc = fadd(0.f, v1);
-      if (top == 2) acc = fadd(acc, v2);
-      w.scores[cix] = fdiv(acc, (float)top);
+      if (!any) nr = 0.f;
+      const float nov = fdiv(nr, fmaxf(sh_kener, 1e-12f));
+      out[0] = fadd(fmul(fadd(sh_part[0], sh_part[1]), 0.5f), fdiv(nov, fadd(1.f, nov)));
     }
     __syncthreads();
   }
@@ -368,7 +342,31 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
     const size_t c = (size_t)b * NC + i;
     flags[i] = w.cand_flags[c];
     size[i] = w.cand_n0[c] + w.cand_n1[c];
-    const double sc = (double)w.scores[c];
+    const float* gp = w.gpart + (size_t)c * g.G * 2;
+    float sf;
+    if (!g.beta) {
+      float a = 0.f, v = 0.f;
+      for (int grp = 0; grp < g.G; ++grp) a = fadd(a, gp[grp * 2]);
+      for (int grp = 0; grp < g.G; ++grp) v = fadd(v, gp[grp * 2 + 1]);
+      sf = fadd(fdiv(a, (float)g.G), fdiv(v, (float)g.G));
+    } else {
+      float v1 = -INFINITY, v2 = -INFINITY;
+      for (int grp = 0; grp < g.G; ++grp) {
+        const float xg = gp[grp * 2];
+        if (xg > v1) {
+          v2 = v1;
+          v1 = xg;
+        } else if (xg > v2) {
+          v2 = xg;
+        }
+      }
+      const int top = g.G < 2 ? g.G : 2;
+      float acc = fadd(0.f, v1);
+      if (top == 2) acc = fadd(acc, v2);
+      sf = fdiv(acc, (float)top);
+    }
+    w.scores[c] = sf;
+    const double sc = (double)sf;
     dens[i] = (flags[i] & 1) ? sc * 1.1 : sc * 1.0;
     chosen[i] = (!(flags[i] & 2)) || (flags[i] & 1);  // mandatory (open) or old
   }
@@ -552,8 +550,8 @@ __global__ void pool_rewrite_kernel(Geo g, logkv_state_t s, Work w) {
     const int row = (int)(i / g.D), d = (int)(i % g.D);
     if (row < nkeep) {
       const int src = w.keep_idx[(size_t)b * g.P + row];
-      kdst[i] = cand_row<T>(g, s, w, snapk, reck, b, grp, src)[d];
-      vdst[i] = cand_row<T>(g, s, w, snapv, recv, b, grp, src)[d];
+      kdst[i] = token_row<T>(g, snapk, reck, b, grp, src)[d];
+      vdst[i] = token_row<T>(g, snapv, recv, b, grp, src)[d];
     } else {
       kdst[i] = Elem<T>::zero();
       vdst[i] = Elem<T>::zero();

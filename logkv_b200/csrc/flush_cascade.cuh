@@ -14,36 +14,6 @@ namespace logkv {
 constexpr int kTileRows = 64;                 // multiple of 4 (Beta groups never straddle tiles)
 constexpr int kTileGroups = kTileRows / 4;
 
-template <typename T>
-struct Vec {
-  static constexpr int N = 16 / sizeof(T);
-};
-
-__device__ __forceinline__ void unpack(const uint4& u, float* out, const float*) {
-  const float* f = reinterpret_cast<const float*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) out[i] = f[i];
-}
-__device__ __forceinline__ void unpack(const uint4& u, float* out, const __nv_bfloat16*) {
-  const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) out[i] = __bfloat162float(h[i]);
-}
-__device__ __forceinline__ uint4 pack(const float* in, const float*) {
-  uint4 u;
-  float* f = reinterpret_cast<float*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) f[i] = in[i];
-  return u;
-}
-__device__ __forceinline__ uint4 pack(const float* in, const __nv_bfloat16*) {
-  uint4 u;
-  __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&u);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) h[i] = __float2bfloat16_rn(in[i]);
-  return u;
-}
-
 template <typename T, bool BETA>
 __global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Work w) {
   LaneCtx<T> x = make_ctx<T>(g, s, w);

@@ -51,6 +51,7 @@ struct Work {
   uint8_t* cand_flags;     // bit0 old, bit1 closed
   int32_t* n_cand;         // [B]
   float* scores;           // [B,NC]
+  float* gpart;            // [B,NC,G,2] per-group parts (Alpha: R_K, R_V; Beta: group score)
   int32_t* keep_idx;       // [B,P]  token indices kept in the pool, candidate order
   int32_t* nkeep;          // [B]
   int32_t* arch_idx;       // [B,NW] archived token indices, position order
@@ -81,6 +82,37 @@ struct Work {
   int64_t* wpos;
   uint8_t* wends;
 };
+
+// 16-byte vectors of storage elements.
+template <typename T>
+struct Vec {
+  static constexpr int N = 16 / sizeof(T);
+};
+
+__device__ __forceinline__ void unpack(const uint4& u, float* out, const float*) {
+  const float* f = reinterpret_cast<const float*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) out[i] = f[i];
+}
+__device__ __forceinline__ void unpack(const uint4& u, float* out, const __nv_bfloat16*) {
+  const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) out[i] = __bfloat162float(h[i]);
+}
+__device__ __forceinline__ uint4 pack(const float* in, const float*) {
+  uint4 u;
+  float* f = reinterpret_cast<float*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) f[i] = in[i];
+  return u;
+}
+__device__ __forceinline__ uint4 pack(const float* in, const __nv_bfloat16*) {
+  uint4 u;
+  __nv_bfloat16* h = reinterpret_cast<__nv_bfloat16*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) h[i] = __float2bfloat16_rn(in[i]);
+  return u;
+}
 
 // Position of token `src` of row b in [old pool | flush] index space.
 __device__ __forceinline__ int64_t token_position(const Geo& g, const logkv_state_t& s, const Work& w, int b,

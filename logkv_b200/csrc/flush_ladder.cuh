@@ -143,21 +143,27 @@ __global__ void __launch_bounds__(256) prepare_kernel(Geo g, logkv_state_t s, Wo
   const int n = w.plan_n[x.lane];
   const float pre = s.n_eff[x.lane];
   float* mu = s.centroid + x.lane * D;
+  extern __shared__ unsigned long long keys[];                       // [sort_cap] (delayed re-insert)
+  int* srcs = reinterpret_cast<int*>(keys + g.sort_cap);             // [NW] token sources
+  for (int i = tid; i < n; i += nt) srcs[i] = x.token_src(i);
+  __syncthreads();
   for (int d = tid; d < D; d += nt) {
     if (type == kJobNew) {
-      const float x0 = Elem<T>::load(token_row<T>(g, x.snapk, x.reck, x.b, x.grp, x.token_src(0)) + d);
+      const float x0 = Elem<T>::load(token_row<T>(g, x.snapk, x.reck, x.b, x.grp, srcs[0]) + d);
       if (n == 1) {
         mu[d] = x0;
       } else {
         float sums = 0.f;
+#pragma unroll 8
         for (int i = 1; i < n; ++i)
-          sums = fadd(sums, Elem<T>::load(token_row<T>(g, x.snapk, x.reck, x.b, x.grp, x.token_src(i)) + d));
+          sums = fadd(sums, Elem<T>::load(token_row<T>(g, x.snapk, x.reck, x.b, x.grp, srcs[i]) + d));
         mu[d] = fdiv(fadd(fmul(1.f, x0), sums), fadd(1.f, (float)(n - 1)));
       }
     } else {
       float sums = 0.f;
+#pragma unroll 8
       for (int i = 0; i < n; ++i)
-        sums = fadd(sums, Elem<T>::load(token_row<T>(g, x.snapk, x.reck, x.b, x.grp, x.token_src(i)) + d));
+        sums = fadd(sums, Elem<T>::load(token_row<T>(g, x.snapk, x.reck, x.b, x.grp, srcs[i]) + d));
       const float p = type == kJobOrdinary ? fmul(pre, 1.f) : pre;
       const float denom = fadd(p, (float)n);
       mu[d] = (type == kJobLate || p > 0.f) ? fdiv(fadd(fmul(p, mu[d]), sums), denom) : fdiv(sums, (float)n);
@@ -197,7 +203,6 @@ __global__ void __launch_bounds__(256) prepare_kernel(Geo g, logkv_state_t s, Wo
   }
   if (type == kJobOrdinary) return;
   if (type == kJobLate) {
-    extern __shared__ unsigned long long keys[];  // [sort_cap]
     const int total = e + n;
     const int cap = g.sort_cap;
     for (int i = tid; i < cap; i += nt) {

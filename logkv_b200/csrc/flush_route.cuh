@@ -44,9 +44,15 @@ __global__ void __launch_bounds__(128) attach_kernel(Geo g, logkv_state_t s, Wor
   const T* rec = static_cast<const T*>(s.recent_k_raw);
   const int* arch = w.arch_idx + (size_t)b * g.NW;
   const int nrow = min(128, na - r0);
-  for (int item = tid; item < nrow * D; item += blockDim.x) {
-    const int row = item / D, d = item % D;
-    xs[row * (D + 1) + d] = Elem<T>::load(token_row<T>(g, snap, rec, b, grp, arch[r0 + row]) + d);
+  constexpr int VN = Vec<T>::N;
+  const int DV = D / VN;
+  for (int item = tid; item < nrow * DV; item += blockDim.x) {
+    const int row = item / DV, v = item % DV;
+    float xv[VN];
+    unpack(*reinterpret_cast<const uint4*>(token_row<T>(g, snap, rec, b, grp, arch[r0 + row]) + v * VN), xv,
+           (const T*)nullptr);
+#pragma unroll
+    for (int e = 0; e < VN; ++e) xs[row * (D + 1) + v * VN + e] = xv[e];
   }
   __syncthreads();
   if (tid >= nrow) return;
@@ -59,29 +65,45 @@ __global__ void __launch_bounds__(128) attach_kernel(Geo g, logkv_state_t s, Wor
   float best_cost = INFINITY, s_win = 0.f, best_ex = INFINITY, sem0 = 0.f;
   int winner = 0, nearest = 0;
   bool any_alive = false;
-  for (int c = 0; c < K; ++c) {
-    float dot = 0.f, ex = 0.f;
-    const float* m = mu + c * D;
+  // Clusters in blocks of 16: 32 independent left-to-right accumulations per feature.
+  constexpr int CB = 16;
+  for (int cb = 0; cb < K; cb += CB) {
+    float dot[CB], ex[CB];
+#pragma unroll
+    for (int j = 0; j < CB; ++j) dot[j] = ex[j] = 0.f;
+    const int nc = min(CB, K - cb);
     for (int d = 0; d < D; ++d) {
-      dot = fadd(dot, fmul(x[d], m[d]));
-      const float df = fsub(x[d], m[d]);
-      ex = fadd(ex, fmul(df, df));
+      const float xd = x[d];
+#pragma unroll
+      for (int j = 0; j < CB; ++j) {
+        if (j < nc) {
+          const float m = mu[(cb + j) * D + d];
+          dot[j] = fadd(dot[j], fmul(xd, m));
+          const float df = fsub(xd, m);
+          ex[j] = fadd(ex[j], fmul(df, df));
+        }
+      }
     }
-    const float sem = fmaxf(fsub(fadd(xx, mm[c]), fmul(2.f, dot)), 0.f);
-    if (c == 0) sem0 = sem;
-    if (!alv[c]) continue;
-    any_alive = true;
-    const float gap = fmaxf((float)(pos - (int64_t)phi[c]), 0.f);
-    const float cost = fadd(sem, fmul(g.eta, fdiv(gap, fadd(gap, g.g0))));
-    if (cost < best_cost) {
-      best_cost = cost;
-      winner = c;
-      s_win = sem;
-    }
-    const float dist = __fsqrt_rn(ex);
-    if (dist < best_ex) {
-      best_ex = dist;
-      nearest = c;
+#pragma unroll
+    for (int j = 0; j < CB; ++j) {
+      if (j >= nc) continue;
+      const int c = cb + j;
+      const float sem = fmaxf(fsub(fadd(xx, mm[c]), fmul(2.f, dot[j])), 0.f);
+      if (c == 0) sem0 = sem;
+      if (!alv[c]) continue;
+      any_alive = true;
+      const float gap = fmaxf((float)(pos - (int64_t)phi[c]), 0.f);
+      const float cost = fadd(sem, fmul(g.eta, fdiv(gap, fadd(gap, g.g0))));
+      if (cost < best_cost) {
+        best_cost = cost;
+        winner = c;
+        s_win = sem;
+      }
+      const float dist = __fsqrt_rn(ex[j]);
+      if (dist < best_ex) {
+        best_ex = dist;
+        nearest = c;
+      }
     }
   }
   if (!any_alive) {
@@ -127,12 +149,20 @@ __device__ ArgMax block_argmax(ArgMax v, ArgMax* sh) {
   return out;
 }
 
+// Left-to-right squared distance between a storage row (read 16 bytes at a time) and a float row.
 template <typename T>
 __device__ __forceinline__ float sq_dist_rows(const T* a, const float* b, int D) {
+  constexpr int VN = Vec<T>::N;
   float acc = 0.f;
-  for (int d = 0; d < D; ++d) {
-    const float df = fsub(Elem<T>::load(a + d), b[d]);
-    acc = fadd(acc, fmul(df, df));
+#pragma unroll 4
+  for (int v = 0; v < D / VN; ++v) {
+    float xa[VN];
+    unpack(*reinterpret_cast<const uint4*>(a + v * VN), xa, (const T*)nullptr);
+#pragma unroll
+    for (int e = 0; e < VN; ++e) {
+      const float df = fsub(xa[e], b[v * VN + e]);
+      acc = fadd(acc, fmul(df, df));
+    }
   }
   return acc;
 }
@@ -203,27 +233,28 @@ __global__ void __launch_bounds__(1024) plan_kernel(Geo g, logkv_state_t s, Work
       __syncthreads();
     }
     // Orphans join the nearest live or seeded cluster (exact distance, lowest id on ties).
+    // Candidate centres (live centroids, seed tokens for the opened slots) staged as float32.
+    float* mus = dist + ((g.NW + 3) & ~3);  // [K][D]
+    __shared__ int cand[kMaxClusters];
+    if (tid < K) cand[tid] = s.alive[lane0 + tid] != 0;
+    __syncthreads();
+    for (int i = tid; i < K * D; i += nt) mus[i] = s.centroid[lane0 * D + i];
+    __syncthreads();
+    for (int i = 0; i < n_use; ++i) {
+      const int c = free_slots[i];
+      if (tid == 0) cand[c] = 1;
+      for (int d = tid; d < D; d += nt)
+        mus[c * D + d] = Elem<T>::load(token_row<T>(g, snap, rec, b, grp, arch[picks[i]]) + d);
+    }
+    __syncthreads();
     for (int t = tid; t < na; t += nt) {
       if (!orph[t]) continue;
       const T* x = token_row<T>(g, snap, rec, b, grp, arch[t]);
       float best_d = INFINITY;
       int best_c = 0;
       for (int c = 0; c < K; ++c) {
-        const T* seed = nullptr;
-        bool cand = s.alive[lane0 + c] != 0;
-        for (int i = 0; i < n_use; ++i)
-          if (free_slots[i] == c) {
-            cand = true;
-            seed = token_row<T>(g, snap, rec, b, grp, arch[picks[i]]);
-          }
-        if (!cand) continue;
-        float acc = 0.f;
-        for (int d = 0; d < D; ++d) {
-          const float m = seed ? Elem<T>::load(seed + d) : s.centroid[(lane0 + c) * D + d];
-          const float df = fsub(Elem<T>::load(x + d), m);
-          acc = fadd(acc, fmul(df, df));
-        }
-        const float dd = __fsqrt_rn(acc);
+        if (!cand[c]) continue;
+        const float dd = __fsqrt_rn(sq_dist_rows<T>(x, mus + c * D, D));
         if (dd < best_d) {
           best_d = dd;
           best_c = c;
