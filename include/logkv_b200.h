@@ -114,6 +114,28 @@ LOGKV_API size_t logkv_flush_workspace_bytes(const logkv_layout_t* layout, int32
 LOGKV_API int logkv_flush(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
                           int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * logkv_flush without a workspace argument, for callers that may not allocate
+ * device memory themselves: serving hosts that carve all GPU memory into fixed
+ * arenas at start-up and lock their allocator afterwards, and language bindings
+ * that cannot pass a device buffer of their own across this C boundary.  (No
+ * counterpart in the reference, which allocates freely through PyTorch.)
+ *
+ * The scratch is one region of 32 MiB compiled into the library: every GPU that
+ * loads the library holds it until the process exits.  Layouts whose
+ * logkv_flush_workspace_bytes exceeds 32 MiB are rejected with LOGKV_E_WORKSPACE
+ * and nothing is launched.  The call itself allocates nothing (no cudaMalloc,
+ * no allocating library call); it clears the region's status word and row
+ * counters with cudaMemsetAsync before the flush.  The first call on each
+ * device looks the region's device address up (with that device current);
+ * make that first call before any stream capture.  All calls share the one
+ * region, which keeps the last call's contents: two calls whose work overlaps
+ * on the GPU (different streams, or different threads on one device) race on
+ * it, so serialize them.
+ */
+LOGKV_API int logkv_flush_static(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                 int32_t recent_count, void* stream);
+
 /* Copy the workspace status word to *out (synchronizes `stream`); nonzero = a capacity was exceeded. */
 LOGKV_API int logkv_read_status(const void* workspace, int32_t* out, void* stream);
 

@@ -14,6 +14,7 @@
 //   K8 window     window shift by the flushed tokens
 #include <algorithm>
 #include <cstdio>
+#include <mutex>
 
 #include "flush_alpha.cuh"
 #include "flush_cascade.cuh"
@@ -331,4 +332,57 @@ extern "C" int logkv_read_counters(const void* workspace, uint64_t* out, int32_t
                                   cudaMemcpyDeviceToHost, st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   return (int)e;
+}
+
+// ---------------------------------------------------------------- allocation-free flush
+// Callers that may not allocate device memory (a host whose allocator is
+// locked after start-up, or a binding that cannot hand a device buffer over
+// the C boundary) flush through one fixed scratch region compiled into this
+// library instead of a caller-provided workspace.
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(32) << 20;  // 32 MiB per GPU, held until process exit
+__device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mutex;
+void* g_static_ptr[kMaxDevices] = {};
+
+// Device address of g_static_scratch on the current device.  The symbol name is
+// only a host-side stand-in; the address is looked up once per device, with
+// that device current, and cached.
+cudaError_t static_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  if (!g_static_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return e;
+    g_static_ptr[dev] = p;
+  }
+  *out = g_static_ptr[dev];
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" int logkv_flush_static(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                  int32_t recent_count, void* stream) {
+  const int v = validate(layout, flush_tokens);
+  if (v != LOGKV_OK) return v;
+  if (!state) return LOGKV_E_POINTER;
+  const size_t need = logkv_flush_workspace_bytes(layout, flush_tokens);
+  if (need == 0 || need > kStaticScratchBytes) return LOGKV_E_WORKSPACE;
+  void* scratch = nullptr;
+  cudaError_t e = static_scratch(&scratch);
+  if (e != cudaSuccess) return (int)e;
+  // The status word and the row counters (first 512 bytes) must start at zero;
+  // everything else in the scratch is written before it is read within a flush.
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  e = cudaMemsetAsync(scratch, 0, 512, st);
+  if (e != cudaSuccess) return (int)e;
+  return run_flush(layout, state, flush_tokens, recent_count, scratch, kStaticScratchBytes, stream, nullptr);
 }
