@@ -237,15 +237,26 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
     cudaFuncSetAttribute(alpha_choose_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)choose_smem);
   alpha_choose_kernel<<<g.B, 1024, choose_smem, st>>>(g, s, w);
   mark();
-  const size_t attach_smem = ((size_t)g.K * g.D + 128 * (size_t)(g.D + 1)) * sizeof(float);
+  const int att_tok = 256 / (g.K <= 16 ? 16 : 32);
+  const size_t attach_smem =
+      ((size_t)(g.K + att_tok) * (g.D + 1) + 2 * (size_t)att_tok * g.K) * sizeof(float);
   if (attach_smem > 48 * 1024)
     cudaFuncSetAttribute(attach_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attach_smem);
-  attach_kernel<T><<<dim3((g.NW + 127) / 128, g.G, g.B), 128, attach_smem, st>>>(g, s, w);
+  attach_kernel<T><<<dim3((g.NW + att_tok - 1) / att_tok, g.G, g.B), 256, attach_smem, st>>>(g, s, w);
   mark();
-  const size_t plan_smem = ((size_t)((g.NW + 3) & ~3) + (size_t)g.K * g.D) * sizeof(float);
-  if (plan_smem > 48 * 1024)
-    cudaFuncSetAttribute(plan_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)plan_smem);
-  plan_kernel<T><<<dim3(g.G, g.B), 1024, plan_smem, st>>>(g, s, w);
+  {
+    // Seeding: one 8-CTA cluster per lane; rows staged in shared memory when they fit.
+    Geo gs = g;
+    const size_t chunk = (size_t)(g.NW + kSeedCluster - 1) / kSeedCluster;
+    const size_t base = ((size_t)g.D + (size_t)g.K * (g.D + 1) + chunk + chunk * g.K) * sizeof(float);
+    const size_t rows = chunk * (size_t)(g.D + 4 / sizeof(T)) * sizeof(T);
+    gs.seed_staged = base + rows <= 200 * 1024 ? 1 : 0;
+    const size_t seed_smem = base + (gs.seed_staged ? rows : 0);
+    if (seed_smem > 48 * 1024)
+      cudaFuncSetAttribute(seed_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)seed_smem);
+    seed_kernel<T><<<dim3(kSeedCluster * g.G, g.B), 512, seed_smem, st>>>(gs, s, w);
+  }
+  plan_kernel<T><<<dim3(g.G, g.B), 1024, 0, st>>>(g, s, w);
   mark();
   const size_t prep_smem = (size_t)g.sort_cap * sizeof(unsigned long long) + (size_t)g.NW * sizeof(int);
   if (prep_smem > 48 * 1024)

@@ -18,6 +18,7 @@ struct Geo {
   int recent_count;       // window fill before the flush
   int S;                  // ladder scratch rows per buffer per (b, g)
   int sort_cap;           // power of two >= L * Bs + NW (delayed re-insert sort)
+  int seed_staged;        // seeding CTAs keep their token rows in shared memory (set per dtype at launch)
   float eta, g0, lam;
 };
 

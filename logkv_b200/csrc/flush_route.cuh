@@ -7,43 +7,46 @@
 // the ordinary/delayed split of _alpha_commit_joins (:3690-3788).
 #pragma once
 
+#include <cooperative_groups.h>
+
 #include "flush_common.cuh"
 
 namespace logkv {
 
 // ---------------------------------------------------------------- K4: attach decisions
-// One thread per archived token (position rank); the block stages its 128
-// token rows and the lane's centres in shared memory.  Every feature sum runs
-// left to right in one thread.
+// One thread per (archived token, cluster): each computes the token's dot product
+// and exact squared distance to one centre, left to right over the features; one
+// thread per token then walks the clusters in index order for the decision
+// (first-index argmin, as torch.argmin).  Token rows and centres are staged in
+// shared memory with an odd word stride (conflict-free).
 template <typename T>
-__global__ void __launch_bounds__(128) attach_kernel(Geo g, logkv_state_t s, Work w) {
+__global__ void __launch_bounds__(256) attach_kernel(Geo g, logkv_state_t s, Work w) {
   const int b = blockIdx.z, grp = blockIdx.y, tid = threadIdx.x;
   const int D = g.D, K = g.K;
+  const int slots = K <= 16 ? 16 : 32;          // threads per token
+  const int ntok = blockDim.x / slots;          // tokens per block
   const int na = w.narch[b];
-  const int r0 = blockIdx.x * 128;
+  const int r0 = blockIdx.x * ntok;
   if (r0 >= na) return;
   extern __shared__ float sm[];
-  float* mu = sm;            // [K][D]
-  float* xs = mu + K * D;    // [128][D + 1]
+  float* mu = sm;                                // [K][D+1]
+  float* xs = mu + K * (D + 1);                  // [ntok][D+1]
+  float* sem = xs + ntok * (D + 1);              // [ntok][K] semantic
+  float* exd = sem + ntok * K;                   // [ntok][K] exact squared distance
   __shared__ float mm[kMaxClusters];
+  __shared__ float xxs[32];
   __shared__ long long phi[kMaxClusters];
   __shared__ int alv[kMaxClusters];
   const size_t lane0 = ((size_t)b * g.G + grp) * K;
-  for (int i = tid; i < K * D; i += blockDim.x) mu[i] = s.centroid[lane0 * D + i];
+  for (int i = tid; i < K * D; i += blockDim.x) mu[(i / D) * (D + 1) + i % D] = s.centroid[lane0 * D + i];
   if (tid < K) {
     alv[tid] = s.alive[lane0 + tid] != 0;
     phi[tid] = s.p_hi_c[lane0 + tid];
   }
-  __syncthreads();
-  if (tid < K) {
-    float a = 0.f;
-    for (int d = 0; d < D; ++d) a = fadd(a, fmul(mu[tid * D + d], mu[tid * D + d]));
-    mm[tid] = a;
-  }
   const T* snap = static_cast<const T*>(w.snap_k);
   const T* rec = static_cast<const T*>(s.recent_k_raw);
   const int* arch = w.arch_idx + (size_t)b * g.NW;
-  const int nrow = min(128, na - r0);
+  const int nrow = min(ntok, na - r0);
   constexpr int VN = Vec<T>::N;
   const int DV = D / VN;
   for (int item = tid; item < nrow * DV; item += blockDim.x) {
@@ -55,55 +58,56 @@ __global__ void __launch_bounds__(128) attach_kernel(Geo g, logkv_state_t s, Wor
     for (int e = 0; e < VN; ++e) xs[row * (D + 1) + v * VN + e] = xv[e];
   }
   __syncthreads();
-  if (tid >= nrow) return;
-  const int r = r0 + tid;
+  if (tid < K) {
+    float a = 0.f;
+    for (int d = 0; d < D; ++d) a = fadd(a, fmul(mu[tid * (D + 1) + d], mu[tid * (D + 1) + d]));
+    mm[tid] = a;
+  }
+  const int tok = tid / slots, c = tid % slots;
+  if (tok < nrow) {
+    const float* x = xs + tok * (D + 1);
+    if (c < K) {
+      const float* m = mu + c * (D + 1);
+      float dot = 0.f, ex = 0.f;
+      for (int d = 0; d < D; ++d) {
+        dot = fadd(dot, fmul(x[d], m[d]));
+        const float df = fsub(x[d], m[d]);
+        ex = fadd(ex, fmul(df, df));
+      }
+      sem[tok * K + c] = dot;  // raw dot; the semantic distance needs |x|^2 and |mu|^2 below
+      exd[tok * K + c] = ex;
+    }
+    if (c == (K < slots ? K : 0)) {
+      float xx = 0.f;
+      for (int d = 0; d < D; ++d) xx = fadd(xx, fmul(x[d], x[d]));
+      xxs[tok] = xx;
+    }
+  }
+  __syncthreads();
+  if (c != 0 || tok >= nrow) return;
+  const int r = r0 + tok;
   const int64_t pos = token_position(g, s, w, b, arch[r]);
-  const float* x = xs + tid * (D + 1);
-  float xx = 0.f;
-  for (int d = 0; d < D; ++d) xx = fadd(xx, fmul(x[d], x[d]));
+  const float xx = xxs[tok];
   const float thresh = fmul(g.lam, s.s_h[(size_t)b * g.G + grp]);
   float best_cost = INFINITY, s_win = 0.f, best_ex = INFINITY, sem0 = 0.f;
   int winner = 0, nearest = 0;
   bool any_alive = false;
-  // Clusters in blocks of 16: 32 independent left-to-right accumulations per feature.
-  constexpr int CB = 16;
-  for (int cb = 0; cb < K; cb += CB) {
-    float dot[CB], ex[CB];
-#pragma unroll
-    for (int j = 0; j < CB; ++j) dot[j] = ex[j] = 0.f;
-    const int nc = min(CB, K - cb);
-    for (int d = 0; d < D; ++d) {
-      const float xd = x[d];
-#pragma unroll
-      for (int j = 0; j < CB; ++j) {
-        if (j < nc) {
-          const float m = mu[(cb + j) * D + d];
-          dot[j] = fadd(dot[j], fmul(xd, m));
-          const float df = fsub(xd, m);
-          ex[j] = fadd(ex[j], fmul(df, df));
-        }
-      }
+  for (int cc = 0; cc < K; ++cc) {
+    const float semv = fmaxf(fsub(fadd(xx, mm[cc]), fmul(2.f, sem[tok * K + cc])), 0.f);
+    if (cc == 0) sem0 = semv;
+    if (!alv[cc]) continue;
+    any_alive = true;
+    const float gap = fmaxf((float)(pos - (int64_t)phi[cc]), 0.f);
+    const float cost = fadd(semv, fmul(g.eta, fdiv(gap, fadd(gap, g.g0))));
+    if (cost < best_cost) {
+      best_cost = cost;
+      winner = cc;
+      s_win = semv;
     }
-#pragma unroll
-    for (int j = 0; j < CB; ++j) {
-      if (j >= nc) continue;
-      const int c = cb + j;
-      const float sem = fmaxf(fsub(fadd(xx, mm[c]), fmul(2.f, dot[j])), 0.f);
-      if (c == 0) sem0 = sem;
-      if (!alv[c]) continue;
-      any_alive = true;
-      const float gap = fmaxf((float)(pos - (int64_t)phi[c]), 0.f);
-      const float cost = fadd(sem, fmul(g.eta, fdiv(gap, fadd(gap, g.g0))));
-      if (cost < best_cost) {
-        best_cost = cost;
-        winner = c;
-        s_win = sem;
-      }
-      const float dist = __fsqrt_rn(ex[j]);
-      if (dist < best_ex) {
-        best_ex = dist;
-        nearest = c;
-      }
+    const float dist = __fsqrt_rn(exd[tok * K + cc]);
+    if (dist < best_ex) {
+      best_ex = dist;
+      nearest = cc;
     }
   }
   if (!any_alive) {
@@ -149,33 +153,25 @@ __device__ ArgMax block_argmax(ArgMax v, ArgMax* sh) {
   return out;
 }
 
-// Left-to-right squared distance between a storage row (read 16 bytes at a time) and a float row.
-template <typename T>
-__device__ __forceinline__ float sq_dist_rows(const T* a, const float* b, int D) {
-  constexpr int VN = Vec<T>::N;
-  float acc = 0.f;
-#pragma unroll 4
-  for (int v = 0; v < D / VN; ++v) {
-    float xa[VN];
-    unpack(*reinterpret_cast<const uint4*>(a + v * VN), xa, (const T*)nullptr);
-#pragma unroll
-    for (int e = 0; e < VN; ++e) {
-      const float df = fsub(xa[e], b[v * VN + e]);
-      acc = fadd(acc, fmul(df, df));
-    }
-  }
-  return acc;
-}
+// ---------------------------------------------------------------- K5a: farthest-point seeding
+// Runs only for lanes with free cluster slots and orphans (in practice the first
+// flushes of a stream).  One thread-block cluster of kSeedCluster CTAs per
+// (batch, group) lane: each CTA stages its share of the archived token rows in
+// shared memory (odd 32-bit word stride, conflict-free), the per-pick argmax is
+// exchanged through distributed shared memory, and the picks follow
+// _semantic_attach_plan_torch (log_kv_cache.py:4636-4680): the first pick is the
+// orphan with the largest semantic distance to its winner, every next pick the
+// orphan farthest (by its minimum distance) from all picks so far; then every
+// orphan joins the nearest live or seeded cluster.  Lanes without seeds exit at
+// once (uniformly across the cluster).
+constexpr int kSeedCluster = 8;
 
-// ---------------------------------------------------------------- K5: seeding + commit plan
-// One block per (batch, group) lane.  Seeds: up to min(free slots, orphans)
-// farthest-point picks among orphans; orphans then join the nearest live or
-// seeded cluster.  Then a stable counting sort groups the archived tokens by
-// cluster and each cluster's job (ordinary, new, delayed) and scratch range
-// are planned.
 template <typename T>
-__global__ void __launch_bounds__(1024) plan_kernel(Geo g, logkv_state_t s, Work w) {
-  const int b = blockIdx.y, grp = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+__global__ void __cluster_dims__(kSeedCluster, 1, 1) __launch_bounds__(512) seed_kernel(Geo g, logkv_state_t s, Work w) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int grp = blockIdx.x / kSeedCluster, b = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
   const int D = g.D, K = g.K;
   const int na = w.narch[b];
   const size_t lane0 = ((size_t)b * g.G + grp) * K;
@@ -185,13 +181,12 @@ __global__ void __launch_bounds__(1024) plan_kernel(Geo g, logkv_state_t s, Work
   const int* arch = w.arch_idx + (size_t)b * g.NW;
   const T* snap = static_cast<const T*>(w.snap_k);
   const T* rec = static_cast<const T*>(s.recent_k_raw);
-  extern __shared__ float dist[];  // [NW]
-  __shared__ ArgMax red[32];
-  __shared__ int wsum[32];
   __shared__ int free_slots[kMaxClusters];
   __shared__ int picks[kMaxClusters];
-  __shared__ int sh_nfree, sh_norph;
-  __shared__ float prow[1024];  // pick row (D <= 1024)
+  __shared__ int cand[kMaxClusters];
+  __shared__ int sh_nfree, sh_norph, sh_pick;
+  __shared__ ArgMax red[32];
+  __shared__ ArgMax slot[2];
   if (tid == 0) {
     int nf = 0;
     for (int c = 0; c < K; ++c)
@@ -200,73 +195,128 @@ __global__ void __launch_bounds__(1024) plan_kernel(Geo g, logkv_state_t s, Work
     sh_norph = 0;
   }
   __syncthreads();
-  int my_orph = 0;
-  for (int t = tid; t < na; t += nt) my_orph += orph[t];
-  atomicAdd(&sh_norph, my_orph);
+  int my = 0;
+  for (int t = tid; t < na; t += nt) my += orph[t];
+  atomicAdd(&sh_norph, my);
   __syncthreads();
   const int n_use = min(sh_nfree, sh_norph);
-  if (n_use > 0) {
+  if (n_use == 0) return;  // same decision in every CTA of the cluster
+  const int chunk = (na + kSeedCluster - 1) / kSeedCluster;
+  const int t_lo = min(na, rank * chunk), t_hi = min(na, t_lo + chunk), nloc = t_hi - t_lo;
+  // Dynamic shared memory: prow [D] f32 | mus [K][D+1] f32 | dist [chunk] f32 | cdist [chunk][K] f32 | rows.
+  extern __shared__ float sm[];
+  float* prow = sm;
+  float* mus = prow + D;
+  float* dist = mus + K * (D + 1);
+  float* cdist = dist + chunk;
+  const int rs = D + 4 / (int)sizeof(T);  // row stride in elements: an odd number of 32-bit words
+  T* rows = reinterpret_cast<T*>(cdist + (size_t)chunk * K);
+  const bool staged = g.seed_staged != 0;
+  constexpr int VN = Vec<T>::N;
+  if (staged) {
+    for (int item = tid; item < nloc * (D / VN); item += nt) {
+      const int t = item / (D / VN), v = item % (D / VN);
+      const uint4 u = *reinterpret_cast<const uint4*>(token_row<T>(g, snap, rec, b, grp, arch[t_lo + t]) + v * VN);
+      const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int j = 0; j < VN; ++j) rows[(size_t)t * rs + v * VN + j] = e[j];
+    }
+  }
+  __syncthreads();
+  auto xval = [&](int tl, int d) -> float {
+    return staged ? Elem<T>::load(rows + (size_t)tl * rs + d)
+                  : Elem<T>::load(token_row<T>(g, snap, rec, b, grp, arch[t_lo + tl]) + d);
+  };
+  for (int i = 0; i < n_use; ++i) {
     ArgMax a{-INFINITY, 0x7fffffff};
-    for (int t = tid; t < na; t += nt) a = argmax_better(a, ArgMax{orph[t] ? w.s_winner[row0 + t] : -INFINITY, t});
-    ArgMax best = block_argmax(a, red);
-    int nxt = best.i;
-    if (tid == 0) picks[0] = nxt;
-    for (int d = tid; d < D; d += nt) prow[d] = Elem<T>::load(token_row<T>(g, snap, rec, b, grp, arch[nxt]) + d);
+    for (int tl = tid; tl < nloc; tl += nt) {
+      const int t = t_lo + tl;
+      const float v = i == 0 ? (orph[t] ? w.s_winner[row0 + t] : -INFINITY) : dist[tl];
+      a = argmax_better(a, ArgMax{v, t});
+    }
+    a = block_argmax(a, red);
+    if (tid == 0) slot[i & 1] = a;
+    cluster.sync();
+    if (tid == 0) {
+      ArgMax best{-INFINITY, 0x7fffffff};
+      for (int r = 0; r < kSeedCluster; ++r) best = argmax_better(best, *cluster.map_shared_rank(&slot[i & 1], r));
+      sh_pick = best.i;
+      picks[i] = best.i;
+    }
     __syncthreads();
-    for (int t = tid; t < na; t += nt)
-      dist[t] = orph[t] ? sq_dist_rows<T>(token_row<T>(g, snap, rec, b, grp, arch[t]), prow, D) : -INFINITY;
+    const int pick = sh_pick;
+    for (int d = tid; d < D; d += nt) prow[d] = Elem<T>::load(token_row<T>(g, snap, rec, b, grp, arch[pick]) + d);
     __syncthreads();
-    for (int i = 1; i < n_use; ++i) {
-      if (tid == 0) dist[nxt] = -INFINITY;
-      __syncthreads();
-      ArgMax m{-INFINITY, 0x7fffffff};
-      for (int t = tid; t < na; t += nt) m = argmax_better(m, ArgMax{dist[t], t});
-      nxt = block_argmax(m, red).i;
-      if (tid == 0) picks[i] = nxt;
-      for (int d = tid; d < D; d += nt) prow[d] = Elem<T>::load(token_row<T>(g, snap, rec, b, grp, arch[nxt]) + d);
-      __syncthreads();
-      for (int t = tid; t < na; t += nt) {
-        const float cur = dist[t];
-        const float nd = sq_dist_rows<T>(token_row<T>(g, snap, rec, b, grp, arch[t]), prow, D);
-        dist[t] = fminf(cur, nd);
+    for (int tl = tid; tl < nloc; tl += nt) {
+      const int t = t_lo + tl;
+      float acc = 0.f;
+      for (int d = 0; d < D; ++d) {
+        const float df = fsub(xval(tl, d), prow[d]);
+        acc = fadd(acc, fmul(df, df));
       }
-      __syncthreads();
+      float v = i == 0 ? (orph[t] ? acc : -INFINITY) : fminf(dist[tl], acc);
+      if (t == pick) v = -INFINITY;  // a pick is never picked again
+      dist[tl] = v;
     }
-    // Orphans join the nearest live or seeded cluster (exact distance, lowest id on ties).
-    // Candidate centres (live centroids, seed tokens for the opened slots) staged as float32.
-    float* mus = dist + ((g.NW + 3) & ~3);  // [K][D]
-    __shared__ int cand[kMaxClusters];
-    if (tid < K) cand[tid] = s.alive[lane0 + tid] != 0;
-    __syncthreads();
-    for (int i = tid; i < K * D; i += nt) mus[i] = s.centroid[lane0 * D + i];
-    __syncthreads();
-    for (int i = 0; i < n_use; ++i) {
-      const int c = free_slots[i];
-      if (tid == 0) cand[c] = 1;
-      for (int d = tid; d < D; d += nt)
-        mus[c * D + d] = Elem<T>::load(token_row<T>(g, snap, rec, b, grp, arch[picks[i]]) + d);
-    }
-    __syncthreads();
-    for (int t = tid; t < na; t += nt) {
-      if (!orph[t]) continue;
-      const T* x = token_row<T>(g, snap, rec, b, grp, arch[t]);
-      float best_d = INFINITY;
-      int best_c = 0;
-      for (int c = 0; c < K; ++c) {
-        if (!cand[c]) continue;
-        const float dd = __fsqrt_rn(sq_dist_rows<T>(x, mus + c * D, D));
-        if (dd < best_d) {
-          best_d = dd;
-          best_c = c;
-        }
-      }
-      asg[t] = (int8_t)best_c;
-    }
-    __syncthreads();
-    if (tid == 0)
-      for (int i = 0; i < n_use; ++i) asg[picks[i]] = (int8_t)free_slots[i];
     __syncthreads();
   }
+  // Orphans join the nearest live or seeded cluster: one (token, cluster) pair per thread.
+  if (tid < K) cand[tid] = s.alive[lane0 + tid] != 0;
+  for (int i = tid; i < K * D; i += nt) mus[(i / D) * (D + 1) + i % D] = s.centroid[lane0 * D + i];
+  __syncthreads();
+  for (int i = 0; i < n_use; ++i) {
+    const int c = free_slots[i];
+    if (tid == 0) cand[c] = 1;
+    for (int d = tid; d < D; d += nt)
+      mus[c * (D + 1) + d] = Elem<T>::load(token_row<T>(g, snap, rec, b, grp, arch[picks[i]]) + d);
+  }
+  __syncthreads();
+  for (int item = tid; item < nloc * K; item += nt) {
+    const int tl = item / K, c = item % K;
+    float out = INFINITY;
+    if (orph[t_lo + tl] && cand[c]) {
+      float acc = 0.f;
+      for (int d = 0; d < D; ++d) {
+        const float df = fsub(xval(tl, d), mus[c * (D + 1) + d]);
+        acc = fadd(acc, fmul(df, df));
+      }
+      out = __fsqrt_rn(acc);
+    }
+    cdist[item] = out;
+  }
+  __syncthreads();
+  for (int tl = tid; tl < nloc; tl += nt) {
+    if (!orph[t_lo + tl]) continue;
+    float best = INFINITY;
+    int bc = 0;
+    for (int c = 0; c < K; ++c)
+      if (cdist[tl * K + c] < best) {
+        best = cdist[tl * K + c];
+        bc = c;
+      }
+    asg[t_lo + tl] = (int8_t)bc;
+  }
+  __syncthreads();
+  if (tid == 0)
+    for (int i = 0; i < n_use; ++i)
+      if (picks[i] >= t_lo && picks[i] < t_hi) asg[picks[i]] = (int8_t)free_slots[i];
+  cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
+}
+
+// ---------------------------------------------------------------- K5b: commit plan
+// One block per (batch, group) lane: a stable counting sort groups the archived
+// tokens by cluster, then each cluster's job (ordinary, new, delayed) and scratch
+// range are planned.
+template <typename T>
+__global__ void __launch_bounds__(1024) plan_kernel(Geo g, logkv_state_t s, Work w) {
+  const int b = blockIdx.y, grp = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+  const int K = g.K;
+  const int na = w.narch[b];
+  const size_t lane0 = ((size_t)b * g.G + grp) * K;
+  const size_t row0 = ((size_t)b * g.G + grp) * g.NW;
+  const int8_t* asg = w.assign + row0;
+  const int* arch = w.arch_idx + (size_t)b * g.NW;
+  __shared__ int wsum[32];
   // Stable counting sort of archive ranks by cluster.
   __shared__ int cl_count[kMaxClusters], cl_off[kMaxClusters];
   __shared__ int tot;
