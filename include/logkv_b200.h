@@ -157,8 +157,9 @@ LOGKV_API int logkv_flush_profiled(const logkv_layout_t* layout, const logkv_sta
  * since the workspace was zeroed) to out, synchronizing `stream`: [0] stored
  * level rows read, [1] incoming rows read, [2] survivor rows written, [3] rows
  * appended, [4] rows zeroed, [5] merged rows carried up, [6] rows gathered for
- * delayed re-inserts, [7] flushes.  The workspace must be zero-filled once
- * when it is allocated.
+ * delayed re-inserts, [7] flushes, [8] Beta groups whose cut was a near tie and
+ * was decided by the canonical sequential evaluation.  The workspace must be
+ * zero-filled once when it is allocated.
  */
 LOGKV_API int logkv_read_counters(const void* workspace, uint64_t* out, int32_t n, void* stream);
 

@@ -22,7 +22,7 @@ DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1}
 
 FLUSH_STAGES = ("snapshot", "span_cut", "span_score", "choose", "attach", "plan", "prepare", "cascade",
                 "pool_rewrite", "window_shift")
-COUNTERS = ("storage_read", "stage_read", "survivor", "fill", "clear", "carry", "gather", "flushes")
+COUNTERS = ("storage_read", "stage_read", "survivor", "fill", "clear", "carry", "gather", "flushes", "exact_cuts")
 
 
 class Layout(ctypes.Structure):

@@ -24,7 +24,17 @@
 namespace logkv {
 
 static size_t cascade_smem(const Geo& g, size_t esize) {
-  return 2 * (size_t)kTileRows * g.D * esize + (size_t)kTileRows * sizeof(Meta) + (size_t)g.NW * sizeof(int) + 16;
+  // two K/V tile buffers, two metadata tiles, token positions and sources
+  return 4 * (size_t)kTileRows * g.D * esize + 2 * (size_t)kTileRows * sizeof(Meta) +
+         (size_t)g.NW * (sizeof(int64_t) + sizeof(int)) + 16;
+}
+
+// Cascade launch for one (dtype, Beta, head dim) instantiation; DC = 0 is the runtime-D kernel.
+template <typename T, bool BETA, int DC>
+static void launch_cascade(const Geo& g, const logkv_state_t& s, const Work& w, size_t smem, cudaStream_t st) {
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(cascade_kernel<T, BETA, DC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cascade_kernel<T, BETA, DC><<<dim3(g.K, g.G, g.B), 512, smem, st>>>(g, s, w);
 }
 
 // ---------------------------------------------------------------- K8: window shift
@@ -265,13 +275,13 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   mark();
   const size_t casc_smem = cascade_smem(g, sizeof(T));
   if (g.beta) {
-    if (casc_smem > 48 * 1024)
-      cudaFuncSetAttribute(cascade_kernel<T, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)casc_smem);
-    cascade_kernel<T, true><<<dim3(g.K, g.G, g.B), 512, casc_smem, st>>>(g, s, w);
+    if (g.D == 128) launch_cascade<T, true, 128>(g, s, w, casc_smem, st);
+    else if (g.D == 64) launch_cascade<T, true, 64>(g, s, w, casc_smem, st);
+    else launch_cascade<T, true, 0>(g, s, w, casc_smem, st);
   } else {
-    if (casc_smem > 48 * 1024)
-      cudaFuncSetAttribute(cascade_kernel<T, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)casc_smem);
-    cascade_kernel<T, false><<<dim3(g.K, g.G, g.B), 512, casc_smem, st>>>(g, s, w);
+    if (g.D == 128) launch_cascade<T, false, 128>(g, s, w, casc_smem, st);
+    else if (g.D == 64) launch_cascade<T, false, 64>(g, s, w, casc_smem, st);
+    else launch_cascade<T, false, 0>(g, s, w, casc_smem, st);
   }
   mark();
   pool_rewrite_kernel<T><<<dim3(per_bg, g.G, g.B), 256, 0, st>>>(g, s, w);

@@ -1,10 +1,13 @@
 // Ladder cascade (K6b): one CTA per (batch, group, cluster) lane walks the
 // levels; each overflowing level streams its pool through shared memory in
-// tiles of kTileRows rows with 16-byte vector loads/stores.
+// tiles of kTileRows rows.  Tiles are double-buffered: while tile t is merged,
+// tile t+1's K/V rows are already in flight (cp.async, 16 bytes per copy) and
+// its metadata is loading into registers.
 //
-// Hazard-free in place: tile t is fully staged before any of its outputs are
-// written, and survivors land in slots below the tile's first row, all of
-// which are already staged; merged rows go to the other scratch buffer.
+// Hazard-free in place: a tile is fully staged before any of its outputs are
+// written, survivors land in slots below the tile's last row (all staged
+// already), the prefetched tile lies above every slot written so far, and
+// merged rows go to the other scratch buffer.
 #pragma once
 
 #include "flush_ladder.cuh"
@@ -14,34 +17,182 @@ namespace logkv {
 constexpr int kTileRows = 64;                 // multiple of 4 (Beta groups never straddle tiles)
 constexpr int kTileGroups = kTileRows / 4;
 
-template <typename T, bool BETA>
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+// Beta cut of one group of four rows, one warp, certified against the canonical order.
+//
+// The canonical cost (beta_log_kv.select_cuts, beta_log_kv.py:29-46) sums every
+// squared deviation left to right over the features in one thread.  Here each
+// lane sums its strided features and the warp adds the partials; the per-feature
+// means and squared terms are computed exactly as in the canonical order, so only
+// the order of adding non-negative terms differs.  For a sum of n non-negative
+// terms that changes the result by at most about 2(n-1)u relative (u = 2^-24), so
+// every cost lies within ~4e-5 relative of its canonical value.  When the best
+// cost beats the runner-up by more than 1e-3 relative the canonical argmin is the
+// same cut; otherwise -1 asks for the canonical evaluation.
+// Energy and the three cut costs of one component (K or V): NPL > 0 features per lane
+// held in registers (compile-time head dim), else read from shared memory per use.
+template <typename T, int NPL>
+__device__ __forceinline__ void beta_costs_comp(const T* base, int start, int D, int lane, const float* wv,
+                                                float tot, float* costs) {
+  constexpr int NR = NPL > 0 ? NPL : 1;
+  float xr[4][NR];
+  if constexpr (NPL > 0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < NPL; ++j) xr[i][j] = Elem<T>::load(base + (start + i) * D + lane + 32 * j);
+  }
+  auto x_at = [&](int i, int j) -> float {
+    if constexpr (NPL > 0) return xr[i][j];
+    else return Elem<T>::load(base + (start + i) * D + lane + 32 * j);
+  };
+  const int nj = NPL > 0 ? NPL : (D - lane + 31) / 32;
+  float e[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < (NPL > 0 ? NPL : 1); ++j) {
+    if constexpr (NPL > 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float xv = x_at(i, j);
+        e[i] = fadd(e[i], fmul(xv, xv));
+      }
+    } else {
+#pragma unroll 1
+      for (int jj = 0; jj < nj; ++jj)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float xv = x_at(i, jj);
+          e[i] = fadd(e[i], fmul(xv, xv));
+        }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) e[i] = fadd(e[i], __shfl_xor_sync(0xffffffffu, e[i], off));
+  float acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc = fadd(acc, fmul(e[i], wv[i]));
+  const float energy = fmaxf(fdiv(acc, tot), 1e-12f);
+#pragma unroll
+  for (int jc = 0; jc < 3; ++jc) {
+    const int cut = jc == 0 ? 2 : (jc == 1 ? 1 : 3);
+#pragma unroll
+    for (int side = 0; side < 2; ++side) {
+      float om[4];
+      float ws = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const bool in = side == 0 ? (i < cut) : (i >= cut);
+        om[i] = fmul(wv[i], in ? 1.f : 0.f);
+        ws = fadd(ws, om[i]);
+      }
+      const float den = fmaxf(ws, 1e-12f);
+      float r[4] = {0.f, 0.f, 0.f, 0.f};
+      auto feature = [&](int j) {
+        float xv[4];
+        float sacc = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          xv[i] = x_at(i, j);
+          sacc = fadd(sacc, fmul(xv[i], om[i]));
+        }
+        const float mean = fdiv(sacc, den);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float df = fsub(xv[i], mean);
+          r[i] = fadd(r[i], fmul(df, df));
+        }
+      };
+      if constexpr (NPL > 0) {
+#pragma unroll
+        for (int j = 0; j < NPL; ++j) feature(j);
+      } else {
+#pragma unroll 1
+        for (int j = 0; j < nj; ++j) feature(j);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) r[i] = fadd(r[i], __shfl_xor_sync(0xffffffffu, r[i], off));
+      float loss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) loss = fadd(loss, fmul(r[i], om[i]));
+      costs[jc] = fadd(costs[jc], fdiv(loss, energy));
+    }
+  }
+}
+
+template <typename T, int DC>
+__device__ int beta_cut_warp(const T* tk, const T* tv, const Meta* tm, int start, int Drt, int lane) {
+  const int D = DC ? DC : Drt;
+  // Features of this lane: d = lane + 32 j.  With a compile-time D that is a multiple of
+  // 32 they are read once per component into registers.
+  constexpr int NPL = (DC >= 32 && DC % 32 == 0) ? DC / 32 : 0;
+  float wv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) wv[i] = tm[start + i].w;
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) tot = fadd(tot, wv[i]);
+  tot = fmaxf(tot, 1e-12f);
+  float costs[3] = {0.f, 0.f, 0.f};
+  beta_costs_comp<T, NPL>(tk, start, D, lane, wv, tot, costs);
+  beta_costs_comp<T, NPL>(tv, start, D, lane, wv, tot, costs);
+  int best = 0;
+  if (costs[1] < costs[best]) best = 1;
+  if (costs[2] < costs[best]) best = 2;
+  float second = INFINITY;
+#pragma unroll
+  for (int j = 0; j < 3; ++j)
+    if (j != best) second = fminf(second, costs[j]);
+  if (!(second - costs[best] > 1e-3f * second)) return -1;  // near tie (or NaN): canonical evaluation
+  return best == 0 ? 2 : (best == 1 ? 1 : 3);
+}
+
+template <typename T, bool BETA, int DC>
 __global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Work w) {
   LaneCtx<T> x = make_ctx<T>(g, s, w);
   const int type = w.plan_type[x.lane];
   if (type == kJobNone) return;
   constexpr int VN = Vec<T>::N;
-  const int tid = threadIdx.x, nt = blockDim.x, D = g.D, Bs = g.Bs, DV = g.D / VN;
+  const int tid = threadIdx.x, nt = blockDim.x, Bs = g.Bs;
+  // Compile-time head dim when DC != 0: every row/vector index map becomes shifts.
+  const int D = DC ? DC : g.D, DV = D / VN;
   extern __shared__ uint4 smem4[];
-  T* tk = reinterpret_cast<T*>(smem4);                 // [kTileRows][D]
-  T* tv = tk + (size_t)kTileRows * D;                  // [kTileRows][D]
-  Meta* tm = reinterpret_cast<Meta*>(tv + (size_t)kTileRows * D);  // [kTileRows]
-  int* srcs = reinterpret_cast<int*>(tm + kTileRows);  // [NW] token sources
+  T* tkb = reinterpret_cast<T*>(smem4);                                 // [2][kTileRows][D]
+  T* tvb = tkb + 2 * (size_t)kTileRows * D;                             // [2][kTileRows][D]
+  Meta* tmb = reinterpret_cast<Meta*>(tvb + 2 * (size_t)kTileRows * D);  // [2][kTileRows]
+  int64_t* tpos = reinterpret_cast<int64_t*>(tmb + 2 * kTileRows);      // [NW] token positions
+  int* srcs = reinterpret_cast<int*>(tpos + g.NW);                      // [NW] token sources
   __shared__ float bloss[kTileGroups][12];
   __shared__ float bener[kTileGroups][2];
   __shared__ int bcut[kTileGroups];
+  __shared__ int sh_exact;  // groups of the current tile needing the canonical cost order
+  if (threadIdx.x == 0) sh_exact = 0;
   T* LK = static_cast<T*>(s.level_k);
   T* LV = static_cast<T*>(s.level_v);
   T* SK = static_cast<T*>(w.sk);
   T* SV = static_cast<T*>(w.sv);
   const int ntok = type == kJobLate ? 0 : w.plan_n[x.lane];
-  for (int i = tid; i < ntok; i += nt) srcs[i] = x.arch[x.toks[x.toff + i]];
+  for (int i = tid; i < ntok; i += nt) {
+    const int src = x.arch[x.toks[x.toff + i]];
+    srcs[i] = src;
+    tpos[i] = token_position(g, s, w, x.b, src);
+  }
   __syncthreads();
   Stage st;
   st.kind = type == kJobLate ? 1 : 0;
   st.buf = 0;
   st.m = w.plan_m0[x.lane];
   int nb = 1;
-  // Row pointers of incoming rows (tokens through the source table, else scratch).
+  // Incoming rows: tokens through the source table, else scratch rows.
   auto stage_k = [&](int i) -> const T* {
     if (st.kind == 0) return token_row<T>(g, x.snapk, x.reck, x.b, x.grp, srcs[i]);
     return SK + x.scr_row(st.buf, i) * D;
@@ -52,7 +203,7 @@ __global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Wo
   };
   auto stage_meta = [&](int i) -> Meta {
     if (st.kind == 0) {
-      const int64_t p = token_position(g, s, w, x.b, srcs[i]);
+      const int64_t p = tpos[i];
       return Meta{1.f, p, p, p, x.base_order + i, 0};
     }
     const size_t r = x.scr_row(st.buf, i);
@@ -92,8 +243,10 @@ __global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Wo
     const int rem = cnt + m - Bs;
     if (ell == g.L - 1) {
       // Saturated top level (rare): slot 0 = left fold of pool[0..rem], rounded each step;
-      // slots 1.. = pool[rem+1..].  Pool rows are read straight from their sources; the
-      // shifted rows are staged through registers in two passes to avoid overlap.
+      // slots 1.. = pool[rem+1..].  Staged through tile buffer 0 (row 0 holds the fold).
+      T* tk = tkb;
+      T* tv = tvb;
+      Meta* tm = tmb;
       for (int d = tid; d < D; d += nt) {
         float ak = Elem<T>::load(pool_k(0) + d), av = Elem<T>::load(pool_v(0) + d);
         float aw = pool_m(0).w;
@@ -105,7 +258,6 @@ __global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Wo
           av = Elem<T>::round(fadd(fmul(alpha, av), fmul(beta, Elem<T>::load(pool_v(t) + d))));
           aw = fadd(aw, bw);
         }
-        // The folded entry waits in tile row 0 until every shifted source row is staged.
         Elem<T>::store(tk + d, ak);
         Elem<T>::store(tv + d, av);
       }
@@ -115,8 +267,7 @@ __global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Wo
         tm[0] = acc;
       }
       __syncthreads();
-      // Shift: slot j (1 <= j < Bs) <- pool[rem + j].  Sources at p = rem + j > j, processed
-      // in tiles of ascending j, staged before written.
+      // Shift: slot j (1 <= j < Bs) <- pool[rem + j]; sources lie above the written slots.
       for (int j0 = 1; j0 < Bs; j0 += kTileRows - 1) {
         const int jn = min(kTileRows - 1, Bs - j0);
         for (int item = tid; item < jn * D; item += nt) {
@@ -151,16 +302,31 @@ __global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Wo
     const int ncarry = npair / 2;
     const int nsurv = cnt + m - npair;
     const int total = cnt + m;
-    for (int t0 = 0; t0 < total; t0 += kTileRows) {
+    // Issue the asynchronous K/V copies of the tile starting at pool row t0 into buffer `buf`;
+    // the calling thread's metadata row (if any) is returned through `pend`.
+    Meta pend{};
+    auto issue = [&](int t0, int buf) {
       const int tn = min(kTileRows, total - t0);
-      // Stage the tile (K and V rows, 16 B per access) and its metadata.
+      T* tk = tkb + (size_t)buf * kTileRows * D;
+      T* tv = tvb + (size_t)buf * kTileRows * D;
       for (int item = tid; item < tn * DV * 2; item += nt) {
         const int r = item / (2 * DV), f = (item / DV) & 1, v = item % DV;
-        const T* src = (f ? pool_v(t0 + r) : pool_k(t0 + r)) + v * VN;
-        *reinterpret_cast<uint4*>((f ? tv : tk) + r * D + v * VN) = *reinterpret_cast<const uint4*>(src);
+        cp_async16((f ? tv : tk) + r * D + v * VN, (f ? pool_v(t0 + r) : pool_k(t0 + r)) + v * VN);
       }
-      for (int r = tid; r < tn; r += nt) tm[r] = pool_m(t0 + r);
+      cp_async_commit();
+      if (tid < tn) pend = pool_m(t0 + tid);
+    };
+    issue(0, 0);
+    int cur = 0;
+    for (int t0 = 0; t0 < total; t0 += kTileRows) {
+      const int tn = min(kTileRows, total - t0);
+      T* tk = tkb + (size_t)cur * kTileRows * D;
+      T* tv = tvb + (size_t)cur * kTileRows * D;
+      Meta* tm = tmb + cur * kTileRows;
+      cp_async_wait_all();
+      if (tid < tn) tm[tid] = pend;
       __syncthreads();
+      if (t0 + kTileRows < total) issue(t0 + kTileRows, cur ^ 1);
       const int mend = min(t0 + tn, npair);  // merge rows of this tile: [t0, mend)
       if (mend > t0) {
         if (!BETA) {
@@ -182,11 +348,23 @@ __global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Wo
           for (int j = tid; j < jn; j += nt) x.put_scratch(nb, j0 + j, merge_meta(tm[2 * j], tm[2 * j + 1]));
         } else {
           const int qn = (mend - t0 + 3) / 4;  // groups of this tile (tile rows 4q..4q+3)
+          // Certified warp-parallel cut per group; near ties fall back to the canonical order below.
+          const int warp = tid >> 5, lane = tid & 31, nwarps = nt >> 5;
+          for (int q = warp; q < qn; q += nwarps) {
+            const int width = min(4, npair - (t0 + 4 * q));
+            const int cut = width == 4 ? beta_cut_warp<T, DC>(tk, tv, tm, 4 * q, D, lane) : 1;
+            if (lane == 0) {
+              bcut[q] = cut;
+              if (cut < 0) atomicAdd(&sh_exact, 1);
+            }
+          }
+          __syncthreads();
+          if (sh_exact) {
           for (int item = tid; item < qn * 14; item += nt) {
             const int q = item / 14, k = item % 14;
-            const int start = 4 * q;                       // tile row of the group
+            const int start = 4 * q;
             const int width = min(4, npair - (t0 + start));
-            if (width != 4) continue;
+            if (width != 4 || bcut[q] >= 0) continue;
             float wv[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) wv[i] = tm[start + i].w;
@@ -194,6 +372,7 @@ __global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Wo
             const T* base = comp == 0 ? tk : tv;
             if (k >= 12) {
               float e[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
               for (int d = 0; d < D; ++d)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -220,6 +399,7 @@ __global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Wo
               }
               const float den = fmaxf(ws, 1e-12f);
               float r[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
               for (int d = 0; d < D; ++d) {
                 float xv[4];
                 float sacc = 0.f;
@@ -243,11 +423,7 @@ __global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Wo
           }
           __syncthreads();
           for (int q = tid; q < qn; q += nt) {
-            const int width = min(4, npair - (t0 + 4 * q));
-            if (width != 4) {
-              bcut[q] = 1;
-              continue;
-            }
+            if (bcut[q] >= 0) continue;
             float costs[3] = {0.f, 0.f, 0.f};
             for (int comp = 0; comp < 2; ++comp)
               for (int j = 0; j < 3; ++j)
@@ -259,6 +435,11 @@ __global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Wo
             bcut[q] = best == 0 ? 2 : (best == 1 ? 1 : 3);
           }
           __syncthreads();
+          if (tid == 0) {
+            atomicAdd(&w.counters[kCntExactCuts], (unsigned long long)sh_exact);
+            sh_exact = 0;
+          }
+          }
           // Apply: per output side, sum over member rows (row order) of w*x / max(mass, 1e-12).
           for (int item = tid; item < qn * 2 * 2 * DV; item += nt) {
             const int q = item / (4 * DV), side = (item / (2 * DV)) & 1, f = (item / DV) & 1, v = item % DV;
@@ -331,6 +512,7 @@ __global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Wo
         for (int r = tid; r < sn; r += nt) x.put_level_meta(lrow0 + sbeg + r - npair, tm[sbeg + r - t0]);
       }
       __syncthreads();
+      cur ^= 1;
     }
     // Tail slots are zeroed.
     const int nclr = Bs - nsurv;

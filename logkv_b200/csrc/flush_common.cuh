@@ -34,7 +34,8 @@ enum Counter : int {
   kCntCarry = 5,         // merged rows written for the next level
   kCntGather = 6,        // rows gathered for delayed re-inserts
   kCntFlushes = 7,       // flush calls
-  kNumCounters = 8,
+  kCntExactCuts = 8,     // Beta groups whose cut needed the canonical-order evaluation (near ties)
+  kNumCounters = 9,
 };
 
 // Views into the caller's workspace (carved by the host in flush.cu).
