@@ -365,7 +365,9 @@ def main():
                     roofline=res["roofline"], flush_roofline=res["flush_roofline"], cpu_baseline=cpu,
                     clocks=res["clocks"], gpu_launches=res["launches"], stages_us=res["stages"],
                     stages_us_median=res["stages_med"], stages_us_max=res["stages_max"],
-                    flushes_per_step=res["flushes_per_step"])
+                    flushes_per_step=res["flushes_per_step"],
+                    rows_per_flush={k: round(v / res["flushes_per_step"], 1) for k, v in res["counters"].items()
+                                    if k != "flushes"})
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -24,127 +24,125 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
 
-// Beta cut of one group of four rows, one warp, certified against the canonical order.
-//
-// The canonical cost (beta_log_kv.select_cuts, beta_log_kv.py:29-46) sums every
-// squared deviation left to right over the features in one thread.  Here each
-// lane sums its strided features and the warp adds the partials; the per-feature
-// means and squared terms are computed exactly as in the canonical order, so only
-// the order of adding non-negative terms differs.  For a sum of n non-negative
-// terms that changes the result by at most about 2(n-1)u relative (u = 2^-24), so
-// every cost lies within ~4e-5 relative of its canonical value.  When the best
-// cost beats the runner-up by more than 1e-3 relative the canonical argmin is the
-// same cut; otherwise -1 asks for the canonical evaluation.
-// Energy and the three cut costs of one component (K or V): NPL > 0 features per lane
-// held in registers (compile-time head dim), else read from shared memory per use.
-template <typename T, int NPL>
-__device__ __forceinline__ void beta_costs_comp(const T* base, int start, int D, int lane, const float* wv,
-                                                float tot, float* costs) {
-  constexpr int NR = NPL > 0 ? NPL : 1;
-  float xr[4][NR];
-  if constexpr (NPL > 0) {
+// Sum 16 per-lane values over the warp; every lane gets all 16 sums.  Transposed
+// butterfly: each exchange halves the values a lane carries (16 shuffles), then one
+// shuffle per value gathers the sums (lane 2k holds sum k).
+__device__ __forceinline__ void warp_allreduce16(float* v, int lane) {
+  const unsigned full = 0xffffffffu;
+  float h8[8], h4[4], h2[2], h1;
+  const bool b4 = lane & 16, b3 = lane & 8, b2 = lane & 4, b1 = lane & 2;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+  for (int k = 0; k < 8; ++k)
+    h8[k] = (b4 ? v[k + 8] : v[k]) + __shfl_xor_sync(full, b4 ? v[k] : v[k + 8], 16);
 #pragma unroll
-      for (int j = 0; j < NPL; ++j) xr[i][j] = Elem<T>::load(base + (start + i) * D + lane + 32 * j);
-  }
-  auto x_at = [&](int i, int j) -> float {
-    if constexpr (NPL > 0) return xr[i][j];
-    else return Elem<T>::load(base + (start + i) * D + lane + 32 * j);
-  };
-  const int nj = NPL > 0 ? NPL : (D - lane + 31) / 32;
-  float e[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k = 0; k < 4; ++k)
+    h4[k] = (b3 ? h8[k + 4] : h8[k]) + __shfl_xor_sync(full, b3 ? h8[k] : h8[k + 4], 8);
 #pragma unroll
-  for (int j = 0; j < (NPL > 0 ? NPL : 1); ++j) {
-    if constexpr (NPL > 0) {
+  for (int k = 0; k < 2; ++k)
+    h2[k] = (b2 ? h4[k + 2] : h4[k]) + __shfl_xor_sync(full, b2 ? h4[k] : h4[k + 2], 4);
+  h1 = (b1 ? h2[1] : h2[0]) + __shfl_xor_sync(full, b1 ? h2[0] : h2[1], 2);
+  h1 += __shfl_xor_sync(full, h1, 1);  // lane l now holds sum number l >> 1
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float xv = x_at(i, j);
-        e[i] = fadd(e[i], fmul(xv, xv));
-      }
-    } else {
-#pragma unroll 1
-      for (int jj = 0; jj < nj; ++jj)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float xv = x_at(i, jj);
-          e[i] = fadd(e[i], fmul(xv, xv));
-        }
-    }
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) e[i] = fadd(e[i], __shfl_xor_sync(0xffffffffu, e[i], off));
-  float acc = 0.f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) acc = fadd(acc, fmul(e[i], wv[i]));
-  const float energy = fmaxf(fdiv(acc, tot), 1e-12f);
-#pragma unroll
-  for (int jc = 0; jc < 3; ++jc) {
-    const int cut = jc == 0 ? 2 : (jc == 1 ? 1 : 3);
-#pragma unroll
-    for (int side = 0; side < 2; ++side) {
-      float om[4];
-      float ws = 0.f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const bool in = side == 0 ? (i < cut) : (i >= cut);
-        om[i] = fmul(wv[i], in ? 1.f : 0.f);
-        ws = fadd(ws, om[i]);
-      }
-      const float den = fmaxf(ws, 1e-12f);
-      float r[4] = {0.f, 0.f, 0.f, 0.f};
-      auto feature = [&](int j) {
-        float xv[4];
-        float sacc = 0.f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          xv[i] = x_at(i, j);
-          sacc = fadd(sacc, fmul(xv[i], om[i]));
-        }
-        const float mean = fdiv(sacc, den);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float df = fsub(xv[i], mean);
-          r[i] = fadd(r[i], fmul(df, df));
-        }
-      };
-      if constexpr (NPL > 0) {
-#pragma unroll
-        for (int j = 0; j < NPL; ++j) feature(j);
-      } else {
-#pragma unroll 1
-        for (int j = 0; j < nj; ++j) feature(j);
-      }
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int off = 16; off > 0; off >>= 1) r[i] = fadd(r[i], __shfl_xor_sync(0xffffffffu, r[i], off));
-      float loss = 0.f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) loss = fadd(loss, fmul(r[i], om[i]));
-      costs[jc] = fadd(costs[jc], fdiv(loss, energy));
-    }
-  }
+  for (int k = 0; k < 16; ++k) v[k] = __shfl_sync(full, h1, 2 * k);
 }
 
+// Beta cut of one group of four rows by one warp, certified against the canonical cost.
+//
+// The canonical cost (beta_log_kv.select_cuts, beta_log_kv.py:29-46) of cut c for one
+// component: energy = max(sum_i w_i E_i / max(sum w, 1e-12), 1e-12) with E_i = sum_d x_id^2;
+// per side, mean_d = (sum_i om_i x_id) / max(sum om, 1e-12) (om = w on the side, else 0),
+// loss = sum_i om_i sum_d (x_id - mean_d)^2; cost_c += loss / energy over sides and
+// components, argmin over cuts (2, 1, 3) with ties to the earlier.  Rows off a side have
+// om = 0 and add exactly zero, so only the side's rows are evaluated here.
+//
+// This warp evaluates the same quantities with three differences: sums over features run
+// per lane and then across lanes (another order of adding non-negative terms); squares
+// are accumulated with fused multiply-adds; and a side mean is the side's sum (the same
+// rounded sum as the canonical one) times a rounded reciprocal of its mass, which lies
+// within 3 u M_d of the canonical mean (u = 2^-24, M_d = max_i |x_id|), so each squared
+// deviation moves by at most 32 u M_d^2 and a component's losses by 32 u (sum w)(sum_i E_i).
+// All other differences are relative: at most about (4 D + 128) u of a cost.  With
+// B = sum over components of 40 u (sum w)(sum_i E_i) / energy and rel = (4 D + 128) u,
+// the returned cut is the canonical one whenever runner-up minus best exceeds
+// 2 rel * runner-up + 2 B (plus a floor for subnormal rounding).  Otherwise, or when a
+// row energy exceeds 1e30 (no overflow anywhere below that), -1 asks for the canonical
+// evaluation.
 template <typename T, int DC>
 __device__ int beta_cut_warp(const T* tk, const T* tv, const Meta* tm, int start, int Drt, int lane) {
   const int D = DC ? DC : Drt;
-  // Features of this lane: d = lane + 32 j.  With a compile-time D that is a multiple of
-  // 32 they are read once per component into registers.
-  constexpr int NPL = (DC >= 32 && DC % 32 == 0) ? DC / 32 : 0;
+  constexpr int NPL = (DC >= 32 && DC % 32 == 0) ? DC / 32 : 0;  // features per lane, compile time
   float wv[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) wv[i] = tm[start + i].w;
-  float tot = 0.f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) tot = fadd(tot, wv[i]);
-  tot = fmaxf(tot, 1e-12f);
+  const float wsum = fadd(fadd(fadd(wv[0], wv[1]), wv[2]), wv[3]);
+  const float tot = fmaxf(wsum, 1e-12f);
+  // Side masses: left of cut c = w_0..w_{c-1}, right = w_c..w_3 (c = 1, 2, 3).
+  const float wl1 = wv[0], wl2 = fadd(wv[0], wv[1]), wl3 = fadd(wl2, wv[2]);
+  const float wr3 = wv[3], wr2 = fadd(wv[2], wv[3]), wr1 = fadd(fadd(wv[1], wv[2]), wv[3]);
+  const float il1 = fdiv(1.f, fmaxf(wl1, 1e-12f)), il2 = fdiv(1.f, fmaxf(wl2, 1e-12f)),
+              il3 = fdiv(1.f, fmaxf(wl3, 1e-12f));
+  const float ir1 = fdiv(1.f, fmaxf(wr1, 1e-12f)), ir2 = fdiv(1.f, fmaxf(wr2, 1e-12f)),
+              ir3 = fdiv(1.f, fmaxf(wr3, 1e-12f));
   float costs[3] = {0.f, 0.f, 0.f};
-  beta_costs_comp<T, NPL>(tk, start, D, lane, wv, tot, costs);
-  beta_costs_comp<T, NPL>(tv, start, D, lane, wv, tot, costs);
+  float bound = 0.f;
+  bool finite = true;
+#pragma unroll
+  for (int comp = 0; comp < 2; ++comp) {
+    const T* base = (comp == 0 ? tk : tv) + start * D;
+    // acc[0..3]: E_i; acc[4 + 4 jc + i]: squared deviations of row i for cut jc (cuts 2, 1, 3).
+    float acc[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) acc[k] = 0.f;
+    auto feature = [&](int d) {
+      float x[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x[i] = Elem<T>::load(base + i * D + d);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[i] = __fmaf_rn(x[i], x[i], acc[i]);
+      const float p0 = __fmul_rn(x[0], wv[0]), p1 = __fmul_rn(x[1], wv[1]), p2 = __fmul_rn(x[2], wv[2]),
+                  p3 = __fmul_rn(x[3], wv[3]);
+      const float l2 = __fadd_rn(p0, p1), r2 = __fadd_rn(p2, p3);
+      const float ml1 = __fmul_rn(p0, il1), ml2 = __fmul_rn(l2, il2), ml3 = __fmul_rn(__fadd_rn(l2, p2), il3);
+      const float mr1 = __fmul_rn(__fadd_rn(__fadd_rn(p1, p2), p3), ir1), mr2 = __fmul_rn(r2, ir2), mr3 = __fmul_rn(p3, ir3);
+      float df;
+      // cut 2: rows 0,1 | 2,3
+      df = __fsub_rn(x[0], ml2); acc[4] = __fmaf_rn(df, df, acc[4]);
+      df = __fsub_rn(x[1], ml2); acc[5] = __fmaf_rn(df, df, acc[5]);
+      df = __fsub_rn(x[2], mr2); acc[6] = __fmaf_rn(df, df, acc[6]);
+      df = __fsub_rn(x[3], mr2); acc[7] = __fmaf_rn(df, df, acc[7]);
+      // cut 1: row 0 | 1,2,3
+      df = __fsub_rn(x[0], ml1); acc[8] = __fmaf_rn(df, df, acc[8]);
+      df = __fsub_rn(x[1], mr1); acc[9] = __fmaf_rn(df, df, acc[9]);
+      df = __fsub_rn(x[2], mr1); acc[10] = __fmaf_rn(df, df, acc[10]);
+      df = __fsub_rn(x[3], mr1); acc[11] = __fmaf_rn(df, df, acc[11]);
+      // cut 3: rows 0,1,2 | 3
+      df = __fsub_rn(x[0], ml3); acc[12] = __fmaf_rn(df, df, acc[12]);
+      df = __fsub_rn(x[1], ml3); acc[13] = __fmaf_rn(df, df, acc[13]);
+      df = __fsub_rn(x[2], ml3); acc[14] = __fmaf_rn(df, df, acc[14]);
+      df = __fsub_rn(x[3], mr3); acc[15] = __fmaf_rn(df, df, acc[15]);
+    };
+    if constexpr (NPL > 0) {
+#pragma unroll
+      for (int j = 0; j < NPL; ++j) feature(lane + 32 * j);
+    } else {
+#pragma unroll 1
+      for (int d = lane; d < D; d += 32) feature(d);
+    }
+    warp_allreduce16(acc, lane);
+    const float esum = acc[0] + acc[1] + acc[2] + acc[3];
+    finite = finite && esum <= 1e30f;  // also false for NaN
+    const float energy = fmaxf(fdiv(fadd(fadd(fadd(fmul(acc[0], wv[0]), fmul(acc[1], wv[1])), fmul(acc[2], wv[2])),
+                                         fmul(acc[3], wv[3])),
+                                    tot),
+                               1e-12f);
+    const float inv_e = fdiv(1.f, energy);
+    // cut 2 (costs[0]), cut 1 (costs[1]), cut 3 (costs[2]); left side then right side.
+    costs[0] += (acc[4] * wv[0] + acc[5] * wv[1]) * inv_e + (acc[6] * wv[2] + acc[7] * wv[3]) * inv_e;
+    costs[1] += (acc[8] * wv[0]) * inv_e + (acc[9] * wv[1] + acc[10] * wv[2] + acc[11] * wv[3]) * inv_e;
+    costs[2] += (acc[12] * wv[0] + acc[13] * wv[1] + acc[14] * wv[2]) * inv_e + (acc[15] * wv[3]) * inv_e;
+    bound += 40.f * 5.9604645e-8f * wsum * esum * inv_e;
+  }
+  if (!finite) return -1;
   int best = 0;
   if (costs[1] < costs[best]) best = 1;
   if (costs[2] < costs[best]) best = 2;
@@ -152,7 +150,9 @@ __device__ int beta_cut_warp(const T* tk, const T* tv, const Meta* tm, int start
 #pragma unroll
   for (int j = 0; j < 3; ++j)
     if (j != best) second = fminf(second, costs[j]);
-  if (!(second - costs[best] > 1e-3f * second)) return -1;  // near tie (or NaN): canonical evaluation
+  const float rel = (4.f * D + 128.f) * 5.9604645e-8f;
+  const float margin = 2.f * rel * second + 2.f * bound + 1e-25f * (1.f + wsum);
+  if (!(second - costs[best] > margin)) return -1;  // near tie (or NaN): canonical evaluation
   return best == 0 ? 2 : (best == 1 ? 1 : 3);
 }
 
