@@ -250,25 +250,42 @@ def bench_ours(args, rank, world, local_rank):
     host = []
     for chunks in layers:
         host.append([tuple(t[:, :, :].cpu().pin_memory() for t in chunks[c]) for c in range(2)])
+    # Two device slots; a copy stream fills slot n % 2 with layer-chunk n's inputs while the
+    # flush of layer-chunk n - 1 runs on `stream` (events order reuse of each slot).
     dev_buf = [tuple(torch.empty_like(t) for t in layers[0][0]) for _ in range(2)]
+    copy_stream = torch.cuda.Stream(device)
+    filled = [torch.cuda.Event() for _ in range(2)]
+    consumed = [torch.cuda.Event() for _ in range(2)]
     h2d_per_step = sum(t.numel() * t.element_size() for t in layers[0][0]) * len(layers) * len(layers[0])
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e_start.record(stream)
-        for _ in range(args.steps):
+    e_start.record(stream)
+    copy_stream.wait_stream(stream)
+    n = 0
+    for _ in range(args.steps):
+        with torch.cuda.stream(stream):
             for cache in caches:
                 cache.reset_parameters()
-            for c in range(len(layers[0])):
-                for li, cache in enumerate(caches):
-                    buf = dev_buf[c % 2]
+        for c in range(len(layers[0])):
+            for li, cache in enumerate(caches):
+                slot = n % 2
+                buf = dev_buf[slot]
+                with torch.cuda.stream(copy_stream):
+                    if n >= 2:
+                        copy_stream.wait_event(consumed[slot])
                     for d, h in zip(buf, host[li][c % 2]):
                         d.copy_(h, non_blocking=True)
+                    filled[slot].record(copy_stream)
+                with torch.cuda.stream(stream):
+                    stream.wait_event(filled[slot])
                     cache.add_recent(buf[0], buf[2], k_raw=buf[1], span_ends=ends_host)
+                    consumed[slot].record(stream)
+                n += 1
+        with torch.cuda.stream(stream):
             readback = caches[-1]._alpha_count_dev.to("cpu", non_blocking=False)
-        e_stop.record(stream)
+    e_stop.record(stream)
     torch.cuda.synchronize()
     e_ms = e_start.elapsed_time(e_stop)
     if world > 1:

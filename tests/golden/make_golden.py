@@ -6,8 +6,11 @@ read-only checkout whose path is given by ``--reference`` (or the
 ``LOGKV_REFERENCE`` environment variable), drives the reference cache through a
 seeded streaming workload and records, after every ``add_recent`` call, every
 ``named_buffers()`` entry plus the host mirrors the reference treats as
-authoritative.  It also records the reference's CPU slot-attention output
-(``log_kv_chunk_attention``, math path) for the chunk about to be committed.
+authoritative.  At every third step it also records, for the chunk about to be committed,
+the reference's CPU slot-attention output (``log_kv_chunk_attention``, math
+path) over the whole chunk and over its first two tokens (the decode shape),
+the mid-anchor attention plan (``_semantic_attention_plan``) and the torch
+packer's output (``log_kv_pack.pack_mid_kv(..., backend="torch")``).
 
 The reference's ``litgpt/__init__`` imports ``lightning``, which is not needed
 by the cache modules; a stub import hook stands in for it (test scaffolding,
@@ -101,6 +104,7 @@ def record_state(cache, out: dict, prefix: str) -> None:
 
 def run_config(cfg: dict, outdir: str) -> str:
     from litgpt.log_kv_cache import LogStructuredKVCache, log_kv_chunk_attention
+    from litgpt.log_kv_pack import pack_mid_kv
 
     torch.set_num_threads(4)
     stream = make_stream(cfg)
@@ -128,9 +132,20 @@ def run_config(cfg: dict, outdir: str) -> str:
         q = torch.from_numpy(chunk["q"]).to(dtype)
         pos = torch.from_numpy(chunk["pos"]) if chunk.get("pos") is not None else None
         if chunk.get("attend"):
+            scale = cfg["dim"] ** -0.5
+            pack_dim = ((cfg["dim"] + 1 + 7) // 8) * 8
             with torch.no_grad():
-                att = log_kv_chunk_attention(cache, q, k, v, cfg["dim"] ** -0.5, 0.0)
+                att = log_kv_chunk_attention(cache, q, k, v, scale, 0.0)
+                dec = log_kv_chunk_attention(cache, q[:, :, :2], k[:, :, :2], v[:, :, :2], scale, 0.0)
+                plan = cache._semantic_attention_plan()
+                ka, va = pack_mid_kv(cache, plan, k, v, pack_dim, backend="torch")
             out[f"step{step}/attention"] = to_np(att.float())
+            out[f"step{step}/decode_attention"] = to_np(dec.float())
+            out[f"step{step}/plan_idx"] = to_np(plan[0])
+            out[f"step{step}/plan_anchor"] = to_np(plan[1])
+            out[f"step{step}/plan_valid"] = to_np(plan[3])
+            out[f"step{step}/pack_k"] = to_np(ka)
+            out[f"step{step}/pack_v"] = to_np(va)
         cache.add_recent(k, v, k_raw=kr, input_pos=pos, span_ends=chunk["span_ends"].tolist())
         record_state(cache, out, f"step{step}")
     path = os.path.join(outdir, f"stream_{cfg['name']}.npz")
