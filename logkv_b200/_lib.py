@@ -44,6 +44,30 @@ class State(ctypes.Structure):
     _fields_ = [(name, ctypes.c_void_p) for name in STATE_FIELDS]
 
 
+class Plan(ctypes.Structure):
+    _fields_ = [("idx", ctypes.c_void_p), ("anchor", ctypes.c_void_p), ("valid", ctypes.c_void_p),
+                ("width", ctypes.c_void_p), ("width_max", ctypes.c_void_p), ("vslot", ctypes.c_void_p),
+                ("vanchor", ctypes.c_void_p), ("nvalid", ctypes.c_void_p), ("exact_rows", ctypes.c_void_p),
+                ("nexact", ctypes.c_void_p)]
+
+
+class Rope(ctypes.Structure):
+    _fields_ = [("cos", ctypes.c_void_p), ("sin", ctypes.c_void_p), ("rows", ctypes.c_int32),
+                ("rope_n", ctypes.c_int32), ("dtype", ctypes.c_int32)]
+
+
+class Prefix(ctypes.Structure):
+    _fields_ = [("k", ctypes.c_void_p), ("v", ctypes.c_void_p), ("mass", ctypes.c_void_p),
+                ("length", ctypes.c_void_p), ("capacity", ctypes.c_int32)]
+
+
+class AttentionArgs(ctypes.Structure):
+    _fields_ = [("q", ctypes.c_void_p), ("k_new", ctypes.c_void_p), ("v_new", ctypes.c_void_p),
+                ("out", ctypes.c_void_p), ("heads", ctypes.c_int32), ("tokens", ctypes.c_int32),
+                ("q_offset", ctypes.c_int32), ("q_tokens", ctypes.c_int32), ("recent_count", ctypes.c_int32),
+                ("causal", ctypes.c_int32), ("scale", ctypes.c_float), ("qx", ctypes.c_float)]
+
+
 _lib = None
 
 
@@ -68,6 +92,22 @@ def lib() -> ctypes.CDLL:
         handle.logkv_read_counters.restype = ctypes.c_int
         handle.logkv_read_counters.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int32,
                                                ctypes.c_void_p]
+        P = ctypes.POINTER
+        handle.logkv_attention_plan.restype = ctypes.c_int
+        handle.logkv_attention_plan.argtypes = [P(Layout), P(State), P(Plan), ctypes.c_void_p]
+        handle.logkv_pack_prefix.restype = ctypes.c_int
+        handle.logkv_pack_prefix.argtypes = [P(Layout), P(State), P(Plan), P(Rope), P(Prefix), ctypes.c_void_p,
+                                             ctypes.c_void_p]
+        handle.logkv_pack_mid.restype = ctypes.c_int
+        handle.logkv_pack_mid.argtypes = [P(Layout), P(State), P(Plan), P(Rope), ctypes.c_int32, ctypes.c_int32,
+                                          ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                          ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+                                          ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]
+        handle.logkv_attention_workspace_bytes.restype = ctypes.c_size_t
+        handle.logkv_attention_workspace_bytes.argtypes = [P(Layout), ctypes.c_int32, ctypes.c_int32, ctypes.c_int32]
+        handle.logkv_attention.restype = ctypes.c_int
+        handle.logkv_attention.argtypes = [P(Layout), P(State), P(Prefix), P(AttentionArgs), ctypes.c_void_p,
+                                           ctypes.c_size_t, ctypes.c_void_p]
         _lib = handle
     return _lib
 

@@ -185,6 +185,7 @@ class LogStructuredKVCache(nn.Module):
             raise ValueError("cache geometry is outside the supported range of the flush kernels")
         self._workspace = torch.zeros(nbytes, dtype=torch.uint8, device=device)
         self._state = None
+        self._ladder_epoch = 0       # bumped whenever a flush or reset rewrites the ladder / exact pool
         self.profile_events = None   # set to a list of LOGKV_FLUSH_STAGES+1 torch.cuda.Event to time stages
 
     # ------------------------------------------------------------------ C-ABI state
@@ -203,6 +204,7 @@ class LogStructuredKVCache(nn.Module):
 
     def flush_device(self, take: int) -> None:
         """One device flush of the ``take`` oldest window tokens plus the window shift."""
+        self._ladder_epoch += 1
         state = self._state_struct()
         args = (ctypes.byref(self._layout), ctypes.byref(state), int(take), int(self.recent_count),
                 ctypes.c_void_p(self._workspace.data_ptr()), self._workspace.numel(),
@@ -308,6 +310,12 @@ class LogStructuredKVCache(nn.Module):
                 self.recent_count = remaining
                 pending -= take
 
+    # ------------------------------------------------------------------ read side
+    def _semantic_attention_plan(self):
+        """(physical_idx, anchors, M_s, valid) of the mid-anchor plan (log_kv_cache.py:5954-6007)."""
+        from .attention import plan
+        return plan(self)
+
     # ------------------------------------------------------------------ host mirrors (lazy, synchronizing)
     @property
     def alpha_count(self) -> int:
@@ -367,3 +375,4 @@ class LogStructuredKVCache(nn.Module):
         self._recent_span_ends = [[False] * R for _ in range(self.batch_size)]
         self.token_count = 0
         self.recent_count = 0
+        self._ladder_epoch += 1

@@ -1,0 +1,837 @@
+// Read side of the SemanticLogKV cache on sm_100a: mid-anchor attention plan,
+// prefix packing and slot attention (C ABI in include/logkv_attention.h).
+//
+//   K1 attn_plan_kernel     one CTA per (b, g) lane: block scans over the lane's
+//                            (cluster, level) counts give every occupied entry its
+//                            plan position and every valid entry its compacted one.
+//   K2 prefix_pack_kernel   one warp per output row: RoPE at the mid anchor with the
+//                            reference's rounding chain, value copy, mass term.
+//   K3 pack_mid_kernel      the reference's 136-wide packed layout (same math as K2).
+//   K4 slot_attn_kernel     split-K attention for a few query tokens: each warp
+//                            streams tiles of slot rows through a private cp.async
+//                            ring (every lane reads back only the 16-byte chunks it
+//                            copied, so a warp never waits for another), online
+//                            softmax in the log2 domain, CTA and cross-CTA combines
+//                            in a fixed order (the last CTA of a lane combines).
+#include <algorithm>
+
+#include "common.cuh"
+#include "../../include/logkv_attention.h"
+
+namespace logkv {
+
+constexpr int32_t kStatusAnchorRange = 1 << 16;
+
+struct PlanGeo {
+  int B, G, K, L, Bs, P, D, cap;
+};
+
+static PlanGeo make_plan_geo(const logkv_layout_t& l) {
+  PlanGeo g;
+  g.B = l.batch;
+  g.G = l.groups;
+  g.K = l.clusters;
+  g.L = l.levels;
+  g.Bs = l.slots;
+  g.P = l.exact;
+  g.D = l.dim;
+  g.cap = l.clusters * l.levels * l.slots;
+  return g;
+}
+
+__device__ __forceinline__ int64_t floor_div(int64_t a, int64_t b) {
+  int64_t q = a / b;
+  if ((a % b != 0) && ((a < 0) != (b < 0))) --q;
+  return q;
+}
+
+// ---------------------------------------------------------------- K1: plan
+__global__ void __launch_bounds__(512) attn_plan_kernel(PlanGeo pg, logkv_state_t s, logkv_plan_t p) {
+  const int g = blockIdx.x, b = blockIdx.y, lane = b * pg.G + g;
+  const int KL = pg.K * pg.L, tid = threadIdx.x, nt = blockDim.x;
+  const int warp = tid >> 5, lid = tid & 31, nwarps = nt >> 5;
+  __shared__ int off[kMaxClusters * kMaxLevels];
+  __shared__ int voff[kMaxClusters * kMaxLevels];
+  __shared__ int vcnt[kMaxClusters * kMaxLevels];
+  __shared__ int wsum[32];
+  __shared__ int tot[2];
+  const int16_t* cnt = s.level_count + (size_t)lane * KL;
+  const float* w = s.level_w + (size_t)lane * pg.cap;
+  const int64_t* swp = s.level_sum_wp + (size_t)lane * pg.cap;
+  // Plan order q = c * L + j walks level L - 1 - j: top level first inside a cluster.
+  auto group_entry0 = [&](int q) { return (q / pg.L * pg.L + (pg.L - 1 - q % pg.L)) * pg.Bs; };
+  auto group_count = [&](int q) { return (int)cnt[q / pg.L * pg.L + (pg.L - 1 - q % pg.L)]; };
+  for (int q = warp; q < KL; q += nwarps) {
+    const int n = group_count(q), e0 = group_entry0(q);
+    int nv = 0;
+    for (int i = lid; i - lid < n; i += 32) {
+      const bool v = i < n && w[e0 + i] > 0.f;
+      nv += __popc(__ballot_sync(0xffffffffu, v));
+    }
+    if (lid == 0) vcnt[q] = nv;
+  }
+  __syncthreads();
+  const int my = tid < KL ? group_count(tid) : 0;
+  const int myv = tid < KL ? vcnt[tid] : 0;
+  const int inc = block_inclusive_scan(my, wsum);
+  const int vinc = block_inclusive_scan(myv, wsum);
+  if (tid < KL) {
+    off[tid] = inc - my;
+    voff[tid] = vinc - myv;
+  }
+  if (tid == nt - 1) {
+    tot[0] = inc;
+    tot[1] = vinc;
+  }
+  __syncthreads();
+  const int width = tot[0], nvalid = tot[1];
+  const size_t base = (size_t)lane * pg.cap;
+  for (int q = warp; q < KL; q += nwarps) {
+    const int n = group_count(q), e0 = group_entry0(q);
+    int vrun = voff[q];
+    for (int i0 = 0; i0 < n; i0 += 32) {
+      const int i = i0 + lid;
+      bool v = false;
+      int64_t anchor = 0;
+      if (i < n) {
+        const float wi = w[e0 + i];
+        v = wi > 0.f;
+        if (v) {
+          const int64_t ww = max((int64_t)wi, (int64_t)1);  // weights.long().clamp_min(1)
+          anchor = floor_div(2 * swp[e0 + i] + ww, 2 * ww);
+        }
+        if (p.idx) {
+          p.idx[base + off[q] + i] = e0 + i;
+          p.anchor[base + off[q] + i] = anchor;
+          p.valid[base + off[q] + i] = v ? 1 : 0;
+        }
+      }
+      const unsigned m = __ballot_sync(0xffffffffu, v);
+      if (v) {
+        const int at = vrun + __popc(m & ((1u << lid) - 1u));
+        p.vslot[base + at] = e0 + i;
+        p.vanchor[base + at] = anchor;
+      }
+      vrun += __popc(m);
+    }
+  }
+  if (p.idx) {
+    for (int i = width + tid; i < pg.cap; i += nt) {
+      p.idx[base + i] = 0;
+      p.anchor[base + i] = 0;
+      p.valid[base + i] = 0;
+    }
+  }
+  if (tid == 0) {
+    if (p.width) p.width[lane] = width;
+    if (p.width_max) atomicMax(p.width_max, width);
+    p.nvalid[lane] = nvalid;
+  }
+  // Valid exact-pool rows of batch row b (computed once, by the g == 0 lane).
+  if (g == 0) {
+    const int ac = min(*s.alpha_count, pg.P);
+    int run = 0;
+    for (int j0 = 0; j0 < ac; j0 += nt) {
+      const int j = j0 + tid;
+      const bool v = j < ac && s.alpha_valid[(size_t)b * pg.P + j] != 0;
+      const int incl = block_inclusive_scan(v ? 1 : 0, wsum);
+      if (v) p.exact_rows[(size_t)b * pg.P + run + incl - 1] = j;
+      if (tid == nt - 1) tot[0] = incl;
+      __syncthreads();
+      run += tot[0];
+      __syncthreads();
+    }
+    if (tid == 0) p.nexact[b] = run;
+  }
+}
+
+// ---------------------------------------------------------------- RoPE arithmetic
+// x * cos + rotate_half(x) * sin (log_kv_position.py:95-99) with torch's promotion:
+// float32 arithmetic unless content and tables are both bfloat16, then every op rounds.
+template <typename T, typename C>
+struct Rope {
+  __device__ __forceinline__ static float apply(float x, float rot, float c, float s) {
+    return Elem<T>::round(__fadd_rn(__fmul_rn(x, c), __fmul_rn(rot, s)));
+  }
+};
+template <>
+struct Rope<__nv_bfloat16, __nv_bfloat16> {
+  __device__ __forceinline__ static float apply(float x, float rot, float c, float s) {
+    const float a = Elem<__nv_bfloat16>::round(__fmul_rn(x, c));
+    const float b = Elem<__nv_bfloat16>::round(__fmul_rn(rot, s));
+    return Elem<__nv_bfloat16>::round(__fadd_rn(a, b));
+  }
+};
+
+template <typename C>
+__device__ __forceinline__ float table_load(const C* t, size_t i) {
+  return Elem<C>::load(t + i);
+}
+
+struct RopeArgs {
+  const void* cos;
+  const void* sin;
+  int rows, rope_n;
+};
+
+// One warp writes the rotated key row `dst` from `src` at position `anchor`.
+template <typename T, typename C>
+__device__ __forceinline__ void rope_row(const RopeArgs& r, int D, const T* src, int64_t anchor, T* dst,
+                                         int lid) {
+  const C* ct = static_cast<const C*>(r.cos) + (size_t)anchor * r.rope_n;
+  const C* st = static_cast<const C*>(r.sin) + (size_t)anchor * r.rope_n;
+  const int half = r.rope_n / 2;
+  for (int d = lid; d < D; d += 32) {
+    const float x = Elem<T>::load(src + d);
+    float y = x;
+    if (d < r.rope_n) {
+      const float rot = d < half ? -Elem<T>::load(src + d + half) : Elem<T>::load(src + d - half);
+      y = Rope<T, C>::apply(x, rot, table_load(ct, d), table_load(st, d));
+    }
+    Elem<T>::store(dst + d, y);
+  }
+}
+
+__device__ __forceinline__ int64_t checked_anchor(int64_t a, int rows, int32_t* status) {
+  if (a < 0 || a >= rows) {
+    if (status) atomicOr(status, kStatusAnchorRange);
+    return a < 0 ? 0 : rows - 1;
+  }
+  return a;
+}
+
+// ---------------------------------------------------------------- K2: prefix pack
+template <typename T, typename C>
+__global__ void __launch_bounds__(256) prefix_pack_kernel(PlanGeo pg, logkv_state_t s, logkv_plan_t p, RopeArgs r,
+                                                          logkv_prefix_t out, int32_t* status) {
+  const int g = blockIdx.y, b = blockIdx.z, lane = b * pg.G + g, D = pg.D;
+  const int warp = threadIdx.x >> 5, lid = threadIdx.x & 31;
+  const int nv = p.nvalid[lane], ne = p.nexact[b], n = nv + ne;
+  if (blockIdx.x == 0 && threadIdx.x == 0) out.length[lane] = n;
+  const T* LK = static_cast<const T*>(s.level_k);
+  const T* LV = static_cast<const T*>(s.level_v);
+  const T* AK = static_cast<const T*>(s.alpha_k_raw);
+  const T* AV = static_cast<const T*>(s.alpha_v);
+  T* OK = static_cast<T*>(out.k);
+  T* OV = static_cast<T*>(out.v);
+  const size_t pbase = (size_t)lane * pg.cap, obase = (size_t)lane * out.capacity;
+  for (int row = blockIdx.x * 8 + warp; row < n; row += gridDim.x * 8) {
+    const T* xk;
+    const T* xv;
+    int64_t anchor;
+    float mass = 0.f;
+    if (row < nv) {
+      const int e = p.vslot[pbase + row];
+      anchor = p.vanchor[pbase + row];
+      xk = LK + (pbase + e) * D;
+      xv = LV + (pbase + e) * D;
+      mass = Elem<T>::round(logf(fmaxf(s.level_w[pbase + e], 1.f)));
+    } else {
+      const int j = p.exact_rows[(size_t)b * pg.P + row - nv];
+      anchor = s.alpha_pos[(size_t)b * pg.P + j];
+      xk = AK + ((size_t)lane * pg.P + j) * D;
+      xv = AV + ((size_t)lane * pg.P + j) * D;
+    }
+    anchor = checked_anchor(anchor, r.rows, status);
+    rope_row<T, C>(r, D, xk, anchor, OK + (obase + row) * D, lid);
+    for (int d = lid; d < D; d += 32) OV[(obase + row) * D + d] = xv[d];
+    if (lid == 0) out.mass[obase + row] = mass;
+  }
+}
+
+// ---------------------------------------------------------------- K3: reference-layout pack
+struct PackArgs {
+  int width, alpha_count, recent_count, tokens, dim, skip_pooled, recent_start, rcap;
+};
+
+template <typename T, typename C>
+__global__ void __launch_bounds__(256) pack_mid_kernel(PlanGeo pg, logkv_state_t s, logkv_plan_t p, RopeArgs r,
+                                                       PackArgs a, const T* kn, const T* vn, T* ok, T* ov,
+                                                       int32_t* status) {
+  const int g = blockIdx.y, b = blockIdx.z, lane = b * pg.G + g, D = pg.D;
+  const int warp = threadIdx.x >> 5, lid = threadIdx.x & 31;
+  const int length = a.width + a.alpha_count + a.recent_count + a.tokens;
+  const int first = a.width + a.alpha_count + a.recent_start;
+  const T* LK = static_cast<const T*>(s.level_k);
+  const T* LV = static_cast<const T*>(s.level_v);
+  const T* AK = static_cast<const T*>(s.alpha_k_raw);
+  const T* AV = static_cast<const T*>(s.alpha_v);
+  const T* RK = static_cast<const T*>(s.recent_k);
+  const T* RV = static_cast<const T*>(s.recent_v);
+  const size_t pbase = (size_t)lane * pg.cap;
+  const float kMask = Elem<T>::round(-10000.f);
+  for (int row = blockIdx.x * 8 + warp; row < length; row += gridDim.x * 8) {
+    if (row < first && (a.skip_pooled || row >= a.width + a.alpha_count)) continue;
+    T* dk = ok + ((size_t)lane * length + row) * a.dim;
+    T* dv = ov + ((size_t)lane * length + row) * a.dim;
+    const T* xk = nullptr;
+    const T* xv = nullptr;
+    bool rotate = false, valid = true;
+    int64_t anchor = 0;
+    float extra = 0.f;
+    if (row < a.width) {
+      valid = p.valid[pbase + row] != 0;
+      const int64_t e = p.idx[pbase + row];
+      xk = LK + (pbase + e) * D;
+      xv = LV + (pbase + e) * D;
+      anchor = p.anchor[pbase + row];
+      rotate = true;
+      extra = valid ? Elem<T>::round(logf(fmaxf(s.level_w[pbase + e], 1.f))) : kMask;
+    } else if (row < a.width + a.alpha_count) {
+      const int j = row - a.width;
+      valid = s.alpha_valid[(size_t)b * pg.P + j] != 0;
+      xk = AK + ((size_t)lane * pg.P + j) * D;
+      xv = AV + ((size_t)lane * pg.P + j) * D;
+      anchor = s.alpha_pos[(size_t)b * pg.P + j];
+      rotate = true;
+      extra = valid ? -0.f : kMask;  // (~valid).to(dtype) * -10000
+    } else if (row < a.width + a.alpha_count + a.recent_count) {
+      const int i = row - a.width - a.alpha_count;
+      xk = RK + ((size_t)lane * a.rcap + i) * D;
+      xv = RV + ((size_t)lane * a.rcap + i) * D;
+    } else {
+      const int t = row - a.width - a.alpha_count - a.recent_count;
+      xk = kn + ((size_t)lane * a.tokens + t) * D;
+      xv = vn + ((size_t)lane * a.tokens + t) * D;
+    }
+    if (!valid) {
+      for (int d = lid; d < a.dim; d += 32) {
+        Elem<T>::store(dk + d, d == D ? extra : 0.f);
+        Elem<T>::store(dv + d, 0.f);
+      }
+      continue;
+    }
+    if (rotate) {
+      anchor = checked_anchor(anchor, r.rows, status);
+      rope_row<T, C>(r, D, xk, anchor, dk, lid);
+    } else {
+      for (int d = lid; d < D; d += 32) dk[d] = xk[d];
+    }
+    for (int d = D + lid; d < a.dim; d += 32) Elem<T>::store(dk + d, d == D ? extra : 0.f);
+    for (int d = lid; d < a.dim; d += 32) {
+      if (d < D) dv[d] = xv[d];
+      else Elem<T>::store(dv + d, 0.f);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- K4: slot attention
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void unpack16(const uint4& u, float* out, const float*) {
+  const float* f = reinterpret_cast<const float*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) out[i] = f[i];
+}
+__device__ __forceinline__ void unpack16(const uint4& u, float* out, const __nv_bfloat16*) {
+  const unsigned* w = reinterpret_cast<const unsigned*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    out[2 * i] = __uint_as_float(w[i] << 16);
+    out[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+struct AttnGeo {
+  int B, G, H, T, rf;
+  int TQ, qoff;  // query tokens of this call and the first one's index among the T new tokens
+  int causal;
+  int nsplit, pcap, rcap, rcount;
+  float scale_log2, qx;
+};
+
+constexpr int kAttnWarps = 4;
+constexpr int kAttnStages = 3;
+
+template <typename T, int D, int NQ>
+struct AttnShape {
+  static constexpr int VN = 16 / (int)sizeof(T);    // elements per 16-byte chunk
+  static constexpr int LPR = D / VN;                 // lanes per slot row
+  static constexpr int GPW = 32 / LPR;               // row groups per warp
+  static constexpr int TS = (32 / NQ) > GPW ? (32 / NQ) : GPW;  // slots per warp tile
+  static constexpr int SPL = TS / GPW;               // slots per lane group per tile
+  static constexpr int PPL = TS * NQ / 32;           // (slot, query) pairs per lane
+  static constexpr size_t warp_elems = (size_t)kAttnStages * 2 * TS * D;
+  static constexpr size_t smem = (size_t)kAttnWarps * (warp_elems * sizeof(T) + kAttnStages * TS * sizeof(float));
+  static_assert(D % VN == 0 && LPR >= 1 && LPR <= 32 && 32 % LPR == 0, "row must be 16..512 bytes, power of two");
+  static_assert(NQ >= 1 && NQ <= 32 && 32 % NQ == 0, "query rows per lane must divide 32");
+};
+
+template <typename T, int D, int NQ>
+__global__ void __launch_bounds__(kAttnWarps * 32) slot_attn_kernel(AttnGeo a, logkv_prefix_t pre, const T* rk,
+                                                                   const T* rv, const T* kn, const T* vn, const T* q,
+                                                                   T* out, float* part, int* ticket) {
+  using S = AttnShape<T, D, NQ>;
+  constexpr int VN = S::VN, LPR = S::LPR, GPW = S::GPW, TS = S::TS, SPL = S::SPL, PPL = S::PPL;
+  extern __shared__ uint4 smem4[];
+  __shared__ float sp[kAttnWarps][TS * NQ];
+  __shared__ float wm_[kAttnWarps][NQ];
+  __shared__ float wl_[kAttnWarps][NQ];
+  __shared__ int sh_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int grp = lane / LPR, u = lane % LPR;
+  const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z, ln = b * a.G + g;
+  T* wbuf = reinterpret_cast<T*>(smem4) + (size_t)warp * S::warp_elems;
+  float* wmass = reinterpret_cast<float*>(reinterpret_cast<T*>(smem4) + (size_t)kAttnWarps * S::warp_elems) +
+                 warp * kAttnStages * TS;
+  const T* PK = static_cast<const T*>(pre.k);
+  const T* PV = static_cast<const T*>(pre.v);
+  const int Lp = pre.length[ln], R = a.rcount, Stot = Lp + R + a.T;
+  int per = (Stot + a.nsplit - 1) / a.nsplit;
+  per = (per + TS - 1) / TS * TS;
+  const int s0 = min(Stot, split * per), s1 = min(Stot, s0 + per);
+  const int ntile = (s1 - s0 + TS - 1) / TS;
+  const int mine = ntile > warp ? (ntile - warp + kAttnWarps - 1) / kAttnWarps : 0;
+
+  float qf[NQ][VN];
+#pragma unroll
+  for (int r = 0; r < NQ; ++r) {
+    const int h = g * a.rf + r / a.TQ, t = a.qoff + r % a.TQ;
+    const uint4 raw = *reinterpret_cast<const uint4*>(q + (((size_t)b * a.H + h) * a.T + t) * D + u * VN);
+    unpack16(raw, qf[r], (const T*)nullptr);
+  }
+
+  auto issue = [&](int k, int stage) {
+    if (k < mine) {
+      const int t0 = s0 + (warp + k * kAttnWarps) * TS;
+      T* dk = wbuf + (size_t)stage * 2 * TS * D;
+      T* dv = dk + TS * D;
+#pragma unroll
+      for (int i = 0; i < SPL; ++i) {
+        const int ts = grp + GPW * i, sl = t0 + ts;
+        if (sl < s1) {
+          const T* sk;
+          const T* sv;
+          if (sl < Lp) {
+            const size_t row = (size_t)ln * pre.capacity + sl;
+            sk = PK + row * D;
+            sv = PV + row * D;
+            if (u == 0) cp_async4(wmass + stage * TS + ts, pre.mass + row);
+          } else {
+            if (sl < Lp + R) {
+              const size_t row = (size_t)ln * a.rcap + (sl - Lp);
+              sk = rk + row * D;
+              sv = rv + row * D;
+            } else {
+              const size_t row = (size_t)ln * a.T + (sl - Lp - R);
+              sk = kn + row * D;
+              sv = vn + row * D;
+            }
+            if (u == 0) wmass[stage * TS + ts] = 0.f;
+          }
+          cp_async16(dk + ts * D + u * VN, sk + u * VN);
+          cp_async16(dv + ts * D + u * VN, sv + u * VN);
+        }
+      }
+    }
+    cp_async_commit();
+  };
+
+  float m[NQ], acc[NQ][VN];
+#pragma unroll
+  for (int r = 0; r < NQ; ++r) {
+    m[r] = -INFINITY;
+#pragma unroll
+    for (int e = 0; e < VN; ++e) acc[r][e] = 0.f;
+  }
+  float lsum = 0.f;
+  const int rown = lane % NQ;
+
+#pragma unroll
+  for (int k = 0; k < kAttnStages - 1; ++k) issue(k, k);
+  for (int k = 0; k < mine; ++k) {
+    issue(k + kAttnStages - 1, (k + kAttnStages - 1) % kAttnStages);
+    cp_async_wait<kAttnStages - 1>();
+    const int stage = k % kAttnStages;
+    const int t0 = s0 + (warp + k * kAttnWarps) * TS;
+    const T* ck = wbuf + (size_t)stage * 2 * TS * D;
+    const T* cv = ck + TS * D;
+    // Scores of this lane group's slots: partial dots over the lane's chunk, then the group sum.
+    float z[SPL][NQ];
+#pragma unroll
+    for (int i = 0; i < SPL; ++i) {
+      float kf[VN];
+      unpack16(*reinterpret_cast<const uint4*>(ck + (grp + GPW * i) * D + u * VN), kf, (const T*)nullptr);
+#pragma unroll
+      for (int r = 0; r < NQ; ++r) {
+        float d = 0.f;
+#pragma unroll
+        for (int e = 0; e < VN; ++e) d = fmaf(qf[r][e], kf[e], d);
+        z[i][r] = d;
+      }
+    }
+#pragma unroll
+    for (int off = 1; off < LPR; off <<= 1)
+#pragma unroll
+      for (int i = 0; i < SPL; ++i)
+#pragma unroll
+        for (int r = 0; r < NQ; ++r) z[i][r] += __shfl_xor_sync(0xffffffffu, z[i][r], off);
+    if (u == 0) {
+#pragma unroll
+      for (int i = 0; i < SPL; ++i) {
+        const int ts = grp + GPW * i, sl = t0 + ts;
+        const float mass = wmass[stage * TS + ts];
+#pragma unroll
+        for (int r = 0; r < NQ; ++r) {
+          const int c = sl - Lp - R;  // new-token index (>= 0 in the causal tail)
+          const bool vis = sl < s1 && (c < 0 || !a.causal || c <= a.qoff + r % a.TQ);
+          sp[warp][ts * NQ + r] = vis ? (z[i][r] + a.qx * mass) * a.scale_log2 : -INFINITY;
+        }
+      }
+    }
+    __syncwarp();
+    // Online softmax: this lane owns pairs j * 32 + lane, all of query row `rown`.
+    float zl[PPL], mt = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < PPL; ++j) {
+      zl[j] = sp[warp][j * 32 + lane];
+      mt = fmaxf(mt, zl[j]);
+    }
+#pragma unroll
+    for (int off = NQ; off < 32; off <<= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
+    float alpha[NQ], mown = -INFINITY, aown = 1.f;
+#pragma unroll
+    for (int r = 0; r < NQ; ++r) {
+      const float mn = fmaxf(m[r], __shfl_sync(0xffffffffu, mt, r));
+      alpha[r] = mn == -INFINITY ? 1.f : exp2f(m[r] - mn);
+      m[r] = mn;
+      if (r == rown) {
+        mown = mn;
+        aown = alpha[r];
+      }
+    }
+    float ps = 0.f;
+#pragma unroll
+    for (int j = 0; j < PPL; ++j) {
+      const float pj = zl[j] == -INFINITY ? 0.f : exp2f(zl[j] - mown);
+      sp[warp][j * 32 + lane] = pj;
+      ps += pj;
+    }
+    lsum = lsum * aown + ps;
+    __syncwarp();
+#pragma unroll
+    for (int r = 0; r < NQ; ++r)
+#pragma unroll
+      for (int e = 0; e < VN; ++e) acc[r][e] *= alpha[r];
+#pragma unroll
+    for (int i = 0; i < SPL; ++i) {
+      const int ts = grp + GPW * i;
+      float vf[VN];
+      unpack16(*reinterpret_cast<const uint4*>(cv + ts * D + u * VN), vf, (const T*)nullptr);
+#pragma unroll
+      for (int r = 0; r < NQ; ++r) {
+        const float pr = sp[warp][ts * NQ + r];
+#pragma unroll
+        for (int e = 0; e < VN; ++e) acc[r][e] = fmaf(pr, vf[e], acc[r][e]);
+      }
+    }
+    __syncwarp();
+  }
+  cp_async_wait<0>();
+  // Warp totals: row sums over the lanes of each query row, accumulators over the lane groups.
+#pragma unroll
+  for (int off = NQ; off < 32; off <<= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
+#pragma unroll
+  for (int r = 0; r < NQ; ++r)
+#pragma unroll
+    for (int off = LPR; off < 32; off <<= 1)
+#pragma unroll
+      for (int e = 0; e < VN; ++e) acc[r][e] += __shfl_xor_sync(0xffffffffu, acc[r][e], off);
+  float* wacc = reinterpret_cast<float*>(wbuf);  // [NQ][D], reuses this warp's own ring
+#pragma unroll
+  for (int r = 0; r < NQ; ++r) {
+    const float lr = __shfl_sync(0xffffffffu, lsum, r);
+    if (lane == 0) {
+      wm_[warp][r] = m[r];
+      wl_[warp][r] = lr;
+    }
+    if (grp == 0) {
+#pragma unroll
+      for (int e = 0; e < VN; ++e) wacc[r * D + u * VN + e] = acc[r][e];
+    }
+  }
+  __syncthreads();
+  // CTA combine (fixed warp order), then either the output or this split's partial.
+  const size_t pstride = (size_t)D + 2;
+  for (int x = tid; x < NQ * D; x += blockDim.x) {
+    const int r = x / D, d = x % D;
+    float mx = -INFINITY;
+    for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, wm_[w][r]);
+    float l = 0.f, o = 0.f;
+    if (mx != -INFINITY) {
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float f = exp2f(wm_[w][r] - mx);
+        l += wl_[w][r] * f;
+        o += reinterpret_cast<float*>(reinterpret_cast<T*>(smem4) + (size_t)w * S::warp_elems)[r * D + d] * f;
+      }
+    }
+    if (a.nsplit == 1) {
+      const int h = g * a.rf + r / a.TQ, t = a.qoff + r % a.TQ;
+      Elem<T>::store(out + (((size_t)b * a.H + h) * a.T + t) * D + d, l > 0.f ? o / l : 0.f);
+    } else {
+      float* pp = part + ((size_t)(ln * a.nsplit + split) * NQ + r) * pstride;
+      if (d == 0) {
+        pp[0] = mx;
+        pp[1] = l;
+      }
+      pp[2 + d] = o;
+    }
+  }
+  if (a.nsplit == 1) return;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) sh_last = atomicAdd(ticket + ln, 1) == a.nsplit - 1;
+  __syncthreads();
+  if (!sh_last) return;
+  __threadfence();
+  for (int x = tid; x < NQ * D; x += blockDim.x) {
+    const int r = x / D, d = x % D;
+    float mx = -INFINITY;
+    for (int sidx = 0; sidx < a.nsplit; ++sidx)
+      mx = fmaxf(mx, __ldcg(part + ((size_t)(ln * a.nsplit + sidx) * NQ + r) * pstride));
+    float l = 0.f, o = 0.f;
+    if (mx != -INFINITY) {
+      for (int sidx = 0; sidx < a.nsplit; ++sidx) {
+        const float* pp = part + ((size_t)(ln * a.nsplit + sidx) * NQ + r) * pstride;
+        const float f = exp2f(__ldcg(pp) - mx);
+        l += __ldcg(pp + 1) * f;
+        o += __ldcg(pp + 2 + d) * f;
+      }
+    }
+    const int h = g * a.rf + r / a.TQ, t = a.qoff + r % a.TQ;
+    Elem<T>::store(out + (((size_t)b * a.H + h) * a.T + t) * D + d, l > 0.f ? o / l : 0.f);
+  }
+  if (tid == 0) ticket[ln] = 0;
+}
+
+// ---------------------------------------------------------------- host side
+static bool dtype_ok(int d) { return d == LOGKV_DTYPE_F32 || d == LOGKV_DTYPE_BF16; }
+static size_t esize_of(int d) { return d == LOGKV_DTYPE_F32 ? 4 : 2; }
+
+static int check_layout(const logkv_layout_t* l) {
+  if (!l) return LOGKV_E_POINTER;
+  if (!dtype_ok(l->dtype)) return LOGKV_E_DTYPE;
+  if (l->batch < 1 || l->groups < 1 || l->dim < 1 || l->clusters < 1 || l->clusters > kMaxClusters ||
+      l->levels < 1 || l->levels > kMaxLevels || l->slots < 1 || l->exact < 0)
+    return LOGKV_E_SHAPE;
+  if ((l->dim * esize_of(l->dtype)) % 16 != 0) return LOGKV_E_SHAPE;
+  return LOGKV_OK;
+}
+
+static int check_rope(const logkv_rope_t* r, int D) {
+  if (!r) return LOGKV_E_POINTER;
+  if (!dtype_ok(r->dtype)) return LOGKV_E_DTYPE;
+  if (r->rope_n < 0 || r->rope_n > D || (r->rope_n & 1)) return LOGKV_E_SHAPE;
+  if (r->rope_n > 0 && (!r->cos || !r->sin || r->rows < 1)) return LOGKV_E_POINTER;
+  return LOGKV_OK;
+}
+
+static int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? LOGKV_OK : (int)e;
+}
+
+template <typename T>
+static void launch_prefix_pack(const PlanGeo& pg, const logkv_state_t& s, const logkv_plan_t& p,
+                               const logkv_rope_t& rope, const logkv_prefix_t& pre, int32_t* status,
+                               cudaStream_t st) {
+  RopeArgs ra{rope.cos, rope.sin, rope.rows, rope.rope_n};
+  const int rows = pg.cap + pg.P;
+  const int blocks = std::max(1, std::min(64, (rows + 63) / 64));
+  const dim3 grid(blocks, pg.G, pg.B);
+  if (rope.dtype == LOGKV_DTYPE_BF16)
+    prefix_pack_kernel<T, __nv_bfloat16><<<grid, 256, 0, st>>>(pg, s, p, ra, pre, status);
+  else
+    prefix_pack_kernel<T, float><<<grid, 256, 0, st>>>(pg, s, p, ra, pre, status);
+}
+
+template <typename T>
+static void launch_pack_mid(const PlanGeo& pg, const logkv_state_t& s, const logkv_plan_t& p,
+                            const logkv_rope_t& rope, const PackArgs& a, const void* kn, const void* vn, void* ok,
+                            void* ov, int32_t* status, cudaStream_t st) {
+  RopeArgs ra{rope.cos, rope.sin, rope.rows, rope.rope_n};
+  const int length = a.width + a.alpha_count + a.recent_count + a.tokens;
+  const int blocks = std::max(1, std::min(64, (length + 63) / 64));
+  const dim3 grid(blocks, pg.G, pg.B);
+  if (rope.dtype == LOGKV_DTYPE_BF16)
+    pack_mid_kernel<T, __nv_bfloat16><<<grid, 256, 0, st>>>(pg, s, p, ra, a, static_cast<const T*>(kn),
+                                                            static_cast<const T*>(vn), static_cast<T*>(ok),
+                                                            static_cast<T*>(ov), status);
+  else
+    pack_mid_kernel<T, float><<<grid, 256, 0, st>>>(pg, s, p, ra, a, static_cast<const T*>(kn),
+                                                    static_cast<const T*>(vn), static_cast<T*>(ok),
+                                                    static_cast<T*>(ov), status);
+}
+
+// Splits per lane: about eight CTAs per SM over the whole grid, at least four tiles per warp.
+static int attn_splits(const logkv_layout_t& l, int prefix_capacity) {
+  const int lanes = l.batch * l.groups;
+  const int smax = prefix_capacity + l.recent_capacity;
+  int n = (8 * 148 + lanes - 1) / lanes;
+  n = std::min(n, std::max(1, smax / (kAttnWarps * 4 * 16)));
+  return std::max(1, std::min(n, 128));
+}
+
+static size_t attn_part_bytes(const logkv_layout_t& l, int nq, int nsplit) {
+  return (size_t)l.batch * l.groups * nsplit * nq * (l.dim + 2) * sizeof(float);
+}
+
+template <typename T, int D, int NQ>
+static int launch_attn_dq(const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
+                          const logkv_attention_args_t& x, float* part, int* ticket, cudaStream_t st) {
+  using S = AttnShape<T, D, NQ>;
+  if (S::smem > 227 * 1024) return LOGKV_E_SMEM;
+  auto kern = slot_attn_kernel<T, D, NQ>;
+  if (S::smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::smem);
+  kern<<<dim3(ag.nsplit, ag.G, ag.B), kAttnWarps * 32, S::smem, st>>>(
+      ag, pre, static_cast<const T*>(s.recent_k), static_cast<const T*>(s.recent_v), static_cast<const T*>(x.k_new),
+      static_cast<const T*>(x.v_new), static_cast<const T*>(x.q), static_cast<T*>(x.out), part, ticket);
+  return launch_status();
+}
+
+template <typename T, int D>
+static int launch_attn_d(int nq, const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
+                         const logkv_attention_args_t& x, float* part, int* ticket, cudaStream_t st) {
+  switch (nq) {
+    case 1: return launch_attn_dq<T, D, 1>(ag, pre, s, x, part, ticket, st);
+    case 2: return launch_attn_dq<T, D, 2>(ag, pre, s, x, part, ticket, st);
+    case 4: return launch_attn_dq<T, D, 4>(ag, pre, s, x, part, ticket, st);
+    case 8: return launch_attn_dq<T, D, 8>(ag, pre, s, x, part, ticket, st);
+    default: return LOGKV_E_SHAPE;
+  }
+}
+
+template <typename T>
+static int launch_attn(int D, int nq, const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
+                       const logkv_attention_args_t& x, float* part, int* ticket, cudaStream_t st) {
+  switch (D) {
+    case 16: return launch_attn_d<T, 16>(nq, ag, pre, s, x, part, ticket, st);
+    case 32: return launch_attn_d<T, 32>(nq, ag, pre, s, x, part, ticket, st);
+    case 64: return launch_attn_d<T, 64>(nq, ag, pre, s, x, part, ticket, st);
+    case 128: return launch_attn_d<T, 128>(nq, ag, pre, s, x, part, ticket, st);
+    default: return LOGKV_E_SHAPE;
+  }
+}
+
+}  // namespace logkv
+
+using namespace logkv;
+
+extern "C" {
+
+LOGKV_API int logkv_attention_plan(const logkv_layout_t* layout, const logkv_state_t* state,
+                                   const logkv_plan_t* plan, void* stream) {
+  int rc = check_layout(layout);
+  if (rc) return rc;
+  if (!state || !plan || !plan->vslot || !plan->vanchor || !plan->nvalid || !plan->exact_rows || !plan->nexact)
+    return LOGKV_E_POINTER;
+  if (plan->idx && (!plan->anchor || !plan->valid)) return LOGKV_E_POINTER;
+  const PlanGeo pg = make_plan_geo(*layout);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (plan->width_max) cudaMemsetAsync(plan->width_max, 0, sizeof(int32_t), st);
+  attn_plan_kernel<<<dim3(pg.G, pg.B), 512, 0, st>>>(pg, *state, *plan);
+  return launch_status();
+}
+
+LOGKV_API int logkv_pack_prefix(const logkv_layout_t* layout, const logkv_state_t* state,
+                                const logkv_plan_t* plan, const logkv_rope_t* rope,
+                                const logkv_prefix_t* prefix, int32_t* status, void* stream) {
+  int rc = check_layout(layout);
+  if (rc) return rc;
+  if (!state || !plan || !prefix || !prefix->k || !prefix->v || !prefix->mass || !prefix->length)
+    return LOGKV_E_POINTER;
+  if ((rc = check_rope(rope, layout->dim))) return rc;
+  const PlanGeo pg = make_plan_geo(*layout);
+  if (prefix->capacity < pg.cap + pg.P) return LOGKV_E_SHAPE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (layout->dtype == LOGKV_DTYPE_BF16)
+    launch_prefix_pack<__nv_bfloat16>(pg, *state, *plan, *rope, *prefix, status, st);
+  else
+    launch_prefix_pack<float>(pg, *state, *plan, *rope, *prefix, status, st);
+  return launch_status();
+}
+
+LOGKV_API int logkv_pack_mid(const logkv_layout_t* layout, const logkv_state_t* state, const logkv_plan_t* plan,
+                             const logkv_rope_t* rope, int32_t width, int32_t alpha_count, int32_t recent_count,
+                             const void* k_new, const void* v_new, int32_t tokens, void* out_k, void* out_v,
+                             int32_t dim, int32_t skip_pooled, int32_t recent_start, int32_t* status, void* stream) {
+  int rc = check_layout(layout);
+  if (rc) return rc;
+  if (!state || !plan || !plan->idx || !plan->anchor || !plan->valid || !out_k || !out_v) return LOGKV_E_POINTER;
+  if (tokens > 0 && (!k_new || !v_new)) return LOGKV_E_POINTER;
+  if ((rc = check_rope(rope, layout->dim))) return rc;
+  const PlanGeo pg = make_plan_geo(*layout);
+  if (dim < layout->dim + 1 || width < 0 || width > pg.cap || alpha_count < 0 || alpha_count > pg.P ||
+      recent_count < 0 || recent_count > layout->recent_capacity || tokens < 0 || recent_start < 0 ||
+      recent_start > recent_count)
+    return LOGKV_E_SHAPE;
+  PackArgs a{width, alpha_count, recent_count, tokens, dim, skip_pooled, recent_start, layout->recent_capacity};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (layout->dtype == LOGKV_DTYPE_BF16)
+    launch_pack_mid<__nv_bfloat16>(pg, *state, *plan, *rope, a, k_new, v_new, out_k, out_v, status, st);
+  else
+    launch_pack_mid<float>(pg, *state, *plan, *rope, a, k_new, v_new, out_k, out_v, status, st);
+  return launch_status();
+}
+
+LOGKV_API size_t logkv_attention_workspace_bytes(const logkv_layout_t* layout, int32_t heads, int32_t q_tokens,
+                                                 int32_t prefix_capacity) {
+  if (check_layout(layout) || heads < layout->groups || heads % layout->groups || q_tokens < 1) return 0;
+  const int nq = heads / layout->groups * q_tokens;
+  const int nsplit = attn_splits(*layout, prefix_capacity);
+  const size_t lanes = (size_t)layout->batch * layout->groups;
+  return 256 + ((lanes * sizeof(int) + 255) / 256) * 256 + attn_part_bytes(*layout, nq, nsplit);
+}
+
+LOGKV_API int logkv_attention(const logkv_layout_t* layout, const logkv_state_t* state,
+                              const logkv_prefix_t* prefix, const logkv_attention_args_t* args,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  int rc = check_layout(layout);
+  if (rc) return rc;
+  if (!state || !prefix || !args || !args->q || !args->out || !prefix->length) return LOGKV_E_POINTER;
+  const int G = layout->groups, H = args->heads, T = args->tokens, TQ = args->q_tokens;
+  if (H < G || H % G || T < 1 || TQ < 1 || args->q_offset < 0 || args->q_offset + TQ > T ||
+      args->recent_count < 0 || args->recent_count > layout->recent_capacity)
+    return LOGKV_E_SHAPE;
+  if (!args->k_new || !args->v_new) return LOGKV_E_POINTER;
+  const int nq = H / G * TQ;
+  const size_t need = logkv_attention_workspace_bytes(layout, H, TQ, prefix->capacity);
+  if (!workspace || workspace_bytes < need) return LOGKV_E_WORKSPACE;
+  const int nsplit = attn_splits(*layout, prefix->capacity);
+  const size_t lanes = (size_t)layout->batch * G;
+  int* ticket = reinterpret_cast<int*>(static_cast<char*>(workspace) + 256);
+  float* part = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256 + ((lanes * sizeof(int) + 255) / 256) * 256);
+  AttnGeo ag;
+  ag.B = layout->batch;
+  ag.G = G;
+  ag.H = H;
+  ag.T = T;
+  ag.rf = H / G;
+  ag.TQ = TQ;
+  ag.qoff = args->q_offset;
+  ag.causal = args->causal ? 1 : 0;
+  ag.nsplit = nsplit;
+  ag.pcap = prefix->capacity;
+  ag.rcap = layout->recent_capacity;
+  ag.rcount = args->recent_count;
+  ag.scale_log2 = args->scale * 1.4426950408889634f;
+  ag.qx = args->qx;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (layout->dtype == LOGKV_DTYPE_BF16)
+    return launch_attn<__nv_bfloat16>(layout->dim, nq, ag, *prefix, *state, *args, part, ticket, st);
+  return launch_attn<float>(layout->dim, nq, ag, *prefix, *state, *args, part, ticket, st);
+}
+
+}  // extern "C"
