@@ -306,6 +306,165 @@ def bench_ours(args, rank, world, local_rank):
                 clocks=clocks.summary(), launches=n_launch)
 
 
+# ---------------------------------------------------------------------------------------------- decode
+DECODE = dict(workload="decode attention over a 32K compressed cache (BASELINE configs[3])", batch=64,
+              heads=16, groups=8, head_dim=128, clusters=12, B=128, filled_levels=4, recent=2048, exact=256,
+              span_cap=64, max_seq=32768, layers=28, distinct_layer_caches=2, geometric_p=0.1)
+
+
+def prefill_decode_cache(torch, cfg, batch, device, cos, sin, seed):
+    """A cache whose state is written directly: full merged levels, exact pool, full window.
+
+    12 clusters x 4 full levels x B' slots per (sequence, KV group); slot counts
+    w ~ Geometric(0.1) (support >= 1), each slot's mid anchor m uniform in
+    [0, max_seq) with sum_wp = w * m (so the mid anchor is m), p_lo/p_hi = m;
+    K/V ~ N(0, 1) in bf16; 256 valid exact rows; a 2048-token window.
+    """
+    from logkv_b200.cache import LogStructuredKVCache
+    G, D = cfg["groups"], cfg["head_dim"]
+    c = LogStructuredKVCache(
+        (batch, G, cfg["max_seq"], D), (batch, G, cfg["max_seq"], D), B=cfg["B"], recent_size=cfg["recent"],
+        device=device, dtype=torch.bfloat16, cluster_k_max=cfg["clusters"], semantic_flush_granularity=cfg["recent"],
+        semantic_centroid_backend="parallel", semantic_replay_updates=True, alpha_exact_tokens=cfg["exact"],
+        alpha_span_max_tokens=cfg["span_cap"], beta_novelty=True, beta_adaptive_merge=True, cos_cache=cos,
+        sin_cache=sin, rope_n_elem=D)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    Lf, Bs = cfg["filled_levels"], c.B_prime
+    lv = (slice(None), slice(None), slice(None), slice(0, Lf))
+    c.level_k[lv].normal_(generator=gen)
+    c.level_v[lv].normal_(generator=gen)
+    u = torch.rand(c.level_w[lv].shape, generator=gen, device=device).clamp_min(1e-7)
+    w = torch.floor(torch.log(u) / np.log(1.0 - cfg["geometric_p"])) + 1.0
+    m = torch.randint(0, cfg["max_seq"], w.shape, generator=gen, device=device)
+    c.level_w[lv] = w
+    c.level_sum_wp[lv] = w.long() * m
+    c.level_p_lo[lv] = m
+    c.level_p_hi[lv] = m
+    c.level_count[:, :, :, :Lf] = Bs
+    P = cfg["exact"]
+    c.alpha_k_raw.normal_(generator=gen)
+    c.alpha_v.normal_(generator=gen)
+    c.alpha_pos.copy_(torch.randint(0, cfg["max_seq"], c.alpha_pos.shape, generator=gen, device=device))
+    c.alpha_valid.fill_(True)
+    c._row_count.fill_(P)
+    c._alpha_count_dev.fill_(P)
+    R = cfg["recent"]
+    c.recent_k[:, :, :R].normal_(generator=gen)
+    c.recent_v[:, :, :R].normal_(generator=gen)
+    c.recent_count = R
+    c.token_count = cfg["max_seq"] // 2
+    c._ladder_epoch += 1
+    return c
+
+
+def bench_decode(args, rank, world, local_rank):
+    """Decode tokens/s: one new token per sequence attends over every layer's compressed cache."""
+    import torch
+    import torch.distributed as dist
+    from logkv_b200.attention import log_kv_chunk_attention, refresh_prefix
+    from logkv_b200.workload import rope_tables
+    device = torch.device("cuda", local_rank)
+    cfg = dict(DECODE, batch=args.decode_batch)
+    batch = max(1, cfg["batch"] // world)
+    H, G, D = cfg["heads"], cfg["groups"], cfg["head_dim"]
+    cos_np, sin_np = rope_tables(cfg["max_seq"] + 1024, D, base=1e6)
+    cos, sin = torch.from_numpy(cos_np).to(device), torch.from_numpy(sin_np).to(device)
+    caches = [prefill_decode_cache(torch, cfg, batch, device, cos, sin, seed=100 * rank + i)
+              for i in range(cfg["distinct_layer_caches"])]
+    for c in caches:
+        refresh_prefix(c)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(7 + rank)
+    q = torch.randn(batch, H, 1, D, generator=gen, device=device).to(torch.bfloat16)
+    k = torch.randn(batch, G, 1, D, generator=gen, device=device).to(torch.bfloat16)
+    v = torch.randn(batch, G, 1, D, generator=gen, device=device).to(torch.bfloat16)
+    outs = [torch.empty(batch, H, 1, D, dtype=torch.bfloat16, device=device) for _ in range(cfg["layers"])]
+    scale = D ** -0.5
+    stream = torch.cuda.Stream(device)
+
+    def step():
+        for layer in range(cfg["layers"]):
+            log_kv_chunk_attention(caches[layer % len(caches)], q, k, v, scale, 0.0, out=outs[layer])
+
+    with torch.no_grad(), torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+        n_steps = args.decode_steps
+        if world > 1:
+            dist.barrier()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local_rank) as clocks:
+            start.record(stream)
+            for _ in range(n_steps):
+                graph.replay()
+            stop.record(stream)
+            torch.cuda.synchronize()
+        ms = start.elapsed_time(stop)
+        # Kernel-only view of one layer (for the roofline): the attention launch alone.
+        one = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(one, stream=stream):
+            log_kv_chunk_attention(caches[0], q, k, v, scale, 0.0, out=outs[0])
+        one.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 50
+        e0.record(stream)
+        for _ in range(reps):
+            one.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        layer_us = e0.elapsed_time(e1) * 1000.0 / reps
+        # e2e: public API per layer, the step's q/k/v copied from pinned host memory, outputs read back.
+        qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
+        qd, kd_, vd = (torch.empty_like(t) for t in (q, k, v))
+        host_out = torch.empty(cfg["layers"], batch, H, 1, D, dtype=torch.bfloat16).pin_memory()
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for _ in range(n_steps):
+            for layer in range(cfg["layers"]):
+                for d_, h_ in ((qd, qh), (kd_, kh), (vd, vh)):
+                    d_.copy_(h_, non_blocking=True)
+                log_kv_chunk_attention(caches[layer % len(caches)], qd, kd_, vd, scale, 0.0, out=outs[layer])
+                host_out[layer].copy_(outs[layer], non_blocking=True)
+        f1.record(stream)
+        torch.cuda.synchronize()
+        e2e_ms = f0.elapsed_time(f1)
+    del graph, one
+    times = torch.tensor([ms, e2e_ms, layer_us], device=device)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ms, e2e_ms, layer_us = times.tolist()
+    lengths = caches[0]._read.length.long()
+    R = cfg["recent"]
+    bytes_layer = int((lengths * (2 * D * 2 + 4)).sum().item()) + batch * G * (R * 2 * D * 2 + 2 * D * 2) \
+        + 2 * batch * H * D * 2
+    peak, peak_kind = measured_peaks()
+    achieved = bytes_layer / (layer_us * 1e-6) / 1e9
+    tokens = batch * world * n_steps
+    step_bytes = (q.numel() + k.numel() + v.numel()) * 2
+    return {"metric": "decode tok/s over a 32K compressed cache (28 layers)", "value": round(tokens / (ms / 1e3), 1),
+            "unit": "tok/s", "n_gpus": world, "steps": n_steps, "batch": batch * world,
+            "scaling": "strong", "us_per_layer_step": round(ms * 1000.0 / (n_steps * cfg["layers"]), 2),
+            "slots_per_lane": int(lengths.float().mean().item()) + R + 1,
+            "e2e": {"value": round(tokens / (e2e_ms / 1e3), 1), "unit": "tok/s",
+                    "h2d_bytes_per_step": step_bytes * cfg["layers"],
+                    "d2h_bytes_per_step": batch * H * D * 2 * cfg["layers"]},
+            "roofline": {"bound": "hbm", "kernel": "slot_attn_mma_kernel", "achieved": round(achieved, 1), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                         "bytes_per_launch": bytes_layer, "launch_us": round(layer_us, 2)},
+            "clocks": clocks.summary(), "gpu_launches": n_steps * cfg["layers"],
+            "config": {k_: cfg[k_] for k_ in cfg}}
+
+
 # ---------------------------------------------------------------------------------------------- CPU leg
 def cpu_flush_sample(n_flushes: int = 3, seed: int = 7):
     """Time the oracle port on flushes of one layer of the same shape (single thread)."""
@@ -339,6 +498,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-flushes", type=int, default=3, help="oracle flushes timed for cpu_baseline (0: skip)")
     ap.add_argument("--layers", type=int, default=WORKLOAD["layers"], help="layer caches (profiling runs only)")
+    ap.add_argument("--decode-steps", type=int, default=32, help="timed decode steps (0: skip the decode leg)")
+    ap.add_argument("--decode-batch", type=int, default=DECODE["batch"], help="decode sequences (profiling runs only)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -368,6 +529,7 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     res = bench_ours(args, rank, world, local_rank)
+    dec = bench_decode(args, rank, world, local_rank) if args.decode_steps > 0 else None
     cpu = None
     if rank == 0 and world == 1 and args.cpu_flushes > 0:
         us, n = cpu_flush_sample(args.cpu_flushes)
@@ -384,7 +546,8 @@ def main():
                     stages_us_median=res["stages_med"], stages_us_max=res["stages_max"],
                     flushes_per_step=res["flushes_per_step"],
                     rows_per_flush={k: round(v / res["flushes_per_step"], 1) for k, v in res["counters"].items()
-                                    if k != "flushes"})
+                                    if k != "flushes"},
+                    decode=dec)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

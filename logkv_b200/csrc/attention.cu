@@ -616,6 +616,347 @@ __global__ void __launch_bounds__(kAttnWarps * 32) slot_attn_kernel(AttnGeo a, l
   if (tid == 0) ticket[ln] = 0;
 }
 
+// ---------------------------------------------------------------- K4b: slot attention on tensor cores (bf16)
+// The query rows of a lane (heads per group x query tokens <= 16) are the M = 16 rows of
+// mma.sync.m16n8k16: per 16-slot tile QK^T is D/16 x 2 MMAs and PV is D/8 MMAs whose A
+// operand is the score accumulator itself.  Tiles never straddle the three segments
+// (prefix, window, new tokens), so a tile's K and V rows are contiguous blocks; each lane
+// copies 16-byte chunks into an XOR-swizzled stage (conflict-free ldmatrix), and a
+// __syncwarp after cp.async.wait_group makes every lane's chunks visible to the warp.
+__device__ __forceinline__ void ldsm_x4(unsigned addr, unsigned& r0, unsigned& r1, unsigned& r2, unsigned& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(unsigned addr, unsigned& r0, unsigned& r1, unsigned& r2, unsigned& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float* c, unsigned a0, unsigned a1, unsigned a2, unsigned a3, unsigned b0,
+                                         unsigned b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ unsigned pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const unsigned*>(&v);
+}
+
+template <int D>
+struct MmaShape {
+  static constexpr int TS = 16;             // slots per tile (two n8 score tiles, one k16 PV step)
+  static constexpr int CPR = D / 8;         // 16-byte chunks per row
+  static constexpr int KS = D / 16;         // k16 steps of QK^T
+  static constexpr int DT = D / 8;          // n8 output tiles of PV
+  static constexpr int STAGE_BYTES = 2 * TS * D * 2 + TS * 4;   // K, V (bf16) and the mass column
+  static constexpr size_t smem = (size_t)kAttnWarps * kAttnStages * STAGE_BYTES;
+  static_assert(D % 16 == 0 && D >= 16 && D <= 256, "head dim must be a multiple of 16 up to 256");
+  // Physical 16-byte chunk of logical chunk c in row r: rows of 8 consecutive ldmatrix
+  // addresses land in 8 distinct 16-byte bank groups.
+  __device__ __forceinline__ static int swz(int r, int c) {
+    if (CPR >= 8) return c ^ (r & 7);
+    return c ^ ((r * CPR / 8) & (CPR - 1));
+  }
+};
+
+template <int D, int NQ>
+__global__ void __launch_bounds__(kAttnWarps * 32) slot_attn_mma_kernel(AttnGeo a, logkv_prefix_t pre,
+                                                                       const __nv_bfloat16* rk,
+                                                                       const __nv_bfloat16* rv,
+                                                                       const __nv_bfloat16* kn,
+                                                                       const __nv_bfloat16* vn,
+                                                                       const __nv_bfloat16* q, __nv_bfloat16* out,
+                                                                       float* part, int* ticket) {
+  using S = MmaShape<D>;
+  constexpr int TS = S::TS, CPR = S::CPR, KS = S::KS, DT = S::DT;
+  static_assert(NQ >= 1 && NQ <= 16, "at most 16 query rows per lane");
+  extern __shared__ uint4 smem4[];
+  __shared__ float wm_[kAttnWarps][NQ];
+  __shared__ float wl_[kAttnWarps][NQ];
+  __shared__ int sh_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int g8 = lane >> 2, t4 = lane & 3;  // fragment row group and column pair
+  const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z, ln = b * a.G + g;
+  unsigned char* wbase = reinterpret_cast<unsigned char*>(smem4) + (size_t)warp * kAttnStages * S::STAGE_BYTES;
+  const unsigned wbase_s = (unsigned)__cvta_generic_to_shared(wbase);
+  const __nv_bfloat16* PK = static_cast<const __nv_bfloat16*>(pre.k);
+  const __nv_bfloat16* PV = static_cast<const __nv_bfloat16*>(pre.v);
+  // Work units: tiles of 16 rows inside each segment.
+  const int Lp = pre.length[ln], R = a.rcount, Tn = a.T;
+  const int up = (Lp + TS - 1) / TS, ur = (R + TS - 1) / TS, uc = (Tn + TS - 1) / TS;
+  const int U = up + ur + uc;
+  const int u0 = (int)((long long)U * split / a.nsplit), u1 = (int)((long long)U * (split + 1) / a.nsplit);
+  const int mine = (u1 - u0) > warp ? (u1 - u0 - warp + kAttnWarps - 1) / kAttnWarps : 0;
+
+  // Query A fragments (rows g8 and g8 + 8 of the 16, zero past NQ), loop invariant.
+  unsigned qa[KS][4];
+  {
+    const int r0 = g8, r1 = g8 + 8;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+      for (int hrow = 0; hrow < 2; ++hrow) {
+        const int r = hrow ? r1 : r0;
+        unsigned lo = 0u, hi = 0u;
+        if (r < NQ) {
+          const int h = g * a.rf + r / a.TQ, t = a.qoff + r % a.TQ;
+          const __nv_bfloat16* qp = q + (((size_t)b * a.H + h) * a.T + t) * D + ks * 16 + 2 * t4;
+          lo = *reinterpret_cast<const unsigned*>(qp);
+          hi = *reinterpret_cast<const unsigned*>(qp + 8);
+        }
+        qa[ks][hrow] = lo;       // a0a1 (row g8) / a2a3 (row g8+8)
+        qa[ks][2 + hrow] = hi;   // a4a5 / a6a7
+      }
+    }
+  }
+
+  // Unit -> (segment base of K, V, mass; first row; rows in the tile; slot class).
+  auto unit_info = [&](int u, const __nv_bfloat16*& kb, const __nv_bfloat16*& vb, const float*& mb, int& rows,
+                       int& cls, int& first) {
+    if (u < up) {
+      first = u * TS;
+      rows = min(TS, Lp - first);
+      const size_t r = (size_t)ln * pre.capacity + first;
+      kb = PK + r * D;
+      vb = PV + r * D;
+      mb = pre.mass + r;
+      cls = 0;
+    } else if (u < up + ur) {
+      first = (u - up) * TS;
+      rows = min(TS, R - first);
+      const size_t r = (size_t)ln * a.rcap + first;
+      kb = rk + r * D;
+      vb = rv + r * D;
+      mb = nullptr;
+      cls = 1;
+    } else {
+      first = (u - up - ur) * TS;
+      rows = min(TS, Tn - first);
+      const size_t r = (size_t)ln * a.T + first;
+      kb = kn + r * D;
+      vb = vn + r * D;
+      mb = nullptr;
+      cls = 2;
+    }
+  };
+
+  auto issue = [&](int k, int stage) {
+    if (k < mine) {
+      const __nv_bfloat16 *kb, *vb;
+      const float* mb;
+      int rows, cls, first;
+      unit_info(u0 + warp + k * kAttnWarps, kb, vb, mb, rows, cls, first);
+      unsigned char* st = wbase + (size_t)stage * S::STAGE_BYTES;
+      unsigned char* sk = st;
+      unsigned char* sv = st + TS * D * 2;
+      float* sm = reinterpret_cast<float*>(st + 2 * TS * D * 2);
+#pragma unroll
+      for (int i = 0; i < (TS * CPR + 31) / 32; ++i) {
+        const int flat = i * 32 + lane;
+        if (flat < TS * CPR) {
+          const int r = flat / CPR, c = flat % CPR;
+          const int off = r * D * 2 + S::swz(r, c) * 16;
+          if (r < rows) {
+            cp_async16(sk + off, kb + (size_t)flat * 8);
+            cp_async16(sv + off, vb + (size_t)flat * 8);
+          } else {
+            *reinterpret_cast<uint4*>(sk + off) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(sv + off) = make_uint4(0, 0, 0, 0);
+          }
+        }
+      }
+      if (lane < TS) {
+        if (cls == 0 && lane < rows) cp_async4(sm + lane, mb + lane);
+        else sm[lane] = 0.f;
+      }
+    }
+    cp_async_commit();
+  };
+
+  float o[DT][4];
+#pragma unroll
+  for (int j = 0; j < DT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;  // rows g8 and g8 + 8
+  const int rq0 = g8 % a.TQ, rq1 = (g8 + 8) % a.TQ;         // query token of each row
+
+#pragma unroll
+  for (int k = 0; k < kAttnStages - 1; ++k) issue(k, k);
+  for (int k = 0; k < mine; ++k) {
+    issue(k + kAttnStages - 1, (k + kAttnStages - 1) % kAttnStages);
+    cp_async_wait<kAttnStages - 1>();
+    __syncwarp();
+    const int stage = k % kAttnStages;
+    const __nv_bfloat16 *kb_, *vb_;
+    const float* mb_;
+    int rows, cls, first;
+    unit_info(u0 + warp + k * kAttnWarps, kb_, vb_, mb_, rows, cls, first);
+    const unsigned sk = wbase_s + stage * S::STAGE_BYTES;
+    const unsigned sv = sk + TS * D * 2;
+    const float* sm = reinterpret_cast<const float*>(wbase + (size_t)stage * S::STAGE_BYTES + 2 * TS * D * 2);
+    // S = Q K^T for the 16 slots: two n8 tiles.
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      // matrices: (tile 0, chunk 2ks), (tile 0, chunk 2ks+1), (tile 1, chunk 2ks), (tile 1, chunk 2ks+1)
+      const int mi = lane >> 3, rr = (mi >> 1) * 8 + (lane & 7), cc = 2 * ks + (mi & 1);
+      unsigned b0, b1, b2, b3;
+      ldsm_x4(sk + rr * D * 2 + S::swz(rr, cc) * 16, b0, b1, b2, b3);
+      mma_bf16(sc[0], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1);
+      mma_bf16(sc[1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b2, b3);
+    }
+    // Scores in the log2 domain with the mass term and masks; columns 8 j + 2 t4 + e.
+    float mt0 = -INFINITY, mt1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int col = 8 * j + 2 * t4 + e;
+        const float mass = sm[col];
+        const bool in = col < rows;
+        const bool v0 = in && (cls != 2 || !a.causal || first + col <= a.qoff + rq0);
+        const bool v1 = in && (cls != 2 || !a.causal || first + col <= a.qoff + rq1);
+        sc[j][e] = v0 ? (sc[j][e] + a.qx * mass) * a.scale_log2 : -INFINITY;
+        sc[j][2 + e] = v1 ? (sc[j][2 + e] + a.qx * mass) * a.scale_log2 : -INFINITY;
+        mt0 = fmaxf(mt0, sc[j][e]);
+        mt1 = fmaxf(mt1, sc[j][2 + e]);
+      }
+    }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      mt0 = fmaxf(mt0, __shfl_xor_sync(0xffffffffu, mt0, off));
+      mt1 = fmaxf(mt1, __shfl_xor_sync(0xffffffffu, mt1, off));
+    }
+    const float mn0 = fmaxf(m0, mt0), mn1 = fmaxf(m1, mt1);
+    const float al0 = mn0 == -INFINITY ? 1.f : exp2f(m0 - mn0);
+    const float al1 = mn1 == -INFINITY ? 1.f : exp2f(m1 - mn1);
+    m0 = mn0;
+    m1 = mn1;
+    float p[2][4];
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        p[j][e] = sc[j][e] == -INFINITY ? 0.f : exp2f(sc[j][e] - mn0);
+        p[j][2 + e] = sc[j][2 + e] == -INFINITY ? 0.f : exp2f(sc[j][2 + e] - mn1);
+        s0 += p[j][e];
+        s1 += p[j][2 + e];
+      }
+    }
+    l0 = l0 * al0 + s0;
+    l1 = l1 * al1 + s1;
+    if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
+#pragma unroll
+      for (int jd = 0; jd < DT; ++jd) {
+        o[jd][0] *= al0;
+        o[jd][1] *= al0;
+        o[jd][2] *= al1;
+        o[jd][3] *= al1;
+      }
+    }
+    // O += P V: P's A fragment is the score accumulator (k = the 16 slots).
+    const unsigned pa0 = pack_bf16x2(p[0][0], p[0][1]), pa1 = pack_bf16x2(p[0][2], p[0][3]);
+    const unsigned pa2 = pack_bf16x2(p[1][0], p[1][1]), pa3 = pack_bf16x2(p[1][2], p[1][3]);
+#pragma unroll
+    for (int jd = 0; jd < DT; jd += 2) {
+      // matrices: (slots 0-7, chunk jd), (slots 8-15, chunk jd), (slots 0-7, chunk jd+1), (slots 8-15, chunk jd+1)
+      const int mi = lane >> 3, rr = (mi & 1) * 8 + (lane & 7), cc = jd + (mi >> 1);
+      unsigned b0, b1, b2, b3;
+      ldsm_x4_t(sv + rr * D * 2 + S::swz(rr, cc) * 16, b0, b1, b2, b3);
+      mma_bf16(o[jd], pa0, pa1, pa2, pa3, b0, b1);
+      mma_bf16(o[jd + 1], pa0, pa1, pa2, pa3, b2, b3);
+    }
+    __syncwarp();
+  }
+  cp_async_wait<0>();
+  __syncwarp();
+  // Row sums over the four lanes of each row group.
+#pragma unroll
+  for (int off = 1; off < 4; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  float* wacc = reinterpret_cast<float*>(wbase);  // [NQ][D], this warp's own ring
+  if (t4 == 0) {
+    if (g8 < NQ) {
+      wm_[warp][g8] = m0;
+      wl_[warp][g8] = l0;
+    }
+    if (g8 + 8 < NQ) {
+      wm_[warp][g8 + 8] = m1;
+      wl_[warp][g8 + 8] = l1;
+    }
+  }
+#pragma unroll
+  for (int jd = 0; jd < DT; ++jd) {
+    const int c0 = jd * 8 + 2 * t4;
+    if (g8 < NQ) {
+      wacc[g8 * D + c0] = o[jd][0];
+      wacc[g8 * D + c0 + 1] = o[jd][1];
+    }
+    if (g8 + 8 < NQ) {
+      wacc[(g8 + 8) * D + c0] = o[jd][2];
+      wacc[(g8 + 8) * D + c0 + 1] = o[jd][3];
+    }
+  }
+  __syncthreads();
+  const size_t pstride = (size_t)D + 2;
+  for (int x = tid; x < NQ * D; x += blockDim.x) {
+    const int r = x / D, d = x % D;
+    float mx = -INFINITY;
+    for (int w = 0; w < kAttnWarps; ++w) mx = fmaxf(mx, wm_[w][r]);
+    float l = 0.f, ov = 0.f;
+    if (mx != -INFINITY) {
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float f = exp2f(wm_[w][r] - mx);
+        l += wl_[w][r] * f;
+        ov += reinterpret_cast<const float*>(reinterpret_cast<unsigned char*>(smem4) +
+                                             (size_t)w * kAttnStages * S::STAGE_BYTES)[r * D + d] * f;
+      }
+    }
+    if (a.nsplit == 1) {
+      const int h = g * a.rf + r / a.TQ, t = a.qoff + r % a.TQ;
+      out[(((size_t)b * a.H + h) * a.T + t) * D + d] = __float2bfloat16_rn(l > 0.f ? ov / l : 0.f);
+    } else {
+      float* pp = part + ((size_t)(ln * a.nsplit + split) * NQ + r) * pstride;
+      if (d == 0) {
+        pp[0] = mx;
+        pp[1] = l;
+      }
+      pp[2 + d] = ov;
+    }
+  }
+  if (a.nsplit == 1) return;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) sh_last = atomicAdd(ticket + ln, 1) == a.nsplit - 1;
+  __syncthreads();
+  if (!sh_last) return;
+  __threadfence();
+  for (int x = tid; x < NQ * D; x += blockDim.x) {
+    const int r = x / D, d = x % D;
+    float mx = -INFINITY;
+    for (int sidx = 0; sidx < a.nsplit; ++sidx)
+      mx = fmaxf(mx, __ldcg(part + ((size_t)(ln * a.nsplit + sidx) * NQ + r) * pstride));
+    float l = 0.f, ov = 0.f;
+    if (mx != -INFINITY) {
+      for (int sidx = 0; sidx < a.nsplit; ++sidx) {
+        const float* pp = part + ((size_t)(ln * a.nsplit + sidx) * NQ + r) * pstride;
+        const float f = exp2f(__ldcg(pp) - mx);
+        l += __ldcg(pp + 1) * f;
+        ov += __ldcg(pp + 2 + d) * f;
+      }
+    }
+    const int h = g * a.rf + r / a.TQ, t = a.qoff + r % a.TQ;
+    out[(((size_t)b * a.H + h) * a.T + t) * D + d] = __float2bfloat16_rn(l > 0.f ? ov / l : 0.f);
+  }
+  if (tid == 0) ticket[ln] = 0;
+}
+
 // ---------------------------------------------------------------- host side
 static bool dtype_ok(int d) { return d == LOGKV_DTYPE_F32 || d == LOGKV_DTYPE_BF16; }
 static size_t esize_of(int d) { return d == LOGKV_DTYPE_F32 ? 4 : 2; }
@@ -675,13 +1016,14 @@ static void launch_pack_mid(const PlanGeo& pg, const logkv_state_t& s, const log
                                                     static_cast<T*>(ov), status);
 }
 
-// Splits per lane: about eight CTAs per SM over the whole grid, at least four tiles per warp.
+// Splits per lane: about sixteen waves of two CTAs per SM over the grid (short tails), but
+// at least eight 16-row tiles per warp of a split.
 static int attn_splits(const logkv_layout_t& l, int prefix_capacity) {
   const int lanes = l.batch * l.groups;
-  const int smax = prefix_capacity + l.recent_capacity;
-  int n = (8 * 148 + lanes - 1) / lanes;
-  n = std::min(n, std::max(1, smax / (kAttnWarps * 4 * 16)));
-  return std::max(1, std::min(n, 128));
+  const int units = (prefix_capacity + l.recent_capacity) / 16 + 1;
+  int n = (16 * 2 * 148 + lanes - 1) / lanes;
+  n = std::min(n, std::max(1, units / (kAttnWarps * 8)));
+  return std::max(1, std::min(n, 256));
 }
 
 static size_t attn_part_bytes(const logkv_layout_t& l, int nq, int nsplit) {
@@ -713,14 +1055,53 @@ static int launch_attn_d(int nq, const AttnGeo& ag, const logkv_prefix_t& pre, c
   }
 }
 
-template <typename T>
-static int launch_attn(int D, int nq, const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
-                       const logkv_attention_args_t& x, float* part, int* ticket, cudaStream_t st) {
+template <int D, int NQ>
+static int launch_mma_dq(const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
+                         const logkv_attention_args_t& x, float* part, int* ticket, cudaStream_t st) {
+  using S = MmaShape<D>;
+  if (S::smem > 227 * 1024) return LOGKV_E_SMEM;
+  auto kern = slot_attn_mma_kernel<D, NQ>;
+  if (S::smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::smem);
+  using B16 = __nv_bfloat16;
+  kern<<<dim3(ag.nsplit, ag.G, ag.B), kAttnWarps * 32, S::smem, st>>>(
+      ag, pre, static_cast<const B16*>(s.recent_k), static_cast<const B16*>(s.recent_v),
+      static_cast<const B16*>(x.k_new), static_cast<const B16*>(x.v_new), static_cast<const B16*>(x.q),
+      static_cast<B16*>(x.out), part, ticket);
+  return launch_status();
+}
+
+template <int D>
+static int launch_mma_d(int nq, const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
+                        const logkv_attention_args_t& x, float* part, int* ticket, cudaStream_t st) {
+  switch (nq) {
+    case 1: return launch_mma_dq<D, 1>(ag, pre, s, x, part, ticket, st);
+    case 2: return launch_mma_dq<D, 2>(ag, pre, s, x, part, ticket, st);
+    case 4: return launch_mma_dq<D, 4>(ag, pre, s, x, part, ticket, st);
+    case 8: return launch_mma_dq<D, 8>(ag, pre, s, x, part, ticket, st);
+    case 16: return launch_mma_dq<D, 16>(ag, pre, s, x, part, ticket, st);
+    default: return LOGKV_E_SHAPE;
+  }
+}
+
+// bf16: tensor-core kernel; fp32: CUDA-core kernel (keeps float32 products).
+static int launch_attn(int dtype, int D, int nq, const AttnGeo& ag, const logkv_prefix_t& pre,
+                       const logkv_state_t& s, const logkv_attention_args_t& x, float* part, int* ticket,
+                       cudaStream_t st) {
+  if (dtype == LOGKV_DTYPE_BF16) {
+    switch (D) {
+      case 16: return launch_mma_d<16>(nq, ag, pre, s, x, part, ticket, st);
+      case 32: return launch_mma_d<32>(nq, ag, pre, s, x, part, ticket, st);
+      case 64: return launch_mma_d<64>(nq, ag, pre, s, x, part, ticket, st);
+      case 128: return launch_mma_d<128>(nq, ag, pre, s, x, part, ticket, st);
+      case 256: return launch_mma_d<256>(nq, ag, pre, s, x, part, ticket, st);
+      default: return LOGKV_E_SHAPE;
+    }
+  }
   switch (D) {
-    case 16: return launch_attn_d<T, 16>(nq, ag, pre, s, x, part, ticket, st);
-    case 32: return launch_attn_d<T, 32>(nq, ag, pre, s, x, part, ticket, st);
-    case 64: return launch_attn_d<T, 64>(nq, ag, pre, s, x, part, ticket, st);
-    case 128: return launch_attn_d<T, 128>(nq, ag, pre, s, x, part, ticket, st);
+    case 16: return launch_attn_d<float, 16>(nq, ag, pre, s, x, part, ticket, st);
+    case 32: return launch_attn_d<float, 32>(nq, ag, pre, s, x, part, ticket, st);
+    case 64: return launch_attn_d<float, 64>(nq, ag, pre, s, x, part, ticket, st);
+    case 128: return launch_attn_d<float, 128>(nq, ag, pre, s, x, part, ticket, st);
     default: return LOGKV_E_SHAPE;
   }
 }
@@ -829,9 +1210,7 @@ LOGKV_API int logkv_attention(const logkv_layout_t* layout, const logkv_state_t*
   ag.scale_log2 = args->scale * 1.4426950408889634f;
   ag.qx = args->qx;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (layout->dtype == LOGKV_DTYPE_BF16)
-    return launch_attn<__nv_bfloat16>(layout->dim, nq, ag, *prefix, *state, *args, part, ticket, st);
-  return launch_attn<float>(layout->dim, nq, ag, *prefix, *state, *args, part, ticket, st);
+  return launch_attn(layout->dtype, layout->dim, nq, ag, *prefix, *state, *args, part, ticket, st);
 }
 
 }  // extern "C"
