@@ -465,6 +465,69 @@ def bench_decode(args, rank, world, local_rank):
             "config": {k_: cfg[k_] for k_ in cfg}}
 
 
+def bench_prefill(args, rank, world, local_rank):
+    """Chunk attention of one 2048-token chunk (16 q / 8 KV heads) over a pre-filled cache, per layer."""
+    import torch
+    import torch.distributed as dist
+    from logkv_b200.attention import log_kv_chunk_attention, refresh_prefix
+    from logkv_b200.workload import rope_tables
+    device = torch.device("cuda", local_rank)
+    cfg = dict(DECODE, batch=1)
+    H, G, D, T = cfg["heads"], cfg["groups"], cfg["head_dim"], 2048
+    cos_np, sin_np = rope_tables(cfg["max_seq"] + 1024, D, base=1e6)
+    cos, sin = torch.from_numpy(cos_np).to(device), torch.from_numpy(sin_np).to(device)
+    caches = [prefill_decode_cache(torch, cfg, 1, device, cos, sin, seed=500 + 100 * rank + i) for i in range(2)]
+    for c in caches:
+        refresh_prefix(c)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(11 + rank)
+    q = torch.randn(1, H, T, D, generator=gen, device=device).to(torch.bfloat16)
+    k = torch.randn(1, G, T, D, generator=gen, device=device).to(torch.bfloat16)
+    v = torch.randn(1, G, T, D, generator=gen, device=device).to(torch.bfloat16)
+    out = torch.empty(1, H, T, D, dtype=torch.bfloat16, device=device)
+    scale = D ** -0.5
+    stream = torch.cuda.Stream(device)
+    reps = max(4, args.decode_steps // 2)
+    with torch.no_grad(), torch.cuda.stream(stream):
+        for _ in range(3):
+            log_kv_chunk_attention(caches[0], q, k, v, scale, 0.0, out=out)
+        g1 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g1, stream=stream):
+            for layer in range(cfg["layers"]):
+                log_kv_chunk_attention(caches[layer % 2], q, k, v, scale, 0.0, out=out)
+        g1.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            g1.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+    del g1
+    t = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    us = t.item() * 1000.0 / (reps * cfg["layers"])
+    Lp = int(caches[0]._read.length[0].float().mean().item())
+    R = cfg["recent"]
+    flops = 4.0 * D * H * (T * (Lp + R) + T * (T + 1) / 2)   # QK^T and PV over the visible slots
+    peak = 1649.1
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            peak = float(json.load(fh)["bf16_tflops"])
+    tflops = flops / (us * 1e-6) / 1e12
+    return {"metric": "chunk attention us per 2048-token chunk/layer", "value": round(us, 2), "unit": "us",
+            "roofline": {"bound": "tensor", "kernel": "chunk_attn_mma_kernel", "achieved": round(tflops, 1),
+                         "peak": peak, "unit": "TFLOP/s", "frac": round(tflops / peak, 4), "traffic": None,
+                         "flops_per_launch": flops},
+            "config": {"heads": H, "groups": G, "head_dim": D, "chunk": T, "prefix_slots": Lp, "recent": R,
+                       "layers": cfg["layers"], "distinct_layer_caches": 2}}
+
+
 # ---------------------------------------------------------------------------------------------- CPU leg
 def cpu_flush_sample(n_flushes: int = 3, seed: int = 7):
     """Time the oracle port on flushes of one layer of the same shape (single thread)."""
@@ -530,6 +593,7 @@ def main():
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     res = bench_ours(args, rank, world, local_rank)
     dec = bench_decode(args, rank, world, local_rank) if args.decode_steps > 0 else None
+    pre = bench_prefill(args, rank, world, local_rank) if args.decode_steps > 0 else None
     cpu = None
     if rank == 0 and world == 1 and args.cpu_flushes > 0:
         us, n = cpu_flush_sample(args.cpu_flushes)
@@ -547,7 +611,7 @@ def main():
                     flushes_per_step=res["flushes_per_step"],
                     rows_per_flush={k: round(v / res["flushes_per_step"], 1) for k, v in res["counters"].items()
                                     if k != "flushes"},
-                    decode=dec)
+                    decode=dec, prefill=pre)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

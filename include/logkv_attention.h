@@ -94,12 +94,16 @@ LOGKV_API int logkv_pack_mid(const logkv_layout_t* layout, const logkv_state_t* 
  * for the query tokens [q_offset, q_offset + q_tokens) of the call:
  *   out = softmax(scale * (q . k_s + qx * mass_s)) v_s,
  * with causal != 0 new token j visible to query token t iff j <= t (the reference's
- * lower-right causal tail), else every new token visible; every other slot visible.  heads / groups * q_tokens must be 1, 2,
- * 4 or 8 (decode: one or two tokens per sequence); a longer chunk is covered by
- * several calls.  Replaces log_kv_chunk_attention (litgpt/log_kv_cache.py:6802-6864
- * -> _mid_chunk_attention :6770-6799 -> Flash SDPA over the packed inputs of
+ * lower-right causal tail), else every new token visible; every other slot visible.
+ * Replaces log_kv_chunk_attention (litgpt/log_kv_cache.py:6802-6864 ->
+ * _mid_chunk_attention :6770-6799 -> Flash SDPA over the packed inputs of
  * _slot_sdpa_inputs :6439-6464).  qx is the query's mass coordinate, 1/scale
  * rounded to the storage dtype.
+ *
+ * Kernels: bf16 caches use tensor cores, a split-K decode kernel for up to 16 query
+ * rows per lane (heads / groups * q_tokens in {1, 2, 4, 8, 16}) and a chunk kernel for
+ * more (heads / groups a power of two <= 8, head dim <= 128); float32 caches use
+ * CUDA cores for 1, 2, 4 or 8 query rows per lane (longer chunks take several calls).
  */
 typedef struct logkv_attention_args {
   const void* q;        /* [B,H,tokens,D] storage dtype, post-RoPE */

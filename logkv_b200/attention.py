@@ -22,7 +22,9 @@ import torch
 
 from . import _lib
 
-_MAX_QUERY_ROWS = 8   # query rows (heads per group x query tokens) per attention launch
+# Query rows (heads per group x query tokens) one decode-kernel launch covers; bf16 chunks
+# with more rows go to the chunk kernel in a single launch.
+_MAX_QUERY_ROWS = {torch.bfloat16: 16, torch.float32: 8}
 
 
 class _ReadState:
@@ -214,11 +216,15 @@ def log_kv_chunk_attention(cache, q_b, k_b, v_b, scale, second_order_scale=1.0, 
         raise NotImplementedError("logkv_b200 attention is forward-only")
     rs = refresh_prefix(cache)
     rf = H // G
-    if rf > _MAX_QUERY_ROWS:
-        raise ValueError(f"{rf} query heads per KV group exceeds {_MAX_QUERY_ROWS}")
-    step = 1
-    while 2 * step * rf <= _MAX_QUERY_ROWS and 2 * step <= T:
-        step *= 2
+    rows = _MAX_QUERY_ROWS[q_b.dtype]
+    if rf > rows or rf & (rf - 1):
+        raise ValueError(f"{rf} query heads per KV group: must be a power of two <= {rows}")
+    if q_b.dtype == torch.bfloat16 and rf * T > rows and cache.k_dim <= 128 and rf <= 8:
+        step = T                    # one launch of the chunk kernel
+    else:
+        step = 1
+        while 2 * step * rf <= rows and 2 * step <= T:
+            step *= 2
     q, k, v = q_b.contiguous(), k_b.contiguous(), v_b.contiguous()
     if out is None:
         out = torch.empty(B, H, T, cache.v_dim, dtype=q.dtype, device=q.device)
@@ -226,7 +232,7 @@ def log_kv_chunk_attention(cache, q_b, k_b, v_b, scale, second_order_scale=1.0, 
     pre = rs.prefix_struct()
     qx = query_extra(scale, q.dtype)
     t0 = 0
-    while t0 < T:               # query blocks of a power-of-two size, at most `step` tokens
+    while t0 < T:               # query blocks: the whole chunk, or powers of two of at most `step`
         n = step
         while n > T - t0:
             n //= 2

@@ -957,6 +957,247 @@ __global__ void __launch_bounds__(kAttnWarps * 32) slot_attn_mma_kernel(AttnGeo 
   if (tid == 0) ticket[ln] = 0;
 }
 
+// ---------------------------------------------------------------- K5: chunk (prefill) attention on tensor cores
+// One CTA = 128 query rows of a lane (rf heads x 128/rf consecutive tokens); warp w owns rows
+// 16w..16w+15 (one head, 16 consecutive tokens).  All warps share 64-slot K/V tiles staged
+// by the whole CTA through a cp.async ring; per tile and warp QK^T is 8 n-tiles x D/16
+// k-steps and PV is D/8 n-tiles x 4 k-steps of mma.sync.m16n8k16 (bf16 in, f32 accumulate).
+// New-token tiles entirely after the CTA's last query token are skipped.
+constexpr int kPfWarps = 8;
+constexpr int kPfRows = 16 * kPfWarps;  // query rows per CTA
+constexpr int kPfTS = 64;               // slots per tile
+constexpr int kPfStages = 3;
+
+template <int D>
+struct PfShape {
+  static constexpr int CPR = D / 8, KS = D / 16, DT = D / 8;
+  static constexpr int TILE_BYTES = kPfTS * D * 2;                      // one of K / V
+  static constexpr int STAGE_BYTES = 2 * TILE_BYTES + kPfTS * 4;        // K, V, mass
+  static constexpr size_t smem = (size_t)kPfStages * STAGE_BYTES;
+  __device__ __forceinline__ static int swz(int r, int c) { return MmaShape<D>::swz(r, c); }
+};
+
+template <int D>
+__global__ void __launch_bounds__(kPfWarps * 32) chunk_attn_mma_kernel(AttnGeo a, logkv_prefix_t pre,
+                                                                      const __nv_bfloat16* rk,
+                                                                      const __nv_bfloat16* rv,
+                                                                      const __nv_bfloat16* kn,
+                                                                      const __nv_bfloat16* vn,
+                                                                      const __nv_bfloat16* q, __nv_bfloat16* out) {
+  using S = PfShape<D>;
+  constexpr int CPR = S::CPR, KS = S::KS, DT = S::DT, TS = kPfTS;
+  extern __shared__ uint4 smem4[];
+  unsigned char* sbase = reinterpret_cast<unsigned char*>(smem4);
+  const unsigned sbase_s = (unsigned)__cvta_generic_to_shared(sbase);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int g8 = lane >> 2, t4 = lane & 3;
+  const int g = blockIdx.y, b = blockIdx.z, ln = b * a.G + g;
+  const int QT = kPfRows / a.rf;                       // tokens per CTA
+  const int tq0 = a.qoff + blockIdx.x * QT;            // first query token of the CTA
+  const int row0 = warp * 16;                          // this warp's first row
+  const int hh = row0 / QT, tw = tq0 + row0 % QT;      // head-in-group and first token of the warp
+  const int h = g * a.rf + hh;
+  const int tlast = min(a.qoff + a.TQ, tq0 + QT) - 1;  // CTA's last query token
+  const __nv_bfloat16* PK = static_cast<const __nv_bfloat16*>(pre.k);
+  const __nv_bfloat16* PV = static_cast<const __nv_bfloat16*>(pre.v);
+  const int Lp = pre.length[ln], R = a.rcount;
+  const int Tvis = a.causal ? min(a.T, tlast + 1) : a.T;   // new tokens any row of the CTA can see
+  const int up = (Lp + TS - 1) / TS, ur = (R + TS - 1) / TS, uc = (Tvis + TS - 1) / TS;
+  const int U = up + ur + uc;
+
+  // Query A fragments of the warp's 16 rows (tokens tw .. tw+15 of head h).
+  unsigned qa[KS][4];
+  {
+    const int t0r = tw + g8, t1r = tw + g8 + 8;
+    const bool ok0 = t0r < a.qoff + a.TQ, ok1 = t1r < a.qoff + a.TQ;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      const __nv_bfloat16* q0 = q + (((size_t)b * a.H + h) * a.T + t0r) * D + ks * 16 + 2 * t4;
+      const __nv_bfloat16* q1 = q + (((size_t)b * a.H + h) * a.T + t1r) * D + ks * 16 + 2 * t4;
+      qa[ks][0] = ok0 ? *reinterpret_cast<const unsigned*>(q0) : 0u;
+      qa[ks][1] = ok1 ? *reinterpret_cast<const unsigned*>(q1) : 0u;
+      qa[ks][2] = ok0 ? *reinterpret_cast<const unsigned*>(q0 + 8) : 0u;
+      qa[ks][3] = ok1 ? *reinterpret_cast<const unsigned*>(q1 + 8) : 0u;
+    }
+  }
+
+  auto unit_info = [&](int u, const __nv_bfloat16*& kb, const __nv_bfloat16*& vb, const float*& mb, int& rows,
+                       int& cls, int& first) {
+    if (u < up) {
+      first = u * TS;
+      rows = min(TS, Lp - first);
+      const size_t r = (size_t)ln * pre.capacity + first;
+      kb = PK + r * D;
+      vb = PV + r * D;
+      mb = pre.mass + r;
+      cls = 0;
+    } else if (u < up + ur) {
+      first = (u - up) * TS;
+      rows = min(TS, R - first);
+      const size_t r = (size_t)ln * a.rcap + first;
+      kb = rk + r * D;
+      vb = rv + r * D;
+      mb = nullptr;
+      cls = 1;
+    } else {
+      first = (u - up - ur) * TS;
+      rows = min(TS, Tvis - first);
+      const size_t r = (size_t)ln * a.T + first;
+      kb = kn + r * D;
+      vb = vn + r * D;
+      mb = nullptr;
+      cls = 2;
+    }
+  };
+
+  auto issue = [&](int u, int stage) {
+    if (u < U) {
+      const __nv_bfloat16 *kb, *vb;
+      const float* mb;
+      int rows, cls, first;
+      unit_info(u, kb, vb, mb, rows, cls, first);
+      unsigned char* st = sbase + (size_t)stage * S::STAGE_BYTES;
+      unsigned char* sk = st;
+      unsigned char* sv = st + S::TILE_BYTES;
+      float* sm = reinterpret_cast<float*>(st + 2 * S::TILE_BYTES);
+      for (int flat = tid; flat < TS * CPR; flat += kPfWarps * 32) {
+        const int r = flat / CPR, c = flat % CPR;
+        const int off = r * D * 2 + S::swz(r, c) * 16;
+        if (r < rows) {
+          cp_async16(sk + off, kb + (size_t)flat * 8);
+          cp_async16(sv + off, vb + (size_t)flat * 8);
+        } else {
+          *reinterpret_cast<uint4*>(sk + off) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(sv + off) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      if (tid < TS) {
+        if (cls == 0 && tid < rows) cp_async4(sm + tid, mb + tid);
+        else sm[tid] = 0.f;
+      }
+    }
+    cp_async_commit();
+  };
+
+  float o[DT][4];
+#pragma unroll
+  for (int j = 0; j < DT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  const int tr0 = tw + g8, tr1 = tw + g8 + 8;  // query tokens of the lane's two rows
+
+#pragma unroll
+  for (int k = 0; k < kPfStages - 1; ++k) issue(k, k);
+  for (int u = 0; u < U; ++u) {
+    issue(u + kPfStages - 1, (u + kPfStages - 1) % kPfStages);
+    cp_async_wait<kPfStages - 1>();
+    __syncthreads();
+    const int stage = u % kPfStages;
+    const __nv_bfloat16 *kb_, *vb_;
+    const float* mb_;
+    int rows, cls, first;
+    unit_info(u, kb_, vb_, mb_, rows, cls, first);
+    const unsigned sk = sbase_s + stage * S::STAGE_BYTES;
+    const unsigned sv = sk + S::TILE_BYTES;
+    const float* sm = reinterpret_cast<const float*>(sbase + (size_t)stage * S::STAGE_BYTES + 2 * S::TILE_BYTES);
+    float sc[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+      for (int jp = 0; jp < 4; ++jp) {
+        const int mi = lane >> 3, rr = (2 * jp + (mi >> 1)) * 8 + (lane & 7), cc = 2 * ks + (mi & 1);
+        unsigned b0, b1, b2, b3;
+        ldsm_x4(sk + rr * D * 2 + S::swz(rr, cc) * 16, b0, b1, b2, b3);
+        mma_bf16(sc[2 * jp], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b0, b1);
+        mma_bf16(sc[2 * jp + 1], qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3], b2, b3);
+      }
+    }
+    float mt0 = -INFINITY, mt1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int col = 8 * j + 2 * t4 + e;
+        const float mass = sm[col];
+        const bool in = col < rows;
+        const bool v0 = in && (cls != 2 || !a.causal || first + col <= tr0);
+        const bool v1 = in && (cls != 2 || !a.causal || first + col <= tr1);
+        sc[j][e] = v0 ? (sc[j][e] + a.qx * mass) * a.scale_log2 : -INFINITY;
+        sc[j][2 + e] = v1 ? (sc[j][2 + e] + a.qx * mass) * a.scale_log2 : -INFINITY;
+        mt0 = fmaxf(mt0, sc[j][e]);
+        mt1 = fmaxf(mt1, sc[j][2 + e]);
+      }
+    }
+#pragma unroll
+    for (int off = 1; off < 4; off <<= 1) {
+      mt0 = fmaxf(mt0, __shfl_xor_sync(0xffffffffu, mt0, off));
+      mt1 = fmaxf(mt1, __shfl_xor_sync(0xffffffffu, mt1, off));
+    }
+    const float mn0 = fmaxf(m0, mt0), mn1 = fmaxf(m1, mt1);
+    const float al0 = mn0 == -INFINITY ? 1.f : exp2f(m0 - mn0);
+    const float al1 = mn1 == -INFINITY ? 1.f : exp2f(m1 - mn1);
+    m0 = mn0;
+    m1 = mn1;
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        sc[j][e] = sc[j][e] == -INFINITY ? 0.f : exp2f(sc[j][e] - mn0);
+        sc[j][2 + e] = sc[j][2 + e] == -INFINITY ? 0.f : exp2f(sc[j][2 + e] - mn1);
+        s0 += sc[j][e];
+        s1 += sc[j][2 + e];
+      }
+    }
+    l0 = l0 * al0 + s0;
+    l1 = l1 * al1 + s1;
+    if (__any_sync(0xffffffffu, al0 != 1.f || al1 != 1.f)) {
+#pragma unroll
+      for (int jd = 0; jd < DT; ++jd) {
+        o[jd][0] *= al0;
+        o[jd][1] *= al0;
+        o[jd][2] *= al1;
+        o[jd][3] *= al1;
+      }
+    }
+#pragma unroll
+    for (int kk = 0; kk < TS / 16; ++kk) {
+      const unsigned pa0 = pack_bf16x2(sc[2 * kk][0], sc[2 * kk][1]);
+      const unsigned pa1 = pack_bf16x2(sc[2 * kk][2], sc[2 * kk][3]);
+      const unsigned pa2 = pack_bf16x2(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
+      const unsigned pa3 = pack_bf16x2(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
+#pragma unroll
+      for (int jd = 0; jd < DT; jd += 2) {
+        const int mi = lane >> 3, rr = 16 * kk + (mi & 1) * 8 + (lane & 7), cc = jd + (mi >> 1);
+        unsigned b0, b1, b2, b3;
+        ldsm_x4_t(sv + rr * D * 2 + S::swz(rr, cc) * 16, b0, b1, b2, b3);
+        mma_bf16(o[jd], pa0, pa1, pa2, pa3, b0, b1);
+        mma_bf16(o[jd + 1], pa0, pa1, pa2, pa3, b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int off = 1; off < 4; off <<= 1) {
+    l0 += __shfl_xor_sync(0xffffffffu, l0, off);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, off);
+  }
+  const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f, inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
+  const bool ok0 = tr0 < a.qoff + a.TQ, ok1 = tr1 < a.qoff + a.TQ;
+#pragma unroll
+  for (int jd = 0; jd < DT; ++jd) {
+    const int c0 = jd * 8 + 2 * t4;
+    if (ok0)
+      *reinterpret_cast<__nv_bfloat162*>(out + (((size_t)b * a.H + h) * a.T + tr0) * D + c0) =
+          __floats2bfloat162_rn(o[jd][0] * inv0, o[jd][1] * inv0);
+    if (ok1)
+      *reinterpret_cast<__nv_bfloat162*>(out + (((size_t)b * a.H + h) * a.T + tr1) * D + c0) =
+          __floats2bfloat162_rn(o[jd][2] * inv1, o[jd][3] * inv1);
+  }
+}
+
 // ---------------------------------------------------------------- host side
 static bool dtype_ok(int d) { return d == LOGKV_DTYPE_F32 || d == LOGKV_DTYPE_BF16; }
 static size_t esize_of(int d) { return d == LOGKV_DTYPE_F32 ? 4 : 2; }
@@ -1083,6 +1324,39 @@ static int launch_mma_d(int nq, const AttnGeo& ag, const logkv_prefix_t& pre, co
   }
 }
 
+// Chunk kernel: bf16, more than 16 query rows per lane, 16 <= D <= 128, rf a power of two <= 8.
+static bool use_chunk_kernel(const logkv_layout_t& l, int heads, int q_tokens) {
+  const int rf = heads / l.groups;
+  return l.dtype == LOGKV_DTYPE_BF16 && rf * q_tokens > 16 && l.dim % 16 == 0 && l.dim <= 128 &&
+         (rf == 1 || rf == 2 || rf == 4 || rf == 8);
+}
+
+template <int D>
+static int launch_chunk_d(const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
+                          const logkv_attention_args_t& x, cudaStream_t st) {
+  using S = PfShape<D>;
+  auto kern = chunk_attn_mma_kernel<D>;
+  if (S::smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::smem);
+  const int QT = kPfRows / ag.rf;
+  using B16 = __nv_bfloat16;
+  kern<<<dim3((ag.TQ + QT - 1) / QT, ag.G, ag.B), kPfWarps * 32, S::smem, st>>>(
+      ag, pre, static_cast<const B16*>(s.recent_k), static_cast<const B16*>(s.recent_v),
+      static_cast<const B16*>(x.k_new), static_cast<const B16*>(x.v_new), static_cast<const B16*>(x.q),
+      static_cast<B16*>(x.out));
+  return launch_status();
+}
+
+static int launch_chunk(int D, const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
+                        const logkv_attention_args_t& x, cudaStream_t st) {
+  switch (D) {
+    case 16: return launch_chunk_d<16>(ag, pre, s, x, st);
+    case 32: return launch_chunk_d<32>(ag, pre, s, x, st);
+    case 64: return launch_chunk_d<64>(ag, pre, s, x, st);
+    case 128: return launch_chunk_d<128>(ag, pre, s, x, st);
+    default: return LOGKV_E_SHAPE;
+  }
+}
+
 // bf16: tensor-core kernel; fp32: CUDA-core kernel (keeps float32 products).
 static int launch_attn(int dtype, int D, int nq, const AttnGeo& ag, const logkv_prefix_t& pre,
                        const logkv_state_t& s, const logkv_attention_args_t& x, float* part, int* ticket,
@@ -1170,6 +1444,7 @@ LOGKV_API int logkv_pack_mid(const logkv_layout_t* layout, const logkv_state_t* 
 LOGKV_API size_t logkv_attention_workspace_bytes(const logkv_layout_t* layout, int32_t heads, int32_t q_tokens,
                                                  int32_t prefix_capacity) {
   if (check_layout(layout) || heads < layout->groups || heads % layout->groups || q_tokens < 1) return 0;
+  if (use_chunk_kernel(*layout, heads, q_tokens)) return 256;
   const int nq = heads / layout->groups * q_tokens;
   const int nsplit = attn_splits(*layout, prefix_capacity);
   const size_t lanes = (size_t)layout->batch * layout->groups;
@@ -1210,6 +1485,7 @@ LOGKV_API int logkv_attention(const logkv_layout_t* layout, const logkv_state_t*
   ag.scale_log2 = args->scale * 1.4426950408889634f;
   ag.qx = args->qx;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (use_chunk_kernel(*layout, H, TQ)) return launch_chunk(layout->dim, ag, *prefix, *state, *args, st);
   return launch_attn(layout->dtype, layout->dim, nq, ag, *prefix, *state, *args, part, ticket, st);
 }
 
