@@ -8,11 +8,12 @@ import re
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADER = os.path.join(ROOT, "include", "logkv_b200.h")
+HEADERS = [os.path.join(ROOT, "include", n) for n in sorted(os.listdir(os.path.join(ROOT, "include")))
+           if n.endswith(".h")]
 
 
 def declared_symbols():
-    text = open(HEADER).read()
+    text = "".join(open(h).read() for h in HEADERS)
     return sorted(set(re.findall(r"LOGKV_API\s+[\w\s\*]+?\b(logkv_\w+)\s*\(", text)))
 
 
@@ -27,6 +28,9 @@ def lib():
 def test_header_declares_entry_points():
     names = declared_symbols()
     assert "logkv_flush" in names and "logkv_flush_workspace_bytes" in names
+    for name in ("logkv_attention_plan", "logkv_pack_prefix", "logkv_pack_mid", "logkv_attention",
+                 "logkv_attention_workspace_bytes"):
+        assert name in names
 
 
 def test_library_exports_every_declared_symbol(lib):
@@ -46,3 +50,17 @@ def test_workspace_size_and_argument_checks(lib):
     state = _lib.State()
     assert lib.logkv_flush(ctypes.byref(bad), ctypes.byref(state), 2048, 4096, None, 0, None) == -1
     assert lib.logkv_flush(ctypes.byref(layout), None, 2048, 4096, None, 0, None) == -4
+
+
+def test_attention_argument_checks(lib):
+    from logkv_b200 import _lib
+    layout = _lib.Layout(1, 8, 128, 12, 7, 125, 4096, 256, 64, 1, 1, 1.0, 2048.0, 1.0)
+    # decode shapes need split partials; a bf16 chunk needs none beyond the header
+    assert lib.logkv_attention_workspace_bytes(ctypes.byref(layout), 16, 1, 10756) > 256
+    assert lib.logkv_attention_workspace_bytes(ctypes.byref(layout), 16, 2048, 10756) == 256
+    assert lib.logkv_attention_workspace_bytes(ctypes.byref(layout), 12, 1, 10756) == 0   # heads % groups
+    state, pre, args = _lib.State(), _lib.Prefix(), _lib.AttentionArgs()
+    assert lib.logkv_attention(ctypes.byref(layout), ctypes.byref(state), ctypes.byref(pre), ctypes.byref(args),
+                               None, 0, None) == -4
+    plan = _lib.Plan()
+    assert lib.logkv_attention_plan(ctypes.byref(layout), ctypes.byref(state), ctypes.byref(plan), None) == -4
