@@ -136,6 +136,31 @@ LOGKV_API int logkv_flush(const logkv_layout_t* layout, const logkv_state_t* sta
 LOGKV_API int logkv_flush_static(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
                                  int32_t recent_count, void* stream);
 
+/*
+ * KV-head sharding of one sequence (no reference counterpart: the reference runs a
+ * layer's cache on one device).  Each rank's layout and state hold its own block of
+ * `groups` KV groups (rank r: global groups [r * groups, (r + 1) * groups)).  Every
+ * group is independent during a flush except the Alpha span score, which is the mean
+ * over all groups of per-group parts (Beta: the mean of the top two groups)
+ * (litgpt/alpha_log_kv.py:154-156, :173).  So a sharded flush is two calls around one
+ * exchange:
+ *   logkv_flush_scores  snapshot, span cut and this rank's per-group span parts;
+ *   (caller)            all-gather the parts, [batch, candidates, groups, 2] float32 at
+ *                       the address logkv_flush_partials gives, over the ranks in rank
+ *                       order into one [ranks, batch, candidates, groups, 2] device buffer;
+ *   logkv_flush_commit  the rest of the flush, reading the gathered parts in global group
+ *                       order, so every rank makes the unsharded flush's span choice.
+ * With ranks == 1 and partials_all == NULL the pair equals logkv_flush.
+ */
+LOGKV_API int logkv_flush_scores(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                 int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream);
+LOGKV_API int logkv_flush_commit(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                 int32_t recent_count, void* workspace, size_t workspace_bytes,
+                                 const float* partials_all, int32_t ranks, void* stream);
+/* Host-side address arithmetic only: where this workspace keeps the rank's span parts, and their float count. */
+LOGKV_API int logkv_flush_partials(const logkv_layout_t* layout, int32_t flush_tokens, void* workspace,
+                                   float** partials, size_t* count);
+
 /* Copy the workspace status word to *out (synchronizes `stream`); nonzero = a capacity was exceeded. */
 LOGKV_API int logkv_read_status(const void* workspace, int32_t* out, void* stream);
 

@@ -93,6 +93,14 @@ def lib() -> ctypes.CDLL:
         handle.logkv_read_counters.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int32,
                                                ctypes.c_void_p]
         P = ctypes.POINTER
+        flush_args = [P(Layout), P(State), ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_size_t]
+        handle.logkv_flush_scores.restype = ctypes.c_int
+        handle.logkv_flush_scores.argtypes = flush_args + [ctypes.c_void_p]
+        handle.logkv_flush_commit.restype = ctypes.c_int
+        handle.logkv_flush_commit.argtypes = flush_args + [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p]
+        handle.logkv_flush_partials.restype = ctypes.c_int
+        handle.logkv_flush_partials.argtypes = [P(Layout), ctypes.c_int32, ctypes.c_void_p,
+                                                P(P(ctypes.c_float)), P(ctypes.c_size_t)]
         handle.logkv_attention_plan.restype = ctypes.c_int
         handle.logkv_attention_plan.argtypes = [P(Layout), P(State), P(Plan), ctypes.c_void_p]
         handle.logkv_pack_prefix.restype = ctypes.c_int

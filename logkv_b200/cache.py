@@ -57,7 +57,8 @@ class LogStructuredKVCache(nn.Module):
                  semantic_centroid_backend: str = "sequential", semantic_replay_updates: bool = False,
                  cos_cache=None, sin_cache=None, rope_n_elem=None, allocate_second_order: bool = False,
                  alpha_exact_tokens: int = 256, alpha_span_max_tokens: int = 64, beta_novelty: bool = False,
-                 beta_adaptive_merge: bool = False, importance_pooling: bool = False, **unused) -> None:
+                 beta_adaptive_merge: bool = False, importance_pooling: bool = False, kv_shard_group=None,
+                 **unused) -> None:
         super().__init__()
         batch, groups, max_seq, k_dim = k_shape
         v_dim = v_shape[3]
@@ -110,7 +111,13 @@ class LogStructuredKVCache(nn.Module):
         self.rope_n_elem = int(rope_n_elem)
         self.allocate_second_order = False
         esize = torch.empty((), dtype=dtype).element_size()
-        self.B_prime, self.L_alloc = ladder_geometry(max_seq, k_dim, v_dim, groups, B, self.K_max,
+        # A KV-head shard sizes its ladder like the whole cache (the exact pool's budget term
+        # is not proportional to the group count).
+        geo_groups = groups
+        if kv_shard_group is not None:
+            import torch.distributed as dist
+            geo_groups = groups * dist.get_world_size(kv_shard_group)
+        self.B_prime, self.L_alloc = ladder_geometry(max_seq, k_dim, v_dim, geo_groups, B, self.K_max,
                                                      self.alpha_exact_tokens, esize)
         self.max_levels = self.L_alloc
         self.B = self.B_prime
@@ -185,6 +192,10 @@ class LogStructuredKVCache(nn.Module):
             raise ValueError("cache geometry is outside the supported range of the flush kernels")
         self._workspace = torch.zeros(nbytes, dtype=torch.uint8, device=device)
         self._state = None
+        # KV-head sharding: this cache holds one rank's block of groups of a longer group axis
+        # (logkv_b200.sharding); flushes exchange span parts over `kv_shard_group`.
+        self.kv_shard_group = kv_shard_group
+        self._span_gather = None
         self._ladder_epoch = 0       # bumped whenever a flush or reset rewrites the ladder / exact pool
         self.profile_events = None   # set to a list of LOGKV_FLUSH_STAGES+1 torch.cuda.Event to time stages
 
@@ -209,11 +220,32 @@ class LogStructuredKVCache(nn.Module):
         args = (ctypes.byref(self._layout), ctypes.byref(state), int(take), int(self.recent_count),
                 ctypes.c_void_p(self._workspace.data_ptr()), self._workspace.numel(),
                 ctypes.c_void_p(_lib.stream_ptr(self.level_k.device)))
+        if self.kv_shard_group is not None:
+            self._sharded_flush(args, int(take))
+            return
         if self.profile_events is None:
             _lib.check(_lib.lib().logkv_flush(*args), "logkv_flush")
             return
         events = (ctypes.c_void_p * len(self.profile_events))(*[e.cuda_event for e in self.profile_events])
         _lib.check(_lib.lib().logkv_flush_profiled(*args, events, len(self.profile_events)), "logkv_flush_profiled")
+
+    def _sharded_flush(self, args, take: int) -> None:
+        """Scores of this rank's groups, all-gather of every rank's span parts, then the commit."""
+        import torch.distributed as dist
+        from .sharding import gather_span_parts
+        lib = _lib.lib()
+        _lib.check(lib.logkv_flush_scores(*args), "logkv_flush_scores")
+        ptr, count = ctypes.POINTER(ctypes.c_float)(), ctypes.c_size_t()
+        _lib.check(lib.logkv_flush_partials(ctypes.byref(self._layout), take, ctypes.c_void_p(self._workspace.data_ptr()),
+                                            ctypes.byref(ptr), ctypes.byref(count)), "logkv_flush_partials")
+        offset = ctypes.cast(ptr, ctypes.c_void_p).value - self._workspace.data_ptr()
+        local = self._workspace[offset:offset + 4 * count.value].view(torch.float32)
+        world = dist.get_world_size(self.kv_shard_group)
+        if self._span_gather is None or self._span_gather.numel() != world * count.value:
+            self._span_gather = torch.empty(world * count.value, dtype=torch.float32, device=self._workspace.device)
+        gather_span_parts(local, self.kv_shard_group, out=self._span_gather)
+        _lib.check(lib.logkv_flush_commit(*args[:6], ctypes.c_void_p(self._span_gather.data_ptr()), world, args[6]),
+                   "logkv_flush_commit")
 
     def read_counters(self) -> dict:
         """Row counters accumulated by every flush of this cache (synchronizes)."""

@@ -157,6 +157,7 @@ static Geo make_geo(const logkv_layout_t& L, int F, int recent_count) {
   g.eta = L.eta;
   g.g0 = L.g0;
   g.lam = L.lam;
+  g.shard_ranks = 1;
   return g;
 }
 
@@ -220,8 +221,14 @@ static int validate(const logkv_layout_t* L, int F) {
   return LOGKV_OK;
 }
 
+// Phases: kPhaseScores = snapshot, span cut, span scores (the group parts of this rank);
+// kPhaseCommit = everything from the bounded greedy on.  A KV-head-sharded flush
+// all-gathers the group parts between the two.
+constexpr int kPhaseScores = 1, kPhaseCommit = 2, kPhaseAll = 3;
+
 template <typename T>
-static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st, cudaEvent_t* ev) {
+static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st, cudaEvent_t* ev,
+                        int phases = kPhaseAll) {
   int stage = 0;
   auto mark = [&]() {
     if (ev) cudaEventRecord(ev[stage], st);
@@ -229,6 +236,7 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   };
   const int sm_count = 148;
   const int per_bg = std::max(1, std::min(64, (g.P * g.D + 255) / 256));
+  if (phases & kPhaseScores) {
   mark();
   snapshot_kernel<T><<<dim3(per_bg, g.G, g.B), 256, 0, st>>>(g, s, w);
   mark();
@@ -241,6 +249,8 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
     cudaFuncSetAttribute(alpha_score_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)score_smem);
   const int score_blocks = std::max(1, std::min(g.NC, 8 * sm_count / std::max(1, g.B * g.G) + 1));
   alpha_score_kernel<T><<<dim3(score_blocks, g.G, g.B), 256, score_smem, st>>>(g, s, w);
+  }
+  if (!(phases & kPhaseCommit)) return (int)cudaGetLastError();
   mark();
   const size_t choose_smem = (size_t)g.NC * (8 + 4 * 4 + 2);
   if (choose_smem > 48 * 1024)
@@ -296,21 +306,25 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
 }
 
 static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
-                     int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream, cudaEvent_t* ev) {
+                     int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream, cudaEvent_t* ev,
+                     int phases = kPhaseAll, const float* gpart_all = nullptr, int ranks = 1) {
   const int v = validate(layout, flush_tokens);
   if (v != LOGKV_OK) return v;
   if (!state || !workspace) return LOGKV_E_POINTER;
   if (recent_count < flush_tokens || recent_count > layout->recent_capacity) return LOGKV_E_SHAPE;
   const size_t esize = layout->dtype == LOGKV_DTYPE_BF16 ? 2 : 4;
-  const Geo g = make_geo(*layout, flush_tokens, recent_count);
+  if (ranks < 1 || (ranks > 1 && !gpart_all)) return LOGKV_E_POINTER;
+  Geo g = make_geo(*layout, flush_tokens, recent_count);
+  g.shard_ranks = ranks;
   Work w{};
   const size_t need = carve(g, esize, static_cast<char*>(workspace), &w);
   if (workspace_bytes < need) return LOGKV_E_WORKSPACE;
   if (cascade_smem(g, esize) > 227 * 1024 || (size_t)g.sort_cap * 8 + (size_t)g.NW * 4 > 227 * 1024)
     return LOGKV_E_SMEM;
+  w.gpart_all = gpart_all;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (layout->dtype == LOGKV_DTYPE_BF16) return launch_flush<__nv_bfloat16>(g, *state, w, st, ev);
-  return launch_flush<float>(g, *state, w, st, ev);
+  if (layout->dtype == LOGKV_DTYPE_BF16) return launch_flush<__nv_bfloat16>(g, *state, w, st, ev, phases);
+  return launch_flush<float>(g, *state, w, st, ev, phases);
 }
 
 }  // namespace logkv
@@ -327,6 +341,32 @@ extern "C" size_t logkv_flush_workspace_bytes(const logkv_layout_t* layout, int3
 extern "C" int logkv_flush(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
                            int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream) {
   return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream, nullptr);
+}
+
+extern "C" int logkv_flush_scores(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                  int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream) {
+  return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream, nullptr,
+                   kPhaseScores);
+}
+
+extern "C" int logkv_flush_commit(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                  int32_t recent_count, void* workspace, size_t workspace_bytes,
+                                  const float* partials_all, int32_t ranks, void* stream) {
+  return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream, nullptr,
+                   kPhaseCommit, partials_all, ranks);
+}
+
+extern "C" int logkv_flush_partials(const logkv_layout_t* layout, int32_t flush_tokens, void* workspace,
+                                    float** partials, size_t* count) {
+  const int v = validate(layout, flush_tokens);
+  if (v != LOGKV_OK) return v;
+  if (!workspace || !partials || !count) return LOGKV_E_POINTER;
+  const Geo g = make_geo(*layout, flush_tokens, layout->recent_capacity);
+  Work w{};
+  carve(g, layout->dtype == LOGKV_DTYPE_BF16 ? 2 : 4, static_cast<char*>(workspace), &w);
+  *partials = w.gpart;
+  *count = (size_t)g.B * g.NC * g.G * 2;
+  return LOGKV_OK;
 }
 
 extern "C" int logkv_flush_profiled(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,

@@ -342,17 +342,23 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
     const size_t c = (size_t)b * NC + i;
     flags[i] = w.cand_flags[c];
     size[i] = w.cand_n0[c] + w.cand_n1[c];
-    const float* gp = w.gpart + (size_t)c * g.G * 2;
+    // Group parts in global group order: this rank's own, or all ranks' gathered parts.
+    const int GT = g.G * g.shard_ranks;
+    auto part = [&](int grp, int k) -> float {
+      if (!w.gpart_all) return w.gpart[((size_t)c * g.G + grp) * 2 + k];
+      const int r = grp / g.G, gl = grp % g.G;
+      return w.gpart_all[((((size_t)r * g.B + b) * NC + i) * g.G + gl) * 2 + k];
+    };
     float sf;
     if (!g.beta) {
       float a = 0.f, v = 0.f;
-      for (int grp = 0; grp < g.G; ++grp) a = fadd(a, gp[grp * 2]);
-      for (int grp = 0; grp < g.G; ++grp) v = fadd(v, gp[grp * 2 + 1]);
-      sf = fadd(fdiv(a, (float)g.G), fdiv(v, (float)g.G));
+      for (int grp = 0; grp < GT; ++grp) a = fadd(a, part(grp, 0));
+      for (int grp = 0; grp < GT; ++grp) v = fadd(v, part(grp, 1));
+      sf = fadd(fdiv(a, (float)GT), fdiv(v, (float)GT));
     } else {
       float v1 = -INFINITY, v2 = -INFINITY;
-      for (int grp = 0; grp < g.G; ++grp) {
-        const float xg = gp[grp * 2];
+      for (int grp = 0; grp < GT; ++grp) {
+        const float xg = part(grp, 0);
         if (xg > v1) {
           v2 = v1;
           v1 = xg;
@@ -360,7 +366,7 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
           v2 = xg;
         }
       }
-      const int top = g.G < 2 ? g.G : 2;
+      const int top = GT < 2 ? GT : 2;
       float acc = fadd(0.f, v1);
       if (top == 2) acc = fadd(acc, v2);
       sf = fdiv(acc, (float)top);

@@ -19,6 +19,7 @@ struct Geo {
   int S;                  // ladder scratch rows per buffer per (b, g)
   int sort_cap;           // power of two >= L * Bs + NW (delayed re-insert sort)
   int seed_staged;        // seeding CTAs keep their token rows in shared memory (set per dtype at launch)
+  int shard_ranks;        // KV-head sharding: ranks holding G groups each (1 = unsharded)
   float eta, g0, lam;
 };
 
@@ -54,6 +55,7 @@ struct Work {
   int32_t* n_cand;         // [B]
   float* scores;           // [B,NC]
   float* gpart;            // [B,NC,G,2] per-group parts (Alpha: R_K, R_V; Beta: group score)
+  const float* gpart_all;  // sharded: [ranks,B,NC,G,2] every rank's gpart in rank order, else null
   int32_t* keep_idx;       // [B,P]  token indices kept in the pool, candidate order
   int32_t* nkeep;          // [B]
   int32_t* arch_idx;       // [B,NW] archived token indices, position order
