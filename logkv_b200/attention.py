@@ -70,13 +70,53 @@ class _ReadState:
         key = (heads, q_tokens)
         ws = self.workspaces.get(key)
         if ws is None:
-            n = _lib.lib().logkv_attention_workspace_bytes(ctypes.byref(cache._layout), heads, q_tokens,
+            n = _lib.lib().logkv_attention_workspace_bytes(ctypes.byref(_structs(cache)[0]), heads, q_tokens,
                                                            self.capacity)
             if not n:
                 raise ValueError(f"attention shape outside the supported range (heads={heads}, tokens={q_tokens})")
             ws = torch.zeros(n, dtype=torch.uint8, device=cache.level_k.device)
             self.workspaces[key] = ws
         return ws
+
+
+class _ForeignCache:
+    """Layout and state structs for a cache object that only has the reference's buffers.
+
+    The reference's own ``LogStructuredKVCache`` on a CUDA device registers the same
+    buffer names, shapes and dtypes (log_kv_cache.py:907-1122); the read-side kernels
+    use only those.  Fields the read side never touches point at one small dummy buffer.
+    """
+
+    def __init__(self, cache):
+        dev = cache.level_k.device
+        self.dummy = torch.zeros(64, dtype=torch.int64, device=dev)
+        self.alpha_count = torch.zeros(1, dtype=torch.int32, device=dev)
+        B, G = cache.batch_size, cache.n_groups
+        self.layout = _lib.Layout(B, G, cache.k_dim, cache.K_max, cache.L_alloc, cache.B_prime,
+                                  cache.recent_k.size(2), cache.alpha_exact_tokens, 1, 0,
+                                  _lib.DTYPE_CODES[cache.level_k.dtype], 1.0, 1.0, 1.0)
+
+    def state(self, cache) -> _lib.State:
+        self.alpha_count.fill_(int(cache.alpha_count))
+        d = self.dummy.data_ptr()
+        views = dict(level_k=cache.level_k, level_v=cache.level_v, level_w=cache.level_w,
+                     level_sum_wp=cache.level_sum_wp, level_count=cache.level_count, recent_k=cache.recent_k,
+                     recent_v=cache.recent_v, alpha_k_raw=cache.alpha_k_raw, alpha_v=cache.alpha_v,
+                     alpha_pos=cache.alpha_pos, alpha_valid=cache.alpha_valid, alpha_count=self.alpha_count)
+        ptrs = {name: d for name in _lib.STATE_FIELDS}
+        ptrs.update({name: _lib.ptr(t) for name, t in views.items()})
+        return _lib.State(**ptrs)
+
+
+def _structs(cache):
+    """(layout, state) of a logkv_b200 cache, or of any cache with the reference's buffers."""
+    if hasattr(cache, "_state_struct"):
+        return cache._layout, cache._state_struct()
+    fc = getattr(cache, "_b200_foreign", None)
+    if fc is None:
+        fc = _ForeignCache(cache)
+        cache._b200_foreign = fc
+    return fc.layout, fc.state(cache)
 
 
 def _read_state(cache) -> _ReadState:
@@ -105,9 +145,9 @@ def _stream(cache) -> ctypes.c_void_p:
 
 def _run_plan(cache, full: bool) -> _ReadState:
     rs = _read_state(cache)
-    state = cache._state_struct()
+    layout, state = _structs(cache)
     plan = rs.plan_struct(full)
-    _lib.check(_lib.lib().logkv_attention_plan(ctypes.byref(cache._layout), ctypes.byref(state), ctypes.byref(plan),
+    _lib.check(_lib.lib().logkv_attention_plan(ctypes.byref(layout), ctypes.byref(state), ctypes.byref(plan),
                                                _stream(cache)), "logkv_attention_plan")
     return rs
 
@@ -115,15 +155,16 @@ def _run_plan(cache, full: bool) -> _ReadState:
 def refresh_prefix(cache) -> _ReadState:
     """Plan and pack the frozen prefix when a flush has changed the ladder since the last pack."""
     rs = _read_state(cache)
-    if rs.epoch == cache._ladder_epoch:
+    epoch = getattr(cache, "_ladder_epoch", None)   # None: a foreign cache, repack every call
+    if epoch is not None and rs.epoch == epoch:
         return rs
     _run_plan(cache, full=False)
-    state = cache._state_struct()
+    layout, state = _structs(cache)
     plan, rope, pre = rs.plan_struct(False), _rope(cache), rs.prefix_struct()
-    _lib.check(_lib.lib().logkv_pack_prefix(ctypes.byref(cache._layout), ctypes.byref(state), ctypes.byref(plan),
+    _lib.check(_lib.lib().logkv_pack_prefix(ctypes.byref(layout), ctypes.byref(state), ctypes.byref(plan),
                                             ctypes.byref(rope), ctypes.byref(pre), rs.status.data_ptr(),
                                             _stream(cache)), "logkv_pack_prefix")
-    rs.epoch = cache._ladder_epoch
+    rs.epoch = epoch if epoch is not None else -1
     return rs
 
 
@@ -177,10 +218,10 @@ def pack_mid_kv(cache, plan_, k, v, dim, *, backend=None, buffers=None, skip_poo
         if not ka.is_contiguous():
             raise ValueError("reusable pack buffers must be contiguous in their first `length` rows")
     kc, vc = k.contiguous(), v.contiguous()
-    state = cache._state_struct()
+    layout, state = _structs(cache)
     plan_s, rope = rs.plan_struct(True), _rope(cache)
     _lib.check(_lib.lib().logkv_pack_mid(
-        ctypes.byref(cache._layout), ctypes.byref(state), ctypes.byref(plan_s), ctypes.byref(rope), width, exact,
+        ctypes.byref(layout), ctypes.byref(state), ctypes.byref(plan_s), ctypes.byref(rope), width, exact,
         recent, kc.data_ptr(), vc.data_ptr(), T, ka.data_ptr(), va.data_ptr(), dim, int(bool(skip_pooled)),
         int(recent_start), rs.status.data_ptr(), _stream(cache)), "logkv_pack_mid")
     return ka, va
@@ -228,7 +269,7 @@ def log_kv_chunk_attention(cache, q_b, k_b, v_b, scale, second_order_scale=1.0, 
     q, k, v = q_b.contiguous(), k_b.contiguous(), v_b.contiguous()
     if out is None:
         out = torch.empty(B, H, T, cache.v_dim, dtype=q.dtype, device=q.device)
-    state = cache._state_struct()
+    layout, state = _structs(cache)
     pre = rs.prefix_struct()
     qx = query_extra(scale, q.dtype)
     t0 = 0
@@ -239,7 +280,7 @@ def log_kv_chunk_attention(cache, q_b, k_b, v_b, scale, second_order_scale=1.0, 
         ws = rs.workspace(cache, H, n)
         args = _lib.AttentionArgs(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), H, T, t0, n,
                                   int(cache.recent_count), int(bool(causal_tail)), float(scale), qx)
-        _lib.check(_lib.lib().logkv_attention(ctypes.byref(cache._layout), ctypes.byref(state), ctypes.byref(pre),
+        _lib.check(_lib.lib().logkv_attention(ctypes.byref(layout), ctypes.byref(state), ctypes.byref(pre),
                                               ctypes.byref(args), ws.data_ptr(), ws.numel(), _stream(cache)),
                    "logkv_attention")
         t0 += n

@@ -1,9 +1,10 @@
 """Build the in-tree C-ABI library ``logkv_b200/liblogkv_b200.so`` for sm_100a with nvcc.
 
-Two translation units with different numerics:
+Three translation units with different numerics:
   flush.cu      -fmad=false: every float expression of the flush is rounded
                  exactly as written (bit-exact with the reference's CPU path);
-  attention.cu  default contraction (FMA) for the attention math.
+  attention.cu  default contraction (FMA) for the attention math;
+  plugin.cu     -fmad=false: the operator-level plugin functions, same contract as flush.cu.
 Run ``python -m logkv_b200.build`` (or ``__graft_entry__.build()``).
 """
 from __future__ import annotations
@@ -24,6 +25,7 @@ COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler",
 UNITS = [
     ("flush.cu", ["-fmad=false"]),
     ("attention.cu", []),
+    ("plugin.cu", ["-fmad=false"]),
 ]
 
 
