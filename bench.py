@@ -521,7 +521,7 @@ def bench_prefill(args, rank, world, local_rank):
             peak = float(json.load(fh)["bf16_tflops"])
     tflops = flops / (us * 1e-6) / 1e12
     return {"metric": "chunk attention us per 2048-token chunk/layer", "value": round(us, 2), "unit": "us",
-            "roofline": {"bound": "tensor", "kernel": "chunk_attn_mma_kernel", "achieved": round(tflops, 1),
+            "roofline": {"bound": "tensor", "kernel": "chunk_attn_tc_kernel", "achieved": round(tflops, 1),
                          "peak": peak, "unit": "TFLOP/s", "frac": round(tflops / peak, 4), "traffic": None,
                          "flops_per_launch": flops},
             "config": {"heads": H, "groups": G, "head_dim": D, "chunk": T, "prefix_slots": Lp, "recent": R,

@@ -16,6 +16,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "tcgen05.cuh"
 #include "../../include/logkv_attention.h"
 
 namespace logkv {
@@ -1198,6 +1199,287 @@ __global__ void __launch_bounds__(kPfWarps * 32) chunk_attn_mma_kernel(AttnGeo a
   }
 }
 
+// ---------------------------------------------------------------- K6: chunk attention on tcgen05 / TMEM
+// One CTA = 128 query rows of a lane (rf heads x 128/rf tokens), the M of
+// tcgen05.mma.cta_group::1.kind::f16 (bf16 in, f32 accumulate).  Q and the 64-slot K/V tiles
+// live in shared memory in the 128-byte-swizzled canonical layouts (written by cp.async with
+// chunk ^ (row & 7)); S (128 x 64) and O (128 x D) accumulate in tensor memory, and P (bf16)
+// is written back over S's first 32 columns (row m in lane m, slot pairs packed per column)
+// as the A operand of the PV MMA.  Per tile: one thread issues S = Q K^T (K-major A and B);
+// four warps (thread = row = TMEM lane) read S, add the mass term, mask, run the online
+// softmax (lazy rescaling: the running max moves only when a tile exceeds it by more than
+// 2^8) and store P; one thread issues O += P V (V as an MN-major B operand).  K/V tiles are
+// double-buffered with cp.async.  Every mbarrier wait is bounded; on expiry the CTA records
+// kStatusTimeout in the status word, stops, frees its tensor memory and returns.
+constexpr int kTcWarps = 8;
+constexpr int kTcRows = 128;
+constexpr int kTcTS = 64;
+constexpr uint32_t kTcCols = 256;          // tensor-memory columns: S/P [0, 64), O [64, 64 + D)
+constexpr int32_t kStatusTimeout = 1 << 17;
+constexpr long long kTcWaitBudget = 4000000000LL;   // clock cycles (about 2 s)
+
+template <int D>
+struct TcShape {
+  static constexpr int KB = D / 64;                      // 128-byte column blocks of a row
+  static constexpr int Q_BYTES = KB * kTcRows * 128;
+  static constexpr int KV_BYTES = KB * kTcTS * 128;      // one K or V tile
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;                  // 2 stages
+  static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;             // 2 stages
+  static constexpr int OFF_M = OFF_V + 2 * KV_BYTES;             // 2 x 64 floats: qx * mass * scale * log2(e)
+  static constexpr int BYTES = OFF_M + 2 * kTcTS * 4;
+  static constexpr size_t smem = (size_t)BYTES + 1024;           // + alignment slack
+  static_assert(D == 64 || D == 128, "tcgen05 chunk attention handles head dims 64 and 128");
+};
+
+template <int D>
+__global__ void __launch_bounds__(kTcWarps * 32) chunk_attn_tc_kernel(AttnGeo a, logkv_prefix_t pre,
+                                                                     const __nv_bfloat16* rk,
+                                                                     const __nv_bfloat16* rv,
+                                                                     const __nv_bfloat16* kn,
+                                                                     const __nv_bfloat16* vn,
+                                                                     const __nv_bfloat16* q, __nv_bfloat16* out,
+                                                                     int32_t* status) {
+  using S = TcShape<D>;
+  constexpr int CPR = D / 8, TS = kTcTS;
+  extern __shared__ uint4 smem4[];
+  __shared__ uint64_t bar_s, bar_pv;
+  __shared__ uint32_t sh_tmem;
+  __shared__ int sh_abort;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  // 1024-byte aligned base for the swizzled operand tiles.
+  unsigned char* raw = reinterpret_cast<unsigned char*>(smem4);
+  unsigned char* base = raw + ((1024u - (tc::smem_u32(raw) & 1023u)) & 1023u);
+  const uint32_t base_s = tc::smem_u32(base);
+  const int g = blockIdx.y, b = blockIdx.z, ln = b * a.G + g;
+  const int QT = kTcRows / a.rf;
+  const int tq0 = a.qoff + blockIdx.x * QT;
+  const int tlast = min(a.qoff + a.TQ, tq0 + QT) - 1;
+  const __nv_bfloat16* PK = static_cast<const __nv_bfloat16*>(pre.k);
+  const __nv_bfloat16* PV = static_cast<const __nv_bfloat16*>(pre.v);
+  const int Lp = pre.length[ln], R = a.rcount;
+  const int Tvis = a.causal ? min(a.T, tlast + 1) : a.T;
+  const int up = (Lp + TS - 1) / TS, ur = (R + TS - 1) / TS, uc = (Tvis + TS - 1) / TS;
+  const int U = up + ur + uc;
+  const float mscale = a.qx * a.scale_log2;
+
+  if (tid == 0) {
+    tc::mbar_init(&bar_s, 1);
+    tc::mbar_init(&bar_pv, 1);
+    tc::mbar_fence_init();
+    sh_abort = 0;
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(&sh_tmem, kTcCols);
+    tc::tmem_relinquish();
+  }
+  // Q tile: row m = head (m / QT) x token (tq0 + m % QT); rows past the query range are zero.
+  for (int flat = tid; flat < kTcRows * CPR; flat += kTcWarps * 32) {
+    const int m = flat / CPR, c = flat % CPR;
+    const int t = tq0 + m % QT, h = g * a.rf + m / QT;
+    unsigned char* dst = base + S::OFF_Q + (c >> 3) * (kTcRows * 128) + m * 128 + (((c & 7) ^ (m & 7)) << 4);
+    if (t < a.qoff + a.TQ) cp_async16(dst, q + (((size_t)b * a.H + h) * a.T + t) * D + c * 8);
+    else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+  }
+  auto unit_info = [&](int u, const __nv_bfloat16*& kb, const __nv_bfloat16*& vb, const float*& mb, int& rows,
+                       int& cls, int& first) {
+    if (u < up) {
+      first = u * TS;
+      rows = min(TS, Lp - first);
+      const size_t r = (size_t)ln * pre.capacity + first;
+      kb = PK + r * D;
+      vb = PV + r * D;
+      mb = pre.mass + r;
+      cls = 0;
+    } else if (u < up + ur) {
+      first = (u - up) * TS;
+      rows = min(TS, R - first);
+      const size_t r = (size_t)ln * a.rcap + first;
+      kb = rk + r * D;
+      vb = rv + r * D;
+      mb = nullptr;
+      cls = 1;
+    } else {
+      first = (u - up - ur) * TS;
+      rows = min(TS, Tvis - first);
+      const size_t r = (size_t)ln * a.T + first;
+      kb = kn + r * D;
+      vb = vn + r * D;
+      mb = nullptr;
+      cls = 2;
+    }
+  };
+  auto issue = [&](int u, int stage) {
+    if (u < U) {
+      const __nv_bfloat16 *kb, *vb;
+      const float* mb;
+      int rows, cls, first;
+      unit_info(u, kb, vb, mb, rows, cls, first);
+      unsigned char* sk = base + S::OFF_K + stage * S::KV_BYTES;
+      unsigned char* sv = base + S::OFF_V + stage * S::KV_BYTES;
+      float* sm = reinterpret_cast<float*>(base + S::OFF_M) + stage * TS;
+      for (int flat = tid; flat < TS * CPR; flat += kTcWarps * 32) {
+        const int r = flat / CPR, c = flat % CPR;
+        const int off = (c >> 3) * (TS * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+        if (r < rows) {
+          cp_async16(sk + off, kb + (size_t)flat * 8);
+          cp_async16(sv + off, vb + (size_t)flat * 8);
+        } else {
+          *reinterpret_cast<uint4*>(sk + off) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(sv + off) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      if (tid < TS) sm[tid] = (cls == 0 && tid < rows) ? mscale * mb[tid] : 0.f;
+    }
+    cp_async_commit();
+  };
+  issue(0, 0);
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = sh_tmem;
+  const uint32_t t_s = tmem, t_o = tmem + 64;
+  const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+  constexpr uint32_t idesc_s = tc::f16_idesc(kTcRows, TS, 0, 0);
+  constexpr uint32_t idesc_o = tc::f16_idesc(kTcRows, D, 0, 1);
+  // Softmax state of row `tid` (threads 0..127).
+  const bool srow = tid < kTcRows;
+  const int row_t = tq0 + (tid % QT);
+  float m_used = -INFINITY, l = 0.f;
+  uint32_t ph_s = 0, ph_pv = 0;
+  for (int u = 0; u < U; ++u) {
+    const int stage = u & 1;
+    issue(u + 1, stage ^ 1);
+    cp_async_wait<1>();
+    tc::fence_proxy_async();
+    __syncthreads();
+    if (tid == 0) {
+      tc::fence_after();
+      const uint32_t qa = base_s + S::OFF_Q, kbs = base_s + S::OFF_K + stage * S::KV_BYTES;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const uint64_t da = tc::sw128_desc(qa + (ks >> 2) * (kTcRows * 128) + (ks & 3) * 32, 16, 1024);
+        const uint64_t db = tc::sw128_desc(kbs + (ks >> 2) * (TS * 128) + (ks & 3) * 32, 16, 1024);
+        tc::umma_f16(t_s, da, db, idesc_s, ks > 0 ? 1u : 0u);
+      }
+      tc::umma_commit(&bar_s);
+    }
+    bool live = true;   // warp-uniform: tcgen05.ld/st are warp-collective
+    if (srow) {
+      live = __all_sync(0xffffffffu, tc::mbar_wait(&bar_s, ph_s, kTcWaitBudget));
+      if (!live && (tid & 31) == 0) sh_abort = 1;
+    }
+    ph_s ^= 1;
+    if (srow && live) {
+      tc::fence_after();
+      const __nv_bfloat16 *kb_, *vb_;
+      const float* mb_;
+      int rows, cls, first;
+      unit_info(u, kb_, vb_, mb_, rows, cls, first);
+      const float* sm = reinterpret_cast<const float*>(base + S::OFF_M) + stage * TS;
+      float sv[TS];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t r32[32];
+        tc::tmem_ld32(t_s + lane_off + half * 32, r32);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sv[half * 32 + j] = __uint_as_float(r32[j]);
+      }
+      float mt = -INFINITY;
+      const bool full = rows == TS && (cls != 2 || !a.causal || first + TS - 1 <= row_t);
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < TS; ++j) {
+          sv[j] = fmaf(sv[j], a.scale_log2, sm[j]);
+          mt = fmaxf(mt, sv[j]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < TS; ++j) {
+          const bool vis = j < rows && (cls != 2 || !a.causal || first + j <= row_t);
+          sv[j] = vis ? fmaf(sv[j], a.scale_log2, sm[j]) : -INFINITY;
+          mt = fmaxf(mt, sv[j]);
+        }
+      }
+      float alpha = 1.f;
+      if (mt > m_used + 8.f || (m_used == -INFINITY && mt != -INFINITY)) {
+        alpha = m_used == -INFINITY ? 0.f : tc::ex2(m_used - mt);
+        m_used = mt;
+      }
+      const float msub = m_used == -INFINITY ? 0.f : m_used;
+      float ps = 0.f;
+      uint32_t pk[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float p0 = tc::ex2(sv[2 * j] - msub), p1 = tc::ex2(sv[2 * j + 1] - msub);
+        ps += p0 + p1;
+        pk[j] = pack_bf16x2(p0, p1);
+      }
+      l = l * alpha + ps;
+      if (u > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < D; c0 += 32) {
+          uint32_t r32[32];
+          tc::tmem_ld32(t_o + lane_off + c0, r32);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r32[j] = __float_as_uint(__uint_as_float(r32[j]) * alpha);
+          tc::tmem_st32(t_o + lane_off + c0, r32);
+        }
+      }
+      tc::tmem_st32(t_s + lane_off, pk);   // P over S's first 32 columns
+    }
+    tc::fence_before();
+    __syncthreads();
+    if (sh_abort) break;
+    if (tid == 0) {
+      tc::fence_after();
+      const uint32_t vbs = base_s + S::OFF_V + stage * S::KV_BYTES;
+#pragma unroll
+      for (int ks = 0; ks < TS / 16; ++ks) {
+        const uint64_t db = tc::sw128_desc(vbs + ks * 16 * 128, TS * 128, 1024);
+        tc::umma_f16_ts(t_o, t_s + ks * 8, db, idesc_o, (u > 0 || ks > 0) ? 1u : 0u);
+      }
+      tc::umma_commit(&bar_pv);
+    }
+    if (!__all_sync(0xffffffffu, tc::mbar_wait(&bar_pv, ph_pv, kTcWaitBudget)) && (tid & 31) == 0) sh_abort = 1;
+    ph_pv ^= 1;
+    __syncthreads();
+    if (sh_abort) break;
+  }
+  cp_async_wait<0>();
+  if (sh_abort) {
+    if (tid == 0 && status) atomicOr(status, kStatusTimeout);
+  } else if (srow && U > 0) {
+    tc::fence_after();
+    const int hh = tid / QT;
+    const bool ok = row_t < a.qoff + a.TQ;
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    __nv_bfloat16* orow = out + (((size_t)b * a.H + g * a.rf + hh) * a.T + row_t) * D;
+#pragma unroll 1
+    for (int c0 = 0; c0 < D; c0 += 32) {
+      uint32_t r32[32];
+      tc::tmem_ld32(t_o + lane_off + c0, r32);
+      if (ok) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(r32[j]) * inv, __uint_as_float(r32[j + 1]) * inv);
+          w.y = pack_bf16x2(__uint_as_float(r32[j + 2]) * inv, __uint_as_float(r32[j + 3]) * inv);
+          w.z = pack_bf16x2(__uint_as_float(r32[j + 4]) * inv, __uint_as_float(r32[j + 5]) * inv);
+          w.w = pack_bf16x2(__uint_as_float(r32[j + 6]) * inv, __uint_as_float(r32[j + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + c0 + j) = w;
+        }
+      }
+    }
+  }
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::fence_after();
+    tc::tmem_dealloc(tmem, kTcCols);
+  }
+}
+
 // ---------------------------------------------------------------- host side
 static bool dtype_ok(int d) { return d == LOGKV_DTYPE_F32 || d == LOGKV_DTYPE_BF16; }
 static size_t esize_of(int d) { return d == LOGKV_DTYPE_F32 ? 4 : 2; }
@@ -1346,13 +1628,28 @@ static int launch_chunk_d(const AttnGeo& ag, const logkv_prefix_t& pre, const lo
   return launch_status();
 }
 
+template <int D>
+static int launch_chunk_tc(const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
+                           const logkv_attention_args_t& x, int32_t* status, cudaStream_t st) {
+  using S = TcShape<D>;
+  auto kern = chunk_attn_tc_kernel<D>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::smem);
+  using B16 = __nv_bfloat16;
+  kern<<<dim3((ag.TQ + kTcRows / ag.rf - 1) / (kTcRows / ag.rf), ag.G, ag.B), kTcWarps * 32, S::smem, st>>>(
+      ag, pre, static_cast<const B16*>(s.recent_k), static_cast<const B16*>(s.recent_v),
+      static_cast<const B16*>(x.k_new), static_cast<const B16*>(x.v_new), static_cast<const B16*>(x.q),
+      static_cast<B16*>(x.out), status);
+  return launch_status();
+}
+
+// Head dims 64 and 128 run on tcgen05 (tensor memory accumulators); 16 and 32 on mma.sync.
 static int launch_chunk(int D, const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
-                        const logkv_attention_args_t& x, cudaStream_t st) {
+                        const logkv_attention_args_t& x, int32_t* status, cudaStream_t st) {
   switch (D) {
     case 16: return launch_chunk_d<16>(ag, pre, s, x, st);
     case 32: return launch_chunk_d<32>(ag, pre, s, x, st);
-    case 64: return launch_chunk_d<64>(ag, pre, s, x, st);
-    case 128: return launch_chunk_d<128>(ag, pre, s, x, st);
+    case 64: return launch_chunk_tc<64>(ag, pre, s, x, status, st);
+    case 128: return launch_chunk_tc<128>(ag, pre, s, x, status, st);
     default: return LOGKV_E_SHAPE;
   }
 }
@@ -1485,7 +1782,8 @@ LOGKV_API int logkv_attention(const logkv_layout_t* layout, const logkv_state_t*
   ag.scale_log2 = args->scale * 1.4426950408889634f;
   ag.qx = args->qx;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (use_chunk_kernel(*layout, H, TQ)) return launch_chunk(layout->dim, ag, *prefix, *state, *args, st);
+  if (use_chunk_kernel(*layout, H, TQ))
+    return launch_chunk(layout->dim, ag, *prefix, *state, *args, static_cast<int32_t*>(workspace), st);
   return launch_attn(layout->dtype, layout->dim, nq, ag, *prefix, *state, *args, part, ticket, st);
 }
 
