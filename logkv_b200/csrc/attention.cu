@@ -1201,35 +1201,37 @@ __global__ void __launch_bounds__(kPfWarps * 32) chunk_attn_mma_kernel(AttnGeo a
 
 // ---------------------------------------------------------------- K6: chunk attention on tcgen05 / TMEM
 // One CTA = 128 query rows of a lane (rf heads x 128/rf tokens), the M of
-// tcgen05.mma.cta_group::1.kind::f16 (bf16 in, f32 accumulate).  Q and the 64-slot K/V tiles
-// live in shared memory in the 128-byte-swizzled canonical layouts (written by cp.async with
-// chunk ^ (row & 7)); S (128 x 64) and O (128 x D) accumulate in tensor memory, and P (bf16)
-// is written back over S's first 32 columns (row m in lane m, slot pairs packed per column)
-// as the A operand of the PV MMA.  Per tile: one thread issues S = Q K^T (K-major A and B);
-// four warps (thread = row = TMEM lane) read S, add the mass term, mask, run the online
-// softmax (lazy rescaling: the running max moves only when a tile exceeds it by more than
-// 2^8) and store P; one thread issues O += P V (V as an MN-major B operand).  K/V tiles are
-// double-buffered with cp.async.  Every mbarrier wait is bounded; on expiry the CTA records
-// kStatusTimeout in the status word, stops, frees its tensor memory and returns.
+// tcgen05.mma.cta_group::1.kind::f16 (bf16 in, f32 accumulate), with warp roles:
+//   warps 0-3  softmax: thread = query row = TMEM lane; read S(u), add the mass term, mask,
+//              online softmax (lazy rescaling: the running max moves only when a tile exceeds
+//              it by more than 2^8), write P(u) as bf16 over S(u)'s first 32 columns;
+//   warp 4     one thread issues S(u+1) = Q K^T while the softmax of tile u runs, then
+//              O += P(u) V (P from tensor memory, V an MN-major shared-memory operand);
+//   warps 5-7  cp.async loaders of the 64-slot K/V tiles (two stages, 128-byte swizzled
+//              canonical layouts, chunk ^ (row & 7)).
+// S is double-buffered in tensor memory (columns [0, 64) and [64, 128)), O sits at [128, 128+D).
+// Stages and buffers are handed over with mbarriers; every wait is bounded, and on expiry a
+// role stops, the CTA records kStatusTimeout, frees its tensor memory and returns.
 constexpr int kTcWarps = 8;
 constexpr int kTcRows = 128;
 constexpr int kTcTS = 64;
-constexpr uint32_t kTcCols = 256;          // tensor-memory columns: S/P [0, 64), O [64, 64 + D)
+constexpr int kTcLoaders = 96;             // warps 5-7
+constexpr uint32_t kTcCols = 256;
 constexpr int32_t kStatusTimeout = 1 << 17;
 constexpr long long kTcWaitBudget = 4000000000LL;   // clock cycles (about 2 s)
 
 template <int D>
 struct TcShape {
-  static constexpr int KB = D / 64;                      // 128-byte column blocks of a row
-  static constexpr int Q_BYTES = KB * kTcRows * 128;
-  static constexpr int KV_BYTES = KB * kTcTS * 128;      // one K or V tile
+  static constexpr int Q_BYTES = (D / 64) * kTcRows * 128;
+  static constexpr int KV_BYTES = (D / 64) * kTcTS * 128;      // one K or V tile
   static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + Q_BYTES;                  // 2 stages
-  static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;             // 2 stages
-  static constexpr int OFF_M = OFF_V + 2 * KV_BYTES;             // 2 x 64 floats: qx * mass * scale * log2(e)
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;                 // 2 stages
+  static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;            // 2 stages
+  static constexpr int OFF_M = OFF_V + 2 * KV_BYTES;            // 2 x 64 raw masses
   static constexpr int BYTES = OFF_M + 2 * kTcTS * 4;
-  static constexpr size_t smem = (size_t)BYTES + 1024;           // + alignment slack
+  static constexpr size_t smem = (size_t)BYTES + 1024;          // + alignment slack
   static_assert(D == 64 || D == 128, "tcgen05 chunk attention handles head dims 64 and 128");
+  static_assert(128 + D <= (int)kTcCols, "tensor-memory columns");
 };
 
 template <int D>
@@ -1243,11 +1245,10 @@ __global__ void __launch_bounds__(kTcWarps * 32) chunk_attn_tc_kernel(AttnGeo a,
   using S = TcShape<D>;
   constexpr int CPR = D / 8, TS = kTcTS;
   extern __shared__ uint4 smem4[];
-  __shared__ uint64_t bar_s, bar_pv;
+  __shared__ uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], p_full[2], pv_done[2];
   __shared__ uint32_t sh_tmem;
   __shared__ int sh_abort;
   const int tid = threadIdx.x, warp = tid >> 5;
-  // 1024-byte aligned base for the swizzled operand tiles.
   unsigned char* raw = reinterpret_cast<unsigned char*>(smem4);
   unsigned char* base = raw + ((1024u - (tc::smem_u32(raw) & 1023u)) & 1023u);
   const uint32_t base_s = tc::smem_u32(base);
@@ -1261,11 +1262,16 @@ __global__ void __launch_bounds__(kTcWarps * 32) chunk_attn_tc_kernel(AttnGeo a,
   const int Tvis = a.causal ? min(a.T, tlast + 1) : a.T;
   const int up = (Lp + TS - 1) / TS, ur = (R + TS - 1) / TS, uc = (Tvis + TS - 1) / TS;
   const int U = up + ur + uc;
-  const float mscale = a.qx * a.scale_log2;
 
   if (tid == 0) {
-    tc::mbar_init(&bar_s, 1);
-    tc::mbar_init(&bar_pv, 1);
+    tc::mbar_init(&q_full, 2 * kTcLoaders);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(&kv_full[i], 2 * kTcLoaders);
+      tc::mbar_init(&kv_empty[i], 1);
+      tc::mbar_init(&s_full[i], 1);
+      tc::mbar_init(&p_full[i], kTcRows);
+      tc::mbar_init(&pv_done[i], 1);
+    }
     tc::mbar_fence_init();
     sh_abort = 0;
   }
@@ -1273,14 +1279,12 @@ __global__ void __launch_bounds__(kTcWarps * 32) chunk_attn_tc_kernel(AttnGeo a,
     tc::tmem_alloc(&sh_tmem, kTcCols);
     tc::tmem_relinquish();
   }
-  // Q tile: row m = head (m / QT) x token (tq0 + m % QT); rows past the query range are zero.
-  for (int flat = tid; flat < kTcRows * CPR; flat += kTcWarps * 32) {
-    const int m = flat / CPR, c = flat % CPR;
-    const int t = tq0 + m % QT, h = g * a.rf + m / QT;
-    unsigned char* dst = base + S::OFF_Q + (c >> 3) * (kTcRows * 128) + m * 128 + (((c & 7) ^ (m & 7)) << 4);
-    if (t < a.qoff + a.TQ) cp_async16(dst, q + (((size_t)b * a.H + h) * a.T + t) * D + c * 8);
-    else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
-  }
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = sh_tmem;
+  const uint32_t t_o = tmem + 128;
+  auto t_s = [&](int buf) { return tmem + 64u * buf; };
   auto unit_info = [&](int u, const __nv_bfloat16*& kb, const __nv_bfloat16*& vb, const float*& mb, int& rows,
                        int& cls, int& first) {
     if (u < up) {
@@ -1309,16 +1313,37 @@ __global__ void __launch_bounds__(kTcWarps * 32) chunk_attn_tc_kernel(AttnGeo a,
       cls = 2;
     }
   };
-  auto issue = [&](int u, int stage) {
-    if (u < U) {
+  auto fail = [&]() {
+    sh_abort = 1;
+    if (status) atomicOr(status, kStatusTimeout);
+  };
+
+  if (warp >= 5) {
+    // ------------------------------------------------ loaders
+    const int lt = tid - 160;
+    for (int flat = lt; flat < kTcRows * CPR; flat += kTcLoaders) {
+      const int m = flat / CPR, c = flat % CPR;
+      const int t = tq0 + m % QT, h = g * a.rf + m / QT;
+      unsigned char* dst = base + S::OFF_Q + (c >> 3) * (kTcRows * 128) + m * 128 + (((c & 7) ^ (m & 7)) << 4);
+      if (t < a.qoff + a.TQ) cp_async16(dst, q + (((size_t)b * a.H + h) * a.T + t) * D + c * 8);
+      else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+    }
+    tc::mbar_arrive_cp_async(&q_full);
+    tc::mbar_arrive(&q_full);
+    for (int u = 0; u < U; ++u) {
+      const int st = u & 1;
+      if (u >= 2 && !tc::mbar_wait(&kv_empty[st], ((u - 2) >> 1) & 1, kTcWaitBudget)) {
+        fail();
+        break;
+      }
       const __nv_bfloat16 *kb, *vb;
       const float* mb;
       int rows, cls, first;
       unit_info(u, kb, vb, mb, rows, cls, first);
-      unsigned char* sk = base + S::OFF_K + stage * S::KV_BYTES;
-      unsigned char* sv = base + S::OFF_V + stage * S::KV_BYTES;
-      float* sm = reinterpret_cast<float*>(base + S::OFF_M) + stage * TS;
-      for (int flat = tid; flat < TS * CPR; flat += kTcWarps * 32) {
+      unsigned char* sk = base + S::OFF_K + st * S::KV_BYTES;
+      unsigned char* sv = base + S::OFF_V + st * S::KV_BYTES;
+      float* sm = reinterpret_cast<float*>(base + S::OFF_M) + st * TS;
+      for (int flat = lt; flat < TS * CPR; flat += kTcLoaders) {
         const int r = flat / CPR, c = flat % CPR;
         const int off = (c >> 3) * (TS * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4);
         if (r < rows) {
@@ -1329,59 +1354,80 @@ __global__ void __launch_bounds__(kTcWarps * 32) chunk_attn_tc_kernel(AttnGeo a,
           *reinterpret_cast<uint4*>(sv + off) = make_uint4(0, 0, 0, 0);
         }
       }
-      if (tid < TS) sm[tid] = (cls == 0 && tid < rows) ? mscale * mb[tid] : 0.f;
-    }
-    cp_async_commit();
-  };
-  issue(0, 0);
-  tc::fence_before();
-  __syncthreads();
-  tc::fence_after();
-  const uint32_t tmem = sh_tmem;
-  const uint32_t t_s = tmem, t_o = tmem + 64;
-  const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-  constexpr uint32_t idesc_s = tc::f16_idesc(kTcRows, TS, 0, 0);
-  constexpr uint32_t idesc_o = tc::f16_idesc(kTcRows, D, 0, 1);
-  // Softmax state of row `tid` (threads 0..127).
-  const bool srow = tid < kTcRows;
-  const int row_t = tq0 + (tid % QT);
-  float m_used = -INFINITY, l = 0.f;
-  uint32_t ph_s = 0, ph_pv = 0;
-  for (int u = 0; u < U; ++u) {
-    const int stage = u & 1;
-    issue(u + 1, stage ^ 1);
-    cp_async_wait<1>();
-    tc::fence_proxy_async();
-    __syncthreads();
-    if (tid == 0) {
-      tc::fence_after();
-      const uint32_t qa = base_s + S::OFF_Q, kbs = base_s + S::OFF_K + stage * S::KV_BYTES;
-#pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks) {
-        const uint64_t da = tc::sw128_desc(qa + (ks >> 2) * (kTcRows * 128) + (ks & 3) * 32, 16, 1024);
-        const uint64_t db = tc::sw128_desc(kbs + (ks >> 2) * (TS * 128) + (ks & 3) * 32, 16, 1024);
-        tc::umma_f16(t_s, da, db, idesc_s, ks > 0 ? 1u : 0u);
+      if (lt < TS) {
+        if (cls == 0 && lt < rows) cp_async4(sm + lt, mb + lt);
+        else sm[lt] = 0.f;
       }
-      tc::umma_commit(&bar_s);
+      tc::mbar_arrive_cp_async(&kv_full[st]);   // when this thread's copies land
+      tc::mbar_arrive(&kv_full[st]);            // releases its plain zero stores
     }
-    bool live = true;   // warp-uniform: tcgen05.ld/st are warp-collective
-    if (srow) {
-      live = __all_sync(0xffffffffu, tc::mbar_wait(&bar_s, ph_s, kTcWaitBudget));
-      if (!live && (tid & 31) == 0) sh_abort = 1;
+  } else if (warp == 4) {
+    // ------------------------------------------------ MMA issuer
+    if ((tid & 31) == 0) {
+      constexpr uint32_t idesc_s = tc::f16_idesc(kTcRows, TS, 0, 0);
+      constexpr uint32_t idesc_o = tc::f16_idesc(kTcRows, D, 0, 1);
+      const uint32_t qa = base_s + S::OFF_Q;
+      auto pv = [&](int v) {
+        const int bp = v & 1;
+        const uint32_t vbs = base_s + S::OFF_V + bp * S::KV_BYTES;
+#pragma unroll
+        for (int ks = 0; ks < TS / 16; ++ks) {
+          const uint64_t db = tc::sw128_desc(vbs + ks * 16 * 128, TS * 128, 1024);
+          tc::umma_f16_ts(t_o, t_s(bp) + ks * 8, db, idesc_o, (v > 0 || ks > 0) ? 1u : 0u);
+        }
+        tc::umma_commit(&pv_done[bp]);
+        tc::umma_commit(&kv_empty[bp]);
+      };
+      bool ok = tc::mbar_wait(&q_full, 0, kTcWaitBudget);
+      for (int u = 0; ok && u <= U; ++u) {
+        if (u < U) {
+          const int st = u & 1;
+          ok = tc::mbar_wait(&kv_full[st], (u >> 1) & 1, kTcWaitBudget) &&
+               (u < 2 || tc::mbar_wait(&pv_done[st], ((u - 2) >> 1) & 1, kTcWaitBudget));
+          if (!ok) break;
+          tc::fence_proxy_async();
+          tc::fence_after();
+          const uint32_t kbs = base_s + S::OFF_K + st * S::KV_BYTES;
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks) {
+            const uint64_t da = tc::sw128_desc(qa + (ks >> 2) * (kTcRows * 128) + (ks & 3) * 32, 16, 1024);
+            const uint64_t db = tc::sw128_desc(kbs + (ks >> 2) * (TS * 128) + (ks & 3) * 32, 16, 1024);
+            tc::umma_f16(t_s(st), da, db, idesc_s, ks > 0 ? 1u : 0u);
+          }
+          tc::umma_commit(&s_full[st]);
+        }
+        if (u >= 1) {
+          ok = tc::mbar_wait(&p_full[(u - 1) & 1], ((u - 1) >> 1) & 1, kTcWaitBudget);
+          if (!ok) break;
+          tc::fence_after();
+          pv(u - 1);
+        }
+      }
+      if (!ok) fail();
     }
-    ph_s ^= 1;
-    if (srow && live) {
+  } else {
+    // ------------------------------------------------ softmax (row tid)
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const int row_t = tq0 + (tid % QT);
+    const float mscale = a.qx * a.scale_log2;
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int u = 0; u < U; ++u) {
+      const int st = u & 1;
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&kv_full[st], (u >> 1) & 1, kTcWaitBudget) &&
+                                       tc::mbar_wait(&s_full[st], (u >> 1) & 1, kTcWaitBudget));
+      if (!ok) break;
       tc::fence_after();
       const __nv_bfloat16 *kb_, *vb_;
       const float* mb_;
       int rows, cls, first;
       unit_info(u, kb_, vb_, mb_, rows, cls, first);
-      const float* sm = reinterpret_cast<const float*>(base + S::OFF_M) + stage * TS;
+      const float* sm = reinterpret_cast<const float*>(base + S::OFF_M) + st * TS;
       float sv[TS];
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
         uint32_t r32[32];
-        tc::tmem_ld32(t_s + lane_off + half * 32, r32);
+        tc::tmem_ld32(t_s(st) + lane_off + half * 32, r32);
 #pragma unroll
         for (int j = 0; j < 32; ++j) sv[half * 32 + j] = __uint_as_float(r32[j]);
       }
@@ -1390,14 +1436,14 @@ __global__ void __launch_bounds__(kTcWarps * 32) chunk_attn_tc_kernel(AttnGeo a,
       if (full) {
 #pragma unroll
         for (int j = 0; j < TS; ++j) {
-          sv[j] = fmaf(sv[j], a.scale_log2, sm[j]);
+          sv[j] = fmaf(sv[j], a.scale_log2, mscale * sm[j]);
           mt = fmaxf(mt, sv[j]);
         }
       } else {
 #pragma unroll
         for (int j = 0; j < TS; ++j) {
           const bool vis = j < rows && (cls != 2 || !a.causal || first + j <= row_t);
-          sv[j] = vis ? fmaf(sv[j], a.scale_log2, sm[j]) : -INFINITY;
+          sv[j] = vis ? fmaf(sv[j], a.scale_log2, mscale * sm[j]) : -INFINITY;
           mt = fmaxf(mt, sv[j]);
         }
       }
@@ -1417,6 +1463,10 @@ __global__ void __launch_bounds__(kTcWarps * 32) chunk_attn_tc_kernel(AttnGeo a,
       }
       l = l * alpha + ps;
       if (u > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        // O must hold PV(u-1) before it is rescaled.
+        ok = __all_sync(0xffffffffu, tc::mbar_wait(&pv_done[(u - 1) & 1], ((u - 1) >> 1) & 1, kTcWaitBudget));
+        if (!ok) break;
+        tc::fence_after();
 #pragma unroll 1
         for (int c0 = 0; c0 < D; c0 += 32) {
           uint32_t r32[32];
@@ -1426,52 +1476,39 @@ __global__ void __launch_bounds__(kTcWarps * 32) chunk_attn_tc_kernel(AttnGeo a,
           tc::tmem_st32(t_o + lane_off + c0, r32);
         }
       }
-      tc::tmem_st32(t_s + lane_off, pk);   // P over S's first 32 columns
+      tc::tmem_st32(t_s(st) + lane_off, pk);
+      tc::fence_before();
+      tc::mbar_arrive(&p_full[st]);
     }
-    tc::fence_before();
-    __syncthreads();
-    if (sh_abort) break;
-    if (tid == 0) {
+    if (ok && U > 0)
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&pv_done[(U - 1) & 1], ((U - 1) >> 1) & 1, kTcWaitBudget));
+    if (!ok) {
+      if ((tid & 31) == 0) fail();
+    } else if (U > 0) {
       tc::fence_after();
-      const uint32_t vbs = base_s + S::OFF_V + stage * S::KV_BYTES;
-#pragma unroll
-      for (int ks = 0; ks < TS / 16; ++ks) {
-        const uint64_t db = tc::sw128_desc(vbs + ks * 16 * 128, TS * 128, 1024);
-        tc::umma_f16_ts(t_o, t_s + ks * 8, db, idesc_o, (u > 0 || ks > 0) ? 1u : 0u);
-      }
-      tc::umma_commit(&bar_pv);
-    }
-    if (!__all_sync(0xffffffffu, tc::mbar_wait(&bar_pv, ph_pv, kTcWaitBudget)) && (tid & 31) == 0) sh_abort = 1;
-    ph_pv ^= 1;
-    __syncthreads();
-    if (sh_abort) break;
-  }
-  cp_async_wait<0>();
-  if (sh_abort) {
-    if (tid == 0 && status) atomicOr(status, kStatusTimeout);
-  } else if (srow && U > 0) {
-    tc::fence_after();
-    const int hh = tid / QT;
-    const bool ok = row_t < a.qoff + a.TQ;
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    __nv_bfloat16* orow = out + (((size_t)b * a.H + g * a.rf + hh) * a.T + row_t) * D;
+      const int hh = tid / QT;
+      const bool in = row_t < a.qoff + a.TQ;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* orow = out + (((size_t)b * a.H + g * a.rf + hh) * a.T + row_t) * D;
 #pragma unroll 1
-    for (int c0 = 0; c0 < D; c0 += 32) {
-      uint32_t r32[32];
-      tc::tmem_ld32(t_o + lane_off + c0, r32);
-      if (ok) {
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t r32[32];
+        tc::tmem_ld32(t_o + lane_off + c0, r32);
+        if (in) {
 #pragma unroll
-        for (int j = 0; j < 32; j += 8) {
-          uint4 w;
-          w.x = pack_bf16x2(__uint_as_float(r32[j]) * inv, __uint_as_float(r32[j + 1]) * inv);
-          w.y = pack_bf16x2(__uint_as_float(r32[j + 2]) * inv, __uint_as_float(r32[j + 3]) * inv);
-          w.z = pack_bf16x2(__uint_as_float(r32[j + 4]) * inv, __uint_as_float(r32[j + 5]) * inv);
-          w.w = pack_bf16x2(__uint_as_float(r32[j + 6]) * inv, __uint_as_float(r32[j + 7]) * inv);
-          *reinterpret_cast<uint4*>(orow + c0 + j) = w;
+          for (int j = 0; j < 32; j += 8) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(r32[j]) * inv, __uint_as_float(r32[j + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(r32[j + 2]) * inv, __uint_as_float(r32[j + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(r32[j + 4]) * inv, __uint_as_float(r32[j + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(r32[j + 6]) * inv, __uint_as_float(r32[j + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c0 + j) = w;
+          }
         }
       }
     }
   }
+  cp_async_wait<0>();
   tc::fence_before();
   __syncthreads();
   if (warp == 0) {

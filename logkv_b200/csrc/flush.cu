@@ -23,6 +23,11 @@
 
 namespace logkv {
 
+// Greedy span choice: per candidate density, size, rank, flags; victims in two buffers.
+static size_t choose_smem_bytes(const Geo& g) {
+  return (size_t)g.NC * (8 + 4 + 4 + 2) + 2 * (size_t)(g.P + 1) * (8 + 4 + 4) + (size_t)(g.P + 1) * (8 + 4) + 16;
+}
+
 static size_t cascade_smem(const Geo& g, size_t esize) {
   // two K/V tile buffers, two metadata tiles, token positions and sources
   return 4 * (size_t)kTileRows * g.D * esize + 2 * (size_t)kTileRows * sizeof(Meta) +
@@ -252,7 +257,7 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   }
   if (!(phases & kPhaseCommit)) return (int)cudaGetLastError();
   mark();
-  const size_t choose_smem = (size_t)g.NC * (8 + 4 * 4 + 2);
+  const size_t choose_smem = choose_smem_bytes(g);
   if (choose_smem > 48 * 1024)
     cudaFuncSetAttribute(alpha_choose_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)choose_smem);
   alpha_choose_kernel<<<g.B, 1024, choose_smem, st>>>(g, s, w);
@@ -319,7 +324,8 @@ static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, i
   Work w{};
   const size_t need = carve(g, esize, static_cast<char*>(workspace), &w);
   if (workspace_bytes < need) return LOGKV_E_WORKSPACE;
-  if (cascade_smem(g, esize) > 227 * 1024 || (size_t)g.sort_cap * 8 + (size_t)g.NW * 4 > 227 * 1024)
+  if (cascade_smem(g, esize) > 227 * 1024 || (size_t)g.sort_cap * 8 + (size_t)g.NW * 4 > 227 * 1024 ||
+      choose_smem_bytes(g) > 227 * 1024)
     return LOGKV_E_SMEM;
   w.gpart_all = gpart_all;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

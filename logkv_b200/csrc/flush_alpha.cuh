@@ -328,15 +328,25 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
   const int b = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
   const int NC = g.NC, P = g.P;
   extern __shared__ unsigned char smraw[];
-  double* dens = reinterpret_cast<double*>(smraw);          // [NC]
-  int* size = reinterpret_cast<int*>(dens + NC);             // [NC]
-  int* vict = size + NC;                                     // [NC] sorted victims
-  int* ranked = vict + NC;                                   // [NC]
-  int* keep_off = ranked + NC;                               // [NC]
-  unsigned char* flags = reinterpret_cast<unsigned char*>(keep_off + NC);  // [NC]
+  const int VC = P + 1;                                      // victims never exceed P (each >= 1 token)
+  double* dens = reinterpret_cast<double*>(smraw);           // [NC]
+  double* vd = dens + NC;                                    // [2][VC] victim densities (ping-pong)
+  int* size = reinterpret_cast<int*>(vd + 2 * VC);           // [NC]
+  int* ranked = size + NC;                                   // [NC]
+  int* vs = ranked + NC;                                     // [2][VC] victim sizes
+  int* vi = vs + 2 * VC;                                     // [2][VC] victim candidate indices
+  double* pls = reinterpret_cast<double*>(vi + 2 * VC);      // [VC] loss prefix, left to right
+  int* psz = reinterpret_cast<int*>(pls + VC);               // [VC] inclusive size prefix
+  unsigned char* flags = reinterpret_cast<unsigned char*>(psz + VC);  // [NC]
   unsigned char* chosen = flags + NC;                        // [NC]
   __shared__ int wsum[32];
   __shared__ int sh_nv, sh_nr, sh_room;
+  if (tid == 0) {
+    sh_nv = 0;
+    sh_nr = 0;
+    sh_room = P;
+  }
+  __syncthreads();
   const int n = w.n_cand[b];
   for (int i = tid; i < n; i += nt) {
     const size_t c = (size_t)b * NC + i;
@@ -377,83 +387,175 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
     chosen[i] = (!(flags[i] & 2)) || (flags[i] & 1);  // mandatory (open) or old
   }
   __syncthreads();
-  // room = budget - sizes of mandatory and old spans (integer, any order)
-  if (tid == 0) {
-    int room = P;
-    for (int i = 0; i < n; ++i)
-      if (chosen[i]) room -= size[i];
-    sh_room = room;
-  }
-  __syncthreads();
-  // victims = chosen and not mandatory, sorted by (density, -i): rank-based placement
+  // room = budget - sizes of mandatory and old spans; victim count (integers, any order)
   for (int i = tid; i < n; i += nt) {
-    if (!(chosen[i] && (flags[i] & 2))) continue;
-    int rank = 0;
-    for (int j = 0; j < n; ++j)
-      if (j != i && chosen[j] && (flags[j] & 2) && victim_less(dens[j], j, dens[i], i)) ++rank;
-    vict[rank] = i;
+    if (chosen[i]) atomicSub(&sh_room, size[i]);
+    if (chosen[i] && (flags[i] & 2)) atomicAdd(&sh_nv, 1);
   }
-  __syncthreads();
-  if (tid == 0) {
-    int nv = 0;
-    for (int i = 0; i < n; ++i) nv += (chosen[i] && (flags[i] & 2)) ? 1 : 0;
-    // make room for the bounded unfinished tail first (victims in order)
-    int room = sh_room, k = 0;
-    while (k < nv && room < 0) {
-      chosen[vict[k]] = 0;
-      room += size[vict[k]];
-      ++k;
+  // victims = chosen and not mandatory, sorted by (density, -i)
+  for (int i = tid; i < n; i += nt) {
+    if (chosen[i] && (flags[i] & 2)) {
+      int rank = 0;
+      for (int j = 0; j < n; ++j)
+        if (j != i && chosen[j] && (flags[j] & 2) && victim_less(dens[j], j, dens[i], i)) ++rank;
+      vd[rank] = dens[i];
+      vs[rank] = size[i];
+      vi[rank] = i;
     }
-    for (int i = k; i < nv; ++i) vict[i - k] = vict[i];
-    sh_nv = nv - k;
-    sh_room = room;
   }
   __syncthreads();
-  // ranked = not chosen, sorted by (-density, i)
+  // Make room for the bounded unfinished tail first (victims in order): remove the shortest
+  // prefix of the sorted victims after which room >= 0 (one warp; exact integer prefix scan).
+  if (tid < 32 && sh_room < 0) {
+    const int lane = tid;
+    const unsigned full = 0xffffffffu;
+    const int nv = sh_nv;
+    int acc = sh_room, k = nv;
+    for (int c0 = 0; c0 < nv; c0 += 32) {
+      const int j = c0 + lane;
+      int incl = j < nv ? vs[j] : 0;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(full, incl, off);
+        if (lane >= off) incl += y;
+      }
+      const unsigned hit = __ballot_sync(full, j < nv && acc + incl >= 0);
+      if (hit) {
+        const int f = __ffs(hit) - 1;
+        k = c0 + f + 1;
+        acc += __shfl_sync(full, incl, f);
+        break;
+      }
+      acc += __shfl_sync(full, incl, 31);
+    }
+    for (int j = lane; j < k; j += 32) chosen[vi[j]] = 0;
+    for (int j = lane; j < nv - k; j += 32) {   // victims [k, nv) -> buffer 1 at [0, nv - k)
+      vd[VC + j] = vd[k + j];
+      vs[VC + j] = vs[k + j];
+      vi[VC + j] = vi[k + j];
+    }
+    __syncwarp();
+    for (int j = lane; j < nv - k; j += 32) {
+      vd[j] = vd[VC + j];
+      vs[j] = vs[VC + j];
+      vi[j] = vi[VC + j];
+    }
+    if (lane == 0) {
+      sh_nv = nv - k;
+      sh_room = acc;
+    }
+  }
+  __syncthreads();
+  // ranked = not chosen (removed victims included), sorted by (-density, i)
   for (int i = tid; i < n; i += nt) {
     if (chosen[i]) continue;
+    atomicAdd(&sh_nr, 1);
     int rank = 0;
     for (int j = 0; j < n; ++j)
       if (j != i && !chosen[j] && ranked_less(dens[j], j, dens[i], i)) ++rank;
     ranked[rank] = i;
   }
-  if (tid == 0) {
-    int nr = 0;
-    for (int i = 0; i < n; ++i) nr += chosen[i] ? 0 : 1;
-    sh_nr = nr;
-  }
   __syncthreads();
-  if (tid == 0) {
-    int room = sh_room, nv = sh_nv;
+  // Bounded greedy (alpha_log_kv.choose_spans) in one warp.  The number of victims a
+  // candidate needs comes from an exact integer prefix scan of victim sizes; the float64
+  // loss over exactly those victims is summed by lane 0 in the reference's order.
+  if (tid < 32) {
+    const int lane = tid;
+    const unsigned full = 0xffffffffu;
+    int cur = 0, nv = sh_nv, room = sh_room;
     const int nr = sh_nr;
-    for (int q = 0; q < nr; ++q) {
-      const int i = ranked[q];
-      const int length = size[i];
-      int available = room, nrem = 0;
-      double loss = 0.0;
-      if (available < length) {
+    // Prefixes of the current victim list: inclusive sizes (exact integers, warp scan) and
+    // the float64 loss sum(density * size) added left to right from 0.0 (lane 0), so any
+    // prefix equals the reference's running `loss` after that many removals.
+    auto prefixes = [&]() {
+      int carry = 0;
+      for (int c0 = 0; c0 < nv; c0 += 32) {
+        const int j = c0 + lane;
+        int incl = j < nv ? vs[cur * VC + j] : 0;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const int y = __shfl_up_sync(full, incl, off);
+          if (lane >= off) incl += y;
+        }
+        if (j < nv) psz[j] = carry + incl;
+        carry += __shfl_sync(full, incl, 31);
+      }
+      if (lane == 0) {
+        double acc = 0.0;
         for (int j = 0; j < nv; ++j) {
-          const int v = vict[j];
-          ++nrem;
-          available += size[v];
-          loss += dens[v] * (double)size[v];
-          if (available >= length) break;
+          acc += vd[cur * VC + j] * (double)vs[cur * VC + j];
+          pls[j] = acc;
         }
       }
-      if (available >= length && (nrem == 0 || dens[i] * (double)length > loss)) {
-        for (int j = 0; j < nrem; ++j) chosen[vict[j]] = 0;
-        // victims: drop the removed prefix, insert i at its sorted place
-        int m = 0;
-        for (int j = nrem; j < nv; ++j) vict[m++] = vict[j];
-        int at = m;
-        while (at > 0 && victim_less(dens[i], i, dens[vict[at - 1]], vict[at - 1])) {
-          vict[at] = vict[at - 1];
-          --at;
+      __syncwarp();
+    };
+    // First victim index j with room + psz[j] >= need: returns j + 1 (victims to remove) and
+    // the room they leave in `avail`, or -1 when all of them do not suffice.
+    auto need_prefix = [&](int need, int& avail) -> int {
+      for (int c0 = 0; c0 < nv; c0 += 32) {
+        const int j = c0 + lane;
+        const unsigned hit = __ballot_sync(full, j < nv && room + psz[j] >= need);
+        if (hit) {
+          const int f = c0 + __ffs(hit) - 1;
+          avail = room + psz[f];
+          return f + 1;
         }
-        vict[at] = i;
-        nv = m + 1;
-        chosen[i] = 1;
-        room = available - length;
+      }
+      avail = nv ? room + psz[nv - 1] : room;
+      return -1;
+    };
+    // Remove the first k victims and insert (di, length, i) at its sorted place.
+    auto rebuild = [&](int k, double di, int length, int i) {
+      const bool ins = true;
+      for (int j = lane; j < k; j += 32) chosen[vi[cur * VC + j]] = 0;
+      int at = 0;
+      if (ins)
+        for (int c0 = k; c0 < nv; c0 += 32) {
+          const int j = c0 + lane;
+          at += __popc(__ballot_sync(full, j < nv && victim_less(vd[cur * VC + j], vi[cur * VC + j], di, i)));
+        }
+      const int nn = nv - k + (ins ? 1 : 0), nx = cur ^ 1;
+      for (int j = lane; j < nn; j += 32) {
+        int src = -1;
+        if (!ins) src = k + j;
+        else if (j < at) src = k + j;
+        else if (j > at) src = k + j - 1;
+        if (src >= 0) {
+          vd[nx * VC + j] = vd[cur * VC + src];
+          vs[nx * VC + j] = vs[cur * VC + src];
+          vi[nx * VC + j] = vi[cur * VC + src];
+        } else {
+          vd[nx * VC + j] = di;
+          vs[nx * VC + j] = length;
+          vi[nx * VC + j] = i;
+        }
+      }
+      __syncwarp();
+      cur = nx;
+      nv = nn;
+      prefixes();
+    };
+    prefixes();
+    for (int q0 = 0; q0 < nr; q0 += 32) {
+      const int qi = q0 + lane < nr ? ranked[q0 + lane] : 0;
+      const double qd = dens[qi];
+      const int qs = size[qi];
+      const int cnt = min(32, nr - q0);
+      for (int t = 0; t < cnt; ++t) {
+        const int i = __shfl_sync(full, qi, t);
+        const double di = __shfl_sync(full, qd, t);
+        const int length = __shfl_sync(full, qs, t);
+        int nrem = 0, available = room;
+        bool ok = room >= length;
+        if (!ok) {
+          nrem = need_prefix(length, available);
+          if (nrem > 0) ok = di * (double)length > pls[nrem - 1];
+        }
+        if (ok) {
+          if (lane == 0) chosen[i] = 1;
+          rebuild(nrem, di, length, i);
+          room = available - length;
+        }
       }
     }
   }
