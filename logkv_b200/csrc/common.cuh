@@ -45,6 +45,14 @@ template <> struct Elem<__nv_bfloat16> {
   __device__ __forceinline__ static __nv_bfloat16 zero() { return __float2bfloat16_rn(0.f); }
 };
 
+// Programmatic dependent launch: wait until the preceding kernel of the stream has completed
+// and its writes are visible (a no-op when the launch carries no programmatic dependency),
+// then let the next kernel start launching while this one runs.
+__device__ __forceinline__ void pdl_entry() {
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
 __device__ __forceinline__ void set_status(int32_t* status, int32_t bit) {
   if (status) atomicOr(status, bit);
 }

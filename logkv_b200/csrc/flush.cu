@@ -34,17 +34,35 @@ static size_t cascade_smem(const Geo& g, size_t esize) {
          (size_t)g.NW * (sizeof(int64_t) + sizeof(int)) + 16;
 }
 
+// Every flush kernel is launched with a programmatic dependency on the previous kernel of the
+// stream (each kernel begins with pdl_entry()), so launch latency overlaps the previous tail.
+template <typename... KArgs, typename... Args>
+static void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // Cascade launch for one (dtype, Beta, head dim) instantiation; DC = 0 is the runtime-D kernel.
 template <typename T, bool BETA, int DC>
 static void launch_cascade(const Geo& g, const logkv_state_t& s, const Work& w, size_t smem, cudaStream_t st) {
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(cascade_kernel<T, BETA, DC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  cascade_kernel<T, BETA, DC><<<dim3(g.K, g.G, g.B), 512, smem, st>>>(g, s, w);
+  launch_pdl(cascade_kernel<T, BETA, DC>, dim3(g.K, g.G, g.B), 512, smem, st, g, s, w);
 }
 
 // ---------------------------------------------------------------- K8: window shift
 template <typename T>
 __global__ void window_stage_kernel(Geo g, logkv_state_t s, Work w, int rem) {
+  pdl_entry();
   // copy [F, F+rem) -> staging [0, rem) when source and destination overlap
   const int b = blockIdx.z, grp = blockIdx.y;
   const size_t base = ((size_t)b * g.G + grp) * g.cap2R * g.D;
@@ -64,6 +82,7 @@ __global__ void window_stage_kernel(Geo g, logkv_state_t s, Work w, int rem) {
 
 template <typename T>
 __global__ void window_shift_kernel(Geo g, logkv_state_t s, Work w, int rem, int staged) {
+  pdl_entry();
   const int b = blockIdx.z, grp = blockIdx.y;
   const size_t base = ((size_t)b * g.G + grp) * g.cap2R * g.D;
   const size_t n = (size_t)g.recent_count * g.D;
@@ -243,31 +262,31 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   const int per_bg = std::max(1, std::min(64, (g.P * g.D + 255) / 256));
   if (phases & kPhaseScores) {
   mark();
-  snapshot_kernel<T><<<dim3(per_bg, g.G, g.B), 256, 0, st>>>(g, s, w);
+  launch_pdl(snapshot_kernel<T>, dim3(per_bg, g.G, g.B), 256, 0, st, g, s, w);
   mark();
   const size_t cut_smem = 2 * (size_t)g.F * sizeof(int);
   if (cut_smem > 48 * 1024) cudaFuncSetAttribute(alpha_cut_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cut_smem);
-  alpha_cut_kernel<<<g.B, 1024, cut_smem, st>>>(g, s, w);
+  launch_pdl(alpha_cut_kernel, g.B, 1024, cut_smem, st, g, s, w);
   mark();
   const size_t score_smem = (64 * (size_t)(g.D + 1) + 2 * (size_t)g.D + 64 + (size_t)g.K) * sizeof(float);
   if (score_smem > 48 * 1024)
     cudaFuncSetAttribute(alpha_score_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)score_smem);
   const int score_blocks = std::max(1, std::min(g.NC, 8 * sm_count / std::max(1, g.B * g.G) + 1));
-  alpha_score_kernel<T><<<dim3(score_blocks, g.G, g.B), 256, score_smem, st>>>(g, s, w);
+  launch_pdl(alpha_score_kernel<T>, dim3(score_blocks, g.G, g.B), 256, score_smem, st, g, s, w);
   }
   if (!(phases & kPhaseCommit)) return (int)cudaGetLastError();
   mark();
   const size_t choose_smem = choose_smem_bytes(g);
   if (choose_smem > 48 * 1024)
     cudaFuncSetAttribute(alpha_choose_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)choose_smem);
-  alpha_choose_kernel<<<g.B, 1024, choose_smem, st>>>(g, s, w);
+  launch_pdl(alpha_choose_kernel, g.B, 1024, choose_smem, st, g, s, w);
   mark();
   const int att_tok = 256 / (g.K <= 16 ? 16 : 32);
   const size_t attach_smem =
       ((size_t)(g.K + att_tok) * (g.D + 1) + 2 * (size_t)att_tok * g.K) * sizeof(float);
   if (attach_smem > 48 * 1024)
     cudaFuncSetAttribute(attach_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attach_smem);
-  attach_kernel<T><<<dim3((g.NW + att_tok - 1) / att_tok, g.G, g.B), 256, attach_smem, st>>>(g, s, w);
+  launch_pdl(attach_kernel<T>, dim3((g.NW + att_tok - 1) / att_tok, g.G, g.B), 256, attach_smem, st, g, s, w);
   mark();
   {
     // Seeding: one 8-CTA cluster per lane; rows staged in shared memory when they fit.
@@ -279,14 +298,14 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
     const size_t seed_smem = base + (gs.seed_staged ? rows : 0);
     if (seed_smem > 48 * 1024)
       cudaFuncSetAttribute(seed_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)seed_smem);
-    seed_kernel<T><<<dim3(kSeedCluster * g.G, g.B), 512, seed_smem, st>>>(gs, s, w);
+    launch_pdl(seed_kernel<T>, dim3(kSeedCluster * g.G, g.B), 512, seed_smem, st, gs, s, w);
   }
-  plan_kernel<T><<<dim3(g.G, g.B), 1024, 0, st>>>(g, s, w);
+  launch_pdl(plan_kernel<T>, dim3(g.G, g.B), 1024, 0, st, g, s, w);
   mark();
   const size_t prep_smem = (size_t)g.sort_cap * sizeof(unsigned long long) + (size_t)g.NW * sizeof(int);
   if (prep_smem > 48 * 1024)
     cudaFuncSetAttribute(prepare_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
-  prepare_kernel<T><<<dim3(g.K, g.G, g.B), 256, prep_smem, st>>>(g, s, w);
+  launch_pdl(prepare_kernel<T>, dim3(g.K, g.G, g.B), 256, prep_smem, st, g, s, w);
   mark();
   const size_t casc_smem = cascade_smem(g, sizeof(T));
   if (g.beta) {
@@ -299,13 +318,13 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
     else launch_cascade<T, false, 0>(g, s, w, casc_smem, st);
   }
   mark();
-  pool_rewrite_kernel<T><<<dim3(per_bg, g.G, g.B), 256, 0, st>>>(g, s, w);
+  launch_pdl(pool_rewrite_kernel<T>, dim3(per_bg, g.G, g.B), 256, 0, st, g, s, w);
   mark();
   const int rem = g.recent_count - g.F;
   const int per_win = std::max(1, std::min(128, (g.recent_count * g.D + 255) / 256));
   const int staged = rem > g.F ? 1 : 0;
-  if (staged) window_stage_kernel<T><<<dim3(per_win, g.G, g.B), 256, 0, st>>>(g, s, w, rem);
-  window_shift_kernel<T><<<dim3(per_win, g.G, g.B), 256, 0, st>>>(g, s, w, rem, staged);
+  if (staged) launch_pdl(window_stage_kernel<T>, dim3(per_win, g.G, g.B), 256, 0, st, g, s, w, rem);
+  launch_pdl(window_shift_kernel<T>, dim3(per_win, g.G, g.B), 256, 0, st, g, s, w, rem, staged);
   mark();
   return (int)cudaGetLastError();
 }

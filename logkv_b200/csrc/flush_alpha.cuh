@@ -16,6 +16,7 @@ namespace logkv {
 // resets the status word and the device alpha_count.
 template <typename T>
 __global__ void snapshot_kernel(Geo g, logkv_state_t s, Work w) {
+  pdl_entry();
   const int b = blockIdx.z, grp = blockIdx.y;
   const size_t n = (size_t)g.P * g.D;
   const T* ksrc = static_cast<const T*>(s.alpha_k_raw) + ((size_t)b * g.G + grp) * n;
@@ -46,6 +47,7 @@ __global__ void snapshot_kernel(Geo g, logkv_state_t s, Work w) {
 // continuing the unfinished span), or the unfinished span alone when no new
 // token arrived.
 __global__ void __launch_bounds__(1024) alpha_cut_kernel(Geo g, logkv_state_t s, Work w) {
+  pdl_entry();
   const int b = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
   const int P = g.P, F = g.F, cap = g.span_cap;
   __shared__ int wsum[32];
@@ -208,6 +210,7 @@ __global__ void __launch_bounds__(1024) alpha_cut_kernel(Geo g, logkv_state_t s,
 // (row, candidate, group): Alpha parts (R_K, R_V) or Beta's per-group score.
 template <typename T>
 __global__ void __launch_bounds__(256) alpha_score_kernel(Geo g, logkv_state_t s, Work w) {
+  pdl_entry();
   const int b = blockIdx.z, grp = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
   const int G = g.G, D = g.D, K = g.K;
   constexpr int VN = Vec<T>::N;
@@ -325,6 +328,7 @@ __device__ __forceinline__ bool ranked_less(double da, int ia, double db, int ib
 }
 
 __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t s, Work w) {
+  pdl_entry();
   const int b = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
   const int NC = g.NC, P = g.P;
   extern __shared__ unsigned char smraw[];
@@ -645,6 +649,7 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
 // ---------------------------------------------------------------- K7: pool rewrite
 template <typename T>
 __global__ void pool_rewrite_kernel(Geo g, logkv_state_t s, Work w) {
+  pdl_entry();
   const int b = blockIdx.z, grp = blockIdx.y;
   const int nkeep = w.nkeep[b];
   T* kdst = static_cast<T*>(s.alpha_k_raw) + ((size_t)b * g.G + grp) * g.P * g.D;

@@ -158,6 +158,7 @@ __device__ int beta_cut_warp(const T* tk, const T* tv, const Meta* tm, int start
 
 template <typename T, bool BETA, int DC>
 __global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Work w) {
+  pdl_entry();
   LaneCtx<T> x = make_ctx<T>(g, s, w);
   const int type = w.plan_type[x.lane];
   if (type == kJobNone) return;

@@ -136,6 +136,7 @@ __device__ LaneCtx<T> make_ctx(const Geo& g, const logkv_state_t& s, const Work&
 // p_lo with orders 0..n-1 (_alpha_commit_joins, log_kv_cache.py:3690-3788).
 template <typename T>
 __global__ void __launch_bounds__(256) prepare_kernel(Geo g, logkv_state_t s, Work w) {
+  pdl_entry();
   LaneCtx<T> x = make_ctx<T>(g, s, w);
   const int type = w.plan_type[x.lane];
   if (type == kJobNone) return;

@@ -21,6 +21,7 @@ namespace logkv {
 // shared memory with an odd word stride (conflict-free).
 template <typename T>
 __global__ void __launch_bounds__(256) attach_kernel(Geo g, logkv_state_t s, Work w) {
+  pdl_entry();
   const int b = blockIdx.z, grp = blockIdx.y, tid = threadIdx.x;
   const int D = g.D, K = g.K;
   const int slots = K <= 16 ? 16 : 32;          // threads per token
@@ -168,6 +169,7 @@ constexpr int kSeedCluster = 8;
 
 template <typename T>
 __global__ void __cluster_dims__(kSeedCluster, 1, 1) __launch_bounds__(512) seed_kernel(Geo g, logkv_state_t s, Work w) {
+  pdl_entry();
   namespace cg = cooperative_groups;
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
@@ -309,6 +311,7 @@ __global__ void __cluster_dims__(kSeedCluster, 1, 1) __launch_bounds__(512) seed
 // range are planned.
 template <typename T>
 __global__ void __launch_bounds__(1024) plan_kernel(Geo g, logkv_state_t s, Work w) {
+  pdl_entry();
   const int b = blockIdx.y, grp = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
   const int K = g.K;
   const int na = w.narch[b];
