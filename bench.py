@@ -200,7 +200,8 @@ def bench_ours(args, rank, world, local_rank):
     ms_per_step = ms / args.steps
 
     # Per-stage profile (eager, one step): stage events around every flush.
-    nstage = 10
+    from logkv_b200._lib import FLUSH_STAGES
+    nstage = len(FLUSH_STAGES)
     events = [[torch.cuda.Event(enable_timing=True) for _ in range(nstage + 1)] for _ in range(flushes_per_step)]
     for evs in events:
         for e in evs:
@@ -229,7 +230,6 @@ def bench_ours(args, rank, world, local_rank):
             per_flush[i].append(t)
     after = [c.read_counters() for c in caches]
     delta = {k: sum(a[k] - b[k] for a, b in zip(after, before)) for k in after[0]}
-    from logkv_b200._lib import FLUSH_STAGES
     stages_us = {name: round(stage_ms[i] * 1000.0 / flushes_per_step, 2) for i, name in enumerate(FLUSH_STAGES)}
     stages_med = {name: round(statistics.median(per_flush[i]) * 1000.0, 2) for i, name in enumerate(FLUSH_STAGES)}
     stages_max = {name: round(max(per_flush[i]) * 1000.0, 2) for i, name in enumerate(FLUSH_STAGES)}

@@ -169,10 +169,10 @@ LOGKV_API int logkv_read_status(const void* workspace, int32_t* out, void* strea
  * with host counters and optional CUDA events, litgpt/log_kv_timing.py:15-50).
  * logkv_flush_profiled is logkv_flush plus one cudaEventRecord (events are
  * cudaEvent_t as void*) before the first and after each of the
- * LOGKV_FLUSH_STAGES kernels stages: snapshot, span cut, span score, choose,
- * attach, plan, prepare, cascade, pool rewrite, window shift.
+ * LOGKV_FLUSH_STAGES kernels stages: snapshot, span cut, span scores with attach
+ * decisions, choose, seed + plan, prepare, cascade, pool rewrite, window shift.
  */
-#define LOGKV_FLUSH_STAGES 10
+#define LOGKV_FLUSH_STAGES 9
 LOGKV_API int logkv_flush_profiled(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
                                    int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream,
                                    void** events, int32_t n_events);

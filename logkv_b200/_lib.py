@@ -20,7 +20,7 @@ ERRORS = {-1: "shape out of the supported range", -2: "unsupported storage dtype
 
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1}
 
-FLUSH_STAGES = ("snapshot", "span_cut", "span_score", "choose", "attach", "plan", "prepare", "cascade",
+FLUSH_STAGES = ("snapshot", "span_cut", "score_attach", "choose", "seed_plan", "prepare", "cascade",
                 "pool_rewrite", "window_shift")
 COUNTERS = ("storage_read", "stage_read", "survivor", "fill", "clear", "carry", "gather", "flushes", "exact_cuts")
 

@@ -4,10 +4,10 @@
 // Launch sequence of one flush (all on the caller's stream, no host sync):
 //   K0 snapshot   old exact pool -> workspace
 //   K1 cut        candidate spans per batch row
-//   K2 score      Alpha / Beta span scores
+//   K2 score      Alpha / Beta span scores, and in the same launch
+//      attach     frozen-centroid decisions for every pool / window token
 //   K3 choose     bounded greedy, keep / archive lists, new span table
-//   K4 attach     frozen-centroid decisions per archived token
-//   K5 plan       farthest-point seeds, per-cluster grouping and jobs
+//   K5 plan       farthest-point seeds (archive rank order), per-cluster grouping and jobs
 //   K6a prepare   centroids, scalars, new / delayed cluster staging
 //   K6b cascade   ladder append with pairwise or Beta merges
 //   K7 pool       exact pool rewrite
@@ -60,6 +60,16 @@ static void launch_cascade(const Geo& g, const logkv_state_t& s, const Work& w, 
 }
 
 // ---------------------------------------------------------------- K8: window shift
+// Span scores and attach decisions in one launch: blocks [0, nscore) stride over the
+// span candidates, the rest take NW/ntok tokens each.  Both read only the snapshot and
+// the frozen cluster state, so attach leaves the critical path of the span choice.
+template <typename T>
+__global__ void __launch_bounds__(256) score_attach_kernel(Geo g, logkv_state_t s, Work w, int nscore) {
+  pdl_entry();
+  if ((int)blockIdx.x < nscore) score_body<T>(g, s, w, blockIdx.x, nscore);
+  else attach_body<T>(g, s, w, blockIdx.x - nscore);
+}
+
 template <typename T>
 __global__ void window_stage_kernel(Geo g, logkv_state_t s, Work w, int rem) {
   pdl_entry();
@@ -207,6 +217,7 @@ static size_t carve(const Geo& g, size_t esize, char* base, Work* w) {
   w->arch_idx = c.take<int32_t>(B * NW, 4);
   w->narch = c.take<int32_t>(B, 4);
   w->assign = c.take<int8_t>(B * G * NW, 1);
+  w->assign_tok = c.take<int8_t>(B * G * NW, 1);
   w->orphan = c.take<uint8_t>(B * G * NW, 1);
   w->s_winner = c.take<float>(B * G * NW, 4);
   w->tok_list = c.take<int32_t>(B * G * NW, 4);
@@ -269,10 +280,16 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   launch_pdl(alpha_cut_kernel, g.B, 1024, cut_smem, st, g, s, w);
   mark();
   const size_t score_smem = (64 * (size_t)(g.D + 1) + 2 * (size_t)g.D + 64 + (size_t)g.K) * sizeof(float);
-  if (score_smem > 48 * 1024)
-    cudaFuncSetAttribute(alpha_score_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)score_smem);
+  const int att_tok = 256 / (g.K <= 16 ? 16 : 32);
+  const size_t attach_smem =
+      ((size_t)(g.K + att_tok) * (g.D + 1) + 2 * (size_t)att_tok * g.K) * sizeof(float);
+  const size_t sa_smem = std::max(score_smem, attach_smem);
+  if (sa_smem > 48 * 1024)
+    cudaFuncSetAttribute(score_attach_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sa_smem);
   const int score_blocks = std::max(1, std::min(g.NC, 8 * sm_count / std::max(1, g.B * g.G) + 1));
-  launch_pdl(alpha_score_kernel<T>, dim3(score_blocks, g.G, g.B), 256, score_smem, st, g, s, w);
+  const int attach_blocks = (g.NW + att_tok - 1) / att_tok;
+  launch_pdl(score_attach_kernel<T>, dim3(score_blocks + attach_blocks, g.G, g.B), 256, sa_smem, st, g, s, w,
+             score_blocks);
   }
   if (!(phases & kPhaseCommit)) return (int)cudaGetLastError();
   mark();
@@ -280,13 +297,6 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   if (choose_smem > 48 * 1024)
     cudaFuncSetAttribute(alpha_choose_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)choose_smem);
   launch_pdl(alpha_choose_kernel, g.B, 1024, choose_smem, st, g, s, w);
-  mark();
-  const int att_tok = 256 / (g.K <= 16 ? 16 : 32);
-  const size_t attach_smem =
-      ((size_t)(g.K + att_tok) * (g.D + 1) + 2 * (size_t)att_tok * g.K) * sizeof(float);
-  if (attach_smem > 48 * 1024)
-    cudaFuncSetAttribute(attach_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attach_smem);
-  launch_pdl(attach_kernel<T>, dim3((g.NW + att_tok - 1) / att_tok, g.G, g.B), 256, attach_smem, st, g, s, w);
   mark();
   {
     // Seeding: one 8-CTA cluster per lane; rows staged in shared memory when they fit.

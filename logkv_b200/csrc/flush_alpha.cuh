@@ -204,13 +204,12 @@ __global__ void __launch_bounds__(1024) alpha_cut_kernel(Geo g, logkv_state_t s,
 }
 
 // ---------------------------------------------------------------- K2: span scores
-// One block per (candidate, group) in a grid-stride over candidates: the span's
+// One block per (candidate, group) in a stride of `nblk` blocks over candidates: the span's
 // rows are staged in shared memory (64 tokens at a time, 16-byte loads); mean
 // per feature and energy per token are left-to-right sums.  Output per
 // (row, candidate, group): Alpha parts (R_K, R_V) or Beta's per-group score.
 template <typename T>
-__global__ void __launch_bounds__(256) alpha_score_kernel(Geo g, logkv_state_t s, Work w) {
-  pdl_entry();
+__device__ void score_body(const Geo& g, const logkv_state_t& s, const Work& w, int blk, int nblk) {
   const int b = blockIdx.z, grp = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
   const int G = g.G, D = g.D, K = g.K;
   constexpr int VN = Vec<T>::N;
@@ -225,7 +224,7 @@ __global__ void __launch_bounds__(256) alpha_score_kernel(Geo g, logkv_state_t s
   const T* snap[2] = {static_cast<const T*>(w.snap_k), static_cast<const T*>(w.snap_v)};
   const T* rec[2] = {static_cast<const T*>(s.recent_k_raw), static_cast<const T*>(s.recent_v)};
   const int ncand = w.n_cand[b];
-  for (int ci = blockIdx.x; ci < ncand; ci += gridDim.x) {
+  for (int ci = blk; ci < ncand; ci += nblk) {
     const size_t cix = (size_t)b * g.NC + ci;
     const int s0 = w.cand_s0[cix], n0 = w.cand_n0[cix], s1 = w.cand_s1[cix], n1 = w.cand_n1[cix];
     const int n = n0 + n1;

@@ -60,9 +60,10 @@ struct Work {
   int32_t* nkeep;          // [B]
   int32_t* arch_idx;       // [B,NW] archived token indices, position order
   int32_t* narch;          // [B]
-  int8_t* assign;          // [B,G,NW] cluster per archived token (position rank)
-  uint8_t* orphan;         // [B,G,NW]
-  float* s_winner;         // [B,G,NW]
+  int8_t* assign;          // [B,G,NW] cluster per archived token (archive rank order)
+  int8_t* assign_tok;      // [B,G,NW] attach decision per token (token index order)
+  uint8_t* orphan;         // [B,G,NW] token index order
+  float* s_winner;         // [B,G,NW] token index order
   int32_t* tok_list;       // [B,G,NW] archive ranks grouped by cluster (stable)
   int32_t* plan_off;       // [B,G,K] offset into tok_list
   int32_t* plan_n;         // [B,G,K] tokens joining the cluster

@@ -14,21 +14,21 @@
 namespace logkv {
 
 // ---------------------------------------------------------------- K4: attach decisions
-// One thread per (archived token, cluster): each computes the token's dot product
-// and exact squared distance to one centre, left to right over the features; one
-// thread per token then walks the clusters in index order for the decision
-// (first-index argmin, as torch.argmin).  Token rows and centres are staged in
-// shared memory with an odd word stride (conflict-free).
+// Decisions for every token of the [old pool | flushed window] index space (the archive
+// is a subset, picked later by the span choice; decisions depend only on the frozen
+// cluster state).  One thread per (token, cluster): each computes the token's dot
+// product and exact squared distance to one centre, left to right over the features;
+// one thread per token then walks the clusters in index order for the decision
+// (first-index argmin, as torch.argmin).  Token rows and centres are staged in shared
+// memory with an odd word stride (conflict-free).  Outputs are indexed by token.
 template <typename T>
-__global__ void __launch_bounds__(256) attach_kernel(Geo g, logkv_state_t s, Work w) {
-  pdl_entry();
+__device__ void attach_body(const Geo& g, const logkv_state_t& s, const Work& w, int blk) {
   const int b = blockIdx.z, grp = blockIdx.y, tid = threadIdx.x;
   const int D = g.D, K = g.K;
   const int slots = K <= 16 ? 16 : 32;          // threads per token
   const int ntok = blockDim.x / slots;          // tokens per block
-  const int na = w.narch[b];
-  const int r0 = blockIdx.x * ntok;
-  if (r0 >= na) return;
+  const int r0 = blk * ntok;
+  if (r0 >= g.NW) return;
   extern __shared__ float sm[];
   float* mu = sm;                                // [K][D+1]
   float* xs = mu + K * (D + 1);                  // [ntok][D+1]
@@ -46,14 +46,13 @@ __global__ void __launch_bounds__(256) attach_kernel(Geo g, logkv_state_t s, Wor
   }
   const T* snap = static_cast<const T*>(w.snap_k);
   const T* rec = static_cast<const T*>(s.recent_k_raw);
-  const int* arch = w.arch_idx + (size_t)b * g.NW;
-  const int nrow = min(ntok, na - r0);
+  const int nrow = min(ntok, g.NW - r0);
   constexpr int VN = Vec<T>::N;
   const int DV = D / VN;
   for (int item = tid; item < nrow * DV; item += blockDim.x) {
     const int row = item / DV, v = item % DV;
     float xv[VN];
-    unpack(*reinterpret_cast<const uint4*>(token_row<T>(g, snap, rec, b, grp, arch[r0 + row]) + v * VN), xv,
+    unpack(*reinterpret_cast<const uint4*>(token_row<T>(g, snap, rec, b, grp, r0 + row) + v * VN), xv,
            (const T*)nullptr);
 #pragma unroll
     for (int e = 0; e < VN; ++e) xs[row * (D + 1) + v * VN + e] = xv[e];
@@ -86,8 +85,8 @@ __global__ void __launch_bounds__(256) attach_kernel(Geo g, logkv_state_t s, Wor
   }
   __syncthreads();
   if (c != 0 || tok >= nrow) return;
-  const int r = r0 + tok;
-  const int64_t pos = token_position(g, s, w, b, arch[r]);
+  const int r = r0 + tok;   // token index
+  const int64_t pos = token_position(g, s, w, b, r);
   const float xx = xxs[tok];
   const float thresh = fmul(g.lam, s.s_h[(size_t)b * g.G + grp]);
   float best_cost = INFINITY, s_win = 0.f, best_ex = INFINITY, sem0 = 0.f;
@@ -118,7 +117,7 @@ __global__ void __launch_bounds__(256) attach_kernel(Geo g, logkv_state_t s, Wor
   }
   const bool direct = any_alive && s_win <= thresh;
   const size_t o = ((size_t)b * g.G + grp) * g.NW + r;
-  w.assign[o] = (int8_t)(direct ? winner : nearest);
+  w.assign_tok[o] = (int8_t)(direct ? winner : nearest);
   w.orphan[o] = direct ? 0 : 1;
   w.s_winner[o] = s_win;
 }
@@ -178,9 +177,12 @@ __global__ void __cluster_dims__(kSeedCluster, 1, 1) __launch_bounds__(512) seed
   const int na = w.narch[b];
   const size_t lane0 = ((size_t)b * g.G + grp) * K;
   const size_t row0 = ((size_t)b * g.G + grp) * g.NW;
-  int8_t* asg = w.assign + row0;
-  const uint8_t* orph = w.orphan + row0;
+  int8_t* asg = w.assign + row0;                 // archive rank order (written here)
+  const int8_t* asg_tok = w.assign_tok + row0;   // token order (attach decisions)
+  const uint8_t* orph_tok = w.orphan + row0;     // token order
+  const float* swin_tok = w.s_winner + row0;     // token order
   const int* arch = w.arch_idx + (size_t)b * g.NW;
+  auto orph = [&](int t) -> int { return orph_tok[arch[t]]; };
   const T* snap = static_cast<const T*>(w.snap_k);
   const T* rec = static_cast<const T*>(s.recent_k_raw);
   __shared__ int free_slots[kMaxClusters];
@@ -197,14 +199,16 @@ __global__ void __cluster_dims__(kSeedCluster, 1, 1) __launch_bounds__(512) seed
     sh_norph = 0;
   }
   __syncthreads();
+  const int chunk = (na + kSeedCluster - 1) / kSeedCluster;
+  const int t_lo = min(na, rank * chunk), t_hi = min(na, t_lo + chunk), nloc = t_hi - t_lo;
+  // Decisions in archive rank order (orphans are overwritten below when seeds open).
+  for (int t = t_lo + tid; t < t_hi; t += nt) asg[t] = asg_tok[arch[t]];
   int my = 0;
-  for (int t = tid; t < na; t += nt) my += orph[t];
+  for (int t = tid; t < na; t += nt) my += orph(t);
   atomicAdd(&sh_norph, my);
   __syncthreads();
   const int n_use = min(sh_nfree, sh_norph);
   if (n_use == 0) return;  // same decision in every CTA of the cluster
-  const int chunk = (na + kSeedCluster - 1) / kSeedCluster;
-  const int t_lo = min(na, rank * chunk), t_hi = min(na, t_lo + chunk), nloc = t_hi - t_lo;
   // Dynamic shared memory: prow [D] f32 | mus [K][D+1] f32 | dist [chunk] f32 | cdist [chunk][K] f32 | rows.
   extern __shared__ float sm[];
   float* prow = sm;
@@ -233,7 +237,7 @@ __global__ void __cluster_dims__(kSeedCluster, 1, 1) __launch_bounds__(512) seed
     ArgMax a{-INFINITY, 0x7fffffff};
     for (int tl = tid; tl < nloc; tl += nt) {
       const int t = t_lo + tl;
-      const float v = i == 0 ? (orph[t] ? w.s_winner[row0 + t] : -INFINITY) : dist[tl];
+      const float v = i == 0 ? (orph(t) ? swin_tok[arch[t]] : -INFINITY) : dist[tl];
       a = argmax_better(a, ArgMax{v, t});
     }
     a = block_argmax(a, red);
@@ -256,7 +260,7 @@ __global__ void __cluster_dims__(kSeedCluster, 1, 1) __launch_bounds__(512) seed
         const float df = fsub(xval(tl, d), prow[d]);
         acc = fadd(acc, fmul(df, df));
       }
-      float v = i == 0 ? (orph[t] ? acc : -INFINITY) : fminf(dist[tl], acc);
+      float v = i == 0 ? (orph(t) ? acc : -INFINITY) : fminf(dist[tl], acc);
       if (t == pick) v = -INFINITY;  // a pick is never picked again
       dist[tl] = v;
     }
@@ -276,7 +280,7 @@ __global__ void __cluster_dims__(kSeedCluster, 1, 1) __launch_bounds__(512) seed
   for (int item = tid; item < nloc * K; item += nt) {
     const int tl = item / K, c = item % K;
     float out = INFINITY;
-    if (orph[t_lo + tl] && cand[c]) {
+    if (orph(t_lo + tl) && cand[c]) {
       float acc = 0.f;
       for (int d = 0; d < D; ++d) {
         const float df = fsub(xval(tl, d), mus[c * (D + 1) + d]);
@@ -288,7 +292,7 @@ __global__ void __cluster_dims__(kSeedCluster, 1, 1) __launch_bounds__(512) seed
   }
   __syncthreads();
   for (int tl = tid; tl < nloc; tl += nt) {
-    if (!orph[t_lo + tl]) continue;
+    if (!orph(t_lo + tl)) continue;
     float best = INFINITY;
     int bc = 0;
     for (int c = 0; c < K; ++c)
