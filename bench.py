@@ -72,6 +72,13 @@ class ClockSampler:
             self.thread.start()
         except (OSError, FileNotFoundError):
             self.proc = None
+            return self
+        # nvidia-smi takes a moment to start: wait for its first sample so that a short timed
+        # region is still covered.
+        t0 = time.time()
+        while not self.samples and time.time() - t0 < 5.0 and self.proc.poll() is None:
+            time.sleep(0.01)
+        self.n_start = len(self.samples)
         return self
 
     def _read(self):
@@ -82,6 +89,10 @@ class ClockSampler:
 
     def __exit__(self, *exc):
         if self.proc:
+            # one more sample at the end of the region (at most one sampling period away)
+            t0 = time.time()
+            while len(self.samples) <= getattr(self, "n_start", 0) and time.time() - t0 < 1.0:
+                time.sleep(0.01)
             self.proc.terminate()
             self.proc.wait(timeout=5)
 
@@ -146,14 +157,37 @@ def make_caches(torch, cfg, device, cos, sin):
     return caches
 
 
-def run_step(caches, layers, ends_host, ends_dev=None):
-    for cache in caches:
-        cache.reset_parameters()
+def run_step(caches, layers, ends_host, ends_dev=None, streams=None):
+    """One step: every layer's chunks in chunk-major order.
+
+    With ``streams``, layer l's cache is updated on ``streams[l % S]``: the layers' caches are
+    independent, so their flushes overlap (as in a model's prefill, where layer l's flush only
+    has to finish before layer l's next chunk).  The streams fork from and join back into the
+    current stream, so the step can be captured in one CUDA graph.
+    """
+    import torch
     n_chunks = len(layers[0])
+    if not streams:
+        for cache in caches:
+            cache.reset_parameters()
+        for c in range(n_chunks):
+            for cache, chunks in zip(caches, layers):
+                k, kr, v = chunks[c]
+                cache.add_recent(k, v, k_raw=kr, span_ends=ends_host, span_ends_device=ends_dev)
+        return
+    main = torch.cuda.current_stream()
+    for st in streams:
+        st.wait_stream(main)
+    for li, cache in enumerate(caches):
+        with torch.cuda.stream(streams[li % len(streams)]):
+            cache.reset_parameters()
     for c in range(n_chunks):
-        for cache, chunks in zip(caches, layers):
+        for li, (cache, chunks) in enumerate(zip(caches, layers)):
             k, kr, v = chunks[c]
-            cache.add_recent(k, v, k_raw=kr, span_ends=ends_host, span_ends_device=ends_dev)
+            with torch.cuda.stream(streams[li % len(streams)]):
+                cache.add_recent(k, v, k_raw=kr, span_ends=ends_host, span_ends_device=ends_dev)
+    for st in streams:
+        main.wait_stream(st)
 
 
 # ---------------------------------------------------------------------------------------------- our arm
@@ -168,14 +202,15 @@ def bench_ours(args, rank, world, local_rank):
     caches = make_caches(torch, cfg, device, cos, sin)
     flushes_per_step = cfg["layers"] * (cfg["tokens"] // cfg["chunk"] - cfg["recent"] // cfg["chunk"])
     stream = torch.cuda.Stream(device)
+    streams = [torch.cuda.Stream(device) for _ in range(args.streams)] if args.streams > 1 else None
     # Warm-up (eager), then one CUDA graph per step.
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
-            run_step(caches, layers, ends_host, ends_dev)
+            run_step(caches, layers, ends_host, ends_dev, streams)
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
-        run_step(caches, layers, ends_host, ends_dev)
+        run_step(caches, layers, ends_host, ends_dev, streams)
     with torch.cuda.stream(stream):
         for _ in range(max(1, args.warmup)):
             graph.replay()
@@ -248,43 +283,54 @@ def bench_ours(args, rank, world, local_rank):
 
     # e2e: public API, eager, host inputs copied each chunk.
     host = []
+    ends_pinned = ends_dev.cpu().pin_memory()
     for chunks in layers:
-        host.append([tuple(t[:, :, :].cpu().pin_memory() for t in chunks[c]) for c in range(2)])
-    # Two device slots; a copy stream fills slot n % 2 with layer-chunk n's inputs while the
-    # flush of layer-chunk n - 1 runs on `stream` (events order reuse of each slot).
-    dev_buf = [tuple(torch.empty_like(t) for t in layers[0][0]) for _ in range(2)]
+        host.append([tuple(t[:, :, :].cpu().pin_memory() for t in chunks[c]) + (ends_pinned,) for c in range(2)])
+    # A ring of device slots; a copy stream fills slot n % nslot with layer-chunk n's inputs
+    # (k, k_raw, v and the span-end flags) while earlier layer-chunks are flushed on their
+    # layers' streams (events order each slot's reuse).
+    nslot = 2 * max(1, args.streams)
+    dev_buf = [tuple(torch.empty_like(t, device=device) for t in host[0][0]) for _ in range(nslot)]
     copy_stream = torch.cuda.Stream(device)
-    filled = [torch.cuda.Event() for _ in range(2)]
-    consumed = [torch.cuda.Event() for _ in range(2)]
-    h2d_per_step = sum(t.numel() * t.element_size() for t in layers[0][0]) * len(layers) * len(layers[0])
+    filled = [torch.cuda.Event() for _ in range(nslot)]
+    consumed = [torch.cuda.Event() for _ in range(nslot)]
+    h2d_per_step = sum(t.numel() * t.element_size() for t in host[0][0]) * len(layers) * len(layers[0])
+    lstreams = streams or [stream]
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
     copy_stream.wait_stream(stream)
+    for st in lstreams:
+        st.wait_stream(stream)
     n = 0
     for _ in range(args.steps):
-        with torch.cuda.stream(stream):
-            for cache in caches:
+        for li, cache in enumerate(caches):
+            with torch.cuda.stream(lstreams[li % len(lstreams)]):
                 cache.reset_parameters()
         for c in range(len(layers[0])):
             for li, cache in enumerate(caches):
-                slot = n % 2
+                slot = n % nslot
                 buf = dev_buf[slot]
+                ls = lstreams[li % len(lstreams)]
                 with torch.cuda.stream(copy_stream):
-                    if n >= 2:
+                    if n >= nslot:
                         copy_stream.wait_event(consumed[slot])
                     for d, h in zip(buf, host[li][c % 2]):
                         d.copy_(h, non_blocking=True)
                     filled[slot].record(copy_stream)
-                with torch.cuda.stream(stream):
-                    stream.wait_event(filled[slot])
-                    cache.add_recent(buf[0], buf[2], k_raw=buf[1], span_ends=ends_host)
-                    consumed[slot].record(stream)
+                with torch.cuda.stream(ls):
+                    ls.wait_event(filled[slot])
+                    cache.add_recent(buf[0], buf[2], k_raw=buf[1], span_ends=ends_host, span_ends_device=buf[3])
+                    consumed[slot].record(ls)
                 n += 1
+        for st in lstreams:
+            stream.wait_stream(st)
         with torch.cuda.stream(stream):
-            readback = caches[-1]._alpha_count_dev.to("cpu", non_blocking=False)
+            readback = torch.stack([cache._alpha_count_dev for cache in caches]).to("cpu", non_blocking=False)
+        for st in lstreams:
+            st.wait_stream(stream)
     e_stop.record(stream)
     torch.cuda.synchronize()
     e_ms = e_start.elapsed_time(e_stop)
@@ -294,7 +340,7 @@ def bench_ours(args, rank, world, local_rank):
         e_ms = float(t.item())
     e2e_us = e_ms * 1000.0 / (args.steps * flushes_per_step)
     del readback
-    n_launch = flushes_per_step * 10 * args.steps
+    n_launch = flushes_per_step * 11 * args.steps   # 11 kernels per flush (no window staging here)
     return dict(value=us_per_flush * 1.0 / world, ms_per_step=ms_per_step, e2e_us=e2e_us / world,
                 h2d=h2d_per_step * world, stages=stages_us, stages_med=stages_med, stages_max=stages_max,
                 counters=delta, flushes_per_step=flushes_per_step,
@@ -563,6 +609,7 @@ def main():
     ap.add_argument("--layers", type=int, default=WORKLOAD["layers"], help="layer caches (profiling runs only)")
     ap.add_argument("--decode-steps", type=int, default=32, help="timed decode steps (0: skip the decode leg)")
     ap.add_argument("--decode-batch", type=int, default=DECODE["batch"], help="decode sequences (profiling runs only)")
+    ap.add_argument("--streams", type=int, default=14, help="streams the layers' flushes are spread over")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -570,6 +617,7 @@ def main():
     config = {k: WORKLOAD[k] for k in ("workload", "layers", "groups", "head_dim", "clusters", "B", "recent",
                                         "granularity", "exact", "span_cap", "tokens", "batch_per_rank")}
     config.update(layers=args.layers, parallelism=f"batch-sharded streams x{world}",
+                  layer_streams=args.streams,
                   l2="inputs larger than L2 (5.6 GB per step at 28 layers)")
     if args.impl == "reference":
         if rank != 0:
@@ -604,7 +652,7 @@ def main():
                     warmup=args.warmup, ms_per_step=round(res["ms_per_step"], 3), higher_is_better=False,
                     scaling="weak", vs_baseline=None, dtype="bf16", data="synthetic", config=config,
                     e2e={"value": round(res["e2e_us"], 2), "unit": "us", "h2d_bytes_per_step": res["h2d"],
-                         "d2h_bytes_per_step": 4},
+                         "d2h_bytes_per_step": 4 * args.layers * world},
                     roofline=res["roofline"], flush_roofline=res["flush_roofline"], cpu_baseline=cpu,
                     clocks=res["clocks"], gpu_launches=res["launches"], stages_us=res["stages"],
                     stages_us_median=res["stages_med"], stages_us_max=res["stages_max"],

@@ -180,8 +180,6 @@ class LogStructuredKVCache(nn.Module):
         self._span_count = torch.zeros(batch, dtype=torch.int32, **z)
         self._row_count = torch.zeros(batch, dtype=torch.int32, **z)
         self._alpha_count_dev = torch.zeros(1, dtype=torch.int32, **z)
-        self._recent_pos_host = [[0] * R for _ in range(batch)]
-        self._recent_span_ends = [[False] * R for _ in range(batch)]
         self.op_log = None
         self.op_log_len = None
         self._layout = _lib.Layout(batch, groups, k_dim, K, L, Bs, R, P, self.alpha_span_max_tokens,
@@ -200,7 +198,15 @@ class LogStructuredKVCache(nn.Module):
         self.profile_events = None   # set to a list of LOGKV_FLUSH_STAGES+1 torch.cuda.Event to time stages
 
     # ------------------------------------------------------------------ C-ABI state
+    def _apply(self, fn, *args, **kwargs):
+        self._state = None           # buffers move: the pointer table is rebuilt on next use
+        return super()._apply(fn, *args, **kwargs)
+
     def _state_struct(self) -> _lib.State:
+        """Device pointers of every state buffer (built once; rebuilt when the buffers move)."""
+        st = self._state
+        if st is not None and st.level_k == self.level_k.data_ptr() and st.recent_k == self.recent_k.data_ptr():
+            return st
         views = dict(level_k=self.level_k, level_v=self.level_v, level_w=self.level_w,
                      level_p_lo=self.level_p_lo, level_p_hi=self.level_p_hi, level_sum_wp=self.level_sum_wp,
                      level_order=self.level_order, pad_mask=self.pad_mask, level_count=self.level_count,
@@ -211,7 +217,8 @@ class LogStructuredKVCache(nn.Module):
                      alpha_pos=self.alpha_pos, alpha_valid=self.alpha_valid, alpha_span_len=self._span_len,
                      alpha_span_closed=self._span_closed, alpha_nspans=self._span_count,
                      alpha_rowcount=self._row_count, alpha_count=self._alpha_count_dev)
-        return _lib.State(**{name: _lib.ptr(t) for name, t in views.items()})
+        self._state = _lib.State(**{name: _lib.ptr(t) for name, t in views.items()})
+        return self._state
 
     def flush_device(self, take: int) -> None:
         """One device flush of the ``take`` oldest window tokens plus the window shift."""
@@ -265,21 +272,19 @@ class LogStructuredKVCache(nn.Module):
 
     # ------------------------------------------------------------------ window
     def _positions(self, n: int, input_pos):
+        """Absolute positions of the chunk's tokens as a [batch, n] int64 device tensor."""
         dev = self.recent_pos.device
         if input_pos is None:
-            host = [list(range(self.token_count, self.token_count + n)) for _ in range(self.batch_size)]
             return torch.arange(self.token_count, self.token_count + n, device=dev).unsqueeze(0).expand(
-                self.batch_size, -1), host
+                self.batch_size, -1)
         if input_pos.dim() == 1:
             if input_pos.numel() != n:
                 raise ValueError(f"input_pos length {input_pos.numel()} != chunk size {n}")
-            row = [int(x) for x in input_pos.detach().cpu().tolist()]
-            return input_pos.to(device=dev, dtype=torch.int64).unsqueeze(0).expand(self.batch_size, -1), \
-                [row[:] for _ in range(self.batch_size)]
+            return input_pos.to(device=dev, dtype=torch.int64).unsqueeze(0).expand(self.batch_size, -1)
         if input_pos.dim() == 2:
             if input_pos.shape != (self.batch_size, n):
                 raise ValueError(f"input_pos shape {tuple(input_pos.shape)} != ({self.batch_size}, {n})")
-            return input_pos.to(device=dev, dtype=torch.int64), [[int(x) for x in r] for r in input_pos.tolist()]
+            return input_pos.to(device=dev, dtype=torch.int64)
         raise ValueError(f"input_pos must be 1-D or 2-D, got shape {tuple(input_pos.shape)}")
 
     def add_recent(self, k, v, *, k_raw=None, input_pos=None, record_op_log=False, span_ends=None,
@@ -302,7 +307,7 @@ class LogStructuredKVCache(nn.Module):
             raise ValueError(f"k_raw shape {tuple(k_raw.shape)} does not match semantic cache shape")
         if span_ends is None or len(span_ends) != self.batch_size or any(len(r) != n for r in span_ends):
             raise ValueError("AlphaLogKV span boundaries must match the input batch and token count")
-        positions, positions_host = self._positions(n, input_pos)
+        positions = self._positions(n, input_pos)
         if self.token_count + n > self.max_seq_length:
             raise RuntimeError(f"LogStructuredKVCache: token overflow! token_count={self.token_count}, n={n}, "
                                f"max_seq_length={self.max_seq_length}.")
@@ -320,9 +325,6 @@ class LogStructuredKVCache(nn.Module):
         else:
             ends = torch.tensor(span_ends, dtype=torch.uint8)
             self._recent_ends[:, dst].copy_(ends.pin_memory() if self.recent_pos.is_cuda else ends, non_blocking=True)
-        for b in range(self.batch_size):
-            self._recent_pos_host[b][dst] = positions_host[b]
-            self._recent_span_ends[b][dst] = [bool(x) for x in span_ends[b]]
         self.recent_count += n
         overflow = self.recent_count - self.recent_size
         if overflow > 0:
@@ -333,13 +335,7 @@ class LogStructuredKVCache(nn.Module):
                 if take > self.recent_count:
                     raise RuntimeError(f"semantic LogKV cannot flush {take} tokens from recent_count={self.recent_count}")
                 self.flush_device(take)
-                remaining = self.recent_count - take
-                for b in range(self.batch_size):
-                    self._recent_pos_host[b][:remaining] = self._recent_pos_host[b][take:self.recent_count]
-                    self._recent_pos_host[b][remaining:self.recent_count] = [0] * take
-                    self._recent_span_ends[b][:remaining] = self._recent_span_ends[b][take:self.recent_count]
-                    self._recent_span_ends[b][remaining:self.recent_count] = [False] * take
-                self.recent_count = remaining
+                self.recent_count -= take
                 pending -= take
 
     # ------------------------------------------------------------------ read side
@@ -378,6 +374,14 @@ class LogStructuredKVCache(nn.Module):
         return self.current_segment.long().tolist()
 
     @property
+    def _recent_pos_host(self):
+        return self.recent_pos.tolist()
+
+    @property
+    def _recent_span_ends(self):
+        return [[bool(x) for x in r] for r in self._recent_ends.tolist()]
+
+    @property
     def _alpha_spans(self):
         lens, closed, count = self._span_len.tolist(), self._span_closed.tolist(), self._span_count.tolist()
         return [[(lens[b][i], bool(closed[b][i])) for i in range(count[b])] for b in range(self.batch_size)]
@@ -402,9 +406,6 @@ class LogStructuredKVCache(nn.Module):
         for t in (self._recent_ends, self._span_len, self._span_closed, self._span_count, self._row_count,
                   self._alpha_count_dev):
             t.zero_()
-        R = self.recent_capacity
-        self._recent_pos_host = [[0] * R for _ in range(self.batch_size)]
-        self._recent_span_ends = [[False] * R for _ in range(self.batch_size)]
         self.token_count = 0
         self.recent_count = 0
         self._ladder_epoch += 1

@@ -4,8 +4,8 @@
 // Launch sequence of one flush (all on the caller's stream, no host sync):
 //   K0 snapshot   old exact pool -> workspace
 //   K1 cut        candidate spans per batch row
-//   K2 score      Alpha / Beta span scores, and in the same launch
-//      attach     frozen-centroid decisions for every pool / window token
+//   K2 score      Alpha / Beta span scores
+//   K4 attach     frozen-centroid decisions for every pool / window token (runs beside K2)
 //   K3 choose     bounded greedy, keep / archive lists, new span table
 //   K5 plan       farthest-point seeds (archive rank order), per-cluster grouping and jobs
 //   K6a prepare   centroids, scalars, new / delayed cluster staging
@@ -26,6 +26,23 @@ namespace logkv {
 // Greedy span choice: per candidate density, size, rank, flags; victims in two buffers.
 static size_t choose_smem_bytes(const Geo& g) {
   return (size_t)g.NC * (8 + 4 + 4 + 2) + 2 * (size_t)(g.P + 1) * (8 + 4 + 4) + (size_t)(g.P + 1) * (8 + 4) + 16;
+}
+
+// Span scores (staged K and V rows, means, token energies, centre distances and, with Beta,
+// the lane's centres) and attach decisions (centres, 8 or 16 token rows, per-pair scores).
+static size_t score_smem_bytes(const Geo& g, size_t esize) {
+  const size_t ws = (size_t)g.D * esize / 4 + 1;  // staged row: words, odd stride
+  return 2 * kScoreRows * ws * 4 +
+         (2 * (size_t)g.D + 2 * kScoreRows + 2 * (size_t)g.K + (g.beta ? (size_t)g.K * g.D : 0)) * sizeof(float);
+}
+static size_t attach_smem_bytes(const Geo& g) {
+  const size_t att_tok = 256 / (g.K <= 16 ? 16 : 32);
+  return ((size_t)(g.K + att_tok) * (g.D + 4) + 3 * att_tok * g.K) * sizeof(float);
+}
+// Delayed re-insert sort keys, token sources and the staged rows of the centroid sum.
+static size_t prep_smem_bytes(const Geo& g, size_t esize) {
+  return (size_t)g.sort_cap * sizeof(unsigned long long) + (size_t)((g.NW + 3) & ~3) * sizeof(int) +
+         (size_t)kPrepRows * g.D * esize;
 }
 
 static size_t cascade_smem(const Geo& g, size_t esize) {
@@ -59,29 +76,41 @@ static void launch_cascade(const Geo& g, const logkv_state_t& s, const Work& w, 
   launch_pdl(cascade_kernel<T, BETA, DC>, dim3(g.K, g.G, g.B), 512, smem, st, g, s, w);
 }
 
-// ---------------------------------------------------------------- K8: window shift
-// Span scores and attach decisions in one launch: blocks [0, nscore) stride over the
-// span candidates, the rest take NW/ntok tokens each.  Both read only the snapshot and
-// the frozen cluster state, so attach leaves the critical path of the span choice.
+// Span scores: blocks stride over the span candidates.
 template <typename T>
-__global__ void __launch_bounds__(256) score_attach_kernel(Geo g, logkv_state_t s, Work w, int nscore) {
+__global__ void __launch_bounds__(256) score_kernel(Geo g, logkv_state_t s, Work w) {
   pdl_entry();
-  if ((int)blockIdx.x < nscore) score_body<T>(g, s, w, blockIdx.x, nscore);
-  else attach_body<T>(g, s, w, blockIdx.x - nscore);
+  score_body<T>(g, s, w, blockIdx.x, gridDim.x);
 }
 
+// Attach decisions run beside the span scores.  They read the snapshot (complete before any
+// score block passed its entry wait, which is what let this grid launch) and the frozen
+// cluster state, so the entry wait is skipped; the wait comes at the end instead, so this
+// grid completes only after the score grid and the next kernel's entry wait covers both.
+template <typename T>
+__global__ void __launch_bounds__(256) attach_kernel(Geo g, logkv_state_t s, Work w) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  attach_body<T>(g, s, w, blockIdx.x);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- K8: window shift
+// The window's K, K_raw and V rows move in 16-byte units (a row is a whole number of them).
 template <typename T>
 __global__ void window_stage_kernel(Geo g, logkv_state_t s, Work w, int rem) {
   pdl_entry();
   // copy [F, F+rem) -> staging [0, rem) when source and destination overlap
+  constexpr int VN = Vec<T>::N;
   const int b = blockIdx.z, grp = blockIdx.y;
-  const size_t base = ((size_t)b * g.G + grp) * g.cap2R * g.D;
-  const size_t n = (size_t)rem * g.D;
+  const size_t base = ((size_t)b * g.G + grp) * g.cap2R * g.D / VN;
+  const size_t n = (size_t)rem * g.D / VN, off = (size_t)g.F * g.D / VN;
+  const uint4* rk = static_cast<const uint4*>(s.recent_k);
+  const uint4* rkr = static_cast<const uint4*>(s.recent_k_raw);
+  const uint4* rv = static_cast<const uint4*>(s.recent_v);
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-    const size_t src = base + (size_t)g.F * g.D + i;
-    static_cast<T*>(w.wk)[base + i] = static_cast<const T*>(s.recent_k)[src];
-    static_cast<T*>(w.wkr)[base + i] = static_cast<const T*>(s.recent_k_raw)[src];
-    static_cast<T*>(w.wv)[base + i] = static_cast<const T*>(s.recent_v)[src];
+    static_cast<uint4*>(w.wk)[base + i] = rk[base + off + i];
+    static_cast<uint4*>(w.wkr)[base + i] = rkr[base + off + i];
+    static_cast<uint4*>(w.wv)[base + i] = rv[base + off + i];
   }
   if (grp == 0 && blockIdx.x == 0)
     for (int i = threadIdx.x; i < rem; i += blockDim.x) {
@@ -93,17 +122,19 @@ __global__ void window_stage_kernel(Geo g, logkv_state_t s, Work w, int rem) {
 template <typename T>
 __global__ void window_shift_kernel(Geo g, logkv_state_t s, Work w, int rem, int staged) {
   pdl_entry();
+  constexpr int VN = Vec<T>::N;
   const int b = blockIdx.z, grp = blockIdx.y;
-  const size_t base = ((size_t)b * g.G + grp) * g.cap2R * g.D;
-  const size_t n = (size_t)g.recent_count * g.D;
-  T* rk = static_cast<T*>(s.recent_k);
-  T* rkr = static_cast<T*>(s.recent_k_raw);
-  T* rv = static_cast<T*>(s.recent_v);
-  const T* sk = staged ? static_cast<const T*>(w.wk) : rk;
-  const T* skr = staged ? static_cast<const T*>(w.wkr) : rkr;
-  const T* sv = staged ? static_cast<const T*>(w.wv) : rv;
-  const size_t F = (size_t)g.F * g.D, R = (size_t)rem * g.D;
-  // Without staging (rem <= F) element j of [F, count) is read and then zeroed by
+  const size_t base = ((size_t)b * g.G + grp) * g.cap2R * g.D / VN;
+  const size_t n = (size_t)g.recent_count * g.D / VN;
+  uint4* rk = static_cast<uint4*>(s.recent_k);
+  uint4* rkr = static_cast<uint4*>(s.recent_k_raw);
+  uint4* rv = static_cast<uint4*>(s.recent_v);
+  const uint4* sk = staged ? static_cast<const uint4*>(w.wk) : rk;
+  const uint4* skr = staged ? static_cast<const uint4*>(w.wkr) : rkr;
+  const uint4* sv = staged ? static_cast<const uint4*>(w.wv) : rv;
+  const size_t F = (size_t)g.F * g.D / VN, R = (size_t)rem * g.D / VN;
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  // Without staging (rem <= F) unit j of [F, count) is read and then zeroed by
   // the same thread; [rem, F) is never read.  With staging every source is a copy.
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     if (staged) {
@@ -112,22 +143,22 @@ __global__ void window_shift_kernel(Geo g, logkv_state_t s, Work w, int rem, int
         rkr[base + i] = skr[base + i];
         rv[base + i] = sv[base + i];
       } else {
-        rk[base + i] = Elem<T>::zero();
-        rkr[base + i] = Elem<T>::zero();
-        rv[base + i] = Elem<T>::zero();
+        rk[base + i] = zero;
+        rkr[base + i] = zero;
+        rv[base + i] = zero;
       }
     } else if (i >= F) {
-      const T a = rk[base + i], c = rkr[base + i], e = rv[base + i];
+      const uint4 a = rk[base + i], c = rkr[base + i], e = rv[base + i];
       rk[base + i - F] = a;
       rkr[base + i - F] = c;
       rv[base + i - F] = e;
-      rk[base + i] = Elem<T>::zero();
-      rkr[base + i] = Elem<T>::zero();
-      rv[base + i] = Elem<T>::zero();
+      rk[base + i] = zero;
+      rkr[base + i] = zero;
+      rv[base + i] = zero;
     } else if (i >= R) {
-      rk[base + i] = Elem<T>::zero();
-      rkr[base + i] = Elem<T>::zero();
-      rv[base + i] = Elem<T>::zero();
+      rk[base + i] = zero;
+      rkr[base + i] = zero;
+      rv[base + i] = zero;
     }
   }
   if (grp == 0 && blockIdx.x == 0) {
@@ -220,6 +251,7 @@ static size_t carve(const Geo& g, size_t esize, char* base, Work* w) {
   w->assign_tok = c.take<int8_t>(B * G * NW, 1);
   w->orphan = c.take<uint8_t>(B * G * NW, 1);
   w->s_winner = c.take<float>(B * G * NW, 4);
+  w->cnorm = c.take<float>(B * G * K, 4);
   w->tok_list = c.take<int32_t>(B * G * NW, 4);
   w->plan_off = c.take<int32_t>(B * G * K, 4);
   w->plan_n = c.take<int32_t>(B * G * K, 4);
@@ -270,7 +302,7 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
     ++stage;
   };
   const int sm_count = 148;
-  const int per_bg = std::max(1, std::min(64, (g.P * g.D + 255) / 256));
+  const int per_bg = std::max(1, std::min(64, (g.P * g.D / (int)(16 / sizeof(T)) + 255) / 256));
   if (phases & kPhaseScores) {
   mark();
   launch_pdl(snapshot_kernel<T>, dim3(per_bg, g.G, g.B), 256, 0, st, g, s, w);
@@ -279,17 +311,16 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   if (cut_smem > 48 * 1024) cudaFuncSetAttribute(alpha_cut_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cut_smem);
   launch_pdl(alpha_cut_kernel, g.B, 1024, cut_smem, st, g, s, w);
   mark();
-  const size_t score_smem = (64 * (size_t)(g.D + 1) + 2 * (size_t)g.D + 64 + (size_t)g.K) * sizeof(float);
-  const int att_tok = 256 / (g.K <= 16 ? 16 : 32);
-  const size_t attach_smem =
-      ((size_t)(g.K + att_tok) * (g.D + 1) + 2 * (size_t)att_tok * g.K) * sizeof(float);
-  const size_t sa_smem = std::max(score_smem, attach_smem);
-  if (sa_smem > 48 * 1024)
-    cudaFuncSetAttribute(score_attach_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sa_smem);
+  const size_t score_smem = score_smem_bytes(g, sizeof(T));
+  if (score_smem > 48 * 1024)
+    cudaFuncSetAttribute(score_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)score_smem);
   const int score_blocks = std::max(1, std::min(g.NC, 8 * sm_count / std::max(1, g.B * g.G) + 1));
-  const int attach_blocks = (g.NW + att_tok - 1) / att_tok;
-  launch_pdl(score_attach_kernel<T>, dim3(score_blocks + attach_blocks, g.G, g.B), 256, sa_smem, st, g, s, w,
-             score_blocks);
+  launch_pdl(score_kernel<T>, dim3(score_blocks, g.G, g.B), 256, score_smem, st, g, s, w);
+  const int att_tok = 256 / (g.K <= 16 ? 16 : 32);
+  const size_t attach_smem = attach_smem_bytes(g);
+  if (attach_smem > 48 * 1024)
+    cudaFuncSetAttribute(attach_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attach_smem);
+  launch_pdl(attach_kernel<T>, dim3((g.NW + att_tok - 1) / att_tok, g.G, g.B), 256, attach_smem, st, g, s, w);
   }
   if (!(phases & kPhaseCommit)) return (int)cudaGetLastError();
   mark();
@@ -312,7 +343,7 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   }
   launch_pdl(plan_kernel<T>, dim3(g.G, g.B), 1024, 0, st, g, s, w);
   mark();
-  const size_t prep_smem = (size_t)g.sort_cap * sizeof(unsigned long long) + (size_t)g.NW * sizeof(int);
+  const size_t prep_smem = prep_smem_bytes(g, sizeof(T));
   if (prep_smem > 48 * 1024)
     cudaFuncSetAttribute(prepare_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
   launch_pdl(prepare_kernel<T>, dim3(g.K, g.G, g.B), 256, prep_smem, st, g, s, w);
@@ -331,7 +362,7 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   launch_pdl(pool_rewrite_kernel<T>, dim3(per_bg, g.G, g.B), 256, 0, st, g, s, w);
   mark();
   const int rem = g.recent_count - g.F;
-  const int per_win = std::max(1, std::min(128, (g.recent_count * g.D + 255) / 256));
+  const int per_win = std::max(1, std::min(128, (g.recent_count * g.D / (int)(16 / sizeof(T)) + 255) / 256));
   const int staged = rem > g.F ? 1 : 0;
   if (staged) launch_pdl(window_stage_kernel<T>, dim3(per_win, g.G, g.B), 256, 0, st, g, s, w, rem);
   launch_pdl(window_shift_kernel<T>, dim3(per_win, g.G, g.B), 256, 0, st, g, s, w, rem, staged);
@@ -345,6 +376,20 @@ static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, i
   const int v = validate(layout, flush_tokens);
   if (v != LOGKV_OK) return v;
   if (!state || !workspace) return LOGKV_E_POINTER;
+  // Rows move in 16-byte units: every K/V buffer, the centres and the workspace start on a
+  // 16-byte boundary; the other buffers at least on their element size.
+  auto a16 = [](const void* p) { return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  auto a8 = [](const void* p) { return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 7) == 0; };
+  auto a4 = [](const void* p) { return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 3) == 0; };
+  const logkv_state_t& S = *state;
+  if (!a16(workspace) || !a16(S.level_k) || !a16(S.level_v) || !a16(S.centroid) || !a16(S.recent_k) ||
+      !a16(S.recent_k_raw) || !a16(S.recent_v) || !a16(S.alpha_k_raw) || !a16(S.alpha_v) || !a4(S.level_w) ||
+      !a8(S.level_p_lo) || !a8(S.level_p_hi) || !a8(S.level_sum_wp) || !a8(S.level_order) || !S.pad_mask ||
+      !S.level_count || !a4(S.n_eff) || !a4(S.n_total) || !a8(S.p_hi_c) || !a4(S.level0_phase) || !S.alive ||
+      !a4(S.s_h) || !a8(S.recent_pos) || !S.recent_ends || !a8(S.alpha_pos) || !S.alpha_valid ||
+      !a4(S.alpha_span_len) || !S.alpha_span_closed || !a4(S.alpha_nspans) || !a4(S.alpha_rowcount) ||
+      !a4(S.alpha_count))
+    return LOGKV_E_POINTER;
   if (recent_count < flush_tokens || recent_count > layout->recent_capacity) return LOGKV_E_SHAPE;
   const size_t esize = layout->dtype == LOGKV_DTYPE_BF16 ? 2 : 4;
   if (ranks < 1 || (ranks > 1 && !gpart_all)) return LOGKV_E_POINTER;
@@ -353,8 +398,8 @@ static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, i
   Work w{};
   const size_t need = carve(g, esize, static_cast<char*>(workspace), &w);
   if (workspace_bytes < need) return LOGKV_E_WORKSPACE;
-  if (cascade_smem(g, esize) > 227 * 1024 || (size_t)g.sort_cap * 8 + (size_t)g.NW * 4 > 227 * 1024 ||
-      choose_smem_bytes(g) > 227 * 1024)
+  if (cascade_smem(g, esize) > 227 * 1024 || prep_smem_bytes(g, esize) > 227 * 1024 ||
+      choose_smem_bytes(g) > 227 * 1024 || score_smem_bytes(g, esize) > 227 * 1024 || attach_smem_bytes(g) > 227 * 1024)
     return LOGKV_E_SMEM;
   w.gpart_all = gpart_all;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -18,14 +18,31 @@ template <typename T>
 __global__ void snapshot_kernel(Geo g, logkv_state_t s, Work w) {
   pdl_entry();
   const int b = blockIdx.z, grp = blockIdx.y;
-  const size_t n = (size_t)g.P * g.D;
-  const T* ksrc = static_cast<const T*>(s.alpha_k_raw) + ((size_t)b * g.G + grp) * n;
-  const T* vsrc = static_cast<const T*>(s.alpha_v) + ((size_t)b * g.G + grp) * n;
-  T* kdst = static_cast<T*>(w.snap_k) + ((size_t)b * g.G + grp) * n;
-  T* vdst = static_cast<T*>(w.snap_v) + ((size_t)b * g.G + grp) * n;
+  const size_t n = (size_t)g.P * g.D / Vec<T>::N;  // 16-byte units (rows are whole units)
+  const uint4* ksrc = static_cast<const uint4*>(s.alpha_k_raw) + ((size_t)b * g.G + grp) * n;
+  const uint4* vsrc = static_cast<const uint4*>(s.alpha_v) + ((size_t)b * g.G + grp) * n;
+  uint4* kdst = static_cast<uint4*>(w.snap_k) + ((size_t)b * g.G + grp) * n;
+  uint4* vdst = static_cast<uint4*>(w.snap_v) + ((size_t)b * g.G + grp) * n;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     kdst[i] = ksrc[i];
     vdst[i] = vsrc[i];
+  }
+  if (blockIdx.x == 0) {
+    // Squared norms of the lane's frozen centres (attach and Beta novelty read them).
+    const size_t lane0 = ((size_t)b * g.G + grp) * g.K;
+    for (int c = threadIdx.x; c < g.K; c += blockDim.x) {
+      const float4* mu = reinterpret_cast<const float4*>(s.centroid + (lane0 + c) * g.D);  // D % 4 == 0
+      float mm = 0.f;
+#pragma unroll 4
+      for (int d4 = 0; d4 < g.D / 4; ++d4) {
+        const float4 v = mu[d4];
+        mm = fadd(mm, fmul(v.x, v.x));
+        mm = fadd(mm, fmul(v.y, v.y));
+        mm = fadd(mm, fmul(v.z, v.z));
+        mm = fadd(mm, fmul(v.w, v.w));
+      }
+      w.cnorm[lane0 + c] = mm;
+    }
   }
   if (grp == 0 && blockIdx.x == 0) {
     for (int i = threadIdx.x; i < g.P; i += blockDim.x) w.snap_pos[(size_t)b * g.P + i] = s.alpha_pos[(size_t)b * g.P + i];
@@ -204,76 +221,118 @@ __global__ void __launch_bounds__(1024) alpha_cut_kernel(Geo g, logkv_state_t s,
 }
 
 // ---------------------------------------------------------------- K2: span scores
-// One block per (candidate, group) in a stride of `nblk` blocks over candidates: the span's
-// rows are staged in shared memory (64 tokens at a time, 16-byte loads); mean
-// per feature and energy per token are left-to-right sums.  Output per
-// (row, candidate, group): Alpha parts (R_K, R_V) or Beta's per-group score.
+// One block per (candidate, group) in a stride of `nblk` blocks over candidates.  The span's
+// K and V rows are staged together in shared memory (kScoreRows tokens at a time, 32-bit
+// words with an odd row stride, so per-row and per-feature walks are conflict-free); the
+// block's two halves then reduce K and V concurrently: mean per feature and energy per token
+// as left-to-right sums.  Output per (row, candidate, group): Alpha parts (R_K, R_V) or
+// Beta's per-group score.
+constexpr int kScoreRows = 64;  // staged tokens per pass
+constexpr int kScoreFeat = 8;   // features per thread of a half block (D <= 1024, 256 threads)
+
+template <typename T>
+__device__ __forceinline__ float staged_elem(const uint32_t* row, int d) {
+  if (sizeof(T) == 4) return __uint_as_float(row[d]);
+  const uint32_t wd = row[d >> 1];
+  return __uint_as_float((d & 1) ? (wd & 0xffff0000u) : (wd << 16));  // bf16 -> f32 is exact
+}
+
 template <typename T>
 __device__ void score_body(const Geo& g, const logkv_state_t& s, const Work& w, int blk, int nblk) {
   const int b = blockIdx.z, grp = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
   const int G = g.G, D = g.D, K = g.K;
+  const int warp = tid >> 5, lane = tid & 31, nwarps = nt >> 5;
   constexpr int VN = Vec<T>::N;
   const int DV = D / VN;
+  const int WPR = D * (int)sizeof(T) / 4, WS = WPR + 1;  // words per row, odd word stride
   extern __shared__ float sm[];
-  float* rows = sm;                          // [64][D + 1]
-  float* kmean = rows + 64 * (D + 1);        // [D]
-  float* mean = kmean + D;                   // [D]
-  float* etok = mean + D;                    // [64]
-  float* cdist = etok + 64;                  // [K]
-  __shared__ float sh_part[2], sh_kener, sh_kms;
-  const T* snap[2] = {static_cast<const T*>(w.snap_k), static_cast<const T*>(w.snap_v)};
-  const T* rec[2] = {static_cast<const T*>(s.recent_k_raw), static_cast<const T*>(s.recent_v)};
+  uint32_t* rows = reinterpret_cast<uint32_t*>(sm);                     // [2][kScoreRows][WS]
+  float* mean = reinterpret_cast<float*>(rows + 2 * kScoreRows * WS);  // [2][D]
+  float* etok = mean + 2 * D;                                           // [2][kScoreRows]
+  float* cdist = etok + 2 * kScoreRows;                                 // [K]
+  float* cmm = cdist + K;                                               // [K] mean square of each centre
+  float* cent = cmm + K;                                                // [K][D] centres (Beta)
+  __shared__ float sh_part[2], sh_ener[2], sh_ms[2];
+  const int half = nt >> 1, comp = tid >= half ? 1 : 0, htid = tid - comp * half;
+  const T* snapk = static_cast<const T*>(w.snap_k);
+  const T* snapv = static_cast<const T*>(w.snap_v);
+  const T* reck = static_cast<const T*>(s.recent_k_raw);
+  const T* recv = static_cast<const T*>(s.recent_v);
   const int ncand = w.n_cand[b];
+  const size_t lane0 = ((size_t)b * G + grp) * K;
+  if (g.beta && blk < ncand) {
+    // The lane's centres and their mean squares, once per block (frozen during the flush).
+    for (int i = tid; i < K * D; i += nt) cent[i] = s.centroid[lane0 * D + i];
+    for (int c = tid; c < K; c += nt) cmm[c] = fdiv(w.cnorm[lane0 + c], (float)D);
+  }
   for (int ci = blk; ci < ncand; ci += nblk) {
     const size_t cix = (size_t)b * g.NC + ci;
     const int s0 = w.cand_s0[cix], n0 = w.cand_n0[cix], s1 = w.cand_s1[cix], n1 = w.cand_n1[cix];
     const int n = n0 + n1;
     const float fn = (float)n;
-    for (int comp = 0; comp < 2; ++comp) {
-      float acc = 0.f, eacc = 0.f;
-      for (int c0 = 0; c0 < n; c0 += 64) {
-        const int cn = min(64, n - c0);
-        for (int item = tid; item < cn * DV; item += nt) {
-          const int t = item / DV, v = item % DV;
-          const int tt = c0 + t;
-          const int src = tt < n0 ? s0 + tt : s1 + (tt - n0);
-          float xv[VN];
-          unpack(*reinterpret_cast<const uint4*>(token_row<T>(g, snap[comp], rec[comp], b, grp, src) + v * VN), xv,
-                 (const T*)nullptr);
+    float acc[kScoreFeat];
 #pragma unroll
-          for (int e = 0; e < VN; ++e) rows[t * (D + 1) + v * VN + e] = xv[e];
+    for (int j = 0; j < kScoreFeat; ++j) acc[j] = 0.f;
+    float eacc = 0.f;
+    const uint32_t* R = rows + comp * kScoreRows * WS;
+    for (int c0 = 0; c0 < n; c0 += kScoreRows) {
+      const int cn = min(kScoreRows, n - c0);
+      for (int r = warp; r < 2 * cn; r += nwarps) {
+        const int f = r >= cn ? 1 : 0, t = r - f * cn;
+        const int tt = c0 + t;
+        const int src = tt < n0 ? s0 + tt : s1 + (tt - n0);
+        const T* row = f ? token_row<T>(g, snapv, recv, b, grp, src) : token_row<T>(g, snapk, reck, b, grp, src);
+        uint32_t* dst = rows + (f * kScoreRows + t) * WS;
+        for (int v = lane; v < DV; v += 32) {
+          const uint4 u = *reinterpret_cast<const uint4*>(row + v * VN);
+          dst[4 * v] = u.x;
+          dst[4 * v + 1] = u.y;
+          dst[4 * v + 2] = u.z;
+          dst[4 * v + 3] = u.w;
         }
-        __syncthreads();
-        if (tid < D)
-          for (int t = 0; t < cn; ++t) acc = fadd(acc, rows[t * (D + 1) + tid]);
-        for (int t = tid; t < cn; t += nt) {
-          float e = 0.f;
-          for (int d = 0; d < D; ++d) e = fadd(e, fmul(rows[t * (D + 1) + d], rows[t * (D + 1) + d]));
-          etok[t] = fdiv(e, (float)D);
-        }
-        __syncthreads();
-        if (tid == 0)
-          for (int t = 0; t < cn; ++t) eacc = fadd(eacc, etok[t]);
-        __syncthreads();
-      }
-      if (tid < D) {
-        mean[tid] = fdiv(acc, fn);
-        if (comp == 0) kmean[tid] = mean[tid];
       }
       __syncthreads();
-      if (tid == 0) {
-        const float energy = fdiv(eacc, fn);
-        float ms = 0.f;
-        for (int d = 0; d < D; ++d) ms = fadd(ms, fmul(mean[d], mean[d]));
-        ms = fdiv(ms, (float)D);
-        sh_part[comp] = fdiv(fmaxf(fsub(energy, ms), 0.f), fmaxf(energy, 1e-12f));
-        if (comp == 0) {
-          sh_kener = energy;
-          sh_kms = ms;
+#pragma unroll
+      for (int j = 0; j < kScoreFeat; ++j) {
+        const int d = htid + j * half;
+        if (d < D) {
+#pragma unroll 8
+          for (int t = 0; t < cn; ++t) acc[j] = fadd(acc[j], staged_elem<T>(R + t * WS, d));
         }
       }
+      for (int t = htid; t < cn; t += half) {
+        const uint32_t* row = R + t * WS;
+        float e = 0.f;
+#pragma unroll 8
+        for (int d = 0; d < D; ++d) {
+          const float x = staged_elem<T>(row, d);
+          e = fadd(e, fmul(x, x));
+        }
+        etok[comp * kScoreRows + t] = fdiv(e, (float)D);
+      }
+      __syncthreads();
+      if (htid == 0)
+        for (int t = 0; t < cn; ++t) eacc = fadd(eacc, etok[comp * kScoreRows + t]);
       __syncthreads();
     }
+#pragma unroll
+    for (int j = 0; j < kScoreFeat; ++j) {
+      const int d = htid + j * half;
+      if (d < D) mean[comp * D + d] = fdiv(acc[j], fn);
+    }
+    __syncthreads();
+    if (htid == 0) {
+      const float energy = fdiv(eacc, fn);
+      const float* mc = mean + comp * D;
+      float ms = 0.f;
+#pragma unroll 8
+      for (int d = 0; d < D; ++d) ms = fadd(ms, fmul(mc[d], mc[d]));
+      ms = fdiv(ms, (float)D);
+      sh_part[comp] = fdiv(fmaxf(fsub(energy, ms), 0.f), fmaxf(energy, 1e-12f));
+      sh_ener[comp] = energy;
+      sh_ms[comp] = ms;
+    }
+    __syncthreads();
     float* out = w.gpart + (cix * G + grp) * 2;
     if (!g.beta) {
       if (tid == 0) {
@@ -284,19 +343,15 @@ __device__ void score_body(const Geo& g, const logkv_state_t& s, const Work& w, 
       continue;
     }
     // Beta novelty: mean-square distance of the key mean to every live centre.
-    const size_t lane0 = ((size_t)b * G + grp) * K;
     for (int c = tid; c < K; c += nt) {
       float dist = INFINITY;
       if (s.alive[lane0 + c]) {
-        const float* mu = s.centroid + (lane0 + c) * D;
-        float dot = 0.f, mm = 0.f;
-        for (int d = 0; d < D; ++d) {
-          dot = fadd(dot, fmul(kmean[d], mu[d]));
-          mm = fadd(mm, fmul(mu[d], mu[d]));
-        }
+        const float* mu = cent + c * D;
+        float dot = 0.f;
+#pragma unroll 8
+        for (int d = 0; d < D; ++d) dot = fadd(dot, fmul(mean[d], mu[d]));
         dot = fdiv(dot, (float)D);
-        mm = fdiv(mm, (float)D);
-        dist = fmaxf(fsub(fadd(sh_kms, mm), fmul(2.f, dot)), 0.f);
+        dist = fmaxf(fsub(fadd(sh_ms[0], cmm[c]), fmul(2.f, dot)), 0.f);
       }
       cdist[c] = dist;
     }
@@ -309,7 +364,7 @@ __device__ void score_body(const Geo& g, const logkv_state_t& s, const Work& w, 
         nr = fminf(nr, cdist[c]);
       }
       if (!any) nr = 0.f;
-      const float nov = fdiv(nr, fmaxf(sh_kener, 1e-12f));
+      const float nov = fdiv(nr, fmaxf(sh_ener[0], 1e-12f));
       out[0] = fadd(fmul(fadd(sh_part[0], sh_part[1]), 0.5f), fdiv(nov, fadd(1.f, nov)));
     }
     __syncthreads();
@@ -657,17 +712,19 @@ __global__ void pool_rewrite_kernel(Geo g, logkv_state_t s, Work w) {
   const T* snapv = static_cast<const T*>(w.snap_v);
   const T* reck = static_cast<const T*>(s.recent_k_raw);
   const T* recv = static_cast<const T*>(s.recent_v);
-  const size_t total = (size_t)g.P * g.D;
+  constexpr int VN = Vec<T>::N;
+  const int DV = g.D / VN;
+  const size_t total = (size_t)g.P * DV;  // 16-byte units
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
-    const int row = (int)(i / g.D), d = (int)(i % g.D);
+    const int row = (int)(i / DV), d = (int)(i % DV) * VN;
+    uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
     if (row < nkeep) {
       const int src = w.keep_idx[(size_t)b * g.P + row];
-      kdst[i] = token_row<T>(g, snapk, reck, b, grp, src)[d];
-      vdst[i] = token_row<T>(g, snapv, recv, b, grp, src)[d];
-    } else {
-      kdst[i] = Elem<T>::zero();
-      vdst[i] = Elem<T>::zero();
+      kv = *reinterpret_cast<const uint4*>(token_row<T>(g, snapk, reck, b, grp, src) + d);
+      vv = *reinterpret_cast<const uint4*>(token_row<T>(g, snapv, recv, b, grp, src) + d);
     }
+    reinterpret_cast<uint4*>(kdst)[i] = kv;
+    reinterpret_cast<uint4*>(vdst)[i] = vv;
   }
   if (grp == 0 && blockIdx.x == 0) {
     for (int row = threadIdx.x; row < g.P; row += blockDim.x) {

@@ -46,103 +46,136 @@ __device__ __forceinline__ void warp_allreduce16(float* v, int lane) {
   for (int k = 0; k < 16; ++k) v[k] = __shfl_sync(full, h1, 2 * k);
 }
 
+// N consecutive elements of a staged row as floats (one vector load when N * sizeof(T) is
+// 4, 8 or 16 bytes; the caller keeps the address aligned to that size).
+template <typename T, int N>
+__device__ __forceinline__ void load_run(const T* p, float* out) {
+  constexpr int BYTES = N * (int)sizeof(T);
+  if constexpr (BYTES == 16) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    unpack(u, out, (const T*)nullptr);
+  } else if constexpr (BYTES == 8) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int j = 0; j < N; ++j) out[j] = Elem<T>::load(e + j);
+  } else if constexpr (BYTES == 4) {
+    const uint32_t u = *reinterpret_cast<const uint32_t*>(p);
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int j = 0; j < N; ++j) out[j] = Elem<T>::load(e + j);
+  } else {
+#pragma unroll
+    for (int j = 0; j < N; ++j) out[j] = Elem<T>::load(p + j);
+  }
+}
+
 // Beta cut of one group of four rows by one warp, certified against the canonical cost.
 //
 // The canonical cost (beta_log_kv.select_cuts, beta_log_kv.py:29-46) of cut c for one
 // component: energy = max(sum_i w_i E_i / max(sum w, 1e-12), 1e-12) with E_i = sum_d x_id^2;
 // per side, mean_d = (sum_i om_i x_id) / max(sum om, 1e-12) (om = w on the side, else 0),
 // loss = sum_i om_i sum_d (x_id - mean_d)^2; cost_c += loss / energy over sides and
-// components, argmin over cuts (2, 1, 3) with ties to the earlier.  Rows off a side have
-// om = 0 and add exactly zero, so only the side's rows are evaluated here.
+// components, argmin over cuts (2, 1, 3) with ties to the earlier.
 //
-// This warp evaluates the same quantities with three differences: sums over features run
-// per lane and then across lanes (another order of adding non-negative terms); squares
-// are accumulated with fused multiply-adds; and a side mean is the side's sum (the same
-// rounded sum as the canonical one) times a rounded reciprocal of its mass, which lies
-// within 3 u M_d of the canonical mean (u = 2^-24, M_d = max_i |x_id|), so each squared
-// deviation moves by at most 32 u M_d^2 and a component's losses by 32 u (sum w)(sum_i E_i).
-// All other differences are relative: at most about (4 D + 128) u of a cost.  With
-// B = sum over components of 40 u (sum w)(sum_i E_i) / energy and rel = (4 D + 128) u,
-// the returned cut is the canonical one whenever runner-up minus best exceeds
-// 2 rel * runner-up + 2 B (plus a floor for subnormal rounding).  Otherwise, or when a
-// row energy exceeds 1e30 (no overflow anywhere below that), -1 asks for the canonical
-// evaluation.
+// This warp uses the identity  sum_i w_i |x_i - m|^2 = (sum_{i<j} w_i w_j |x_i - x_j|^2) / W
+// (m the weighted mean, W the side's mass): a side's loss from the pairwise squared
+// distances D_ab of its rows (pairs 01, 02, 12, 13, 23 cover every side of the three cuts;
+// single-row sides lose nothing).  Every term is non-negative, so the result is within a
+// relative (D / 16 + 30) u of the exact cost (u = 2^-24: (D / 32 + 7) u for a distance or a
+// row energy summed per lane and across lanes, 7 u for a side's products, sums and division,
+// 5 u more for the energy, 4 u for the cost's sum).  The canonical evaluation is within
+// (2 D + 25) u relative of the exact cost
+// at its rounded means, and a mean rounded by delta changes a side's loss by only
+// W |delta|^2 <= 36 u^2 W sum_i E_i (the mean minimises the loss).  So the returned cut is the
+// canonical one whenever runner-up minus best exceeds 2 rel * runner-up with
+// rel = (4 D + 128) u >= the sum of both relative bounds, plus twice
+// B = sum over components of 40 u^2 (sum w)(sum_i E_i) / energy, plus a floor for subnormal
+// rounding.  Otherwise (a near tie), when a side's mass lies in (0, 1e-12) (the canonical
+// clamp), or when a row energy exceeds 1e30 (no overflow anywhere below that), -1 asks for
+// the canonical evaluation.
 template <typename T, int DC>
 __device__ int beta_cut_warp(const T* tk, const T* tv, const Meta* tm, int start, int Drt, int lane) {
   const int D = DC ? DC : Drt;
-  constexpr int NPL = (DC >= 32 && DC % 32 == 0) ? DC / 32 : 0;  // features per lane, compile time
+  constexpr int NPL = (DC >= 32 && DC % 32 == 0) ? DC / 32 : 0;  // consecutive features per lane
   float wv[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) wv[i] = tm[start + i].w;
-  const float wsum = fadd(fadd(fadd(wv[0], wv[1]), wv[2]), wv[3]);
-  const float tot = fmaxf(wsum, 1e-12f);
-  // Side masses: left of cut c = w_0..w_{c-1}, right = w_c..w_3 (c = 1, 2, 3).
-  const float wl1 = wv[0], wl2 = fadd(wv[0], wv[1]), wl3 = fadd(wl2, wv[2]);
-  const float wr3 = wv[3], wr2 = fadd(wv[2], wv[3]), wr1 = fadd(fadd(wv[1], wv[2]), wv[3]);
-  const float il1 = fdiv(1.f, fmaxf(wl1, 1e-12f)), il2 = fdiv(1.f, fmaxf(wl2, 1e-12f)),
-              il3 = fdiv(1.f, fmaxf(wl3, 1e-12f));
-  const float ir1 = fdiv(1.f, fmaxf(wr1, 1e-12f)), ir2 = fdiv(1.f, fmaxf(wr2, 1e-12f)),
-              ir3 = fdiv(1.f, fmaxf(wr3, 1e-12f));
-  float costs[3] = {0.f, 0.f, 0.f};
-  float bound = 0.f;
-  bool finite = true;
+  // v[0..8]: K's E_0..E_3, D_01, D_02, D_12, D_13, D_23; v[9..15] + x[0..1]: the same for V.
+  float v[16], x2[2];
 #pragma unroll
   for (int comp = 0; comp < 2; ++comp) {
     const T* base = (comp == 0 ? tk : tv) + start * D;
-    // acc[0..3]: E_i; acc[4 + 4 jc + i]: squared deviations of row i for cut jc (cuts 2, 1, 3).
-    float acc[16];
-#pragma unroll
-    for (int k = 0; k < 16; ++k) acc[k] = 0.f;
-    auto feature = [&](int d) {
-      float x[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) x[i] = Elem<T>::load(base + i * D + d);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[i] = __fmaf_rn(x[i], x[i], acc[i]);
-      const float p0 = __fmul_rn(x[0], wv[0]), p1 = __fmul_rn(x[1], wv[1]), p2 = __fmul_rn(x[2], wv[2]),
-                  p3 = __fmul_rn(x[3], wv[3]);
-      const float l2 = __fadd_rn(p0, p1), r2 = __fadd_rn(p2, p3);
-      const float ml1 = __fmul_rn(p0, il1), ml2 = __fmul_rn(l2, il2), ml3 = __fmul_rn(__fadd_rn(l2, p2), il3);
-      const float mr1 = __fmul_rn(__fadd_rn(__fadd_rn(p1, p2), p3), ir1), mr2 = __fmul_rn(r2, ir2), mr3 = __fmul_rn(p3, ir3);
-      float df;
-      // cut 2: rows 0,1 | 2,3
-      df = __fsub_rn(x[0], ml2); acc[4] = __fmaf_rn(df, df, acc[4]);
-      df = __fsub_rn(x[1], ml2); acc[5] = __fmaf_rn(df, df, acc[5]);
-      df = __fsub_rn(x[2], mr2); acc[6] = __fmaf_rn(df, df, acc[6]);
-      df = __fsub_rn(x[3], mr2); acc[7] = __fmaf_rn(df, df, acc[7]);
-      // cut 1: row 0 | 1,2,3
-      df = __fsub_rn(x[0], ml1); acc[8] = __fmaf_rn(df, df, acc[8]);
-      df = __fsub_rn(x[1], mr1); acc[9] = __fmaf_rn(df, df, acc[9]);
-      df = __fsub_rn(x[2], mr1); acc[10] = __fmaf_rn(df, df, acc[10]);
-      df = __fsub_rn(x[3], mr1); acc[11] = __fmaf_rn(df, df, acc[11]);
-      // cut 3: rows 0,1,2 | 3
-      df = __fsub_rn(x[0], ml3); acc[12] = __fmaf_rn(df, df, acc[12]);
-      df = __fsub_rn(x[1], ml3); acc[13] = __fmaf_rn(df, df, acc[13]);
-      df = __fsub_rn(x[2], ml3); acc[14] = __fmaf_rn(df, df, acc[14]);
-      df = __fsub_rn(x[3], mr3); acc[15] = __fmaf_rn(df, df, acc[15]);
+    float e0 = 0.f, e1 = 0.f, e2 = 0.f, e3 = 0.f, p01 = 0.f, p02 = 0.f, p12 = 0.f, p13 = 0.f, p23 = 0.f;
+    auto feature = [&](float a, float b, float c, float d) {
+      e0 = __fmaf_rn(a, a, e0);
+      e1 = __fmaf_rn(b, b, e1);
+      e2 = __fmaf_rn(c, c, e2);
+      e3 = __fmaf_rn(d, d, e3);
+      float t;
+      t = __fsub_rn(a, b); p01 = __fmaf_rn(t, t, p01);
+      t = __fsub_rn(a, c); p02 = __fmaf_rn(t, t, p02);
+      t = __fsub_rn(b, c); p12 = __fmaf_rn(t, t, p12);
+      t = __fsub_rn(b, d); p13 = __fmaf_rn(t, t, p13);
+      t = __fsub_rn(c, d); p23 = __fmaf_rn(t, t, p23);
     };
     if constexpr (NPL > 0) {
+      float r0[NPL], r1[NPL], r2[NPL], r3[NPL];
+      load_run<T, NPL>(base + NPL * lane, r0);
+      load_run<T, NPL>(base + D + NPL * lane, r1);
+      load_run<T, NPL>(base + 2 * D + NPL * lane, r2);
+      load_run<T, NPL>(base + 3 * D + NPL * lane, r3);
 #pragma unroll
-      for (int j = 0; j < NPL; ++j) feature(lane + 32 * j);
+      for (int j = 0; j < NPL; ++j) feature(r0[j], r1[j], r2[j], r3[j]);
     } else {
 #pragma unroll 1
-      for (int d = lane; d < D; d += 32) feature(d);
+      for (int d = lane; d < D; d += 32)
+        feature(Elem<T>::load(base + d), Elem<T>::load(base + D + d), Elem<T>::load(base + 2 * D + d),
+                Elem<T>::load(base + 3 * D + d));
     }
-    warp_allreduce16(acc, lane);
-    const float esum = acc[0] + acc[1] + acc[2] + acc[3];
-    finite = finite && esum <= 1e30f;  // also false for NaN
-    const float energy = fmaxf(fdiv(fadd(fadd(fadd(fmul(acc[0], wv[0]), fmul(acc[1], wv[1])), fmul(acc[2], wv[2])),
-                                         fmul(acc[3], wv[3])),
-                                    tot),
+    const float vals[9] = {e0, e1, e2, e3, p01, p02, p12, p13, p23};
+#pragma unroll
+    for (int k = 0; k < 9; ++k) {
+      const int idx = comp * 9 + k;
+      if (idx < 16) v[idx] = vals[k];
+      else x2[idx - 16] = vals[k];
+    }
+  }
+  warp_allreduce16(v, lane);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    x2[0] += __shfl_xor_sync(0xffffffffu, x2[0], off);
+    x2[1] += __shfl_xor_sync(0xffffffffu, x2[1], off);
+  }
+  const float w0 = wv[0], w1 = wv[1], w2 = wv[2], w3 = wv[3];
+  const float wsum = fadd(fadd(fadd(w0, w1), w2), w3);
+  const float tot = fmaxf(wsum, 1e-12f);
+  const float m01 = fadd(w0, w1), m23 = fadd(w2, w3), m123 = fadd(fadd(w1, w2), w3), m012 = fadd(m01, w2);
+  auto mass_ok = [](float m) { return m == 0.f || m >= 1e-12f; };
+  bool ok = mass_ok(w0) && mass_ok(w3) && mass_ok(m01) && mass_ok(m23) && mass_ok(m123) && mass_ok(m012);
+  const float w01 = fmul(w0, w1), w02 = fmul(w0, w2), w12 = fmul(w1, w2), w13 = fmul(w1, w3), w23 = fmul(w2, w3);
+  float costs[3] = {0.f, 0.f, 0.f};
+  float bound = 0.f;
+#pragma unroll
+  for (int comp = 0; comp < 2; ++comp) {
+    const float E0 = v[comp * 9], E1 = v[comp * 9 + 1], E2 = v[comp * 9 + 2], E3 = v[comp * 9 + 3];
+    const float P01 = v[comp * 9 + 4], P02 = v[comp * 9 + 5], P12 = v[comp * 9 + 6];
+    const float P13 = comp == 0 ? v[7] : x2[0], P23 = comp == 0 ? v[8] : x2[1];
+    const float esum = E0 + E1 + E2 + E3;
+    ok = ok && esum <= 1e30f;  // also false for NaN
+    const float energy = fmaxf(fdiv(fadd(fadd(fadd(fmul(E0, w0), fmul(E1, w1)), fmul(E2, w2)), fmul(E3, w3)), tot),
                                1e-12f);
     const float inv_e = fdiv(1.f, energy);
-    // cut 2 (costs[0]), cut 1 (costs[1]), cut 3 (costs[2]); left side then right side.
-    costs[0] += (acc[4] * wv[0] + acc[5] * wv[1]) * inv_e + (acc[6] * wv[2] + acc[7] * wv[3]) * inv_e;
-    costs[1] += (acc[8] * wv[0]) * inv_e + (acc[9] * wv[1] + acc[10] * wv[2] + acc[11] * wv[3]) * inv_e;
-    costs[2] += (acc[12] * wv[0] + acc[13] * wv[1] + acc[14] * wv[2]) * inv_e + (acc[15] * wv[3]) * inv_e;
-    bound += 40.f * 5.9604645e-8f * wsum * esum * inv_e;
+    const float l2 = fdiv(fmul(w01, P01), fmaxf(m01, 1e-12f));
+    const float r2 = fdiv(fmul(w23, P23), fmaxf(m23, 1e-12f));
+    const float r1 = fdiv(fadd(fadd(fmul(w12, P12), fmul(w13, P13)), fmul(w23, P23)), fmaxf(m123, 1e-12f));
+    const float l3 = fdiv(fadd(fadd(fmul(w01, P01), fmul(w02, P02)), fmul(w12, P12)), fmaxf(m012, 1e-12f));
+    costs[0] = fadd(costs[0], fmul(fadd(l2, r2), inv_e));  // cut 2: rows 0,1 | 2,3
+    costs[1] = fadd(costs[1], fmul(r1, inv_e));            // cut 1: row 0 | 1,2,3
+    costs[2] = fadd(costs[2], fmul(l3, inv_e));            // cut 3: rows 0,1,2 | 3
+    bound += 40.f * 3.5527137e-15f * wsum * esum * inv_e;  // 40 u^2 (sum w)(sum E) / energy
   }
-  if (!finite) return -1;
+  if (!ok) return -1;
   int best = 0;
   if (costs[1] < costs[best]) best = 1;
   if (costs[2] < costs[best]) best = 2;

@@ -64,6 +64,7 @@ struct Work {
   int8_t* assign_tok;      // [B,G,NW] attach decision per token (token index order)
   uint8_t* orphan;         // [B,G,NW] token index order
   float* s_winner;         // [B,G,NW] token index order
+  float* cnorm;            // [B,G,K] sum_d mu_d^2 of every centre (left to right), before the flush
   int32_t* tok_list;       // [B,G,NW] archive ranks grouped by cluster (stable)
   int32_t* plan_off;       // [B,G,K] offset into tok_list
   int32_t* plan_n;         // [B,G,K] tokens joining the cluster

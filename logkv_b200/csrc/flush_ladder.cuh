@@ -134,6 +134,9 @@ __device__ LaneCtx<T> make_ctx(const Geo& g, const logkv_state_t& s, const Work&
 // clusters and delayed (late) clusters are cleared, and a delayed cluster's
 // entries plus its new tokens are staged in scratch buffer 0, stably sorted by
 // p_lo with orders 0..n-1 (_alpha_commit_joins, log_kv_cache.py:3690-3788).
+constexpr int kPrepRows = 64;  // token rows staged per pass of the centroid sum
+constexpr int kPrepFeat = 4;   // features per thread of the centroid sum (D <= 1024, 256 threads)
+
 template <typename T>
 __global__ void __launch_bounds__(256) prepare_kernel(Geo g, logkv_state_t s, Work w) {
   pdl_entry();
@@ -146,28 +149,47 @@ __global__ void __launch_bounds__(256) prepare_kernel(Geo g, logkv_state_t s, Wo
   float* mu = s.centroid + x.lane * D;
   extern __shared__ unsigned long long keys[];                       // [sort_cap] (delayed re-insert)
   int* srcs = reinterpret_cast<int*>(keys + g.sort_cap);             // [NW] token sources
+  T* trows = reinterpret_cast<T*>(srcs + ((g.NW + 3) & ~3));         // [kPrepRows][D] staged token rows
   for (int i = tid; i < n; i += nt) srcs[i] = x.token_src(i);
   __syncthreads();
-  for (int d = tid; d < D; d += nt) {
+  // Centroid: per feature, a left-to-right sum over the lane's new tokens (a new cluster's
+  // first token is kept apart, as the reference adds it after the others' sum).  Rows are
+  // staged through shared memory kPrepRows at a time with 16-byte loads.
+  constexpr int VN = Vec<T>::N;
+  const int DV = D / VN;
+  const int i0 = type == kJobNew ? 1 : 0;
+  float sums[kPrepFeat];  // features tid, tid + nt, ... (D <= kPrepFeat * blockDim.x)
+#pragma unroll
+  for (int j = 0; j < kPrepFeat; ++j) sums[j] = 0.f;
+  for (int c0 = i0; c0 < n; c0 += kPrepRows) {
+    const int cn = min(kPrepRows, n - c0);
+    for (int item = tid; item < cn * DV; item += nt) {
+      const int t = item / DV, v = item % DV;
+      *reinterpret_cast<uint4*>(trows + t * D + v * VN) =
+          *reinterpret_cast<const uint4*>(token_row<T>(g, x.snapk, x.reck, x.b, x.grp, srcs[c0 + t]) + v * VN);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kPrepFeat; ++j) {
+      const int d = tid + j * nt;
+      if (d < D) {
+#pragma unroll 8
+        for (int t = 0; t < cn; ++t) sums[j] = fadd(sums[j], Elem<T>::load(trows + t * D + d));
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int j = 0; j < kPrepFeat; ++j) {
+    const int d = tid + j * nt;
+    if (d >= D) continue;
     if (type == kJobNew) {
       const float x0 = Elem<T>::load(token_row<T>(g, x.snapk, x.reck, x.b, x.grp, srcs[0]) + d);
-      if (n == 1) {
-        mu[d] = x0;
-      } else {
-        float sums = 0.f;
-#pragma unroll 8
-        for (int i = 1; i < n; ++i)
-          sums = fadd(sums, Elem<T>::load(token_row<T>(g, x.snapk, x.reck, x.b, x.grp, srcs[i]) + d));
-        mu[d] = fdiv(fadd(fmul(1.f, x0), sums), fadd(1.f, (float)(n - 1)));
-      }
+      mu[d] = n == 1 ? x0 : fdiv(fadd(fmul(1.f, x0), sums[j]), fadd(1.f, (float)(n - 1)));
     } else {
-      float sums = 0.f;
-#pragma unroll 8
-      for (int i = 0; i < n; ++i)
-        sums = fadd(sums, Elem<T>::load(token_row<T>(g, x.snapk, x.reck, x.b, x.grp, srcs[i]) + d));
       const float p = type == kJobOrdinary ? fmul(pre, 1.f) : pre;
       const float denom = fadd(p, (float)n);
-      mu[d] = (type == kJobLate || p > 0.f) ? fdiv(fadd(fmul(p, mu[d]), sums), denom) : fdiv(sums, (float)n);
+      mu[d] = (type == kJobLate || p > 0.f) ? fdiv(fadd(fmul(p, mu[d]), sums[j]), denom) : fdiv(sums[j], (float)n);
     }
   }
   __shared__ int counts[kMaxLevels + 1];
@@ -238,21 +260,24 @@ __global__ void __launch_bounds__(256) prepare_kernel(Geo g, logkv_state_t s, Wo
     }
     T* sk = static_cast<T*>(w.sk);
     T* sv = static_cast<T*>(w.sv);
-    for (int item = tid; item < total * D; item += nt) {
-      const int r = item / D, d = item % D;
+    for (int item = tid; item < total * DV; item += nt) {
+      const int r = item / DV, d = (item % DV) * VN;
       const int idx = (int)(keys[r] & 0x3FFFull);
       const size_t dst = x.scr_row(0, r) * D + d;
+      const T *pk, *pv;
       if (idx < e) {
         int l = 0;
         while (l + 1 < g.L && counts[l + 1] <= idx) ++l;
         const size_t src = x.level_row(l, idx - counts[l]) * D + d;
-        sk[dst] = static_cast<const T*>(s.level_k)[src];
-        sv[dst] = static_cast<const T*>(s.level_v)[src];
+        pk = static_cast<const T*>(s.level_k) + src;
+        pv = static_cast<const T*>(s.level_v) + src;
       } else {
-        const int src = x.token_src(idx - e);
-        sk[dst] = token_row<T>(g, x.snapk, x.reck, x.b, x.grp, src)[d];
-        sv[dst] = token_row<T>(g, x.snapv, x.recv, x.b, x.grp, src)[d];
+        const int src = srcs[idx - e];
+        pk = token_row<T>(g, x.snapk, x.reck, x.b, x.grp, src) + d;
+        pv = token_row<T>(g, x.snapv, x.recv, x.b, x.grp, src) + d;
       }
+      *reinterpret_cast<uint4*>(sk + dst) = *reinterpret_cast<const uint4*>(pk);
+      *reinterpret_cast<uint4*>(sv + dst) = *reinterpret_cast<const uint4*>(pv);
     }
     for (int r = tid; r < total; r += nt) {
       const int idx = (int)(keys[r] & 0x3FFFull);
@@ -279,11 +304,12 @@ __global__ void __launch_bounds__(256) prepare_kernel(Geo g, logkv_state_t s, Wo
   }
   // Clear every level of the lane (new clusters and delayed re-inserts).
   const size_t rows = (size_t)g.L * g.Bs;
-  T* lk = static_cast<T*>(s.level_k) + x.level_row(0, 0) * D;
-  T* lv = static_cast<T*>(s.level_v) + x.level_row(0, 0) * D;
-  for (size_t i = tid; i < rows * D; i += nt) {
-    lk[i] = Elem<T>::zero();
-    lv[i] = Elem<T>::zero();
+  uint4* lk = reinterpret_cast<uint4*>(static_cast<T*>(s.level_k) + x.level_row(0, 0) * D);
+  uint4* lv = reinterpret_cast<uint4*>(static_cast<T*>(s.level_v) + x.level_row(0, 0) * D);
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  for (size_t i = tid; i < rows * DV; i += nt) {
+    lk[i] = zero;
+    lv[i] = zero;
   }
   for (size_t r = tid; r < rows; r += nt) {
     const size_t row = x.level_row(0, 0) + r;

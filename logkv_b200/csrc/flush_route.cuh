@@ -16,11 +16,12 @@ namespace logkv {
 // ---------------------------------------------------------------- K4: attach decisions
 // Decisions for every token of the [old pool | flushed window] index space (the archive
 // is a subset, picked later by the span choice; decisions depend only on the frozen
-// cluster state).  One thread per (token, cluster): each computes the token's dot
-// product and exact squared distance to one centre, left to right over the features;
-// one thread per token then walks the clusters in index order for the decision
-// (first-index argmin, as torch.argmin).  Token rows and centres are staged in shared
-// memory with an odd word stride (conflict-free).  Outputs are indexed by token.
+// cluster state).  One thread per (token, cluster) computes the token's dot product and
+// exact squared distance to one centre, left to right over the features, and then the
+// semantic distance, routing cost and exact distance; one thread per token walks the
+// clusters in index order for the decision (first-index argmin, as torch.argmin).  Token
+// rows and centres are staged in shared memory with an odd word stride (conflict-free);
+// centre norms come from the snapshot kernel.  Outputs are indexed by token.
 template <typename T>
 __device__ void attach_body(const Geo& g, const logkv_state_t& s, const Work& w, int blk) {
   const int b = blockIdx.z, grp = blockIdx.y, tid = threadIdx.x;
@@ -29,97 +30,139 @@ __device__ void attach_body(const Geo& g, const logkv_state_t& s, const Work& w,
   const int ntok = blockDim.x / slots;          // tokens per block
   const int r0 = blk * ntok;
   if (r0 >= g.NW) return;
-  extern __shared__ float sm[];
-  float* mu = sm;                                // [K][D+1]
-  float* xs = mu + K * (D + 1);                  // [ntok][D+1]
-  float* sem = xs + ntok * (D + 1);              // [ntok][K] semantic
-  float* exd = sem + ntok * K;                   // [ntok][K] exact squared distance
-  __shared__ float mm[kMaxClusters];
+  extern __shared__ float4 sm4[];
+  const int RS = D + 4;                          // row stride in floats: 16-byte rows, conflict-free
+  float* mu = reinterpret_cast<float*>(sm4);     // [K][RS]
+  float* xs = mu + K * RS;                       // [ntok][RS]
+  float* sem = xs + ntok * RS;                   // [ntok][K] raw dot, then semantic distance
+  float* exd = sem + ntok * K;                   // [ntok][K] exact distance (orphans only)
+  float* cst = exd + ntok * K;                   // [ntok][K] routing cost
   __shared__ float xxs[32];
-  __shared__ long long phi[kMaxClusters];
-  __shared__ int alv[kMaxClusters];
+  __shared__ int orph_tok[32];
+  __shared__ int n_orph;
   const size_t lane0 = ((size_t)b * g.G + grp) * K;
-  for (int i = tid; i < K * D; i += blockDim.x) mu[(i / D) * (D + 1) + i % D] = s.centroid[lane0 * D + i];
-  if (tid < K) {
-    alv[tid] = s.alive[lane0 + tid] != 0;
-    phi[tid] = s.p_hi_c[lane0 + tid];
-  }
+  if (tid == 0) n_orph = 0;
+  const int warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
+  const int D4 = D / 4;
+  // Centres and token rows into shared memory: one row per warp at a time, 16-byte units.
+  const float4* cent4 = reinterpret_cast<const float4*>(s.centroid + lane0 * D);
+  for (int cc = warp; cc < K; cc += nwarps)
+    for (int d4 = lane; d4 < D4; d4 += 32) reinterpret_cast<float4*>(mu + cc * RS)[d4] = cent4[cc * D4 + d4];
   const T* snap = static_cast<const T*>(w.snap_k);
   const T* rec = static_cast<const T*>(s.recent_k_raw);
   const int nrow = min(ntok, g.NW - r0);
   constexpr int VN = Vec<T>::N;
   const int DV = D / VN;
-  for (int item = tid; item < nrow * DV; item += blockDim.x) {
-    const int row = item / DV, v = item % DV;
-    float xv[VN];
-    unpack(*reinterpret_cast<const uint4*>(token_row<T>(g, snap, rec, b, grp, r0 + row) + v * VN), xv,
-           (const T*)nullptr);
+  for (int row = warp; row < nrow; row += nwarps) {
+    const T* src = token_row<T>(g, snap, rec, b, grp, r0 + row);
+    for (int v = lane; v < DV; v += 32) {
+      float xv[VN];
+      unpack(*reinterpret_cast<const uint4*>(src + v * VN), xv, (const T*)nullptr);
 #pragma unroll
-    for (int e = 0; e < VN; ++e) xs[row * (D + 1) + v * VN + e] = xv[e];
+      for (int e = 0; e < VN; e += 4)
+        *reinterpret_cast<float4*>(xs + row * RS + v * VN + e) = make_float4(xv[e], xv[e + 1], xv[e + 2], xv[e + 3]);
+    }
   }
   __syncthreads();
-  if (tid < K) {
-    float a = 0.f;
-    for (int d = 0; d < D; ++d) a = fadd(a, fmul(mu[tid * (D + 1) + d], mu[tid * (D + 1) + d]));
-    mm[tid] = a;
-  }
+  // Pass 1, one thread per (token, centre): the dot product, left to right over the features.
+  // When a lane of the token's group is spare (K < slots), lane K runs the same loop against
+  // the token itself, so its "dot" is |x|^2 (same operations).
   const int tok = tid / slots, c = tid % slots;
-  if (tok < nrow) {
-    const float* x = xs + tok * (D + 1);
-    if (c < K) {
-      const float* m = mu + c * (D + 1);
-      float dot = 0.f, ex = 0.f;
-      for (int d = 0; d < D; ++d) {
-        dot = fadd(dot, fmul(x[d], m[d]));
-        const float df = fsub(x[d], m[d]);
+  const bool spare = K < slots;
+  if (tok < nrow && c <= (spare ? K : K - 1)) {
+    const float4* x = reinterpret_cast<const float4*>(xs + tok * RS);
+    const float4* m = reinterpret_cast<const float4*>(c < K ? mu + c * RS : xs + tok * RS);
+    float dot = 0.f;
+    for (int d4 = 0; d4 < D4; ++d4) {
+      const float4 xv = x[d4], mv = m[d4];
+      dot = fadd(dot, fmul(xv.x, mv.x));
+      dot = fadd(dot, fmul(xv.y, mv.y));
+      dot = fadd(dot, fmul(xv.z, mv.z));
+      dot = fadd(dot, fmul(xv.w, mv.w));
+    }
+    if (c < K) sem[tok * K + c] = dot;
+    else xxs[tok] = dot;
+  }
+  if (!spare && tok < nrow && c == 0) {
+    const float* x = xs + tok * RS;
+    float xx = 0.f;
+    for (int d = 0; d < D; ++d) xx = fadd(xx, fmul(x[d], x[d]));
+    xxs[tok] = xx;
+  }
+  __syncthreads();
+  // Pass 2, one thread per (token, centre): semantic distance and routing cost.
+  const int r = r0 + tok;   // token index
+  if (tok < nrow && c < K) {
+    const int64_t pos = token_position(g, s, w, b, r);
+    const float semv = fmaxf(fsub(fadd(xxs[tok], w.cnorm[lane0 + c]), fmul(2.f, sem[tok * K + c])), 0.f);
+    const float gap = fmaxf((float)(pos - (int64_t)s.p_hi_c[lane0 + c]), 0.f);
+    sem[tok * K + c] = semv;
+    cst[tok * K + c] = fadd(semv, fmul(g.eta, fdiv(gap, fadd(gap, g.g0))));
+  }
+  __syncthreads();
+  // Decision, one thread per token: centres in index order (first-index argmin, as
+  // torch.argmin).  Direct joins are final; orphans of a lane with live centres queue for
+  // the exact distances.
+  const size_t o = ((size_t)b * g.G + grp) * g.NW + r;
+  if (c == 0 && tok < nrow) {
+    const float thresh = fmul(g.lam, s.s_h[(size_t)b * g.G + grp]);
+    float best_cost = INFINITY, s_win = 0.f;
+    int winner = 0;
+    bool any_alive = false;
+    for (int cc = 0; cc < K; ++cc) {
+      if (!s.alive[lane0 + cc]) continue;
+      any_alive = true;
+      if (cst[tok * K + cc] < best_cost) {
+        best_cost = cst[tok * K + cc];
+        winner = cc;
+        s_win = sem[tok * K + cc];
+      }
+    }
+    if (!any_alive) s_win = sem[tok * K];   // winner 0; the token is an orphan
+    const bool direct = any_alive && s_win <= thresh;
+    w.orphan[o] = direct ? 0 : 1;
+    w.s_winner[o] = s_win;
+    if (direct || !any_alive) w.assign_tok[o] = (int8_t)winner;   // no live centre: 0
+    else orph_tok[atomicAdd(&n_orph, 1)] = tok;
+  }
+  __syncthreads();
+  const int no = n_orph;
+  if (no == 0) return;
+  // Exact distances of the queued orphans to the live centres, one thread per pair.
+  for (int item = tid; item < no * K; item += blockDim.x) {
+    const int t = orph_tok[item / K], cc = item % K;
+    float dist = INFINITY;
+    if (s.alive[lane0 + cc]) {
+      const float4* x = reinterpret_cast<const float4*>(xs + t * RS);
+      const float4* m = reinterpret_cast<const float4*>(mu + cc * RS);
+      float ex = 0.f;
+      for (int d4 = 0; d4 < D4; ++d4) {
+        const float4 xv = x[d4], mv = m[d4];
+        float df = fsub(xv.x, mv.x);
+        ex = fadd(ex, fmul(df, df));
+        df = fsub(xv.y, mv.y);
+        ex = fadd(ex, fmul(df, df));
+        df = fsub(xv.z, mv.z);
+        ex = fadd(ex, fmul(df, df));
+        df = fsub(xv.w, mv.w);
         ex = fadd(ex, fmul(df, df));
       }
-      sem[tok * K + c] = dot;  // raw dot; the semantic distance needs |x|^2 and |mu|^2 below
-      exd[tok * K + c] = ex;
+      dist = __fsqrt_rn(ex);
     }
-    if (c == (K < slots ? K : 0)) {
-      float xx = 0.f;
-      for (int d = 0; d < D; ++d) xx = fadd(xx, fmul(x[d], x[d]));
-      xxs[tok] = xx;
-    }
+    exd[t * K + cc] = dist;
   }
   __syncthreads();
-  if (c != 0 || tok >= nrow) return;
-  const int r = r0 + tok;   // token index
-  const int64_t pos = token_position(g, s, w, b, r);
-  const float xx = xxs[tok];
-  const float thresh = fmul(g.lam, s.s_h[(size_t)b * g.G + grp]);
-  float best_cost = INFINITY, s_win = 0.f, best_ex = INFINITY, sem0 = 0.f;
-  int winner = 0, nearest = 0;
-  bool any_alive = false;
-  for (int cc = 0; cc < K; ++cc) {
-    const float semv = fmaxf(fsub(fadd(xx, mm[cc]), fmul(2.f, sem[tok * K + cc])), 0.f);
-    if (cc == 0) sem0 = semv;
-    if (!alv[cc]) continue;
-    any_alive = true;
-    const float gap = fmaxf((float)(pos - (int64_t)phi[cc]), 0.f);
-    const float cost = fadd(semv, fmul(g.eta, fdiv(gap, fadd(gap, g.g0))));
-    if (cost < best_cost) {
-      best_cost = cost;
-      winner = cc;
-      s_win = semv;
-    }
-    const float dist = __fsqrt_rn(exd[tok * K + cc]);
-    if (dist < best_ex) {
-      best_ex = dist;
-      nearest = cc;
-    }
+  for (int j = tid; j < no; j += blockDim.x) {
+    const int t = orph_tok[j];
+    float best = INFINITY;
+    int nearest = 0;
+    for (int cc = 0; cc < K; ++cc)
+      if (exd[t * K + cc] < best) {
+        best = exd[t * K + cc];
+        nearest = cc;
+      }
+    w.assign_tok[((size_t)b * g.G + grp) * g.NW + r0 + t] = (int8_t)nearest;
   }
-  if (!any_alive) {
-    winner = 0;
-    s_win = sem0;
-    nearest = 0;
-  }
-  const bool direct = any_alive && s_win <= thresh;
-  const size_t o = ((size_t)b * g.G + grp) * g.NW + r;
-  w.assign_tok[o] = (int8_t)(direct ? winner : nearest);
-  w.orphan[o] = direct ? 0 : 1;
-  w.s_winner[o] = s_win;
 }
 
 // (value, index) argmax with the lowest index winning ties.
