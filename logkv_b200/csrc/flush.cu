@@ -28,16 +28,14 @@ static size_t choose_smem_bytes(const Geo& g) {
   return (size_t)g.NC * (8 + 4 + 4 + 2) + 2 * (size_t)(g.P + 1) * (8 + 4 + 4) + (size_t)(g.P + 1) * (8 + 4) + 16;
 }
 
-// Span scores (staged K and V rows, means, token energies, centre distances and, with Beta,
-// the lane's centres) and attach decisions (centres, 8 or 16 token rows, per-pair scores).
+// Span scores (per warp: means, token energies, centre distances) and attach decisions
+// (centres, 8 or 16 token rows, per-pair scores).
 static size_t score_smem_bytes(const Geo& g, size_t esize) {
-  const size_t ws = (size_t)g.D * esize / 4 + 1;  // staged row: words, odd stride
-  return 2 * kScoreRows * ws * 4 +
-         (2 * (size_t)g.D + 2 * kScoreRows + 2 * (size_t)g.K + (g.beta ? (size_t)g.K * g.D : 0)) * sizeof(float);
+  return 8 * (size_t)score_warp_floats(g.D, g.K, (int)esize) * sizeof(float);  // 8 warps
 }
 static size_t attach_smem_bytes(const Geo& g) {
   const size_t att_tok = 256 / (g.K <= 16 ? 16 : 32);
-  return ((size_t)(g.K + att_tok) * (g.D + 4) + 3 * att_tok * g.K) * sizeof(float);
+  return (size_t)(g.K + att_tok) * (g.D + 4) * sizeof(float);
 }
 // Delayed re-insert sort keys, token sources and the staged rows of the centroid sum.
 static size_t prep_smem_bytes(const Geo& g, size_t esize) {
@@ -76,22 +74,40 @@ static void launch_cascade(const Geo& g, const logkv_state_t& s, const Work& w, 
   launch_pdl(cascade_kernel<T, BETA, DC>, dim3(g.K, g.G, g.B), 512, smem, st, g, s, w);
 }
 
-// Span scores: blocks stride over the span candidates.
+// Span scores: the block's warps stride over the (candidate, group) pairs of batch row
+// blockIdx.y, one pair per warp at a time.
 template <typename T>
 __global__ void __launch_bounds__(256) score_kernel(Geo g, logkv_state_t s, Work w) {
   pdl_entry();
-  score_body<T>(g, s, w, blockIdx.x, gridDim.x);
+  extern __shared__ float sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const int b = blockIdx.y;
+  float* ws = sm + warp * score_warp_floats(g.D, g.K, (int)sizeof(T));
+  const int npairs = w.n_cand[b] * g.G;
+  for (int p = blockIdx.x * nwarps + warp; p < npairs; p += gridDim.x * nwarps) {
+    score_pair<T>(g, s, w, b, p / g.G, p % g.G, lane, ws);
+    __syncwarp();
+  }
 }
 
 // Attach decisions run beside the span scores.  They read the snapshot (complete before any
 // score block passed its entry wait, which is what let this grid launch) and the frozen
-// cluster state, so the entry wait is skipped; the wait comes at the end instead, so this
-// grid completes only after the score grid and the next kernel's entry wait covers both.
-template <typename T>
+// cluster state, so the entry wait is skipped.  Block (0, 0, 0) waits at its end instead:
+// this grid then completes only after the score grid, and the next kernel's entry wait
+// covers both, while every other block leaves as soon as its tokens are done.
+template <typename T, int DC>
 __global__ void __launch_bounds__(256) attach_kernel(Geo g, logkv_state_t s, Work w) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  attach_body<T>(g, s, w, blockIdx.x);
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  attach_body<T, DC>(g, s, w, blockIdx.x);
+  if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+template <typename T, int DC>
+static void launch_attach(const Geo& g, const logkv_state_t& s, const Work& w, size_t smem, int grid_x,
+                          cudaStream_t st) {
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(attach_kernel<T, DC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  launch_pdl(attach_kernel<T, DC>, dim3(grid_x, g.G, g.B), 256, smem, st, g, s, w);
 }
 
 // ---------------------------------------------------------------- K8: window shift
@@ -314,13 +330,14 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   const size_t score_smem = score_smem_bytes(g, sizeof(T));
   if (score_smem > 48 * 1024)
     cudaFuncSetAttribute(score_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)score_smem);
-  const int score_blocks = std::max(1, std::min(g.NC, 8 * sm_count / std::max(1, g.B * g.G) + 1));
-  launch_pdl(score_kernel<T>, dim3(score_blocks, g.G, g.B), 256, score_smem, st, g, s, w);
+  const int score_blocks = std::max(1, std::min((g.NC * g.G + 7) / 8, 2 * sm_count / g.B + 1));
+  launch_pdl(score_kernel<T>, dim3(score_blocks, g.B), 256, score_smem, st, g, s, w);
   const int att_tok = 256 / (g.K <= 16 ? 16 : 32);
   const size_t attach_smem = attach_smem_bytes(g);
-  if (attach_smem > 48 * 1024)
-    cudaFuncSetAttribute(attach_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attach_smem);
-  launch_pdl(attach_kernel<T>, dim3((g.NW + att_tok - 1) / att_tok, g.G, g.B), 256, attach_smem, st, g, s, w);
+  const int attach_x = (g.NW + att_tok * kAttachRounds - 1) / (att_tok * kAttachRounds);
+  if (g.D == 128) launch_attach<T, 128>(g, s, w, attach_smem, attach_x, st);
+  else if (g.D == 64) launch_attach<T, 64>(g, s, w, attach_smem, attach_x, st);
+  else launch_attach<T, 0>(g, s, w, attach_smem, attach_x, st);
   }
   if (!(phases & kPhaseCommit)) return (int)cudaGetLastError();
   mark();

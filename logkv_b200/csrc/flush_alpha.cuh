@@ -221,153 +221,165 @@ __global__ void __launch_bounds__(1024) alpha_cut_kernel(Geo g, logkv_state_t s,
 }
 
 // ---------------------------------------------------------------- K2: span scores
-// One block per (candidate, group) in a stride of `nblk` blocks over candidates.  The span's
-// K and V rows are staged together in shared memory (kScoreRows tokens at a time, 32-bit
-// words with an odd row stride, so per-row and per-feature walks are conflict-free); the
-// block's two halves then reduce K and V concurrently: mean per feature and energy per token
-// as left-to-right sums.  Output per (row, candidate, group): Alpha parts (R_K, R_V) or
-// Beta's per-group score.
-constexpr int kScoreRows = 64;  // staged tokens per pass
-constexpr int kScoreFeat = 8;   // features per thread of a half block (D <= 1024, 256 threads)
-
-template <typename T>
-__device__ __forceinline__ float staged_elem(const uint32_t* row, int d) {
-  if (sizeof(T) == 4) return __uint_as_float(row[d]);
-  const uint32_t wd = row[d >> 1];
-  return __uint_as_float((d & 1) ? (wd & 0xffff0000u) : (wd << 16));  // bf16 -> f32 is exact
+// One warp per (candidate, group) pair, no block-wide barriers.  The warp copies the span's
+// K and V rows into its own shared memory, up to score_rows() tokens per pass (cp.async, all
+// copies in flight at once; 16-byte chunks XOR-swizzled by token so that per-token and
+// per-feature walks are conflict-free), then per component: the mean of every feature (lanes
+// own 4 consecutive features and walk the tokens in order), the energy of every token (lanes
+// own tokens and walk the features in order), their sum in token order, and the mean square
+// of the mean vector; with Beta, the novelty of the key mean against every live centre (lanes
+// own centres).  Every sum runs left to right, as the reference's CPU path.  Output per
+// (row, candidate, group): Alpha parts (R_K, R_V) or Beta's per-group score.
+__host__ __device__ inline int score_rows(int D, int esize) {
+  const int r = 8192 / (D * esize);
+  return r < 1 ? 1 : (r > 32 ? 32 : r);
+}
+// Per-warp shared memory in floats: rows [2][rows][D] (storage dtype), means [2][D], token
+// energies [2][32], centre distances [K].
+__host__ __device__ inline int score_warp_floats(int D, int K, int esize) {
+  return (2 * score_rows(D, esize) * D * esize / 4 + 2 * D + 64 + K + 3) & ~3;
 }
 
 template <typename T>
-__device__ void score_body(const Geo& g, const logkv_state_t& s, const Work& w, int blk, int nblk) {
-  const int b = blockIdx.z, grp = blockIdx.y, tid = threadIdx.x, nt = blockDim.x;
-  const int G = g.G, D = g.D, K = g.K;
-  const int warp = tid >> 5, lane = tid & 31, nwarps = nt >> 5;
+__device__ void score_pair(const Geo& g, const logkv_state_t& s, const Work& w, int b, int ci, int grp, int lane,
+                           float* ws) {
+  const int D = g.D, K = g.K, G = g.G;
   constexpr int VN = Vec<T>::N;
-  const int DV = D / VN;
-  const int WPR = D * (int)sizeof(T) / 4, WS = WPR + 1;  // words per row, odd word stride
-  extern __shared__ float sm[];
-  uint32_t* rows = reinterpret_cast<uint32_t*>(sm);                     // [2][kScoreRows][WS]
-  float* mean = reinterpret_cast<float*>(rows + 2 * kScoreRows * WS);  // [2][D]
-  float* etok = mean + 2 * D;                                           // [2][kScoreRows]
-  float* cdist = etok + 2 * kScoreRows;                                 // [K]
-  float* cmm = cdist + K;                                               // [K] mean square of each centre
-  float* cent = cmm + K;                                                // [K][D] centres (Beta)
-  __shared__ float sh_part[2], sh_ener[2], sh_ms[2];
-  const int half = nt >> 1, comp = tid >= half ? 1 : 0, htid = tid - comp * half;
+  const int DV = D / VN;                                    // 16-byte chunks per row
+  const int swz = (DV & (DV - 1)) == 0 ? min(DV, 16) - 1 : 0;  // chunk swizzle mask
+  const int CR = score_rows(D, (int)sizeof(T));
+  T* rows = reinterpret_cast<T*>(ws);                       // [2][CR][D]
+  float* mean_s = ws + 2 * CR * D * (int)sizeof(T) / 4;    // [2][D] partial sums, then means
+  float* etok_s = mean_s + 2 * D;                           // [2][32]
+  float* cd_s = etok_s + 64;                                // [K]
+  const size_t cix = (size_t)b * g.NC + ci;
+  const int s0 = w.cand_s0[cix], n0 = w.cand_n0[cix], s1 = w.cand_s1[cix], n1 = w.cand_n1[cix];
+  const int n = n0 + n1;
+  const float fn = (float)n;
   const T* snapk = static_cast<const T*>(w.snap_k);
   const T* snapv = static_cast<const T*>(w.snap_v);
   const T* reck = static_cast<const T*>(s.recent_k_raw);
   const T* recv = static_cast<const T*>(s.recent_v);
-  const int ncand = w.n_cand[b];
-  const size_t lane0 = ((size_t)b * G + grp) * K;
-  if (g.beta && blk < ncand) {
-    // The lane's centres and their mean squares, once per block (frozen during the flush).
-    for (int i = tid; i < K * D; i += nt) cent[i] = s.centroid[lane0 * D + i];
-    for (int c = tid; c < K; c += nt) cmm[c] = fdiv(w.cnorm[lane0 + c], (float)D);
-  }
-  for (int ci = blk; ci < ncand; ci += nblk) {
-    const size_t cix = (size_t)b * g.NC + ci;
-    const int s0 = w.cand_s0[cix], n0 = w.cand_n0[cix], s1 = w.cand_s1[cix], n1 = w.cand_n1[cix];
-    const int n = n0 + n1;
-    const float fn = (float)n;
-    float acc[kScoreFeat];
+  // Element (t, d) of staged component f: chunk d / VN of row t sits at chunk (d / VN) ^ (t & swz).
+  auto staged = [&](int f, int t, int d) -> const T* {
+    return rows + ((size_t)f * CR + t) * D + (((d / VN) ^ (t & swz)) * VN) + d % VN;
+  };
+  float eacc[2] = {0.f, 0.f};
+  for (int t0 = 0; t0 < n; t0 += CR) {
+    const int cn = min(CR, n - t0);
+    for (int item = lane; item < 2 * cn * DV; item += 32) {
+      const int f = item >= cn * DV ? 1 : 0, r = item - f * cn * DV, t = r / DV, c = r % DV;
+      const int tt = t0 + t;
+      const int src = tt < n0 ? s0 + tt : s1 + (tt - n0);
+      const T* row = f ? token_row<T>(g, snapv, recv, b, grp, src) : token_row<T>(g, snapk, reck, b, grp, src);
+      cp_async16(rows + ((size_t)f * CR + t) * D + ((c ^ (t & swz)) * VN), row + c * VN);
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncwarp();
 #pragma unroll
-    for (int j = 0; j < kScoreFeat; ++j) acc[j] = 0.f;
-    float eacc = 0.f;
-    const uint32_t* R = rows + comp * kScoreRows * WS;
-    for (int c0 = 0; c0 < n; c0 += kScoreRows) {
-      const int cn = min(kScoreRows, n - c0);
-      for (int r = warp; r < 2 * cn; r += nwarps) {
-        const int f = r >= cn ? 1 : 0, t = r - f * cn;
-        const int tt = c0 + t;
-        const int src = tt < n0 ? s0 + tt : s1 + (tt - n0);
-        const T* row = f ? token_row<T>(g, snapv, recv, b, grp, src) : token_row<T>(g, snapk, reck, b, grp, src);
-        uint32_t* dst = rows + (f * kScoreRows + t) * WS;
-        for (int v = lane; v < DV; v += 32) {
-          const uint4 u = *reinterpret_cast<const uint4*>(row + v * VN);
-          dst[4 * v] = u.x;
-          dst[4 * v + 1] = u.y;
-          dst[4 * v + 2] = u.z;
-          dst[4 * v + 3] = u.w;
-        }
-      }
-      __syncthreads();
-#pragma unroll
-      for (int j = 0; j < kScoreFeat; ++j) {
-        const int d = htid + j * half;
-        if (d < D) {
+    for (int f = 0; f < 2; ++f) {
+      // Mean partial sums: lane owns features f0 + 4 lane .. + 3, tokens in order.
+      for (int f0 = 0; f0 < D; f0 += 128) {
+        const int d = f0 + 4 * lane;
+        if (d >= D) continue;
+        float* ms = mean_s + f * D + d;
+        float a0 = t0 ? ms[0] : 0.f, a1 = t0 ? ms[1] : 0.f, a2 = t0 ? ms[2] : 0.f, a3 = t0 ? ms[3] : 0.f;
 #pragma unroll 8
-          for (int t = 0; t < cn; ++t) acc[j] = fadd(acc[j], staged_elem<T>(R + t * WS, d));
+        for (int t = 0; t < cn; ++t) {
+          const T* p = staged(f, t, d);  // 4 consecutive features never straddle a chunk
+          a0 = fadd(a0, Elem<T>::load(p));
+          a1 = fadd(a1, Elem<T>::load(p + 1));
+          a2 = fadd(a2, Elem<T>::load(p + 2));
+          a3 = fadd(a3, Elem<T>::load(p + 3));
         }
+        ms[0] = a0;
+        ms[1] = a1;
+        ms[2] = a2;
+        ms[3] = a3;
       }
-      for (int t = htid; t < cn; t += half) {
-        const uint32_t* row = R + t * WS;
+      // Energies: lane owns a token, features in order.
+      if (lane < cn) {
         float e = 0.f;
-#pragma unroll 8
-        for (int d = 0; d < D; ++d) {
-          const float x = staged_elem<T>(row, d);
-          e = fadd(e, fmul(x, x));
-        }
-        etok[comp * kScoreRows + t] = fdiv(e, (float)D);
-      }
-      __syncthreads();
-      if (htid == 0)
-        for (int t = 0; t < cn; ++t) eacc = fadd(eacc, etok[comp * kScoreRows + t]);
-      __syncthreads();
-    }
+#pragma unroll 4
+        for (int c = 0; c < DV; ++c) {
+          float x[VN];
+          unpack(*reinterpret_cast<const uint4*>(rows + ((size_t)f * CR + lane) * D + ((c ^ (lane & swz)) * VN)), x,
+                 (const T*)nullptr);
 #pragma unroll
-    for (int j = 0; j < kScoreFeat; ++j) {
-      const int d = htid + j * half;
-      if (d < D) mean[comp * D + d] = fdiv(acc[j], fn);
+          for (int j = 0; j < VN; ++j) e = fadd(e, fmul(x[j], x[j]));
+        }
+        etok_s[f * 32 + lane] = fdiv(e, (float)D);
+      }
     }
-    __syncthreads();
-    if (htid == 0) {
-      const float energy = fdiv(eacc, fn);
-      const float* mc = mean + comp * D;
+    __syncwarp();
+    if (lane == 0)
+      for (int f = 0; f < 2; ++f)
+        for (int k = 0; k < cn; ++k) eacc[f] = fadd(eacc[f], etok_s[f * 32 + k]);
+    __syncwarp();
+  }
+  for (int f = 0; f < 2; ++f)
+    for (int d = 4 * lane; d < D; d += 128)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) mean_s[f * D + d + j] = fdiv(mean_s[f * D + d + j], fn);
+  __syncwarp();
+  float part[2] = {0.f, 0.f}, ener0 = 0.f, kms = 0.f;
+  if (lane == 0) {
+#pragma unroll
+    for (int f = 0; f < 2; ++f) {
+      const float energy = fdiv(eacc[f], fn);
+      const float* mc = mean_s + f * D;
       float ms = 0.f;
 #pragma unroll 8
       for (int d = 0; d < D; ++d) ms = fadd(ms, fmul(mc[d], mc[d]));
       ms = fdiv(ms, (float)D);
-      sh_part[comp] = fdiv(fmaxf(fsub(energy, ms), 0.f), fmaxf(energy, 1e-12f));
-      sh_ener[comp] = energy;
-      sh_ms[comp] = ms;
-    }
-    __syncthreads();
-    float* out = w.gpart + (cix * G + grp) * 2;
-    if (!g.beta) {
-      if (tid == 0) {
-        out[0] = sh_part[0];
-        out[1] = sh_part[1];
+      part[f] = fdiv(fmaxf(fsub(energy, ms), 0.f), fmaxf(energy, 1e-12f));
+      if (f == 0) {
+        ener0 = energy;
+        kms = ms;
       }
-      __syncthreads();
-      continue;
     }
-    // Beta novelty: mean-square distance of the key mean to every live centre.
-    for (int c = tid; c < K; c += nt) {
-      float dist = INFINITY;
-      if (s.alive[lane0 + c]) {
-        const float* mu = cent + c * D;
-        float dot = 0.f;
+  }
+  float* out = w.gpart + (cix * G + grp) * 2;
+  if (!g.beta) {
+    if (lane == 0) {
+      out[0] = part[0];
+      out[1] = part[1];
+    }
+    return;
+  }
+  // Beta novelty: mean-square distance of the key mean to every live centre (lane owns a centre).
+  kms = __shfl_sync(0xffffffffu, kms, 0);
+  const size_t lane0 = ((size_t)b * G + grp) * K;
+  for (int c = lane; c < K; c += 32) {
+    float dist = INFINITY;
+    if (s.alive[lane0 + c]) {
+      const float4* mu = reinterpret_cast<const float4*>(s.centroid + (lane0 + c) * D);  // D % 4 == 0
+      float dot = 0.f;
 #pragma unroll 8
-        for (int d = 0; d < D; ++d) dot = fadd(dot, fmul(mean[d], mu[d]));
-        dot = fdiv(dot, (float)D);
-        dist = fmaxf(fsub(fadd(sh_ms[0], cmm[c]), fmul(2.f, dot)), 0.f);
+      for (int d4 = 0; d4 < D / 4; ++d4) {
+        const float4 m = mu[d4];
+        dot = fadd(dot, fmul(mean_s[4 * d4], m.x));
+        dot = fadd(dot, fmul(mean_s[4 * d4 + 1], m.y));
+        dot = fadd(dot, fmul(mean_s[4 * d4 + 2], m.z));
+        dot = fadd(dot, fmul(mean_s[4 * d4 + 3], m.w));
       }
-      cdist[c] = dist;
+      dot = fdiv(dot, (float)D);
+      dist = fmaxf(fsub(fadd(kms, fdiv(w.cnorm[lane0 + c], (float)D)), fmul(2.f, dot)), 0.f);
     }
-    __syncthreads();
-    if (tid == 0) {
-      bool any = false;
-      float nr = INFINITY;
-      for (int c = 0; c < K; ++c) {
-        any |= s.alive[lane0 + c] != 0;
-        nr = fminf(nr, cdist[c]);
-      }
-      if (!any) nr = 0.f;
-      const float nov = fdiv(nr, fmaxf(sh_ener[0], 1e-12f));
-      out[0] = fadd(fmul(fadd(sh_part[0], sh_part[1]), 0.5f), fdiv(nov, fadd(1.f, nov)));
+    cd_s[c] = dist;
+  }
+  __syncwarp();
+  if (lane == 0) {
+    bool any = false;
+    float nr = INFINITY;
+    for (int c = 0; c < K; ++c) {
+      any |= s.alive[lane0 + c] != 0;
+      nr = fminf(nr, cd_s[c]);
     }
-    __syncthreads();
+    if (!any) nr = 0.f;
+    const float nov = fdiv(nr, fmaxf(ener0, 1e-12f));
+    out[0] = fadd(fmul(fadd(part[0], part[1]), 0.5f), fdiv(nov, fadd(1.f, nov)));
   }
 }
 

@@ -17,12 +17,6 @@ namespace logkv {
 constexpr int kTileRows = 64;                 // multiple of 4 (Beta groups never straddle tiles)
 constexpr int kTileGroups = kTileRows / 4;
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
 
 // Sum 16 per-lane values over the warp; every lane gets all 16 sums.  Transposed
 // butterfly: each exchange halves the values a lane carries (16 shuffles), then one

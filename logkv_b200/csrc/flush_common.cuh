@@ -23,6 +23,14 @@ struct Geo {
   float eta, g0, lam;
 };
 
+// 16-byte asynchronous global -> shared copies (both addresses 16-byte aligned).
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
 enum JobType : int32_t { kJobNone = 0, kJobOrdinary = 1, kJobNew = 2, kJobLate = 3 };
 
 // Traffic counters (rows) accumulated across flushes in the workspace.

@@ -16,32 +16,60 @@ namespace logkv {
 // ---------------------------------------------------------------- K4: attach decisions
 // Decisions for every token of the [old pool | flushed window] index space (the archive
 // is a subset, picked later by the span choice; decisions depend only on the frozen
-// cluster state).  One thread per (token, cluster) computes the token's dot product and
-// exact squared distance to one centre, left to right over the features, and then the
-// semantic distance, routing cost and exact distance; one thread per token walks the
-// clusters in index order for the decision (first-index argmin, as torch.argmin).  Token
-// rows and centres are staged in shared memory with an odd word stride (conflict-free);
-// centre norms come from the snapshot kernel.  Outputs are indexed by token.
-template <typename T>
+// cluster state).  A token owns 16 (K <= 16) or 32 consecutive lanes, one per centre: each
+// computes the token's dot product with its centre left to right over the features, then
+// the semantic distance and routing cost; the token's winner is the first-index argmin of
+// the costs over live centres (as the reference's in-order scan / torch.argmin), found by a
+// shuffle reduction over the token's lanes.  Orphans then get exact distances to the live
+// centres the same way (nearest = first-index argmin).  Token rows and centres are staged
+// in shared memory (16-byte rows, conflict-free); centre norms come from the snapshot
+// kernel.  Outputs are indexed by token.  DC != 0 is a compile-time head dim.
+
+// First-index argmin over the `width` lanes of a token (width 16 or 32, aligned): lanes with
+// valid = false never win; returns the winning lane offset, or width if none is valid.
+__device__ __forceinline__ int group_argmin(float v, bool valid, int c, int width, float* best_v) {
+  float bv = valid ? v : INFINITY;
+  int bi = valid ? c : width;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    if (off >= width) continue;
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    if (ov < bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  *best_v = bv;
+  return bi;
+}
+
+constexpr int kAttachRounds = 1;  // token rounds per block (the staged centres are reused)
+
+template <typename T, int DC>
 __device__ void attach_body(const Geo& g, const logkv_state_t& s, const Work& w, int blk) {
   const int b = blockIdx.z, grp = blockIdx.y, tid = threadIdx.x;
-  const int D = g.D, K = g.K;
-  const int slots = K <= 16 ? 16 : 32;          // threads per token
-  const int ntok = blockDim.x / slots;          // tokens per block
-  const int r0 = blk * ntok;
-  if (r0 >= g.NW) return;
+  const int D = DC ? DC : g.D, K = g.K;
+  const int slots = K <= 16 ? 16 : 32;          // lanes per token
+  const int ntok = blockDim.x / slots;          // tokens per round
+  if (blk * kAttachRounds * ntok >= g.NW) return;
   extern __shared__ float4 sm4[];
   const int RS = D + 4;                          // row stride in floats: 16-byte rows, conflict-free
   float* mu = reinterpret_cast<float*>(sm4);     // [K][RS]
   float* xs = mu + K * RS;                       // [ntok][RS]
-  float* sem = xs + ntok * RS;                   // [ntok][K] raw dot, then semantic distance
-  float* exd = sem + ntok * K;                   // [ntok][K] exact distance (orphans only)
-  float* cst = exd + ntok * K;                   // [ntok][K] routing cost
   __shared__ float xxs[32];
   __shared__ int orph_tok[32];
   __shared__ int n_orph;
+  __shared__ float cn_s[kMaxClusters];
+  __shared__ long long phi_s[kMaxClusters];
+  __shared__ uint8_t alv_s[kMaxClusters];
   const size_t lane0 = ((size_t)b * g.G + grp) * K;
   if (tid == 0) n_orph = 0;
+  for (int cc = tid; cc < K; cc += blockDim.x) {
+    cn_s[cc] = w.cnorm[lane0 + cc];
+    phi_s[cc] = s.p_hi_c[lane0 + cc];
+    alv_s[cc] = s.alive[lane0 + cc] != 0;
+  }
   const int warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
   const int D4 = D / 4;
   // Centres and token rows into shared memory: one row per warp at a time, 16-byte units.
@@ -50,118 +78,116 @@ __device__ void attach_body(const Geo& g, const logkv_state_t& s, const Work& w,
     for (int d4 = lane; d4 < D4; d4 += 32) reinterpret_cast<float4*>(mu + cc * RS)[d4] = cent4[cc * D4 + d4];
   const T* snap = static_cast<const T*>(w.snap_k);
   const T* rec = static_cast<const T*>(s.recent_k_raw);
-  const int nrow = min(ntok, g.NW - r0);
-  constexpr int VN = Vec<T>::N;
-  const int DV = D / VN;
-  for (int row = warp; row < nrow; row += nwarps) {
-    const T* src = token_row<T>(g, snap, rec, b, grp, r0 + row);
-    for (int v = lane; v < DV; v += 32) {
-      float xv[VN];
-      unpack(*reinterpret_cast<const uint4*>(src + v * VN), xv, (const T*)nullptr);
+  for (int round = 0; round < kAttachRounds; ++round) {
+    const int r0 = (blk * kAttachRounds + round) * ntok;
+    if (r0 >= g.NW) break;   // uniform across the block
+    const int nrow = min(ntok, g.NW - r0);
+    constexpr int VN = Vec<T>::N;
+    const int DV = D / VN;
+    for (int row = warp; row < nrow; row += nwarps) {
+      const T* src = token_row<T>(g, snap, rec, b, grp, r0 + row);
+      for (int v = lane; v < DV; v += 32) {
+        float xv[VN];
+        unpack(*reinterpret_cast<const uint4*>(src + v * VN), xv, (const T*)nullptr);
 #pragma unroll
-      for (int e = 0; e < VN; e += 4)
-        *reinterpret_cast<float4*>(xs + row * RS + v * VN + e) = make_float4(xv[e], xv[e + 1], xv[e + 2], xv[e + 3]);
-    }
-  }
-  __syncthreads();
-  // Pass 1, one thread per (token, centre): the dot product, left to right over the features.
-  // When a lane of the token's group is spare (K < slots), lane K runs the same loop against
-  // the token itself, so its "dot" is |x|^2 (same operations).
-  const int tok = tid / slots, c = tid % slots;
-  const bool spare = K < slots;
-  if (tok < nrow && c <= (spare ? K : K - 1)) {
-    const float4* x = reinterpret_cast<const float4*>(xs + tok * RS);
-    const float4* m = reinterpret_cast<const float4*>(c < K ? mu + c * RS : xs + tok * RS);
-    float dot = 0.f;
-    for (int d4 = 0; d4 < D4; ++d4) {
-      const float4 xv = x[d4], mv = m[d4];
-      dot = fadd(dot, fmul(xv.x, mv.x));
-      dot = fadd(dot, fmul(xv.y, mv.y));
-      dot = fadd(dot, fmul(xv.z, mv.z));
-      dot = fadd(dot, fmul(xv.w, mv.w));
-    }
-    if (c < K) sem[tok * K + c] = dot;
-    else xxs[tok] = dot;
-  }
-  if (!spare && tok < nrow && c == 0) {
-    const float* x = xs + tok * RS;
-    float xx = 0.f;
-    for (int d = 0; d < D; ++d) xx = fadd(xx, fmul(x[d], x[d]));
-    xxs[tok] = xx;
-  }
-  __syncthreads();
-  // Pass 2, one thread per (token, centre): semantic distance and routing cost.
-  const int r = r0 + tok;   // token index
-  if (tok < nrow && c < K) {
-    const int64_t pos = token_position(g, s, w, b, r);
-    const float semv = fmaxf(fsub(fadd(xxs[tok], w.cnorm[lane0 + c]), fmul(2.f, sem[tok * K + c])), 0.f);
-    const float gap = fmaxf((float)(pos - (int64_t)s.p_hi_c[lane0 + c]), 0.f);
-    sem[tok * K + c] = semv;
-    cst[tok * K + c] = fadd(semv, fmul(g.eta, fdiv(gap, fadd(gap, g.g0))));
-  }
-  __syncthreads();
-  // Decision, one thread per token: centres in index order (first-index argmin, as
-  // torch.argmin).  Direct joins are final; orphans of a lane with live centres queue for
-  // the exact distances.
-  const size_t o = ((size_t)b * g.G + grp) * g.NW + r;
-  if (c == 0 && tok < nrow) {
-    const float thresh = fmul(g.lam, s.s_h[(size_t)b * g.G + grp]);
-    float best_cost = INFINITY, s_win = 0.f;
-    int winner = 0;
-    bool any_alive = false;
-    for (int cc = 0; cc < K; ++cc) {
-      if (!s.alive[lane0 + cc]) continue;
-      any_alive = true;
-      if (cst[tok * K + cc] < best_cost) {
-        best_cost = cst[tok * K + cc];
-        winner = cc;
-        s_win = sem[tok * K + cc];
+        for (int e = 0; e < VN; e += 4)
+          *reinterpret_cast<float4*>(xs + row * RS + v * VN + e) = make_float4(xv[e], xv[e + 1], xv[e + 2], xv[e + 3]);
       }
     }
-    if (!any_alive) s_win = sem[tok * K];   // winner 0; the token is an orphan
-    const bool direct = any_alive && s_win <= thresh;
-    w.orphan[o] = direct ? 0 : 1;
-    w.s_winner[o] = s_win;
-    if (direct || !any_alive) w.assign_tok[o] = (int8_t)winner;   // no live centre: 0
-    else orph_tok[atomicAdd(&n_orph, 1)] = tok;
-  }
-  __syncthreads();
-  const int no = n_orph;
-  if (no == 0) return;
-  // Exact distances of the queued orphans to the live centres, one thread per pair.
-  for (int item = tid; item < no * K; item += blockDim.x) {
-    const int t = orph_tok[item / K], cc = item % K;
-    float dist = INFINITY;
-    if (s.alive[lane0 + cc]) {
-      const float4* x = reinterpret_cast<const float4*>(xs + t * RS);
-      const float4* m = reinterpret_cast<const float4*>(mu + cc * RS);
-      float ex = 0.f;
+    __syncthreads();
+    // Pass 1, one lane per (token, centre): the dot product, left to right over the features.
+    // When a lane of the token's group is spare (K < slots), lane K runs the same loop against
+    // the token itself, so its "dot" is |x|^2 (same operations).
+    const int tok = tid / slots, c = tid % slots;
+    const bool spare = K < slots;
+    const bool live_tok = tok < nrow;
+    float dot = 0.f;
+    if (live_tok && c <= (spare ? K : K - 1)) {
+      const float4* x = reinterpret_cast<const float4*>(xs + tok * RS);
+      const float4* m = reinterpret_cast<const float4*>(c < K ? mu + c * RS : xs + tok * RS);
+#pragma unroll(DC ? 8 : 1)
       for (int d4 = 0; d4 < D4; ++d4) {
         const float4 xv = x[d4], mv = m[d4];
-        float df = fsub(xv.x, mv.x);
-        ex = fadd(ex, fmul(df, df));
-        df = fsub(xv.y, mv.y);
-        ex = fadd(ex, fmul(df, df));
-        df = fsub(xv.z, mv.z);
-        ex = fadd(ex, fmul(df, df));
-        df = fsub(xv.w, mv.w);
-        ex = fadd(ex, fmul(df, df));
+        dot = fadd(dot, fmul(xv.x, mv.x));
+        dot = fadd(dot, fmul(xv.y, mv.y));
+        dot = fadd(dot, fmul(xv.z, mv.z));
+        dot = fadd(dot, fmul(xv.w, mv.w));
       }
-      dist = __fsqrt_rn(ex);
+      if (c == K) xxs[tok] = dot;
     }
-    exd[t * K + cc] = dist;
-  }
-  __syncthreads();
-  for (int j = tid; j < no; j += blockDim.x) {
-    const int t = orph_tok[j];
-    float best = INFINITY;
-    int nearest = 0;
-    for (int cc = 0; cc < K; ++cc)
-      if (exd[t * K + cc] < best) {
-        best = exd[t * K + cc];
-        nearest = cc;
+    if (!spare && live_tok && c == 0) {
+      const float* x = xs + tok * RS;
+      float xx = 0.f;
+      for (int d = 0; d < D; ++d) xx = fadd(xx, fmul(x[d], x[d]));
+      xxs[tok] = xx;
+    }
+    __syncthreads();
+    // Pass 2, one lane per (token, centre): semantic distance and routing cost; then the
+    // token's decision by a shuffle argmin over its lanes.
+    const int r = r0 + tok;   // token index
+    const bool mine = live_tok && c < K;
+    const bool alive_c = mine && alv_s[c];
+    float semv = 0.f, cost = INFINITY;
+    if (mine) {
+      const int64_t pos = token_position(g, s, w, b, r);
+      semv = fmaxf(fsub(fadd(xxs[tok], cn_s[c]), fmul(2.f, dot)), 0.f);
+      const float gap = fmaxf((float)(pos - (int64_t)phi_s[c]), 0.f);
+      cost = fadd(semv, fmul(g.eta, fdiv(gap, fadd(gap, g.g0))));
+    }
+    const unsigned gmask = (slots == 32 ? 0xffffffffu : 0xffffu) << (lane & ~(slots - 1) & 31);
+    const bool any_alive = (__ballot_sync(0xffffffffu, alive_c) & gmask) != 0u;
+    float best_cost;
+    // Live centres with a cost below +inf compete (NaN and +inf never replace the initial +inf).
+    const int wi = group_argmin(cost, alive_c && cost < INFINITY, c, slots, &best_cost);
+    const int winner = wi < slots ? wi : 0;
+    const int src_lane = (lane & ~(slots - 1)) + winner;
+    const float sem_win = __shfl_sync(0xffffffffu, semv, src_lane);
+    // No live centre: winner 0 with cluster 0's semantic distance (the token is an orphan);
+    // live centres but no finite cost: winner 0 with s = 0 (the scan's initial values).
+    const float s_win = !any_alive ? sem_win : (wi < slots ? sem_win : 0.f);
+    const size_t o = ((size_t)b * g.G + grp) * g.NW + r;
+    if (live_tok && c == 0) {
+      const float thresh = fmul(g.lam, s.s_h[(size_t)b * g.G + grp]);
+      const bool direct = any_alive && s_win <= thresh;
+      w.orphan[o] = direct ? 0 : 1;
+      w.s_winner[o] = s_win;
+      if (direct || !any_alive) w.assign_tok[o] = (int8_t)winner;   // no live centre: 0
+      else orph_tok[atomicAdd(&n_orph, 1)] = tok;
+    }
+    __syncthreads();
+    const int no = n_orph;
+    if (no > 0) {
+      // Exact distances of the queued orphans to the live centres: orphan j takes the lanes of
+      // token slot j; nearest = first-index argmin (NaN and +inf never win; none: centre 0).
+      const int j = tok;
+      float dist = INFINITY;
+      const bool act = j < no && c < K && alv_s[c];
+      if (act) {
+        const int t = orph_tok[j];
+        const float4* x = reinterpret_cast<const float4*>(xs + t * RS);
+        const float4* m = reinterpret_cast<const float4*>(mu + c * RS);
+        float ex = 0.f;
+#pragma unroll(DC ? 8 : 1)
+        for (int d4 = 0; d4 < D4; ++d4) {
+          const float4 xv = x[d4], mv = m[d4];
+          float df = fsub(xv.x, mv.x);
+          ex = fadd(ex, fmul(df, df));
+          df = fsub(xv.y, mv.y);
+          ex = fadd(ex, fmul(df, df));
+          df = fsub(xv.z, mv.z);
+          ex = fadd(ex, fmul(df, df));
+          df = fsub(xv.w, mv.w);
+          ex = fadd(ex, fmul(df, df));
+        }
+        dist = __fsqrt_rn(ex);
       }
-    w.assign_tok[((size_t)b * g.G + grp) * g.NW + r0 + t] = (int8_t)nearest;
+      float best_d;
+      const int ni = group_argmin(dist, act && dist < INFINITY, c, slots, &best_d);
+      if (j < no && c == 0)
+        w.assign_tok[((size_t)b * g.G + grp) * g.NW + r0 + orph_tok[j]] = (int8_t)(ni < slots ? ni : 0);
+    }
+    __syncthreads();  // token rows and the orphan queue are reused by the next round
+    if (tid == 0) n_orph = 0;
   }
 }
 
