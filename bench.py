@@ -12,10 +12,13 @@ the path); span boundaries every 23rd token.
 
 value     = device time per flush (chunk x layer), us, CUDA-graph replay of whole
             steps with inputs resident in HBM (each step's 5.6 GB of chunk inputs is
-            larger than L2).
+            larger than L2).  Layer l's add_recent calls run on stream l % --streams
+            (default 14): the layers' caches are independent, so their flushes overlap,
+            while each layer's chunks stay in order on its stream.
 e2e       = the same metric through the public API: add_recent called eagerly per
-            chunk and layer, with every chunk's K, pre-RoPE K and V copied from pinned
-            host memory inside the timed region and the cache's alpha_count read back.
+            chunk and layer on the layers' streams, with every chunk's K, pre-RoPE K, V
+            and span-end flags copied from pinned host memory inside the timed region
+            and every layer's alpha_count read back.
 roofline  = the ladder cascade kernel (the dominant flush stage): algorithmic
             bytes of its rows (549 B per bf16 row: K and V 256 B each, w 4 B,
             p_lo/p_hi/sum_wp/order 8 B each, pad 1 B) over its CUDA-event time,
