@@ -161,6 +161,26 @@ LOGKV_API int logkv_flush_commit(const logkv_layout_t* layout, const logkv_state
 LOGKV_API int logkv_flush_partials(const logkv_layout_t* layout, int32_t flush_tokens, void* workspace,
                                    float** partials, size_t* count);
 
+/*
+ * Update tape (replaces the record / replay branches of route_and_flush_batch,
+ * litgpt/log_kv_cache.py:4946-5031, with the _SemanticReplayUpdates store :111-137).
+ * logkv_flush_record is logkv_flush that also writes, into a caller-owned device buffer of
+ * logkv_tape_bytes (16-byte aligned): the flushed window rows (pre-RoPE K, V) as the flush
+ * saw them, the kept / archived token lists, the new span table, the per-cluster plan and
+ * every Beta cut of the cascade.  logkv_flush_replay applies such a record to a cache in the
+ * state the recorded flush started from: the recorded rows replace the window's flushed rows,
+ * nothing is routed, scored or chosen, and the cache ends exactly as the recorded flush left
+ * it (buffers bit for bit).  The order of replays is the caller's to keep (the Python cache
+ * checks it).  Neither runs KV-head sharded.
+ */
+LOGKV_API size_t logkv_tape_bytes(const logkv_layout_t* layout, int32_t flush_tokens);
+LOGKV_API int logkv_flush_record(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                 int32_t recent_count, void* workspace, size_t workspace_bytes, void* tape,
+                                 size_t tape_bytes, void* stream);
+LOGKV_API int logkv_flush_replay(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                 int32_t recent_count, void* workspace, size_t workspace_bytes, const void* tape,
+                                 size_t tape_bytes, void* stream);
+
 /* Copy the workspace status word to *out (synchronizes `stream`); nonzero = a capacity was exceeded. */
 LOGKV_API int logkv_read_status(const void* workspace, int32_t* out, void* stream);
 

@@ -101,6 +101,12 @@ def lib() -> ctypes.CDLL:
         handle.logkv_flush_partials.restype = ctypes.c_int
         handle.logkv_flush_partials.argtypes = [P(Layout), ctypes.c_int32, ctypes.c_void_p,
                                                 P(P(ctypes.c_float)), P(ctypes.c_size_t)]
+        handle.logkv_tape_bytes.restype = ctypes.c_size_t
+        handle.logkv_tape_bytes.argtypes = [P(Layout), ctypes.c_int32]
+        handle.logkv_flush_record.restype = ctypes.c_int
+        handle.logkv_flush_record.argtypes = flush_args + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+        handle.logkv_flush_replay.restype = ctypes.c_int
+        handle.logkv_flush_replay.argtypes = flush_args + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
         handle.logkv_attention_plan.restype = ctypes.c_int
         handle.logkv_attention_plan.argtypes = [P(Layout), P(State), P(Plan), ctypes.c_void_p]
         handle.logkv_pack_prefix.restype = ctypes.c_int

@@ -13,6 +13,7 @@ host synchronization; the reference's host mirrors (``_semantic_counts``,
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import math
 
@@ -43,6 +44,36 @@ def ladder_geometry(max_seq_length: int, k_dim: int, v_dim: int, n_groups: int, 
         if n_groups * clusters * lv * (cand * entry + 2) + exact_bytes <= baseline:
             return cand, lv
     raise ValueError("compressed ladder budget is too small for alpha_exact_tokens; increase B or reduce exact capacity")
+
+
+class _SemanticReplayUpdates:
+    """Update tape of one training invocation (the reference's _SemanticReplayUpdates,
+    litgpt/log_kv_cache.py:111-137): one device record per flush, written by
+    ``logkv_flush_record`` and applied by ``logkv_flush_replay``.
+
+    ``flushes`` maps a flush key (the cache's flush index since its last reset, the flushed
+    token count and the window fill) to (signature, tensor index, ready event); ``tensors``
+    holds the device records.
+    """
+
+    def __init__(self, flushes=None, tensors=None):
+        self.flushes = {} if flushes is None else flushes
+        self.tensors = [] if tensors is None else tensors
+
+    def wait(self, device):
+        """Make the current stream wait until every record has been written (no host sync)."""
+        if torch.device(device).type == "cuda":
+            stream = torch.cuda.current_stream(device)
+            for record in self.flushes.values():
+                if record[-1] is not None:
+                    stream.wait_event(record[-1])
+
+    def save(self, tensor, owned=False):
+        if tensor is None:
+            return None
+        index = len(self.tensors)
+        self.tensors.append(tensor.detach() if owned else tensor.detach().clone())
+        return index
 
 
 class LogStructuredKVCache(nn.Module):
@@ -195,6 +226,10 @@ class LogStructuredKVCache(nn.Module):
         self.kv_shard_group = kv_shard_group
         self._span_gather = None
         self._ladder_epoch = 0       # bumped whenever a flush or reset rewrites the ladder / exact pool
+        self._flush_cursor = 0       # flushes since the last reset (orders update-tape records)
+        self._active_updates = None  # update tape being recorded or replayed
+        self._replaying_updates = False
+        self._update_actions = None
         self.profile_events = None   # set to a list of LOGKV_FLUSH_STAGES+1 torch.cuda.Event to time stages
 
     # ------------------------------------------------------------------ C-ABI state
@@ -219,6 +254,66 @@ class LogStructuredKVCache(nn.Module):
                      alpha_rowcount=self._row_count, alpha_count=self._alpha_count_dev)
         self._state = _lib.State(**{name: _lib.ptr(t) for name, t in views.items()})
         return self._state
+
+    @contextlib.contextmanager
+    def _semantic_update_context(self, updates, *, replay=False):
+        """Record flushes into ``updates`` (replay=False) or apply its records (replay=True)."""
+        previous = self._active_updates, self._replaying_updates
+        self._active_updates, self._replaying_updates = updates, replay
+        try:
+            yield
+        finally:
+            self._active_updates, self._replaying_updates = previous
+
+    def _update_signature(self, take: int):
+        L = self._layout
+        return (L.batch, L.groups, L.dim, L.clusters, L.levels, L.slots, L.recent_capacity, L.exact, L.span_cap,
+                L.beta, L.dtype, L.eta, L.g0, L.lam, int(take), int(self.recent_count))
+
+    def _flush_with_updates(self, take: int, record_op_log: bool, replay: bool) -> None:
+        """One flush under an update context: record it, or replay its record without routing."""
+        updates = self._active_updates
+        key = (self._flush_cursor, int(take), int(self.recent_count))
+        lib = _lib.lib()
+        dev = self.level_k.device
+        if self._replaying_updates:
+            if not replay or key not in updates.flushes:
+                if replay and any(k[0] < key[0] for k in updates.flushes):
+                    raise RuntimeError("semantic update replay flushes are out of order")
+                raise RuntimeError("missing semantic update record; rerouting is not allowed")
+            signature, index, ready = updates.flushes[key]
+            if signature != self._update_signature(take):
+                raise RuntimeError("semantic update record does not match this flush/configuration")
+            tape = updates.tensors[index]
+            stream = torch.cuda.current_stream(dev)
+            if ready is not None:
+                stream.wait_event(ready)   # device-side wait only
+            tape.record_stream(stream)
+            self._ladder_epoch += 1
+            state = self._state_struct()
+            _lib.check(lib.logkv_flush_replay(
+                ctypes.byref(self._layout), ctypes.byref(state), int(take), int(self.recent_count),
+                ctypes.c_void_p(self._workspace.data_ptr()), self._workspace.numel(), ctypes.c_void_p(tape.data_ptr()),
+                tape.numel(), ctypes.c_void_p(_lib.stream_ptr(dev))), "logkv_flush_replay")
+            return
+        if replay or key in updates.flushes:
+            raise RuntimeError("duplicate or incorrectly bound semantic update recording")
+        if not record_op_log:
+            raise RuntimeError("semantic update recording requires record_op_log=True")
+        if self.kv_shard_group is not None:
+            raise NotImplementedError("update recording is not implemented for KV-head-sharded caches")
+        nbytes = lib.logkv_tape_bytes(ctypes.byref(self._layout), int(take))
+        tape = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self._ladder_epoch += 1
+        state = self._state_struct()
+        _lib.check(lib.logkv_flush_record(
+            ctypes.byref(self._layout), ctypes.byref(state), int(take), int(self.recent_count),
+            ctypes.c_void_p(self._workspace.data_ptr()), self._workspace.numel(), ctypes.c_void_p(tape.data_ptr()),
+            tape.numel(), ctypes.c_void_p(_lib.stream_ptr(dev))), "logkv_flush_record")
+        ready = torch.cuda.Event()
+        ready.record(torch.cuda.current_stream(dev))
+        index = updates.save(tape, owned=True)
+        updates.flushes[key] = (self._update_signature(take), index, ready)
 
     def flush_device(self, take: int) -> None:
         """One device flush of the ``take`` oldest window tokens plus the window shift."""
@@ -298,8 +393,10 @@ class LogStructuredKVCache(nn.Module):
         """
         if k_raw is None:
             raise ValueError("semantic LogKV add_recent requires pre-RoPE k_raw")
-        if record_op_log or any(v_ is not None for v_ in replay.values()):
-            raise NotImplementedError("op-log recording and replay are not implemented by logkv_b200")
+        replaying = any(v_ is not None for v_ in replay.values())
+        if self._active_updates is None and (record_op_log or replaying):
+            raise NotImplementedError("op-log recording and replay outside an update tape context are not "
+                                      "implemented by logkv_b200")
         n = k.size(2)
         if n > self.recent_size:
             raise ValueError(f"chunk size {n} exceeds recent_size {self.recent_size}")
@@ -334,7 +431,11 @@ class LogStructuredKVCache(nn.Module):
                 take = min(gran, pending)
                 if take > self.recent_count:
                     raise RuntimeError(f"semantic LogKV cannot flush {take} tokens from recent_count={self.recent_count}")
-                self.flush_device(take)
+                if self._active_updates is not None:
+                    self._flush_with_updates(take, record_op_log, replaying or self._replaying_updates)
+                else:
+                    self.flush_device(take)
+                self._flush_cursor += 1
                 self.recent_count -= take
                 pending -= take
 
@@ -408,4 +509,5 @@ class LogStructuredKVCache(nn.Module):
             t.zero_()
         self.token_count = 0
         self.recent_count = 0
+        self._flush_cursor = 0
         self._ladder_epoch += 1

@@ -20,6 +20,7 @@
 #include "flush_cascade.cuh"
 #include "flush_ladder.cuh"
 #include "flush_route.cuh"
+#include "flush_tape.cuh"
 
 namespace logkv {
 
@@ -304,6 +305,35 @@ static int validate(const logkv_layout_t* L, int F) {
   return LOGKV_OK;
 }
 
+// The decision arrays of a flush: workspace and state <-> tape (to_tape selects the direction).
+static TapeSegs tape_segments(const Geo& g, const logkv_state_t& s, const Work& w, const TapeView& t, bool to_tape) {
+  TapeSegs segs{};
+  const size_t B = g.B, G = g.G, K = g.K, P = g.P, NW = g.NW;
+  auto add = [&](void* live, void* rec, size_t bytes) {
+    segs.src[segs.n] = to_tape ? live : rec;
+    segs.dst[segs.n] = to_tape ? rec : live;
+    segs.bytes[segs.n] = bytes;
+    ++segs.n;
+  };
+  add(w.keep_idx, t.keep_idx, B * P * 4);
+  add(w.nkeep, t.nkeep, B * 4);
+  add(w.arch_idx, t.arch_idx, B * NW * 4);
+  add(w.narch, t.narch, B * 4);
+  add(s.alpha_span_len, t.span_len, B * P * 4);
+  add(s.alpha_span_closed, t.span_closed, B * P);
+  add(s.alpha_nspans, t.nspans, B * 4);
+  add(s.alpha_rowcount, t.rowcount, B * 4);
+  add(s.alpha_count, t.alpha_count, 4);
+  add(w.tok_list, t.tok_list, B * G * NW * 4);
+  add(w.plan_off, t.plan_off, B * G * K * 4);
+  add(w.plan_n, t.plan_n, B * G * K * 4);
+  add(w.plan_type, t.plan_type, B * G * K * 4);
+  add(w.plan_m0, t.plan_m0, B * G * K * 4);
+  add(w.plan_scr, t.plan_scr, B * G * K * 4);
+  add(w.plan_base, t.plan_base, B * G * K * 8);
+  return segs;
+}
+
 // Phases: kPhaseScores = snapshot, span cut, span scores (the group parts of this rank);
 // kPhaseCommit = everything from the bounded greedy on.  A KV-head-sharded flush
 // all-gathers the group parts between the two.
@@ -311,7 +341,7 @@ constexpr int kPhaseScores = 1, kPhaseCommit = 2, kPhaseAll = 3;
 
 template <typename T>
 static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st, cudaEvent_t* ev,
-                        int phases = kPhaseAll) {
+                        int phases = kPhaseAll, const TapeView* tape = nullptr) {
   int stage = 0;
   auto mark = [&]() {
     if (ev) cudaEventRecord(ev[stage], st);
@@ -319,6 +349,9 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   };
   const int sm_count = 148;
   const int per_bg = std::max(1, std::min(64, (g.P * g.D / (int)(16 / sizeof(T)) + 255) / 256));
+  const int per_pay = std::max(1, std::min(64, (g.F * g.D / (int)(16 / sizeof(T)) + 255) / 256));
+  // Recording: the flushed window rows as this flush sees them, before anything moves.
+  if (tape) launch_pdl(tape_payload_kernel<T>, dim3(per_pay, g.G, g.B), 256, 0, st, g, s, *tape, 1);
   if (phases & kPhaseScores) {
   mark();
   launch_pdl(snapshot_kernel<T>, dim3(per_bg, g.G, g.B), 256, 0, st, g, s, w);
@@ -384,12 +417,49 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   if (staged) launch_pdl(window_stage_kernel<T>, dim3(per_win, g.G, g.B), 256, 0, st, g, s, w, rem);
   launch_pdl(window_shift_kernel<T>, dim3(per_win, g.G, g.B), 256, 0, st, g, s, w, rem, staged);
   mark();
+  // Recording: the decisions (workspace) and the new span table (state) into the tape.
+  if (tape) launch_pdl(tape_copy_kernel, dim3(2 * sm_count), 256, 0, st, tape_segments(g, s, w, *tape, true));
+  return (int)cudaGetLastError();
+}
+
+// Replay of a recorded flush: the recorded payload replaces the window's flushed rows, the
+// recorded decisions replace the span cut / scores / choice / attach / seeding / plan kernels,
+// and the cascade takes the recorded Beta cuts; the state transition is the recorded one.
+template <typename T>
+static int launch_replay(const Geo& g, const logkv_state_t& s, const Work& w, const TapeView& tape, cudaStream_t st) {
+  const int sm_count = 148;
+  const int per_bg = std::max(1, std::min(64, (g.P * g.D / (int)(16 / sizeof(T)) + 255) / 256));
+  const int per_pay = std::max(1, std::min(64, (g.F * g.D / (int)(16 / sizeof(T)) + 255) / 256));
+  launch_pdl(snapshot_kernel<T>, dim3(per_bg, g.G, g.B), 256, 0, st, g, s, w);
+  launch_pdl(tape_payload_kernel<T>, dim3(per_pay, g.G, g.B), 256, 0, st, g, s, tape, 0);
+  launch_pdl(tape_copy_kernel, dim3(2 * sm_count), 256, 0, st, tape_segments(g, s, w, tape, false));
+  const size_t prep_smem = prep_smem_bytes(g, sizeof(T));
+  if (prep_smem > 48 * 1024)
+    cudaFuncSetAttribute(prepare_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
+  launch_pdl(prepare_kernel<T>, dim3(g.K, g.G, g.B), 256, prep_smem, st, g, s, w);
+  const size_t casc_smem = cascade_smem(g, sizeof(T));
+  if (g.beta) {
+    if (g.D == 128) launch_cascade<T, true, 128>(g, s, w, casc_smem, st);
+    else if (g.D == 64) launch_cascade<T, true, 64>(g, s, w, casc_smem, st);
+    else launch_cascade<T, true, 0>(g, s, w, casc_smem, st);
+  } else {
+    if (g.D == 128) launch_cascade<T, false, 128>(g, s, w, casc_smem, st);
+    else if (g.D == 64) launch_cascade<T, false, 64>(g, s, w, casc_smem, st);
+    else launch_cascade<T, false, 0>(g, s, w, casc_smem, st);
+  }
+  launch_pdl(pool_rewrite_kernel<T>, dim3(per_bg, g.G, g.B), 256, 0, st, g, s, w);
+  const int rem = g.recent_count - g.F;
+  const int per_win = std::max(1, std::min(128, (g.recent_count * g.D / (int)(16 / sizeof(T)) + 255) / 256));
+  const int staged = rem > g.F ? 1 : 0;
+  if (staged) launch_pdl(window_stage_kernel<T>, dim3(per_win, g.G, g.B), 256, 0, st, g, s, w, rem);
+  launch_pdl(window_shift_kernel<T>, dim3(per_win, g.G, g.B), 256, 0, st, g, s, w, rem, staged);
   return (int)cudaGetLastError();
 }
 
 static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
                      int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream, cudaEvent_t* ev,
-                     int phases = kPhaseAll, const float* gpart_all = nullptr, int ranks = 1) {
+                     int phases = kPhaseAll, const float* gpart_all = nullptr, int ranks = 1,
+                     int tape_mode = kTapeNone, void* tape = nullptr, size_t tape_bytes = 0) {
   const int v = validate(layout, flush_tokens);
   if (v != LOGKV_OK) return v;
   if (!state || !workspace) return LOGKV_E_POINTER;
@@ -420,6 +490,20 @@ static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, i
     return LOGKV_E_SMEM;
   w.gpart_all = gpart_all;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (tape_mode != kTapeNone) {
+    TapeView t{};
+    if (!tape || (reinterpret_cast<uintptr_t>(tape) & 15) != 0 || ranks != 1 || phases != kPhaseAll)
+      return LOGKV_E_POINTER;
+    if (tape_bytes < tape_carve(g, esize, static_cast<char*>(tape), &t)) return LOGKV_E_WORKSPACE;
+    g.tape = tape_mode;
+    w.tape_cuts = t.cuts;
+    if (tape_mode == kTapeReplay) {
+      if (layout->dtype == LOGKV_DTYPE_BF16) return launch_replay<__nv_bfloat16>(g, *state, w, t, st);
+      return launch_replay<float>(g, *state, w, t, st);
+    }
+    if (layout->dtype == LOGKV_DTYPE_BF16) return launch_flush<__nv_bfloat16>(g, *state, w, st, ev, phases, &t);
+    return launch_flush<float>(g, *state, w, st, ev, phases, &t);
+  }
   if (layout->dtype == LOGKV_DTYPE_BF16) return launch_flush<__nv_bfloat16>(g, *state, w, st, ev, phases);
   return launch_flush<float>(g, *state, w, st, ev, phases);
 }
@@ -438,6 +522,27 @@ extern "C" size_t logkv_flush_workspace_bytes(const logkv_layout_t* layout, int3
 extern "C" int logkv_flush(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
                            int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream) {
   return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream, nullptr);
+}
+
+extern "C" size_t logkv_tape_bytes(const logkv_layout_t* layout, int32_t flush_tokens) {
+  if (validate(layout, flush_tokens) != LOGKV_OK) return 0;
+  const Geo g = make_geo(*layout, flush_tokens, layout->recent_capacity);
+  TapeView t{};
+  return tape_carve(g, layout->dtype == LOGKV_DTYPE_BF16 ? 2 : 4, nullptr, &t);
+}
+
+extern "C" int logkv_flush_record(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                  int32_t recent_count, void* workspace, size_t workspace_bytes, void* tape,
+                                  size_t tape_bytes, void* stream) {
+  return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream, nullptr,
+                   kPhaseAll, nullptr, 1, kTapeRecord, tape, tape_bytes);
+}
+
+extern "C" int logkv_flush_replay(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                  int32_t recent_count, void* workspace, size_t workspace_bytes, const void* tape,
+                                  size_t tape_bytes, void* stream) {
+  return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream, nullptr,
+                   kPhaseAll, nullptr, 1, kTapeReplay, const_cast<void*>(tape), tape_bytes);
 }
 
 extern "C" int logkv_flush_scores(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,

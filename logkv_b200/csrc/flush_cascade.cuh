@@ -11,6 +11,7 @@
 #pragma once
 
 #include "flush_ladder.cuh"
+#include "flush_tape.cuh"
 
 namespace logkv {
 
@@ -376,6 +377,14 @@ __global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Wo
           for (int j = tid; j < jn; j += nt) x.put_scratch(nb, j0 + j, merge_meta(tm[2 * j], tm[2 * j + 1]));
         } else {
           const int qn = (mend - t0 + 3) / 4;  // groups of this tile (tile rows 4q..4q+3)
+          // Recorded cuts of this (lane, level, tile): written when recording, read when replaying.
+          uint8_t* tcut = g.tape != kTapeNone
+                              ? w.tape_cuts + ((size_t)x.lane * g.L + ell) * tape_cut_stride(g) + t0 / 4
+                              : nullptr;
+          if (g.tape == kTapeReplay) {
+            for (int q = tid; q < qn; q += nt) bcut[q] = tcut[q];
+            __syncthreads();
+          } else {
           // Certified warp-parallel cut per group; near ties fall back to the canonical order below.
           const int warp = tid >> 5, lane = tid & 31, nwarps = nt >> 5;
           for (int q = warp; q < qn; q += nwarps) {
@@ -467,6 +476,9 @@ __global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Wo
             atomicAdd(&w.counters[kCntExactCuts], (unsigned long long)sh_exact);
             sh_exact = 0;
           }
+          }
+          if (g.tape == kTapeRecord)
+            for (int q = tid; q < qn; q += nt) tcut[q] = (uint8_t)bcut[q];
           }
           // Apply: per output side, sum over member rows (row order) of w*x / max(mass, 1e-12).
           for (int item = tid; item < qn * 2 * 2 * DV; item += nt) {

@@ -20,6 +20,7 @@ struct Geo {
   int sort_cap;           // power of two >= L * Bs + NW (delayed re-insert sort)
   int seed_staged;        // seeding CTAs keep their token rows in shared memory (set per dtype at launch)
   int shard_ranks;        // KV-head sharding: ranks holding G groups each (1 = unsharded)
+  int tape;               // update tape: kTapeNone, kTapeRecord (save Beta cuts), kTapeReplay (use them)
   float eta, g0, lam;
 };
 
@@ -30,6 +31,8 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+enum TapeMode : int { kTapeNone = 0, kTapeRecord = 1, kTapeReplay = 2 };
 
 enum JobType : int32_t { kJobNone = 0, kJobOrdinary = 1, kJobNew = 2, kJobLate = 3 };
 
@@ -73,6 +76,7 @@ struct Work {
   uint8_t* orphan;         // [B,G,NW] token index order
   float* s_winner;         // [B,G,NW] token index order
   float* cnorm;            // [B,G,K] sum_d mu_d^2 of every centre (left to right), before the flush
+  uint8_t* tape_cuts;      // update tape's Beta cuts [B,G,K,L,cut stride] (record / replay), else null
   int32_t* tok_list;       // [B,G,NW] archive ranks grouped by cluster (stable)
   int32_t* plan_off;       // [B,G,K] offset into tok_list
   int32_t* plan_n;         // [B,G,K] tokens joining the cluster
