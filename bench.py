@@ -13,7 +13,7 @@ the path); span boundaries every 23rd token.
 value     = device time per flush (chunk x layer), us, CUDA-graph replay of whole
             steps with inputs resident in HBM (each step's 5.6 GB of chunk inputs is
             larger than L2).  Layer l's add_recent calls run on stream l % --streams
-            (default 14): the layers' caches are independent, so their flushes overlap,
+            (default 28): the layers' caches are independent, so their flushes overlap,
             while each layer's chunks stay in order on its stream.
 e2e       = the same metric through the public API: add_recent called eagerly per
             chunk and layer on the layers' streams, with every chunk's K, pre-RoPE K, V
@@ -612,7 +612,7 @@ def main():
     ap.add_argument("--layers", type=int, default=WORKLOAD["layers"], help="layer caches (profiling runs only)")
     ap.add_argument("--decode-steps", type=int, default=32, help="timed decode steps (0: skip the decode leg)")
     ap.add_argument("--decode-batch", type=int, default=DECODE["batch"], help="decode sequences (profiling runs only)")
-    ap.add_argument("--streams", type=int, default=14, help="streams the layers' flushes are spread over")
+    ap.add_argument("--streams", type=int, default=28, help="streams the layers' flushes are spread over")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

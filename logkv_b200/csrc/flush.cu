@@ -72,7 +72,7 @@ template <typename T, bool BETA, int DC>
 static void launch_cascade(const Geo& g, const logkv_state_t& s, const Work& w, size_t smem, cudaStream_t st) {
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(cascade_kernel<T, BETA, DC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  launch_pdl(cascade_kernel<T, BETA, DC>, dim3(g.K, g.G, g.B), 512, smem, st, g, s, w);
+  launch_pdl(cascade_kernel<T, BETA, DC>, dim3(g.K, g.G, g.B), kCascadeThreads, smem, st, g, s, w);
 }
 
 // Span scores: the block's warps stride over the (candidate, group) pairs of batch row

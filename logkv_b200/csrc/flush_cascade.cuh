@@ -184,8 +184,10 @@ __device__ int beta_cut_warp(const T* tk, const T* tv, const Meta* tm, int start
   return best == 0 ? 2 : (best == 1 ? 1 : 3);
 }
 
+constexpr int kCascadeThreads = 256;  // two CTAs per SM (registers and shared memory)
+
 template <typename T, bool BETA, int DC>
-__global__ void __launch_bounds__(512) cascade_kernel(Geo g, logkv_state_t s, Work w) {
+__global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logkv_state_t s, Work w) {
   pdl_entry();
   LaneCtx<T> x = make_ctx<T>(g, s, w);
   const int type = w.plan_type[x.lane];
