@@ -1200,52 +1200,64 @@ __global__ void __launch_bounds__(kPfWarps * 32) chunk_attn_mma_kernel(AttnGeo a
 }
 
 // ---------------------------------------------------------------- K6: chunk attention on tcgen05 / TMEM
-// One CTA = 128 query rows of a lane (rf heads x 128/rf tokens), the M of
-// tcgen05.mma.cta_group::1.kind::f16 (bf16 in, f32 accumulate), with warp roles:
-//   warps 0-3  softmax: thread = query row = TMEM lane; read S(u), add the mass term, mask,
-//              online softmax (lazy rescaling: the running max moves only when a tile exceeds
-//              it by more than 2^8), write P(u) as bf16 over S(u)'s first 32 columns;
-//   warp 4     one thread issues S(u+1) = Q K^T while the softmax of tile u runs, then
-//              O += P(u) V (P from tensor memory, V an MN-major shared-memory operand);
-//   warps 5-7  cp.async loaders of the 64-slot K/V tiles (two stages, 128-byte swizzled
-//              canonical layouts, chunk ^ (row & 7)).
-// S is double-buffered in tensor memory (columns [0, 64) and [64, 128)), O sits at [128, 128+D).
-// Stages and buffers are handed over with mbarriers; every wait is bounded, and on expiry a
-// role stops, the CTA records kStatusTimeout, frees its tensor memory and returns.
-constexpr int kTcWarps = 8;
+// One CTA = NQ tiles of 128 query rows of a lane (each rf heads x 128/rf tokens), the M of
+// tcgen05.mma.cta_group::1.kind::f16 (bf16 in, f32 accumulate); every K/V tile the loaders
+// bring in serves all NQ query tiles.  Warp roles:
+//   warps 0..4NQ-1  softmax, one warpgroup per query tile: thread = query row = TMEM lane; read
+//                   S(t,u), add the mass term, mask, online softmax (lazy rescaling: the running
+//                   max moves only when a tile exceeds it by more than 2^8), write P(t,u) as bf16
+//                   over S(t,u)'s first 32 columns;
+//   warp 4NQ        one thread issues S(t,u+1) = Q_t K^T for every tile t while the softmax of
+//                   tile u runs, then O_t += P(t,u) V (P from tensor memory, V an MN-major
+//                   shared-memory operand); with NQ = 2 the tensor core alternates between the
+//                   two query tiles, so one warpgroup's softmax hides behind the other's products;
+//   next 3 warps    cp.async loaders of the 64-slot K/V tiles (two stages, 128-byte swizzled
+//                   canonical layouts, chunk ^ (row & 7)).
+// Tensor memory: tile t's S is double-buffered in columns [128t, 128t+64) and [128t+64, 128t+128),
+// its O sits at [128NQ + tD, 128NQ + (t+1)D).  Stages and buffers are handed over with
+// mbarriers; every wait is bounded, and on expiry a role stops, the CTA records kStatusTimeout,
+// frees its tensor memory and returns.
 constexpr int kTcRows = 128;
 constexpr int kTcTS = 64;
-constexpr int kTcLoaders = 96;             // warps 5-7
-constexpr uint32_t kTcCols = 256;
+constexpr int kTcLoaders = 96;             // three loader warps
 constexpr int32_t kStatusTimeout = 1 << 17;
 constexpr long long kTcWaitBudget = 4000000000LL;   // clock cycles (about 2 s)
 
-template <int D>
-struct TcShape {
-  static constexpr int Q_BYTES = (D / 64) * kTcRows * 128;
-  static constexpr int KV_BYTES = (D / 64) * kTcTS * 128;      // one K or V tile
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + Q_BYTES;                 // 2 stages
-  static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;            // 2 stages
-  static constexpr int OFF_M = OFF_V + 2 * KV_BYTES;            // 2 x 64 raw masses
-  static constexpr int BYTES = OFF_M + 2 * kTcTS * 4;
-  static constexpr size_t smem = (size_t)BYTES + 1024;          // + alignment slack
-  static_assert(D == 64 || D == 128, "tcgen05 chunk attention handles head dims 64 and 128");
-  static_assert(128 + D <= (int)kTcCols, "tensor-memory columns");
+template <int NQ>
+struct TcRoles {
+  static constexpr int STAGES = NQ == 1 ? 2 : 4;   // K/V stages in shared memory
+  static constexpr int SOFTMAX_WARPS = 4 * NQ;
+  static constexpr int MMA_WARP = 4 * NQ;
+  static constexpr int LOADER_WARP0 = 4 * NQ + 1;
+  static constexpr int WARPS = 4 * NQ + 4;
+  static constexpr uint32_t COLS = NQ == 1 ? 256u : 512u;
 };
 
-template <int D>
-__global__ void __launch_bounds__(kTcWarps * 32) chunk_attn_tc_kernel(AttnGeo a, logkv_prefix_t pre,
-                                                                     const __nv_bfloat16* rk,
-                                                                     const __nv_bfloat16* rv,
-                                                                     const __nv_bfloat16* kn,
-                                                                     const __nv_bfloat16* vn,
-                                                                     const __nv_bfloat16* q, __nv_bfloat16* out,
-                                                                     int32_t* status) {
-  using S = TcShape<D>;
-  constexpr int CPR = D / 8, TS = kTcTS;
+template <int D, int NQ>
+struct TcShape {
+  static constexpr int Q1_BYTES = (D / 64) * kTcRows * 128;     // one query tile
+  static constexpr int KV_BYTES = (D / 64) * kTcTS * 128;      // one K or V tile
+  static constexpr int OFF_Q = 0;
+  static constexpr int ST = TcRoles<NQ>::STAGES;
+  static constexpr int OFF_K = OFF_Q + NQ * Q1_BYTES;           // ST stages
+  static constexpr int OFF_V = OFF_K + ST * KV_BYTES;           // ST stages
+  static constexpr int OFF_M = OFF_V + ST * KV_BYTES;           // ST x 64 raw masses
+  static constexpr int BYTES = OFF_M + ST * kTcTS * 4;
+  static constexpr size_t smem = (size_t)BYTES + 1024;          // + alignment slack
+  static_assert(D == 64 || D == 128, "tcgen05 chunk attention handles head dims 64 and 128");
+  static_assert(128 * NQ + NQ * D <= (int)TcRoles<NQ>::COLS, "tensor-memory columns");
+};
+
+template <int D, int NQ>
+__global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
+    chunk_attn_tc_kernel(AttnGeo a, logkv_prefix_t pre, const __nv_bfloat16* rk, const __nv_bfloat16* rv,
+                         const __nv_bfloat16* kn, const __nv_bfloat16* vn, const __nv_bfloat16* q,
+                         __nv_bfloat16* out, int32_t* status) {
+  using S = TcShape<D, NQ>;
+  using RL = TcRoles<NQ>;
+  constexpr int CPR = D / 8, TS = kTcTS, ST = RL::STAGES;
   extern __shared__ uint4 smem4[];
-  __shared__ uint64_t q_full, kv_full[2], kv_empty[2], s_full[2], p_full[2], pv_done[2];
+  __shared__ uint64_t q_full, kv_full[ST], kv_empty[ST], s_full[NQ][2], p_full[NQ][2], pv_done[NQ][2];
   __shared__ uint32_t sh_tmem;
   __shared__ int sh_abort;
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -1254,8 +1266,9 @@ __global__ void __launch_bounds__(kTcWarps * 32) chunk_attn_tc_kernel(AttnGeo a,
   const uint32_t base_s = tc::smem_u32(base);
   const int g = blockIdx.y, b = blockIdx.z, ln = b * a.G + g;
   const int QT = kTcRows / a.rf;
-  const int tq0 = a.qoff + blockIdx.x * QT;
-  const int tlast = min(a.qoff + a.TQ, tq0 + QT) - 1;
+  const int tile0 = blockIdx.x * NQ;                        // first query tile of this CTA
+  const int tq0 = a.qoff + tile0 * QT;
+  const int tlast = min(a.qoff + a.TQ, tq0 + NQ * QT) - 1;   // last query token of the CTA
   const __nv_bfloat16* PK = static_cast<const __nv_bfloat16*>(pre.k);
   const __nv_bfloat16* PV = static_cast<const __nv_bfloat16*>(pre.v);
   const int Lp = pre.length[ln], R = a.rcount;
@@ -1265,26 +1278,30 @@ __global__ void __launch_bounds__(kTcWarps * 32) chunk_attn_tc_kernel(AttnGeo a,
 
   if (tid == 0) {
     tc::mbar_init(&q_full, 2 * kTcLoaders);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < ST; ++i) {
       tc::mbar_init(&kv_full[i], 2 * kTcLoaders);
       tc::mbar_init(&kv_empty[i], 1);
-      tc::mbar_init(&s_full[i], 1);
-      tc::mbar_init(&p_full[i], kTcRows);
-      tc::mbar_init(&pv_done[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      for (int t = 0; t < NQ; ++t) {
+        tc::mbar_init(&s_full[t][i], 1);
+        tc::mbar_init(&p_full[t][i], kTcRows);
+        tc::mbar_init(&pv_done[t][i], 1);
+      }
     }
     tc::mbar_fence_init();
     sh_abort = 0;
   }
   if (warp == 0) {
-    tc::tmem_alloc(&sh_tmem, kTcCols);
+    tc::tmem_alloc(&sh_tmem, RL::COLS);
     tc::tmem_relinquish();
   }
   tc::fence_before();
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = sh_tmem;
-  const uint32_t t_o = tmem + 128;
-  auto t_s = [&](int buf) { return tmem + 64u * buf; };
+  auto t_s = [&](int t, int buf) { return tmem + 128u * t + 64u * buf; };
+  auto t_o = [&](int t) { return tmem + 128u * NQ + (uint32_t)(t * D); };
   auto unit_info = [&](int u, const __nv_bfloat16*& kb, const __nv_bfloat16*& vb, const float*& mb, int& rows,
                        int& cls, int& first) {
     if (u < up) {
@@ -1318,21 +1335,23 @@ __global__ void __launch_bounds__(kTcWarps * 32) chunk_attn_tc_kernel(AttnGeo a,
     if (status) atomicOr(status, kStatusTimeout);
   };
 
-  if (warp >= 5) {
+  if (warp >= RL::LOADER_WARP0) {
     // ------------------------------------------------ loaders
-    const int lt = tid - 160;
-    for (int flat = lt; flat < kTcRows * CPR; flat += kTcLoaders) {
-      const int m = flat / CPR, c = flat % CPR;
-      const int t = tq0 + m % QT, h = g * a.rf + m / QT;
-      unsigned char* dst = base + S::OFF_Q + (c >> 3) * (kTcRows * 128) + m * 128 + (((c & 7) ^ (m & 7)) << 4);
-      if (t < a.qoff + a.TQ) cp_async16(dst, q + (((size_t)b * a.H + h) * a.T + t) * D + c * 8);
+    const int lt = tid - RL::LOADER_WARP0 * 32;
+    for (int flat = lt; flat < NQ * kTcRows * CPR; flat += kTcLoaders) {
+      const int mq = flat / CPR, c = flat % CPR;
+      const int t = mq / kTcRows, m = mq % kTcRows;
+      const int tok = tq0 + t * QT + m % QT, h = g * a.rf + m / QT;
+      unsigned char* dst = base + S::OFF_Q + t * S::Q1_BYTES + (c >> 3) * (kTcRows * 128) + m * 128 +
+                           (((c & 7) ^ (m & 7)) << 4);
+      if (tok < a.qoff + a.TQ) cp_async16(dst, q + (((size_t)b * a.H + h) * a.T + tok) * D + c * 8);
       else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
     }
     tc::mbar_arrive_cp_async(&q_full);
     tc::mbar_arrive(&q_full);
     for (int u = 0; u < U; ++u) {
-      const int st = u & 1;
-      if (u >= 2 && !tc::mbar_wait(&kv_empty[st], ((u - 2) >> 1) & 1, kTcWaitBudget)) {
+      const int st = u % ST;
+      if (u >= ST && !tc::mbar_wait(&kv_empty[st], ((u - ST) / ST) & 1, kTcWaitBudget)) {
         fail();
         break;
       }
@@ -1361,83 +1380,92 @@ __global__ void __launch_bounds__(kTcWarps * 32) chunk_attn_tc_kernel(AttnGeo a,
       tc::mbar_arrive_cp_async(&kv_full[st]);   // when this thread's copies land
       tc::mbar_arrive(&kv_full[st]);            // releases its plain zero stores
     }
-  } else if (warp == 4) {
+  } else if (warp == RL::MMA_WARP) {
     // ------------------------------------------------ MMA issuer
     if ((tid & 31) == 0) {
       constexpr uint32_t idesc_s = tc::f16_idesc(kTcRows, TS, 0, 0);
       constexpr uint32_t idesc_o = tc::f16_idesc(kTcRows, D, 0, 1);
-      const uint32_t qa = base_s + S::OFF_Q;
-      auto pv = [&](int v) {
-        const int bp = v & 1;
-        const uint32_t vbs = base_s + S::OFF_V + bp * S::KV_BYTES;
-#pragma unroll
-        for (int ks = 0; ks < TS / 16; ++ks) {
-          const uint64_t db = tc::sw128_desc(vbs + ks * 16 * 128, TS * 128, 1024);
-          tc::umma_f16_ts(t_o, t_s(bp) + ks * 8, db, idesc_o, (v > 0 || ks > 0) ? 1u : 0u);
-        }
-        tc::umma_commit(&pv_done[bp]);
-        tc::umma_commit(&kv_empty[bp]);
-      };
       bool ok = tc::mbar_wait(&q_full, 0, kTcWaitBudget);
       for (int u = 0; ok && u <= U; ++u) {
         if (u < U) {
-          const int st = u & 1;
-          ok = tc::mbar_wait(&kv_full[st], (u >> 1) & 1, kTcWaitBudget) &&
-               (u < 2 || tc::mbar_wait(&pv_done[st], ((u - 2) >> 1) & 1, kTcWaitBudget));
+          const int st = u % ST, sb = u & 1;
+          ok = tc::mbar_wait(&kv_full[st], (u / ST) & 1, kTcWaitBudget);
+          for (int t = 0; ok && t < NQ && u >= 2; ++t)
+            ok = tc::mbar_wait(&pv_done[t][sb], ((u - 2) >> 1) & 1, kTcWaitBudget);
           if (!ok) break;
           tc::fence_proxy_async();
           tc::fence_after();
           const uint32_t kbs = base_s + S::OFF_K + st * S::KV_BYTES;
 #pragma unroll
-          for (int ks = 0; ks < D / 16; ++ks) {
-            const uint64_t da = tc::sw128_desc(qa + (ks >> 2) * (kTcRows * 128) + (ks & 3) * 32, 16, 1024);
-            const uint64_t db = tc::sw128_desc(kbs + (ks >> 2) * (TS * 128) + (ks & 3) * 32, 16, 1024);
-            tc::umma_f16(t_s(st), da, db, idesc_s, ks > 0 ? 1u : 0u);
+          for (int t = 0; t < NQ; ++t) {
+            const uint32_t qa = base_s + S::OFF_Q + t * S::Q1_BYTES;
+#pragma unroll
+            for (int ks = 0; ks < D / 16; ++ks) {
+              const uint64_t da = tc::sw128_desc(qa + (ks >> 2) * (kTcRows * 128) + (ks & 3) * 32, 16, 1024);
+              const uint64_t db = tc::sw128_desc(kbs + (ks >> 2) * (TS * 128) + (ks & 3) * 32, 16, 1024);
+              tc::umma_f16(t_s(t, sb), da, db, idesc_s, ks > 0 ? 1u : 0u);
+            }
+            tc::umma_commit(&s_full[t][sb]);
           }
-          tc::umma_commit(&s_full[st]);
         }
         if (u >= 1) {
-          ok = tc::mbar_wait(&p_full[(u - 1) & 1], ((u - 1) >> 1) & 1, kTcWaitBudget);
+          const int v = u - 1, bp = v & 1, vs = v % ST;
+          const uint32_t vbs = base_s + S::OFF_V + vs * S::KV_BYTES;
+          for (int t = 0; t < NQ; ++t) {
+            ok = tc::mbar_wait(&p_full[t][bp], (v >> 1) & 1, kTcWaitBudget);
+            if (!ok) break;
+            tc::fence_after();
+#pragma unroll
+            for (int ks = 0; ks < TS / 16; ++ks) {
+              const uint64_t db = tc::sw128_desc(vbs + ks * 16 * 128, TS * 128, 1024);
+              tc::umma_f16_ts(t_o(t), t_s(t, bp) + ks * 8, db, idesc_o, (v > 0 || ks > 0) ? 1u : 0u);
+            }
+            tc::umma_commit(&pv_done[t][bp]);
+          }
           if (!ok) break;
-          tc::fence_after();
-          pv(u - 1);
+          tc::umma_commit(&kv_empty[vs]);
         }
       }
       if (!ok) fail();
     }
   } else {
-    // ------------------------------------------------ softmax (row tid)
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    const int row_t = tq0 + (tid % QT);
+    // ------------------------------------------------ softmax (query tile qt, row tid % 128)
+    const int qt = warp >> 2;
+    const int row = tid - qt * kTcRows;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const int row_t = tq0 + qt * QT + (row % QT);
     const float mscale = a.qx * a.scale_log2;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int u = 0; u < U; ++u) {
-      const int st = u & 1;
-      ok = __all_sync(0xffffffffu, tc::mbar_wait(&kv_full[st], (u >> 1) & 1, kTcWaitBudget) &&
-                                       tc::mbar_wait(&s_full[st], (u >> 1) & 1, kTcWaitBudget));
+      const int st = u & 1, ks_ = u % ST;
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&kv_full[ks_], (u / ST) & 1, kTcWaitBudget) &&
+                                       tc::mbar_wait(&s_full[qt][st], (u >> 1) & 1, kTcWaitBudget));
       if (!ok) break;
       tc::fence_after();
       const __nv_bfloat16 *kb_, *vb_;
       const float* mb_;
       int rows, cls, first;
       unit_info(u, kb_, vb_, mb_, rows, cls, first);
-      const float* sm = reinterpret_cast<const float*>(base + S::OFF_M) + st * TS;
+      const float* sm = reinterpret_cast<const float*>(base + S::OFF_M) + ks_ * TS;
       float sv[TS];
+      {
+        uint32_t r64[64];
+        tc::tmem_ld64(t_s(qt, st) + lane_off, r64);
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t r32[32];
-        tc::tmem_ld32(t_s(st) + lane_off + half * 32, r32);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) sv[half * 32 + j] = __uint_as_float(r32[j]);
+        for (int j = 0; j < TS; ++j) sv[j] = __uint_as_float(r64[j]);
       }
       float mt = -INFINITY;
       const bool full = rows == TS && (cls != 2 || !a.causal || first + TS - 1 <= row_t);
       if (full) {
 #pragma unroll
-        for (int j = 0; j < TS; ++j) {
-          sv[j] = fmaf(sv[j], a.scale_log2, mscale * sm[j]);
-          mt = fmaxf(mt, sv[j]);
+        for (int j = 0; j < TS; j += 4) {
+          const float4 m4 = *reinterpret_cast<const float4*>(sm + j);
+          sv[j] = fmaf(sv[j], a.scale_log2, mscale * m4.x);
+          sv[j + 1] = fmaf(sv[j + 1], a.scale_log2, mscale * m4.y);
+          sv[j + 2] = fmaf(sv[j + 2], a.scale_log2, mscale * m4.z);
+          sv[j + 3] = fmaf(sv[j + 3], a.scale_log2, mscale * m4.w);
+          mt = fmaxf(mt, fmaxf(fmaxf(sv[j], sv[j + 1]), fmaxf(sv[j + 2], sv[j + 3])));
         }
       } else {
 #pragma unroll
@@ -1464,36 +1492,38 @@ __global__ void __launch_bounds__(kTcWarps * 32) chunk_attn_tc_kernel(AttnGeo a,
       l = l * alpha + ps;
       if (u > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
         // O must hold PV(u-1) before it is rescaled.
-        ok = __all_sync(0xffffffffu, tc::mbar_wait(&pv_done[(u - 1) & 1], ((u - 1) >> 1) & 1, kTcWaitBudget));
+        ok = __all_sync(0xffffffffu,
+                        tc::mbar_wait(&pv_done[qt][(u - 1) & 1], ((u - 1) >> 1) & 1, kTcWaitBudget));
         if (!ok) break;
         tc::fence_after();
 #pragma unroll 1
         for (int c0 = 0; c0 < D; c0 += 32) {
           uint32_t r32[32];
-          tc::tmem_ld32(t_o + lane_off + c0, r32);
+          tc::tmem_ld32(t_o(qt) + lane_off + c0, r32);
 #pragma unroll
           for (int j = 0; j < 32; ++j) r32[j] = __float_as_uint(__uint_as_float(r32[j]) * alpha);
-          tc::tmem_st32(t_o + lane_off + c0, r32);
+          tc::tmem_st32(t_o(qt) + lane_off + c0, r32);
         }
       }
-      tc::tmem_st32(t_s(st) + lane_off, pk);
+      tc::tmem_st32(t_s(qt, st) + lane_off, pk);
       tc::fence_before();
-      tc::mbar_arrive(&p_full[st]);
+      tc::mbar_arrive(&p_full[qt][st]);
     }
     if (ok && U > 0)
-      ok = __all_sync(0xffffffffu, tc::mbar_wait(&pv_done[(U - 1) & 1], ((U - 1) >> 1) & 1, kTcWaitBudget));
+      ok = __all_sync(0xffffffffu,
+                      tc::mbar_wait(&pv_done[qt][(U - 1) & 1], ((U - 1) >> 1) & 1, kTcWaitBudget));
     if (!ok) {
       if ((tid & 31) == 0) fail();
     } else if (U > 0) {
       tc::fence_after();
-      const int hh = tid / QT;
+      const int hh = row / QT;
       const bool in = row_t < a.qoff + a.TQ;
       const float inv = l > 0.f ? 1.f / l : 0.f;
       __nv_bfloat16* orow = out + (((size_t)b * a.H + g * a.rf + hh) * a.T + row_t) * D;
 #pragma unroll 1
       for (int c0 = 0; c0 < D; c0 += 32) {
         uint32_t r32[32];
-        tc::tmem_ld32(t_o + lane_off + c0, r32);
+        tc::tmem_ld32(t_o(qt) + lane_off + c0, r32);
         if (in) {
 #pragma unroll
           for (int j = 0; j < 32; j += 8) {
@@ -1513,7 +1543,7 @@ __global__ void __launch_bounds__(kTcWarps * 32) chunk_attn_tc_kernel(AttnGeo a,
   __syncthreads();
   if (warp == 0) {
     tc::fence_after();
-    tc::tmem_dealloc(tmem, kTcCols);
+    tc::tmem_dealloc(tmem, RL::COLS);
   }
 }
 
@@ -1665,18 +1695,30 @@ static int launch_chunk_d(const AttnGeo& ag, const logkv_prefix_t& pre, const lo
   return launch_status();
 }
 
-template <int D>
+template <int D, int NQ>
 static int launch_chunk_tc(const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
                            const logkv_attention_args_t& x, int32_t* status, cudaStream_t st) {
-  using S = TcShape<D>;
-  auto kern = chunk_attn_tc_kernel<D>;
+  using S = TcShape<D, NQ>;
+  auto kern = chunk_attn_tc_kernel<D, NQ>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::smem);
   using B16 = __nv_bfloat16;
-  kern<<<dim3((ag.TQ + kTcRows / ag.rf - 1) / (kTcRows / ag.rf), ag.G, ag.B), kTcWarps * 32, S::smem, st>>>(
+  const int QT = kTcRows / ag.rf;
+  const int tiles = (ag.TQ + QT - 1) / QT;
+  kern<<<dim3((tiles + NQ - 1) / NQ, ag.G, ag.B), TcRoles<NQ>::WARPS * 32, S::smem, st>>>(
       ag, pre, static_cast<const B16*>(s.recent_k), static_cast<const B16*>(s.recent_v),
       static_cast<const B16*>(x.k_new), static_cast<const B16*>(x.v_new), static_cast<const B16*>(x.q),
       static_cast<B16*>(x.out), status);
   return launch_status();
+}
+
+// Two query tiles per CTA once there are enough tiles to give every SM a pair.
+template <int D>
+static int launch_chunk_tc_auto(const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
+                                const logkv_attention_args_t& x, int32_t* status, cudaStream_t st) {
+  const int QT = kTcRows / ag.rf;
+  const int tiles = (ag.TQ + QT - 1) / QT;
+  if ((size_t)tiles * ag.G * ag.B >= 148) return launch_chunk_tc<D, 2>(ag, pre, s, x, status, st);
+  return launch_chunk_tc<D, 1>(ag, pre, s, x, status, st);
 }
 
 // Head dims 64 and 128 run on tcgen05 (tensor memory accumulators); 16 and 32 on mma.sync.
@@ -1685,8 +1727,8 @@ static int launch_chunk(int D, const AttnGeo& ag, const logkv_prefix_t& pre, con
   switch (D) {
     case 16: return launch_chunk_d<16>(ag, pre, s, x, st);
     case 32: return launch_chunk_d<32>(ag, pre, s, x, st);
-    case 64: return launch_chunk_tc<64>(ag, pre, s, x, status, st);
-    case 128: return launch_chunk_tc<128>(ag, pre, s, x, status, st);
+    case 64: return launch_chunk_tc_auto<64>(ag, pre, s, x, status, st);
+    case 128: return launch_chunk_tc_auto<128>(ag, pre, s, x, status, st);
     default: return LOGKV_E_SHAPE;
   }
 }
