@@ -14,6 +14,10 @@
 //                            softmax in the log2 domain, CTA and cross-CTA combines
 //                            in a fixed order (the last CTA of a lane combines).
 #include <algorithm>
+#include <cstring>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include "common.cuh"
 #include "tcgen05.cuh"
@@ -1213,8 +1217,10 @@ __global__ void __launch_bounds__(kPfWarps * 32) chunk_attn_mma_kernel(AttnGeo a
 //                   two query tiles, so one warpgroup's softmax hides behind the other's products;
 //   next 3 warps    cp.async loaders of the 64-slot K/V tiles (two stages, 128-byte swizzled
 //                   canonical layouts, chunk ^ (row & 7)).
-// Tensor memory: tile t's S is double-buffered in columns [128t, 128t+64) and [128t+64, 128t+128),
-// its O sits at [128NQ + tD, 128NQ + (t+1)D).  Stages and buffers are handed over with
+// Tensor memory: tile t's S in columns [64t, 64t+64), released as soon as the softmax has loaded it
+// (so S(t,u+1) is computed while the softmax of tile u runs); its P double-buffered as bf16 in
+// [64NQ + 64t + 32b, +32) (b = u & 1); its O at [128NQ + tD, 128NQ + (t+1)D).  Stages and buffers
+// are handed over with
 // mbarriers; every wait is bounded, and on expiry a role stops, the CTA records kStatusTimeout,
 // frees its tensor memory and returns.
 constexpr int kTcRows = 128;
@@ -1248,16 +1254,25 @@ struct TcShape {
   static_assert(128 * NQ + NQ * D <= (int)TcRoles<NQ>::COLS, "tensor-memory columns");
 };
 
+// K/V tile sources as 2-D tensor maps ([rows of every lane, D] bf16, 64 x 64 boxes, 128-byte
+// swizzle): prefix, window and new chunk, K then V.  tma_mask bit c set = full tiles of source
+// class c come in by TMA; partial tiles (and classes whose map could not be encoded) by cp.async.
+struct TcMaps {
+  CUtensorMap k[3];
+  CUtensorMap v[3];
+};
+
 template <int D, int NQ>
 __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
     chunk_attn_tc_kernel(AttnGeo a, logkv_prefix_t pre, const __nv_bfloat16* rk, const __nv_bfloat16* rv,
                          const __nv_bfloat16* kn, const __nv_bfloat16* vn, const __nv_bfloat16* q,
-                         __nv_bfloat16* out, int32_t* status) {
+                         __nv_bfloat16* out, int32_t* status, const __grid_constant__ TcMaps maps,
+                         int tma_mask) {
   using S = TcShape<D, NQ>;
   using RL = TcRoles<NQ>;
   constexpr int CPR = D / 8, TS = kTcTS, ST = RL::STAGES;
   extern __shared__ uint4 smem4[];
-  __shared__ uint64_t q_full, kv_full[ST], kv_empty[ST], s_full[NQ][2], p_full[NQ][2], pv_done[NQ][2];
+  __shared__ uint64_t q_full, kv_full[ST], kv_empty[ST], s_full[NQ], s_free[NQ], p_full[NQ][2], pv_done[NQ][2];
   __shared__ uint32_t sh_tmem;
   __shared__ int sh_abort;
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -1279,12 +1294,13 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
   if (tid == 0) {
     tc::mbar_init(&q_full, 2 * kTcLoaders);
     for (int i = 0; i < ST; ++i) {
-      tc::mbar_init(&kv_full[i], 2 * kTcLoaders);
+      tc::mbar_init(&kv_full[i], 2 * kTcLoaders + 1);   // + the TMA issuer's (expect-tx) arrival
       tc::mbar_init(&kv_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      for (int t = 0; t < NQ; ++t) {
-        tc::mbar_init(&s_full[t][i], 1);
+    for (int t = 0; t < NQ; ++t) {
+      tc::mbar_init(&s_full[t], 1);
+      tc::mbar_init(&s_free[t], kTcRows);
+      for (int i = 0; i < 2; ++i) {
         tc::mbar_init(&p_full[t][i], kTcRows);
         tc::mbar_init(&pv_done[t][i], 1);
       }
@@ -1300,7 +1316,8 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = sh_tmem;
-  auto t_s = [&](int t, int buf) { return tmem + 128u * t + 64u * buf; };
+  auto t_s = [&](int t) { return tmem + 64u * t; };
+  auto t_p = [&](int t, int buf) { return tmem + 64u * NQ + 64u * t + 32u * buf; };
   auto t_o = [&](int t) { return tmem + 128u * NQ + (uint32_t)(t * D); };
   auto unit_info = [&](int u, const __nv_bfloat16*& kb, const __nv_bfloat16*& vb, const float*& mb, int& rows,
                        int& cls, int& first) {
@@ -1362,16 +1379,32 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
       unsigned char* sk = base + S::OFF_K + st * S::KV_BYTES;
       unsigned char* sv = base + S::OFF_V + st * S::KV_BYTES;
       float* sm = reinterpret_cast<float*>(base + S::OFF_M) + st * TS;
-      for (int flat = lt; flat < TS * CPR; flat += kTcLoaders) {
-        const int r = flat / CPR, c = flat % CPR;
-        const int off = (c >> 3) * (TS * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4);
-        if (r < rows) {
-          cp_async16(sk + off, kb + (size_t)flat * 8);
-          cp_async16(sv + off, vb + (size_t)flat * 8);
-        } else {
-          *reinterpret_cast<uint4*>(sk + off) = make_uint4(0, 0, 0, 0);
-          *reinterpret_cast<uint4*>(sv + off) = make_uint4(0, 0, 0, 0);
+      const bool by_tma = rows == TS && ((tma_mask >> cls) & 1);
+      if (by_tma) {
+        // One thread: 2 x (D/64) boxes of 64 rows x 128 bytes, already in the swizzled layout.
+        if (lt == 0) {
+          const int row0 = cls == 0 ? ln * pre.capacity + first : (cls == 1 ? ln * a.rcap + first : ln * a.T + first);
+          tc::fence_proxy_async();   // earlier plain zero stores to this stage before the async writes
+          tc::mbar_arrive_expect_tx(&kv_full[st], 2 * S::KV_BYTES);
+#pragma unroll
+          for (int c64 = 0; c64 < D / 64; ++c64) {
+            tc::tma_load_2d(tc::smem_u32(sk) + c64 * (TS * 128), &maps.k[cls], c64 * 64, row0, &kv_full[st]);
+            tc::tma_load_2d(tc::smem_u32(sv) + c64 * (TS * 128), &maps.v[cls], c64 * 64, row0, &kv_full[st]);
+          }
         }
+      } else {
+        for (int flat = lt; flat < TS * CPR; flat += kTcLoaders) {
+          const int r = flat / CPR, c = flat % CPR;
+          const int off = (c >> 3) * (TS * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+          if (r < rows) {
+            cp_async16(sk + off, kb + (size_t)flat * 8);
+            cp_async16(sv + off, vb + (size_t)flat * 8);
+          } else {
+            *reinterpret_cast<uint4*>(sk + off) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(sv + off) = make_uint4(0, 0, 0, 0);
+          }
+        }
+        if (lt == 0) tc::mbar_arrive(&kv_full[st]);   // the issuer's arrival without a TMA
       }
       if (lt < TS) {
         if (cls == 0 && lt < rows) cp_async4(sm + lt, mb + lt);
@@ -1388,25 +1421,30 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
       bool ok = tc::mbar_wait(&q_full, 0, kTcWaitBudget);
       for (int u = 0; ok && u <= U; ++u) {
         if (u < U) {
-          const int st = u % ST, sb = u & 1;
+          const int st = u % ST;
           ok = tc::mbar_wait(&kv_full[st], (u / ST) & 1, kTcWaitBudget);
-          for (int t = 0; ok && t < NQ && u >= 2; ++t)
-            ok = tc::mbar_wait(&pv_done[t][sb], ((u - 2) >> 1) & 1, kTcWaitBudget);
           if (!ok) break;
           tc::fence_proxy_async();
           tc::fence_after();
           const uint32_t kbs = base_s + S::OFF_K + st * S::KV_BYTES;
 #pragma unroll
           for (int t = 0; t < NQ; ++t) {
+            // S(t) is free once the softmax has loaded S(t, u-1) into registers.
+            if (u >= 1 && !tc::mbar_wait(&s_free[t], (u - 1) & 1, kTcWaitBudget)) {
+              ok = false;
+              break;
+            }
+            tc::fence_after();
             const uint32_t qa = base_s + S::OFF_Q + t * S::Q1_BYTES;
 #pragma unroll
             for (int ks = 0; ks < D / 16; ++ks) {
               const uint64_t da = tc::sw128_desc(qa + (ks >> 2) * (kTcRows * 128) + (ks & 3) * 32, 16, 1024);
               const uint64_t db = tc::sw128_desc(kbs + (ks >> 2) * (TS * 128) + (ks & 3) * 32, 16, 1024);
-              tc::umma_f16(t_s(t, sb), da, db, idesc_s, ks > 0 ? 1u : 0u);
+              tc::umma_f16(t_s(t), da, db, idesc_s, ks > 0 ? 1u : 0u);
             }
-            tc::umma_commit(&s_full[t][sb]);
+            tc::umma_commit(&s_full[t]);
           }
+          if (!ok) break;
         }
         if (u >= 1) {
           const int v = u - 1, bp = v & 1, vs = v % ST;
@@ -1418,7 +1456,7 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
 #pragma unroll
             for (int ks = 0; ks < TS / 16; ++ks) {
               const uint64_t db = tc::sw128_desc(vbs + ks * 16 * 128, TS * 128, 1024);
-              tc::umma_f16_ts(t_o(t), t_s(t, bp) + ks * 8, db, idesc_o, (v > 0 || ks > 0) ? 1u : 0u);
+              tc::umma_f16_ts(t_o(t), t_p(t, bp) + ks * 8, db, idesc_o, (v > 0 || ks > 0) ? 1u : 0u);
             }
             tc::umma_commit(&pv_done[t][bp]);
           }
@@ -1440,7 +1478,7 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
     for (int u = 0; u < U; ++u) {
       const int st = u & 1, ks_ = u % ST;
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&kv_full[ks_], (u / ST) & 1, kTcWaitBudget) &&
-                                       tc::mbar_wait(&s_full[qt][st], (u >> 1) & 1, kTcWaitBudget));
+                                       tc::mbar_wait(&s_full[qt], u & 1, kTcWaitBudget));
       if (!ok) break;
       tc::fence_after();
       const __nv_bfloat16 *kb_, *vb_;
@@ -1451,10 +1489,12 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
       float sv[TS];
       {
         uint32_t r64[64];
-        tc::tmem_ld64(t_s(qt, st) + lane_off, r64);
+        tc::tmem_ld64(t_s(qt) + lane_off, r64);
 #pragma unroll
         for (int j = 0; j < TS; ++j) sv[j] = __uint_as_float(r64[j]);
       }
+      tc::fence_before();
+      tc::mbar_arrive(&s_free[qt]);   // S(qt) may now take the next tile's scores
       float mt = -INFINITY;
       const bool full = rows == TS && (cls != 2 || !a.causal || first + TS - 1 <= row_t);
       if (full) {
@@ -1490,6 +1530,11 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
         pk[j] = pack_bf16x2(p0, p1);
       }
       l = l * alpha + ps;
+      if (u >= 2) {
+        // P buffer st still feeds PV(u-2) until that product completes.
+        ok = __all_sync(0xffffffffu, tc::mbar_wait(&pv_done[qt][st], ((u - 2) >> 1) & 1, kTcWaitBudget));
+        if (!ok) break;
+      }
       if (u > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
         // O must hold PV(u-1) before it is rescaled.
         ok = __all_sync(0xffffffffu,
@@ -1505,7 +1550,7 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
           tc::tmem_st32(t_o(qt) + lane_off + c0, r32);
         }
       }
-      tc::tmem_st32(t_s(qt, st) + lane_off, pk);
+      tc::tmem_st32(t_p(qt, st) + lane_off, pk);
       tc::fence_before();
       tc::mbar_arrive(&p_full[qt][st]);
     }
@@ -1695,6 +1740,35 @@ static int launch_chunk_d(const AttnGeo& ag, const logkv_prefix_t& pre, const lo
   return launch_status();
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// [rows, D] bf16 rows of D * 2 bytes; 64 x 64-element boxes in the 128-byte swizzle; rows past
+// the end read as zeros.  False if the encoder is missing or refuses (e.g. a misaligned base).
+static bool encode_rows_map(CUtensorMap* m, const void* base, size_t rows, int D) {
+  auto enc = tensor_map_encoder();
+  if (!enc || !base || rows == 0 || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)D * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)kTcTS};
+  const cuuint32_t estr[2] = {1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int D, int NQ>
 static int launch_chunk_tc(const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
                            const logkv_attention_args_t& x, int32_t* status, cudaStream_t st) {
@@ -1704,10 +1778,22 @@ static int launch_chunk_tc(const AttnGeo& ag, const logkv_prefix_t& pre, const l
   using B16 = __nv_bfloat16;
   const int QT = kTcRows / ag.rf;
   const int tiles = (ag.TQ + QT - 1) / QT;
+  const size_t lanes = (size_t)ag.B * ag.G;
+  TcMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  int mask = 0;
+  if (encode_rows_map(&maps.k[0], pre.k, lanes * pre.capacity, D) &&
+      encode_rows_map(&maps.v[0], pre.v, lanes * pre.capacity, D))
+    mask |= 1;
+  if (encode_rows_map(&maps.k[1], s.recent_k, lanes * ag.rcap, D) &&
+      encode_rows_map(&maps.v[1], s.recent_v, lanes * ag.rcap, D))
+    mask |= 2;
+  if (encode_rows_map(&maps.k[2], x.k_new, lanes * ag.T, D) && encode_rows_map(&maps.v[2], x.v_new, lanes * ag.T, D))
+    mask |= 4;
   kern<<<dim3((tiles + NQ - 1) / NQ, ag.G, ag.B), TcRoles<NQ>::WARPS * 32, S::smem, st>>>(
       ag, pre, static_cast<const B16*>(s.recent_k), static_cast<const B16*>(s.recent_v),
       static_cast<const B16*>(x.k_new), static_cast<const B16*>(x.v_new), static_cast<const B16*>(x.q),
-      static_cast<B16*>(x.out), status);
+      static_cast<B16*>(x.out), status, maps, mask);
   return launch_status();
 }
 
