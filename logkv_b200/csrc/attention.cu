@@ -1355,6 +1355,7 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
   if (warp >= RL::LOADER_WARP0) {
     // ------------------------------------------------ loaders
     const int lt = tid - RL::LOADER_WARP0 * 32;
+    const float mscale_l = a.qx * a.scale_log2;
     for (int flat = lt; flat < NQ * kTcRows * CPR; flat += kTcLoaders) {
       const int mq = flat / CPR, c = flat % CPR;
       const int t = mq / kTcRows, m = mq % kTcRows;
@@ -1406,10 +1407,7 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
         }
         if (lt == 0) tc::mbar_arrive(&kv_full[st]);   // the issuer's arrival without a TMA
       }
-      if (lt < TS) {
-        if (cls == 0 && lt < rows) cp_async4(sm + lt, mb + lt);
-        else sm[lt] = 0.f;
-      }
+      if (lt < TS) sm[lt] = cls == 0 && lt < rows ? mscale_l * mb[lt] : 0.f;   // log2-scaled mass term
       tc::mbar_arrive_cp_async(&kv_full[st]);   // when this thread's copies land
       tc::mbar_arrive(&kv_full[st]);            // releases its plain zero stores
     }
@@ -1472,7 +1470,6 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
     const int row = tid - qt * kTcRows;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const int row_t = tq0 + qt * QT + (row % QT);
-    const float mscale = a.qx * a.scale_log2;
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int u = 0; u < U; ++u) {
@@ -1498,20 +1495,19 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
       float mt = -INFINITY;
       const bool full = rows == TS && (cls != 2 || !a.causal || first + TS - 1 <= row_t);
       if (full) {
+        const uint64_t c2 = tc::f2pack(a.scale_log2, a.scale_log2);
 #pragma unroll
         for (int j = 0; j < TS; j += 4) {
-          const float4 m4 = *reinterpret_cast<const float4*>(sm + j);
-          sv[j] = fmaf(sv[j], a.scale_log2, mscale * m4.x);
-          sv[j + 1] = fmaf(sv[j + 1], a.scale_log2, mscale * m4.y);
-          sv[j + 2] = fmaf(sv[j + 2], a.scale_log2, mscale * m4.z);
-          sv[j + 3] = fmaf(sv[j + 3], a.scale_log2, mscale * m4.w);
+          const float4 m4 = *reinterpret_cast<const float4*>(sm + j);   // masses arrive log2-scaled
+          tc::f2unpack(tc::ffma2(tc::f2pack(sv[j], sv[j + 1]), c2, tc::f2pack(m4.x, m4.y)), sv[j], sv[j + 1]);
+          tc::f2unpack(tc::ffma2(tc::f2pack(sv[j + 2], sv[j + 3]), c2, tc::f2pack(m4.z, m4.w)), sv[j + 2], sv[j + 3]);
           mt = fmaxf(mt, fmaxf(fmaxf(sv[j], sv[j + 1]), fmaxf(sv[j + 2], sv[j + 3])));
         }
       } else {
 #pragma unroll
         for (int j = 0; j < TS; ++j) {
           const bool vis = j < rows && (cls != 2 || !a.causal || first + j <= row_t);
-          sv[j] = vis ? fmaf(sv[j], a.scale_log2, mscale * sm[j]) : -INFINITY;
+          sv[j] = vis ? fmaf(sv[j], a.scale_log2, sm[j]) : -INFINITY;
           mt = fmaxf(mt, sv[j]);
         }
       }
@@ -1521,14 +1517,20 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
         m_used = mt;
       }
       const float msub = m_used == -INFINITY ? 0.f : m_used;
-      float ps = 0.f;
+      const uint64_t nm2 = tc::f2pack(-msub, -msub);
+      uint64_t ps2 = tc::f2pack(0.f, 0.f);
       uint32_t pk[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
-        const float p0 = tc::ex2(sv[2 * j] - msub), p1 = tc::ex2(sv[2 * j + 1] - msub);
-        ps += p0 + p1;
+        float x0, x1;
+        tc::f2unpack(tc::fadd2(tc::f2pack(sv[2 * j], sv[2 * j + 1]), nm2), x0, x1);
+        const float p0 = tc::ex2(x0), p1 = tc::ex2(x1);
+        ps2 = tc::fadd2(ps2, tc::f2pack(p0, p1));
         pk[j] = pack_bf16x2(p0, p1);
       }
+      float ps0, ps1;
+      tc::f2unpack(ps2, ps0, ps1);
+      const float ps = ps0 + ps1;
       l = l * alpha + ps;
       if (u >= 2) {
         // P buffer st still feeds PV(u-2) until that product completes.
