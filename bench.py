@@ -355,6 +355,63 @@ def bench_ours(args, rank, world, local_rank):
                 clocks=clocks.summary(), launches=n_launch)
 
 
+# ---------------------------------------------------------------------------------------------- KV-head sharded
+KVSHARD = dict(workload="qwen3-1.7b-shaped streaming prefill flush, one sequence KV-head-sharded "
+                        "(BASELINE configs[2]: recent 4096, 2048-token flushes)",
+               layers=28, groups=8, head_dim=128, clusters=12, B=128, recent=4096, granularity=2048,
+               exact=256, span_cap=64, beta=True, tokens=32768, chunk=2048, batch_per_rank=1)
+
+
+def bench_kv_sharded(args, rank, world, local_rank):
+    """One long sequence, its 8 KV groups split over the ranks (G / world each): every flush
+    all-gathers the ranks' per-group span parts (NCCL) between its score and commit phases.
+    Eager add_recent calls on one stream, device time of whole steps, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from logkv_b200.cache import LogStructuredKVCache
+    from logkv_b200.sharding import group_block
+    device = torch.device("cuda", local_rank)
+    cfg = dict(KVSHARD)
+    cfg["layers"] = args.kv_layers
+    lo, hi = group_block(cfg["groups"], rank, world)
+    layers, cos, sin, ends_host, ends_dev = make_inputs(torch, cfg, device, seed=4321)   # same on every rank
+    layers = [[tuple(t[:, lo:hi].contiguous() for t in chunk) for chunk in chunks] for chunks in layers]
+    group = dist.group.WORLD if world > 1 else None
+    caches = [LogStructuredKVCache(
+        (1, hi - lo, cfg["tokens"], cfg["head_dim"]), (1, hi - lo, cfg["tokens"], cfg["head_dim"]),
+        B=cfg["B"], recent_size=cfg["recent"], device=device, dtype=torch.bfloat16, cluster_k_max=cfg["clusters"],
+        semantic_flush_granularity=cfg["granularity"], semantic_centroid_backend="parallel",
+        semantic_replay_updates=True, alpha_exact_tokens=cfg["exact"], alpha_span_max_tokens=cfg["span_cap"],
+        beta_novelty=cfg["beta"], beta_adaptive_merge=cfg["beta"], cos_cache=cos, sin_cache=sin,
+        rope_n_elem=cfg["head_dim"], kv_shard_group=group) for _ in range(cfg["layers"])]
+    n_chunks = cfg["tokens"] // cfg["chunk"]
+    flushes_per_step = cfg["layers"] * (n_chunks - cfg["recent"] // cfg["chunk"])
+    for _ in range(max(1, args.warmup)):
+        run_step(caches, layers, ends_host, ends_dev)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        run_step(caches, layers, ends_host, ends_dev)
+    stop.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(stop)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    assert all(c.read_status() == 0 for c in caches)
+    parts = caches[0]._span_gather.numel() * 4 if caches[0]._span_gather is not None else 0
+    return {"metric": "flush us per 2048-tok chunk/layer, one sequence KV-head-sharded", "unit": "us",
+            "value": round(ms * 1000.0 / (args.steps * flushes_per_step), 2), "higher_is_better": False,
+            "n_gpus": world, "scaling": "strong", "groups_per_rank": hi - lo, "flushes_per_step": flushes_per_step,
+            "exchange_bytes_per_flush": parts, "timing": "eager add_recent, one stream, max over ranks",
+            "config": {k: cfg[k] for k in ("workload", "layers", "groups", "head_dim", "clusters", "B", "recent",
+                                           "granularity", "exact", "span_cap", "tokens")}}
+
+
 # ---------------------------------------------------------------------------------------------- decode
 DECODE = dict(workload="decode attention over a 32K compressed cache (BASELINE configs[3])", batch=64,
               heads=16, groups=8, head_dim=128, clusters=12, B=128, filled_levels=4, recent=2048, exact=256,
@@ -613,6 +670,8 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=32, help="timed decode steps (0: skip the decode leg)")
     ap.add_argument("--decode-batch", type=int, default=DECODE["batch"], help="decode sequences (profiling runs only)")
     ap.add_argument("--streams", type=int, default=28, help="streams the layers' flushes are spread over")
+    ap.add_argument("--kv-layers", type=int, default=28,
+                    help="layers of the KV-head-sharded leg (BASELINE configs[2]; 0 skips it)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -645,6 +704,7 @@ def main():
     res = bench_ours(args, rank, world, local_rank)
     dec = bench_decode(args, rank, world, local_rank) if args.decode_steps > 0 else None
     pre = bench_prefill(args, rank, world, local_rank) if args.decode_steps > 0 else None
+    kvs = bench_kv_sharded(args, rank, world, local_rank) if args.kv_layers > 0 else None
     cpu = None
     if rank == 0 and world == 1 and args.cpu_flushes > 0:
         us, n = cpu_flush_sample(args.cpu_flushes)
@@ -662,7 +722,7 @@ def main():
                     flushes_per_step=res["flushes_per_step"],
                     rows_per_flush={k: round(v / res["flushes_per_step"], 1) for k, v in res["counters"].items()
                                     if k != "flushes"},
-                    decode=dec, prefill=pre)
+                    decode=dec, prefill=pre, kv_sharded=kvs)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -27,7 +27,7 @@ __device__ __forceinline__ void mbar_arrive_cp_async(uint64_t* bar) {
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
-// One box of a 2-D tensor map (no multicast) into this CTA's shared memory; the bytes count
+// One box of a 2-D tensor map into this CTA's own shared memory; the bytes count
 // toward `bar`'s transaction count.  x, the inner coordinate, is a multiple of 16 bytes.
 __device__ __forceinline__ void tma_load_2d(uint32_t smem_dst, const void* tmap, int x, int y, uint64_t* bar) {
   asm volatile(
