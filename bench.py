@@ -365,7 +365,7 @@ KVSHARD = dict(workload="qwen3-1.7b-shaped streaming prefill flush, one sequence
 def bench_kv_sharded(args, rank, world, local_rank):
     """One long sequence, its 8 KV groups split over the ranks (G / world each): every flush
     all-gathers the ranks' per-group span parts (NCCL) between its score and commit phases.
-    Eager add_recent calls on one stream, device time of whole steps, max over ranks."""
+    Whole steps captured in a CUDA graph on one stream, device time, max over ranks."""
     import torch
     import torch.distributed as dist
     from logkv_b200.cache import LogStructuredKVCache
@@ -386,17 +386,29 @@ def bench_kv_sharded(args, rank, world, local_rank):
         rope_n_elem=cfg["head_dim"], kv_shard_group=group) for _ in range(cfg["layers"])]
     n_chunks = cfg["tokens"] // cfg["chunk"]
     flushes_per_step = cfg["layers"] * (n_chunks - cfg["recent"] // cfg["chunk"])
-    for _ in range(max(1, args.warmup)):
+    stream = torch.cuda.Stream(device)
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup)):
+            run_step(caches, layers, ends_host, ends_dev)
+    torch.cuda.synchronize()
+    # One CUDA graph per step (the span-part all-gathers are captured with the flushes, in the
+    # same order on every rank); released before the process group goes away.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
         run_step(caches, layers, ends_host, ends_dev)
+    with torch.cuda.stream(stream):
+        graph.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(args.steps):
-        run_step(caches, layers, ends_host, ends_dev)
-    stop.record()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        stop.record(stream)
     torch.cuda.synchronize()
+    del graph
     ms = start.elapsed_time(stop)
     if world > 1:
         t = torch.tensor([ms], device=device)
@@ -407,7 +419,7 @@ def bench_kv_sharded(args, rank, world, local_rank):
     return {"metric": "flush us per 2048-tok chunk/layer, one sequence KV-head-sharded", "unit": "us",
             "value": round(ms * 1000.0 / (args.steps * flushes_per_step), 2), "higher_is_better": False,
             "n_gpus": world, "scaling": "strong", "groups_per_rank": hi - lo, "flushes_per_step": flushes_per_step,
-            "exchange_bytes_per_flush": parts, "timing": "eager add_recent, one stream, max over ranks",
+            "exchange_bytes_per_flush": parts, "timing": "CUDA-graph steps on one stream (NCCL inside), max over ranks",
             "config": {k: cfg[k] for k in ("workload", "layers", "groups", "head_dim", "clusters", "B", "recent",
                                            "granularity", "exact", "span_cap", "tokens")}}
 
