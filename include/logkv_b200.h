@@ -173,6 +173,20 @@ LOGKV_API int logkv_flush_partials(const logkv_layout_t* layout, int32_t flush_t
  * it (buffers bit for bit).  The order of replays is the caller's to keep (the Python cache
  * checks it).  Neither runs KV-head sharded.
  */
+/*
+ * Route op-log (replaces the op-log rows of _record_ops, litgpt/log_kv_cache.py:2043-2071,
+ * recorded by the attach route and the joins).  After a flush (any of the entry points above,
+ * same workspace, before the next flush), append that flush's rows to a caller-owned log
+ * op_log [batch, groups, capacity, 4] int32 (16-byte aligned) with lengths op_log_len
+ * [batch, groups] int32: per lane, NEW_CLUSTER (0, cluster, 0, position) for every cluster it
+ * opened, in cluster order; then JOIN (2, cluster, 0, position) for the joined tokens of every
+ * ordinary or new cluster, cluster by cluster, positions ascending; then JOIN rows for the new
+ * tokens of delayed clusters.  A lane whose rows do not fit gets no rows and its length becomes
+ * capacity + 1 (and stays there): the caller reports the overflow.
+ */
+LOGKV_API int logkv_flush_oplog_append(const logkv_layout_t* layout, int32_t flush_tokens, void* workspace,
+                                       int32_t* op_log, int32_t* op_log_len, int32_t capacity, void* stream);
+
 LOGKV_API size_t logkv_tape_bytes(const logkv_layout_t* layout, int32_t flush_tokens);
 LOGKV_API int logkv_flush_record(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
                                  int32_t recent_count, void* workspace, size_t workspace_bytes, void* tape,

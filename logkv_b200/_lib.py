@@ -101,6 +101,9 @@ def lib() -> ctypes.CDLL:
         handle.logkv_flush_partials.restype = ctypes.c_int
         handle.logkv_flush_partials.argtypes = [P(Layout), ctypes.c_int32, ctypes.c_void_p,
                                                 P(P(ctypes.c_float)), P(ctypes.c_size_t)]
+        handle.logkv_flush_oplog_append.restype = ctypes.c_int
+        handle.logkv_flush_oplog_append.argtypes = [P(Layout), ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p,
+                                                    ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p]
         handle.logkv_tape_bytes.restype = ctypes.c_size_t
         handle.logkv_tape_bytes.argtypes = [P(Layout), ctypes.c_int32]
         handle.logkv_flush_record.restype = ctypes.c_int

@@ -315,6 +315,33 @@ class LogStructuredKVCache(nn.Module):
         index = updates.save(tape, owned=True)
         updates.flushes[key] = (self._update_signature(take), index, ready)
 
+    # ------------------------------------------------------------------ op-log
+    def begin_op_log(self) -> None:
+        """Bind a fresh per-(batch, group) route log (the reference's begin_op_log, :2006-2028)."""
+        cap = max(1, self.max_seq_length * 3)
+        dev = self.level_count.device
+        self.op_log = torch.zeros(self.batch_size, self.n_groups, cap, 4, device=dev, dtype=torch.int32)
+        self.op_log_len = torch.zeros(self.batch_size, self.n_groups, device=dev, dtype=torch.int32)
+
+    def take_op_log(self):
+        """(log [B, G, max_len, 4], lengths [B, G]) as the reference's take_op_log (:2030-2038); synchronizes."""
+        if getattr(self, "op_log", None) is None or getattr(self, "op_log_len", None) is None:
+            return None, None
+        lengths = self.op_log_len.clone()
+        max_len = int(lengths.max().item()) if lengths.numel() else 0
+        if max_len > self.op_log.size(2):
+            raise RuntimeError("semantic LogKV op_log overflow")
+        return self.op_log[:, :, :max_len].clone(), lengths
+
+    def _append_op_log(self, take: int) -> None:
+        """Append the rows of the flush just enqueued (same workspace) to the bound op-log."""
+        if getattr(self, "op_log", None) is None:
+            self.begin_op_log()
+        _lib.check(_lib.lib().logkv_flush_oplog_append(
+            ctypes.byref(self._layout), int(take), ctypes.c_void_p(self._workspace.data_ptr()),
+            ctypes.c_void_p(self.op_log.data_ptr()), ctypes.c_void_p(self.op_log_len.data_ptr()),
+            self.op_log.size(2), ctypes.c_void_p(_lib.stream_ptr(self.level_k.device))), "logkv_flush_oplog_append")
+
     def flush_device(self, take: int) -> None:
         """One device flush of the ``take`` oldest window tokens plus the window shift."""
         self._ladder_epoch += 1
@@ -394,9 +421,9 @@ class LogStructuredKVCache(nn.Module):
         if k_raw is None:
             raise ValueError("semantic LogKV add_recent requires pre-RoPE k_raw")
         replaying = any(v_ is not None for v_ in replay.values())
-        if self._active_updates is None and (record_op_log or replaying):
-            raise NotImplementedError("op-log recording and replay outside an update tape context are not "
-                                      "implemented by logkv_b200")
+        if self._active_updates is None and replaying:
+            raise NotImplementedError("op-log replay outside an update tape context is not implemented by "
+                                      "logkv_b200 (replay a recorded update tape instead)")
         n = k.size(2)
         if n > self.recent_size:
             raise ValueError(f"chunk size {n} exceeds recent_size {self.recent_size}")
@@ -435,6 +462,8 @@ class LogStructuredKVCache(nn.Module):
                     self._flush_with_updates(take, record_op_log, replaying or self._replaying_updates)
                 else:
                     self.flush_device(take)
+                if record_op_log:
+                    self._append_op_log(take)
                 self._flush_cursor += 1
                 self.recent_count -= take
                 pending -= take

@@ -269,6 +269,7 @@ static size_t carve(const Geo& g, size_t esize, char* base, Work* w) {
   w->orphan = c.take<uint8_t>(B * G * NW, 1);
   w->s_winner = c.take<float>(B * G * NW, 4);
   w->cnorm = c.take<float>(B * G * K, 4);
+  w->tok_pos = c.take<int64_t>(B * NW, 8);
   w->tok_list = c.take<int32_t>(B * G * NW, 4);
   w->plan_off = c.take<int32_t>(B * G * K, 4);
   w->plan_n = c.take<int32_t>(B * G * K, 4);
@@ -543,6 +544,20 @@ extern "C" int logkv_flush_replay(const logkv_layout_t* layout, const logkv_stat
                                   size_t tape_bytes, void* stream) {
   return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream, nullptr,
                    kPhaseAll, nullptr, 1, kTapeReplay, const_cast<void*>(tape), tape_bytes);
+}
+
+extern "C" int logkv_flush_oplog_append(const logkv_layout_t* layout, int32_t flush_tokens, void* workspace,
+                                        int32_t* op_log, int32_t* op_log_len, int32_t capacity, void* stream) {
+  const int v = validate(layout, flush_tokens);
+  if (v != LOGKV_OK) return v;
+  if (!workspace || !op_log || !op_log_len || capacity < 1) return LOGKV_E_POINTER;
+  if ((reinterpret_cast<uintptr_t>(op_log) & 15) || (reinterpret_cast<uintptr_t>(op_log_len) & 3)) return LOGKV_E_POINTER;
+  const Geo g = make_geo(*layout, flush_tokens, layout->recent_capacity);
+  Work w{};
+  carve(g, layout->dtype == LOGKV_DTYPE_BF16 ? 2 : 4, static_cast<char*>(workspace), &w);
+  oplog_append_kernel<<<dim3(g.G, g.B), 256, 0, static_cast<cudaStream_t>(stream)>>>(g, w, op_log, op_log_len,
+                                                                                   capacity);
+  return (int)cudaGetLastError();
 }
 
 extern "C" int logkv_flush_scores(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,

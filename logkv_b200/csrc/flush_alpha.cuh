@@ -46,6 +46,10 @@ __global__ void snapshot_kernel(Geo g, logkv_state_t s, Work w) {
   }
   if (grp == 0 && blockIdx.x == 0) {
     for (int i = threadIdx.x; i < g.P; i += blockDim.x) w.snap_pos[(size_t)b * g.P + i] = s.alpha_pos[(size_t)b * g.P + i];
+    // Positions of the whole [old pool | flushed window] index space, as the flush starts.
+    for (int i = threadIdx.x; i < g.NW; i += blockDim.x)
+      w.tok_pos[(size_t)b * g.NW + i] =
+          i < g.P ? s.alpha_pos[(size_t)b * g.P + i] : s.recent_pos[(size_t)b * g.cap2R + (i - g.P)];
     if (threadIdx.x == 0) {
       w.snap_rowcount[b] = s.alpha_rowcount[b];
       if (b == 0) {

@@ -453,4 +453,80 @@ __global__ void __launch_bounds__(1024) plan_kernel(Geo g, logkv_state_t s, Work
   }
 }
 
+// ---------------------------------------------------------------- op-log append
+// The route log rows of the last flush (_record_ops, litgpt/log_kv_cache.py:2043-2071), per
+// (batch, group) lane in the reference's order: a NEW_CLUSTER row (op 0, cluster, 0, position of
+// the opening token) for every cluster the flush opened, in cluster order (_semantic_new_clusters
+// :2276-2298); then JOIN rows (op 2, cluster, 0, position) for the joined tokens of every
+// ordinary or newly opened cluster, cluster by cluster, positions ascending
+// (_semantic_commit_joins_unsegmented :4158-4170); then JOIN rows for the new tokens of every
+// delayed cluster (_alpha_commit_joins :3781-3788).  Reads the plan the flush left in its
+// workspace; appends at op_len[lane] unless the log's capacity would be exceeded, in which case
+// no row is written and op_len[lane] becomes capacity + 1 (sticky: later appends refuse too).
+
+__global__ void __launch_bounds__(256) oplog_append_kernel(Geo g, Work w, int32_t* op_log, int32_t* op_len,
+                                                           int cap) {
+  const int b = blockIdx.y, grp = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+  const int K = g.K;
+  const size_t bg = (size_t)b * g.G + grp, row0 = bg * K;
+  __shared__ int off_new[kMaxClusters], off_join[kMaxClusters], off_late[kMaxClusters];
+  __shared__ int sh_total, sh_new, sh_join, sh_len;
+  if (tid == 0) {
+    int nn = 0, nj = 0, nl = 0;
+    for (int c = 0; c < K; ++c) {
+      const int type = w.plan_type[row0 + c], n = w.plan_n[row0 + c];
+      off_new[c] = nn;
+      off_join[c] = nj;
+      off_late[c] = nl;
+      if (type == kJobNew && n > 0) {
+        nn += 1;
+        nj += n - 1;
+      } else if (type == kJobOrdinary) {
+        nj += n;
+      } else if (type == kJobLate) {
+        nl += n;
+      }
+    }
+    sh_new = nn;
+    sh_join = nj;
+    sh_total = nn + nj + nl;
+    sh_len = op_len[bg];
+    if (sh_len > cap || sh_len + sh_total > cap) {
+      op_len[bg] = cap + 1;
+      sh_total = -1;
+    }
+  }
+  __syncthreads();
+  if (sh_total < 0) return;
+  const int len0 = sh_len;
+  const int* arch = w.arch_idx + (size_t)b * g.NW;
+  const int* toks = w.tok_list + bg * g.NW;
+  const int64_t* pos = w.tok_pos + (size_t)b * g.NW;
+  int4* log = reinterpret_cast<int4*>(op_log) + bg * (size_t)cap;
+  for (int c = 0; c < K; ++c) {
+    const int type = w.plan_type[row0 + c], n = w.plan_n[row0 + c], toff = w.plan_off[row0 + c];
+    if (type == kJobNone || n == 0) continue;
+    for (int i = tid; i < n; i += nt) {
+      const int p = (int)pos[arch[toks[toff + i]]];
+      int at;
+      int op = 2;
+      if (type == kJobNew) {
+        if (i == 0) {
+          op = 0;
+          at = len0 + off_new[c];
+        } else {
+          at = len0 + sh_new + off_join[c] + i - 1;
+        }
+      } else if (type == kJobOrdinary) {
+        at = len0 + sh_new + off_join[c] + i;
+      } else {
+        at = len0 + sh_new + sh_join + off_late[c] + i;
+      }
+      log[at] = make_int4(op, c, 0, p);
+    }
+  }
+  __syncthreads();
+  if (tid == 0) op_len[bg] = len0 + sh_total;
+}
+
 }  // namespace logkv

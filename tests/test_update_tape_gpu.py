@@ -124,11 +124,11 @@ def test_replay_errors_and_prefilled_cache():
             pytest.raises(RuntimeError, match="missing"):
         for chunk in chunks:
             push(fresh, cfg, chunk)
-    # Recording needs record_op_log=True; outside a context, op-log arguments are refused.
+    # Recording needs record_op_log=True; outside a context, replay arguments are refused.
     fresh.reset_parameters()
     with fresh._semantic_update_context(_SemanticReplayUpdates()), pytest.raises(RuntimeError, match="record_op_log"):
         for chunk in chunks:
             push(fresh, cfg, chunk)
     fresh.reset_parameters()
     with pytest.raises(NotImplementedError):
-        push(fresh, cfg, chunks[0], record_op_log=True)
+        push(fresh, cfg, chunks[0], replay_op_log=torch.zeros(1))
