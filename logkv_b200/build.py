@@ -26,6 +26,7 @@ UNITS = [
     ("flush.cu", ["-fmad=false"]),
     ("attention.cu", []),
     ("plugin.cu", ["-fmad=false"]),
+    ("unified.cu", ["-fmad=false"]),
 ]
 
 

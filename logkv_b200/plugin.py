@@ -14,7 +14,11 @@ include/logkv_plugin.h (and include/logkv_attention.h for ``pack``):
 Results follow the reference's CPU order (feature sums left to right, no fused
 multiply-adds), so they equal its CPU path; ``centroid_parallel`` is the same
 ordered reduction.  The unified-route functions of log_kv_route_triton.py
-(pair_distances, mirror, UnifiedReduce, ...) are not provided.
+(:546-838) are provided too, by include/logkv_unified.h:
+
+  pair_distances, mirror, UnifiedReduce (single-pass rounds)
+
+with the results of the reference's Torch reducer (_UnifiedReduceTorch).
 """
 from __future__ import annotations
 
@@ -52,6 +56,12 @@ class Attach(ctypes.Structure):
 _bound = False
 
 
+class Unified(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ("dist", "mu", "mass", "limits", "status", "alive", "radius",
+                                                "packed", "merges", "stuck", "trace")] + \
+               [(n, ctypes.c_int32) for n in ("lanes", "size", "dim", "target")]
+
+
 def _lib_plugin():
     global _bound
     lib = _lib.lib()
@@ -68,6 +78,14 @@ def _lib_plugin():
         lib.logkv_alpha_partition.argtypes = [P(Partition), v]
         lib.logkv_attach_assign.restype = ctypes.c_int
         lib.logkv_attach_assign.argtypes = [P(Attach), v]
+        lib.logkv_pair_distances.restype = ctypes.c_int
+        lib.logkv_pair_distances.argtypes = [v, v, i32, i32, v]
+        lib.logkv_mirror.restype = ctypes.c_int
+        lib.logkv_mirror.argtypes = [v, i32, i32, v]
+        lib.logkv_unified_init.restype = ctypes.c_int
+        lib.logkv_unified_init.argtypes = [P(Unified), v]
+        lib.logkv_unified_step.restype = ctypes.c_int
+        lib.logkv_unified_step.argtypes = [P(Unified), v]
         _bound = True
     return lib
 
@@ -219,3 +237,82 @@ def pack(cache, plan, k, v, dim, buffers=None, skip_pooled=False, recent_start=0
     """Packed K/V with the mass coordinate (log_kv_pack_triton.py:95), bit for bit with the torch packer."""
     from .attention import pack_mid_kv
     return pack_mid_kv(cache, plan, k, v, dim, buffers=buffers, skip_pooled=skip_pooled, recent_start=recent_start)
+
+
+# ------------------------------------------------------------------------------------------ unified route
+def _f32(t: torch.Tensor, what: str) -> torch.Tensor:
+    if t.dtype != torch.float32 or not t.is_cuda or not t.is_contiguous():
+        raise ValueError(f"{what} must be a contiguous float32 CUDA tensor")
+    return t
+
+
+def pair_distances(gram, norm):
+    """Contiguous FP32 Gram products [L, M, M] -> symmetric squared distances, in place
+    (log_kv_route_triton.py:585-607): max((n_i + n_j) - 2 G_ij, 0) from the upper triangle."""
+    _f32(gram, "gram")
+    norm = norm.contiguous()
+    _f32(norm, "norm")
+    lanes, size = gram.shape[:2]
+    _lib.check(_lib_plugin().logkv_pair_distances(ctypes.c_void_p(gram.data_ptr()), ctypes.c_void_p(norm.data_ptr()),
+                                                  lanes, size, _stream(gram)), "logkv_pair_distances")
+    return gram
+
+
+def mirror(dist):
+    """Make [L, M, M] exactly symmetric (log_kv_route_triton.py:546-553), in place."""
+    _f32(dist, "dist")
+    lanes, size = dist.shape[:2]
+    _lib.check(_lib_plugin().logkv_mirror(ctypes.c_void_p(dist.data_ptr()), lanes, size, _stream(dist)),
+               "logkv_mirror")
+    return dist
+
+
+class UnifiedReduce:
+    """Device state of the incremental Ward rounds (log_kv_route_triton.py:610-838).
+
+    Same constructor and methods as the reference's ``UnifiedReduce``: ``step(round_)`` queues
+    one round and returns the per-lane active flags (int32, on the device), ``status`` holds
+    (active, live count) per lane for the host to poll, ``limit_live`` is accepted (it only
+    narrows launch grids in the reference; results do not depend on it), and ``finish()`` reads
+    back (traces per lane [n, 2] int64, alive [L, M] bool, stuck [L] bool).  ``dist``, ``mu`` and
+    ``mass`` are updated in place.  Only single-pass rounds: ``passes > 1`` (frozen-centre
+    sweeps) raises NotImplementedError.
+    """
+
+    def __init__(self, dist, mu, mass, count, limits, target, passes=1):
+        if int(passes) != 1:
+            raise NotImplementedError("frozen-centre sweeps (passes > 1) are not implemented by logkv_b200")
+        self.dist, self.mu, self.mass = _f32(dist, "dist"), _f32(mu, "mu"), _f32(mass, "mass")
+        self.limits = None if limits is None else _f32(limits.contiguous(), "limits")
+        lanes, size = mass.shape
+        dev = mass.device
+        self.target = int(target)
+        self.status = torch.stack((torch.zeros(lanes, dtype=torch.int32, device=dev),
+                                   count.to(device=dev, dtype=torch.int32)))
+        self.active, self.count = self.status.unbind(0)
+        self.alive = torch.zeros((lanes, size), dtype=torch.uint8, device=dev)
+        self.radius = torch.zeros((lanes, size), dtype=torch.float32, device=dev)
+        self.packed = torch.zeros((lanes, size), dtype=torch.int64, device=dev)
+        self.merges = torch.zeros(lanes, dtype=torch.int32, device=dev)
+        self.stuck = torch.zeros(lanes, dtype=torch.uint8, device=dev)
+        self.trace = torch.zeros((lanes, size, 2), dtype=torch.int32, device=dev)
+        self._u = Unified(*[ctypes.c_void_p(t.data_ptr()) if t is not None else None
+                            for t in (self.dist, self.mu, self.mass, self.limits, self.status, self.alive,
+                                      self.radius, self.packed, self.merges, self.stuck, self.trace)],
+                          lanes, size, mu.size(-1), self.target)
+        _lib.check(_lib_plugin().logkv_unified_init(ctypes.byref(self._u), _stream(mass)), "logkv_unified_init")
+
+    def limit_live(self, count):
+        """Accepted for interface parity; launch sizes here do not depend on a live bound."""
+        return None
+
+    def step(self, round_=None):
+        _lib.check(_lib_plugin().logkv_unified_step(ctypes.byref(self._u), _stream(self.mass)), "logkv_unified_step")
+        return self.active
+
+    def finish(self):
+        merges = self.merges.cpu().numpy()
+        trace = self.trace.cpu().numpy().astype("int64")
+        alive = self.alive.cpu().numpy().astype(bool)
+        stuck = self.stuck.cpu().numpy().astype(bool)
+        return [trace[lane, :n] for lane, n in enumerate(merges)], alive, stuck

@@ -1,0 +1,208 @@
+"""Unified (Ward / radius) route operators, restated in numpy (test infrastructure only).
+
+Follows the reference's Torch reducer ``_UnifiedReduceTorch`` (litgpt/log_kv_cache.py:448-638)
+with its helpers ``_unified_pack`` / ``_unified_pair_cost`` (:428-446), and the fused pair
+distances / mirror of ``log_kv_route_triton.py:546-607``.  Every operation is float32 and
+rounded as the reference writes it (one rounding per product, quotient, sum); the one sum over
+features (the exact squared distance of a candidate pair, ``(diff * diff).sum(-1)`` in the
+reference, whose order torch leaves to its vectorised CPU kernel) runs left to right here, and
+the CUDA operators use the same order.  Frozen-centre sweeps (``passes > 1``) are not restated.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+F32 = np.float32
+INF_KEY = np.int64(0x7F800000) << np.int64(32)
+
+
+def pair_distances(gram: np.ndarray, norm: np.ndarray) -> np.ndarray:
+    """max((n_i + n_j) - 2 G_ij, 0) from the upper triangle of G, mirrored (route:556-607)."""
+    gram = np.asarray(gram, F32)
+    norm = np.asarray(norm, F32)
+    L, M, _ = gram.shape
+    d = np.maximum((norm[:, :, None] + norm[:, None, :]).astype(F32) - (F32(2) * gram).astype(F32), F32(0))
+    upper = np.triu(np.ones((M, M), bool))
+    return np.where(upper[None], d, np.transpose(d, (0, 2, 1))).astype(F32)
+
+
+def mirror(dist: np.ndarray) -> np.ndarray:
+    """Copy the upper triangle onto the lower one (route:546-553)."""
+    M = dist.shape[1]
+    upper = np.triu(np.ones((M, M), bool))
+    return np.where(upper[None], dist, np.transpose(dist, (0, 2, 1))).astype(F32)
+
+
+def pack(cost: np.ndarray, key: np.ndarray) -> np.ndarray:
+    """(cost bits << 32) | key with -0.0 written as +0.0 (log_kv_cache.py:431-434)."""
+    cost = np.where(cost == 0, F32(0), np.asarray(cost, F32)).astype(F32)
+    return (cost.view(np.int32).astype(np.int64) << np.int64(32)) | np.asarray(key, np.int64)
+
+
+def pair_cost(d2, mi, mj, ri, rj, limit, valid):
+    """Ward cost and validity (log_kv_cache.py:437-445), float32 in the reference's order."""
+    d2, mi, mj = np.asarray(d2, F32), np.asarray(mi, F32), np.asarray(mj, F32)
+    denom = np.maximum((mi + mj).astype(F32), F32(1))
+    valid = valid & (mi > 0) & (mj > 0)
+    if limit is not None:
+        distance = np.sqrt(d2).astype(F32)
+        b1 = (np.asarray(ri, F32) + ((mj / denom).astype(F32) * distance).astype(F32)).astype(F32)
+        b2 = (np.asarray(rj, F32) + ((mi / denom).astype(F32) * distance).astype(F32)).astype(F32)
+        valid = valid & (np.maximum(b1, b2) <= limit)
+    cost = (d2 * ((mi * mj).astype(F32) / denom).astype(F32)).astype(F32)
+    return np.where(valid, cost, F32(np.inf)).astype(F32), valid
+
+
+def sq_dist(x: np.ndarray, y: np.ndarray) -> F32:
+    """sum_d (x_d - y_d)^2, left to right in float32."""
+    acc = F32(0)
+    for a, b in zip(x.tolist(), y.tolist()):
+        d = F32(F32(a) - F32(b))
+        acc = F32(acc + F32(d * d))
+    return acc
+
+
+class UnifiedReduce:
+    """Mutual-nearest Ward rounds on [L, M] clusters (single-pass rounds).
+
+    dist [L, M, M] squared centre distances (symmetric), mu [L, M, D] centres, mass [L, M],
+    count [L] live clusters (rows < count), limits [L] radius limits or None, target clusters
+    per lane.  ``step()`` runs one round and returns the lanes still active; ``finish()`` returns
+    (per-lane merge traces [(left, right), ...] in round then (cost, left) order, alive [L, M],
+    stuck [L]).  Arrays are updated in place.
+    """
+
+    def __init__(self, dist, mu, mass, count, limits, target):
+        self.dist = np.array(dist, F32)
+        self.mu = np.array(mu, F32)
+        self.mass = np.array(mass, F32)
+        self.limits = None if limits is None else np.array(limits, F32)
+        self.target = int(target)
+        L, M = self.mass.shape
+        self.L, self.M = L, M
+        self.ids = np.arange(M, dtype=np.int64)
+        self.count = np.array(count, np.int64).copy()
+        self.alive = self.ids[None, :] < self.count[:, None]
+        self.radius = np.zeros((L, M), F32)
+        self.stuck = np.zeros(L, bool)
+        self.traces = [[] for _ in range(L)]
+        self.packed = np.full((L, M), INF_KEY, np.int64)
+        for lane in range(L):
+            for row in np.flatnonzero(self.alive[lane]):
+                self.packed[lane, row] = self._scan(lane, row)
+
+    def _scan(self, lane, row):
+        lim = None if self.limits is None else self.limits[lane]
+        cost, _ = pair_cost(self.dist[lane, row], self.mass[lane, row], self.mass[lane], self.radius[lane, row],
+                            self.radius[lane], lim, self.ids != row)
+        return pack(cost, np.int64(row) ^ self.ids).min()
+
+    def step(self):
+        M, ids = self.M, self.ids
+        active = np.zeros(self.L, bool)
+        for lane in range(self.L):
+            packed = self.packed[lane]
+            best = np.clip((packed & np.int64(0xFFFFFFFF)) ^ ids, 0, M - 1)
+            cost = (packed >> np.int64(32)).astype(np.int32).view(np.float32)
+            valid = self.alive[lane] & (ids < best) & (best[best] == ids) & (cost < np.inf)
+            nprop = int(valid.sum())
+            rejected = np.zeros(M, bool)
+            bound = None
+            if self.limits is not None:
+                bound = np.zeros(M, F32)
+                for row in np.flatnonzero(valid):
+                    other = best[row]
+                    exact2 = sq_dist(self.mu[lane, row], self.mu[lane, other])
+                    exact = F32(np.sqrt(exact2))
+                    ma, mb = self.mass[lane, row], self.mass[lane, other]
+                    denom = max(F32(ma + mb), F32(1))
+                    v1 = F32(self.radius[lane, row] + F32(F32(mb / denom) * exact))
+                    v2 = F32(self.radius[lane, other] + F32(F32(ma / denom) * exact))
+                    verified = max(v1, v2)
+                    if verified > self.limits[lane]:
+                        self.dist[lane, row, other] = exact2
+                        self.dist[lane, other, row] = exact2
+                        rejected[row] = rejected[other] = True
+                        valid[row] = False
+                    bound[row] = verified
+            pair_c = np.where(valid, cost, F32(np.inf)).astype(F32)
+            order = np.argsort(pair_c, kind="stable")[:M // 2]
+            ok = pair_c[order] < np.inf
+            ok &= np.cumsum(ok) <= (self.count[lane] - self.target)
+            a = order[ok]
+            b = best[a]
+            keep = np.zeros(M, bool)
+            merged = np.zeros(M, bool)
+            if len(a):
+                self._merge(lane, a, b, bound, keep, merged)
+            dirty = self.alive[lane] & ~keep & (merged[best] | rejected)
+            for row in np.flatnonzero(dirty):
+                self.packed[lane, row] = self._scan(lane, row)
+            self.count[lane] -= int(ok.sum())
+            remaining = self.count[lane] > self.target
+            self.stuck[lane] |= remaining and nprop == 0
+            active[lane] = remaining and nprop > 0
+        return active
+
+    def _merge(self, lane, a, b, bound, keep, merged):
+        M, ids = self.M, self.ids
+        dist, mass = self.dist[lane], self.mass[lane]
+        ma, mb = mass[a].copy(), mass[b].copy()
+        dab = dist[a, b].copy()
+        total = (ma + mb).astype(F32)
+        alpha = (ma / total).astype(F32)
+        beta = (mb / total).astype(F32)
+        shift = ((alpha * beta).astype(F32) * dab).astype(F32)
+        keep[a] = True
+        merged[a] = True
+        merged[b] = True
+        partner = np.zeros(M, np.int64)
+        partner[a] = b
+        pma, pmb, pdab = np.ones(M, F32), np.zeros(M, F32), np.zeros(M, F32)
+        pma[a], pmb[a], pdab[a] = ma, mb, dab
+        x_aa, x_ba = dist[a].copy(), dist[b].copy()                  # [n, M], read before any write
+        x_ab, x_bb = dist[a[:, None], partner[None, :]].copy(), dist[b[:, None], partner[None, :]].copy()
+        mass[a] = total
+        mass[b] = 0
+        self.alive[lane, b] = False
+        if bound is not None:
+            self.radius[lane, a] = bound[a]
+        mu = self.mu[lane]
+        mu[a] = (((ma[:, None] * mu[a]).astype(F32) + (mb[:, None] * mu[b]).astype(F32)).astype(F32)
+                 / np.maximum(total, F32(1))[:, None]).astype(F32)
+        al, be, sh = alpha[:, None], beta[:, None], shift[:, None]
+        new = ((((al * x_aa).astype(F32) + (be * x_ba).astype(F32)).astype(F32)) - sh).astype(F32)
+        is_keep = keep[None, :]
+        qa, qb, qd = pma[None, :], pmb[None, :], pdab[None, :]
+        qsum = (qa + qb).astype(F32)
+        qal, qbe = (qa / qsum).astype(F32), (qb / qsum).astype(F32)
+        qsh = ((qal * qbe).astype(F32) * qd).astype(F32)
+        inner = ((((al * x_ab).astype(F32) + (be * x_bb).astype(F32)).astype(F32)) - sh).astype(F32)
+        own_first = (((qal * new).astype(F32) + (qbe * inner).astype(F32)).astype(F32) - qsh).astype(F32)
+        t1 = ((((qal * x_aa).astype(F32) + (qbe * x_ab).astype(F32)).astype(F32)) - qsh).astype(F32)
+        t2 = ((((qal * x_ba).astype(F32) + (qbe * x_bb).astype(F32)).astype(F32)) - qsh).astype(F32)
+        other_first = ((((al * t1).astype(F32) + (be * t2).astype(F32)).astype(F32)) - sh).astype(F32)
+        both = np.where(a[:, None] < ids[None, :], own_first, other_first)
+        new = np.maximum(np.where(is_keep, both, new), F32(0)).astype(F32)
+        new[np.arange(len(a)), a] = 0
+        alive = self.alive[lane]
+        for m in range(len(a)):
+            cols = np.flatnonzero(alive & ~keep)
+            dist[cols, a[m]] = new[m, cols]
+        for m in range(len(a)):
+            cols = np.flatnonzero(alive)
+            dist[a[m], cols] = new[m, cols]
+        lim = None if self.limits is None else self.limits[lane]
+        cost, valid = pair_cost(new, total[:, None], mass[None, :], self.radius[lane, a][:, None],
+                                self.radius[lane][None, :], lim, alive[None, :] & (ids[None, :] != a[:, None]))
+        packed_new = pack(cost, ids[None, :] ^ a[:, None])
+        for m in range(len(a)):
+            cols = np.flatnonzero(valid[m] & ~keep)
+            self.packed[lane, cols] = np.minimum(self.packed[lane, cols], packed_new[m, cols])
+        for m in range(len(a)):
+            self.packed[lane, a[m]] = packed_new[m].min()
+            self.traces[lane].append((int(a[m]), int(b[m])))
+
+    def finish(self):
+        traces = [np.asarray(t, np.int64).reshape(-1, 2) for t in self.traces]
+        return traces, self.alive.copy(), self.stuck.copy()

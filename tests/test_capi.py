@@ -14,7 +14,7 @@ HEADERS = [os.path.join(ROOT, "include", n) for n in sorted(os.listdir(os.path.j
 
 def declared_symbols():
     text = "".join(open(h).read() for h in HEADERS)
-    return sorted(set(re.findall(r"LOGKV_API\s+[\w\s\*]+?\b(logkv_\w+)\s*\(", text)))
+    return sorted(set(re.findall(r"LOGKV_\w*API\s+[\w\s\*]+?\b(logkv_\w+)\s*\(", text)))
 
 
 @pytest.fixture(scope="module")
@@ -29,7 +29,8 @@ def test_header_declares_entry_points():
     names = declared_symbols()
     assert "logkv_flush" in names and "logkv_flush_workspace_bytes" in names
     for name in ("logkv_attention_plan", "logkv_pack_prefix", "logkv_pack_mid", "logkv_attention",
-                 "logkv_attention_workspace_bytes"):
+                 "logkv_attention_workspace_bytes", "logkv_pair_distances", "logkv_mirror", "logkv_unified_init",
+                 "logkv_unified_step"):
         assert name in names
 
 
@@ -64,3 +65,18 @@ def test_attention_argument_checks(lib):
                                None, 0, None) == -4
     plan = _lib.Plan()
     assert lib.logkv_attention_plan(ctypes.byref(layout), ctypes.byref(state), ctypes.byref(plan), None) == -4
+
+
+def test_unified_argument_checks(lib):
+    """Null pointers and out-of-range shapes are refused before anything is launched."""
+    from logkv_b200.plugin import Unified, _lib_plugin
+    plug = _lib_plugin()
+    assert plug.logkv_pair_distances(None, None, 1, 4, None) == -4
+    assert plug.logkv_mirror(None, 1, 4, None) == -4
+    assert plug.logkv_unified_init(None, None) == -4
+    assert plug.logkv_unified_step(ctypes.byref(Unified()), None) == -4
+    fake = ctypes.c_void_p(64)
+    u = Unified(*([fake] * 3 + [None] + [fake] * 7), 1, 4097, 8, 1)
+    assert plug.logkv_unified_init(ctypes.byref(u), None) == -1
+    u = Unified(*([fake] * 3 + [None] + [fake] * 7), 0, 16, 8, 1)
+    assert plug.logkv_unified_step(ctypes.byref(u), None) == -1
