@@ -352,7 +352,150 @@ def bench_ours(args, rank, world, local_rank):
                           "traffic": None, "bytes_per_launch": round(casc_bytes_per_launch)},
                 flush_roofline={"achieved": round(flush_achieved, 1), "unit": "GB/s",
                                 "frac": round(flush_achieved / peak, 4), "bytes_per_flush": round(flush_bytes)},
-                clocks=clocks.summary(), launches=n_launch)
+                clocks=clocks.summary(), launches=n_launch, inputs=(caches, layers, ends_host, ends_dev))
+
+
+def bench_flush_attend(args, rank, world, local_rank, inputs):
+    """Flush-and-attend prefill in model order: per layer-chunk the chunk attention of the layer's
+    16 query heads over its cache, then ``add_recent`` of the chunk (a 2048-token flush); chunks
+    in sequence, the 28 layers in sequence within a chunk, on one stream, one CUDA graph per step.
+    Timed twice: with the route decisions on the caller's stream, and with route overlap (the
+    decisions of each flush on a side stream, ordered only after the layer's previous flush).
+    """
+    import torch
+    import torch.distributed as dist
+    from logkv_b200.attention import log_kv_chunk_attention
+    caches, layers, ends_host, ends_dev = inputs
+    device = caches[0].level_k.device
+    H, D, T = 16, WORKLOAD["head_dim"], WORKLOAD["chunk"]
+    gen = torch.Generator(device=device).manual_seed(77 + rank)
+    q = torch.randn(1, H, T, D, generator=gen, device=device).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    scale = D ** -0.5
+    stream = torch.cuda.Stream(device)
+    n_chunks = len(layers[0])
+
+    def step():
+        for cache in caches:
+            cache.reset_parameters()
+        for c in range(n_chunks):
+            for cache, chunks in zip(caches, layers):
+                k, kr, v = chunks[c]
+                log_kv_chunk_attention(cache, q, k, v, scale, 0.0, out=out)
+                cache.add_recent(k, v, k_raw=kr, span_ends=ends_host, span_ends_device=ends_dev)
+
+    us = {}
+    for overlap in (False, True):
+        for cache in caches:
+            cache._route_overlap = overlap
+        with torch.no_grad(), torch.cuda.stream(stream):
+            for _ in range(max(1, args.warmup)):
+                step()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                step()
+            graph.replay()
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        del graph
+        t = torch.tensor([e0.elapsed_time(e1)], device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        us["overlap" if overlap else "plain"] = round(t.item() * 1000.0 / (args.steps * n_chunks * len(caches)), 2)
+    for cache in caches:
+        cache._route_overlap = False
+    return {"metric": "flush-and-attend prefill us per 2048-token chunk/layer (chunk attention + add_recent)",
+            "unit": "us", "value": us["overlap"], "value_without_route_overlap": us["plain"],
+            "config": {"layers": len(caches), "chunks": n_chunks, "heads": H, "groups": WORKLOAD["groups"],
+                       "head_dim": D, "chunk": T, "flushes_per_step": len(caches) * (n_chunks - 1)}}
+
+
+# ---------------------------------------------------------------------------------------------- unified route
+UNIFIED = dict(workload="unified (Ward) route passes, BASELINE configs[4] shapes: 16 lanes of one flush tile, "
+                        "2060 points each (2048 flushed + exact pool remainder + centres), 48-component mixture",
+               lanes=16, points=2060, head_dim=128, components=48, orphan_frac=0.10, target=12)
+
+
+def unified_points(torch, cfg, device, seed):
+    """[lanes, points, D] float32 keys: a 48-component mixture (sigma_j ~ U[0.1, 0.6]) with 10 % orphans."""
+    L, M, D, C = cfg["lanes"], cfg["points"], cfg["head_dim"], cfg["components"]
+    gen = torch.Generator(device=device).manual_seed(seed)
+    centres = torch.randn(L, C, D, generator=gen, device=device) * 2.0
+    sigma = torch.rand(L, C, generator=gen, device=device) * 0.5 + 0.1
+    z = torch.randint(0, C, (L, M), generator=gen, device=device)
+    lane = torch.arange(L, device=device)[:, None]
+    x = centres[lane, z] + sigma[lane, z][..., None] * torch.randn(L, M, D, generator=gen, device=device)
+    orphan = torch.rand(L, M, generator=gen, device=device) < cfg["orphan_frac"]
+    u = torch.randn(L, M, D, generator=gen, device=device)
+    u = u / u.norm(dim=-1, keepdim=True) * (4 * 0.35 * D ** 0.5)
+    return torch.where(orphan[..., None], centres[lane, z] + u, x).contiguous()
+
+
+def bench_unified(args, rank, world, local_rank):
+    """The unified route's two reductions per flush tile, as the reference runs them
+    (log_kv_cache.py:3185-3376): FP32 Gram (cuBLAS, highest precision) + fused pair distances,
+    then UnifiedReduce rounds with the host polling (active, live) every four rounds; first the
+    radius-limited candidate pass to one cluster per radius, then the global pass to K = 12."""
+    import torch
+    import torch.distributed as dist
+    from logkv_b200.plugin import UnifiedReduce, pair_distances
+    device = torch.device("cuda", local_rank)
+    cfg = UNIFIED
+    L, M, D = cfg["lanes"], cfg["points"], cfg["head_dim"]
+    mu0 = unified_points(torch, cfg, device, seed=900 + rank)
+    limits = torch.full((L,), 1.2 * 0.35 * D ** 0.5, device=device)
+    count = torch.full((L,), M, dtype=torch.int64, device=device)
+    stream = torch.cuda.Stream(device)
+    prec = torch.get_float32_matmul_precision()
+    torch.set_float32_matmul_precision("highest")
+
+    def one_pass(mu, mass, lim, target):
+        centred = mu - mu[:, :1]
+        norm = centred.square().sum(-1)
+        dist_ = pair_distances(torch.bmm(centred, centred.transpose(1, 2)), norm)
+        red = UnifiedReduce(dist_, mu, mass, count, lim, target)
+        rounds = 0
+        for r in range(1, 2 * M + 8):
+            red.step(r)
+            rounds = r
+            if r % 4 == 0 and not bool(red.status[0].any()):
+                break
+        traces, alive, stuck = red.finish()
+        return rounds, int(red.count.max().item())
+
+    out = {}
+    with torch.no_grad(), torch.cuda.stream(stream):
+        for name, lim, target in (("candidate_pass", limits, 1), ("global_pass", None, cfg["target"])):
+            times, rounds, live = [], 0, 0
+            for it in range(max(3, args.warmup) + max(3, args.steps)):
+                mu = mu0.clone()
+                mass = torch.ones(L, M, device=device)
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                rounds, live = one_pass(mu, mass, lim, target)
+                e1.record(stream)
+                torch.cuda.synchronize()
+                if it >= max(3, args.warmup):
+                    times.append(e0.elapsed_time(e1))
+            t = torch.tensor([statistics.median(times)], device=device)
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            out[name] = {"us": round(t.item() * 1000.0, 1), "rounds": rounds, "clusters_left_max": live}
+    torch.set_float32_matmul_precision(prec)
+    total = out["candidate_pass"]["us"] + out["global_pass"]["us"]
+    return {"metric": "unified route us per flush tile (16 lanes x 2060 points, both passes)", "unit": "us",
+            "value": round(total, 1), "passes": out,
+            "config": {k: v for k, v in cfg.items()} | {"radius_limit": round(float(limits[0]), 3),
+                                                        "l2": "16 x 2060^2 float32 distances = 272 MB > L2"}}
 
 
 # ---------------------------------------------------------------------------------------------- KV-head sharded
@@ -682,6 +825,8 @@ def main():
     ap.add_argument("--decode-steps", type=int, default=32, help="timed decode steps (0: skip the decode leg)")
     ap.add_argument("--decode-batch", type=int, default=DECODE["batch"], help="decode sequences (profiling runs only)")
     ap.add_argument("--streams", type=int, default=28, help="streams the layers' flushes are spread over")
+    ap.add_argument("--flush-attend", type=int, default=1, help="run the flush-and-attend prefill leg (0: skip)")
+    ap.add_argument("--unified", type=int, default=1, help="run the unified-route leg (0: skip)")
     ap.add_argument("--kv-layers", type=int, default=28,
                     help="layers of the KV-head-sharded leg (BASELINE configs[2]; 0 skips it)")
     args = ap.parse_args()
@@ -714,9 +859,13 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     res = bench_ours(args, rank, world, local_rank)
+    inputs = res.pop("inputs")
+    fa = bench_flush_attend(args, rank, world, local_rank, inputs) if args.flush_attend else None
+    del inputs
     dec = bench_decode(args, rank, world, local_rank) if args.decode_steps > 0 else None
     pre = bench_prefill(args, rank, world, local_rank) if args.decode_steps > 0 else None
     kvs = bench_kv_sharded(args, rank, world, local_rank) if args.kv_layers > 0 else None
+    uni = bench_unified(args, rank, world, local_rank) if args.unified else None
     cpu = None
     if rank == 0 and world == 1 and args.cpu_flushes > 0:
         us, n = cpu_flush_sample(args.cpu_flushes)
@@ -734,7 +883,8 @@ def main():
                     flushes_per_step=res["flushes_per_step"],
                     rows_per_flush={k: round(v / res["flushes_per_step"], 1) for k, v in res["counters"].items()
                                     if k != "flushes"},
-                    decode=dec, prefill=pre, kv_sharded=kvs)
+                    decode=dec, prefill=pre, flush_attend=fa, kv_sharded=kvs,
+                    unified=uni)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

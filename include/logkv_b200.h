@@ -157,6 +157,23 @@ LOGKV_API int logkv_flush_scores(const logkv_layout_t* layout, const logkv_state
 LOGKV_API int logkv_flush_commit(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
                                  int32_t recent_count, void* workspace, size_t workspace_bytes,
                                  const float* partials_all, int32_t ranks, void* stream);
+/*
+ * Route overlap (replaces the side-stream route decisions of LOGKV_ROUTE_OVERLAP,
+ * litgpt/log_kv_cache.py:3814-3849).  A flush's decisions (snapshot, span cut, span scores,
+ * attach decisions, span choice, seeding, per-cluster plan) read only the flushed window rows,
+ * the exact pool and the cluster state that the previous flush committed, and write only the
+ * workspace; so they need not wait for readers of the cache (attention) queued since the
+ * previous flush.  logkv_flush_decide enqueues them (on a side stream that waits for the end of
+ * the previous flush); logkv_flush_apply enqueues the rest (ladder, pool rewrite, window shift)
+ * on the caller's stream after the decisions.  The pair equals logkv_flush.  Valid when every
+ * flushed row was in the window when the previous flush ended, and when nothing between the
+ * two writes the rows or state the decisions read.
+ */
+LOGKV_API int logkv_flush_decide(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                 int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream);
+LOGKV_API int logkv_flush_apply(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Host-side address arithmetic only: where this workspace keeps the rank's span parts, and their float count. */
 LOGKV_API int logkv_flush_partials(const logkv_layout_t* layout, int32_t flush_tokens, void* workspace,
                                    float** partials, size_t* count);

@@ -98,6 +98,9 @@ def lib() -> ctypes.CDLL:
         handle.logkv_flush_scores.argtypes = flush_args + [ctypes.c_void_p]
         handle.logkv_flush_commit.restype = ctypes.c_int
         handle.logkv_flush_commit.argtypes = flush_args + [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p]
+        for name in ("logkv_flush_decide", "logkv_flush_apply"):
+            getattr(handle, name).restype = ctypes.c_int
+            getattr(handle, name).argtypes = flush_args + [ctypes.c_void_p]
         handle.logkv_flush_partials.restype = ctypes.c_int
         handle.logkv_flush_partials.argtypes = [P(Layout), ctypes.c_int32, ctypes.c_void_p,
                                                 P(P(ctypes.c_float)), P(ctypes.c_size_t)]

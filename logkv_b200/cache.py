@@ -16,6 +16,7 @@ from __future__ import annotations
 import contextlib
 import ctypes
 import math
+import os
 
 import torch
 import torch.nn as nn
@@ -77,6 +78,12 @@ class _SemanticReplayUpdates:
 
 
 class LogStructuredKVCache(nn.Module):
+    # Route decisions beside the attention on a side stream (the reference's LOGKV_ROUTE_OVERLAP,
+    # log_kv_cache.py:3814-3849): the flush's decision kernels wait only for the end of the
+    # previous flush of this cache, not for the work queued on the caller's stream since then.
+    _route_overlap = os.environ.get("LOGKV_ROUTE_OVERLAP", "0") == "1"
+    _ROUTE_STREAMS: dict = {}
+
     def __init__(self, k_shape, v_shape, B: int = 512, recent_size: int = 0, device=None, dtype=None, *,
                  semantic_clusters: bool = True, cluster_k_max: int = 12, cluster_lambda_rel: float = 1.0,
                  seg_eta: float = 1.0, seg_g0: float = 2048.0, seg_gap_max=None, seg_block_level: int = 0,
@@ -231,6 +238,10 @@ class LogStructuredKVCache(nn.Module):
         self._replaying_updates = False
         self._update_actions = None
         self.profile_events = None   # set to a list of LOGKV_FLUSH_STAGES+1 torch.cuda.Event to time stages
+        self._route_ready = None     # end of the last flush (route overlap), with the window rows it had
+        self._route_ready_rows = 0
+        self._route_ready_captured = False
+        self._route_done = None
 
     # ------------------------------------------------------------------ C-ABI state
     def _apply(self, fn, *args, **kwargs):
@@ -342,6 +353,40 @@ class LogStructuredKVCache(nn.Module):
             ctypes.c_void_p(self.op_log.data_ptr()), ctypes.c_void_p(self.op_log_len.data_ptr()),
             self.op_log.size(2), ctypes.c_void_p(_lib.stream_ptr(self.level_k.device))), "logkv_flush_oplog_append")
 
+    def _route_decision_stream(self, take: int):
+        """High-priority side stream ordered after the previous flush, or None.
+
+        The decisions read the flushed window rows, the exact pool and the cluster state that
+        the previous flush committed, and write only this cache's workspace; the rest of the
+        flush returns to the caller's stream after them.  Only when every flushed row was
+        already in the window at the end of the previous flush (rows appended since then keep
+        the caller's stream), without profiling or KV-head sharding, and inside a CUDA-graph
+        capture only when the previous flush was captured too (the fork becomes a graph branch).
+        """
+        dev = self.level_k.device
+        if (not self._route_overlap or dev.type != "cuda" or self._route_ready is None
+                or self.kv_shard_group is not None or self.profile_events is not None
+                or take > self._route_ready_rows
+                or self._route_ready_captured != torch.cuda.is_current_stream_capturing()):
+            return None
+        stream = self._ROUTE_STREAMS.get(dev)
+        if stream is None:
+            stream = self._ROUTE_STREAMS[dev] = torch.cuda.Stream(dev, priority=-1)
+        stream.wait_event(self._route_ready)
+        return stream
+
+    def _route_mark_ready(self) -> None:
+        """Record where the next flush's decisions may start (after this flush and its readers)."""
+        dev = self.level_k.device
+        if not self._route_overlap or dev.type != "cuda":
+            self._route_ready = None
+            return
+        if self._route_ready is None:
+            self._route_ready = torch.cuda.Event()
+        self._route_ready.record(torch.cuda.current_stream(dev))
+        self._route_ready_rows = self.recent_count
+        self._route_ready_captured = torch.cuda.is_current_stream_capturing()
+
     def flush_device(self, take: int) -> None:
         """One device flush of the ``take`` oldest window tokens plus the window shift."""
         self._ladder_epoch += 1
@@ -351,6 +396,16 @@ class LogStructuredKVCache(nn.Module):
                 ctypes.c_void_p(_lib.stream_ptr(self.level_k.device)))
         if self.kv_shard_group is not None:
             self._sharded_flush(args, int(take))
+            return
+        side = self._route_decision_stream(int(take))
+        if side is not None:
+            lib = _lib.lib()
+            _lib.check(lib.logkv_flush_decide(*args[:6], ctypes.c_void_p(side.cuda_stream)), "logkv_flush_decide")
+            if self._route_done is None:
+                self._route_done = torch.cuda.Event()
+            self._route_done.record(side)
+            torch.cuda.current_stream(self.level_k.device).wait_event(self._route_done)
+            _lib.check(lib.logkv_flush_apply(*args), "logkv_flush_apply")
             return
         if self.profile_events is None:
             _lib.check(_lib.lib().logkv_flush(*args), "logkv_flush")
@@ -467,6 +522,7 @@ class LogStructuredKVCache(nn.Module):
                 self._flush_cursor += 1
                 self.recent_count -= take
                 pending -= take
+                self._route_mark_ready()
 
     # ------------------------------------------------------------------ read side
     def _semantic_attention_plan(self):
@@ -539,4 +595,5 @@ class LogStructuredKVCache(nn.Module):
         self.token_count = 0
         self.recent_count = 0
         self._flush_cursor = 0
+        self._route_ready = None
         self._ladder_epoch += 1

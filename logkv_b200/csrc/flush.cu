@@ -35,8 +35,7 @@ static size_t score_smem_bytes(const Geo& g, size_t esize) {
   return 8 * (size_t)score_warp_floats(g.D, g.K, (int)esize) * sizeof(float);  // 8 warps
 }
 static size_t attach_smem_bytes(const Geo& g) {
-  const size_t att_tok = 256 / (g.K <= 16 ? 16 : 32);
-  return (size_t)(g.K + att_tok) * (g.D + 4) * sizeof(float);
+  return (size_t)(g.K + kAttachTokens) * (g.D + 4) * sizeof(float);
 }
 // Delayed re-insert sort keys, token sources and the staged rows of the centroid sum.
 static size_t prep_smem_bytes(const Geo& g, size_t esize) {
@@ -96,19 +95,28 @@ __global__ void __launch_bounds__(256) score_kernel(Geo g, logkv_state_t s, Work
 // cluster state, so the entry wait is skipped.  Block (0, 0, 0) waits at its end instead:
 // this grid then completes only after the score grid, and the next kernel's entry wait
 // covers both, while every other block leaves as soon as its tokens are done.
-template <typename T, int DC>
+template <typename T, int DC, int CPL>
 __global__ void __launch_bounds__(256) attach_kernel(Geo g, logkv_state_t s, Work w) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  attach_body<T, DC>(g, s, w, blockIdx.x);
+  attach_body<T, DC, CPL>(g, s, w, blockIdx.x);
   if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+template <typename T, int DC, int CPL>
+static void launch_attach_cpl(const Geo& g, const logkv_state_t& s, const Work& w, size_t smem, int grid_x,
+                              cudaStream_t st) {
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(attach_kernel<T, DC, CPL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  launch_pdl(attach_kernel<T, DC, CPL>, dim3(grid_x, g.G, g.B), 256, smem, st, g, s, w);
+}
+
+// Centres per lane: a token's 4 lanes cover K <= 4 * CPL centres.
 template <typename T, int DC>
 static void launch_attach(const Geo& g, const logkv_state_t& s, const Work& w, size_t smem, int grid_x,
                           cudaStream_t st) {
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(attach_kernel<T, DC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  launch_pdl(attach_kernel<T, DC>, dim3(grid_x, g.G, g.B), 256, smem, st, g, s, w);
+  if (g.K <= 12) launch_attach_cpl<T, DC, 3>(g, s, w, smem, grid_x, st);
+  else if (g.K <= 16) launch_attach_cpl<T, DC, 4>(g, s, w, smem, grid_x, st);
+  else launch_attach_cpl<T, DC, 8>(g, s, w, smem, grid_x, st);
 }
 
 // ---------------------------------------------------------------- K8: window shift
@@ -264,6 +272,9 @@ static size_t carve(const Geo& g, size_t esize, char* base, Work* w) {
   w->nkeep = c.take<int32_t>(B, 4);
   w->arch_idx = c.take<int32_t>(B * NW, 4);
   w->narch = c.take<int32_t>(B, 4);
+  w->span_len = c.take<int32_t>(B * P, 4);
+  w->span_closed = c.take<uint8_t>(B * P, 1);
+  w->nspans = c.take<int32_t>(B, 4);
   w->assign = c.take<int8_t>(B * G * NW, 1);
   w->assign_tok = c.take<int8_t>(B * G * NW, 1);
   w->orphan = c.take<uint8_t>(B * G * NW, 1);
@@ -320,11 +331,9 @@ static TapeSegs tape_segments(const Geo& g, const logkv_state_t& s, const Work& 
   add(w.nkeep, t.nkeep, B * 4);
   add(w.arch_idx, t.arch_idx, B * NW * 4);
   add(w.narch, t.narch, B * 4);
-  add(s.alpha_span_len, t.span_len, B * P * 4);
-  add(s.alpha_span_closed, t.span_closed, B * P);
-  add(s.alpha_nspans, t.nspans, B * 4);
-  add(s.alpha_rowcount, t.rowcount, B * 4);
-  add(s.alpha_count, t.alpha_count, 4);
+  add(w.span_len, t.span_len, B * P * 4);
+  add(w.span_closed, t.span_closed, B * P);
+  add(w.nspans, t.nspans, B * 4);
   add(w.tok_list, t.tok_list, B * G * NW * 4);
   add(w.plan_off, t.plan_off, B * G * K * 4);
   add(w.plan_n, t.plan_n, B * G * K * 4);
@@ -335,10 +344,12 @@ static TapeSegs tape_segments(const Geo& g, const logkv_state_t& s, const Work& 
   return segs;
 }
 
-// Phases: kPhaseScores = snapshot, span cut, span scores (the group parts of this rank);
-// kPhaseCommit = everything from the bounded greedy on.  A KV-head-sharded flush
-// all-gathers the group parts between the two.
-constexpr int kPhaseScores = 1, kPhaseCommit = 2, kPhaseAll = 3;
+// Phases: kPhaseScores = snapshot, span cut, span scores (the group parts of this rank) and
+// attach decisions; kPhaseRoute = the bounded greedy, seeding and the per-cluster plan;
+// kPhaseApply = the ladder (prepare, cascade), the pool rewrite and the window shift.  Scores
+// and route write only the workspace.  A KV-head-sharded flush all-gathers the group parts
+// between scores and route; an overlapped flush runs scores + route on a side stream.
+constexpr int kPhaseScores = 1, kPhaseRoute = 2, kPhaseApply = 4, kPhaseDecide = 3, kPhaseCommit = 6, kPhaseAll = 7;
 
 template <typename T>
 static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st, cudaEvent_t* ev,
@@ -366,14 +377,13 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
     cudaFuncSetAttribute(score_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)score_smem);
   const int score_blocks = std::max(1, std::min((g.NC * g.G + 7) / 8, 2 * sm_count / g.B + 1));
   launch_pdl(score_kernel<T>, dim3(score_blocks, g.B), 256, score_smem, st, g, s, w);
-  const int att_tok = 256 / (g.K <= 16 ? 16 : 32);
   const size_t attach_smem = attach_smem_bytes(g);
-  const int attach_x = (g.NW + att_tok * kAttachRounds - 1) / (att_tok * kAttachRounds);
+  const int attach_x = (g.NW + kAttachTokens - 1) / kAttachTokens;
   if (g.D == 128) launch_attach<T, 128>(g, s, w, attach_smem, attach_x, st);
   else if (g.D == 64) launch_attach<T, 64>(g, s, w, attach_smem, attach_x, st);
   else launch_attach<T, 0>(g, s, w, attach_smem, attach_x, st);
   }
-  if (!(phases & kPhaseCommit)) return (int)cudaGetLastError();
+  if (phases & kPhaseRoute) {
   mark();
   const size_t choose_smem = choose_smem_bytes(g);
   if (choose_smem > 48 * 1024)
@@ -393,6 +403,8 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
     launch_pdl(seed_kernel<T>, dim3(kSeedCluster * g.G, g.B), 512, seed_smem, st, gs, s, w);
   }
   launch_pdl(plan_kernel<T>, dim3(g.G, g.B), 1024, 0, st, g, s, w);
+  }
+  if (!(phases & kPhaseApply)) return (int)cudaGetLastError();
   mark();
   const size_t prep_smem = prep_smem_bytes(g, sizeof(T));
   if (prep_smem > 48 * 1024)
@@ -523,6 +535,18 @@ extern "C" size_t logkv_flush_workspace_bytes(const logkv_layout_t* layout, int3
 extern "C" int logkv_flush(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
                            int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream) {
   return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream, nullptr);
+}
+
+extern "C" int logkv_flush_decide(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                  int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream) {
+  return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream, nullptr,
+                   kPhaseDecide);
+}
+
+extern "C" int logkv_flush_apply(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                 int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream) {
+  return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream, nullptr,
+                   kPhaseApply);
 }
 
 extern "C" size_t logkv_tape_bytes(const logkv_layout_t* layout, int32_t flush_tokens) {

@@ -54,7 +54,6 @@ __global__ void snapshot_kernel(Geo g, logkv_state_t s, Work w) {
       w.snap_rowcount[b] = s.alpha_rowcount[b];
       if (b == 0) {
         *w.status = 0;
-        *s.alpha_count = 0;
         w.counters[kCntFlushes] += 1ull;
       }
     }
@@ -656,8 +655,8 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
         }
         const int sp = carry_sp + sincl - 1;
         if (sp < P) {
-          s.alpha_span_len[(size_t)b * P + sp] = sz;
-          s.alpha_span_closed[(size_t)b * P + sp] = (flags[i] & 2) ? 1 : 0;
+          w.span_len[(size_t)b * P + sp] = sz;
+          w.span_closed[(size_t)b * P + sp] = (flags[i] & 2) ? 1 : 0;
         }
       } else {
         const int at = carry_arch + aincl - sz;
@@ -686,9 +685,7 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
     }
     w.nkeep[b] = nkeep;
     w.narch[b] = carry_arch;
-    s.alpha_nspans[b] = carry_sp < P ? carry_sp : P;
-    s.alpha_rowcount[b] = nkeep;
-    atomicMax(s.alpha_count, nkeep);
+    w.nspans[b] = carry_sp < P ? carry_sp : P;
   }
   __syncthreads();
   // Archive rows in position order (stable).  Usually already sorted.
@@ -747,6 +744,22 @@ __global__ void pool_rewrite_kernel(Geo g, logkv_state_t s, Work w) {
       const bool kept = row < nkeep;
       s.alpha_pos[(size_t)b * g.P + row] = kept ? token_position(g, s, w, b, w.keep_idx[(size_t)b * g.P + row]) : 0;
       s.alpha_valid[(size_t)b * g.P + row] = kept ? 1 : 0;
+    }
+    // The choice's span table and counts become the pool's (the decision kernels write
+    // only the workspace, so that they may run beside readers of the cache).
+    const int ns = w.nspans[b];
+    for (int i = threadIdx.x; i < ns; i += blockDim.x) {
+      s.alpha_span_len[(size_t)b * g.P + i] = w.span_len[(size_t)b * g.P + i];
+      s.alpha_span_closed[(size_t)b * g.P + i] = w.span_closed[(size_t)b * g.P + i];
+    }
+    if (threadIdx.x == 0) {
+      s.alpha_nspans[b] = ns;
+      s.alpha_rowcount[b] = nkeep;
+      if (b == 0) {
+        int most = 0;
+        for (int j = 0; j < g.B; ++j) most = max(most, w.nkeep[j]);
+        *s.alpha_count = most;
+      }
     }
   }
 }

@@ -71,6 +71,9 @@ struct Work {
   int32_t* nkeep;          // [B]
   int32_t* arch_idx;       // [B,NW] archived token indices, position order
   int32_t* narch;          // [B]
+  int32_t* span_len;       // [B,P] the pool's new span table, written by the choice, committed by K7
+  uint8_t* span_closed;    // [B,P]
+  int32_t* nspans;         // [B]
   int8_t* assign;          // [B,G,NW] cluster per archived token (archive rank order)
   int8_t* assign_tok;      // [B,G,NW] attach decision per token (token index order)
   uint8_t* orphan;         // [B,G,NW] token index order

@@ -16,179 +16,189 @@ namespace logkv {
 // ---------------------------------------------------------------- K4: attach decisions
 // Decisions for every token of the [old pool | flushed window] index space (the archive
 // is a subset, picked later by the span choice; decisions depend only on the frozen
-// cluster state).  A token owns 16 (K <= 16) or 32 consecutive lanes, one per centre: each
-// computes the token's dot product with its centre left to right over the features, then
-// the semantic distance and routing cost; the token's winner is the first-index argmin of
-// the costs over live centres (as the reference's in-order scan / torch.argmin), found by a
-// shuffle reduction over the token's lanes.  Orphans then get exact distances to the live
-// centres the same way (nearest = first-index argmin).  Token rows and centres are staged
-// in shared memory (16-byte rows, conflict-free); centre norms come from the snapshot
-// kernel.  Outputs are indexed by token.  DC != 0 is a compile-time head dim.
+// cluster state).  A warp takes 8 tokens; a token's 4 lanes each own CPL consecutive centres
+// (lane q: centres q*CPL .. q*CPL+CPL-1) and compute, left to right over the features, the
+// token's dot product with each of them and |x|^2, then the semantic distances and routing
+// costs; the winner is the first-index argmin of the costs over live centres (as the
+// reference's in-order scan / torch.argmin): first over the lane's centres in index order,
+// then by a shuffle reduction over the token's 4 lanes.  Orphans then get exact distances to
+// the live centres the same way (nearest = first-index argmin), in a second pass that a warp
+// runs only when one of its tokens is an orphan.  Token rows (64 per block) and centres are
+// staged in shared memory as float rows of D+4 words: the 8 token rows of a warp fall in
+// distinct bank quads, and a centre load of a warp reads 4 rows (one per lane of a token),
+// which for K <= 12 also fall in distinct bank quads, so every 16-byte shared load is one
+// wavefront; a token row is read by 4 lanes and a centre row by 8 tokens' lanes at once,
+// instead of once per (token, centre).  Centre norms come from the snapshot kernel.
+// Outputs are indexed by token.  DC != 0 is a compile-time head dim.
+constexpr int kAttachTokens = 64;   // tokens per 256-thread block: 8 warps x 8 tokens
 
-// First-index argmin over the `width` lanes of a token (width 16 or 32, aligned): lanes with
-// valid = false never win; returns the winning lane offset, or width if none is valid.
-__device__ __forceinline__ int group_argmin(float v, bool valid, int c, int width, float* best_v) {
-  float bv = valid ? v : INFINITY;
-  int bi = valid ? c : width;
+template <int CPL>
+__device__ __forceinline__ void lane_argmin(const float (&v)[CPL], const bool (&ok)[CPL], int c0, float* bv, int* bi,
+                                            int none) {
+  *bv = INFINITY;
+  *bi = none;
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) {
-    if (off >= width) continue;
-    const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-    if (ov < bv || (ov == bv && oi < bi)) {
-      bv = ov;
-      bi = oi;
+  for (int j = 0; j < CPL; ++j)
+    if (ok[j] && v[j] < *bv) {   // strict: the first index wins ties; NaN never wins
+      *bv = v[j];
+      *bi = c0 + j;
     }
-  }
-  *best_v = bv;
-  return bi;
 }
 
-constexpr int kAttachRounds = 1;  // token rounds per block (the staged centres are reused)
+// (value, index) minimum over the 4 lanes of a token, lowest index on ties; `aux` follows the winner.
+__device__ __forceinline__ void quad_argmin(float* bv, int* bi, float* aux) {
+#pragma unroll
+  for (int off = 1; off < 4; off <<= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, *bv, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, *bi, off);
+    const float oa = __shfl_xor_sync(0xffffffffu, *aux, off);
+    if (ov < *bv || (ov == *bv && oi < *bi)) {
+      *bv = ov;
+      *bi = oi;
+      *aux = oa;
+    }
+  }
+}
 
-template <typename T, int DC>
+template <typename T, int DC, int CPL>
 __device__ void attach_body(const Geo& g, const logkv_state_t& s, const Work& w, int blk) {
   const int b = blockIdx.z, grp = blockIdx.y, tid = threadIdx.x;
   const int D = DC ? DC : g.D, K = g.K;
-  const int slots = K <= 16 ? 16 : 32;          // lanes per token
-  const int ntok = blockDim.x / slots;          // tokens per round
-  if (blk * kAttachRounds * ntok >= g.NW) return;
+  const int r0 = blk * kAttachTokens;
+  if (r0 >= g.NW) return;
+  const int nrow = min(kAttachTokens, g.NW - r0);
   extern __shared__ float4 sm4[];
-  const int RS = D + 4;                          // row stride in floats: 16-byte rows, conflict-free
-  float* mu = reinterpret_cast<float*>(sm4);     // [K][RS]
-  float* xs = mu + K * RS;                       // [ntok][RS]
-  __shared__ float xxs[32];
-  __shared__ int orph_tok[32];
-  __shared__ int n_orph;
+  const int RS4 = D / 4 + 1;                     // row stride in float4: D + 4 words
+  float4* mu4 = sm4;                             // [K][RS4]
+  float4* xs4 = sm4 + K * RS4;                   // [kAttachTokens][RS4]
   __shared__ float cn_s[kMaxClusters];
   __shared__ long long phi_s[kMaxClusters];
   __shared__ uint8_t alv_s[kMaxClusters];
+  __shared__ int any_alive_s;
   const size_t lane0 = ((size_t)b * g.G + grp) * K;
-  if (tid == 0) n_orph = 0;
+  if (tid == 0) any_alive_s = 0;
+  __syncthreads();
   for (int cc = tid; cc < K; cc += blockDim.x) {
     cn_s[cc] = w.cnorm[lane0 + cc];
     phi_s[cc] = s.p_hi_c[lane0 + cc];
     alv_s[cc] = s.alive[lane0 + cc] != 0;
+    if (s.alive[lane0 + cc]) any_alive_s = 1;
   }
-  const int warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
   const int D4 = D / 4;
-  // Centres and token rows into shared memory: one row per warp at a time, 16-byte units.
   const float4* cent4 = reinterpret_cast<const float4*>(s.centroid + lane0 * D);
-  for (int cc = warp; cc < K; cc += nwarps)
-    for (int d4 = lane; d4 < D4; d4 += 32) reinterpret_cast<float4*>(mu + cc * RS)[d4] = cent4[cc * D4 + d4];
+  for (int i = tid; i < K * D4; i += blockDim.x) mu4[(i / D4) * RS4 + i % D4] = cent4[i];
   const T* snap = static_cast<const T*>(w.snap_k);
   const T* rec = static_cast<const T*>(s.recent_k_raw);
-  for (int round = 0; round < kAttachRounds; ++round) {
-    const int r0 = (blk * kAttachRounds + round) * ntok;
-    if (r0 >= g.NW) break;   // uniform across the block
-    const int nrow = min(ntok, g.NW - r0);
-    constexpr int VN = Vec<T>::N;
-    const int DV = D / VN;
-    for (int row = warp; row < nrow; row += nwarps) {
-      const T* src = token_row<T>(g, snap, rec, b, grp, r0 + row);
-      for (int v = lane; v < DV; v += 32) {
-        float xv[VN];
-        unpack(*reinterpret_cast<const uint4*>(src + v * VN), xv, (const T*)nullptr);
+  constexpr int VN = Vec<T>::N;
+  const int DV = D / VN;
+  for (int i = tid; i < nrow * DV; i += blockDim.x) {
+    const int row = i / DV, v = i % DV;
+    float xv[VN];
+    unpack(*reinterpret_cast<const uint4*>(token_row<T>(g, snap, rec, b, grp, r0 + row) + v * VN), xv,
+           (const T*)nullptr);
 #pragma unroll
-        for (int e = 0; e < VN; e += 4)
-          *reinterpret_cast<float4*>(xs + row * RS + v * VN + e) = make_float4(xv[e], xv[e + 1], xv[e + 2], xv[e + 3]);
-      }
-    }
-    __syncthreads();
-    // Pass 1, one lane per (token, centre): the dot product, left to right over the features.
-    // When a lane of the token's group is spare (K < slots), lane K runs the same loop against
-    // the token itself, so its "dot" is |x|^2 (same operations).
-    const int tok = tid / slots, c = tid % slots;
-    const bool spare = K < slots;
-    const bool live_tok = tok < nrow;
-    float dot = 0.f;
-    if (live_tok && c <= (spare ? K : K - 1)) {
-      const float4* x = reinterpret_cast<const float4*>(xs + tok * RS);
-      const float4* m = reinterpret_cast<const float4*>(c < K ? mu + c * RS : xs + tok * RS);
-#pragma unroll(DC ? 8 : 1)
-      for (int d4 = 0; d4 < D4; ++d4) {
-        const float4 xv = x[d4], mv = m[d4];
-        dot = fadd(dot, fmul(xv.x, mv.x));
-        dot = fadd(dot, fmul(xv.y, mv.y));
-        dot = fadd(dot, fmul(xv.z, mv.z));
-        dot = fadd(dot, fmul(xv.w, mv.w));
-      }
-      if (c == K) xxs[tok] = dot;
-    }
-    if (!spare && live_tok && c == 0) {
-      const float* x = xs + tok * RS;
-      float xx = 0.f;
-      for (int d = 0; d < D; ++d) xx = fadd(xx, fmul(x[d], x[d]));
-      xxs[tok] = xx;
-    }
-    __syncthreads();
-    // Pass 2, one lane per (token, centre): semantic distance and routing cost; then the
-    // token's decision by a shuffle argmin over its lanes.
-    const int r = r0 + tok;   // token index
-    const bool mine = live_tok && c < K;
-    const bool alive_c = mine && alv_s[c];
-    float semv = 0.f, cost = INFINITY;
-    if (mine) {
-      const int64_t pos = token_position(g, s, w, b, r);
-      semv = fmaxf(fsub(fadd(xxs[tok], cn_s[c]), fmul(2.f, dot)), 0.f);
-      const float gap = fmaxf((float)(pos - (int64_t)phi_s[c]), 0.f);
-      cost = fadd(semv, fmul(g.eta, fdiv(gap, fadd(gap, g.g0))));
-    }
-    const unsigned gmask = (slots == 32 ? 0xffffffffu : 0xffffu) << (lane & ~(slots - 1) & 31);
-    const bool any_alive = (__ballot_sync(0xffffffffu, alive_c) & gmask) != 0u;
-    float best_cost;
-    // Live centres with a cost below +inf compete (NaN and +inf never replace the initial +inf).
-    const int wi = group_argmin(cost, alive_c && cost < INFINITY, c, slots, &best_cost);
-    const int winner = wi < slots ? wi : 0;
-    const int src_lane = (lane & ~(slots - 1)) + winner;
-    const float sem_win = __shfl_sync(0xffffffffu, semv, src_lane);
-    // No live centre: winner 0 with cluster 0's semantic distance (the token is an orphan);
-    // live centres but no finite cost: winner 0 with s = 0 (the scan's initial values).
-    const float s_win = !any_alive ? sem_win : (wi < slots ? sem_win : 0.f);
-    const size_t o = ((size_t)b * g.G + grp) * g.NW + r;
-    if (live_tok && c == 0) {
-      const float thresh = fmul(g.lam, s.s_h[(size_t)b * g.G + grp]);
-      const bool direct = any_alive && s_win <= thresh;
-      w.orphan[o] = direct ? 0 : 1;
-      w.s_winner[o] = s_win;
-      if (direct || !any_alive) w.assign_tok[o] = (int8_t)winner;   // no live centre: 0
-      else orph_tok[atomicAdd(&n_orph, 1)] = tok;
-    }
-    __syncthreads();
-    const int no = n_orph;
-    if (no > 0) {
-      // Exact distances of the queued orphans to the live centres: orphan j takes the lanes of
-      // token slot j; nearest = first-index argmin (NaN and +inf never win; none: centre 0).
-      const int j = tok;
-      float dist = INFINITY;
-      const bool act = j < no && c < K && alv_s[c];
-      if (act) {
-        const int t = orph_tok[j];
-        const float4* x = reinterpret_cast<const float4*>(xs + t * RS);
-        const float4* m = reinterpret_cast<const float4*>(mu + c * RS);
-        float ex = 0.f;
-#pragma unroll(DC ? 8 : 1)
-        for (int d4 = 0; d4 < D4; ++d4) {
-          const float4 xv = x[d4], mv = m[d4];
-          float df = fsub(xv.x, mv.x);
-          ex = fadd(ex, fmul(df, df));
-          df = fsub(xv.y, mv.y);
-          ex = fadd(ex, fmul(df, df));
-          df = fsub(xv.z, mv.z);
-          ex = fadd(ex, fmul(df, df));
-          df = fsub(xv.w, mv.w);
-          ex = fadd(ex, fmul(df, df));
-        }
-        dist = __fsqrt_rn(ex);
-      }
-      float best_d;
-      const int ni = group_argmin(dist, act && dist < INFINITY, c, slots, &best_d);
-      if (j < no && c == 0)
-        w.assign_tok[((size_t)b * g.G + grp) * g.NW + r0 + orph_tok[j]] = (int8_t)(ni < slots ? ni : 0);
-    }
-    __syncthreads();  // token rows and the orphan queue are reused by the next round
-    if (tid == 0) n_orph = 0;
+    for (int e = 0; e < VN; e += 4)
+      xs4[row * RS4 + (v * VN + e) / 4] = make_float4(xv[e], xv[e + 1], xv[e + 2], xv[e + 3]);
   }
+  __syncthreads();
+  const int lane = tid & 31, q = lane & 3;
+  const int t = (tid >> 5) * 8 + (lane >> 2);   // token slot in the block
+  const bool live_tok = t < nrow;
+  const int c0 = q * CPL;
+  int cj[CPL];
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) cj[j] = min(c0 + j, K - 1);   // spare slots read a real row
+  const float4* x = xs4 + t * RS4;
+  // Pass 1: dot products with the lane's centres and |x|^2, left to right.
+  float dot[CPL];
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) dot[j] = 0.f;
+  float xx = 0.f;
+#pragma unroll(DC ? 4 : 1)
+  for (int d4 = 0; d4 < D4; ++d4) {
+    const float4 xv = x[d4];
+    xx = fadd(xx, fmul(xv.x, xv.x));
+    xx = fadd(xx, fmul(xv.y, xv.y));
+    xx = fadd(xx, fmul(xv.z, xv.z));
+    xx = fadd(xx, fmul(xv.w, xv.w));
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+      const float4 mv = mu4[cj[j] * RS4 + d4];
+      dot[j] = fadd(dot[j], fmul(xv.x, mv.x));
+      dot[j] = fadd(dot[j], fmul(xv.y, mv.y));
+      dot[j] = fadd(dot[j], fmul(xv.z, mv.z));
+      dot[j] = fadd(dot[j], fmul(xv.w, mv.w));
+    }
+  }
+  // Semantic distances and routing costs of the lane's centres.
+  const int r = r0 + t;   // token index
+  const int64_t pos = live_tok ? token_position(g, s, w, b, r) : 0;
+  float semv[CPL], cost[CPL];
+  bool ok[CPL];
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) {
+    const int c = cj[j];
+    semv[j] = fmaxf(fsub(fadd(xx, cn_s[c]), fmul(2.f, dot[j])), 0.f);
+    const float gap = fmaxf((float)(pos - (int64_t)phi_s[c]), 0.f);
+    cost[j] = fadd(semv[j], fmul(g.eta, fdiv(gap, fadd(gap, g.g0))));
+    // Live centres with a cost below +inf compete (NaN and +inf never replace the initial +inf).
+    ok[j] = c0 + j < K && alv_s[c] && cost[j] < INFINITY;
+  }
+  float best_cost, sem_win = 0.f;
+  int wi;
+  lane_argmin<CPL>(cost, ok, c0, &best_cost, &wi, kMaxClusters);
+#pragma unroll
+  for (int j = 0; j < CPL; ++j)
+    if (c0 + j == wi) sem_win = semv[j];
+  quad_argmin(&best_cost, &wi, &sem_win);
+  const bool any_alive = any_alive_s != 0;
+  const int winner = wi < kMaxClusters ? wi : 0;
+  // No live centre: winner 0 with cluster 0's semantic distance (the token is an orphan);
+  // live centres but no finite cost: winner 0 with s = 0 (the scan's initial values).
+  const float sem0 = __shfl_sync(0xffffffffu, semv[0], lane & ~3);
+  const float s_win = !any_alive ? sem0 : (wi < kMaxClusters ? sem_win : 0.f);
+  const size_t o = ((size_t)b * g.G + grp) * g.NW + r;
+  const float thresh = fmul(g.lam, s.s_h[(size_t)b * g.G + grp]);
+  const bool direct = any_alive && s_win <= thresh;
+  const bool orphan = live_tok && any_alive && !direct;
+  if (live_tok && q == 0) {
+    w.orphan[o] = direct ? 0 : 1;
+    w.s_winner[o] = s_win;
+    if (!orphan) w.assign_tok[o] = (int8_t)winner;   // no live centre: 0
+  }
+  if (!__any_sync(0xffffffffu, orphan)) return;
+  // Pass 2 (warps with an orphan): exact distances to the lane's live centres, left to right;
+  // nearest = first-index argmin (NaN and +inf never win; none: centre 0).
+  float ex[CPL];
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) ex[j] = 0.f;
+#pragma unroll(DC ? 4 : 1)
+  for (int d4 = 0; d4 < D4; ++d4) {
+    const float4 xv = x[d4];
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+      const float4 mv = mu4[cj[j] * RS4 + d4];
+      float df = fsub(xv.x, mv.x);
+      ex[j] = fadd(ex[j], fmul(df, df));
+      df = fsub(xv.y, mv.y);
+      ex[j] = fadd(ex[j], fmul(df, df));
+      df = fsub(xv.z, mv.z);
+      ex[j] = fadd(ex[j], fmul(df, df));
+      df = fsub(xv.w, mv.w);
+      ex[j] = fadd(ex[j], fmul(df, df));
+    }
+  }
+  float dist[CPL];
+#pragma unroll
+  for (int j = 0; j < CPL; ++j) {
+    dist[j] = __fsqrt_rn(ex[j]);
+    ok[j] = c0 + j < K && alv_s[cj[j]] && dist[j] < INFINITY;
+  }
+  float best_d, unused = 0.f;
+  int ni;
+  lane_argmin<CPL>(dist, ok, c0, &best_d, &ni, kMaxClusters);
+  quad_argmin(&best_d, &ni, &unused);
+  if (orphan && q == 0) w.assign_tok[o] = (int8_t)(ni < kMaxClusters ? ni : 0);
 }
 
 // (value, index) argmax with the lowest index winning ties.

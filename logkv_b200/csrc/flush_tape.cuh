@@ -8,7 +8,7 @@
 // buffer written by the flush itself:
 //   payload   the flushed window rows (pre-RoPE K and V, [B,G,F,D]) as the recorded flush saw them
 //   choice    kept and archived token indices and counts, the new span table (lengths, closed
-//             flags, span and row counts, alpha_count)
+//             flags, span count); the row counts and alpha_count follow from the kept counts
 //   plan      per-cluster jobs (token lists, offsets, counts, kinds, scratch ranges, base orders)
 //   cuts      the Beta cut of every 4-row group the cascade merged, per (lane, level, group)
 #pragma once
@@ -27,8 +27,6 @@ struct TapeView {
   int32_t* span_len;       // [B,P]
   uint8_t* span_closed;    // [B,P]
   int32_t* nspans;         // [B]
-  int32_t* rowcount;       // [B]
-  int32_t* alpha_count;    // [1]
   int32_t* tok_list;       // [B,G,NW]
   int32_t* plan_off;       // [B,G,K] each
   int32_t* plan_n;
@@ -62,8 +60,6 @@ inline size_t tape_carve(const Geo& g, size_t esize, char* base, TapeView* t) {
   t->span_len = static_cast<int32_t*>(take(B * P * 4));
   t->span_closed = static_cast<uint8_t*>(take(B * P));
   t->nspans = static_cast<int32_t*>(take(B * 4));
-  t->rowcount = static_cast<int32_t*>(take(B * 4));
-  t->alpha_count = static_cast<int32_t*>(take(4));
   t->tok_list = static_cast<int32_t*>(take(B * G * NW * 4));
   t->plan_off = static_cast<int32_t*>(take(B * G * K * 4));
   t->plan_n = static_cast<int32_t*>(take(B * G * K * 4));
