@@ -74,11 +74,12 @@ def random_case(seed, L, M, D, limited):
 
 
 @pytest.mark.parametrize("limited", [False, True])
-def test_unified_reduce_matches_oracle_random(limited):
-    dist, mu, mass, count, limits = random_case(11 + limited, L=4, M=300, D=64, limited=limited)
+@pytest.mark.parametrize("L,M,D", [(4, 300, 64), (1, 1500, 32)])
+def test_unified_reduce_matches_oracle_random(limited, L, M, D):
+    dist, mu, mass, count, limits = random_case(11 + limited + M, L=L, M=M, D=D, limited=limited)
     target = 1 if limited else 12
     red = U.UnifiedReduce(dist, mu, mass, count, limits, target)
-    for _ in range(2 * 300 + 8):
+    for _ in range(2 * M + 8):
         if not red.step().any():
             break
     traces, alive, stuck = red.finish()
