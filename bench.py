@@ -441,59 +441,76 @@ def unified_points(torch, cfg, device, seed):
 
 def bench_unified(args, rank, world, local_rank):
     """The unified route's two reductions per flush tile, as the reference runs them
-    (log_kv_cache.py:3185-3376): FP32 Gram (cuBLAS, highest precision) + fused pair distances,
-    then UnifiedReduce rounds with the host polling (active, live) every four rounds; first the
-    radius-limited candidate pass to one cluster per radius, then the global pass to K = 12."""
+    (log_kv_cache.py:3185-3376, :3589-3688): FP32 Gram (cuBLAS, highest precision) + fused pair
+    distances, then UnifiedReduce rounds with the host polling (active, live) every four rounds.
+    First the radius-limited candidate pass over the tile's points (to one cluster per radius),
+    then the global pass to K = 12 over each lane's 12 old centres (weight 128) followed by the
+    candidate centres (weights = their merged masses), padded to the widest lane."""
     import torch
     import torch.distributed as dist
     from logkv_b200.plugin import UnifiedReduce, pair_distances
     device = torch.device("cuda", local_rank)
     cfg = UNIFIED
-    L, M, D = cfg["lanes"], cfg["points"], cfg["head_dim"]
+    L, M, D, K = cfg["lanes"], cfg["points"], cfg["head_dim"], cfg["target"]
     mu0 = unified_points(torch, cfg, device, seed=900 + rank)
+    gen = torch.Generator(device=device).manual_seed(950 + rank)
+    old_mu = torch.randn(L, K, D, generator=gen, device=device) * 2.0
     limits = torch.full((L,), 1.2 * 0.35 * D ** 0.5, device=device)
-    count = torch.full((L,), M, dtype=torch.int64, device=device)
     stream = torch.cuda.Stream(device)
     prec = torch.get_float32_matmul_precision()
     torch.set_float32_matmul_precision("highest")
 
-    def one_pass(mu, mass, lim, target):
+    def one_pass(mu, mass, count, lim, target):
         centred = mu - mu[:, :1]
         norm = centred.square().sum(-1)
         dist_ = pair_distances(torch.bmm(centred, centred.transpose(1, 2)), norm)
         red = UnifiedReduce(dist_, mu, mass, count, lim, target)
         rounds = 0
-        for r in range(1, 2 * M + 8):
+        for r in range(1, 2 * mu.size(1) + 8):
             red.step(r)
             rounds = r
             if r % 4 == 0 and not bool(red.status[0].any()):
                 break
         traces, alive, stuck = red.finish()
-        return rounds, int(red.count.max().item())
+        return rounds, alive
 
-    out = {}
+    def route():
+        mu = mu0.clone()
+        mass = torch.ones(L, M, device=device)
+        count = torch.full((L,), M, dtype=torch.int64, device=device)
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        e[0].record(stream)
+        r1, alive = one_pass(mu, mass, count, limits, 1)
+        e[1].record(stream)
+        # Global pass input: old centres, then the candidate centres of each lane, padded.
+        keep = torch.from_numpy(alive).to(device)
+        n_new = keep.sum(1)
+        size = K + int(n_new.max())
+        order = torch.argsort((~keep).to(torch.int8), dim=1, stable=True)[:, :size - K]
+        mu2 = torch.zeros(L, size, D, device=device)
+        mass2 = torch.zeros(L, size, device=device)
+        mu2[:, :K] = old_mu
+        mass2[:, :K] = 128.0
+        mu2[:, K:] = torch.gather(mu, 1, order[..., None].expand(-1, -1, D))
+        valid = torch.arange(size - K, device=device)[None, :] < n_new[:, None]
+        mass2[:, K:] = torch.where(valid, torch.gather(mass, 1, order), 0.0)
+        r2, _ = one_pass(mu2, mass2, K + n_new, None, K)
+        e[2].record(stream)
+        torch.cuda.synchronize()
+        return e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2]), r1, r2, size
+
     with torch.no_grad(), torch.cuda.stream(stream):
-        for name, lim, target in (("candidate_pass", limits, 1), ("global_pass", None, cfg["target"])):
-            times, rounds, live = [], 0, 0
-            for it in range(max(3, args.warmup) + max(3, args.steps)):
-                mu = mu0.clone()
-                mass = torch.ones(L, M, device=device)
-                torch.cuda.synchronize()
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                rounds, live = one_pass(mu, mass, lim, target)
-                e1.record(stream)
-                torch.cuda.synchronize()
-                if it >= max(3, args.warmup):
-                    times.append(e0.elapsed_time(e1))
-            t = torch.tensor([statistics.median(times)], device=device)
-            if world > 1:
-                dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            out[name] = {"us": round(t.item() * 1000.0, 1), "rounds": rounds, "clusters_left_max": live}
+        runs = [route() for _ in range(max(3, args.warmup) + max(3, args.steps))][max(3, args.warmup):]
     torch.set_float32_matmul_precision(prec)
-    total = out["candidate_pass"]["us"] + out["global_pass"]["us"]
+    t = torch.tensor([statistics.median(r[0] for r in runs), statistics.median(r[1] for r in runs)], device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    c_us, g_us = t[0].item() * 1000.0, t[1].item() * 1000.0
+    _, _, r1, r2, size = runs[-1]
     return {"metric": "unified route us per flush tile (16 lanes x 2060 points, both passes)", "unit": "us",
-            "value": round(total, 1), "passes": out,
+            "value": round(c_us + g_us, 1),
+            "passes": {"candidate_pass": {"us": round(c_us, 1), "rounds": r1, "points": M},
+                       "global_pass": {"us": round(g_us, 1), "rounds": r2, "points": size}},
             "config": {k: v for k, v in cfg.items()} | {"radius_limit": round(float(limits[0]), 3),
                                                         "l2": "16 x 2060^2 float32 distances = 272 MB > L2"}}
 

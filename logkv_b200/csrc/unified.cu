@@ -46,6 +46,10 @@ __device__ __forceinline__ float pair_cost(float d2, float mi, float mj, float r
   const float denom = fmaxf(fadd(mi, mj), 1.f);
   valid = valid && mi > 0.f && mj > 0.f;
   if (limit) {
+    // Exact early out: with radii >= 0 and mi + mj >= 1, every rounding above leaves
+    // max(b1, b2) >= sqrt(d2) (1 - 5u) / 2 (u = 2^-24), so d2 > 4.0001 limit^2 proves the pair
+    // invalid without its divisions (an infinite or NaN limit never takes this branch).
+    if (denom == fadd(mi, mj) && d2 > fmul(fmul(4.0001f, *limit), *limit)) return __int_as_float(0x7F800000);
     const float distance = __fsqrt_rn(d2);
     const float b1 = fadd(ri, fmul(fdiv(mj, denom), distance));
     const float b2 = fadd(rj, fmul(fdiv(mi, denom), distance));
@@ -82,15 +86,30 @@ __device__ Lane lane_of(const logkv_unified_t& u, int lane) {
 // r ^ c > 0, never below the key of the row's own column, (+inf, 0), which starts the minimum.
 __device__ void scan_rows(const Lane& l, int M, const int* rows, int nrows, const int* cols, int ncols) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  constexpr int kBatch = 4;   // columns per lane whose loads are in flight together
   for (int i = warp; i < nrows; i += nwarps) {
     const int r = rows[i];
     const float* drow = l.dist + (size_t)r * M;
     const float mr = l.mass[r], rr = l.radius[r];
     long long best = kInfKey;
-    for (int k = lane; k < ncols; k += 32) {
-      const int c = cols ? cols[k] : k;
-      const float cost = pair_cost(drow[c], mr, l.mass[c], rr, l.radius[c], l.limit, c != r);
-      best = min(best, pack_key(cost, (long long)(r ^ c)));
+    for (int kb = lane; kb < ncols; kb += 32 * kBatch) {
+      int cv[kBatch];
+      float dv[kBatch], mv[kBatch], rv[kBatch];
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int k = kb + 32 * j;
+        cv[j] = k < ncols ? (cols ? cols[k] : k) : -1;
+        const int c = cv[j] < 0 ? r : cv[j];
+        dv[j] = drow[c];
+        mv[j] = l.mass[c];
+        rv[j] = l.radius[c];
+      }
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        if (cv[j] < 0) continue;
+        const float cost = pair_cost(dv[j], mr, mv[j], rr, rv[j], l.limit, cv[j] != r);
+        best = min(best, pack_key(cost, (long long)(r ^ cv[j])));
+      }
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, off));
@@ -246,6 +265,7 @@ __device__ void select_pairs(const logkv_unified_t& u, const Lane& l, int lane, 
       const float* xa = l.mu + (size_t)r * D;
       const float* xb = l.mu + (size_t)o * D;
       float exact2 = 0.f;
+#pragma unroll 8
       for (int d = 0; d < D; ++d) {
         const float df = fsub(xa[d], xb[d]);
         exact2 = fadd(exact2, fmul(df, df));
@@ -418,29 +438,46 @@ __global__ void __launch_bounds__(kThreads) round_kernel(logkv_unified_t u, int 
   }
   __syncthreads();
   const int ncols = ncols_s;
-  // ---- Lance-Williams: this CTA's share [k0, k0 + CW) of the live columns, every merged row.
-  // Items run column fastest in whole warps, so a warp's 32 items share their merge (one
-  // row-minimum atomic); a merge's scalars were computed once by the leader.
+  // ---- Lance-Williams: this CTA's share [k0, k0 + CW) of the live columns, every merged row,
+  // as warp tasks of (merge, 32 columns); a merge's scalars were computed once by the leader.
   const int CW = column_width(ncols), k0 = part * CW;
   for (int i = tid; i < n_ok; i += nt) sm.rowmin[i] = kInfKey;
   for (int i = tid; i < CW; i += nt) sm.colmin[i] = 0x7FFFFFFFFFFFFFFFLL;
   __syncthreads();
-  const int lanew = tid & 31;
-  for (size_t item = tid; k0 < ncols && item < (size_t)n_ok * CW; item += nt) {
-    const int m = (int)(item / CW), kl = (int)(item % CW), k = k0 + kl;
+  constexpr int kChunks = 4;   // 32-column chunks per warp task, their loads in flight together
+  const int lanew = tid & 31, nchunk = CW / 32, ngrp = (nchunk + kChunks - 1) / kChunks;
+  const int ntask = k0 < ncols ? n_ok * ngrp : 0;
+  for (int task = tid >> 5; task < ntask; task += nt >> 5) {
+    const int m = task / ngrp, g0 = (task - m * ngrp) * kChunks;
+    const int a = sm.pairs[m], b = sm.best[a];
+    const float alpha = sm.alpha[a], beta = sm.beta[a], shift = sm.shift[a];
+    const float total = fadd(sm.pma[a], sm.pmb[a]), ra = l.radius[a];
+    const float* rowa = l.dist + (size_t)a * M;
+    const float* rowb = l.dist + (size_t)b * M;
+    int cv[kChunks];
+    float xaa[kChunks], xba[kChunks], mc[kChunks], rc[kChunks];
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) {
+      const int k = k0 + (g0 + j) * 32 + lanew;
+      cv[j] = (g0 + j < nchunk && k < ncols) ? sm.cols[k] : -1;
+      const int c = cv[j] < 0 ? a : cv[j];
+      xaa[j] = rowa[c];
+      xba[j] = rowb[c];
+      mc[j] = l.mass[c];
+      rc[j] = l.radius[c];
+    }
     long long rkey = kInfKey;
-    if (k < ncols) {
-      const int c = sm.cols[k];
-      const int a = sm.pairs[m], b = sm.best[a];
-      const float alpha = sm.alpha[a], beta = sm.beta[a], shift = sm.shift[a];
-      const float total = fadd(sm.pma[a], sm.pmb[a]);
-      const float x_aa = l.dist[(size_t)a * M + c], x_ba = l.dist[(size_t)b * M + c];
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) {
+      const int c = cv[j];
+      if (c < 0) continue;
+      const float x_aa = xaa[j], x_ba = xba[j];
       float nv = fsub(fadd(fmul(alpha, x_aa), fmul(beta, x_ba)), shift);
       const bool keep_c = sm.flags[c] & 4;
       if (keep_c) {
         // Both clusters merged this round: the lower keep index's order, so both owners agree.
         const int q = sm.partner[c];
-        const float x_ab = l.dist[(size_t)a * M + q], x_bb = l.dist[(size_t)b * M + q];
+        const float x_ab = rowa[q], x_bb = rowb[q];
         const float qal = sm.alpha[c], qbe = sm.beta[c], qsh = sm.shift[c];
         float v;
         if (a < c) {
@@ -457,12 +494,12 @@ __global__ void __launch_bounds__(kThreads) round_kernel(logkv_unified_t u, int 
       if (c == a) nv = 0.f;
       if (!keep_c) l.dist[(size_t)c * M + a] = nv;
       l.dist[(size_t)a * M + c] = nv;
-      const float cost = pair_cost(nv, total, l.mass[c], l.radius[a], l.radius[c], l.limit, c != a);
+      const float cost = pair_cost(nv, total, mc[j], ra, rc[j], l.limit, c != a);
       const long long key = pack_key(cost, (long long)(a ^ c));
-      if (cost < __int_as_float(0x7F800000) && !keep_c) atomicMin(&sm.colmin[kl], key);
-      rkey = key;
+      if (cost < __int_as_float(0x7F800000) && !keep_c) atomicMin(&sm.colmin[(g0 + j) * 32 + lanew], key);
+      rkey = min(rkey, key);
     }
-    // CW is a multiple of 32 and the loop stride is a multiple of 32: the warp shares m.
+    // A warp task covers columns of one merge only: one row-minimum atomic per task.
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) rkey = min(rkey, __shfl_xor_sync(0xffffffffu, rkey, off));
     if (lanew == 0) atomicMin(&sm.rowmin[m], rkey);
