@@ -76,7 +76,7 @@ static void launch_cascade(const Geo& g, const logkv_state_t& s, const Work& w, 
 
 // Span scores: the block's warps stride over the (candidate, group) pairs of batch row
 // blockIdx.y, one pair per warp at a time.
-template <typename T>
+template <typename T, int DC>
 __global__ void __launch_bounds__(256) score_kernel(Geo g, logkv_state_t s, Work w) {
   pdl_entry();
   extern __shared__ float sm[];
@@ -85,9 +85,17 @@ __global__ void __launch_bounds__(256) score_kernel(Geo g, logkv_state_t s, Work
   float* ws = sm + warp * score_warp_floats(g.D, g.K, (int)sizeof(T));
   const int npairs = w.n_cand[b] * g.G;
   for (int p = blockIdx.x * nwarps + warp; p < npairs; p += gridDim.x * nwarps) {
-    score_pair<T>(g, s, w, b, p / g.G, p % g.G, lane, ws);
+    score_pair<T, DC>(g, s, w, b, p / g.G, p % g.G, lane, ws);
     __syncwarp();
   }
+}
+
+template <typename T, int DC>
+static void launch_score(const Geo& g, const logkv_state_t& s, const Work& w, size_t smem, int blocks,
+                         cudaStream_t st) {
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(score_kernel<T, DC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  launch_pdl(score_kernel<T, DC>, dim3(blocks, g.B), 256, smem, st, g, s, w);
 }
 
 // Attach decisions run beside the span scores.  They read the snapshot (complete before any
@@ -373,10 +381,10 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   launch_pdl(alpha_cut_kernel, g.B, 1024, cut_smem, st, g, s, w);
   mark();
   const size_t score_smem = score_smem_bytes(g, sizeof(T));
-  if (score_smem > 48 * 1024)
-    cudaFuncSetAttribute(score_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)score_smem);
   const int score_blocks = std::max(1, std::min((g.NC * g.G + 7) / 8, 2 * sm_count / g.B + 1));
-  launch_pdl(score_kernel<T>, dim3(score_blocks, g.B), 256, score_smem, st, g, s, w);
+  if (g.D == 128) launch_score<T, 128>(g, s, w, score_smem, score_blocks, st);
+  else if (g.D == 64) launch_score<T, 64>(g, s, w, score_smem, score_blocks, st);
+  else launch_score<T, 0>(g, s, w, score_smem, score_blocks, st);
   const size_t attach_smem = attach_smem_bytes(g);
   const int attach_x = (g.NW + kAttachTokens - 1) / kAttachTokens;
   if (g.D == 128) launch_attach<T, 128>(g, s, w, attach_smem, attach_x, st);

@@ -243,10 +243,26 @@ __host__ __device__ inline int score_warp_floats(int D, int K, int esize) {
   return (2 * score_rows(D, esize) * D * esize / 4 + 2 * D + 64 + K + 3) & ~3;
 }
 
-template <typename T>
+// Four consecutive staged elements (8 or 16 bytes, aligned) as floats, in order.
+__device__ __forceinline__ void load4(const float* p, float* out) {
+  const float4 v = *reinterpret_cast<const float4*>(p);
+  out[0] = v.x;
+  out[1] = v.y;
+  out[2] = v.z;
+  out[3] = v.w;
+}
+__device__ __forceinline__ void load4(const __nv_bfloat16* p, float* out) {
+  const uint2 v = *reinterpret_cast<const uint2*>(p);
+  out[0] = __uint_as_float(v.x << 16);
+  out[1] = __uint_as_float(v.x & 0xFFFF0000u);
+  out[2] = __uint_as_float(v.y << 16);
+  out[3] = __uint_as_float(v.y & 0xFFFF0000u);
+}
+
+template <typename T, int DC>
 __device__ void score_pair(const Geo& g, const logkv_state_t& s, const Work& w, int b, int ci, int grp, int lane,
                            float* ws) {
-  const int D = g.D, K = g.K, G = g.G;
+  const int D = DC ? DC : g.D, K = g.K, G = g.G;
   constexpr int VN = Vec<T>::N;
   const int DV = D / VN;                                    // 16-byte chunks per row
   const int swz = (DV & (DV - 1)) == 0 ? min(DV, 16) - 1 : 0;  // chunk swizzle mask
@@ -264,9 +280,6 @@ __device__ void score_pair(const Geo& g, const logkv_state_t& s, const Work& w, 
   const T* reck = static_cast<const T*>(s.recent_k_raw);
   const T* recv = static_cast<const T*>(s.recent_v);
   // Element (t, d) of staged component f: chunk d / VN of row t sits at chunk (d / VN) ^ (t & swz).
-  auto staged = [&](int f, int t, int d) -> const T* {
-    return rows + ((size_t)f * CR + t) * D + (((d / VN) ^ (t & swz)) * VN) + d % VN;
-  };
   float eacc[2] = {0.f, 0.f};
   for (int t0 = 0; t0 < n; t0 += CR) {
     const int cn = min(CR, n - t0);
@@ -288,13 +301,17 @@ __device__ void score_pair(const Geo& g, const logkv_state_t& s, const Work& w, 
         if (d >= D) continue;
         float* ms = mean_s + f * D + d;
         float a0 = t0 ? ms[0] : 0.f, a1 = t0 ? ms[1] : 0.f, a2 = t0 ? ms[2] : 0.f, a3 = t0 ? ms[3] : 0.f;
+        // 4 consecutive features never straddle a chunk: one 8- or 16-byte load per token.
+        const T* fbase = rows + (size_t)f * CR * D + d % VN;
+        const int dc = d / VN;
 #pragma unroll 8
         for (int t = 0; t < cn; ++t) {
-          const T* p = staged(f, t, d);  // 4 consecutive features never straddle a chunk
-          a0 = fadd(a0, Elem<T>::load(p));
-          a1 = fadd(a1, Elem<T>::load(p + 1));
-          a2 = fadd(a2, Elem<T>::load(p + 2));
-          a3 = fadd(a3, Elem<T>::load(p + 3));
+          float x4[4];
+          load4(fbase + t * D + ((dc ^ (t & swz)) * VN), x4);
+          a0 = fadd(a0, x4[0]);
+          a1 = fadd(a1, x4[1]);
+          a2 = fadd(a2, x4[2]);
+          a3 = fadd(a3, x4[3]);
         }
         ms[0] = a0;
         ms[1] = a1;

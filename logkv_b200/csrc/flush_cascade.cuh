@@ -206,6 +206,7 @@ __global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logk
   __shared__ float bener[kTileGroups][2];
   __shared__ int bcut[kTileGroups];
   __shared__ int sh_exact;  // groups of the current tile needing the canonical cost order
+  __shared__ const T* rowp[2][kTileRows];  // source rows (K, V) of the tile being issued
   if (threadIdx.x == 0) sh_exact = 0;
   T* LK = static_cast<T*>(s.level_k);
   T* LV = static_cast<T*>(s.level_v);
@@ -336,16 +337,23 @@ __global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logk
     // Issue the asynchronous K/V copies of the tile starting at pool row t0 into buffer `buf`;
     // the calling thread's metadata row (if any) is returned through `pend`.
     Meta pend{};
+    // Every row's source pointers are resolved once (one thread per row) and shared, so a
+    // 16-byte copy costs an offset, not the pool / token / scratch address arithmetic.
     auto issue = [&](int t0, int buf) {
       const int tn = min(kTileRows, total - t0);
       T* tk = tkb + (size_t)buf * kTileRows * D;
       T* tv = tvb + (size_t)buf * kTileRows * D;
+      if (tid < tn) {
+        rowp[0][tid] = pool_k(t0 + tid);
+        rowp[1][tid] = pool_v(t0 + tid);
+        pend = pool_m(t0 + tid);
+      }
+      __syncthreads();
       for (int item = tid; item < tn * DV * 2; item += nt) {
         const int r = item / (2 * DV), f = (item / DV) & 1, v = item % DV;
-        cp_async16((f ? tv : tk) + r * D + v * VN, (f ? pool_v(t0 + r) : pool_k(t0 + r)) + v * VN);
+        cp_async16((f ? tv : tk) + r * D + v * VN, rowp[f][r] + v * VN);
       }
       cp_async_commit();
-      if (tid < tn) pend = pool_m(t0 + tid);
     };
     issue(0, 0);
     int cur = 0;
