@@ -98,6 +98,21 @@ static void launch_score(const Geo& g, const logkv_state_t& s, const Work& w, si
   launch_pdl(score_kernel<T, DC>, dim3(blocks, g.B), 256, smem, st, g, s, w);
 }
 
+template <typename T, int DC>
+static void launch_prepare_d(const Geo& g, const logkv_state_t& s, const Work& w, size_t smem, cudaStream_t st) {
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(prepare_kernel<T, DC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  launch_pdl(prepare_kernel<T, DC>, dim3(g.K, g.G, g.B), 256, smem, st, g, s, w);
+}
+
+template <typename T>
+static void launch_prepare(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st) {
+  const size_t smem = prep_smem_bytes(g, sizeof(T));
+  if (g.D == 128) launch_prepare_d<T, 128>(g, s, w, smem, st);
+  else if (g.D == 64) launch_prepare_d<T, 64>(g, s, w, smem, st);
+  else launch_prepare_d<T, 0>(g, s, w, smem, st);
+}
+
 // Attach decisions run beside the span scores.  They read the snapshot (complete before any
 // score block passed its entry wait, which is what let this grid launch) and the frozen
 // cluster state, so the entry wait is skipped.  Block (0, 0, 0) waits at its end instead:
@@ -414,10 +429,7 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   }
   if (!(phases & kPhaseApply)) return (int)cudaGetLastError();
   mark();
-  const size_t prep_smem = prep_smem_bytes(g, sizeof(T));
-  if (prep_smem > 48 * 1024)
-    cudaFuncSetAttribute(prepare_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
-  launch_pdl(prepare_kernel<T>, dim3(g.K, g.G, g.B), 256, prep_smem, st, g, s, w);
+  launch_prepare<T>(g, s, w, st);
   mark();
   const size_t casc_smem = cascade_smem(g, sizeof(T));
   if (g.beta) {
@@ -454,10 +466,7 @@ static int launch_replay(const Geo& g, const logkv_state_t& s, const Work& w, co
   launch_pdl(snapshot_kernel<T>, dim3(per_bg, g.G, g.B), 256, 0, st, g, s, w);
   launch_pdl(tape_payload_kernel<T>, dim3(per_pay, g.G, g.B), 256, 0, st, g, s, tape, 0);
   launch_pdl(tape_copy_kernel, dim3(2 * sm_count), 256, 0, st, tape_segments(g, s, w, tape, false));
-  const size_t prep_smem = prep_smem_bytes(g, sizeof(T));
-  if (prep_smem > 48 * 1024)
-    cudaFuncSetAttribute(prepare_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prep_smem);
-  launch_pdl(prepare_kernel<T>, dim3(g.K, g.G, g.B), 256, prep_smem, st, g, s, w);
+  launch_prepare<T>(g, s, w, st);
   const size_t casc_smem = cascade_smem(g, sizeof(T));
   if (g.beta) {
     if (g.D == 128) launch_cascade<T, true, 128>(g, s, w, casc_smem, st);

@@ -137,13 +137,13 @@ __device__ LaneCtx<T> make_ctx(const Geo& g, const logkv_state_t& s, const Work&
 constexpr int kPrepRows = 64;  // token rows staged per pass of the centroid sum
 constexpr int kPrepFeat = 4;   // features per thread of the centroid sum (D <= 1024, 256 threads)
 
-template <typename T>
+template <typename T, int DC>
 __global__ void __launch_bounds__(256) prepare_kernel(Geo g, logkv_state_t s, Work w) {
   pdl_entry();
   LaneCtx<T> x = make_ctx<T>(g, s, w);
   const int type = w.plan_type[x.lane];
   if (type == kJobNone) return;
-  const int tid = threadIdx.x, nt = blockDim.x, D = g.D;
+  const int tid = threadIdx.x, nt = blockDim.x, D = DC ? DC : g.D;
   const int n = w.plan_n[x.lane];
   const float pre = s.n_eff[x.lane];
   float* mu = s.centroid + x.lane * D;
@@ -161,12 +161,14 @@ __global__ void __launch_bounds__(256) prepare_kernel(Geo g, logkv_state_t s, Wo
   float sums[kPrepFeat];  // features tid, tid + nt, ... (D <= kPrepFeat * blockDim.x)
 #pragma unroll
   for (int j = 0; j < kPrepFeat; ++j) sums[j] = 0.f;
+  __shared__ const T* rowp[kPrepRows];  // source rows of the pass, resolved once per row
   for (int c0 = i0; c0 < n; c0 += kPrepRows) {
     const int cn = min(kPrepRows, n - c0);
+    if (tid < cn) rowp[tid] = token_row<T>(g, x.snapk, x.reck, x.b, x.grp, srcs[c0 + tid]);
+    __syncthreads();
     for (int item = tid; item < cn * DV; item += nt) {
       const int t = item / DV, v = item % DV;
-      *reinterpret_cast<uint4*>(trows + t * D + v * VN) =
-          *reinterpret_cast<const uint4*>(token_row<T>(g, x.snapk, x.reck, x.b, x.grp, srcs[c0 + t]) + v * VN);
+      *reinterpret_cast<uint4*>(trows + t * D + v * VN) = *reinterpret_cast<const uint4*>(rowp[t] + v * VN);
     }
     __syncthreads();
 #pragma unroll
