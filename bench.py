@@ -46,6 +46,7 @@ WORKLOAD = dict(workload="qwen3-0.6b streaming prefill flush (28 layers, 32K tok
                 layers=28, groups=8, head_dim=128, clusters=12, B=128, recent=2048, granularity=2048,
                 exact=256, span_cap=64, beta=True, tokens=32768, chunk=2048, batch_per_rank=1, dtype="bf16")
 ROW_BYTES = 256 + 256 + 4 + 4 * 8 + 1   # one bf16 ladder entry (13 fields, first-order subset)
+CASCADE_TRAFFIC = 30_712_320            # dram read + write bytes of one cascade launch (ncu capture)
 METRIC = "flush us per 2048-tok chunk/layer"
 
 
@@ -349,7 +350,8 @@ def bench_ours(args, rank, world, local_rank):
                 counters=delta, flushes_per_step=flushes_per_step,
                 roofline={"bound": "hbm", "kernel": "cascade_kernel", "achieved": round(achieved, 1),
                           "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                          "traffic": None, "bytes_per_launch": round(casc_bytes_per_launch)},
+                          "traffic": CASCADE_TRAFFIC, "traffic_source": "profiles/cascade_kernel_qwen3-0.6b.md (ncu, same layer shape)",
+                          "bytes_per_launch": round(casc_bytes_per_launch)},
                 flush_roofline={"achieved": round(flush_achieved, 1), "unit": "GB/s",
                                 "frac": round(flush_achieved / peak, 4), "bytes_per_flush": round(flush_bytes)},
                 clocks=clocks.summary(), launches=n_launch, inputs=(caches, layers, ends_host, ends_dev))
