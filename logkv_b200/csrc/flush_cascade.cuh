@@ -206,7 +206,7 @@ __global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logk
   __shared__ float bener[kTileGroups][2];
   __shared__ int bcut[kTileGroups];
   __shared__ int sh_exact;  // groups of the current tile needing the canonical cost order
-  __shared__ const T* rowp[2][kTileRows];  // source rows (K, V) of the tile being issued
+  __shared__ const T* rowp[2][2][kTileRows];  // [tile buffer][K, V][row] source rows of staged tiles
   if (threadIdx.x == 0) sh_exact = 0;
   T* LK = static_cast<T*>(s.level_k);
   T* LV = static_cast<T*>(s.level_v);
@@ -337,24 +337,30 @@ __global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logk
     // Issue the asynchronous K/V copies of the tile starting at pool row t0 into buffer `buf`;
     // the calling thread's metadata row (if any) is returned through `pend`.
     Meta pend{};
-    // Every row's source pointers are resolved once (one thread per row) and shared, so a
-    // 16-byte copy costs an offset, not the pool / token / scratch address arithmetic.
+    // Every row's source pointers are resolved once (one thread per row) into rowp[buf] before
+    // a barrier that precedes the tile's issue, so a 16-byte copy costs an offset, not the
+    // pool / token / scratch address arithmetic.  Tile t0 uses buffer (t0 / kTileRows) & 1.
+    auto resolve = [&](int t0, int buf) {
+      const int tn = min(kTileRows, total - t0);
+      if (tid < tn) {
+        rowp[buf][0][tid] = pool_k(t0 + tid);
+        rowp[buf][1][tid] = pool_v(t0 + tid);
+      }
+    };
     auto issue = [&](int t0, int buf) {
       const int tn = min(kTileRows, total - t0);
       T* tk = tkb + (size_t)buf * kTileRows * D;
       T* tv = tvb + (size_t)buf * kTileRows * D;
-      if (tid < tn) {
-        rowp[0][tid] = pool_k(t0 + tid);
-        rowp[1][tid] = pool_v(t0 + tid);
-        pend = pool_m(t0 + tid);
-      }
-      __syncthreads();
       for (int item = tid; item < tn * DV * 2; item += nt) {
         const int r = item / (2 * DV), f = (item / DV) & 1, v = item % DV;
-        cp_async16((f ? tv : tk) + r * D + v * VN, rowp[f][r] + v * VN);
+        cp_async16((f ? tv : tk) + r * D + v * VN, rowp[buf][f][r] + v * VN);
       }
       cp_async_commit();
+      if (tid < tn) pend = pool_m(t0 + tid);
     };
+    resolve(0, 0);
+    if (kTileRows < total) resolve(kTileRows, 1);
+    __syncthreads();
     issue(0, 0);
     int cur = 0;
     for (int t0 = 0; t0 < total; t0 += kTileRows) {
@@ -366,6 +372,9 @@ __global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logk
       if (tid < tn) tm[tid] = pend;
       __syncthreads();
       if (t0 + kTileRows < total) issue(t0 + kTileRows, cur ^ 1);
+      // Buffer `cur` was last read by this tile's issue, before the barrier above; the next
+      // reader (tile t0 + 2 tiles) issues after the next iteration's barrier.
+      if (t0 + 2 * kTileRows < total) resolve(t0 + 2 * kTileRows, cur);
       const int mend = min(t0 + tn, npair);  // merge rows of this tile: [t0, mend)
       if (mend > t0) {
         if (!BETA) {
