@@ -359,6 +359,9 @@ struct AttnGeo {
 
 constexpr int kAttnWarps = 4;
 constexpr int kAttnStages = 3;
+// The tensor-core decode kernel keeps two tiles per warp in flight and fits three CTAs (12 warps)
+// per SM, so more warps overlap one tile's math with the next tiles' loads.
+constexpr int kMmaStages = 2;
 
 template <typename T, int D, int NQ>
 struct AttnShape {
@@ -658,7 +661,7 @@ struct MmaShape {
   static constexpr int KS = D / 16;         // k16 steps of QK^T
   static constexpr int DT = D / 8;          // n8 output tiles of PV
   static constexpr int STAGE_BYTES = 2 * TS * D * 2 + TS * 4;   // K, V (bf16) and the mass column
-  static constexpr size_t smem = (size_t)kAttnWarps * kAttnStages * STAGE_BYTES;
+  static constexpr size_t smem = (size_t)kAttnWarps * kMmaStages * STAGE_BYTES;
   static_assert(D % 16 == 0 && D >= 16 && D <= 256, "head dim must be a multiple of 16 up to 256");
   // Physical 16-byte chunk of logical chunk c in row r: rows of 8 consecutive ldmatrix
   // addresses land in 8 distinct 16-byte bank groups.
@@ -669,7 +672,7 @@ struct MmaShape {
 };
 
 template <int D, int NQ>
-__global__ void __launch_bounds__(kAttnWarps * 32) slot_attn_mma_kernel(AttnGeo a, logkv_prefix_t pre,
+__global__ void __launch_bounds__(kAttnWarps * 32, 3) slot_attn_mma_kernel(AttnGeo a, logkv_prefix_t pre,
                                                                        const __nv_bfloat16* rk,
                                                                        const __nv_bfloat16* rv,
                                                                        const __nv_bfloat16* kn,
@@ -686,7 +689,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) slot_attn_mma_kernel(AttnGeo 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int g8 = lane >> 2, t4 = lane & 3;  // fragment row group and column pair
   const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z, ln = b * a.G + g;
-  unsigned char* wbase = reinterpret_cast<unsigned char*>(smem4) + (size_t)warp * kAttnStages * S::STAGE_BYTES;
+  unsigned char* wbase = reinterpret_cast<unsigned char*>(smem4) + (size_t)warp * kMmaStages * S::STAGE_BYTES;
   const unsigned wbase_s = (unsigned)__cvta_generic_to_shared(wbase);
   const __nv_bfloat16* PK = static_cast<const __nv_bfloat16*>(pre.k);
   const __nv_bfloat16* PV = static_cast<const __nv_bfloat16*>(pre.v);
@@ -789,12 +792,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32) slot_attn_mma_kernel(AttnGeo 
   const int rq0 = g8 % a.TQ, rq1 = (g8 + 8) % a.TQ;         // query token of each row
 
 #pragma unroll
-  for (int k = 0; k < kAttnStages - 1; ++k) issue(k, k);
+  for (int k = 0; k < kMmaStages - 1; ++k) issue(k, k);
   for (int k = 0; k < mine; ++k) {
-    issue(k + kAttnStages - 1, (k + kAttnStages - 1) % kAttnStages);
-    cp_async_wait<kAttnStages - 1>();
+    issue(k + kMmaStages - 1, (k + kMmaStages - 1) % kMmaStages);
+    cp_async_wait<kMmaStages - 1>();
     __syncwarp();
-    const int stage = k % kAttnStages;
+    const int stage = k % kMmaStages;
     const __nv_bfloat16 *kb_, *vb_;
     const float* mb_;
     int rows, cls, first;
@@ -920,7 +923,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) slot_attn_mma_kernel(AttnGeo 
         const float f = exp2f(wm_[w][r] - mx);
         l += wl_[w][r] * f;
         ov += reinterpret_cast<const float*>(reinterpret_cast<unsigned char*>(smem4) +
-                                             (size_t)w * kAttnStages * S::STAGE_BYTES)[r * D + d] * f;
+                                             (size_t)w * kMmaStages * S::STAGE_BYTES)[r * D + d] * f;
       }
     }
     if (a.nsplit == 1) {
