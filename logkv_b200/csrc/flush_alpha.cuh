@@ -234,7 +234,9 @@ __global__ void __launch_bounds__(1024) alpha_cut_kernel(Geo g, logkv_state_t s,
 // own centres).  Every sum runs left to right, as the reference's CPU path.  Output per
 // (row, candidate, group): Alpha parts (R_K, R_V) or Beta's per-group score.
 __host__ __device__ inline int score_rows(int D, int esize) {
-  const int r = 8192 / (D * esize);
+  // 24 rows of D = 128 bf16 per pass (a typical span in one pass) keep a block's staging
+  // near 107 KB, so two 8-warp blocks share an SM.
+  const int r = 6144 / (D * esize);
   return r < 1 ? 1 : (r > 32 ? 32 : r);
 }
 // Per-warp shared memory in floats: rows [2][rows][D] (storage dtype), means [2][D], token
