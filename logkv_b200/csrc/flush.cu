@@ -183,8 +183,10 @@ __global__ void window_shift_kernel(Geo g, logkv_state_t s, Work w, int rem, int
   const size_t F = (size_t)g.F * g.D / VN, R = (size_t)rem * g.D / VN;
   const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
   // Without staging (rem <= F) unit j of [F, count) is read and then zeroed by
-  // the same thread; [rem, F) is never read.  With staging every source is a copy.
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+  // the same thread; [rem, F) is never read, and units below rem are only written by the
+  // threads of their sources, so the loop starts at rem.  With staging every source is a copy.
+  const size_t i0 = staged ? 0 : R;
+  for (size_t i = i0 + blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     if (staged) {
       if (i < R) {
         rk[base + i] = sk[base + i];
