@@ -361,8 +361,11 @@ def bench_flush_attend(args, rank, world, local_rank, inputs):
     """Flush-and-attend prefill in model order: per layer-chunk the chunk attention of the layer's
     16 query heads over its cache, then ``add_recent`` of the chunk (a 2048-token flush); chunks
     in sequence, the 28 layers in sequence within a chunk, on one stream, one CUDA graph per step.
-    Timed twice: with the route decisions on the caller's stream, and with route overlap (the
-    decisions of each flush on a side stream, ordered only after the layer's previous flush).
+    Timed three ways: with the route decisions on the caller's stream; with route overlap (the
+    decisions of each flush on a side stream, ordered only after the layer's previous flush); and
+    with route overlap and each layer's ``add_recent`` on that layer's own stream, ordered after
+    the layer's attention, with the layer's next attention ordered after it (a layer's flush only
+    has to finish before that layer's next chunk, so it runs beside the next layers' attention).
     """
     import torch
     import torch.distributed as dist
@@ -375,28 +378,44 @@ def bench_flush_attend(args, rank, world, local_rank, inputs):
     out = torch.empty_like(q)
     scale = D ** -0.5
     stream = torch.cuda.Stream(device)
+    lstreams = [torch.cuda.Stream(device) for _ in caches]
     n_chunks = len(layers[0])
 
-    def step():
+    def step(layer_streams):
+        main = torch.cuda.current_stream()
+        if layer_streams:
+            for st in lstreams:
+                st.wait_stream(main)                      # fork (joins a capture too)
         for cache in caches:
             cache.reset_parameters()
         for c in range(n_chunks):
-            for cache, chunks in zip(caches, layers):
+            for li, (cache, chunks) in enumerate(zip(caches, layers)):
                 k, kr, v = chunks[c]
+                if layer_streams:
+                    main.wait_stream(lstreams[li])        # the layer's previous flush
                 log_kv_chunk_attention(cache, q, k, v, scale, 0.0, out=out)
-                cache.add_recent(k, v, k_raw=kr, span_ends=ends_host, span_ends_device=ends_dev)
+                if layer_streams:
+                    lstreams[li].wait_stream(main)        # after this attention
+                    with torch.cuda.stream(lstreams[li]):
+                        cache.add_recent(k, v, k_raw=kr, span_ends=ends_host, span_ends_device=ends_dev)
+                else:
+                    cache.add_recent(k, v, k_raw=kr, span_ends=ends_host, span_ends_device=ends_dev)
+        if layer_streams:
+            for st in lstreams:
+                main.wait_stream(st)
 
     us = {}
-    for overlap in (False, True):
+    for mode in ("plain", "overlap", "layer_streams"):
+        overlap, layered = mode != "plain", mode == "layer_streams"
         for cache in caches:
             cache._route_overlap = overlap
         with torch.no_grad(), torch.cuda.stream(stream):
             for _ in range(max(1, args.warmup)):
-                step()
+                step(layered)
             torch.cuda.synchronize()
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=stream):
-                step()
+                step(layered)
             graph.replay()
             torch.cuda.synchronize()
             if world > 1:
@@ -411,11 +430,12 @@ def bench_flush_attend(args, rank, world, local_rank, inputs):
         t = torch.tensor([e0.elapsed_time(e1)], device=device)
         if world > 1:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        us["overlap" if overlap else "plain"] = round(t.item() * 1000.0 / (args.steps * n_chunks * len(caches)), 2)
+        us[mode] = round(t.item() * 1000.0 / (args.steps * n_chunks * len(caches)), 2)
     for cache in caches:
         cache._route_overlap = False
     return {"metric": "flush-and-attend prefill us per 2048-token chunk/layer (chunk attention + add_recent)",
-            "unit": "us", "value": us["overlap"], "value_without_route_overlap": us["plain"],
+            "unit": "us", "value": us["layer_streams"], "value_route_overlap_one_stream": us["overlap"],
+            "value_one_stream": us["plain"],
             "config": {"layers": len(caches), "chunks": n_chunks, "heads": H, "groups": WORKLOAD["groups"],
                        "head_dim": D, "chunk": T, "flushes_per_step": len(caches) * (n_chunks - 1)}}
 
