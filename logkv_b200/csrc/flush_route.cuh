@@ -403,28 +403,50 @@ __global__ void __launch_bounds__(1024) plan_kernel(Geo g, logkv_state_t s, Work
   const int8_t* asg = w.assign + row0;
   const int* arch = w.arch_idx + (size_t)b * g.NW;
   __shared__ int wsum[32];
-  // Stable counting sort of archive ranks by cluster.
+  // Stable counting sort of archive ranks by cluster, in one pass: per 32-rank chunk and cluster
+  // a ballot count, one block scan of those counts in (cluster, chunk) order, then each rank goes
+  // to its (cluster, chunk) offset plus its lane rank among the chunk's ranks of that cluster.
+  // NW <= 8192 ranks make at most 256 chunks; K <= kMaxClusters.
   __shared__ int cl_count[kMaxClusters], cl_off[kMaxClusters];
-  __shared__ int tot;
-  int running = 0;
-  for (int c = 0; c < K; ++c) {
-    int carry = 0;
-    for (int base = 0; base < na; base += nt) {
-      const int t = base + tid;
-      const int f = (t < na && asg[t] == c) ? 1 : 0;
-      const int incl = block_inclusive_scan(f, wsum);
-      if (f) w.tok_list[row0 + running + carry + incl - 1] = t;
-      if (tid == nt - 1) tot = incl;
-      __syncthreads();
-      carry += tot;
-      __syncthreads();
+  __shared__ int cnt[(8192 / 32) * kMaxClusters];  // [chunk][cluster] counts, then offsets
+  const int lane = tid & 31, warp = tid >> 5, nwarps = nt >> 5;
+  const int nchunk = (na + 31) / 32;
+  for (int ch = warp; ch < nchunk; ch += nwarps) {
+    const int t = ch * 32 + lane;
+    const int a = t < na ? asg[t] : -1;
+    int mine = 0;
+    for (int c = 0; c < K; ++c) {
+      const int m = __popc(__ballot_sync(0xffffffffu, a == c));
+      if (lane == c) mine = m;
     }
-    if (tid == 0) {
-      cl_count[c] = carry;
-      cl_off[c] = running;
-    }
-    running += carry;
+    if (lane < K) cnt[ch * K + lane] = mine;
   }
+  __syncthreads();
+  {
+    // Exclusive scan of cnt in (cluster, chunk) order: thread tid owns q consecutive entries.
+    const int n2 = K * nchunk, q = (n2 + nt - 1) / nt;
+    const int j0 = min(n2, tid * q), j1 = min(n2, j0 + q);
+    int local = 0;
+    for (int j = j0; j < j1; ++j) local += cnt[(j % nchunk) * K + j / nchunk];
+    const int incl = block_inclusive_scan(local, wsum);
+    int run = incl - local;
+    for (int j = j0; j < j1; ++j) {
+      const int at = (j % nchunk) * K + j / nchunk;
+      const int v = cnt[at];
+      cnt[at] = run;
+      run += v;
+    }
+  }
+  __syncthreads();
+  for (int ch = warp; ch < nchunk; ch += nwarps) {
+    const int t = ch * 32 + lane;
+    const int a = t < na ? asg[t] : -1;
+    const unsigned same = __match_any_sync(0xffffffffu, a);
+    if (t < na && a >= 0 && a < K) w.tok_list[row0 + cnt[ch * K + a] + __popc(same & ((1u << lane) - 1u))] = t;
+  }
+  if (tid < K) cl_off[tid] = nchunk ? cnt[tid] : 0;   // chunk 0's offset of cluster tid
+  __syncthreads();
+  if (tid < K) cl_count[tid] = (tid + 1 < K ? cl_off[tid + 1] : na) - cl_off[tid];
   __syncthreads();
   if (tid == 0) {
     int scr = 0;
