@@ -212,6 +212,13 @@ LOGKV_API int logkv_flush_replay(const logkv_layout_t* layout, const logkv_state
                                  int32_t recent_count, void* workspace, size_t workspace_bytes, const void* tape,
                                  size_t tape_bytes, void* stream);
 
+/*
+ * Host-side helper for route overlap under CUDA-graph capture (no reference counterpart): *id = the
+ * id of the capture `stream` takes part in, or 0 when it is not capturing.  A flush's decisions fork
+ * to a side stream only after an event recorded in the same capture (or outside any capture).
+ */
+LOGKV_API int logkv_stream_capture_id(void* stream, unsigned long long* id);
+
 /* Copy the workspace status word to *out (synchronizes `stream`); nonzero = a capacity was exceeded. */
 LOGKV_API int logkv_read_status(const void* workspace, int32_t* out, void* stream);
 

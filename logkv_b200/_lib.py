@@ -83,6 +83,8 @@ def lib() -> ctypes.CDLL:
         handle.logkv_flush.restype = ctypes.c_int
         handle.logkv_flush.argtypes = [ctypes.POINTER(Layout), ctypes.POINTER(State), ctypes.c_int32,
                                        ctypes.c_int32, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+        handle.logkv_stream_capture_id.restype = ctypes.c_int
+        handle.logkv_stream_capture_id.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_ulonglong)]
         handle.logkv_read_status.restype = ctypes.c_int
         handle.logkv_read_status.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32), ctypes.c_void_p]
         handle.logkv_flush_profiled.restype = ctypes.c_int
@@ -136,6 +138,14 @@ def check(code: int, what: str) -> None:
     if code != 0:
         reason = ERRORS.get(code, f"CUDA error {code}")
         raise RuntimeError(f"{what} failed: {reason}")
+
+
+def capture_id(device: torch.device) -> int:
+    """Id of the CUDA-graph capture the current stream of `device` takes part in, 0 if none."""
+    out = ctypes.c_ulonglong(0)
+    check(lib().logkv_stream_capture_id(ctypes.c_void_p(stream_ptr(device)), ctypes.byref(out)),
+          "logkv_stream_capture_id")
+    return int(out.value)
 
 
 def stream_ptr(device: torch.device) -> int:

@@ -240,7 +240,7 @@ class LogStructuredKVCache(nn.Module):
         self.profile_events = None   # set to a list of LOGKV_FLUSH_STAGES+1 torch.cuda.Event to time stages
         self._route_ready = None     # end of the last flush (route overlap), with the window rows it had
         self._route_ready_rows = 0
-        self._route_ready_captured = False
+        self._route_ready_capture = 0
         self._route_done = None
 
     # ------------------------------------------------------------------ C-ABI state
@@ -361,13 +361,14 @@ class LogStructuredKVCache(nn.Module):
         flush returns to the caller's stream after them.  Only when every flushed row was
         already in the window at the end of the previous flush (rows appended since then keep
         the caller's stream), without profiling or KV-head sharding, and inside a CUDA-graph
-        capture only when the previous flush was captured too (the fork becomes a graph branch).
+        capture only when the previous flush was recorded in the same capture (the fork becomes
+        a graph branch; an event of another capture or of eager work cannot be waited on there).
         """
         dev = self.level_k.device
         if (not self._route_overlap or dev.type != "cuda" or self._route_ready is None
                 or self.kv_shard_group is not None or self.profile_events is not None
                 or take > self._route_ready_rows
-                or self._route_ready_captured != torch.cuda.is_current_stream_capturing()):
+                or self._route_ready_capture != _lib.capture_id(dev)):
             return None
         stream = self._ROUTE_STREAMS.get(dev)
         if stream is None:
@@ -385,7 +386,7 @@ class LogStructuredKVCache(nn.Module):
             self._route_ready = torch.cuda.Event()
         self._route_ready.record(torch.cuda.current_stream(dev))
         self._route_ready_rows = self.recent_count
-        self._route_ready_captured = torch.cuda.is_current_stream_capturing()
+        self._route_ready_capture = _lib.capture_id(dev)
 
     def flush_device(self, take: int) -> None:
         """One device flush of the ``take`` oldest window tokens plus the window shift."""

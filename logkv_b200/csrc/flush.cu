@@ -637,6 +637,16 @@ extern "C" int logkv_flush_profiled(const logkv_layout_t* layout, const logkv_st
                    reinterpret_cast<cudaEvent_t*>(events));
 }
 
+extern "C" int logkv_stream_capture_id(void* stream, unsigned long long* id) {
+  if (!id) return LOGKV_E_POINTER;
+  cudaStreamCaptureStatus status = cudaStreamCaptureStatusNone;
+  unsigned long long cid = 0;
+  const cudaError_t e = cudaStreamGetCaptureInfo(static_cast<cudaStream_t>(stream), &status, &cid);
+  if (e != cudaSuccess) return (int)e;
+  *id = status == cudaStreamCaptureStatusActive ? cid : 0ull;
+  return LOGKV_OK;
+}
+
 extern "C" int logkv_read_status(const void* workspace, int32_t* out, void* stream) {
   if (!workspace || !out) return LOGKV_E_POINTER;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

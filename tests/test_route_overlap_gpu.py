@@ -74,3 +74,38 @@ def test_decisions_finish_while_the_callers_stream_is_busy():
                 break
             torch.cuda.synchronize()
     assert overlapped, "decisions waited for the caller's stream"
+
+
+def test_overlap_under_graph_capture_matches_plain_flushes():
+    """Flushes captured in CUDA graphs with overlap on: a flush whose previous flush ran in
+    another capture (or eagerly) does not fork; two flushes in one capture fork within it.
+    Each graph is replayed once, in order; every buffer equals the plain eager cache's."""
+    from test_flush_gpu import torch_dtype
+    cfg = next(c for c in CONFIGS if c["beta"] and c["chunk"] == c["granularity"])
+    stream = make_stream(cfg)
+    plain, over = make_cache(cfg, stream), make_cache(cfg, stream)
+    over._route_overlap = True
+    dt = torch_dtype(cfg)
+    chunks = stream["chunks"]
+    with torch.no_grad():
+        for chunk in chunks[:2]:                       # fill the window, first flush (eager)
+            push(plain, cfg, chunk)
+            push(over, cfg, chunk)
+        groups = [chunks[2:3], chunks[3:5]]            # one flush alone, then two in one capture
+        for group in groups:
+            staged = []
+            for chunk in group:
+                push(plain, cfg, chunk)
+                staged.append(tuple(torch.from_numpy(chunk[n]).to("cuda", dt) for n in ("k", "k_raw", "v"))
+                              + (torch.from_numpy(chunk["span_ends"].astype("uint8")).cuda(),
+                                 chunk["span_ends"].tolist()))
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for k, kr, v, ends, ends_host in staged:
+                    over.add_recent(k, v, k_raw=kr, span_ends=ends_host, span_ends_device=ends)
+            graph.replay()
+            torch.cuda.synchronize()
+            assert over.read_status() == 0
+            assert_state(over, state(plain))
+            del graph
