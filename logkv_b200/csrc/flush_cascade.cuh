@@ -500,20 +500,24 @@ __global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logk
             for (int q = tid; q < qn; q += nt) tcut[q] = (uint8_t)bcut[q];
           }
           // Apply: per output side, sum over member rows (row order) of w*x / max(mass, 1e-12).
-          for (int item = tid; item < qn * 2 * 2 * DV; item += nt) {
-            const int q = item / (4 * DV), side = (item / (2 * DV)) & 1, f = (item / DV) & 1, v = item % DV;
+          // One item computes both sides of a (group, component, 16-byte column) from one load
+          // of each member row; each side keeps its own products (x * 0 for rows of the other
+          // side) and sums in row order.  Groups are 4 rows wide, or 2 (the tail: one side).
+          for (int item = tid; item < qn * 2 * DV; item += nt) {
+            const int q = item / (2 * DV), f = (item / DV) & 1, v = item % DV;
             const int start = 4 * q;
             const int width = min(4, npair - (t0 + start));
-            if (side == 1 && width != 4) continue;
+            const bool two = width == 4;
             const int cut = bcut[q];
             const T* base = f ? tv : tk;
-            float acc[VN], mass = 0.f;
+            float acc0[VN], acc1[VN], mass0 = 0.f, mass1 = 0.f;
 #pragma unroll
-            for (int e = 0; e < VN; ++e) acc[e] = 0.f;
+            for (int e = 0; e < VN; ++e) acc0[e] = acc1[e] = 0.f;
             for (int i = 0; i < 4; ++i) {
               const bool valid = i < width;
-              const bool in = valid && (width == 2 ? side == 0 : (side == 0 ? i < cut : i >= cut));
-              const float om = fmul(valid ? tm[start + i].w : 0.f, in ? 1.f : 0.f);
+              const bool in0 = valid && (!two || i < cut), in1 = valid && two && i >= cut;
+              const float wi = valid ? tm[start + i].w : 0.f;
+              const float om0 = fmul(wi, in0 ? 1.f : 0.f), om1 = fmul(wi, in1 ? 1.f : 0.f);
               float xr[VN];
               if (valid) {
                 unpack(*reinterpret_cast<const uint4*>(base + (start + i) * D + v * VN), xr, (const T*)nullptr);
@@ -521,15 +525,26 @@ __global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logk
 #pragma unroll
                 for (int e = 0; e < VN; ++e) xr[e] = 0.f;
               }
-              mass = fadd(mass, om);
+              mass0 = fadd(mass0, om0);
+              mass1 = fadd(mass1, om1);
 #pragma unroll
-              for (int e = 0; e < VN; ++e) acc[e] = fadd(acc[e], fmul(xr[e], om));
+              for (int e = 0; e < VN; ++e) {
+                acc0[e] = fadd(acc0[e], fmul(xr[e], om0));
+                acc1[e] = fadd(acc1[e], fmul(xr[e], om1));
+              }
             }
-            const float den = fmaxf(mass, 1e-12f);
+            const float den0 = fmaxf(mass0, 1e-12f);
 #pragma unroll
-            for (int e = 0; e < VN; ++e) acc[e] = fdiv(acc[e], den);
-            const int outrow = (t0 + start) / 2 + side;
-            *reinterpret_cast<uint4*>((f ? SV : SK) + x.scr_row(nb, outrow) * D + v * VN) = pack(acc, (const T*)nullptr);
+            for (int e = 0; e < VN; ++e) acc0[e] = fdiv(acc0[e], den0);
+            const int outrow = (t0 + start) / 2;
+            *reinterpret_cast<uint4*>((f ? SV : SK) + x.scr_row(nb, outrow) * D + v * VN) = pack(acc0, (const T*)nullptr);
+            if (two) {
+              const float den1 = fmaxf(mass1, 1e-12f);
+#pragma unroll
+              for (int e = 0; e < VN; ++e) acc1[e] = fdiv(acc1[e], den1);
+              *reinterpret_cast<uint4*>((f ? SV : SK) + x.scr_row(nb, outrow + 1) * D + v * VN) =
+                  pack(acc1, (const T*)nullptr);
+            }
           }
           for (int item = tid; item < qn * 2; item += nt) {
             const int q = item / 2, side = item % 2;
