@@ -1284,14 +1284,32 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
   const uint32_t base_s = tc::smem_u32(base);
   const int g = blockIdx.y, b = blockIdx.z, ln = b * a.G + g;
   const int QT = kTcRows / a.rf;
-  const int tile0 = blockIdx.x * NQ;                        // first query tile of this CTA
-  const int tq0 = a.qoff + tile0 * QT;
-  const int tlast = min(a.qoff + a.TQ, tq0 + NQ * QT) - 1;   // last query token of the CTA
+  // Query tiles of this CTA.  With two tiles and an even tile count, CTA x takes tiles x and
+  // ntiles - 1 - x, so every CTA sees the same number of causal chunk units in total (adjacent
+  // tiles would leave the last CTA with the two longest); otherwise tiles NQ x .. NQ x + NQ - 1.
+  const int ntiles = (a.TQ + QT - 1) / QT;
+  const bool mirror = NQ == 2 && (ntiles & 1) == 0;
+  auto tq_of = [&](int t) {
+    const int tile = mirror ? (t == 0 ? (int)blockIdx.x : ntiles - 1 - (int)blockIdx.x) : (int)blockIdx.x * NQ + t;
+    return a.qoff + tile * QT;
+  };
   const __nv_bfloat16* PK = static_cast<const __nv_bfloat16*>(pre.k);
   const __nv_bfloat16* PV = static_cast<const __nv_bfloat16*>(pre.v);
   const int Lp = pre.length[ln], R = a.rcount;
+  const int up = (Lp + TS - 1) / TS, ur = (R + TS - 1) / TS;
+  // Units (64-slot K/V tiles) each query tile attends to: prefix, window, then the new tokens up
+  // to its last token (causal); the CTA streams the longest tile's units.
+  int Ut[NQ];
+  int tlast = 0;
+#pragma unroll
+  for (int t = 0; t < NQ; ++t) {
+    const int last = min(a.qoff + a.TQ, tq_of(t) + QT) - 1;
+    tlast = t ? max(tlast, last) : last;
+    const int tv = a.causal ? min(a.T, last + 1) : a.T;
+    Ut[t] = up + ur + (tv + TS - 1) / TS;
+  }
   const int Tvis = a.causal ? min(a.T, tlast + 1) : a.T;
-  const int up = (Lp + TS - 1) / TS, ur = (R + TS - 1) / TS, uc = (Tvis + TS - 1) / TS;
+  const int uc = (Tvis + TS - 1) / TS;
   const int U = up + ur + uc;
 
   if (tid == 0) {
@@ -1362,7 +1380,7 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
     for (int flat = lt; flat < NQ * kTcRows * CPR; flat += kTcLoaders) {
       const int mq = flat / CPR, c = flat % CPR;
       const int t = mq / kTcRows, m = mq % kTcRows;
-      const int tok = tq0 + t * QT + m % QT, h = g * a.rf + m / QT;
+      const int tok = tq_of(t) + m % QT, h = g * a.rf + m / QT;
       unsigned char* dst = base + S::OFF_Q + t * S::Q1_BYTES + (c >> 3) * (kTcRows * 128) + m * 128 +
                            (((c & 7) ^ (m & 7)) << 4);
       if (tok < a.qoff + a.TQ) cp_async16(dst, q + (((size_t)b * a.H + h) * a.T + tok) * D + c * 8);
@@ -1430,6 +1448,7 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
           const uint32_t kbs = base_s + S::OFF_K + st * S::KV_BYTES;
 #pragma unroll
           for (int t = 0; t < NQ; ++t) {
+            if (u >= Ut[t]) continue;   // tile t's causal range ends before unit u
             // S(t) is free once the softmax has loaded S(t, u-1) into registers.
             if (u >= 1 && !tc::mbar_wait(&s_free[t], (u - 1) & 1, kTcWaitBudget)) {
               ok = false;
@@ -1451,6 +1470,7 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
           const int v = u - 1, bp = v & 1, vs = v % ST;
           const uint32_t vbs = base_s + S::OFF_V + vs * S::KV_BYTES;
           for (int t = 0; t < NQ; ++t) {
+            if (v >= Ut[t]) continue;
             ok = tc::mbar_wait(&p_full[t][bp], (v >> 1) & 1, kTcWaitBudget);
             if (!ok) break;
             tc::fence_after();
@@ -1472,10 +1492,11 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
     const int qt = warp >> 2;
     const int row = tid - qt * kTcRows;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const int row_t = tq0 + qt * QT + (row % QT);
+    const int row_t = tq_of(qt) + (row % QT);
+    const int Uq = Ut[qt];
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int u = 0; u < U; ++u) {
+    for (int u = 0; u < Uq; ++u) {
       const int st = u & 1, ks_ = u % ST;
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&kv_full[ks_], (u / ST) & 1, kTcWaitBudget) &&
                                        tc::mbar_wait(&s_full[qt], u & 1, kTcWaitBudget));
@@ -1559,12 +1580,12 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
       tc::fence_before();
       tc::mbar_arrive(&p_full[qt][st]);
     }
-    if (ok && U > 0)
+    if (ok && Uq > 0)
       ok = __all_sync(0xffffffffu,
-                      tc::mbar_wait(&pv_done[qt][(U - 1) & 1], ((U - 1) >> 1) & 1, kTcWaitBudget));
+                      tc::mbar_wait(&pv_done[qt][(Uq - 1) & 1], ((Uq - 1) >> 1) & 1, kTcWaitBudget));
     if (!ok) {
       if ((tid & 31) == 0) fail();
-    } else if (U > 0) {
+    } else if (Uq > 0) {
       tc::fence_after();
       const int hh = row / QT;
       const bool in = row_t < a.qoff + a.TQ;
