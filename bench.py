@@ -153,6 +153,7 @@ def make_caches(torch, cfg, device, cos, sin):
             (cfg["batch_per_rank"], cfg["groups"], cfg["tokens"], cfg["head_dim"]),
             (cfg["batch_per_rank"], cfg["groups"], cfg["tokens"], cfg["head_dim"]),
             B=cfg["B"], recent_size=cfg["recent"], device=device, dtype=torch.bfloat16,
+            semantic_clusters=True, semantic_anchor_mode="mid", allocate_second_order=False,
             cluster_k_max=cfg["clusters"], semantic_flush_granularity=cfg["granularity"],
             semantic_centroid_backend="parallel", semantic_replay_updates=True,
             alpha_exact_tokens=cfg["exact"], alpha_span_max_tokens=cfg["span_cap"],
@@ -561,7 +562,8 @@ def bench_kv_sharded(args, rank, world, local_rank):
     group = dist.group.WORLD if world > 1 else None
     caches = [LogStructuredKVCache(
         (1, hi - lo, cfg["tokens"], cfg["head_dim"]), (1, hi - lo, cfg["tokens"], cfg["head_dim"]),
-        B=cfg["B"], recent_size=cfg["recent"], device=device, dtype=torch.bfloat16, cluster_k_max=cfg["clusters"],
+        B=cfg["B"], recent_size=cfg["recent"], device=device, dtype=torch.bfloat16, semantic_clusters=True,
+        semantic_anchor_mode="mid", allocate_second_order=False, cluster_k_max=cfg["clusters"],
         semantic_flush_granularity=cfg["granularity"], semantic_centroid_backend="parallel",
         semantic_replay_updates=True, alpha_exact_tokens=cfg["exact"], alpha_span_max_tokens=cfg["span_cap"],
         beta_novelty=cfg["beta"], beta_adaptive_merge=cfg["beta"], cos_cache=cos, sin_cache=sin,
@@ -624,7 +626,8 @@ def prefill_decode_cache(torch, cfg, batch, device, cos, sin, seed):
     G, D = cfg["groups"], cfg["head_dim"]
     c = LogStructuredKVCache(
         (batch, G, cfg["max_seq"], D), (batch, G, cfg["max_seq"], D), B=cfg["B"], recent_size=cfg["recent"],
-        device=device, dtype=torch.bfloat16, cluster_k_max=cfg["clusters"], semantic_flush_granularity=cfg["recent"],
+        device=device, dtype=torch.bfloat16, semantic_clusters=True, semantic_anchor_mode="mid",
+        allocate_second_order=False, cluster_k_max=cfg["clusters"], semantic_flush_granularity=cfg["recent"],
         semantic_centroid_backend="parallel", semantic_replay_updates=True, alpha_exact_tokens=cfg["exact"],
         alpha_span_max_tokens=cfg["span_cap"], beta_novelty=True, beta_adaptive_merge=True, cos_cache=cos,
         sin_cache=sin, rope_n_elem=D)

@@ -36,6 +36,7 @@ extern "C" {
 #define LOGKV_E_WORKSPACE (-3)  /* workspace missing or too small            */
 #define LOGKV_E_POINTER (-4)    /* a required pointer is NULL or misaligned  */
 #define LOGKV_E_SMEM (-5)       /* the shape needs more shared memory        */
+#define LOGKV_E_DEVICE (-6)     /* the state lives on another device than the current one */
 
 #define LOGKV_DTYPE_F32 0
 #define LOGKV_DTYPE_BF16 1
@@ -126,12 +127,17 @@ LOGKV_API int logkv_flush(const logkv_layout_t* layout, const logkv_state_t* sta
  * logkv_flush_workspace_bytes exceeds 32 MiB are rejected with LOGKV_E_WORKSPACE
  * and nothing is launched.  The call itself allocates nothing (no cudaMalloc,
  * no allocating library call); it clears the region's status word and row
- * counters with cudaMemsetAsync before the flush.  The first call on each
- * device looks the region's device address up (with that device current);
- * make that first call before any stream capture.  All calls share the one
- * region, which keeps the last call's contents: two calls whose work overlaps
- * on the GPU (different streams, or different threads on one device) race on
- * it, so serialize them.
+ * counters with cudaMemsetAsync before the flush.  The state must live on the
+ * current device (else LOGKV_E_DEVICE, nothing launched).  The first call in
+ * each CUDA context looks the region's device address up (with that device
+ * current) and caches it for that context; make that first call before any
+ * stream capture.  After a device reset the next call looks it up again.  All
+ * calls share the one region, which keeps the last call's contents: two calls
+ * whose work overlaps on the GPU (different streams, or different threads on
+ * one device) race on it, so serialize them.  The flush's status word and row
+ * counters stay readable in the region until the next static flush clears
+ * them: logkv_read_status / logkv_read_counters with workspace = NULL read
+ * them (current device).
  */
 LOGKV_API int logkv_flush_static(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
                                  int32_t recent_count, void* stream);
@@ -219,7 +225,11 @@ LOGKV_API int logkv_flush_replay(const logkv_layout_t* layout, const logkv_state
  */
 LOGKV_API int logkv_stream_capture_id(void* stream, unsigned long long* id);
 
-/* Copy the workspace status word to *out (synchronizes `stream`); nonzero = a capacity was exceeded. */
+/*
+ * Copy the workspace status word to *out (synchronizes `stream`); nonzero = a capacity was
+ * exceeded.  workspace = NULL reads the status of the last logkv_flush_static on the current
+ * device.
+ */
 LOGKV_API int logkv_read_status(const void* workspace, int32_t* out, void* stream);
 
 /*
@@ -242,7 +252,8 @@ LOGKV_API int logkv_flush_profiled(const logkv_layout_t* layout, const logkv_sta
  * appended, [4] rows zeroed, [5] merged rows carried up, [6] rows gathered for
  * delayed re-inserts, [7] flushes, [8] Beta groups whose cut was a near tie and
  * was decided by the canonical sequential evaluation.  The workspace must be
- * zero-filled once when it is allocated.
+ * zero-filled once when it is allocated.  workspace = NULL reads the counters of
+ * the last logkv_flush_static on the current device.
  */
 LOGKV_API int logkv_read_counters(const void* workspace, uint64_t* out, int32_t n, void* stream);
 

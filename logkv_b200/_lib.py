@@ -16,7 +16,8 @@ LIB_PATH = os.path.join(HERE, "liblogkv_b200.so")
 
 ERRORS = {-1: "shape out of the supported range", -2: "unsupported storage dtype",
           -3: "workspace missing or too small", -4: "null or misaligned pointer",
-          -5: "shape needs more shared memory than one SM has"}
+          -5: "shape needs more shared memory than one SM has",
+          -6: "the cache state lives on another device than the current one"}
 
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1}
 

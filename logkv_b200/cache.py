@@ -84,19 +84,23 @@ class LogStructuredKVCache(nn.Module):
     _route_overlap = os.environ.get("LOGKV_ROUTE_OVERLAP", "0") == "1"
     _ROUTE_STREAMS: dict = {}
 
-    def __init__(self, k_shape, v_shape, B: int = 512, recent_size: int = 0, device=None, dtype=None, *,
-                 semantic_clusters: bool = True, cluster_k_max: int = 12, cluster_lambda_rel: float = 1.0,
-                 seg_eta: float = 1.0, seg_g0: float = 2048.0, seg_gap_max=None, seg_block_level: int = 0,
-                 seg_forget: float = 0.5, semantic_s_h=None, semantic_flush_granularity: int = 2,
-                 semantic_cluster_chunk_size: int = 0, semantic_capacity_beta: float = 0.0,
-                 semantic_capacity_hard_cap_mult: float = 0.0, semantic_legacy_route: bool = False,
-                 semantic_unified_route: bool = False, semantic_merge_passes: int = 1,
-                 semantic_anchor_mode: str = "mid", semantic_pack_backend: str = "auto",
-                 semantic_centroid_backend: str = "sequential", semantic_replay_updates: bool = False,
-                 cos_cache=None, sin_cache=None, rope_n_elem=None, allocate_second_order: bool = False,
-                 alpha_exact_tokens: int = 256, alpha_span_max_tokens: int = 64, beta_novelty: bool = False,
-                 beta_adaptive_merge: bool = False, importance_pooling: bool = False, kv_shard_group=None,
-                 **unused) -> None:
+    def __init__(self, k_shape, v_shape, B: int = 512, recent_size: int = 0, device=None, dtype=None,
+                 importance_pooling: bool = False, importance_pooling_lambda: float = 1.0,
+                 importance_pooling_temperature: float = 1.0, semantic_clusters: bool = False,
+                 cluster_k_max: int = 1, cluster_lambda_rel: float = 1.0, seg_eta: float = 1.0,
+                 seg_g0: float = 2048.0, seg_gap_max=None, seg_block_level: int = 0, seg_forget: float = 0.5,
+                 semantic_s_h=None, semantic_flush_granularity: int = 2, semantic_cluster_chunk_size: int = 0,
+                 semantic_capacity_beta: float = 0.0, semantic_capacity_hard_cap_mult: float = 0.0,
+                 semantic_legacy_route: bool = False, semantic_unified_route: bool = False,
+                 semantic_merge_passes: int = 1, semantic_anchor_mode: str = "multi",
+                 semantic_pack_backend: str = "auto", semantic_centroid_backend: str = "sequential",
+                 semantic_replay_updates: bool = False, cos_cache=None, sin_cache=None, rope_n_elem=None,
+                 allocate_second_order: bool = True, alpha_exact_tokens: int = 0, alpha_span_max_tokens: int = 64,
+                 beta_novelty: bool = False, beta_adaptive_merge: bool = False, *, kv_shard_group=None) -> None:
+        """The reference's constructor (litgpt/log_kv_cache.py:681-720): same keywords, order and
+        defaults, so an unknown or misspelt keyword raises TypeError.  ``kv_shard_group`` (keyword
+        only, no reference counterpart) makes this cache one rank's block of groups of a
+        KV-head-sharded sequence."""
         super().__init__()
         batch, groups, max_seq, k_dim = k_shape
         v_dim = v_shape[3]

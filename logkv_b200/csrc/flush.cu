@@ -647,24 +647,6 @@ extern "C" int logkv_stream_capture_id(void* stream, unsigned long long* id) {
   return LOGKV_OK;
 }
 
-extern "C" int logkv_read_status(const void* workspace, int32_t* out, void* stream) {
-  if (!workspace || !out) return LOGKV_E_POINTER;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemcpyAsync(out, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-  return (int)e;
-}
-
-extern "C" int logkv_read_counters(const void* workspace, uint64_t* out, int32_t n, void* stream) {
-  if (!workspace || !out || n < 1) return LOGKV_E_POINTER;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int m = n < kNumCounters ? n : kNumCounters;
-  cudaError_t e = cudaMemcpyAsync(out, static_cast<const char*>(workspace) + 256, m * sizeof(uint64_t),
-                                  cudaMemcpyDeviceToHost, st);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
-  return (int)e;
-}
-
 // ---------------------------------------------------------------- allocation-free flush
 // Callers that may not allocate device memory (a host whose allocator is
 // locked after start-up, or a binding that cannot hand a device buffer over
@@ -675,27 +657,76 @@ namespace {
 constexpr size_t kStaticScratchBytes = size_t(32) << 20;  // 32 MiB per GPU, held until process exit
 __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
-constexpr int kMaxDevices = 64;
+// The symbol name is only a host-side stand-in; its device address belongs to the CUDA context
+// the library's module was loaded into.  Addresses are cached per context, keyed by the
+// driver's context id (unique for the life of the process), so a context torn down and
+// created again (cudaDeviceReset) gets a fresh lookup instead of a dangling address.
+typedef int (*CtxGetCurrentFn)(void**);
+typedef int (*CtxGetIdFn)(void*, unsigned long long*);
+struct StaticSlot {
+  unsigned long long ctx_id;
+  void* ptr;
+};
+constexpr int kMaxContexts = 64;
 std::mutex g_static_mutex;
-void* g_static_ptr[kMaxDevices] = {};
+StaticSlot g_static_slots[kMaxContexts] = {};
+int g_static_next = 0;
+CtxGetCurrentFn g_ctx_current = nullptr;
+CtxGetIdFn g_ctx_id = nullptr;
 
-// Device address of g_static_scratch on the current device.  The symbol name is
-// only a host-side stand-in; the address is looked up once per device, with
-// that device current, and cached.
-cudaError_t static_scratch(void** out) {
+// Id of the current context (called with g_static_mutex held).
+int current_context_id(unsigned long long* id) {
+  if (!g_ctx_current || !g_ctx_id) {
+    void* f_cur = nullptr;
+    void* f_id = nullptr;
+    cudaDriverEntryPointQueryResult q_cur = cudaDriverEntryPointSymbolNotFound, q_id = q_cur;
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f_cur, 12000, cudaEnableDefault, &q_cur);
+    if (e != cudaSuccess) return (int)e;
+    e = cudaGetDriverEntryPointByVersion("cuCtxGetId", &f_id, 12000, cudaEnableDefault, &q_id);
+    if (e != cudaSuccess) return (int)e;
+    if (q_cur != cudaDriverEntryPointSuccess || q_id != cudaDriverEntryPointSuccess || !f_cur || !f_id)
+      return (int)cudaErrorSymbolNotFound;
+    g_ctx_current = reinterpret_cast<CtxGetCurrentFn>(f_cur);
+    g_ctx_id = reinterpret_cast<CtxGetIdFn>(f_id);
+  }
+  void* ctx = nullptr;
+  if (g_ctx_current(&ctx) != 0 || !ctx) return (int)cudaErrorDeviceUninitialized;
+  if (g_ctx_id(ctx, id) != 0) return (int)cudaErrorDeviceUninitialized;
+  return LOGKV_OK;
+}
+
+// Device address of g_static_scratch on the current device.  When `owner` is given it must be
+// device memory of that device (the cache state the flush works on): a state on another device
+// is refused with LOGKV_E_DEVICE instead of flushing through the wrong GPU's scratch.
+int static_scratch(const void* owner, void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lock(g_static_mutex);
-  if (!g_static_ptr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_static_scratch);
-    if (e != cudaSuccess) return e;
-    g_static_ptr[dev] = p;
+  if (e != cudaSuccess) return (int)e;
+  if (owner) {
+    cudaPointerAttributes attr{};
+    e = cudaPointerGetAttributes(&attr, owner);
+    if (e != cudaSuccess) return (int)e;
+    if ((attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged) || attr.device != dev)
+      return LOGKV_E_DEVICE;
   }
-  *out = g_static_ptr[dev];
-  return cudaSuccess;
+  e = cudaSetDevice(dev);  // makes the device's primary context current (creating nothing else)
+  if (e != cudaSuccess) return (int)e;
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  unsigned long long cid = 0;
+  const int c = current_context_id(&cid);
+  if (c != LOGKV_OK) return c;
+  for (int i = 0; i < kMaxContexts; ++i)
+    if (g_static_slots[i].ptr && g_static_slots[i].ctx_id == cid) {
+      *out = g_static_slots[i].ptr;
+      return LOGKV_OK;
+    }
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_static_scratch);
+  if (e != cudaSuccess) return (int)e;
+  g_static_slots[g_static_next] = StaticSlot{cid, p};
+  g_static_next = (g_static_next + 1) % kMaxContexts;
+  *out = p;
+  return LOGKV_OK;
 }
 
 }  // namespace
@@ -704,16 +735,46 @@ extern "C" int logkv_flush_static(const logkv_layout_t* layout, const logkv_stat
                                   int32_t recent_count, void* stream) {
   const int v = validate(layout, flush_tokens);
   if (v != LOGKV_OK) return v;
-  if (!state) return LOGKV_E_POINTER;
+  if (!state || !state->level_k) return LOGKV_E_POINTER;
   const size_t need = logkv_flush_workspace_bytes(layout, flush_tokens);
   if (need == 0 || need > kStaticScratchBytes) return LOGKV_E_WORKSPACE;
   void* scratch = nullptr;
-  cudaError_t e = static_scratch(&scratch);
-  if (e != cudaSuccess) return (int)e;
+  const int r = static_scratch(state->level_k, &scratch);
+  if (r != LOGKV_OK) return r;
   // The status word and the row counters (first 512 bytes) must start at zero;
   // everything else in the scratch is written before it is read within a flush.
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  e = cudaMemsetAsync(scratch, 0, 512, st);
+  const cudaError_t e = cudaMemsetAsync(scratch, 0, 512, st);
   if (e != cudaSuccess) return (int)e;
   return run_flush(layout, state, flush_tokens, recent_count, scratch, kStaticScratchBytes, stream, nullptr);
+}
+
+extern "C" int logkv_read_status(const void* workspace, int32_t* out, void* stream) {
+  if (!out) return LOGKV_E_POINTER;
+  if (!workspace) {
+    void* scratch = nullptr;
+    const int r = static_scratch(nullptr, &scratch);
+    if (r != LOGKV_OK) return r;
+    workspace = scratch;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(out, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  return (int)e;
+}
+
+extern "C" int logkv_read_counters(const void* workspace, uint64_t* out, int32_t n, void* stream) {
+  if (!out || n < 1) return LOGKV_E_POINTER;
+  if (!workspace) {
+    void* scratch = nullptr;
+    const int r = static_scratch(nullptr, &scratch);
+    if (r != LOGKV_OK) return r;
+    workspace = scratch;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int m = n < kNumCounters ? n : kNumCounters;
+  cudaError_t e = cudaMemcpyAsync(out, static_cast<const char*>(workspace) + 256, m * sizeof(uint64_t),
+                                  cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  return (int)e;
 }

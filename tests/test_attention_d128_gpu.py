@@ -25,6 +25,7 @@ def make_state(seed=0, B=1, G=2, D=128, K=4, levels=3, recent=512, R=300, P=64, 
     cos, sin = rope_tables(max_seq + 64, D, base=1e6)
     cache = LogStructuredKVCache(
         (B, G, max_seq, D), (B, G, max_seq, D), B=32, recent_size=recent, device="cuda", dtype=torch.bfloat16,
+        semantic_clusters=True, semantic_anchor_mode="mid", allocate_second_order=False,
         cluster_k_max=K, semantic_flush_granularity=recent, alpha_exact_tokens=P, alpha_span_max_tokens=16,
         beta_novelty=True, beta_adaptive_merge=True, cos_cache=torch.from_numpy(cos), sin_cache=torch.from_numpy(sin),
         rope_n_elem=D)

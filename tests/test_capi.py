@@ -80,3 +80,14 @@ def test_unified_argument_checks(lib):
     assert plug.logkv_unified_init(ctypes.byref(u), None) == -1
     u = Unified(*([fake] * 3 + [None] + [fake] * 7), 0, 16, 8, 1)
     assert plug.logkv_unified_step(ctypes.byref(u), None) == -1
+
+
+def test_constructor_rejects_unknown_keywords():
+    """The cache takes the reference's keywords only (litgpt/log_kv_cache.py:681-720): a misspelt
+    YAML switch raises TypeError instead of being dropped; the reference's defaults (no semantic
+    clusters, multi anchors) are outside this path and raise NotImplementedError."""
+    from logkv_b200.cache import LogStructuredKVCache
+    with pytest.raises(TypeError):
+        LogStructuredKVCache((1, 1, 64, 8), (1, 1, 64, 8), semantic_clusterz=True)
+    with pytest.raises(NotImplementedError):
+        LogStructuredKVCache((1, 1, 64, 8), (1, 1, 64, 8), device="cpu")

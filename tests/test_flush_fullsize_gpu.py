@@ -42,7 +42,8 @@ def test_fullsize_flush_matches_oracle():
     from logkv_b200.workload import rope_tables
     cos, sin = rope_tables(32768, D, base=1e6)
     cache = LogStructuredKVCache((1, G, 32768, D), (1, G, 32768, D), B=128, recent_size=2048, device="cuda",
-                                 dtype=torch.bfloat16, cluster_k_max=K, semantic_flush_granularity=2048,
+                                 dtype=torch.bfloat16, semantic_clusters=True, semantic_anchor_mode="mid",
+                                 allocate_second_order=False, cluster_k_max=K, semantic_flush_granularity=2048,
                                  alpha_exact_tokens=256, alpha_span_max_tokens=64, beta_novelty=True,
                                  beta_adaptive_merge=True, cos_cache=torch.from_numpy(cos),
                                  sin_cache=torch.from_numpy(sin), rope_n_elem=D)

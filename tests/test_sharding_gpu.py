@@ -54,6 +54,7 @@ def worker(rank: int, world: int, port: int, name: str, out: dict) -> None:
         shape = (cfg["batch"], g1 - g0, cfg["max_seq"], cfg["dim"])
         cache = LogStructuredKVCache(
             shape, shape, B=cfg["slots"], recent_size=cfg["recent"], device=f"cuda:{rank}", dtype=dt,
+            semantic_clusters=True, semantic_anchor_mode="mid", allocate_second_order=False,
             cluster_k_max=cfg["clusters"], semantic_flush_granularity=cfg["granularity"],
             semantic_centroid_backend="sequential", semantic_replay_updates=True,
             alpha_exact_tokens=cfg["exact"], alpha_span_max_tokens=cfg["span_cap"], beta_novelty=cfg["beta"],
