@@ -99,6 +99,41 @@ typedef struct logkv_state {
   int32_t* alpha_count;     /* [1] max over rows (the reference's alpha_count) */
 } logkv_state_t;
 
+/*
+ * Near-tie log (no reference counterpart).  Every decision of a flush whose two best candidates,
+ * or whose value and threshold, lie within a relative gap |a - b| / max(|a|, |b|) < 1e-6 is
+ * recorded in the workspace, so that a decision which a different floating-point summation
+ * order could flip is logged, not waived silently.  Kinds and their fields:
+ *   ATTACH_COST   frozen-centroid routing cost argmin (log_kv_cache.py:2649-2681): index = token
+ *                 position, first / second = best / runner-up cluster, value = best cost;
+ *   DIRECT        winner's semantic distance against lambda * s_h (:4597-4634): first = 1 if the
+ *                 token joined directly, second = winner cluster, value = the distance;
+ *   NEAREST       an orphan's exact-distance nearest live cluster (:4671-4677): clusters;
+ *   SEED_PICK     farthest-point seed argmax (:4650-4668): index = pick number, first / second =
+ *                 token positions of the best and runner-up;
+ *   SEED_NEAREST  an orphan's nearest live-or-seeded cluster after seeding: clusters;
+ *   BETA_CUT      Beta 4->2 cut costs (beta_log_kv.py:29-46) of groups decided in canonical
+ *                 order: cluster = c, index = level * 65536 + group, first / second = cuts;
+ *   ALPHA_ORDER   two span candidates of one batch row with near-equal densities
+ *                 (alpha_log_kv.py:177-226 sorts by density): first / second = candidates;
+ *   ALPHA_SWAP    the greedy's replacement test density * length > evicted loss: first =
+ *                 candidate, second = 1 if the span was taken.
+ * `flush` = flushes of this workspace before the logging one (0-based).
+ */
+#define LOGKV_TIE_ATTACH_COST 1
+#define LOGKV_TIE_DIRECT 2
+#define LOGKV_TIE_NEAREST 3
+#define LOGKV_TIE_SEED_PICK 4
+#define LOGKV_TIE_SEED_NEAREST 5
+#define LOGKV_TIE_BETA_CUT 6
+#define LOGKV_TIE_ALPHA_ORDER 7
+#define LOGKV_TIE_ALPHA_SWAP 8
+typedef struct logkv_tie {
+  int32_t kind, flush, batch, group, cluster, index, first, second;
+  float gap;    /* relative gap of the two values */
+  float value;  /* the winning (or tested) value */
+} logkv_tie_t;
+
 /* Bytes of scratch one logkv_flush call needs for this layout and flush size. */
 LOGKV_API size_t logkv_flush_workspace_bytes(const logkv_layout_t* layout, int32_t flush_tokens);
 
@@ -256,6 +291,15 @@ LOGKV_API int logkv_flush_profiled(const logkv_layout_t* layout, const logkv_sta
  * the last logkv_flush_static on the current device.
  */
 LOGKV_API int logkv_read_counters(const void* workspace, uint64_t* out, int32_t n, void* stream);
+
+/*
+ * Copy the near-tie log to out (up to cap entries, in logging order) and the number of entries
+ * requested since the log was last cleared to *total (entries beyond the log's 4096-entry
+ * capacity are counted but not kept); with clear != 0 the log is emptied after the copy.
+ * Synchronizes `stream`.  workspace = NULL reads the log of logkv_flush_static (current device).
+ */
+LOGKV_API int logkv_read_ties(void* workspace, logkv_tie_t* out, int32_t cap, int64_t* total, int32_t clear,
+                              void* stream);
 
 #ifdef __cplusplus
 }

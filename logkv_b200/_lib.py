@@ -23,7 +23,10 @@ DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1}
 
 FLUSH_STAGES = ("snapshot", "span_cut", "score_attach", "choose", "seed_plan", "prepare", "cascade",
                 "pool_rewrite", "window_shift")
-COUNTERS = ("storage_read", "stage_read", "survivor", "fill", "clear", "carry", "gather", "flushes", "exact_cuts")
+COUNTERS = ("storage_read", "stage_read", "survivor", "fill", "clear", "carry", "gather", "flushes", "exact_cuts",
+            "ties")
+TIE_KINDS = {1: "attach_cost", 2: "direct", 3: "nearest", 4: "seed_pick", 5: "seed_nearest", 6: "beta_cut",
+             7: "alpha_order", 8: "alpha_swap"}
 
 
 class Layout(ctypes.Structure):
@@ -43,6 +46,11 @@ STATE_FIELDS = ["level_k", "level_v", "level_w", "level_p_lo", "level_p_hi", "le
 
 class State(ctypes.Structure):
     _fields_ = [(name, ctypes.c_void_p) for name in STATE_FIELDS]
+
+
+class Tie(ctypes.Structure):
+    _fields_ = [(name, ctypes.c_int32) for name in ("kind", "flush", "batch", "group", "cluster", "index", "first",
+                                                     "second")] + [("gap", ctypes.c_float), ("value", ctypes.c_float)]
 
 
 class Plan(ctypes.Structure):
@@ -96,6 +104,9 @@ def lib() -> ctypes.CDLL:
         handle.logkv_read_counters.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int32,
                                                ctypes.c_void_p]
         P = ctypes.POINTER
+        handle.logkv_read_ties.restype = ctypes.c_int
+        handle.logkv_read_ties.argtypes = [ctypes.c_void_p, P(Tie), ctypes.c_int32, P(ctypes.c_int64), ctypes.c_int32,
+                                           ctypes.c_void_p]
         flush_args = [P(Layout), P(State), ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_size_t]
         handle.logkv_flush_scores.restype = ctypes.c_int
         handle.logkv_flush_scores.argtypes = flush_args + [ctypes.c_void_p]

@@ -445,6 +445,27 @@ class LogStructuredKVCache(nn.Module):
                    "logkv_read_counters")
         return dict(zip(_lib.COUNTERS, (int(x) for x in out)))
 
+    def read_ties(self, clear: bool = True) -> list[dict]:
+        """Near-tie log of this cache's flushes since the last clear (synchronizes).
+
+        One dict per decision whose two best candidates (or value and threshold) were within a
+        relative gap of 1e-6: kind, flush (0-based, counted since the cache was built), batch,
+        group, cluster, index, first, second, gap, value (fields of logkv_tie_t).  Entries beyond
+        the device log's 4096-entry capacity are only counted, in ``self.ties_dropped``.
+        """
+        cap = 4096
+        out = (_lib.Tie * cap)()
+        total = ctypes.c_int64(0)
+        _lib.check(_lib.lib().logkv_read_ties(ctypes.c_void_p(self._workspace.data_ptr()), out, cap,
+                                              ctypes.byref(total), int(clear),
+                                              ctypes.c_void_p(_lib.stream_ptr(self.level_k.device))),
+                   "logkv_read_ties")
+        n = min(int(total.value), cap)
+        self.ties_dropped = int(total.value) - n
+        return [dict(kind=_lib.TIE_KINDS.get(e.kind, str(e.kind)), flush=e.flush, batch=e.batch, group=e.group,
+                     cluster=e.cluster, index=e.index, first=e.first, second=e.second, gap=e.gap, value=e.value)
+                for e in out[:n]]
+
     def read_status(self) -> int:
         out = ctypes.c_int32(0)
         _lib.check(_lib.lib().logkv_read_status(ctypes.c_void_p(self._workspace.data_ptr()), ctypes.byref(out),

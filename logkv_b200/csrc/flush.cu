@@ -281,6 +281,7 @@ static size_t carve(const Geo& g, size_t esize, char* base, Work* w) {
   const size_t B = g.B, G = g.G, D = g.D, K = g.K, P = g.P, NC = g.NC, NW = g.NW, S = g.S;
   w->status = c.take<int32_t>(1, 4);
   w->counters = c.take<unsigned long long>(kNumCounters, 8);
+  w->ties = c.take<TieEntry>(kTieCap, sizeof(TieEntry));  // lands at kTieOffset (checked below)
   w->snap_k = c.take<char>(B * G * P * D, esize);
   w->snap_v = c.take<char>(B * G * P * D, esize);
   w->snap_pos = c.take<int64_t>(B * P, 8);
@@ -517,6 +518,7 @@ static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, i
   Work w{};
   const size_t need = carve(g, esize, static_cast<char*>(workspace), &w);
   if (workspace_bytes < need) return LOGKV_E_WORKSPACE;
+  if (reinterpret_cast<char*>(w.ties) != static_cast<char*>(workspace) + kTieOffset) return LOGKV_E_WORKSPACE;
   if (cascade_smem(g, esize) > 227 * 1024 || prep_smem_bytes(g, esize) > 227 * 1024 ||
       choose_smem_bytes(g) > 227 * 1024 || score_smem_bytes(g, esize) > 227 * 1024 || attach_smem_bytes(g) > 227 * 1024)
     return LOGKV_E_SMEM;
@@ -759,6 +761,30 @@ extern "C" int logkv_read_status(const void* workspace, int32_t* out, void* stre
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaMemcpyAsync(out, workspace, sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  return (int)e;
+}
+
+extern "C" int logkv_read_ties(void* workspace, logkv_tie_t* out, int32_t cap, int64_t* total, int32_t clear,
+                               void* stream) {
+  if (!total || cap < 0 || (cap > 0 && !out)) return LOGKV_E_POINTER;
+  if (!workspace) {
+    void* scratch = nullptr;
+    const int r = static_scratch(nullptr, &scratch);
+    if (r != LOGKV_OK) return r;
+    workspace = scratch;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* base = static_cast<char*>(workspace);
+  unsigned long long* count = reinterpret_cast<unsigned long long*>(base + 256) + kCntTies;
+  unsigned long long n = 0;
+  cudaError_t e = cudaMemcpyAsync(&n, count, sizeof(n), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return (int)e;
+  *total = (int64_t)n;
+  const size_t keep = std::min<size_t>(std::min<size_t>((size_t)n, (size_t)kTieCap), (size_t)cap);
+  if (keep) e = cudaMemcpyAsync(out, base + kTieOffset, keep * sizeof(TieEntry), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess && clear) e = cudaMemsetAsync(count, 0, sizeof(unsigned long long), st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   return (int)e;
 }

@@ -414,6 +414,13 @@ __device__ __forceinline__ bool victim_less(double da, int ia, double db, int ib
 __device__ __forceinline__ bool ranked_less(double da, int ia, double db, int ib) {
   return da > db || (da == db && ia < ib);  // (-density, i) ascending
 }
+// Near tie of two float64 values (relative gap below the tie-log threshold).
+__device__ __forceinline__ bool near_tie_d(double a, double b, float* gap) {
+  const double den = fmax(fabs(a), fabs(b));
+  const double r = den > 0.0 ? fabs(a - b) / den : 0.0;
+  *gap = (float)r;
+  return r < (double)kTieRel;
+}
 
 __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t s, Work w) {
   pdl_entry();
@@ -548,6 +555,20 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
     ranked[rank] = i;
   }
   __syncthreads();
+  // Near ties of the two sorted orders the greedy walks (candidates by density, victims by
+  // density): two near-equal values of a sorted list are always neighbours in it.
+  for (int r = tid; r + 1 < sh_nr; r += nt) {
+    const int i = ranked[r], j = ranked[r + 1];
+    float gap;
+    if (near_tie_d(dens[i], dens[j], &gap))
+      log_tie(w, LOGKV_TIE_ALPHA_ORDER, b, -1, -1, r, min(i, j), max(i, j), gap, (float)dens[i]);
+  }
+  for (int r = tid; r + 1 < sh_nv; r += nt) {
+    float gap;
+    if (near_tie_d(vd[r], vd[r + 1], &gap))
+      log_tie(w, LOGKV_TIE_ALPHA_ORDER, b, -1, -1, r, min(vi[r], vi[r + 1]), max(vi[r], vi[r + 1]), gap,
+              (float)vd[r]);
+  }
   // Bounded greedy (alpha_log_kv.choose_spans) in one warp.  The number of victims a
   // candidate needs comes from an exact integer prefix scan of victim sizes; the float64
   // loss over exactly those victims is summed by lane 0 in the reference's order.
@@ -606,6 +627,16 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
           const int j = c0 + lane;
           at += __popc(__ballot_sync(full, j < nv && victim_less(vd[cur * VC + j], vi[cur * VC + j], di, i)));
         }
+      if (lane == 0) {
+        // The new victim's neighbours in the density order it is inserted into.
+        float gap;
+        for (int nb = -1; nb <= 0; ++nb) {
+          const int j = k + at + nb;
+          if (j >= k && j < nv && near_tie_d(vd[cur * VC + j], di, &gap))
+            log_tie(w, LOGKV_TIE_ALPHA_ORDER, b, -1, -1, j, min(i, vi[cur * VC + j]), max(i, vi[cur * VC + j]),
+                    gap, (float)di);
+        }
+      }
       const int nn = nv - k + (ins ? 1 : 0), nx = cur ^ 1;
       for (int j = lane; j < nn; j += 32) {
         int src = -1;
@@ -641,7 +672,12 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
         bool ok = room >= length;
         if (!ok) {
           nrem = need_prefix(length, available);
-          if (nrem > 0) ok = di * (double)length > pls[nrem - 1];
+          if (nrem > 0) {
+            ok = di * (double)length > pls[nrem - 1];
+            float gap;
+            if (lane == 0 && near_tie_d(di * (double)length, pls[nrem - 1], &gap))
+              log_tie(w, LOGKV_TIE_ALPHA_SWAP, b, -1, -1, i, i, ok ? 1 : 0, gap, (float)(di * (double)length));
+          }
         }
         if (ok) {
           if (lane == 0) chosen[i] = 1;

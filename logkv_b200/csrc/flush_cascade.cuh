@@ -489,6 +489,12 @@ __global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logk
             if (costs[1] < costs[best]) best = 1;
             if (costs[2] < costs[best]) best = 2;
             bcut[q] = best == 0 ? 2 : (best == 1 ? 1 : 3);
+            // Runner-up (earlier cut on equal costs) for the near-tie log.
+            const int r = best == 0 ? (costs[2] < costs[1] ? 2 : 1) : (best == 1 ? (costs[2] < costs[0] ? 2 : 0)
+                                                                                  : (costs[1] < costs[0] ? 1 : 0));
+            if (near_tie(costs[best], costs[r]))
+              log_tie(w, LOGKV_TIE_BETA_CUT, x.b, x.grp, x.c, ell * 65536 + (t0 + 4 * q) / 4, bcut[q],
+                      r == 0 ? 2 : (r == 1 ? 1 : 3), rel_gap(costs[best], costs[r]), costs[best]);
           }
           __syncthreads();
           if (tid == 0) {

@@ -47,13 +47,29 @@ enum Counter : int {
   kCntGather = 6,        // rows gathered for delayed re-inserts
   kCntFlushes = 7,       // flush calls
   kCntExactCuts = 8,     // Beta groups whose cut needed the canonical-order evaluation (near ties)
-  kNumCounters = 9,
+  kCntTies = 9,          // near-tie log entries requested (entries beyond kTieCap are counted only)
+  kNumCounters = 10,
 };
+
+// Near-tie log: every decision of a flush whose two best candidates (or whose value and
+// threshold) lie within a relative gap of kTieRel is recorded, so a caller can see where a
+// different summation order (the reference's vectorised CPU sums) could have decided the other
+// way.  Entries live in the workspace right after the counters (byte offset kTieOffset), in the
+// order the kernels reach them; the count is counters[kCntTies].  Layout = logkv_tie_t.
+constexpr float kTieRel = 1e-6f;
+constexpr int kTieCap = 4096;
+constexpr size_t kTieOffset = 512;
+struct TieEntry {
+  int32_t kind, flush, b, g, c, index, first, second;
+  float gap, value;
+};
+static_assert(sizeof(TieEntry) == sizeof(logkv_tie_t), "tie entry layout");
 
 // Views into the caller's workspace (carved by the host in flush.cu).
 struct Work {
   int32_t* status;
   unsigned long long* counters;  // [kNumCounters]
+  TieEntry* ties;                // [kTieCap] near-tie log (workspace byte kTieOffset)
   void* snap_k;            // [B,G,P,D] T  old pool snapshot
   void* snap_v;
   int64_t* snap_pos;       // [B,P]
@@ -104,6 +120,24 @@ struct Work {
   int64_t* wpos;
   uint8_t* wends;
 };
+
+// Relative gap of two values: |a - b| / max(|a|, |b|) (0 when both are 0; NaN-safe: NaN gives
+// a gap that is not below any threshold).
+__device__ __forceinline__ float rel_gap(float a, float b) {
+  const float den = fmaxf(fabsf(a), fabsf(b));
+  return den > 0.f ? fdiv(fabsf(fsub(a, b)), den) : 0.f;
+}
+__device__ __forceinline__ bool near_tie(float a, float b) { return rel_gap(a, b) < kTieRel; }
+
+// Append one near-tie entry (flush index = flushes counted so far, minus one).
+__device__ __forceinline__ void log_tie(const Work& w, int kind, int b, int g, int c, int index, int first,
+                                        int second, float gap, float value) {
+  const unsigned long long slot = atomicAdd(&w.counters[kCntTies], 1ull);
+  if (slot >= (unsigned long long)kTieCap) return;
+  const unsigned long long flushes = *reinterpret_cast<volatile unsigned long long*>(&w.counters[kCntFlushes]);
+  TieEntry e{kind, (int32_t)flushes - 1, b, g, c, index, first, second, gap, value};
+  w.ties[slot] = e;
+}
 
 // 16-byte vectors of storage elements.
 template <typename T>

@@ -32,30 +32,55 @@ namespace logkv {
 // Outputs are indexed by token.  DC != 0 is a compile-time head dim.
 constexpr int kAttachTokens = 64;   // tokens per 256-thread block: 8 warps x 8 tokens
 
+// Best and runner-up (value, index) over the lane's centres, in index order: a later equal
+// value never replaces the best (first index wins), so an exact tie becomes the runner-up.
 template <int CPL>
-__device__ __forceinline__ void lane_argmin(const float (&v)[CPL], const bool (&ok)[CPL], int c0, float* bv, int* bi,
-                                            int none) {
+__device__ __forceinline__ void lane_top2(const float (&v)[CPL], const bool (&ok)[CPL], int c0, float* bv, int* bi,
+                                          float* sv, int* si, int none) {
   *bv = INFINITY;
   *bi = none;
+  *sv = INFINITY;
+  *si = none;
 #pragma unroll
-  for (int j = 0; j < CPL; ++j)
-    if (ok[j] && v[j] < *bv) {   // strict: the first index wins ties; NaN never wins
+  for (int j = 0; j < CPL; ++j) {
+    if (!ok[j]) continue;
+    if (v[j] < *bv) {
+      *sv = *bv;
+      *si = *bi;
       *bv = v[j];
       *bi = c0 + j;
+    } else if (v[j] < *sv) {
+      *sv = v[j];
+      *si = c0 + j;
     }
+  }
 }
 
-// (value, index) minimum over the 4 lanes of a token, lowest index on ties; `aux` follows the winner.
-__device__ __forceinline__ void quad_argmin(float* bv, int* bi, float* aux) {
+// (value, index) best and runner-up over the 4 lanes of a token, lowest index on ties; `aux`
+// follows the best.  The merge is symmetric, so both lanes of every exchange agree.
+__device__ __forceinline__ void quad_top2(float* bv, int* bi, float* sv, int* si, float* aux) {
+  auto better = [](float v1, int i1, float v2, int i2) { return v1 < v2 || (v1 == v2 && i1 < i2); };
 #pragma unroll
   for (int off = 1; off < 4; off <<= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, *bv, off);
     const int oi = __shfl_xor_sync(0xffffffffu, *bi, off);
+    const float osv = __shfl_xor_sync(0xffffffffu, *sv, off);
+    const int osi = __shfl_xor_sync(0xffffffffu, *si, off);
     const float oa = __shfl_xor_sync(0xffffffffu, *aux, off);
-    if (ov < *bv || (ov == *bv && oi < *bi)) {
+    if (better(ov, oi, *bv, *bi)) {
+      if (better(*bv, *bi, osv, osi)) {
+        *sv = *bv;
+        *si = *bi;
+      } else {
+        *sv = osv;
+        *si = osi;
+      }
       *bv = ov;
       *bi = oi;
       *aux = oa;
+    } else if (better(ov, oi, *sv, *si)) {
+      *sv = ov;
+      *si = oi;
     }
   }
 }
@@ -144,13 +169,13 @@ __device__ void attach_body(const Geo& g, const logkv_state_t& s, const Work& w,
     // Live centres with a cost below +inf compete (NaN and +inf never replace the initial +inf).
     ok[j] = c0 + j < K && alv_s[c] && cost[j] < INFINITY;
   }
-  float best_cost, sem_win = 0.f;
-  int wi;
-  lane_argmin<CPL>(cost, ok, c0, &best_cost, &wi, kMaxClusters);
+  float best_cost, second_cost, sem_win = 0.f;
+  int wi, ri;
+  lane_top2<CPL>(cost, ok, c0, &best_cost, &wi, &second_cost, &ri, kMaxClusters);
 #pragma unroll
   for (int j = 0; j < CPL; ++j)
     if (c0 + j == wi) sem_win = semv[j];
-  quad_argmin(&best_cost, &wi, &sem_win);
+  quad_top2(&best_cost, &wi, &second_cost, &ri, &sem_win);
   const bool any_alive = any_alive_s != 0;
   const int winner = wi < kMaxClusters ? wi : 0;
   // No live centre: winner 0 with cluster 0's semantic distance (the token is an orphan);
@@ -165,6 +190,10 @@ __device__ void attach_body(const Geo& g, const logkv_state_t& s, const Work& w,
     w.orphan[o] = direct ? 0 : 1;
     w.s_winner[o] = s_win;
     if (!orphan) w.assign_tok[o] = (int8_t)winner;   // no live centre: 0
+    if (any_alive && ri < kMaxClusters && near_tie(best_cost, second_cost))
+      log_tie(w, LOGKV_TIE_ATTACH_COST, b, grp, -1, (int)pos, wi, ri, rel_gap(best_cost, second_cost), best_cost);
+    if (any_alive && near_tie(s_win, thresh))
+      log_tie(w, LOGKV_TIE_DIRECT, b, grp, -1, (int)pos, direct ? 1 : 0, winner, rel_gap(s_win, thresh), s_win);
   }
   if (!__any_sync(0xffffffffu, orphan)) return;
   // Pass 2 (warps with an orphan): exact distances to the lane's live centres, left to right;
@@ -194,21 +223,44 @@ __device__ void attach_body(const Geo& g, const logkv_state_t& s, const Work& w,
     dist[j] = __fsqrt_rn(ex[j]);
     ok[j] = c0 + j < K && alv_s[cj[j]] && dist[j] < INFINITY;
   }
-  float best_d, unused = 0.f;
-  int ni;
-  lane_argmin<CPL>(dist, ok, c0, &best_d, &ni, kMaxClusters);
-  quad_argmin(&best_d, &ni, &unused);
-  if (orphan && q == 0) w.assign_tok[o] = (int8_t)(ni < kMaxClusters ? ni : 0);
+  float best_d, second_d, unused = 0.f;
+  int ni, nri;
+  lane_top2<CPL>(dist, ok, c0, &best_d, &ni, &second_d, &nri, kMaxClusters);
+  quad_top2(&best_d, &ni, &second_d, &nri, &unused);
+  if (orphan && q == 0) {
+    w.assign_tok[o] = (int8_t)(ni < kMaxClusters ? ni : 0);
+    if (nri < kMaxClusters && near_tie(best_d, second_d))
+      log_tie(w, LOGKV_TIE_NEAREST, b, grp, -1, (int)pos, ni, nri, rel_gap(best_d, second_d), best_d);
+  }
 }
 
-// (value, index) argmax with the lowest index winning ties.
+// (value, index) argmax with the lowest index winning ties, plus the runner-up (for the
+// near-tie log).  merge() is symmetric, so every order of combining gives the same pair.
 struct ArgMax {
   float v;
   int i;
+  float v2;
+  int i2;
 };
-__device__ __forceinline__ ArgMax argmax_better(ArgMax a, ArgMax b) {
-  if (b.v > a.v || (b.v == a.v && b.i < a.i)) return b;
+__device__ __forceinline__ bool argmax_before(float v1, int i1, float v2, int i2) {
+  return v1 > v2 || (v1 == v2 && i1 < i2);
+}
+__device__ __forceinline__ ArgMax argmax_none() { return ArgMax{-INFINITY, 0x7fffffff, -INFINITY, 0x7fffffff}; }
+__device__ __forceinline__ ArgMax argmax_merge(ArgMax a, ArgMax b) {
+  if (argmax_before(b.v, b.i, a.v, a.i)) {
+    const ArgMax t = a;
+    a = b;
+    b = t;
+  }
+  // a holds the best head; the runner-up is the better of a's runner-up and b's head.
+  if (argmax_before(b.v, b.i, a.v2, a.i2)) {
+    a.v2 = b.v;
+    a.i2 = b.i;
+  }
   return a;
+}
+__device__ __forceinline__ ArgMax argmax_push(ArgMax a, float v, int i) {
+  return argmax_merge(a, ArgMax{v, i, -INFINITY, 0x7fffffff});
 }
 __device__ ArgMax block_argmax(ArgMax v, ArgMax* sh) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
@@ -217,13 +269,15 @@ __device__ ArgMax block_argmax(ArgMax v, ArgMax* sh) {
     ArgMax o;
     o.v = __shfl_xor_sync(0xffffffffu, v.v, off);
     o.i = __shfl_xor_sync(0xffffffffu, v.i, off);
-    v = argmax_better(v, o);
+    o.v2 = __shfl_xor_sync(0xffffffffu, v.v2, off);
+    o.i2 = __shfl_xor_sync(0xffffffffu, v.i2, off);
+    v = argmax_merge(v, o);
   }
   if (lane == 0) sh[warp] = v;
   __syncthreads();
   if (threadIdx.x == 0) {
     ArgMax best = sh[0];
-    for (int k = 1; k < nwarps; ++k) best = argmax_better(best, sh[k]);
+    for (int k = 1; k < nwarps; ++k) best = argmax_merge(best, sh[k]);
     sh[0] = best;
   }
   __syncthreads();
@@ -313,18 +367,21 @@ __global__ void __cluster_dims__(kSeedCluster, 1, 1) __launch_bounds__(512) seed
                   : Elem<T>::load(token_row<T>(g, snap, rec, b, grp, arch[t_lo + tl]) + d);
   };
   for (int i = 0; i < n_use; ++i) {
-    ArgMax a{-INFINITY, 0x7fffffff};
+    ArgMax a = argmax_none();
     for (int tl = tid; tl < nloc; tl += nt) {
       const int t = t_lo + tl;
       const float v = i == 0 ? (orph(t) ? swin_tok[arch[t]] : -INFINITY) : dist[tl];
-      a = argmax_better(a, ArgMax{v, t});
+      a = argmax_push(a, v, t);
     }
     a = block_argmax(a, red);
     if (tid == 0) slot[i & 1] = a;
     cluster.sync();
     if (tid == 0) {
-      ArgMax best{-INFINITY, 0x7fffffff};
-      for (int r = 0; r < kSeedCluster; ++r) best = argmax_better(best, *cluster.map_shared_rank(&slot[i & 1], r));
+      ArgMax best = argmax_none();
+      for (int r = 0; r < kSeedCluster; ++r) best = argmax_merge(best, *cluster.map_shared_rank(&slot[i & 1], r));
+      if (rank == 0 && best.i2 < na && near_tie(best.v, best.v2))
+        log_tie(w, LOGKV_TIE_SEED_PICK, b, grp, -1, i, (int)token_position(g, s, w, b, arch[best.i]),
+                (int)token_position(g, s, w, b, arch[best.i2]), rel_gap(best.v, best.v2), best.v);
       sh_pick = best.i;
       picks[i] = best.i;
     }
@@ -372,14 +429,24 @@ __global__ void __cluster_dims__(kSeedCluster, 1, 1) __launch_bounds__(512) seed
   __syncthreads();
   for (int tl = tid; tl < nloc; tl += nt) {
     if (!orph(t_lo + tl)) continue;
-    float best = INFINITY;
-    int bc = 0;
-    for (int c = 0; c < K; ++c)
-      if (cdist[tl * K + c] < best) {
-        best = cdist[tl * K + c];
+    float best = INFINITY, second = INFINITY;
+    int bc = 0, sc = -1;
+    for (int c = 0; c < K; ++c) {
+      const float dv = cdist[tl * K + c];
+      if (dv < best) {
+        second = best;
+        sc = best < INFINITY ? bc : -1;
+        best = dv;
         bc = c;
+      } else if (dv < second) {
+        second = dv;
+        sc = c;
       }
+    }
     asg[t_lo + tl] = (int8_t)bc;
+    if (sc >= 0 && near_tie(best, second))
+      log_tie(w, LOGKV_TIE_SEED_NEAREST, b, grp, -1, (int)token_position(g, s, w, b, arch[t_lo + tl]), bc, sc,
+              rel_gap(best, second), best);
   }
   __syncthreads();
   if (tid == 0)
