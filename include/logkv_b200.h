@@ -286,7 +286,8 @@ LOGKV_API int logkv_flush_profiled(const logkv_layout_t* layout, const logkv_sta
  * level rows read, [1] incoming rows read, [2] survivor rows written, [3] rows
  * appended, [4] rows zeroed, [5] merged rows carried up, [6] rows gathered for
  * delayed re-inserts, [7] flushes, [8] Beta groups whose cut was a near tie and
- * was decided by the canonical sequential evaluation.  The workspace must be
+ * was decided by the canonical sequential evaluation, [9] near-tie log entries,
+ * [10] lanes whose ladder cascade took the sequential level walk.  The workspace must be
  * zero-filled once when it is allocated.  workspace = NULL reads the counters of
  * the last logkv_flush_static on the current device.
  */

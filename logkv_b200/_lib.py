@@ -24,7 +24,7 @@ DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1}
 FLUSH_STAGES = ("snapshot", "span_cut", "score_attach", "choose", "seed_plan", "prepare", "cascade",
                 "pool_rewrite", "window_shift")
 COUNTERS = ("storage_read", "stage_read", "survivor", "fill", "clear", "carry", "gather", "flushes", "exact_cuts",
-            "ties")
+            "ties", "seq_lanes")
 TIE_KINDS = {1: "attach_cost", 2: "direct", 3: "nearest", 4: "seed_pick", 5: "seed_nearest", 6: "beta_cut",
              7: "alpha_order", 8: "alpha_swap"}
 

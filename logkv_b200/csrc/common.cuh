@@ -24,6 +24,7 @@ enum StatusBits : int32_t {
   kStatusListOverflow = 2,
   kStatusCandidateOverflow = 4,
   kStatusBadCluster = 8,
+  kStatusCopyTimeout = 16,   // a bounded wait for the kernel's own bulk copies gave up
 };
 
 __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }

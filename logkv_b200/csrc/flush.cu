@@ -14,6 +14,8 @@
 //   K8 window     window shift by the flushed tokens
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "flush_alpha.cuh"
@@ -26,7 +28,8 @@ namespace logkv {
 
 // Greedy span choice: per candidate density, size, rank, flags; victims in two buffers.
 static size_t choose_smem_bytes(const Geo& g) {
-  return (size_t)g.NC * (8 + 4 + 4 + 2) + 2 * (size_t)(g.P + 1) * (8 + 4 + 4) + (size_t)(g.P + 1) * (8 + 4) + 16;
+  return (size_t)g.NC * (8 + 4 + 4 + 2) + 2 * (size_t)(g.P + 1) * (8 + 4 + 4) + (size_t)(g.P + 1) * (8 + 4) + 16 +
+         (size_t)g.NC * (8 + 8 + 4 + 1) + 8;  // swap tests, closed-span order, swap flags
 }
 
 // Span scores (per warp: means, token energies, centre distances) and attach decisions
@@ -66,12 +69,54 @@ static void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-// Cascade launch for one (dtype, Beta, head dim) instantiation; DC = 0 is the runtime-D kernel.
+template <typename K>
+static void smem_limit(K* kern, size_t smem) {
+  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
+// Cascade launches for one (dtype, Beta, head dim) instantiation; DC = 0 is the runtime-D kernel.
+// Parallel: merges of every level at once, every level's survivor moves, then the sequential walk
+// of the lanes that need it (disjoint from the others).  Otherwise one sequential walk per lane.
 template <typename T, bool BETA, int DC>
-static void launch_cascade(const Geo& g, const logkv_state_t& s, const Work& w, size_t smem, cudaStream_t st) {
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(cascade_kernel<T, BETA, DC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  launch_pdl(cascade_kernel<T, BETA, DC>, dim3(g.K, g.G, g.B), kCascadeThreads, smem, st, g, s, w);
+static void launch_cascade(const Geo& g, const logkv_state_t& s, const Work& w, size_t smem, bool parallel,
+                           cudaStream_t st) {
+  if (!parallel) {
+    smem_limit(cascade_kernel<T, BETA, DC, false>, smem);
+    launch_pdl(cascade_kernel<T, BETA, DC, false>, dim3(g.K, g.G, g.B), kCascadeThreads, smem, st, g, s, w);
+    return;
+  }
+  const size_t ms = merge_smem(g.D, sizeof(T)), vs = move_smem(g.D, g.Bs, sizeof(T));
+  smem_limit(cascade_merge_kernel<T, BETA, DC>, ms);
+  launch_pdl(cascade_merge_kernel<T, BETA, DC>, dim3(kMergeCtas, g.K, g.B * g.G), kMergeWarps * 32, ms, st, g, s, w);
+  smem_limit(cascade_move_kernel<T>, vs);
+  launch_pdl(cascade_move_kernel<T>, dim3(g.L, g.K, g.B * g.G), kMoveThreads, vs, st, g, s, w);
+  smem_limit(cascade_kernel<T, BETA, DC, true>, smem);
+  launch_pdl(cascade_kernel<T, BETA, DC, true>, dim3(g.K, g.G, g.B), kCascadeThreads, smem, st, g, s, w);
+}
+
+// The parallel cascade needs one level's survivors (at most B' rows) in one CTA's shared memory
+// and B * G <= 65535; LOGKV_CASCADE=sequential forces the sequential walk (both paths give the
+// same bits; tests run both).
+static bool parallel_cascade(const Geo& g, size_t esize) {
+  const char* env = getenv("LOGKV_CASCADE");
+  if (env && strcmp(env, "sequential") == 0) return false;
+  return move_smem(g.D, g.Bs, esize) <= 227 * 1024 && merge_smem(g.D, esize) <= 227 * 1024 &&
+         (size_t)g.B * g.G <= 65535;
+}
+
+template <typename T>
+static void launch_cascade_all(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st) {
+  const size_t smem = cascade_smem(g, sizeof(T));
+  const bool par = parallel_cascade(g, sizeof(T));
+  if (g.beta) {
+    if (g.D == 128) launch_cascade<T, true, 128>(g, s, w, smem, par, st);
+    else if (g.D == 64) launch_cascade<T, true, 64>(g, s, w, smem, par, st);
+    else launch_cascade<T, true, 0>(g, s, w, smem, par, st);
+  } else {
+    if (g.D == 128) launch_cascade<T, false, 128>(g, s, w, smem, par, st);
+    else if (g.D == 64) launch_cascade<T, false, 64>(g, s, w, smem, par, st);
+    else launch_cascade<T, false, 0>(g, s, w, smem, par, st);
+  }
 }
 
 // Span scores: the block's warps stride over the (candidate, group) pairs of batch row
@@ -267,7 +312,7 @@ static Geo make_geo(const logkv_layout_t& L, int F, int recent_count) {
   g.NW = g.P + F;
   g.NC = g.P + F;
   g.recent_count = recent_count;
-  g.S = g.NW + g.K * g.L * g.Bs + 2 * g.K;
+  g.S = g.NW + g.K * g.L * g.Bs + g.K * (g.L + 2);
   g.sort_cap = next_pow2(g.L * g.Bs + g.NW);
   g.eta = L.eta;
   g.g0 = L.g0;
@@ -314,6 +359,8 @@ static size_t carve(const Geo& g, size_t esize, char* base, Work* w) {
   w->plan_m0 = c.take<int32_t>(B * G * K, 4);
   w->plan_scr = c.take<int32_t>(B * G * K, 4);
   w->plan_base = c.take<int64_t>(B * G * K, 8);
+  w->lane_mode = c.take<int32_t>(B * G * K, 4);
+  w->lane_plan = c.take<LevelPlan>(B * G * K * (size_t)g.L, sizeof(LevelPlan));
   w->sk = c.take<char>(B * G * 2 * S * D, esize);
   w->sv = c.take<char>(B * G * 2 * S * D, esize);
   w->sw = c.take<float>(B * G * 2 * S, 4);
@@ -434,16 +481,7 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   mark();
   launch_prepare<T>(g, s, w, st);
   mark();
-  const size_t casc_smem = cascade_smem(g, sizeof(T));
-  if (g.beta) {
-    if (g.D == 128) launch_cascade<T, true, 128>(g, s, w, casc_smem, st);
-    else if (g.D == 64) launch_cascade<T, true, 64>(g, s, w, casc_smem, st);
-    else launch_cascade<T, true, 0>(g, s, w, casc_smem, st);
-  } else {
-    if (g.D == 128) launch_cascade<T, false, 128>(g, s, w, casc_smem, st);
-    else if (g.D == 64) launch_cascade<T, false, 64>(g, s, w, casc_smem, st);
-    else launch_cascade<T, false, 0>(g, s, w, casc_smem, st);
-  }
+  launch_cascade_all<T>(g, s, w, st);
   mark();
   launch_pdl(pool_rewrite_kernel<T>, dim3(per_bg, g.G, g.B), 256, 0, st, g, s, w);
   mark();
@@ -470,16 +508,7 @@ static int launch_replay(const Geo& g, const logkv_state_t& s, const Work& w, co
   launch_pdl(tape_payload_kernel<T>, dim3(per_pay, g.G, g.B), 256, 0, st, g, s, tape, 0);
   launch_pdl(tape_copy_kernel, dim3(2 * sm_count), 256, 0, st, tape_segments(g, s, w, tape, false));
   launch_prepare<T>(g, s, w, st);
-  const size_t casc_smem = cascade_smem(g, sizeof(T));
-  if (g.beta) {
-    if (g.D == 128) launch_cascade<T, true, 128>(g, s, w, casc_smem, st);
-    else if (g.D == 64) launch_cascade<T, true, 64>(g, s, w, casc_smem, st);
-    else launch_cascade<T, true, 0>(g, s, w, casc_smem, st);
-  } else {
-    if (g.D == 128) launch_cascade<T, false, 128>(g, s, w, casc_smem, st);
-    else if (g.D == 64) launch_cascade<T, false, 64>(g, s, w, casc_smem, st);
-    else launch_cascade<T, false, 0>(g, s, w, casc_smem, st);
-  }
+  launch_cascade_all<T>(g, s, w, st);
   launch_pdl(pool_rewrite_kernel<T>, dim3(per_bg, g.G, g.B), 256, 0, st, g, s, w);
   const int rem = g.recent_count - g.F;
   const int per_win = std::max(1, std::min(128, (g.recent_count * g.D / (int)(16 / sizeof(T)) + 255) / 256));

@@ -414,12 +414,13 @@ __device__ __forceinline__ bool victim_less(double da, int ia, double db, int ib
 __device__ __forceinline__ bool ranked_less(double da, int ia, double db, int ib) {
   return da > db || (da == db && ia < ib);  // (-density, i) ascending
 }
-// Near tie of two float64 values (relative gap below the tie-log threshold).
-__device__ __forceinline__ bool near_tie_d(double a, double b, float* gap) {
+// Near tie of two float64 values (relative gap below the tie-log threshold), division-free.
+__device__ __forceinline__ bool near_tie_d(double a, double b) {
+  return fabs(a - b) < (double)kTieRel * fmax(fabs(a), fabs(b));
+}
+__device__ __forceinline__ float rel_gap_d(double a, double b) {
   const double den = fmax(fabs(a), fabs(b));
-  const double r = den > 0.0 ? fabs(a - b) / den : 0.0;
-  *gap = (float)r;
-  return r < (double)kTieRel;
+  return den > 0.0 ? (float)(fabs(a - b) / den) : 0.f;
 }
 
 __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t s, Work w) {
@@ -436,8 +437,12 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
   int* vi = vs + 2 * VC;                                     // [2][VC] victim candidate indices
   double* pls = reinterpret_cast<double*>(vi + 2 * VC);      // [VC] loss prefix, left to right
   int* psz = reinterpret_cast<int*>(pls + VC);               // [VC] inclusive size prefix
-  unsigned char* flags = reinterpret_cast<unsigned char*>(psz + VC);  // [NC]
+  double* swap_a = reinterpret_cast<double*>(psz + VC + (VC & 1));  // [NC] density * length of a swap test
+  double* swap_b = swap_a + NC;                              // [NC] the victims' loss it was tested against
+  int* uni = reinterpret_cast<int*>(swap_b + NC);            // [NC] closed candidates by (density, index)
+  unsigned char* flags = reinterpret_cast<unsigned char*>(uni + NC);  // [NC]
   unsigned char* chosen = flags + NC;                        // [NC]
+  unsigned char* swap_t = chosen + NC;                       // [NC] 0 untested, 1 rejected, 2 taken
   __shared__ int wsum[32];
   __shared__ int sh_nv, sh_nr, sh_room;
   if (tid == 0) {
@@ -484,6 +489,7 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
     const double sc = (double)sf;
     dens[i] = (flags[i] & 1) ? sc * 1.1 : sc * 1.0;
     chosen[i] = (!(flags[i] & 2)) || (flags[i] & 1);  // mandatory (open) or old
+    swap_t[i] = 0;
   }
   __syncthreads();
   // room = budget - sizes of mandatory and old spans; victim count (integers, any order)
@@ -555,23 +561,13 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
     ranked[rank] = i;
   }
   __syncthreads();
-  // Near ties of the two sorted orders the greedy walks (candidates by density, victims by
-  // density): two near-equal values of a sorted list are always neighbours in it.
-  for (int r = tid; r + 1 < sh_nr; r += nt) {
-    const int i = ranked[r], j = ranked[r + 1];
-    float gap;
-    if (near_tie_d(dens[i], dens[j], &gap))
-      log_tie(w, LOGKV_TIE_ALPHA_ORDER, b, -1, -1, r, min(i, j), max(i, j), gap, (float)dens[i]);
-  }
-  for (int r = tid; r + 1 < sh_nv; r += nt) {
-    float gap;
-    if (near_tie_d(vd[r], vd[r + 1], &gap))
-      log_tie(w, LOGKV_TIE_ALPHA_ORDER, b, -1, -1, r, min(vi[r], vi[r + 1]), max(vi[r], vi[r + 1]), gap,
-              (float)vd[r]);
-  }
+
   // Bounded greedy (alpha_log_kv.choose_spans) in one warp.  The number of victims a
   // candidate needs comes from an exact integer prefix scan of victim sizes; the float64
-  // loss over exactly those victims is summed by lane 0 in the reference's order.
+  // loss over exactly those victims is the loss prefix summed by lane 0 in the reference's
+  // order.  The walk takes candidates 32 at a time: a rejection leaves the victim list as it
+  // was, so the warp's lanes test 32 consecutive candidates against the current list at once,
+  // and only the first one taken changes it (the walk then goes on right after it).
   if (tid < 32) {
     const int lane = tid;
     const unsigned full = 0xffffffffu;
@@ -602,21 +598,6 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
       }
       __syncwarp();
     };
-    // First victim index j with room + psz[j] >= need: returns j + 1 (victims to remove) and
-    // the room they leave in `avail`, or -1 when all of them do not suffice.
-    auto need_prefix = [&](int need, int& avail) -> int {
-      for (int c0 = 0; c0 < nv; c0 += 32) {
-        const int j = c0 + lane;
-        const unsigned hit = __ballot_sync(full, j < nv && room + psz[j] >= need);
-        if (hit) {
-          const int f = c0 + __ffs(hit) - 1;
-          avail = room + psz[f];
-          return f + 1;
-        }
-      }
-      avail = nv ? room + psz[nv - 1] : room;
-      return -1;
-    };
     // Remove the first k victims and insert (di, length, i) at its sorted place.
     auto rebuild = [&](int k, double di, int length, int i) {
       const bool ins = true;
@@ -627,16 +608,6 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
           const int j = c0 + lane;
           at += __popc(__ballot_sync(full, j < nv && victim_less(vd[cur * VC + j], vi[cur * VC + j], di, i)));
         }
-      if (lane == 0) {
-        // The new victim's neighbours in the density order it is inserted into.
-        float gap;
-        for (int nb = -1; nb <= 0; ++nb) {
-          const int j = k + at + nb;
-          if (j >= k && j < nv && near_tie_d(vd[cur * VC + j], di, &gap))
-            log_tie(w, LOGKV_TIE_ALPHA_ORDER, b, -1, -1, j, min(i, vi[cur * VC + j]), max(i, vi[cur * VC + j]),
-                    gap, (float)di);
-        }
-      }
       const int nn = nv - k + (ins ? 1 : 0), nx = cur ^ 1;
       for (int j = lane; j < nn; j += 32) {
         int src = -1;
@@ -659,34 +630,74 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
       prefixes();
     };
     prefixes();
-    for (int q0 = 0; q0 < nr; q0 += 32) {
-      const int qi = q0 + lane < nr ? ranked[q0 + lane] : 0;
-      const double qd = dens[qi];
-      const int qs = size[qi];
-      const int cnt = min(32, nr - q0);
-      for (int t = 0; t < cnt; ++t) {
-        const int i = __shfl_sync(full, qi, t);
-        const double di = __shfl_sync(full, qd, t);
-        const int length = __shfl_sync(full, qs, t);
-        int nrem = 0, available = room;
-        bool ok = room >= length;
-        if (!ok) {
-          nrem = need_prefix(length, available);
-          if (nrem > 0) {
-            ok = di * (double)length > pls[nrem - 1];
-            float gap;
-            if (lane == 0 && near_tie_d(di * (double)length, pls[nrem - 1], &gap))
-              log_tie(w, LOGKV_TIE_ALPHA_SWAP, b, -1, -1, i, i, ok ? 1 : 0, gap, (float)(di * (double)length));
+    int q = 0;
+    while (q < nr) {
+      const int j = q + lane;
+      int i = 0, length = 0, nrem = 0, avail = room;
+      double di = 0.0;
+      bool take = false, tested = false;
+      if (j < nr) {
+        i = ranked[j];
+        di = dens[i];
+        length = size[i];
+        if (room >= length) {
+          take = true;
+        } else if (nv > 0 && room + psz[nv - 1] >= length) {
+          int lo = 0, hi = nv - 1;   // first victim index with room + psz >= length
+          while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (room + psz[mid] >= length) hi = mid;
+            else lo = mid + 1;
           }
-        }
-        if (ok) {
-          if (lane == 0) chosen[i] = 1;
-          rebuild(nrem, di, length, i);
-          room = available - length;
+          nrem = lo + 1;
+          avail = room + psz[lo];
+          take = di * (double)length > pls[lo];
+          tested = true;
         }
       }
+      const unsigned hit = __ballot_sync(full, take);
+      const int f = hit ? __ffs(hit) - 1 : 32;   // first candidate taken in this chunk (32: none)
+      if (tested && lane <= f) {   // the candidates decided here; checked for near ties after the walk
+        swap_a[i] = di * (double)length;
+        swap_b[i] = pls[nrem - 1];
+        swap_t[i] = take ? 2 : 1;
+      }
+      if (!hit) {
+        q += 32;
+        continue;
+      }
+      const int ti = __shfl_sync(full, i, f), tlen = __shfl_sync(full, length, f);
+      const int trem = __shfl_sync(full, nrem, f), tavail = __shfl_sync(full, avail, f);
+      const double tdi = __shfl_sync(full, di, f);
+      if (lane == 0) chosen[ti] = 1;
+      rebuild(trem, tdi, tlen, ti);
+      room = tavail - tlen;
+      q += f + 1;
     }
   }
+  // Near ties of the walk, logged after it.  Every density comparison of the greedy (the victim
+  // and candidate orders, a victim's insertion among the others) is between two closed spans;
+  // two near-equal densities are neighbours in the closed spans' (density, index) order.
+  for (int i = tid; i < n; i += nt) {
+    if (!(flags[i] & 2)) continue;
+    int rank = 0;
+    for (int j = 0; j < n; ++j)
+      if ((flags[j] & 2) && victim_less(dens[j], j, dens[i], i)) ++rank;
+    uni[rank] = i;
+  }
+  __syncthreads();
+  int nclosed = 0;
+  for (int i = 0; i < n; ++i) nclosed += (flags[i] & 2) ? 1 : 0;
+  for (int r = tid; r + 1 < nclosed; r += nt) {
+    const int i = uni[r], j = uni[r + 1];
+    if (near_tie_d(dens[i], dens[j]))
+      log_tie(w, LOGKV_TIE_ALPHA_ORDER, b, -1, -1, r, min(i, j), max(i, j), rel_gap_d(dens[i], dens[j]),
+              (float)dens[i]);
+  }
+  for (int i = tid; i < n; i += nt)
+    if (swap_t[i] && near_tie_d(swap_a[i], swap_b[i]))
+      log_tie(w, LOGKV_TIE_ALPHA_SWAP, b, -1, -1, i, i, swap_t[i] == 2 ? 1 : 0, rel_gap_d(swap_a[i], swap_b[i]),
+              (float)swap_a[i]);
   __syncthreads();
   // Emit keep/archive token lists in candidate order and the new span table.
   int carry_keep = 0, carry_arch = 0, carry_sp = 0;

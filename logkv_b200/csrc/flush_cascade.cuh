@@ -184,14 +184,234 @@ __device__ int beta_cut_warp(const T* tk, const T* tv, const Meta* tm, int start
   return best == 0 ? 2 : (best == 1 ? 1 : 3);
 }
 
+// Merges of pool rows [t0, mend) of level `ell` (staged in shared memory as rows 0.. of tk / tv /
+// tm) into merged rows t0 / 2 + j of scratch buffer `out_buf`, counted from row `out_off` of the
+// lane's range: pairwise count-weighted merges, or Beta 4->2 cuts (certified warp cut, canonical
+// order on near ties, recorded / replayed cuts under an update tape).  Called by the whole block.
+template <typename T, bool BETA, int DC>
+__device__ void merge_tile(const LaneCtx<T>& x, const Geo& g, const Work& w, const T* tk, const T* tv,
+                           const Meta* tm, int t0, int mend, int npair, int ell, int out_buf, int out_off,
+                           float (*bloss)[12], float (*bener)[2], int* bcut, int* sh_exact) {
+  constexpr int VN = Vec<T>::N;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int D = DC ? DC : g.D, DV = D / VN;
+  T* SK = static_cast<T*>(w.sk);
+  T* SV = static_cast<T*>(w.sv);
+    if (!BETA) {
+      const int j0 = t0 / 2, jn = (mend - t0) / 2;
+      for (int item = tid; item < jn * DV * 2; item += nt) {
+        const int j = item / (2 * DV), f = (item / DV) & 1, v = item % DV;
+        const int ra = 2 * j, rb = 2 * j + 1;
+        const float wa = tm[ra].w, wb = tm[rb].w;
+        const float alpha = fdiv(wa, fmaxf(fadd(wa, wb), 1e-8f));
+        const float beta = fsub(1.f, alpha);
+        const T* base = f ? tv : tk;
+        float a[VN], b[VN], o[VN];
+        unpack(*reinterpret_cast<const uint4*>(base + ra * D + v * VN), a, (const T*)nullptr);
+        unpack(*reinterpret_cast<const uint4*>(base + rb * D + v * VN), b, (const T*)nullptr);
+#pragma unroll
+        for (int e = 0; e < VN; ++e) o[e] = fadd(fmul(alpha, a[e]), fmul(beta, b[e]));
+        *reinterpret_cast<uint4*>((f ? SV : SK) + x.scr_row(out_buf, out_off + j0 + j) * D + v * VN) = pack(o, (const T*)nullptr);
+      }
+      for (int j = tid; j < jn; j += nt) x.put_scratch(out_buf, out_off + j0 + j, merge_meta(tm[2 * j], tm[2 * j + 1]));
+    } else {
+      const int qn = (mend - t0 + 3) / 4;  // groups of this tile (tile rows 4q..4q+3)
+      // Recorded cuts of this (lane, level, tile): written when recording, read when replaying.
+      uint8_t* tcut = g.tape != kTapeNone
+                          ? w.tape_cuts + ((size_t)x.lane * g.L + ell) * tape_cut_stride(g) + t0 / 4
+                          : nullptr;
+      if (g.tape == kTapeReplay) {
+        for (int q = tid; q < qn; q += nt) bcut[q] = tcut[q];
+        __syncthreads();
+      } else {
+      // Certified warp-parallel cut per group; near ties fall back to the canonical order below.
+      const int warp = tid >> 5, lane = tid & 31, nwarps = nt >> 5;
+      for (int q = warp; q < qn; q += nwarps) {
+        const int width = min(4, npair - (t0 + 4 * q));
+        const int cut = width == 4 ? beta_cut_warp<T, DC>(tk, tv, tm, 4 * q, D, lane) : 1;
+        if (lane == 0) {
+          bcut[q] = cut;
+          if (cut < 0) atomicAdd(sh_exact, 1);
+        }
+      }
+      __syncthreads();
+      if (*sh_exact) {
+      for (int item = tid; item < qn * 14; item += nt) {
+        const int q = item / 14, k = item % 14;
+        const int start = 4 * q;
+        const int width = min(4, npair - (t0 + start));
+        if (width != 4 || bcut[q] >= 0) continue;
+        float wv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) wv[i] = tm[start + i].w;
+        const int comp = k < 12 ? k / 6 : k - 12;
+        const T* base = comp == 0 ? tk : tv;
+        if (k >= 12) {
+          float e[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+          for (int d = 0; d < D; ++d)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float xv = Elem<T>::load(base + (start + i) * D + d);
+              e[i] = fadd(e[i], fmul(xv, xv));
+            }
+          float tot = 0.f, acc = 0.f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) tot = fadd(tot, wv[i]);
+          tot = fmaxf(tot, 1e-12f);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc = fadd(acc, fmul(e[i], wv[i]));
+          bener[q][comp] = fmaxf(fdiv(acc, tot), 1e-12f);
+        } else {
+          const int j = (k % 6) / 2, side = k % 2;
+          const int cut = j == 0 ? 2 : (j == 1 ? 1 : 3);
+          float om[4];
+          float ws = 0.f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const bool in = side == 0 ? (i < cut) : (i >= cut);
+            om[i] = fmul(wv[i], in ? 1.f : 0.f);
+            ws = fadd(ws, om[i]);
+          }
+          const float den = fmaxf(ws, 1e-12f);
+          float r[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+          for (int d = 0; d < D; ++d) {
+            float xv[4];
+            float sacc = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              xv[i] = Elem<T>::load(base + (start + i) * D + d);
+              sacc = fadd(sacc, fmul(xv[i], om[i]));
+            }
+            const float mean = fdiv(sacc, den);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float df = fsub(xv[i], mean);
+              r[i] = fadd(r[i], fmul(df, df));
+            }
+          }
+          float loss = 0.f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) loss = fadd(loss, fmul(r[i], om[i]));
+          bloss[q][k] = loss;
+        }
+      }
+      __syncthreads();
+      for (int q = tid; q < qn; q += nt) {
+        if (bcut[q] >= 0) continue;
+        float costs[3] = {0.f, 0.f, 0.f};
+        for (int comp = 0; comp < 2; ++comp)
+          for (int j = 0; j < 3; ++j)
+            for (int side = 0; side < 2; ++side)
+              costs[j] = fadd(costs[j], fdiv(bloss[q][comp * 6 + j * 2 + side], bener[q][comp]));
+        int best = 0;
+        if (costs[1] < costs[best]) best = 1;
+        if (costs[2] < costs[best]) best = 2;
+        bcut[q] = best == 0 ? 2 : (best == 1 ? 1 : 3);
+        // Runner-up (earlier cut on equal costs) for the near-tie log.
+        const int r = best == 0 ? (costs[2] < costs[1] ? 2 : 1) : (best == 1 ? (costs[2] < costs[0] ? 2 : 0)
+                                                                              : (costs[1] < costs[0] ? 1 : 0));
+        if (near_tie(costs[best], costs[r]))
+          log_tie(w, LOGKV_TIE_BETA_CUT, x.b, x.grp, x.c, ell * 65536 + (t0 + 4 * q) / 4, bcut[q],
+                  r == 0 ? 2 : (r == 1 ? 1 : 3), rel_gap(costs[best], costs[r]), costs[best]);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        atomicAdd(&w.counters[kCntExactCuts], (unsigned long long)*sh_exact);
+        *sh_exact = 0;
+      }
+      }
+      if (g.tape == kTapeRecord)
+        for (int q = tid; q < qn; q += nt) tcut[q] = (uint8_t)bcut[q];
+      }
+      // Apply: per output side, sum over member rows (row order) of w*x / max(mass, 1e-12).
+      // One item computes both sides of a (group, component, 16-byte column) from one load
+      // of each member row; each side keeps its own products (x * 0 for rows of the other
+      // side) and sums in row order.  Groups are 4 rows wide, or 2 (the tail: one side).
+      for (int item = tid; item < qn * 2 * DV; item += nt) {
+        const int q = item / (2 * DV), f = (item / DV) & 1, v = item % DV;
+        const int start = 4 * q;
+        const int width = min(4, npair - (t0 + start));
+        const bool two = width == 4;
+        const int cut = bcut[q];
+        const T* base = f ? tv : tk;
+        float acc0[VN], acc1[VN], mass0 = 0.f, mass1 = 0.f;
+#pragma unroll
+        for (int e = 0; e < VN; ++e) acc0[e] = acc1[e] = 0.f;
+        for (int i = 0; i < 4; ++i) {
+          const bool valid = i < width;
+          const bool in0 = valid && (!two || i < cut), in1 = valid && two && i >= cut;
+          const float wi = valid ? tm[start + i].w : 0.f;
+          const float om0 = fmul(wi, in0 ? 1.f : 0.f), om1 = fmul(wi, in1 ? 1.f : 0.f);
+          float xr[VN];
+          if (valid) {
+            unpack(*reinterpret_cast<const uint4*>(base + (start + i) * D + v * VN), xr, (const T*)nullptr);
+          } else {
+#pragma unroll
+            for (int e = 0; e < VN; ++e) xr[e] = 0.f;
+          }
+          mass0 = fadd(mass0, om0);
+          mass1 = fadd(mass1, om1);
+#pragma unroll
+          for (int e = 0; e < VN; ++e) {
+            acc0[e] = fadd(acc0[e], fmul(xr[e], om0));
+            acc1[e] = fadd(acc1[e], fmul(xr[e], om1));
+          }
+        }
+        const float den0 = fmaxf(mass0, 1e-12f);
+#pragma unroll
+        for (int e = 0; e < VN; ++e) acc0[e] = fdiv(acc0[e], den0);
+        const int outrow = (t0 + start) / 2;
+        *reinterpret_cast<uint4*>((f ? SV : SK) + x.scr_row(out_buf, out_off + outrow) * D + v * VN) = pack(acc0, (const T*)nullptr);
+        if (two) {
+          const float den1 = fmaxf(mass1, 1e-12f);
+#pragma unroll
+          for (int e = 0; e < VN; ++e) acc1[e] = fdiv(acc1[e], den1);
+          *reinterpret_cast<uint4*>((f ? SV : SK) + x.scr_row(out_buf, out_off + outrow + 1) * D + v * VN) =
+              pack(acc1, (const T*)nullptr);
+        }
+      }
+      for (int item = tid; item < qn * 2; item += nt) {
+        const int q = item / 2, side = item % 2;
+        const int start = 4 * q;
+        const int width = min(4, npair - (t0 + start));
+        if (side == 1 && width != 4) continue;
+        const int cut = bcut[q];
+        float mass = 0.f;
+        int64_t lo = INT64_MAX, hi = INT64_MIN, swp = 0, ord = INT64_MAX;
+        uint8_t pad = 1;
+        for (int i = 0; i < width; ++i) {
+          const bool in = width == 2 ? side == 0 : (side == 0 ? i < cut : i >= cut);
+          const Meta& r = tm[start + i];
+          mass = fadd(mass, fmul(r.w, in ? 1.f : 0.f));
+          if (!in) continue;
+          if (r.w > 0.f) {
+            lo = min(lo, r.lo);
+            hi = max(hi, r.hi);
+          }
+          swp += r.swp;
+          ord = min(ord, r.ord);
+          pad &= r.pad;
+        }
+        x.put_scratch(out_buf, out_off + (t0 + start) / 2 + side,
+                      Meta{mass, mass > 0.f ? lo : 0, mass > 0.f ? hi : 0, swp, ord, pad});
+      }
+    }
+}
+
 constexpr int kCascadeThreads = 256;  // two CTAs per SM (registers and shared memory)
 
-template <typename T, bool BETA, int DC>
+// Sequential level walk, one CTA per lane: every level in order, each overflowing level's pool
+// streamed through double-buffered tiles.  SEQ_ONLY: only the lanes the parallel merge kernel
+// left to it (lane_mode 2).
+template <typename T, bool BETA, int DC, bool SEQ_ONLY>
 __global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logkv_state_t s, Work w) {
   pdl_entry();
   LaneCtx<T> x = make_ctx<T>(g, s, w);
   const int type = w.plan_type[x.lane];
   if (type == kJobNone) return;
+  if (SEQ_ONLY && w.lane_mode[x.lane] != 2) return;
   constexpr int VN = Vec<T>::N;
   const int tid = threadIdx.x, nt = blockDim.x, Bs = g.Bs;
   // Compile-time head dim when DC != 0: every row/vector index map becomes shifts.
@@ -376,209 +596,8 @@ __global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logk
       // reader (tile t0 + 2 tiles) issues after the next iteration's barrier.
       if (t0 + 2 * kTileRows < total) resolve(t0 + 2 * kTileRows, cur);
       const int mend = min(t0 + tn, npair);  // merge rows of this tile: [t0, mend)
-      if (mend > t0) {
-        if (!BETA) {
-          const int j0 = t0 / 2, jn = (mend - t0) / 2;
-          for (int item = tid; item < jn * DV * 2; item += nt) {
-            const int j = item / (2 * DV), f = (item / DV) & 1, v = item % DV;
-            const int ra = 2 * j, rb = 2 * j + 1;
-            const float wa = tm[ra].w, wb = tm[rb].w;
-            const float alpha = fdiv(wa, fmaxf(fadd(wa, wb), 1e-8f));
-            const float beta = fsub(1.f, alpha);
-            const T* base = f ? tv : tk;
-            float a[VN], b[VN], o[VN];
-            unpack(*reinterpret_cast<const uint4*>(base + ra * D + v * VN), a, (const T*)nullptr);
-            unpack(*reinterpret_cast<const uint4*>(base + rb * D + v * VN), b, (const T*)nullptr);
-#pragma unroll
-            for (int e = 0; e < VN; ++e) o[e] = fadd(fmul(alpha, a[e]), fmul(beta, b[e]));
-            *reinterpret_cast<uint4*>((f ? SV : SK) + x.scr_row(nb, j0 + j) * D + v * VN) = pack(o, (const T*)nullptr);
-          }
-          for (int j = tid; j < jn; j += nt) x.put_scratch(nb, j0 + j, merge_meta(tm[2 * j], tm[2 * j + 1]));
-        } else {
-          const int qn = (mend - t0 + 3) / 4;  // groups of this tile (tile rows 4q..4q+3)
-          // Recorded cuts of this (lane, level, tile): written when recording, read when replaying.
-          uint8_t* tcut = g.tape != kTapeNone
-                              ? w.tape_cuts + ((size_t)x.lane * g.L + ell) * tape_cut_stride(g) + t0 / 4
-                              : nullptr;
-          if (g.tape == kTapeReplay) {
-            for (int q = tid; q < qn; q += nt) bcut[q] = tcut[q];
-            __syncthreads();
-          } else {
-          // Certified warp-parallel cut per group; near ties fall back to the canonical order below.
-          const int warp = tid >> 5, lane = tid & 31, nwarps = nt >> 5;
-          for (int q = warp; q < qn; q += nwarps) {
-            const int width = min(4, npair - (t0 + 4 * q));
-            const int cut = width == 4 ? beta_cut_warp<T, DC>(tk, tv, tm, 4 * q, D, lane) : 1;
-            if (lane == 0) {
-              bcut[q] = cut;
-              if (cut < 0) atomicAdd(&sh_exact, 1);
-            }
-          }
-          __syncthreads();
-          if (sh_exact) {
-          for (int item = tid; item < qn * 14; item += nt) {
-            const int q = item / 14, k = item % 14;
-            const int start = 4 * q;
-            const int width = min(4, npair - (t0 + start));
-            if (width != 4 || bcut[q] >= 0) continue;
-            float wv[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) wv[i] = tm[start + i].w;
-            const int comp = k < 12 ? k / 6 : k - 12;
-            const T* base = comp == 0 ? tk : tv;
-            if (k >= 12) {
-              float e[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-              for (int d = 0; d < D; ++d)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const float xv = Elem<T>::load(base + (start + i) * D + d);
-                  e[i] = fadd(e[i], fmul(xv, xv));
-                }
-              float tot = 0.f, acc = 0.f;
-#pragma unroll
-              for (int i = 0; i < 4; ++i) tot = fadd(tot, wv[i]);
-              tot = fmaxf(tot, 1e-12f);
-#pragma unroll
-              for (int i = 0; i < 4; ++i) acc = fadd(acc, fmul(e[i], wv[i]));
-              bener[q][comp] = fmaxf(fdiv(acc, tot), 1e-12f);
-            } else {
-              const int j = (k % 6) / 2, side = k % 2;
-              const int cut = j == 0 ? 2 : (j == 1 ? 1 : 3);
-              float om[4];
-              float ws = 0.f;
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const bool in = side == 0 ? (i < cut) : (i >= cut);
-                om[i] = fmul(wv[i], in ? 1.f : 0.f);
-                ws = fadd(ws, om[i]);
-              }
-              const float den = fmaxf(ws, 1e-12f);
-              float r[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 4
-              for (int d = 0; d < D; ++d) {
-                float xv[4];
-                float sacc = 0.f;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  xv[i] = Elem<T>::load(base + (start + i) * D + d);
-                  sacc = fadd(sacc, fmul(xv[i], om[i]));
-                }
-                const float mean = fdiv(sacc, den);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                  const float df = fsub(xv[i], mean);
-                  r[i] = fadd(r[i], fmul(df, df));
-                }
-              }
-              float loss = 0.f;
-#pragma unroll
-              for (int i = 0; i < 4; ++i) loss = fadd(loss, fmul(r[i], om[i]));
-              bloss[q][k] = loss;
-            }
-          }
-          __syncthreads();
-          for (int q = tid; q < qn; q += nt) {
-            if (bcut[q] >= 0) continue;
-            float costs[3] = {0.f, 0.f, 0.f};
-            for (int comp = 0; comp < 2; ++comp)
-              for (int j = 0; j < 3; ++j)
-                for (int side = 0; side < 2; ++side)
-                  costs[j] = fadd(costs[j], fdiv(bloss[q][comp * 6 + j * 2 + side], bener[q][comp]));
-            int best = 0;
-            if (costs[1] < costs[best]) best = 1;
-            if (costs[2] < costs[best]) best = 2;
-            bcut[q] = best == 0 ? 2 : (best == 1 ? 1 : 3);
-            // Runner-up (earlier cut on equal costs) for the near-tie log.
-            const int r = best == 0 ? (costs[2] < costs[1] ? 2 : 1) : (best == 1 ? (costs[2] < costs[0] ? 2 : 0)
-                                                                                  : (costs[1] < costs[0] ? 1 : 0));
-            if (near_tie(costs[best], costs[r]))
-              log_tie(w, LOGKV_TIE_BETA_CUT, x.b, x.grp, x.c, ell * 65536 + (t0 + 4 * q) / 4, bcut[q],
-                      r == 0 ? 2 : (r == 1 ? 1 : 3), rel_gap(costs[best], costs[r]), costs[best]);
-          }
-          __syncthreads();
-          if (tid == 0) {
-            atomicAdd(&w.counters[kCntExactCuts], (unsigned long long)sh_exact);
-            sh_exact = 0;
-          }
-          }
-          if (g.tape == kTapeRecord)
-            for (int q = tid; q < qn; q += nt) tcut[q] = (uint8_t)bcut[q];
-          }
-          // Apply: per output side, sum over member rows (row order) of w*x / max(mass, 1e-12).
-          // One item computes both sides of a (group, component, 16-byte column) from one load
-          // of each member row; each side keeps its own products (x * 0 for rows of the other
-          // side) and sums in row order.  Groups are 4 rows wide, or 2 (the tail: one side).
-          for (int item = tid; item < qn * 2 * DV; item += nt) {
-            const int q = item / (2 * DV), f = (item / DV) & 1, v = item % DV;
-            const int start = 4 * q;
-            const int width = min(4, npair - (t0 + start));
-            const bool two = width == 4;
-            const int cut = bcut[q];
-            const T* base = f ? tv : tk;
-            float acc0[VN], acc1[VN], mass0 = 0.f, mass1 = 0.f;
-#pragma unroll
-            for (int e = 0; e < VN; ++e) acc0[e] = acc1[e] = 0.f;
-            for (int i = 0; i < 4; ++i) {
-              const bool valid = i < width;
-              const bool in0 = valid && (!two || i < cut), in1 = valid && two && i >= cut;
-              const float wi = valid ? tm[start + i].w : 0.f;
-              const float om0 = fmul(wi, in0 ? 1.f : 0.f), om1 = fmul(wi, in1 ? 1.f : 0.f);
-              float xr[VN];
-              if (valid) {
-                unpack(*reinterpret_cast<const uint4*>(base + (start + i) * D + v * VN), xr, (const T*)nullptr);
-              } else {
-#pragma unroll
-                for (int e = 0; e < VN; ++e) xr[e] = 0.f;
-              }
-              mass0 = fadd(mass0, om0);
-              mass1 = fadd(mass1, om1);
-#pragma unroll
-              for (int e = 0; e < VN; ++e) {
-                acc0[e] = fadd(acc0[e], fmul(xr[e], om0));
-                acc1[e] = fadd(acc1[e], fmul(xr[e], om1));
-              }
-            }
-            const float den0 = fmaxf(mass0, 1e-12f);
-#pragma unroll
-            for (int e = 0; e < VN; ++e) acc0[e] = fdiv(acc0[e], den0);
-            const int outrow = (t0 + start) / 2;
-            *reinterpret_cast<uint4*>((f ? SV : SK) + x.scr_row(nb, outrow) * D + v * VN) = pack(acc0, (const T*)nullptr);
-            if (two) {
-              const float den1 = fmaxf(mass1, 1e-12f);
-#pragma unroll
-              for (int e = 0; e < VN; ++e) acc1[e] = fdiv(acc1[e], den1);
-              *reinterpret_cast<uint4*>((f ? SV : SK) + x.scr_row(nb, outrow + 1) * D + v * VN) =
-                  pack(acc1, (const T*)nullptr);
-            }
-          }
-          for (int item = tid; item < qn * 2; item += nt) {
-            const int q = item / 2, side = item % 2;
-            const int start = 4 * q;
-            const int width = min(4, npair - (t0 + start));
-            if (side == 1 && width != 4) continue;
-            const int cut = bcut[q];
-            float mass = 0.f;
-            int64_t lo = INT64_MAX, hi = INT64_MIN, swp = 0, ord = INT64_MAX;
-            uint8_t pad = 1;
-            for (int i = 0; i < width; ++i) {
-              const bool in = width == 2 ? side == 0 : (side == 0 ? i < cut : i >= cut);
-              const Meta& r = tm[start + i];
-              mass = fadd(mass, fmul(r.w, in ? 1.f : 0.f));
-              if (!in) continue;
-              if (r.w > 0.f) {
-                lo = min(lo, r.lo);
-                hi = max(hi, r.hi);
-              }
-              swp += r.swp;
-              ord = min(ord, r.ord);
-              pad &= r.pad;
-            }
-            x.put_scratch(nb, (t0 + start) / 2 + side,
-                          Meta{mass, mass > 0.f ? lo : 0, mass > 0.f ? hi : 0, swp, ord, pad});
-          }
-        }
-      }
+      if (mend > t0)
+        merge_tile<T, BETA, DC>(x, g, w, tk, tv, tm, t0, mend, npair, ell, nb, 0, bloss, bener, bcut, &sh_exact);
       // Survivors of this tile: pool row p >= npair -> slot p - npair.
       const int sbeg = max(t0, npair);
       const int sn = t0 + tn - sbeg;
@@ -615,6 +634,463 @@ __global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logk
     st.buf = nb;
     st.m = ncarry;
     nb = 1 - nb;
+  }
+}
+
+// ---------------------------------------------------------------- parallel cascade
+// What every level of one lane does in this flush, from its counts and the lane's incoming row
+// count: the sequential walk's control flow without touching a row.  In the steady state every
+// level's merges read only that level's stored rows (level 0 also its incoming tokens), so the
+// merges of all levels run at once (cascade_merge_kernel: carries of level l land in scratch
+// buffer 1 as level l + 1's incoming rows) and then every level moves its survivors
+// (cascade_move_kernel).  A level >= 1 whose merges would read incoming rows (carries of the
+// level below) and the top level's fold need the levels in order: such lanes take the
+// sequential walk.
+// Block-wide: the lane's plan (written by the prepare kernel) into lp, its mode returned to every
+// thread.  L2-coherent loads: the move kernel reads the plan before its grid dependency wait.
+__device__ int plan_lane(const Geo& g, const Work& w, size_t lane, LevelPlan* lp) {
+  __shared__ int sh_mode;
+  const int tid = threadIdx.x;
+  if (tid < g.L) {
+    const int* src = reinterpret_cast<const int*>(w.lane_plan + lane * g.L + tid);
+    lp[tid] = LevelPlan{__ldcg(src), __ldcg(src + 1), __ldcg(src + 2), __ldcg(src + 3), __ldcg(src + 4),
+                        __ldcg(src + 5)};
+  }
+  if (tid == 32) sh_mode = __ldcg(w.lane_mode + lane);
+  __syncthreads();
+  return sh_mode;
+}
+
+// Source rows and metadata of pool row p of level l: a stored slot (p < cnt), else incoming row
+// p - cnt: the lane's tokens (level 0, ordinary / new jobs), its staged re-inserts (level 0,
+// delayed jobs: scratch buffer 0) or the carries of level l - 1 (scratch buffer 1).
+template <typename T>
+struct PoolRow {
+  const T* k;
+  const T* v;
+  Meta m;
+};
+template <typename T>
+__device__ PoolRow<T> pool_row(const LaneCtx<T>& x, const LevelPlan& p, int l, int row, bool late) {
+  const Geo& g = x.g;
+  if (row < p.cnt) {
+    const size_t r = x.level_row(l, row);
+    return PoolRow<T>{static_cast<const T*>(x.s.level_k) + r * g.D, static_cast<const T*>(x.s.level_v) + r * g.D,
+                      Meta{x.s.level_w[r], x.s.level_p_lo[r], x.s.level_p_hi[r], x.s.level_sum_wp[r],
+                           x.s.level_order[r], x.s.pad_mask[r]}};
+  }
+  const int i = row - p.cnt;
+  Stage st{late || l > 0 ? 1 : 0, l > 0 ? 1 : 0, p.m};
+  const int si = l > 0 ? p.in_off + i : i;
+  return PoolRow<T>{x.stage_k(st, si), x.stage_v(st, si), st.kind == 0 ? x.stage_meta(st, i) : x.stage_meta(st, si)};
+}
+
+// Canonical-order cut of one 4-row group by one warp (the near-tie fallback of beta_cut_warp):
+// lanes 0..11 each sum one (component, cut, side) loss, lanes 12..13 one component's energy, in
+// the reference's order (beta_log_kv.select_cuts); the costs are then added comp-major as there.
+// Returns the cut (2, 1 or 3); *best / *second / *second_cut describe the argmin for the tie log.
+template <typename T, int DC>
+__device__ int beta_cut_canonical_warp(const T* gk, const T* gv, const Meta* gm, int Drt, int lane, float* best_cost,
+                                       float* second_cost, int* second_cut) {
+  const int D = DC ? DC : Drt;
+  float wv[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) wv[i] = gm[i].w;
+  float val = 0.f;
+  if (lane < 14) {
+    const int k = lane;
+    const int comp = k < 12 ? k / 6 : k - 12;
+    const T* base = comp == 0 ? gk : gv;
+    if (k >= 12) {
+      float e[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int d = 0; d < D; ++d)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float xv = Elem<T>::load(base + i * D + d);
+          e[i] = fadd(e[i], fmul(xv, xv));
+        }
+      float tot = 0.f, acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) tot = fadd(tot, wv[i]);
+      tot = fmaxf(tot, 1e-12f);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc = fadd(acc, fmul(e[i], wv[i]));
+      val = fmaxf(fdiv(acc, tot), 1e-12f);
+    } else {
+      const int j = (k % 6) / 2, side = k % 2;
+      const int cut = j == 0 ? 2 : (j == 1 ? 1 : 3);
+      float om[4];
+      float ws = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const bool in = side == 0 ? (i < cut) : (i >= cut);
+        om[i] = fmul(wv[i], in ? 1.f : 0.f);
+        ws = fadd(ws, om[i]);
+      }
+      const float den = fmaxf(ws, 1e-12f);
+      float r[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int d = 0; d < D; ++d) {
+        float xv[4];
+        float sacc = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          xv[i] = Elem<T>::load(base + i * D + d);
+          sacc = fadd(sacc, fmul(xv[i], om[i]));
+        }
+        const float mean = fdiv(sacc, den);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float df = fsub(xv[i], mean);
+          r[i] = fadd(r[i], fmul(df, df));
+        }
+      }
+      float loss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) loss = fadd(loss, fmul(r[i], om[i]));
+      val = loss;
+    }
+  }
+  float loss[12], ener[2];
+#pragma unroll
+  for (int k = 0; k < 12; ++k) loss[k] = __shfl_sync(0xffffffffu, val, k);
+  ener[0] = __shfl_sync(0xffffffffu, val, 12);
+  ener[1] = __shfl_sync(0xffffffffu, val, 13);
+  float costs[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+  for (int comp = 0; comp < 2; ++comp)
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+#pragma unroll
+      for (int side = 0; side < 2; ++side) costs[j] = fadd(costs[j], fdiv(loss[comp * 6 + j * 2 + side], ener[comp]));
+  int best = 0;
+  if (costs[1] < costs[best]) best = 1;
+  if (costs[2] < costs[best]) best = 2;
+  const int r = best == 0 ? (costs[2] < costs[1] ? 2 : 1) : (best == 1 ? (costs[2] < costs[0] ? 2 : 0)
+                                                                        : (costs[1] < costs[0] ? 1 : 0));
+  *best_cost = costs[best];
+  *second_cost = costs[r];
+  *second_cut = r == 0 ? 2 : (r == 1 ? 1 : 3);
+  return best == 0 ? 2 : (best == 1 ? 1 : 3);
+}
+
+// One merge group by one warp: pool rows r0 .. r0 + width - 1 of level `ell` (width 4, or 2 at a
+// level's tail), staged as rows 0.. of gk / gv / gm, into merged rows r0 / 2 + j of scratch buffer 1
+// from row out_off.  Pairwise: rows (0, 1) and (2, 3) merge count-weighted.  Beta: the cut is the
+// certified warp cut, the canonical order on a near tie, or the update tape's; then every lane
+// takes one (component, 16-byte column) pair of both sides.  Same arithmetic, in the same order,
+// as merge_tile.
+template <typename T, bool BETA, int DC>
+__device__ void merge_group_warp(const LaneCtx<T>& x, const Geo& g, const Work& w, const T* gk, const T* gv,
+                                 const Meta* gm, int r0, int width, int ell, int out_off, int lane) {
+  constexpr int VN = Vec<T>::N;
+  const int D = DC ? DC : g.D, DV = D / VN;
+  T* SK = static_cast<T*>(w.sk);
+  T* SV = static_cast<T*>(w.sv);
+  const int orow = out_off + r0 / 2;
+  if (!BETA) {
+    const int np = width / 2;
+    for (int item = lane; item < np * 2 * DV; item += 32) {
+      const int j = item / (2 * DV), f = (item / DV) & 1, v = item % DV;
+      const float wa = gm[2 * j].w, wb = gm[2 * j + 1].w;
+      const float alpha = fdiv(wa, fmaxf(fadd(wa, wb), 1e-8f));
+      const float beta = fsub(1.f, alpha);
+      const T* base = f ? gv : gk;
+      float a[VN], b[VN], o[VN];
+      unpack(*reinterpret_cast<const uint4*>(base + 2 * j * D + v * VN), a, (const T*)nullptr);
+      unpack(*reinterpret_cast<const uint4*>(base + (2 * j + 1) * D + v * VN), b, (const T*)nullptr);
+#pragma unroll
+      for (int e = 0; e < VN; ++e) o[e] = fadd(fmul(alpha, a[e]), fmul(beta, b[e]));
+      *reinterpret_cast<uint4*>((f ? SV : SK) + x.scr_row(1, orow + j) * D + v * VN) = pack(o, (const T*)nullptr);
+    }
+    if (lane < np) x.put_scratch(1, orow + lane, merge_meta(gm[2 * lane], gm[2 * lane + 1]));
+    return;
+  }
+  const bool two = width == 4;
+  int cut = 1;
+  uint8_t* tcut = g.tape != kTapeNone
+                      ? w.tape_cuts + ((size_t)x.lane * g.L + ell) * tape_cut_stride(g) + r0 / 4
+                      : nullptr;
+  if (two) {
+    if (g.tape == kTapeReplay) {
+      cut = *tcut;
+    } else {
+      cut = beta_cut_warp<T, DC>(gk, gv, gm, 0, D, lane);
+      if (cut < 0) {
+        float bc, sc;
+        int scut;
+        cut = beta_cut_canonical_warp<T, DC>(gk, gv, gm, D, lane, &bc, &sc, &scut);
+        if (lane == 0) {
+          atomicAdd(&w.counters[kCntExactCuts], 1ull);
+          if (near_tie(bc, sc))
+            log_tie(w, LOGKV_TIE_BETA_CUT, x.b, x.grp, x.c, ell * 65536 + r0 / 4, cut, scut, rel_gap(bc, sc), bc);
+        }
+      }
+    }
+  }
+  if (g.tape == kTapeRecord && lane == 0) *tcut = (uint8_t)cut;   // a 2-row tail records its sentinel 1
+  // Apply: per output side, sum over member rows (row order) of w * x / max(mass, 1e-12); each
+  // side keeps its own products (x * 0 for rows of the other side) and sums in row order.
+  for (int item = lane; item < 2 * DV; item += 32) {
+    const int f = item / DV, v = item % DV;
+    const T* base = f ? gv : gk;
+    float acc0[VN], acc1[VN], mass0 = 0.f, mass1 = 0.f;
+#pragma unroll
+    for (int e = 0; e < VN; ++e) acc0[e] = acc1[e] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const bool valid = i < width;
+      const bool in0 = valid && (!two || i < cut), in1 = valid && two && i >= cut;
+      const float wi = valid ? gm[i].w : 0.f;
+      const float om0 = fmul(wi, in0 ? 1.f : 0.f), om1 = fmul(wi, in1 ? 1.f : 0.f);
+      float xr[VN];
+      if (valid) {
+        unpack(*reinterpret_cast<const uint4*>(base + i * D + v * VN), xr, (const T*)nullptr);
+      } else {
+#pragma unroll
+        for (int e = 0; e < VN; ++e) xr[e] = 0.f;
+      }
+      mass0 = fadd(mass0, om0);
+      mass1 = fadd(mass1, om1);
+#pragma unroll
+      for (int e = 0; e < VN; ++e) {
+        acc0[e] = fadd(acc0[e], fmul(xr[e], om0));
+        acc1[e] = fadd(acc1[e], fmul(xr[e], om1));
+      }
+    }
+    const float den0 = fmaxf(mass0, 1e-12f);
+#pragma unroll
+    for (int e = 0; e < VN; ++e) acc0[e] = fdiv(acc0[e], den0);
+    *reinterpret_cast<uint4*>((f ? SV : SK) + x.scr_row(1, orow) * D + v * VN) = pack(acc0, (const T*)nullptr);
+    if (two) {
+      const float den1 = fmaxf(mass1, 1e-12f);
+#pragma unroll
+      for (int e = 0; e < VN; ++e) acc1[e] = fdiv(acc1[e], den1);
+      *reinterpret_cast<uint4*>((f ? SV : SK) + x.scr_row(1, orow + 1) * D + v * VN) = pack(acc1, (const T*)nullptr);
+    }
+  }
+  if (lane < (two ? 2 : 1)) {
+    const int side = lane;
+    float mass = 0.f;
+    int64_t lo = INT64_MAX, hi = INT64_MIN, swp = 0, ord = INT64_MAX;
+    uint8_t pad = 1;
+    for (int i = 0; i < width; ++i) {
+      const bool in = width == 2 ? side == 0 : (side == 0 ? i < cut : i >= cut);
+      const Meta& r = gm[i];
+      mass = fadd(mass, fmul(r.w, in ? 1.f : 0.f));
+      if (!in) continue;
+      if (r.w > 0.f) {
+        lo = min(lo, r.lo);
+        hi = max(hi, r.hi);
+      }
+      swp += r.swp;
+      ord = min(ord, r.ord);
+      pad &= r.pad;
+    }
+    x.put_scratch(1, orow + side, Meta{mass, mass > 0.f ? lo : 0, mass > 0.f ? hi : 0, swp, ord, pad});
+  }
+}
+
+constexpr int kMergeWarps = 8;
+constexpr int kMergeCtas = 4;  // CTAs per lane; the lane's merge groups are dealt to their warps
+
+inline size_t merge_smem(int D, size_t esize) {
+  return (size_t)kMergeWarps * 2 * (8 * (size_t)D * esize + 4 * sizeof(Meta));
+}
+
+// Grid (kMergeCtas, K, B * G).  The merge groups (4 pool rows; 2 at a level's tail) of every merging
+// level of the lane, level by level, are dealt round-robin to the warps of the lane's CTAs.  A warp
+// keeps two groups in flight: while it merges one (from its own shared rows) into the next level's
+// incoming rows (scratch buffer 1), the next one's rows are arriving (16-byte cp.async).
+template <typename T, bool BETA, int DC>
+__global__ void __launch_bounds__(kMergeWarps * 32) cascade_merge_kernel(Geo g, logkv_state_t s, Work w) {
+  pdl_entry();
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int bgi = blockIdx.z;
+  const LaneCtx<T> x = make_ctx_at<T>(g, s, w, blockIdx.y, bgi % g.G, bgi / g.G);
+  __shared__ LevelPlan lp[kMaxLevels];
+  __shared__ int gstart[kMaxLevels + 1];   // first group index of every level
+  __shared__ const T* rowp[kMergeWarps][2][2][4];
+  const int mode = plan_lane(g, w, x.lane, lp);
+  if (tid == 0) {
+    int ng = 0;
+    for (int l = 0; l < g.L; ++l) {
+      gstart[l] = ng;
+      if (lp[l].kind == kLvlMerge) ng += (lp[l].npair + 3) / 4;
+    }
+    gstart[g.L] = ng;
+    if (blockIdx.x == 0) {
+      if (mode == 2) atomicAdd(&w.counters[kCntSeqLanes], 1ull);
+      if (mode == 1) {
+        unsigned long long carries = 0;
+        for (int l = 0; l < g.L; ++l)
+          if (lp[l].kind == kLvlMerge) carries += lp[l].npair / 2;
+        if (carries) atomicAdd(&w.counters[kCntCarry], carries);
+      }
+    }
+  }
+  __syncthreads();
+  if (mode != 1) return;
+  constexpr int VN = Vec<T>::N;
+  const int D = DC ? DC : g.D, DV = D / VN;
+  const bool late = w.plan_type[x.lane] == kJobLate;
+  extern __shared__ uint4 smem4[];
+  T* rows = reinterpret_cast<T*>(smem4) + (size_t)warp * 2 * 8 * D;   // [2 buffers][4 K rows, 4 V rows][D]
+  Meta* metas = reinterpret_cast<Meta*>(reinterpret_cast<T*>(smem4) + (size_t)kMergeWarps * 2 * 8 * D) + warp * 8;
+  const int ng = gstart[g.L];
+  const int stride = gridDim.x * kMergeWarps;
+  // Group q -> (level, first pool row, width); issue its rows into buffer `buf`.
+  auto locate = [&](int q, int& l, int& r0, int& width) {
+    l = 0;
+    while (gstart[l + 1] <= q) ++l;
+    r0 = 4 * (q - gstart[l]);
+    width = min(4, lp[l].npair - r0);
+  };
+  auto stage = [&](int q, int buf) {
+    int l, r0, width;
+    locate(q, l, r0, width);
+    T* gk = rows + (size_t)buf * 8 * D;
+    T* gv = gk + 4 * (size_t)D;
+    if (lane < width) {
+      const PoolRow<T> r = pool_row<T>(x, lp[l], l, r0 + lane, late);
+      rowp[warp][buf][0][lane] = r.k;
+      rowp[warp][buf][1][lane] = r.v;
+      metas[buf * 4 + lane] = r.m;
+    }
+    __syncwarp();
+    for (int item = lane; item < width * 2 * DV; item += 32) {
+      const int r = item / (2 * DV), f = (item / DV) & 1, v = item % DV;
+      cp_async16((f ? gv : gk) + r * D + v * VN, rowp[warp][buf][f][r] + v * VN);
+    }
+    cp_async_commit();
+  };
+  int q = blockIdx.x * kMergeWarps + warp, buf = 0;
+  if (q < ng) stage(q, 0);
+  for (; q < ng; q += stride, buf ^= 1) {
+    const int qn = q + stride;
+    if (qn < ng) {
+      stage(qn, buf ^ 1);
+      asm volatile("cp.async.wait_group 1;\n" ::: "memory");   // the current group's rows have landed
+    } else {
+      cp_async_wait_all();
+    }
+    __syncwarp();
+    int l, r0, width;
+    locate(q, l, r0, width);
+    const T* gk = rows + (size_t)buf * 8 * D;
+    merge_group_warp<T, BETA, DC>(x, g, w, gk, gk + 4 * (size_t)D, metas + buf * 4, r0, width, l,
+                                  lp[l + 1].in_off, lane);
+    __syncwarp();  // buffer `buf` is free for the group after next
+  }
+}
+
+constexpr int kMoveThreads = 256;
+
+inline size_t move_smem(int D, int Bs, size_t esize) {
+  return 2 * (size_t)Bs * D * esize + (size_t)Bs * sizeof(Meta) + 16;
+}
+
+// Grid (L, K, B * G): one CTA per (lane, level) of the lanes the merge kernel handles.  The rows the level writes (a filling level: its incoming rows,
+// to slots cnt..; a merging level: all its survivors, pool rows npair.., to slots 0..) are first
+// brought into shared memory by TMA bulk copies (the stored survivors and carried rows are
+// contiguous runs, one copy each; level-0 token rows one copy per row), then written back with one
+// bulk copy per K and V run, so no stored row is overwritten before it has been read.  The launch
+// may overlap the merge kernel (programmatic dependent launch): the plan and the stored survivors
+// (which the merge kernel only reads) and level 0's incoming rows (ready since the prepare kernel)
+// are fetched before the grid dependency wait; the carried rows and every write come after it.
+// A merging level then zeroes its tail slots.  The copy wait is bounded: past the limit the
+// status word gets kStatusCopyTimeout and nothing is written.
+template <typename T>
+__global__ void __launch_bounds__(kMoveThreads) cascade_move_kernel(Geo g, logkv_state_t s, Work w) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int tid = threadIdx.x, nt = blockDim.x, l = blockIdx.x, bgi = blockIdx.z;
+  const LaneCtx<T> x = make_ctx_at<T>(g, s, w, blockIdx.y, bgi % g.G, bgi / g.G);
+  __shared__ LevelPlan lp[kMaxLevels];
+  const int mode = plan_lane(g, w, x.lane, lp);
+  const LevelPlan p = lp[l];
+  if (mode != 1 || (p.kind != kLvlFill && p.kind != kLvlMerge)) return;
+  const int D = g.D, Bs = g.Bs;
+  const bool late = w.plan_type[x.lane] == kJobLate;
+  const bool fill = p.kind == kLvlFill;
+  const int n = fill ? p.m : p.nsurv;                  // rows written, to slots dst0 ..
+  const int dst0 = fill ? p.cnt : 0;
+  const int nst = fill ? 0 : max(0, p.cnt - p.npair);  // stored survivors: slots npair .. cnt - 1
+  const int src0 = fill ? p.cnt : p.npair;             // pool row of staged row 0
+  const int in0 = src0 + nst - p.cnt;                   // incoming row of staged row nst
+  const int nin = n - nst;
+  const unsigned rowb = (unsigned)(D * sizeof(T));
+  T* LK = static_cast<T*>(s.level_k);
+  T* LV = static_cast<T*>(s.level_v);
+  const size_t lrow0 = x.level_row(l, 0);
+  extern __shared__ uint4 smem4[];
+  T* tk = reinterpret_cast<T*>(smem4);                          // [Bs][D]
+  T* tv = tk + (size_t)Bs * D;                                  // [Bs][D]
+  Meta* tm = reinterpret_cast<Meta*>(tv + (size_t)Bs * D);      // [Bs]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(tm + Bs);
+  const bool tokens = l == 0 && !late;
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  if (tid == 0) mbar_arrive_expect_tx(bar, 2u * (unsigned)n * rowb);
+  __syncthreads();
+  auto issue_incoming = [&]() {
+    if (tid == 0 && nin && !tokens) {
+      const size_t r = x.scr_row(l > 0 ? 1 : 0, (l > 0 ? p.in_off : 0) + in0);
+      bulk_load(tk + (size_t)nst * D, static_cast<const T*>(w.sk) + r * D, (unsigned)nin * rowb, bar);
+      bulk_load(tv + (size_t)nst * D, static_cast<const T*>(w.sv) + r * D, (unsigned)nin * rowb, bar);
+    }
+    if (tokens)
+      for (int i = tid; i < nin; i += nt) {
+        const int src = x.token_src(in0 + i);
+        bulk_load(tk + (size_t)(nst + i) * D, token_row<T>(g, x.snapk, x.reck, x.b, x.grp, src), rowb, bar);
+        bulk_load(tv + (size_t)(nst + i) * D, token_row<T>(g, x.snapv, x.recv, x.b, x.grp, src), rowb, bar);
+      }
+    for (int r = nst + tid; r < n; r += nt) tm[r] = pool_row<T>(x, p, l, src0 + r, late).m;
+  };
+  if (tid == 0 && nst) {
+    bulk_load(tk, LK + (lrow0 + p.npair) * D, (unsigned)nst * rowb, bar);
+    bulk_load(tv, LV + (lrow0 + p.npair) * D, (unsigned)nst * rowb, bar);
+  }
+  for (int r = tid; r < nst; r += nt) tm[r] = pool_row<T>(x, p, l, src0 + r, late).m;
+  if (l == 0) issue_incoming();   // tokens or staged re-inserts: ready since the prepare kernel
+  asm volatile("griddepcontrol.wait;" ::: "memory");   // the merge kernel has completed
+  if (l > 0) issue_incoming();    // carries of level l - 1
+  const bool ok = mbar_wait_bounded(bar, 0);
+  __syncthreads();
+  if (!ok) {
+    if (tid == 0) set_status(w.status, kStatusCopyTimeout);
+    mbar_wait_bounded(bar, 0);   // give the copies in flight one more bounded wait before leaving
+    return;
+  }
+  if (tid == 0 && n > 0) {
+    fence_proxy_async();
+    bulk_store(LK + (lrow0 + dst0) * D, tk, (unsigned)n * rowb);
+    bulk_store(LV + (lrow0 + dst0) * D, tv, (unsigned)n * rowb);
+    bulk_commit();
+  }
+  for (int r = tid; r < n; r += nt) x.put_level_meta(lrow0 + dst0 + r, tm[r]);
+  if (!fill) {
+    constexpr int VN = Vec<T>::N;
+    const int DV = D / VN, nclr = Bs - n;
+    const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+    for (int item = tid; item < nclr * DV * 2; item += nt) {
+      const int r = item / (2 * DV), f = (item / DV) & 1, v = item % DV;
+      *reinterpret_cast<uint4*>((f ? LV : LK) + (lrow0 + n + r) * D + v * VN) = zero;
+    }
+    for (int r = tid; r < nclr; r += nt) x.put_level_meta(lrow0 + n + r, Meta{0.f, 0, 0, 0, 0, 0});
+  }
+  if (tid == 0) {
+    s.level_count[x.lane * g.L + l] = (int16_t)(fill ? p.cnt + p.m : n);
+    atomicAdd(&w.counters[kCntStageRead], (unsigned long long)p.m);
+    if (fill) {
+      atomicAdd(&w.counters[kCntFill], (unsigned long long)p.m);
+    } else {
+      atomicAdd(&w.counters[kCntStorageRead], (unsigned long long)p.cnt);
+      atomicAdd(&w.counters[kCntSurvivor], (unsigned long long)n);
+      atomicAdd(&w.counters[kCntClear], (unsigned long long)(Bs - n));
+    }
+    bulk_wait_all();   // the shared rows stay allocated until the stores have read them
   }
 }
 

@@ -5,6 +5,8 @@
 
 namespace logkv {
 
+struct LevelPlan;
+
 // Per-call constants (by value into every kernel).
 struct Geo {
   int B, G, D, K, L, Bs;  // batch, KV groups, head dim, clusters, levels, slots per level
@@ -16,7 +18,7 @@ struct Geo {
   int NW;                 // token index space per batch row: P + F
   int NC;                 // candidate capacity per row: P + F
   int recent_count;       // window fill before the flush
-  int S;                  // ladder scratch rows per buffer per (b, g)
+  int S;                  // ladder scratch rows per buffer per (b, g): NW + K*L*B' + K*(L+2)
   int sort_cap;           // power of two >= L * Bs + NW (delayed re-insert sort)
   int seed_staged;        // seeding CTAs keep their token rows in shared memory (set per dtype at launch)
   int shard_ranks;        // KV-head sharding: ranks holding G groups each (1 = unsharded)
@@ -31,6 +33,50 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+// TMA bulk copies (cp.async.bulk, no multicast) completing on a shared-memory mbarrier.  Both
+// addresses 16-byte aligned, sizes multiples of 16 bytes.
+__device__ __forceinline__ unsigned smem_u32(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbarrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, unsigned bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+               ::"r"(smem_u32(smem_dst)), "l"(gsrc), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
+  unsigned done;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+               : "=r"(done) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return done != 0;
+}
+// Bounded wait for phase `parity` of an mbarrier: false once kMbarWaitNs of device time (the
+// global nanosecond timer) have passed without the phase completing.
+constexpr unsigned long long kMbarWaitNs = 2000000000ull;
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity) {
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_ns() - t0 > kMbarWaitNs) return false;
+  return true;
+}
+__device__ __forceinline__ void bulk_store(void* gdst, const void* smem_src, unsigned bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n"
+               ::"l"(gdst), "r"(smem_u32(smem_src)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 
 enum TapeMode : int { kTapeNone = 0, kTapeRecord = 1, kTapeReplay = 2 };
 
@@ -48,7 +94,8 @@ enum Counter : int {
   kCntFlushes = 7,       // flush calls
   kCntExactCuts = 8,     // Beta groups whose cut needed the canonical-order evaluation (near ties)
   kCntTies = 9,          // near-tie log entries requested (entries beyond kTieCap are counted only)
-  kNumCounters = 10,
+  kCntSeqLanes = 10,     // lanes whose cascade took the sequential walk in the parallel cascade
+  kNumCounters = 11,
 };
 
 // Near-tie log: every decision of a flush whose two best candidates (or whose value and
@@ -103,6 +150,8 @@ struct Work {
   int32_t* plan_type;      // [B,G,K] JobType
   int32_t* plan_m0;        // [B,G,K] level-0 stage rows
   int32_t* plan_scr;       // [B,G,K] first scratch row of the cluster in its (b,g) region
+  int32_t* lane_mode;      // [B,G,K] cascade of this flush: 0 none, 1 parallel kernels, 2 sequential walk
+  struct LevelPlan* lane_plan;  // [B,G,K,L] what every level does in this flush (prepare kernel)
   int64_t* plan_base;      // [B,G,K] order of the first token row (level0_phase before the flush)
   // Ladder scratch: [B*G][2][S] rows, structure of arrays.
   void* sk;
@@ -127,7 +176,10 @@ __device__ __forceinline__ float rel_gap(float a, float b) {
   const float den = fmaxf(fabsf(a), fabsf(b));
   return den > 0.f ? fdiv(fabsf(fsub(a, b)), den) : 0.f;
 }
-__device__ __forceinline__ bool near_tie(float a, float b) { return rel_gap(a, b) < kTieRel; }
+// Division-free test of rel_gap(a, b) < kTieRel (false for NaN); rel_gap is computed only when logging.
+__device__ __forceinline__ bool near_tie(float a, float b) {
+  return fabsf(fsub(a, b)) < fmul(kTieRel, fmaxf(fabsf(a), fabsf(b)));
+}
 
 // Append one near-tie entry (flush index = flushes counted so far, minus one).
 __device__ __forceinline__ void log_tie(const Work& w, int kind, int b, int g, int c, int index, int first,

@@ -107,14 +107,14 @@ struct LaneCtx {
 };
 
 template <typename T>
-__device__ LaneCtx<T> make_ctx(const Geo& g, const logkv_state_t& s, const Work& w) {
+__device__ LaneCtx<T> make_ctx_at(const Geo& g, const logkv_state_t& s, const Work& w, int c, int grp, int b) {
   LaneCtx<T> x;
   x.g = g;
   x.s = s;
   x.w = w;
-  x.c = blockIdx.x;
-  x.grp = blockIdx.y;
-  x.b = blockIdx.z;
+  x.c = c;
+  x.grp = grp;
+  x.b = b;
   x.bg = (size_t)x.b * g.G + x.grp;
   x.lane = x.bg * g.K + x.c;
   x.toff = w.plan_off[x.lane];
@@ -127,6 +127,57 @@ __device__ LaneCtx<T> make_ctx(const Geo& g, const logkv_state_t& s, const Work&
   x.reck = static_cast<const T*>(s.recent_k_raw);
   x.recv = static_cast<const T*>(s.recent_v);
   return x;
+}
+
+// Lane of a (cluster, group, batch) grid.
+template <typename T>
+__device__ LaneCtx<T> make_ctx(const Geo& g, const logkv_state_t& s, const Work& w) {
+  return make_ctx_at<T>(g, s, w, blockIdx.x, blockIdx.y, blockIdx.z);
+}
+
+// ---------------------------------------------------------------- cascade plan
+// What every level of one lane does in this flush, from its counts and the lane's incoming row
+// count: the sequential walk's control flow without touching a row.  In the steady state every
+// level's merges read only that level's stored rows (level 0 also its incoming tokens), so the
+// merges of all levels run at once (cascade_merge_kernel: carries of level l land in scratch
+// buffer 1 as level l + 1's incoming rows) and then every level moves its survivors
+// (cascade_move_kernel).  A level >= 1 whose merges would read incoming rows (carries of the
+// level below) and the top level's fold need the levels in order: such lanes take the
+// sequential walk.  The prepare kernel writes the plan once per lane (the move kernel's CTAs
+// update the level counts of their own levels, so the plan must not be recomputed from them).
+enum LevelKind : int { kLvlNone = 0, kLvlFill = 1, kLvlMerge = 2, kLvlFold = 3 };
+struct LevelPlan {
+  int kind, cnt, m, npair, nsurv, in_off;  // in_off: the level's first incoming row in scratch buffer 1 (l >= 1)
+};
+
+// Returns 0 (no job), 1 (parallel kernels) or 2 (sequential walk).  One thread, from the lane's
+// job type, incoming row count and level counts.
+__device__ int plan_levels(const Geo& g, int type, int m0, const int* counts, LevelPlan* lp) {
+  for (int l = 0; l < g.L; ++l) lp[l] = LevelPlan{kLvlNone, 0, 0, 0, 0, 0};
+  if (type == kJobNone) return 0;
+  int mode = 1, m = m0, off = 0;
+  for (int l = 0; l < g.L && m > 0; ++l) {
+    const int cnt = counts[l];
+    LevelPlan p{kLvlFill, cnt, m, 0, cnt + m, off};
+    int next = 0;
+    if (cnt + m > g.Bs) {
+      const int rem = cnt + m - g.Bs;
+      if (l == g.L - 1) {
+        p.kind = kLvlFold;
+        mode = 2;
+      } else {
+        p.kind = kLvlMerge;
+        p.npair = 2 * ((rem + 1) / 2);
+        p.nsurv = cnt + m - p.npair;
+        next = p.npair / 2;
+        if (l > 0 && p.npair > cnt) mode = 2;
+      }
+    }
+    lp[l] = p;
+    if (l > 0) off += m;
+    m = next;
+  }
+  return mode;
 }
 
 // ---------------------------------------------------------------- K6a: prepare
@@ -142,6 +193,16 @@ __global__ void __launch_bounds__(256) prepare_kernel(Geo g, logkv_state_t s, Wo
   pdl_entry();
   LaneCtx<T> x = make_ctx<T>(g, s, w);
   const int type = w.plan_type[x.lane];
+  if (threadIdx.x == 0) {
+    // The cascade plan, from the counts the cascade will start from (new and delayed clusters
+    // are cleared below).
+    int counts[kMaxLevels];
+    for (int l = 0; l < g.L; ++l)
+      counts[l] = (type == kJobNew || type == kJobLate) ? 0 : s.level_count[x.lane * g.L + l];
+    LevelPlan lp[kMaxLevels];
+    w.lane_mode[x.lane] = plan_levels(g, type, w.plan_m0[x.lane], counts, lp);
+    for (int l = 0; l < g.L; ++l) w.lane_plan[x.lane * g.L + l] = lp[l];
+  }
   if (type == kJobNone) return;
   const int tid = threadIdx.x, nt = blockDim.x, D = DC ? DC : g.D;
   const int n = w.plan_n[x.lane];

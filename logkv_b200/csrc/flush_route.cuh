@@ -546,7 +546,10 @@ __global__ void __launch_bounds__(1024) plan_kernel(Geo g, logkv_state_t s, Work
       w.plan_m0[lane] = m0;
       w.plan_scr[lane] = scr;
       w.plan_base[lane] = base_order;
-      if (type != kJobNone) scr += m0 + 2;
+      // The lane's scratch range holds every level's incoming rows at once (the parallel cascade
+      // keeps all levels' carries): at most m0 + L of them (each level carries at most half of
+      // its incoming rows, rounded up).
+      if (type != kJobNone) scr += m0 + g.L + 2;
     }
     if (scr > g.S) set_status(w.status, kStatusCarryOverflow);
   }

@@ -55,7 +55,7 @@ def bits_and_values(t: torch.Tensor):
 
 
 @pytest.mark.parametrize("name", [c["name"] for c in CASES])
-def test_fullshape_flush_matches_reference(name):
+def test_fullshape_flush_matches_reference(name, cascade_path):
     cfg = case(name)
     inputs = make_case(cfg)
     cache = build_cache(cfg, inputs)

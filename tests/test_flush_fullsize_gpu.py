@@ -37,7 +37,7 @@ def stream(n_chunks, seed=3):
     return out
 
 
-def test_fullsize_flush_matches_oracle():
+def test_fullsize_flush_matches_oracle(cascade_path):
     from logkv_b200.cache import LogStructuredKVCache
     from logkv_b200.workload import rope_tables
     cos, sin = rope_tables(32768, D, base=1e6)

@@ -57,7 +57,7 @@ def push_chunk(cache, cfg, chunk):
 
 
 @pytest.mark.parametrize("name", [c["name"] for c in CONFIGS])
-def test_device_flush_matches_reference_stream(name):
+def test_device_flush_matches_reference_stream(name, cascade_path):
     cfg = config(name)
     stream = make_stream(cfg)
     ref_steps = load(name)
