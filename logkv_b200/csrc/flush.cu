@@ -507,6 +507,7 @@ static int launch_replay(const Geo& g, const logkv_state_t& s, const Work& w, co
   launch_pdl(snapshot_kernel<T>, dim3(per_bg, g.G, g.B), 256, 0, st, g, s, w);
   launch_pdl(tape_payload_kernel<T>, dim3(per_pay, g.G, g.B), 256, 0, st, g, s, tape, 0);
   launch_pdl(tape_copy_kernel, dim3(2 * sm_count), 256, 0, st, tape_segments(g, s, w, tape, false));
+  launch_pdl(lane_plan_kernel, dim3(g.G, g.B), 32 * ((g.K + 31) / 32), 0, st, g, s, w);
   launch_prepare<T>(g, s, w, st);
   launch_cascade_all<T>(g, s, w, st);
   launch_pdl(pool_rewrite_kernel<T>, dim3(per_bg, g.G, g.B), 256, 0, st, g, s, w);

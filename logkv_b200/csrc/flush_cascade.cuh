@@ -807,6 +807,7 @@ __device__ void merge_group_warp(const LaneCtx<T>& x, const Geo& g, const Work& 
   }
   const bool two = width == 4;
   int cut = 1;
+  bool finite = false;   // the certified warp cut saw every row finite (energies <= 1e30)
   uint8_t* tcut = g.tape != kTapeNone
                       ? w.tape_cuts + ((size_t)x.lane * g.L + ell) * tape_cut_stride(g) + r0 / 4
                       : nullptr;
@@ -815,6 +816,7 @@ __device__ void merge_group_warp(const LaneCtx<T>& x, const Geo& g, const Work& 
       cut = *tcut;
     } else {
       cut = beta_cut_warp<T, DC>(gk, gv, gm, 0, D, lane);
+      finite = cut >= 0;
       if (cut < 0) {
         float bc, sc;
         int scut;
@@ -829,7 +831,41 @@ __device__ void merge_group_warp(const LaneCtx<T>& x, const Geo& g, const Work& 
   }
   if (g.tape == kTapeRecord && lane == 0) *tcut = (uint8_t)cut;   // a 2-row tail records its sentinel 1
   // Apply: per output side, sum over member rows (row order) of w * x / max(mass, 1e-12); each
-  // side keeps its own products (x * 0 for rows of the other side) and sums in row order.
+  // side keeps its own products (x * 0 for rows of the other side) and sums in row order.  With
+  // finite rows the other side's products are skipped: each sum starts at +0, which adding
+  // +-0 leaves unchanged, and a sum of products never becomes -0, so the bits are the same.
+  if (finite) {
+    for (int item = lane; item < 2 * DV; item += 32) {
+      const int f = item / DV, v = item % DV;
+      const T* base = f ? gv : gk;
+      float acc0[VN], acc1[VN], mass0 = 0.f, mass1 = 0.f;
+#pragma unroll
+      for (int e = 0; e < VN; ++e) acc0[e] = acc1[e] = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float xr[VN];
+        unpack(*reinterpret_cast<const uint4*>(base + i * D + v * VN), xr, (const T*)nullptr);
+        const float om = fmul(gm[i].w, 1.f);
+        if (i < cut) {
+          mass0 = fadd(mass0, om);
+#pragma unroll
+          for (int e = 0; e < VN; ++e) acc0[e] = fadd(acc0[e], fmul(xr[e], om));
+        } else {
+          mass1 = fadd(mass1, om);
+#pragma unroll
+          for (int e = 0; e < VN; ++e) acc1[e] = fadd(acc1[e], fmul(xr[e], om));
+        }
+      }
+      const float den0 = fmaxf(mass0, 1e-12f), den1 = fmaxf(mass1, 1e-12f);
+#pragma unroll
+      for (int e = 0; e < VN; ++e) {
+        acc0[e] = fdiv(acc0[e], den0);
+        acc1[e] = fdiv(acc1[e], den1);
+      }
+      *reinterpret_cast<uint4*>((f ? SV : SK) + x.scr_row(1, orow) * D + v * VN) = pack(acc0, (const T*)nullptr);
+      *reinterpret_cast<uint4*>((f ? SV : SK) + x.scr_row(1, orow + 1) * D + v * VN) = pack(acc1, (const T*)nullptr);
+    }
+  } else
   for (int item = lane; item < 2 * DV; item += 32) {
     const int f = item / DV, v = item % DV;
     const T* base = f ? gv : gk;
@@ -903,10 +939,16 @@ inline size_t merge_smem(int D, size_t esize) {
 // incoming rows (scratch buffer 1), the next one's rows are arriving (16-byte cp.async).
 template <typename T, bool BETA, int DC>
 __global__ void __launch_bounds__(kMergeWarps * 32) cascade_merge_kernel(Geo g, logkv_state_t s, Work w) {
-  pdl_entry();
+  // Launched right behind the prepare kernel, whose writes only delayed lanes read (their staged
+  // re-inserts; new and delayed clusters, which prepare clears, merge no stored rows): those lanes
+  // wait for it, the others run beside it.  CTA (0, 0, 0) always waits, so this grid completes
+  // only after the prepare kernel has, and the move kernel's wait on this grid covers both.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bgi = blockIdx.z;
   const LaneCtx<T> x = make_ctx_at<T>(g, s, w, blockIdx.y, bgi % g.G, bgi / g.G);
+  const bool late = __ldcg(w.plan_type + x.lane) == kJobLate;
+  if (late || (blockIdx.x | blockIdx.y | blockIdx.z) == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ LevelPlan lp[kMaxLevels];
   __shared__ int gstart[kMaxLevels + 1];   // first group index of every level
   __shared__ const T* rowp[kMergeWarps][2][2][4];
@@ -932,7 +974,6 @@ __global__ void __launch_bounds__(kMergeWarps * 32) cascade_merge_kernel(Geo g, 
   if (mode != 1) return;
   constexpr int VN = Vec<T>::N;
   const int D = DC ? DC : g.D, DV = D / VN;
-  const bool late = w.plan_type[x.lane] == kJobLate;
   extern __shared__ uint4 smem4[];
   T* rows = reinterpret_cast<T*>(smem4) + (size_t)warp * 2 * 8 * D;   // [2 buffers][4 K rows, 4 V rows][D]
   Meta* metas = reinterpret_cast<Meta*>(reinterpret_cast<T*>(smem4) + (size_t)kMergeWarps * 2 * 8 * D) + warp * 8;
@@ -994,9 +1035,9 @@ inline size_t move_smem(int D, int Bs, size_t esize) {
 // brought into shared memory by TMA bulk copies (the stored survivors and carried rows are
 // contiguous runs, one copy each; level-0 token rows one copy per row), then written back with one
 // bulk copy per K and V run, so no stored row is overwritten before it has been read.  The launch
-// may overlap the merge kernel (programmatic dependent launch): the plan and the stored survivors
-// (which the merge kernel only reads) and level 0's incoming rows (ready since the prepare kernel)
-// are fetched before the grid dependency wait; the carried rows and every write come after it.
+// may overlap the merge kernel (programmatic dependent launch): the plan, the stored survivors
+// (which the merge kernel only reads) and level-0 token rows are fetched before the grid
+// dependency wait; carried rows, a delayed lane's staged rows and every write come after it.
 // A merging level then zeroes its tail slots.  The copy wait is bounded: past the limit the
 // status word gets kStatusCopyTimeout and nothing is written.
 template <typename T>
@@ -1053,9 +1094,9 @@ __global__ void __launch_bounds__(kMoveThreads) cascade_move_kernel(Geo g, logkv
     bulk_load(tv, LV + (lrow0 + p.npair) * D, (unsigned)nst * rowb, bar);
   }
   for (int r = tid; r < nst; r += nt) tm[r] = pool_row<T>(x, p, l, src0 + r, late).m;
-  if (l == 0) issue_incoming();   // tokens or staged re-inserts: ready since the prepare kernel
-  asm volatile("griddepcontrol.wait;" ::: "memory");   // the merge kernel has completed
-  if (l > 0) issue_incoming();    // carries of level l - 1
+  if (tokens) issue_incoming();   // level-0 tokens: ready since the snapshot kernel
+  asm volatile("griddepcontrol.wait;" ::: "memory");   // the merge (and so the prepare) kernel has completed
+  if (!tokens) issue_incoming();  // carries of level l - 1, or a delayed lane's staged re-inserts
   const bool ok = mbar_wait_bounded(bar, 0);
   __syncthreads();
   if (!ok) {

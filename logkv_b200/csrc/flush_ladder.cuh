@@ -143,8 +143,8 @@ __device__ LaneCtx<T> make_ctx(const Geo& g, const logkv_state_t& s, const Work&
 // buffer 1 as level l + 1's incoming rows) and then every level moves its survivors
 // (cascade_move_kernel).  A level >= 1 whose merges would read incoming rows (carries of the
 // level below) and the top level's fold need the levels in order: such lanes take the
-// sequential walk.  The prepare kernel writes the plan once per lane (the move kernel's CTAs
-// update the level counts of their own levels, so the plan must not be recomputed from them).
+// sequential walk.  The plan kernel writes the plan once per lane (the move kernel's CTAs update
+// the level counts of their own levels, so the plan must not be recomputed from them).
 enum LevelKind : int { kLvlNone = 0, kLvlFill = 1, kLvlMerge = 2, kLvlFold = 3 };
 struct LevelPlan {
   int kind, cnt, m, npair, nsurv, in_off;  // in_off: the level's first incoming row in scratch buffer 1 (l >= 1)
@@ -180,6 +180,18 @@ __device__ int plan_levels(const Geo& g, int type, int m0, const int* counts, Le
   return mode;
 }
 
+// The cascade plan of one lane, from the counts the cascade will start from (the prepare kernel
+// clears new and delayed clusters), into the workspace.  One thread.
+__device__ void write_lane_plan(const Geo& g, const logkv_state_t& s, const Work& w, size_t lane) {
+  const int type = w.plan_type[lane];
+  int counts[kMaxLevels];
+  for (int l = 0; l < g.L; ++l)
+    counts[l] = (type == kJobNew || type == kJobLate) ? 0 : s.level_count[lane * g.L + l];
+  LevelPlan lp[kMaxLevels];
+  w.lane_mode[lane] = plan_levels(g, type, w.plan_m0[lane], counts, lp);
+  for (int l = 0; l < g.L; ++l) w.lane_plan[lane * g.L + l] = lp[l];
+}
+
 // ---------------------------------------------------------------- K6a: prepare
 // Centroid and scalar updates of every cluster that receives tokens; new
 // clusters and delayed (late) clusters are cleared, and a delayed cluster's
@@ -193,16 +205,6 @@ __global__ void __launch_bounds__(256) prepare_kernel(Geo g, logkv_state_t s, Wo
   pdl_entry();
   LaneCtx<T> x = make_ctx<T>(g, s, w);
   const int type = w.plan_type[x.lane];
-  if (threadIdx.x == 0) {
-    // The cascade plan, from the counts the cascade will start from (new and delayed clusters
-    // are cleared below).
-    int counts[kMaxLevels];
-    for (int l = 0; l < g.L; ++l)
-      counts[l] = (type == kJobNew || type == kJobLate) ? 0 : s.level_count[x.lane * g.L + l];
-    LevelPlan lp[kMaxLevels];
-    w.lane_mode[x.lane] = plan_levels(g, type, w.plan_m0[x.lane], counts, lp);
-    for (int l = 0; l < g.L; ++l) w.lane_plan[x.lane * g.L + l] = lp[l];
-  }
   if (type == kJobNone) return;
   const int tid = threadIdx.x, nt = blockDim.x, D = DC ? DC : g.D;
   const int n = w.plan_n[x.lane];

@@ -10,6 +10,7 @@
 #include <cooperative_groups.h>
 
 #include "flush_common.cuh"
+#include "flush_ladder.cuh"
 
 namespace logkv {
 
@@ -553,6 +554,15 @@ __global__ void __launch_bounds__(1024) plan_kernel(Geo g, logkv_state_t s, Work
     }
     if (scr > g.S) set_status(w.status, kStatusCarryOverflow);
   }
+  __syncthreads();
+  if (tid < K) write_lane_plan(g, s, w, lane0 + tid);
+}
+
+// Lane plans of a replayed flush (the replay copies the recorded per-cluster plan and skips this
+// file's kernels): grid (G, B), one thread per cluster.
+__global__ void lane_plan_kernel(Geo g, logkv_state_t s, Work w) {
+  pdl_entry();
+  if ((int)threadIdx.x < g.K) write_lane_plan(g, s, w, ((size_t)blockIdx.y * g.G + blockIdx.x) * g.K + threadIdx.x);
 }
 
 // ---------------------------------------------------------------- op-log append
