@@ -24,7 +24,8 @@ roofline  = the ladder cascade kernel (the dominant flush stage): algorithmic
             p_lo/p_hi/sum_wp/order 8 B each, pad 1 B) over its CUDA-event time,
             against the measured HBM copy bandwidth.
 --impl reference times the CPU oracle port (a numpy restatement of the
-reference's flush, single-threaded) on a bounded sample of the same workload.
+reference's flush) on every host core: one worker process per layer, --warmup
+untimed and --steps timed steps, a step being one flush in every worker.
 """
 from __future__ import annotations
 
@@ -46,7 +47,12 @@ WORKLOAD = dict(workload="qwen3-0.6b streaming prefill flush (28 layers, 32K tok
                 layers=28, groups=8, head_dim=128, clusters=12, B=128, recent=2048, granularity=2048,
                 exact=256, span_cap=64, beta=True, tokens=32768, chunk=2048, batch_per_rank=1, dtype="bf16")
 ROW_BYTES = 256 + 256 + 4 + 4 * 8 + 1   # one bf16 ladder entry (13 fields, first-order subset)
-CASCADE_TRAFFIC = 30_712_320            # dram read + write bytes of one cascade launch (ncu capture)
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one flush's cascade kernels (merge
+# and move) in the one-launch ncu capture of this build at this layer shape (the
+# profiling command is in the cascade profile summary).  Written rows mostly stay in L2 within the
+# launch, so the figure is below the algorithmic bytes.
+CASCADE_TRAFFIC = 35_741_952
+FLUSH_KERNELS = 13                      # kernel launches per layer-chunk: window append + 12 per flush
 METRIC = "flush us per 2048-tok chunk/layer"
 
 
@@ -273,9 +279,11 @@ def bench_ours(args, rank, world, local_rank):
     stages_us = {name: round(stage_ms[i] * 1000.0 / flushes_per_step, 2) for i, name in enumerate(FLUSH_STAGES)}
     stages_med = {name: round(statistics.median(per_flush[i]) * 1000.0, 2) for i, name in enumerate(FLUSH_STAGES)}
     stages_max = {name: round(max(per_flush[i]) * 1000.0, 2) for i, name in enumerate(FLUSH_STAGES)}
-    casc_rows = delta["storage_read"] + delta["stage_read"] + delta["survivor"] + delta["fill"] + delta["clear"] \
-        + delta["carry"]
+    # Algorithmic cascade bytes: rows read and written by the ladder append, carries excluded
+    # (a carried row is produced and consumed inside the cascade).
+    casc_rows = delta["storage_read"] + delta["stage_read"] + delta["survivor"] + delta["fill"] + delta["clear"]
     casc_bytes_per_launch = casc_rows * ROW_BYTES / flushes_per_step
+    casc_bytes_carry = (casc_rows + delta["carry"]) * ROW_BYTES / flushes_per_step
     casc_s = stage_ms[FLUSH_STAGES.index("cascade")] / 1000.0 / flushes_per_step
     peak, peak_kind = measured_peaks()
     achieved = casc_bytes_per_launch / casc_s / 1e9
@@ -345,14 +353,19 @@ def bench_ours(args, rank, world, local_rank):
         e_ms = float(t.item())
     e2e_us = e_ms * 1000.0 / (args.steps * flushes_per_step)
     del readback
-    n_launch = flushes_per_step * 11 * args.steps   # 11 kernels per flush (no window staging here)
+    chunks_per_step = cfg["layers"] * (cfg["tokens"] // cfg["chunk"])
+    n_launch = (flushes_per_step * FLUSH_KERNELS + (chunks_per_step - flushes_per_step)) * args.steps
     return dict(value=us_per_flush * 1.0 / world, ms_per_step=ms_per_step, e2e_us=e2e_us / world,
                 h2d=h2d_per_step * world, stages=stages_us, stages_med=stages_med, stages_max=stages_max,
                 counters=delta, flushes_per_step=flushes_per_step,
-                roofline={"bound": "hbm", "kernel": "cascade_kernel", "achieved": round(achieved, 1),
-                          "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                          "traffic": CASCADE_TRAFFIC, "traffic_source": "profiles/cascade_kernel_qwen3-0.6b.md (ncu, same layer shape)",
-                          "bytes_per_launch": round(casc_bytes_per_launch)},
+                roofline={"bound": "hbm", "kernel": "ladder cascade (cascade_merge_kernel + cascade_move_kernel)",
+                          "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                          "frac": round(achieved / peak, 4), "traffic": CASCADE_TRAFFIC,
+                          "traffic_source": "ncu capture of this build's cascade kernels, one flush, same layer shape",
+                          "bytes_per_launch": round(casc_bytes_per_launch),
+                          "bytes_per_launch_with_carries": round(casc_bytes_carry),
+                          "frac_with_carries": round(casc_bytes_carry / casc_s / 1e9 / peak, 4),
+                          "launch_us": round(casc_s * 1e6, 2)},
                 flush_roofline={"achieved": round(flush_achieved, 1), "unit": "GB/s",
                                 "frac": round(flush_achieved / peak, 4), "bytes_per_flush": round(flush_bytes)},
                 clocks=clocks.summary(), launches=n_launch, inputs=(caches, layers, ends_host, ends_dev))
@@ -856,39 +869,52 @@ def cpu_flush_sample(n_flushes: int = 3, seed: int = 7):
     return statistics.median(times) * 1e6, n_flushes
 
 
-def _cpu_layer_worker(layer, n_flushes, barrier):
-    """One layer's oracle flushes in a worker process: one warm-up flush, then, after every
-    worker is ready, n_flushes timed ones; returns the wall-clock (start, end) of the timed part."""
+def _cpu_layer_worker(layer, steps, barrier):
+    """One layer's oracle flushes in a worker process: `steps` flushes, one per step, each started
+    after every worker has reached the step's barrier; returns the wall-clock (start, end) of every
+    flush.  The next chunk is drawn before the barrier, and a stream that reaches the maximum
+    sequence length restarts as a new stream (window refilled) outside the timed part."""
     from logkv_b200.workload import MixtureKeys, boundary_pattern
     from oracle.cache import OracleCache
     cfg = WORKLOAD
     rng = np.random.default_rng(1000 + layer)
     G, D, T = cfg["groups"], cfg["head_dim"], cfg["chunk"]
     mix = MixtureKeys(rng, G, D, cfg["clusters"])
-    oc = OracleCache(batch=1, groups=G, max_seq=cfg["tokens"], dim=D, B=cfg["B"], recent=cfg["recent"],
-                     clusters=cfg["clusters"], granularity=cfg["granularity"], exact=cfg["exact"],
-                     span_cap=cfg["span_cap"], beta=cfg["beta"], dtype="bf16")
 
     def chunk(c):
         kr = mix.draw(1, T)
         v = rng.standard_normal((1, G, T, D)).astype(np.float32)
         return kr, v, np.arange(c * T, (c + 1) * T)[None], boundary_pattern(rng, 1, T, "mod23")
 
-    for c in range(2):                       # fill the window, then one warm-up flush
+    def new_stream():
+        oc = OracleCache(batch=1, groups=G, max_seq=cfg["tokens"], dim=D, B=cfg["B"], recent=cfg["recent"],
+                         clusters=cfg["clusters"], granularity=cfg["granularity"], exact=cfg["exact"],
+                         span_cap=cfg["span_cap"], beta=cfg["beta"], dtype="bf16")
+        kr, v, pos, ends = chunk(0)
+        oc.add_recent(kr, v, kr, pos, ends)      # fills the window, no flush
+        return oc, 1
+
+    oc, c = new_stream()
+    spans = []
+    for _ in range(steps):
+        if (c + 1) * T > cfg["tokens"]:
+            oc, c = new_stream()
         kr, v, pos, ends = chunk(c)
-        oc.add_recent(kr, v, kr, pos, ends)
-    inputs = [chunk(c) for c in range(2, 2 + n_flushes)]
-    barrier.wait()
-    t0 = time.time()
-    for kr, v, pos, ends in inputs:
-        oc.add_recent(kr, v, kr, pos, ends)
-    return t0, time.time()
+        c += 1
+        barrier.wait()
+        t0 = time.time()
+        oc.add_recent(kr, v, kr, pos, ends)      # one 2048-token flush
+        spans.append((t0, time.time()))
+    return spans
 
 
-def cpu_flush_throughput(n_flushes: int = 2):
-    """The oracle port on every host core: one worker process per layer (spawned, one BLAS thread
-    each; the 28 layers' flushes are independent), n_flushes timed flushes each after a common
-    barrier; microseconds per flush = wall time of the timed part / flushes done."""
+def cpu_flush_steps(warmup: int, steps: int):
+    """The reference arm: the oracle port on every host core.  One worker process per layer
+    (spawned, one BLAS thread each; the 28 layers' flushes are independent, so up to the core
+    count run at once); a step is one flush in every worker, started together.  Returns
+    (microseconds per flush, milliseconds per step, workers) over the `steps` timed steps that
+    follow `warmup` untimed ones; a step's time runs from its first flush's start to its last
+    flush's end."""
     import multiprocessing as mp
     workers = max(1, min(WORKLOAD["layers"], os.cpu_count() or 1))
     for var in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
@@ -897,9 +923,10 @@ def cpu_flush_throughput(n_flushes: int = 2):
     with ctx.Manager() as manager:
         barrier = manager.Barrier(workers)
         with ctx.Pool(workers) as pool:
-            spans = pool.starmap(_cpu_layer_worker, [(layer, n_flushes, barrier) for layer in range(workers)])
-    wall = max(e for _, e in spans) - min(s for s, _ in spans)
-    return wall * 1e6 / (workers * n_flushes), workers, n_flushes
+            spans = pool.starmap(_cpu_layer_worker, [(layer, warmup + steps, barrier) for layer in range(workers)])
+    step_s = [max(sp[i][1] for sp in spans) - min(sp[i][0] for sp in spans) for i in range(warmup, warmup + steps)]
+    total = sum(step_s)
+    return total * 1e6 / (steps * workers), total * 1e3 / steps, workers
 
 
 def main():
@@ -929,14 +956,16 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        us, workers, n = cpu_flush_throughput(max(1, min(args.cpu_flushes, 2)))
+        us, ms_step, workers = cpu_flush_steps(args.warmup, args.steps)
+        sample = (f"{args.steps} timed steps after {args.warmup} warm-up steps; a step = one 2048-token flush "
+                  f"of each of {workers} layers, in parallel worker processes (oracle/ numpy port of the "
+                  "reference's CPU path, one thread each); value = step time / flushes per step")
         line = dict(metric=METRIC, value=round(us, 1), unit="us", n_gpus=args.gpus, steps=args.steps,
-                    warmup=args.warmup, ms_per_step=round(us * 420 / 1000.0, 1), higher_is_better=False,
+                    warmup=args.warmup, ms_per_step=round(ms_step, 2), higher_is_better=False,
                     scaling="weak", vs_baseline=None, dtype="bf16", data="synthetic", config=config,
-                    impl="reference",
+                    impl="reference", flushes_per_step=workers,
                     cpu_baseline={"value": round(us, 1), "unit": "us", "cores": workers, "kind": "port",
-                                  "sample": f"{n} flushes on each of {workers} layers in parallel worker processes "
-                                            "(oracle/, numpy, one thread each), wall time per flush"},
+                                  "sample": sample},
                     e2e={"value": round(us, 1), "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
         print(json.dumps(line), flush=True)
         return

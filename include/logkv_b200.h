@@ -178,6 +178,21 @@ LOGKV_API int logkv_flush_static(const logkv_layout_t* layout, const logkv_state
                                  int32_t recent_count, void* stream);
 
 /*
+ * Append a chunk of n tokens to the recent window at rows [recent_count, recent_count + n): the
+ * window write of LogStructuredKVCache._semantic_add_recent (log_kv_cache.py:5701-5704, and the
+ * span-end flags of :5693).  k (post-RoPE), k_raw (pre-RoPE) and v are [B, G, n, D] in the cache's
+ * storage dtype with the given element strides of their batch, group and token axes (the head dim
+ * contiguous, every row 16-byte aligned); positions [B, n] int64 with strides, or NULL for the
+ * consecutive positions pos0, pos0 + 1, ... of every row; ends [B, n] uint8 contiguous on the
+ * device.  One kernel on `stream`; returns LOGKV_E_POINTER for misaligned rows.
+ */
+LOGKV_API int logkv_window_append(const logkv_layout_t* layout, const logkv_state_t* state, const void* k,
+                                  const int64_t* k_strides, const void* k_raw, const int64_t* k_raw_strides,
+                                  const void* v, const int64_t* v_strides, const int64_t* positions,
+                                  const int64_t* pos_strides, int64_t pos0, const uint8_t* ends, int32_t n,
+                                  int32_t recent_count, void* stream);
+
+/*
  * KV-head sharding of one sequence (no reference counterpart: the reference runs a
  * layer's cache on one device).  Each rank's layout and state hold its own block of
  * `groups` KV groups (rank r: global groups [r * groups, (r + 1) * groups)).  Every
@@ -272,8 +287,10 @@ LOGKV_API int logkv_read_status(const void* workspace, int32_t* out, void* strea
  * with host counters and optional CUDA events, litgpt/log_kv_timing.py:15-50).
  * logkv_flush_profiled is logkv_flush plus one cudaEventRecord (events are
  * cudaEvent_t as void*) before the first and after each of the
- * LOGKV_FLUSH_STAGES kernels stages: snapshot, span cut, span scores with attach
- * decisions, choose, seed + plan, prepare, cascade, pool rewrite, window shift.
+ * LOGKV_FLUSH_STAGES kernel stages: snapshot, span cut, span scores with attach
+ * decisions, choose, seed + plan, prepare, cascade (merge and move kernels), pool
+ * rewrite, window shift.  (Events between the kernels end their programmatic
+ * overlap, so a profiled flush is slower than a plain one.)
  */
 #define LOGKV_FLUSH_STAGES 9
 LOGKV_API int logkv_flush_profiled(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,

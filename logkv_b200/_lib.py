@@ -104,6 +104,11 @@ def lib() -> ctypes.CDLL:
         handle.logkv_read_counters.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int32,
                                                ctypes.c_void_p]
         P = ctypes.POINTER
+        I64 = P(ctypes.c_int64)
+        handle.logkv_window_append.restype = ctypes.c_int
+        handle.logkv_window_append.argtypes = [P(Layout), P(State), ctypes.c_void_p, I64, ctypes.c_void_p, I64,
+                                               ctypes.c_void_p, I64, ctypes.c_void_p, I64, ctypes.c_int64,
+                                               ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]
         handle.logkv_read_ties.restype = ctypes.c_int
         handle.logkv_read_ties.argtypes = [ctypes.c_void_p, P(Tie), ctypes.c_int32, P(ctypes.c_int64), ctypes.c_int32,
                                            ctypes.c_void_p]

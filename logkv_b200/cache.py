@@ -217,6 +217,7 @@ class LogStructuredKVCache(nn.Module):
         reg("s_h", s_h)
         # Device form of the reference's host-side pool lists (not registered buffers).
         self._recent_ends = torch.zeros(batch, R, dtype=torch.uint8, **z)
+        self._ends_stage = torch.zeros(batch * R, dtype=torch.uint8, **z)   # host span-end lists, staged
         self._span_len = torch.zeros(batch, P, dtype=torch.int32, **z)
         self._span_closed = torch.zeros(batch, P, dtype=torch.uint8, **z)
         self._span_count = torch.zeros(batch, dtype=torch.int32, **z)
@@ -475,11 +476,11 @@ class LogStructuredKVCache(nn.Module):
 
     # ------------------------------------------------------------------ window
     def _positions(self, n: int, input_pos):
-        """Absolute positions of the chunk's tokens as a [batch, n] int64 device tensor."""
+        """Absolute positions of the chunk's tokens as a [batch, n] int64 device tensor, or None for
+        the consecutive positions token_count, token_count + 1, ... (written by the append kernel)."""
         dev = self.recent_pos.device
         if input_pos is None:
-            return torch.arange(self.token_count, self.token_count + n, device=dev).unsqueeze(0).expand(
-                self.batch_size, -1)
+            return None
         if input_pos.dim() == 1:
             if input_pos.numel() != n:
                 raise ValueError(f"input_pos length {input_pos.numel()} != chunk size {n}")
@@ -520,16 +521,13 @@ class LogStructuredKVCache(nn.Module):
             raise RuntimeError(f"semantic LogKV recent buffer overflow: recent_count={self.recent_count}, n={n}, "
                                f"capacity={self.recent_capacity}")
         self.token_count += n
-        dst = slice(self.recent_count, self.recent_count + n)
-        self.recent_k[:, :, dst] = k
-        self.recent_k_raw[:, :, dst] = k_raw
-        self.recent_v[:, :, dst] = v
-        self.recent_pos[:, dst] = positions
         if span_ends_device is not None:
-            self._recent_ends[:, dst].copy_(span_ends_device)
+            ends = span_ends_device.to(device=self.recent_pos.device, dtype=torch.uint8).contiguous()
         else:
-            ends = torch.tensor(span_ends, dtype=torch.uint8)
-            self._recent_ends[:, dst].copy_(ends.pin_memory() if self.recent_pos.is_cuda else ends, non_blocking=True)
+            host = torch.tensor(span_ends, dtype=torch.uint8)
+            ends = self._ends_stage[:self.batch_size * n].view(self.batch_size, n)
+            ends.copy_(host.pin_memory() if self.recent_pos.is_cuda else host, non_blocking=True)
+        self._append_window(k, k_raw, v, positions, ends, n)
         self.recent_count += n
         overflow = self.recent_count - self.recent_size
         if overflow > 0:
@@ -549,6 +547,32 @@ class LogStructuredKVCache(nn.Module):
                 self.recent_count -= take
                 pending -= take
                 self._route_mark_ready()
+
+    def _append_window(self, k, k_raw, v, positions, ends, n: int) -> None:
+        """The chunk into window rows [recent_count, recent_count + n) with one kernel
+        (logkv_window_append).  Rows must be in the storage dtype, contiguous along the head dim
+        and 16-byte aligned; other inputs are made so first."""
+        dt, dev = self.recent_k.dtype, self.recent_k.device
+        esize = self.recent_k.element_size()
+
+        def rows(t):
+            if (t.dtype != dt or t.device != dev or t.stride(-1) != 1 or t.data_ptr() % 16
+                    or any((st * esize) % 16 for st in t.stride()[:3])):
+                t = t.to(device=dev, dtype=dt).contiguous()
+            return t, (ctypes.c_int64 * 3)(*t.stride()[:3])
+
+        (k, ks), (kr, krs), (v, vs) = rows(k), rows(k_raw), rows(v)
+        pos_ptr, ps = None, None
+        if positions is not None:
+            if positions.dtype != torch.int64 or positions.device != dev:
+                positions = positions.to(device=dev, dtype=torch.int64)
+            pos_ptr, ps = ctypes.c_void_p(positions.data_ptr()), (ctypes.c_int64 * 2)(*positions.stride())
+        state = self._state_struct()
+        _lib.check(_lib.lib().logkv_window_append(
+            ctypes.byref(self._layout), ctypes.byref(state), ctypes.c_void_p(k.data_ptr()), ks,
+            ctypes.c_void_p(kr.data_ptr()), krs, ctypes.c_void_p(v.data_ptr()), vs, pos_ptr, ps,
+            int(self.token_count - n), ctypes.c_void_p(ends.data_ptr()), int(n), int(self.recent_count),
+            ctypes.c_void_p(_lib.stream_ptr(dev))), "logkv_window_append")
 
     # ------------------------------------------------------------------ read side
     def _semantic_attention_plan(self):

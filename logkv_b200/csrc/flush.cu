@@ -46,11 +46,7 @@ static size_t prep_smem_bytes(const Geo& g, size_t esize) {
          (size_t)kPrepRows * g.D * esize;
 }
 
-static size_t cascade_smem(const Geo& g, size_t esize) {
-  // two K/V tile buffers, two metadata tiles, token positions and sources
-  return 4 * (size_t)kTileRows * g.D * esize + 2 * (size_t)kTileRows * sizeof(Meta) +
-         (size_t)g.NW * (sizeof(int64_t) + sizeof(int)) + 16;
-}
+static size_t cascade_smem(const Geo& g, size_t esize) { return walk_smem(g, esize, kTileRows); }
 
 // Every flush kernel is launched with a programmatic dependency on the previous kernel of the
 // stream (each kernel begins with pdl_entry()), so launch latency overlaps the previous tail.
@@ -77,21 +73,21 @@ static void smem_limit(K* kern, size_t smem) {
 // Cascade launches for one (dtype, Beta, head dim) instantiation; DC = 0 is the runtime-D kernel.
 // Parallel: merges of every level at once, every level's survivor moves, then the sequential walk
 // of the lanes that need it (disjoint from the others).  Otherwise one sequential walk per lane.
+// Parallel: merges of every level at once, then every level's survivor moves (the move kernel
+// also runs the sequential walk of the lanes that need it).  Otherwise one sequential walk per lane.
 template <typename T, bool BETA, int DC>
 static void launch_cascade(const Geo& g, const logkv_state_t& s, const Work& w, size_t smem, bool parallel,
                            cudaStream_t st) {
   if (!parallel) {
-    smem_limit(cascade_kernel<T, BETA, DC, false>, smem);
-    launch_pdl(cascade_kernel<T, BETA, DC, false>, dim3(g.K, g.G, g.B), kCascadeThreads, smem, st, g, s, w);
+    smem_limit(cascade_kernel<T, BETA, DC>, smem);
+    launch_pdl(cascade_kernel<T, BETA, DC>, dim3(g.K, g.G, g.B), kCascadeThreads, smem, st, g, s, w);
     return;
   }
-  const size_t ms = merge_smem(g.D, sizeof(T)), vs = move_smem(g.D, g.Bs, sizeof(T));
+  const size_t ms = merge_smem(g.D, sizeof(T)), vs = move_smem(g, sizeof(T));
   smem_limit(cascade_merge_kernel<T, BETA, DC>, ms);
   launch_pdl(cascade_merge_kernel<T, BETA, DC>, dim3(kMergeCtas, g.K, g.B * g.G), kMergeWarps * 32, ms, st, g, s, w);
-  smem_limit(cascade_move_kernel<T>, vs);
-  launch_pdl(cascade_move_kernel<T>, dim3(g.L, g.K, g.B * g.G), kMoveThreads, vs, st, g, s, w);
-  smem_limit(cascade_kernel<T, BETA, DC, true>, smem);
-  launch_pdl(cascade_kernel<T, BETA, DC, true>, dim3(g.K, g.G, g.B), kCascadeThreads, smem, st, g, s, w);
+  smem_limit(cascade_move_kernel<T, BETA, DC>, vs);
+  launch_pdl(cascade_move_kernel<T, BETA, DC>, dim3(g.L, g.K, g.B * g.G), kMoveThreads, vs, st, g, s, w);
 }
 
 // The parallel cascade needs one level's survivors (at most B' rows) in one CTA's shared memory
@@ -100,8 +96,7 @@ static void launch_cascade(const Geo& g, const logkv_state_t& s, const Work& w, 
 static bool parallel_cascade(const Geo& g, size_t esize) {
   const char* env = getenv("LOGKV_CASCADE");
   if (env && strcmp(env, "sequential") == 0) return false;
-  return move_smem(g.D, g.Bs, esize) <= 227 * 1024 && merge_smem(g.D, esize) <= 227 * 1024 &&
-         (size_t)g.B * g.G <= 65535;
+  return move_smem(g, esize) <= 227 * 1024 && merge_smem(g.D, esize) <= 227 * 1024 && (size_t)g.B * g.G <= 65535;
 }
 
 template <typename T>
@@ -275,6 +270,47 @@ __global__ void window_shift_kernel(Geo g, logkv_state_t s, Work w, int rem, int
       }
     }
   }
+}
+
+// ---------------------------------------------------------------- window append
+// The chunk's post-RoPE K, pre-RoPE K and V rows into window rows [recent_count, recent_count + n)
+// (16-byte moves; every source row is contiguous and 16-byte aligned, rows addressed through
+// element strides), its positions into recent_pos and its span-end flags into recent_ends.
+struct AppendArgs {
+  const void* k;
+  const void* k_raw;
+  const void* v;
+  long long ks[3], krs[3], vs[3];   // element strides of the batch, group and token axes
+  const int64_t* pos;               // [B, n] positions, or null: positions pos0 + t
+  long long ps[2];                  // element strides of positions [B, n]
+  long long pos0;
+  const uint8_t* ends;              // [B, n] contiguous
+  int n, recent_count;
+};
+
+template <typename T>
+__global__ void window_append_kernel(Geo g, logkv_state_t s, AppendArgs a) {
+  pdl_entry();
+  constexpr int VN = Vec<T>::N;
+  const int b = blockIdx.z, grp = blockIdx.y, DV = g.D / VN;
+  const size_t dst0 = (((size_t)b * g.G + grp) * g.cap2R + a.recent_count) * g.D;
+  const size_t units = (size_t)a.n * DV;
+  for (size_t u = blockIdx.x * (size_t)blockDim.x + threadIdx.x; u < units; u += (size_t)gridDim.x * blockDim.x) {
+    const size_t t = u / DV, v = u % DV;
+    const size_t d = dst0 + t * g.D + v * VN;
+    const T* sk = static_cast<const T*>(a.k) + b * a.ks[0] + grp * a.ks[1] + t * a.ks[2] + v * VN;
+    const T* skr = static_cast<const T*>(a.k_raw) + b * a.krs[0] + grp * a.krs[1] + t * a.krs[2] + v * VN;
+    const T* sv = static_cast<const T*>(a.v) + b * a.vs[0] + grp * a.vs[1] + t * a.vs[2] + v * VN;
+    *reinterpret_cast<uint4*>(static_cast<T*>(s.recent_k) + d) = *reinterpret_cast<const uint4*>(sk);
+    *reinterpret_cast<uint4*>(static_cast<T*>(s.recent_k_raw) + d) = *reinterpret_cast<const uint4*>(skr);
+    *reinterpret_cast<uint4*>(static_cast<T*>(s.recent_v) + d) = *reinterpret_cast<const uint4*>(sv);
+  }
+  if (grp == 0 && blockIdx.x == 0)
+    for (int t = threadIdx.x; t < a.n; t += blockDim.x) {
+      const size_t r = (size_t)b * g.cap2R + a.recent_count + t;
+      s.recent_pos[r] = a.pos ? a.pos[b * a.ps[0] + t * a.ps[1]] : a.pos0 + t;
+      s.recent_ends[r] = a.ends[(size_t)b * a.n + t];
+    }
 }
 
 // ---------------------------------------------------------------- workspace
@@ -619,6 +655,51 @@ extern "C" int logkv_flush_replay(const logkv_layout_t* layout, const logkv_stat
                                   size_t tape_bytes, void* stream) {
   return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream, nullptr,
                    kPhaseAll, nullptr, 1, kTapeReplay, const_cast<void*>(tape), tape_bytes);
+}
+
+extern "C" int logkv_window_append(const logkv_layout_t* layout, const logkv_state_t* state, const void* k,
+                                   const int64_t* k_strides, const void* k_raw, const int64_t* k_raw_strides,
+                                   const void* v, const int64_t* v_strides, const int64_t* positions,
+                                   const int64_t* pos_strides, int64_t pos0, const uint8_t* ends, int32_t n,
+                                   int32_t recent_count, void* stream) {
+  const int val = validate(layout, 1);
+  if (val != LOGKV_OK) return val;
+  if (!state || !k || !k_raw || !v || !ends || !k_strides || !k_raw_strides || !v_strides ||
+      (positions && !pos_strides))
+    return LOGKV_E_POINTER;
+  if (n < 1 || recent_count < 0 || recent_count + n > layout->recent_capacity) return LOGKV_E_SHAPE;
+  const size_t esize = layout->dtype == LOGKV_DTYPE_BF16 ? 2 : 4;
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  AppendArgs a{};
+  a.k = k;
+  a.k_raw = k_raw;
+  a.v = v;
+  for (int i = 0; i < 3; ++i) {
+    a.ks[i] = k_strides[i];
+    a.krs[i] = k_raw_strides[i];
+    a.vs[i] = v_strides[i];
+    // Every row must start on a 16-byte boundary (rows are contiguous along the head dim).
+    if ((a.ks[i] * (long long)esize) % 16 || (a.krs[i] * (long long)esize) % 16 || (a.vs[i] * (long long)esize) % 16)
+      return LOGKV_E_POINTER;
+  }
+  a.ps[0] = positions ? pos_strides[0] : 0;
+  a.ps[1] = positions ? pos_strides[1] : 0;
+  a.pos = positions;
+  a.pos0 = pos0;
+  a.ends = ends;
+  a.n = n;
+  a.recent_count = recent_count;
+  if (!a16(k) || !a16(k_raw) || !a16(v) || !a16(state->recent_k) || !a16(state->recent_k_raw) ||
+      !a16(state->recent_v) || !state->recent_pos || !state->recent_ends)
+    return LOGKV_E_POINTER;
+  const Geo g = make_geo(*layout, 1, recent_count);
+  const int per = std::max(1, std::min(64, (int)(((size_t)n * g.D / (16 / esize) + 255) / 256)));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (layout->dtype == LOGKV_DTYPE_BF16)
+    launch_pdl(window_append_kernel<__nv_bfloat16>, dim3(per, g.G, g.B), 256, 0, st, g, *state, a);
+  else
+    launch_pdl(window_append_kernel<float>, dim3(per, g.G, g.B), 256, 0, st, g, *state, a);
+  return (int)cudaGetLastError();
 }
 
 extern "C" int logkv_flush_oplog_append(const logkv_layout_t* layout, int32_t flush_tokens, void* workspace,

@@ -402,31 +402,28 @@ __device__ void merge_tile(const LaneCtx<T>& x, const Geo& g, const Work& w, con
 
 constexpr int kCascadeThreads = 256;  // two CTAs per SM (registers and shared memory)
 
-// Sequential level walk, one CTA per lane: every level in order, each overflowing level's pool
-// streamed through double-buffered tiles.  SEQ_ONLY: only the lanes the parallel merge kernel
-// left to it (lane_mode 2).
-template <typename T, bool BETA, int DC, bool SEQ_ONLY>
-__global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logkv_state_t s, Work w) {
-  pdl_entry();
-  LaneCtx<T> x = make_ctx<T>(g, s, w);
+// Sequential level walk of one lane by the whole block: every level in order, each overflowing
+// level's pool streamed through double-buffered tiles of TILE rows (dynamic shared memory of
+// walk_smem(g, esize, TILE) bytes).
+template <typename T, bool BETA, int DC, int TILE>
+__device__ void cascade_walk(const LaneCtx<T>& x, const Geo& g, const logkv_state_t& s, const Work& w) {
+  static_assert(TILE % 4 == 0, "Beta groups never straddle tiles");
   const int type = w.plan_type[x.lane];
-  if (type == kJobNone) return;
-  if (SEQ_ONLY && w.lane_mode[x.lane] != 2) return;
   constexpr int VN = Vec<T>::N;
   const int tid = threadIdx.x, nt = blockDim.x, Bs = g.Bs;
   // Compile-time head dim when DC != 0: every row/vector index map becomes shifts.
   const int D = DC ? DC : g.D, DV = D / VN;
   extern __shared__ uint4 smem4[];
-  T* tkb = reinterpret_cast<T*>(smem4);                                 // [2][kTileRows][D]
-  T* tvb = tkb + 2 * (size_t)kTileRows * D;                             // [2][kTileRows][D]
-  Meta* tmb = reinterpret_cast<Meta*>(tvb + 2 * (size_t)kTileRows * D);  // [2][kTileRows]
-  int64_t* tpos = reinterpret_cast<int64_t*>(tmb + 2 * kTileRows);      // [NW] token positions
+  T* tkb = reinterpret_cast<T*>(smem4);                                 // [2][TILE][D]
+  T* tvb = tkb + 2 * (size_t)TILE * D;                             // [2][TILE][D]
+  Meta* tmb = reinterpret_cast<Meta*>(tvb + 2 * (size_t)TILE * D);  // [2][TILE]
+  int64_t* tpos = reinterpret_cast<int64_t*>(tmb + 2 * TILE);      // [NW] token positions
   int* srcs = reinterpret_cast<int*>(tpos + g.NW);                      // [NW] token sources
-  __shared__ float bloss[kTileGroups][12];
-  __shared__ float bener[kTileGroups][2];
-  __shared__ int bcut[kTileGroups];
+  __shared__ float bloss[(TILE / 4)][12];
+  __shared__ float bener[(TILE / 4)][2];
+  __shared__ int bcut[(TILE / 4)];
   __shared__ int sh_exact;  // groups of the current tile needing the canonical cost order
-  __shared__ const T* rowp[2][2][kTileRows];  // [tile buffer][K, V][row] source rows of staged tiles
+  __shared__ const T* rowp[2][2][TILE];  // [tile buffer][K, V][row] source rows of staged tiles
   if (threadIdx.x == 0) sh_exact = 0;
   T* LK = static_cast<T*>(s.level_k);
   T* LV = static_cast<T*>(s.level_v);
@@ -520,8 +517,8 @@ __global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logk
       }
       __syncthreads();
       // Shift: slot j (1 <= j < Bs) <- pool[rem + j]; sources lie above the written slots.
-      for (int j0 = 1; j0 < Bs; j0 += kTileRows - 1) {
-        const int jn = min(kTileRows - 1, Bs - j0);
+      for (int j0 = 1; j0 < Bs; j0 += TILE - 1) {
+        const int jn = min(TILE - 1, Bs - j0);
         for (int item = tid; item < jn * D; item += nt) {
           const int r = item / D, d = item % D;
           tk[(1 + r) * D + d] = pool_k(rem + j0 + r)[d];
@@ -559,18 +556,18 @@ __global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logk
     Meta pend{};
     // Every row's source pointers are resolved once (one thread per row) into rowp[buf] before
     // a barrier that precedes the tile's issue, so a 16-byte copy costs an offset, not the
-    // pool / token / scratch address arithmetic.  Tile t0 uses buffer (t0 / kTileRows) & 1.
+    // pool / token / scratch address arithmetic.  Tile t0 uses buffer (t0 / TILE) & 1.
     auto resolve = [&](int t0, int buf) {
-      const int tn = min(kTileRows, total - t0);
+      const int tn = min(TILE, total - t0);
       if (tid < tn) {
         rowp[buf][0][tid] = pool_k(t0 + tid);
         rowp[buf][1][tid] = pool_v(t0 + tid);
       }
     };
     auto issue = [&](int t0, int buf) {
-      const int tn = min(kTileRows, total - t0);
-      T* tk = tkb + (size_t)buf * kTileRows * D;
-      T* tv = tvb + (size_t)buf * kTileRows * D;
+      const int tn = min(TILE, total - t0);
+      T* tk = tkb + (size_t)buf * TILE * D;
+      T* tv = tvb + (size_t)buf * TILE * D;
       for (int item = tid; item < tn * DV * 2; item += nt) {
         const int r = item / (2 * DV), f = (item / DV) & 1, v = item % DV;
         cp_async16((f ? tv : tk) + r * D + v * VN, rowp[buf][f][r] + v * VN);
@@ -579,22 +576,22 @@ __global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logk
       if (tid < tn) pend = pool_m(t0 + tid);
     };
     resolve(0, 0);
-    if (kTileRows < total) resolve(kTileRows, 1);
+    if (TILE < total) resolve(TILE, 1);
     __syncthreads();
     issue(0, 0);
     int cur = 0;
-    for (int t0 = 0; t0 < total; t0 += kTileRows) {
-      const int tn = min(kTileRows, total - t0);
-      T* tk = tkb + (size_t)cur * kTileRows * D;
-      T* tv = tvb + (size_t)cur * kTileRows * D;
-      Meta* tm = tmb + cur * kTileRows;
+    for (int t0 = 0; t0 < total; t0 += TILE) {
+      const int tn = min(TILE, total - t0);
+      T* tk = tkb + (size_t)cur * TILE * D;
+      T* tv = tvb + (size_t)cur * TILE * D;
+      Meta* tm = tmb + cur * TILE;
       cp_async_wait_all();
       if (tid < tn) tm[tid] = pend;
       __syncthreads();
-      if (t0 + kTileRows < total) issue(t0 + kTileRows, cur ^ 1);
+      if (t0 + TILE < total) issue(t0 + TILE, cur ^ 1);
       // Buffer `cur` was last read by this tile's issue, before the barrier above; the next
       // reader (tile t0 + 2 tiles) issues after the next iteration's barrier.
-      if (t0 + 2 * kTileRows < total) resolve(t0 + 2 * kTileRows, cur);
+      if (t0 + 2 * TILE < total) resolve(t0 + 2 * TILE, cur);
       const int mend = min(t0 + tn, npair);  // merge rows of this tile: [t0, mend)
       if (mend > t0)
         merge_tile<T, BETA, DC>(x, g, w, tk, tv, tm, t0, mend, npair, ell, nb, 0, bloss, bener, bcut, &sh_exact);
@@ -635,6 +632,21 @@ __global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logk
     st.m = ncarry;
     nb = 1 - nb;
   }
+}
+
+inline size_t walk_smem(const Geo& g, size_t esize, int tile) {
+  // two K/V tile buffers, two metadata tiles, token positions and sources
+  return 4 * (size_t)tile * g.D * esize + 2 * (size_t)tile * sizeof(Meta) + (size_t)g.NW * (sizeof(int64_t) + sizeof(int)) +
+         16;
+}
+
+// The sequential walk as its own kernel, one CTA per lane (used when the parallel cascade is off).
+template <typename T, bool BETA, int DC>
+__global__ void __launch_bounds__(kCascadeThreads, 2) cascade_kernel(Geo g, logkv_state_t s, Work w) {
+  pdl_entry();
+  const LaneCtx<T> x = make_ctx<T>(g, s, w);
+  if (w.plan_type[x.lane] == kJobNone) return;
+  cascade_walk<T, BETA, DC, kTileRows>(x, g, s, w);
 }
 
 // ---------------------------------------------------------------- parallel cascade
@@ -1025,12 +1037,16 @@ __global__ void __launch_bounds__(kMergeWarps * 32) cascade_merge_kernel(Geo g, 
 }
 
 constexpr int kMoveThreads = 256;
+constexpr int kMoveWalkTile = 32;   // tile rows of a sequential walk inside the move kernel
 
-inline size_t move_smem(int D, int Bs, size_t esize) {
-  return 2 * (size_t)Bs * D * esize + (size_t)Bs * sizeof(Meta) + 16;
+inline size_t move_smem(const Geo& g, size_t esize) {
+  const size_t moves = 2 * (size_t)g.Bs * g.D * esize + (size_t)g.Bs * sizeof(Meta) + 16;
+  const size_t walk = walk_smem(g, esize, kMoveWalkTile);
+  return moves > walk ? moves : walk;
 }
 
-// Grid (L, K, B * G): one CTA per (lane, level) of the lanes the merge kernel handles.  The rows the level writes (a filling level: its incoming rows,
+// Grid (L, K, B * G): one CTA per (lane, level) of the lanes the merge kernel handles (and the
+// level-0 CTA of every lane left to the sequential walk).  The rows the level writes (a filling level: its incoming rows,
 // to slots cnt..; a merging level: all its survivors, pool rows npair.., to slots 0..) are first
 // brought into shared memory by TMA bulk copies (the stored survivors and carried rows are
 // contiguous runs, one copy each; level-0 token rows one copy per row), then written back with one
@@ -1040,13 +1056,21 @@ inline size_t move_smem(int D, int Bs, size_t esize) {
 // dependency wait; carried rows, a delayed lane's staged rows and every write come after it.
 // A merging level then zeroes its tail slots.  The copy wait is bounded: past the limit the
 // status word gets kStatusCopyTimeout and nothing is written.
-template <typename T>
-__global__ void __launch_bounds__(kMoveThreads) cascade_move_kernel(Geo g, logkv_state_t s, Work w) {
+template <typename T, bool BETA, int DC>
+__global__ void __launch_bounds__(kMoveThreads, 3) cascade_move_kernel(Geo g, logkv_state_t s, Work w) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int tid = threadIdx.x, nt = blockDim.x, l = blockIdx.x, bgi = blockIdx.z;
   const LaneCtx<T> x = make_ctx_at<T>(g, s, w, blockIdx.y, bgi % g.G, bgi / g.G);
   __shared__ LevelPlan lp[kMaxLevels];
   const int mode = plan_lane(g, w, x.lane, lp);
+  if (mode == 2) {
+    // A lane the parallel kernels leave alone: its level-0 CTA walks the levels in order, once
+    // the prepare kernel (staged re-inserts, cleared clusters) has completed.
+    if (l != 0) return;
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    cascade_walk<T, BETA, DC, kMoveWalkTile>(x, g, s, w);
+    return;
+  }
   const LevelPlan p = lp[l];
   if (mode != 1 || (p.kind != kLvlFill && p.kind != kLvlMerge)) return;
   const int D = g.D, Bs = g.Bs;
