@@ -559,13 +559,20 @@ KVSHARD = dict(workload="qwen3-1.7b-shaped streaming prefill flush, one sequence
 
 
 def bench_kv_sharded(args, rank, world, local_rank):
-    """One long sequence, its 8 KV groups split over the ranks (G / world each): every flush
-    all-gathers the ranks' per-group span parts (NCCL) between its score and commit phases.
-    Whole steps captured in a CUDA graph on one stream, device time, max over ranks."""
+    """One long sequence, its 8 KV groups split over the ranks (G / world each).  Every chunk of
+    the 28 layers is flushed through ``sharding.BatchedFlush``: each layer's score phase on its
+    own stream, ONE all-gather of all layers' span parts per chunk (NCCL), then each layer's
+    commit on its stream.  Timed two ways, whole steps captured in a CUDA graph, device time,
+    max over ranks: the flushes alone (``value``, per layer-flush), and in model order
+    (``flush_attend``, per layer-chunk): per layer the chunk attention of the rank's query heads
+    over its cache and the all-gather of the attention outputs (``sharding.gather_heads``), then
+    the layer's score phase on its stream, the chunk's one span-part exchange after the last
+    layer, and the layers' commits beside the next chunk's attention."""
     import torch
     import torch.distributed as dist
+    from logkv_b200.attention import log_kv_chunk_attention
     from logkv_b200.cache import LogStructuredKVCache
-    from logkv_b200.sharding import group_block
+    from logkv_b200.sharding import BatchedFlush, gather_heads, group_block
     device = torch.device("cuda", local_rank)
     cfg = dict(KVSHARD)
     cfg["layers"] = args.kv_layers
@@ -581,42 +588,74 @@ def bench_kv_sharded(args, rank, world, local_rank):
         semantic_replay_updates=True, alpha_exact_tokens=cfg["exact"], alpha_span_max_tokens=cfg["span_cap"],
         beta_novelty=cfg["beta"], beta_adaptive_merge=cfg["beta"], cos_cache=cos, sin_cache=sin,
         rope_n_elem=cfg["head_dim"], kv_shard_group=group) for _ in range(cfg["layers"])]
+    batch = BatchedFlush(caches, group)
     n_chunks = cfg["tokens"] // cfg["chunk"]
     flushes_per_step = cfg["layers"] * (n_chunks - cfg["recent"] // cfg["chunk"])
+    H_local, D, T = 16 // cfg["groups"] * (hi - lo), cfg["head_dim"], cfg["chunk"]
+    gen = torch.Generator(device=device).manual_seed(99 + rank)
+    q = torch.randn(1, H_local, T, D, generator=gen, device=device).to(torch.bfloat16)
+    out = torch.empty_like(q)
     stream = torch.cuda.Stream(device)
-    with torch.cuda.stream(stream):
-        for _ in range(max(1, args.warmup)):
-            run_step(caches, layers, ends_host, ends_dev)
-    torch.cuda.synchronize()
-    # One CUDA graph per step (the span-part all-gathers are captured with the flushes, in the
-    # same order on every rank); released before the process group goes away.
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        run_step(caches, layers, ends_host, ends_dev)
-    with torch.cuda.stream(stream):
-        graph.replay()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        start.record(stream)
-        for _ in range(args.steps):
+    lstreams = [torch.cuda.Stream(device) for _ in caches]
+
+    def step(attend):
+        main = torch.cuda.current_stream()
+        for st in lstreams:
+            st.wait_stream(main)
+        for cache, st in zip(caches, lstreams):
+            with torch.cuda.stream(st):
+                cache.reset_parameters()
+        for c in range(n_chunks):
+            for i, cache in enumerate(caches):
+                k, kr, v = layers[i][c]
+                if attend:
+                    main.wait_stream(lstreams[i])          # the layer's previous commit
+                    log_kv_chunk_attention(cache, q, k, v, D ** -0.5, 0.0, out=out)
+                    if world > 1:
+                        gather_heads(out, group)
+                batch.begin(i, dict(k=k, v=v, k_raw=kr, span_ends=ends_host, span_ends_device=ends_dev), lstreams[i])
+            batch.finish()
+        for st in lstreams:
+            main.wait_stream(st)
+
+    res = {}
+    for mode in ("flush", "flush_attend"):
+        with torch.no_grad(), torch.cuda.stream(stream):
+            for _ in range(max(1, args.warmup)):
+                step(mode == "flush_attend")
+            torch.cuda.synchronize()
+            # One CUDA graph per step (every collective captured in the same order on every
+            # rank); released before the process group goes away.
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                step(mode == "flush_attend")
             graph.replay()
-        stop.record(stream)
-    torch.cuda.synchronize()
-    del graph
-    ms = start.elapsed_time(stop)
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+        del graph
+        t = torch.tensor([e0.elapsed_time(e1)], device=device)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res[mode] = t.item() * 1000.0 / args.steps
     assert all(c.read_status() == 0 for c in caches)
-    parts = caches[0]._span_gather.numel() * 4 if caches[0]._span_gather is not None else 0
     return {"metric": "flush us per 2048-tok chunk/layer, one sequence KV-head-sharded", "unit": "us",
-            "value": round(ms * 1000.0 / (args.steps * flushes_per_step), 2), "higher_is_better": False,
+            "value": round(res["flush"] / flushes_per_step, 2), "higher_is_better": False,
             "n_gpus": world, "scaling": "strong", "groups_per_rank": hi - lo, "flushes_per_step": flushes_per_step,
-            "exchange_bytes_per_flush": parts, "timing": "CUDA-graph steps on one stream (NCCL inside), max over ranks",
+            "exchange_bytes_per_chunk": batch.send.numel() * 4 * world,
+            "flush_attend": {"metric": "sharded flush-and-attend prefill us per 2048-token chunk/layer (chunk "
+                                       "attention of the rank's heads + output all-gather + add_recent)",
+                             "unit": "us", "value": round(res["flush_attend"] / (cfg["layers"] * n_chunks), 2),
+                             "heads_per_rank": H_local,
+                             "gather_bytes_per_layer_chunk": out.numel() * out.element_size() * world},
+            "timing": "CUDA-graph steps, layer flushes on per-layer streams, one span-part all-gather per chunk, "
+                      "max over ranks",
             "config": {k: cfg[k] for k in ("workload", "layers", "groups", "head_dim", "clusters", "B", "recent",
                                            "granularity", "exact", "span_cap", "tokens")}}
 

@@ -214,6 +214,15 @@ LOGKV_API int logkv_flush_commit(const logkv_layout_t* layout, const logkv_state
                                  int32_t recent_count, void* workspace, size_t workspace_bytes,
                                  const float* partials_all, int32_t ranks, void* stream);
 /*
+ * logkv_flush_commit with rank r's parts at partials_all + r * rank_stride floats (rank_stride at
+ * least the rank's part count): the layout of one all-gather of many layers' parts at once, where
+ * each rank sends its layers' parts back to back.
+ */
+LOGKV_API int logkv_flush_commit_strided(const logkv_layout_t* layout, const logkv_state_t* state,
+                                         int32_t flush_tokens, int32_t recent_count, void* workspace,
+                                         size_t workspace_bytes, const float* partials_all, int32_t ranks,
+                                         int64_t rank_stride, void* stream);
+/*
  * Route overlap (replaces the side-stream route decisions of LOGKV_ROUTE_OVERLAP,
  * litgpt/log_kv_cache.py:3814-3849).  A flush's decisions (snapshot, span cut, span scores,
  * attach decisions, span choice, seeding, per-cluster plan) read only the flushed window rows,

@@ -117,6 +117,9 @@ def lib() -> ctypes.CDLL:
         handle.logkv_flush_scores.argtypes = flush_args + [ctypes.c_void_p]
         handle.logkv_flush_commit.restype = ctypes.c_int
         handle.logkv_flush_commit.argtypes = flush_args + [ctypes.c_void_p, ctypes.c_int32, ctypes.c_void_p]
+        handle.logkv_flush_commit_strided.restype = ctypes.c_int
+        handle.logkv_flush_commit_strided.argtypes = flush_args + [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
+                                                                   ctypes.c_void_p]
         for name in ("logkv_flush_decide", "logkv_flush_apply"):
             getattr(handle, name).restype = ctypes.c_int
             getattr(handle, name).argtypes = flush_args + [ctypes.c_void_p]

@@ -247,6 +247,7 @@ class LogStructuredKVCache(nn.Module):
         self._route_ready_rows = 0
         self._route_ready_capture = 0
         self._route_done = None
+        self._deferred_take = None   # flush started by add_recent_deferred, committed by commit_deferred
 
     # ------------------------------------------------------------------ C-ABI state
     def _apply(self, fn, *args, **kwargs):
@@ -393,13 +394,25 @@ class LogStructuredKVCache(nn.Module):
         self._route_ready_rows = self.recent_count
         self._route_ready_capture = _lib.capture_id(dev)
 
+    def _flush_args(self, take: int):
+        state = self._state_struct()
+        return (ctypes.byref(self._layout), ctypes.byref(state), int(take), int(self.recent_count),
+                ctypes.c_void_p(self._workspace.data_ptr()), self._workspace.numel(),
+                ctypes.c_void_p(_lib.stream_ptr(self.level_k.device)))
+
+    def _local_parts(self, take: int) -> torch.Tensor:
+        """This rank's per-group span parts of a flush of ``take`` tokens (a workspace view)."""
+        ptr, count = ctypes.POINTER(ctypes.c_float)(), ctypes.c_size_t()
+        _lib.check(_lib.lib().logkv_flush_partials(ctypes.byref(self._layout), int(take),
+                                                   ctypes.c_void_p(self._workspace.data_ptr()), ctypes.byref(ptr),
+                                                   ctypes.byref(count)), "logkv_flush_partials")
+        offset = ctypes.cast(ptr, ctypes.c_void_p).value - self._workspace.data_ptr()
+        return self._workspace[offset:offset + 4 * count.value].view(torch.float32)
+
     def flush_device(self, take: int) -> None:
         """One device flush of the ``take`` oldest window tokens plus the window shift."""
         self._ladder_epoch += 1
-        state = self._state_struct()
-        args = (ctypes.byref(self._layout), ctypes.byref(state), int(take), int(self.recent_count),
-                ctypes.c_void_p(self._workspace.data_ptr()), self._workspace.numel(),
-                ctypes.c_void_p(_lib.stream_ptr(self.level_k.device)))
+        args = self._flush_args(take)
         if self.kv_shard_group is not None:
             self._sharded_flush(args, int(take))
             return
@@ -425,14 +438,10 @@ class LogStructuredKVCache(nn.Module):
         from .sharding import gather_span_parts
         lib = _lib.lib()
         _lib.check(lib.logkv_flush_scores(*args), "logkv_flush_scores")
-        ptr, count = ctypes.POINTER(ctypes.c_float)(), ctypes.c_size_t()
-        _lib.check(lib.logkv_flush_partials(ctypes.byref(self._layout), take, ctypes.c_void_p(self._workspace.data_ptr()),
-                                            ctypes.byref(ptr), ctypes.byref(count)), "logkv_flush_partials")
-        offset = ctypes.cast(ptr, ctypes.c_void_p).value - self._workspace.data_ptr()
-        local = self._workspace[offset:offset + 4 * count.value].view(torch.float32)
+        local = self._local_parts(take)
         world = dist.get_world_size(self.kv_shard_group)
-        if self._span_gather is None or self._span_gather.numel() != world * count.value:
-            self._span_gather = torch.empty(world * count.value, dtype=torch.float32, device=self._workspace.device)
+        if self._span_gather is None or self._span_gather.numel() != world * local.numel():
+            self._span_gather = torch.empty(world * local.numel(), dtype=torch.float32, device=self._workspace.device)
         gather_span_parts(local, self.kv_shard_group, out=self._span_gather)
         _lib.check(lib.logkv_flush_commit(*args[:6], ctypes.c_void_p(self._span_gather.data_ptr()), world, args[6]),
                    "logkv_flush_commit")
@@ -500,12 +509,65 @@ class LogStructuredKVCache(nn.Module):
         the same flags already on the device, so the call issues no host-to-device
         copy and can be captured in a CUDA graph.
         """
-        if k_raw is None:
-            raise ValueError("semantic LogKV add_recent requires pre-RoPE k_raw")
         replaying = any(v_ is not None for v_ in replay.values())
         if self._active_updates is None and replaying:
             raise NotImplementedError("op-log replay outside an update tape context is not implemented by "
                                       "logkv_b200 (replay a recorded update tape instead)")
+        self._append_chunk(k, v, k_raw, input_pos, span_ends, span_ends_device)
+        for take in self._pending_flushes():
+            if self._active_updates is not None:
+                self._flush_with_updates(take, record_op_log, replaying or self._replaying_updates)
+            else:
+                self.flush_device(take)
+            if record_op_log:
+                self._append_op_log(take)
+            self._finish_flush(take)
+
+    def add_recent_deferred(self, k, v, *, k_raw=None, input_pos=None, span_ends=None, span_ends_device=None):
+        """add_recent whose flush stops before the span choice, so that the caller can exchange many
+        caches' span parts in one collective (``logkv_b200.sharding.BatchedFlush``); no reference
+        counterpart.  Appends the chunk; when it makes the window overflow by one flush, runs the
+        flush up to this cache's per-group span parts (``logkv_flush_scores``) and returns them (a
+        [parts] float32 view of the workspace); ``commit_deferred`` must follow before any other
+        call.  Returns None when the chunk flushes nothing."""
+        if self._active_updates is not None:
+            raise NotImplementedError("deferred flushes do not record or replay update tapes")
+        if self._deferred_take is not None:
+            raise RuntimeError("commit_deferred must follow add_recent_deferred")
+        self._append_chunk(k, v, k_raw, input_pos, span_ends, span_ends_device)
+        takes = list(self._pending_flushes())
+        if not takes:
+            return None
+        if len(takes) > 1:
+            raise NotImplementedError("a deferred chunk may overflow the window by one flush only")
+        take = takes[0]
+        self._ladder_epoch += 1
+        args = self._flush_args(take)
+        lib = _lib.lib()
+        _lib.check(lib.logkv_flush_scores(*args), "logkv_flush_scores")
+        self._deferred_take = take
+        return self._local_parts(take)
+
+    def commit_deferred(self, parts_all=None, ranks: int = 1, rank_stride: int = 0) -> None:
+        """Finish the flush ``add_recent_deferred`` started: rank r's span parts of this cache at
+        parts_all[r * rank_stride:] (float32 on the device; None with ranks == 1: this cache's own)."""
+        take = self._deferred_take
+        if take is None:
+            raise RuntimeError("no deferred flush to commit")
+        if ranks > 1 and parts_all is None:
+            raise ValueError("the gathered span parts of every rank are needed")
+        args = self._flush_args(take)
+        ptr = ctypes.c_void_p(parts_all.data_ptr()) if parts_all is not None else None
+        stride = int(rank_stride) if rank_stride else int(self._local_parts(take).numel())
+        _lib.check(_lib.lib().logkv_flush_commit_strided(*args[:6], ptr, int(ranks), stride, args[6]),
+                   "logkv_flush_commit_strided")
+        self._deferred_take = None
+        self._finish_flush(take)
+
+    def _append_chunk(self, k, v, k_raw, input_pos, span_ends, span_ends_device) -> None:
+        """Validation and the window write of add_recent (log_kv_cache.py:5668-5707)."""
+        if k_raw is None:
+            raise ValueError("semantic LogKV add_recent requires pre-RoPE k_raw")
         n = k.size(2)
         if n > self.recent_size:
             raise ValueError(f"chunk size {n} exceeds recent_size {self.recent_size}")
@@ -529,24 +591,27 @@ class LogStructuredKVCache(nn.Module):
             ends.copy_(host.pin_memory() if self.recent_pos.is_cuda else host, non_blocking=True)
         self._append_window(k, k_raw, v, positions, ends, n)
         self.recent_count += n
+
+    def _pending_flushes(self):
+        """Sizes of the flushes the window overflow needs (_semantic_add_recent :5708-5718)."""
         overflow = self.recent_count - self.recent_size
-        if overflow > 0:
-            gran = self.semantic_flush_granularity
-            pending = gran * ((overflow + gran - 1) // gran)
-            while pending > 0:
-                take = min(gran, pending)
-                if take > self.recent_count:
-                    raise RuntimeError(f"semantic LogKV cannot flush {take} tokens from recent_count={self.recent_count}")
-                if self._active_updates is not None:
-                    self._flush_with_updates(take, record_op_log, replaying or self._replaying_updates)
-                else:
-                    self.flush_device(take)
-                if record_op_log:
-                    self._append_op_log(take)
-                self._flush_cursor += 1
-                self.recent_count -= take
-                pending -= take
-                self._route_mark_ready()
+        if overflow <= 0:
+            return
+        gran = self.semantic_flush_granularity
+        pending = gran * ((overflow + gran - 1) // gran)
+        left = self.recent_count
+        while pending > 0:
+            take = min(gran, pending)
+            if take > left:
+                raise RuntimeError(f"semantic LogKV cannot flush {take} tokens from recent_count={left}")
+            yield take
+            left -= take
+            pending -= take
+
+    def _finish_flush(self, take: int) -> None:
+        self._flush_cursor += 1
+        self.recent_count -= take
+        self._route_mark_ready()
 
     def _append_window(self, k, k_raw, v, positions, ends, n: int) -> None:
         """The chunk into window rows [recent_count, recent_count + n) with one kernel
@@ -646,4 +711,5 @@ class LogStructuredKVCache(nn.Module):
         self.recent_count = 0
         self._flush_cursor = 0
         self._route_ready = None
+        self._deferred_take = None
         self._ladder_epoch += 1

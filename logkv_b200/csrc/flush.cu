@@ -558,7 +558,8 @@ static int launch_replay(const Geo& g, const logkv_state_t& s, const Work& w, co
 static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
                      int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream, cudaEvent_t* ev,
                      int phases = kPhaseAll, const float* gpart_all = nullptr, int ranks = 1,
-                     int tape_mode = kTapeNone, void* tape = nullptr, size_t tape_bytes = 0) {
+                     int tape_mode = kTapeNone, void* tape = nullptr, size_t tape_bytes = 0,
+                     long long rank_stride = 0) {
   const int v = validate(layout, flush_tokens);
   if (v != LOGKV_OK) return v;
   if (!state || !workspace) return LOGKV_E_POINTER;
@@ -581,6 +582,8 @@ static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, i
   if (ranks < 1 || (ranks > 1 && !gpart_all)) return LOGKV_E_POINTER;
   Geo g = make_geo(*layout, flush_tokens, recent_count);
   g.shard_ranks = ranks;
+  g.gpart_stride = rank_stride > 0 ? rank_stride : (long long)g.B * g.NC * g.G * 2;
+  if (rank_stride > 0 && rank_stride < (long long)g.B * g.NC * g.G * 2) return LOGKV_E_SHAPE;
   Work w{};
   const size_t need = carve(g, esize, static_cast<char*>(workspace), &w);
   if (workspace_bytes < need) return LOGKV_E_WORKSPACE;
@@ -727,6 +730,15 @@ extern "C" int logkv_flush_commit(const logkv_layout_t* layout, const logkv_stat
                                   const float* partials_all, int32_t ranks, void* stream) {
   return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream, nullptr,
                    kPhaseCommit, partials_all, ranks);
+}
+
+extern "C" int logkv_flush_commit_strided(const logkv_layout_t* layout, const logkv_state_t* state,
+                                          int32_t flush_tokens, int32_t recent_count, void* workspace,
+                                          size_t workspace_bytes, const float* partials_all, int32_t ranks,
+                                          int64_t rank_stride, void* stream) {
+  if (rank_stride < 1) return LOGKV_E_SHAPE;
+  return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream, nullptr,
+                   kPhaseCommit, partials_all, ranks, kTapeNone, nullptr, 0, rank_stride);
 }
 
 extern "C" int logkv_flush_partials(const logkv_layout_t* layout, int32_t flush_tokens, void* workspace,

@@ -461,7 +461,7 @@ __global__ void __launch_bounds__(1024) alpha_choose_kernel(Geo g, logkv_state_t
     auto part = [&](int grp, int k) -> float {
       if (!w.gpart_all) return w.gpart[((size_t)c * g.G + grp) * 2 + k];
       const int r = grp / g.G, gl = grp % g.G;
-      return w.gpart_all[((((size_t)r * g.B + b) * NC + i) * g.G + gl) * 2 + k];
+      return w.gpart_all[(size_t)r * g.gpart_stride + (((size_t)b * NC + i) * g.G + gl) * 2 + k];
     };
     float sf;
     if (!g.beta) {

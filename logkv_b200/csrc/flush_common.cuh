@@ -22,6 +22,7 @@ struct Geo {
   int sort_cap;           // power of two >= L * Bs + NW (delayed re-insert sort)
   int seed_staged;        // seeding CTAs keep their token rows in shared memory (set per dtype at launch)
   int shard_ranks;        // KV-head sharding: ranks holding G groups each (1 = unsharded)
+  long long gpart_stride; // KV-head sharding: floats between two ranks' span parts in gpart_all
   int tape;               // update tape: kTapeNone, kTapeRecord (save Beta cuts), kTapeReplay (use them)
   float eta, g0, lam;
 };
@@ -34,7 +35,7 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
 
-// TMA bulk copies (cp.async.bulk, no multicast) completing on a shared-memory mbarrier.  Both
+// TMA bulk copies (cp.async.bulk into this CTA's own shared memory) completing on an mbarrier.  Both
 // addresses 16-byte aligned, sizes multiples of 16 bytes.
 __device__ __forceinline__ unsigned smem_u32(const void* p) { return (unsigned)__cvta_generic_to_shared(p); }
 __device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {

@@ -62,3 +62,34 @@ def test_two_rank_gathers_follow_global_group_order():
     out = manager.dict()
     mp.spawn(worker, args=(2, free_port(), out), nprocs=2, join=True)
     assert dict(out) == {0: True, 1: True}
+
+
+def batched_worker(rank: int, world: int, port: int, out: dict) -> None:
+    """Many layers' parts packed back to back, one all-gather: layer i of rank r is read at
+    r * (layers * parts) + i * parts, the strided layout logkv_flush_commit_strided reads."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        layers, parts = 5, 11
+        gen = torch.Generator().manual_seed(7)
+        every = torch.randn(world, layers, parts, generator=gen)   # [rank, layer, parts]
+        send = every[rank].reshape(-1).contiguous()
+        recv = torch.empty(world * layers * parts)
+        dist.all_gather_into_tensor(recv, send)
+        stride = layers * parts
+        ok = True
+        for i in range(layers):
+            base = recv[i * parts:]
+            for r in range(world):
+                ok &= bool(torch.equal(base[r * stride:r * stride + parts], every[r, i]))
+        out[rank] = ok
+    finally:
+        dist.destroy_process_group()
+
+
+def test_batched_gather_layout_matches_strided_commit():
+    ctx = mp.get_context("spawn")
+    manager = ctx.Manager()
+    out = manager.dict()
+    mp.spawn(batched_worker, args=(2, free_port(), out), nprocs=2, join=True)
+    assert dict(out) == {0: True, 1: True}
