@@ -820,6 +820,95 @@ def bench_decode(args, rank, world, local_rank):
             "config": {k_: cfg[k_] for k_ in cfg}}
 
 
+def bench_generate(args, rank, world, local_rank):
+    """BASELINE configs[3] as the model runs it: 512 generated tokens per sequence, every layer's
+    decode step through ``LogKVDecoder`` (the reference's pending-token pairing: attention over the
+    cache and [pending, current], then add_recent of the pair; the first pair overflows the full
+    2048-token window and flushes 2048 tokens, batch-wide).  Eager (every step's window length
+    differs), device time, max over ranks.  The token inputs (q, k, k_raw, v) of every step are
+    copied from pinned host memory and the last layer's output is read back every token, inside
+    the timed region.  Layer caches are independent and identical in work, so when the 28 layers'
+    caches do not all fit in memory the leg runs as many distinct caches as fit and reports the
+    28-layer rate from the measured time per layer-token."""
+    import torch
+    import torch.distributed as dist
+    from logkv_b200.attention import refresh_prefix
+    from logkv_b200.decode import LogKVDecoder
+    from logkv_b200.workload import rope_tables
+    device = torch.device("cuda", local_rank)
+    cfg = dict(DECODE, batch=args.decode_batch)
+    batch = max(1, cfg["batch"] // world)
+    H, G, D = cfg["heads"], cfg["groups"], cfg["head_dim"]
+    n_tokens = args.generate_tokens
+    cos_np, sin_np = rope_tables(cfg["max_seq"] + 1024, D, base=1e6)
+    cos, sin = torch.from_numpy(cos_np).to(device), torch.from_numpy(sin_np).to(device)
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info(device)[0]
+    first = prefill_decode_cache(torch, cfg, batch, device, cos, sin, seed=500 + rank)
+    refresh_prefix(first)
+    torch.cuda.synchronize()
+    per_cache = max(1, free0 - torch.cuda.mem_get_info(device)[0])
+    fit = int(0.8 * torch.cuda.mem_get_info(device)[0] // per_cache) + 1
+    layers_real = max(1, min(cfg["layers"], fit))
+    if world > 1:
+        t = torch.tensor([layers_real], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        layers_real = int(t.item())
+    caches = [first] + [prefill_decode_cache(torch, cfg, batch, device, cos, sin, seed=500 + rank + 17 * i)
+                        for i in range(1, layers_real)]
+    for c in caches:
+        refresh_prefix(c)
+    scale = D ** -0.5
+    decoders = [LogKVDecoder(c, scale) for c in caches]
+    gen = torch.Generator(device="cpu").manual_seed(9 + rank)
+    nsets = 8   # distinct token inputs, cycled
+    host = [tuple(torch.randn(batch, n, 1, D, generator=gen).to(torch.bfloat16).pin_memory()
+                  for n in (H, G, G, G)) for _ in range(nsets)]
+    dev_in = [tuple(torch.empty_like(t, device=device) for t in host[0]) for _ in range(2)]
+    ends_host = [[False] for _ in range(batch)]
+    ends_dev = torch.zeros(batch, 1, dtype=torch.uint8, device=device)
+    outs = [torch.empty(batch, H, 1, D, dtype=torch.bfloat16, device=device) for _ in caches]
+    readback = torch.empty(batch, H, 1, D, dtype=torch.bfloat16).pin_memory()
+    stream = torch.cuda.Stream(device)
+    flushes0 = sum(c.read_counters()["flushes"] for c in caches)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.no_grad(), torch.cuda.stream(stream), ClockSampler(local_rank) as clocks:
+        e0.record(stream)
+        for t in range(n_tokens):
+            buf = dev_in[t % 2]
+            for d_, h_ in zip(buf, host[t % nsets]):
+                d_.copy_(h_, non_blocking=True)
+            q, k, kr, v = buf
+            for dec, o in zip(decoders, outs):
+                dec.step(q, k, v, k_raw=kr, span_ends=ends_host, span_ends_device=ends_dev, out=o)
+            readback.copy_(outs[-1], non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    t_ = torch.tensor([ms], device=device)
+    if world > 1:
+        dist.all_reduce(t_, op=dist.ReduceOp.MAX)
+    ms = float(t_.item())
+    flushes = sum(c.read_counters()["flushes"] for c in caches) - flushes0
+    assert all(c.read_status() == 0 for c in caches)
+    us_layer_token = ms * 1000.0 / (n_tokens * layers_real)
+    tok_s = batch * world / (us_layer_token * cfg["layers"] * 1e-6)
+    step_bytes = sum(t.numel() * t.element_size() for t in host[0])
+    return {"metric": "decode tok/s over a 32K compressed cache (28 layers), generating with commits",
+            "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": world, "batch": batch * world,
+            "tokens_per_sequence": n_tokens, "scaling": "strong", "us_per_layer_token": round(us_layer_token, 2),
+            "layers_timed": layers_real, "flushes": flushes,
+            "e2e": {"value": round(tok_s, 1), "unit": "tok/s", "h2d_bytes_per_step": step_bytes,
+                    "d2h_bytes_per_step": readback.numel() * readback.element_size()},
+            "timing": "eager steps (public LogKVDecoder API), host token inputs copied in and the last layer's "
+                      "output read back every token, device time, max over ranks",
+            "clocks": clocks.summary(),
+            "config": {k_: cfg[k_] for k_ in cfg}}
+
+
 def bench_prefill(args, rank, world, local_rank):
     """Chunk attention of one 2048-token chunk (16 q / 8 KV heads) over a pre-filled cache, per layer."""
     import torch
@@ -978,6 +1067,8 @@ def main():
     ap.add_argument("--layers", type=int, default=WORKLOAD["layers"], help="layer caches (profiling runs only)")
     ap.add_argument("--decode-steps", type=int, default=32, help="timed decode steps (0: skip the decode leg)")
     ap.add_argument("--decode-batch", type=int, default=DECODE["batch"], help="decode sequences (profiling runs only)")
+    ap.add_argument("--generate-tokens", type=int, default=512,
+                    help="tokens generated per sequence in the decode-with-commits leg (0: skip it)")
     ap.add_argument("--streams", type=int, default=28, help="streams the layers' flushes are spread over")
     ap.add_argument("--flush-attend", type=int, default=1, help="run the flush-and-attend prefill leg (0: skip)")
     ap.add_argument("--unified", type=int, default=1, help="run the unified-route leg (0: skip)")
@@ -1020,6 +1111,10 @@ def main():
     fa = bench_flush_attend(args, rank, world, local_rank, inputs) if args.flush_attend else None
     del inputs
     dec = bench_decode(args, rank, world, local_rank) if args.decode_steps > 0 else None
+    if dec is not None and args.generate_tokens > 0:
+        torch.cuda.empty_cache()
+        dec["generate"] = bench_generate(args, rank, world, local_rank)
+        torch.cuda.empty_cache()
     pre = bench_prefill(args, rank, world, local_rank) if args.decode_steps > 0 else None
     kvs = bench_kv_sharded(args, rank, world, local_rank) if args.kv_layers > 0 else None
     uni = bench_unified(args, rank, world, local_rank) if args.unified else None

@@ -106,10 +106,10 @@ LOGKV_API int logkv_pack_mid(const logkv_layout_t* layout, const logkv_state_t* 
  * CUDA cores for 1, 2, 4 or 8 query rows per lane (longer chunks take several calls).
  */
 typedef struct logkv_attention_args {
-  const void* q;        /* [B,H,tokens,D] storage dtype, post-RoPE */
+  const void* q;        /* [B,H,q_stride,D] storage dtype, post-RoPE */
   const void* k_new;    /* [B,G,tokens,D] post-RoPE                */
   const void* v_new;    /* [B,G,tokens,D]                          */
-  void* out;            /* [B,H,tokens,D] storage dtype; rows [q_offset, q_offset + q_tokens) written */
+  void* out;            /* [B,H,q_stride,D] storage dtype; rows [q_offset, q_offset + q_tokens) written */
   int32_t heads;        /* H, a multiple of groups                 */
   int32_t tokens;       /* new tokens (>= 1)                       */
   int32_t q_offset;     /* first query token of this call          */
@@ -118,6 +118,9 @@ typedef struct logkv_attention_args {
   int32_t causal;       /* 1: causal tail over the new tokens, 0: none */
   float scale;
   float qx;
+  int32_t q_stride;     /* query / output rows per head: 0 = tokens; fewer (causal 0 only) when the queries
+                           are the first of the new tokens, e.g. a decode step whose single query sees a
+                           pending token and itself (litgpt/model.py:1219-1226, causal_tail=0) */
 } logkv_attention_args_t;
 
 /* Scratch bytes of logkv_attention (zero-fill it once when allocated; calls leave it reusable). */

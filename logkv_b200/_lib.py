@@ -74,7 +74,8 @@ class AttentionArgs(ctypes.Structure):
     _fields_ = [("q", ctypes.c_void_p), ("k_new", ctypes.c_void_p), ("v_new", ctypes.c_void_p),
                 ("out", ctypes.c_void_p), ("heads", ctypes.c_int32), ("tokens", ctypes.c_int32),
                 ("q_offset", ctypes.c_int32), ("q_tokens", ctypes.c_int32), ("recent_count", ctypes.c_int32),
-                ("causal", ctypes.c_int32), ("scale", ctypes.c_float), ("qx", ctypes.c_float)]
+                ("causal", ctypes.c_int32), ("scale", ctypes.c_float), ("qx", ctypes.c_float),
+                ("q_stride", ctypes.c_int32)]
 
 
 _lib = None

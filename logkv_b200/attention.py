@@ -248,8 +248,9 @@ def log_kv_chunk_attention(cache, q_b, k_b, v_b, scale, second_order_scale=1.0, 
     B, H, T, kd = q_b.shape
     if B != cache.batch_size or kd != cache.k_dim or q_b.dtype != cache.level_k.dtype:
         raise ValueError(f"q_b must be [B={cache.batch_size}, H, T, {cache.k_dim}] in the cache dtype")
-    if T != k_b.size(2):
-        raise ValueError("q_b and k_b must cover the same tokens")
+    Tk = k_b.size(2)
+    if T != Tk and (causal_tail or T > Tk):
+        raise ValueError("q_b and k_b must cover the same tokens (fewer queries only with causal_tail=0)")
     G = cache.n_groups
     if H % G:
         raise ValueError(f"query heads {H} must be a multiple of KV groups {G}")
@@ -278,8 +279,8 @@ def log_kv_chunk_attention(cache, q_b, k_b, v_b, scale, second_order_scale=1.0, 
         while n > T - t0:
             n //= 2
         ws = rs.workspace(cache, H, n)
-        args = _lib.AttentionArgs(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), H, T, t0, n,
-                                  int(cache.recent_count), int(bool(causal_tail)), float(scale), qx)
+        args = _lib.AttentionArgs(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), H, Tk, t0, n,
+                                  int(cache.recent_count), int(bool(causal_tail)), float(scale), qx, T)
         _lib.check(_lib.lib().logkv_attention(ctypes.byref(layout), ctypes.byref(state), ctypes.byref(pre),
                                               ctypes.byref(args), ws.data_ptr(), ws.numel(), _stream(cache)),
                    "logkv_attention")

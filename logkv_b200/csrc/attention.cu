@@ -351,6 +351,7 @@ __device__ __forceinline__ void unpack16(const uint4& u, float* out, const __nv_
 
 struct AttnGeo {
   int B, G, H, T, rf;
+  int QS;        // token stride of the query and output rows (T unless the caller passes fewer queries)
   int TQ, qoff;  // query tokens of this call and the first one's index among the T new tokens
   int causal;
   int nsplit, pcap, rcap, rcount;
@@ -407,7 +408,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) slot_attn_kernel(AttnGeo a, l
 #pragma unroll
   for (int r = 0; r < NQ; ++r) {
     const int h = g * a.rf + r / a.TQ, t = a.qoff + r % a.TQ;
-    const uint4 raw = *reinterpret_cast<const uint4*>(q + (((size_t)b * a.H + h) * a.T + t) * D + u * VN);
+    const uint4 raw = *reinterpret_cast<const uint4*>(q + (((size_t)b * a.H + h) * a.QS + t) * D + u * VN);
     unpack16(raw, qf[r], (const T*)nullptr);
   }
 
@@ -587,7 +588,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) slot_attn_kernel(AttnGeo a, l
     }
     if (a.nsplit == 1) {
       const int h = g * a.rf + r / a.TQ, t = a.qoff + r % a.TQ;
-      Elem<T>::store(out + (((size_t)b * a.H + h) * a.T + t) * D + d, l > 0.f ? o / l : 0.f);
+      Elem<T>::store(out + (((size_t)b * a.H + h) * a.QS + t) * D + d, l > 0.f ? o / l : 0.f);
     } else {
       float* pp = part + ((size_t)(ln * a.nsplit + split) * NQ + r) * pstride;
       if (d == 0) {
@@ -619,7 +620,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) slot_attn_kernel(AttnGeo a, l
       }
     }
     const int h = g * a.rf + r / a.TQ, t = a.qoff + r % a.TQ;
-    Elem<T>::store(out + (((size_t)b * a.H + h) * a.T + t) * D + d, l > 0.f ? o / l : 0.f);
+    Elem<T>::store(out + (((size_t)b * a.H + h) * a.QS + t) * D + d, l > 0.f ? o / l : 0.f);
   }
   if (tid == 0) ticket[ln] = 0;
 }
@@ -712,7 +713,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) slot_attn_mma_kernel(AttnG
         unsigned lo = 0u, hi = 0u;
         if (r < NQ) {
           const int h = g * a.rf + r / a.TQ, t = a.qoff + r % a.TQ;
-          const __nv_bfloat16* qp = q + (((size_t)b * a.H + h) * a.T + t) * D + ks * 16 + 2 * t4;
+          const __nv_bfloat16* qp = q + (((size_t)b * a.H + h) * a.QS + t) * D + ks * 16 + 2 * t4;
           lo = *reinterpret_cast<const unsigned*>(qp);
           hi = *reinterpret_cast<const unsigned*>(qp + 8);
         }
@@ -928,7 +929,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) slot_attn_mma_kernel(AttnG
     }
     if (a.nsplit == 1) {
       const int h = g * a.rf + r / a.TQ, t = a.qoff + r % a.TQ;
-      out[(((size_t)b * a.H + h) * a.T + t) * D + d] = __float2bfloat16_rn(l > 0.f ? ov / l : 0.f);
+      out[(((size_t)b * a.H + h) * a.QS + t) * D + d] = __float2bfloat16_rn(l > 0.f ? ov / l : 0.f);
     } else {
       float* pp = part + ((size_t)(ln * a.nsplit + split) * NQ + r) * pstride;
       if (d == 0) {
@@ -960,7 +961,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) slot_attn_mma_kernel(AttnG
       }
     }
     const int h = g * a.rf + r / a.TQ, t = a.qoff + r % a.TQ;
-    out[(((size_t)b * a.H + h) * a.T + t) * D + d] = __float2bfloat16_rn(l > 0.f ? ov / l : 0.f);
+    out[(((size_t)b * a.H + h) * a.QS + t) * D + d] = __float2bfloat16_rn(l > 0.f ? ov / l : 0.f);
   }
   if (tid == 0) ticket[ln] = 0;
 }
@@ -1020,8 +1021,8 @@ __global__ void __launch_bounds__(kPfWarps * 32) chunk_attn_mma_kernel(AttnGeo a
     const bool ok0 = t0r < a.qoff + a.TQ, ok1 = t1r < a.qoff + a.TQ;
 #pragma unroll
     for (int ks = 0; ks < KS; ++ks) {
-      const __nv_bfloat16* q0 = q + (((size_t)b * a.H + h) * a.T + t0r) * D + ks * 16 + 2 * t4;
-      const __nv_bfloat16* q1 = q + (((size_t)b * a.H + h) * a.T + t1r) * D + ks * 16 + 2 * t4;
+      const __nv_bfloat16* q0 = q + (((size_t)b * a.H + h) * a.QS + t0r) * D + ks * 16 + 2 * t4;
+      const __nv_bfloat16* q1 = q + (((size_t)b * a.H + h) * a.QS + t1r) * D + ks * 16 + 2 * t4;
       qa[ks][0] = ok0 ? *reinterpret_cast<const unsigned*>(q0) : 0u;
       qa[ks][1] = ok1 ? *reinterpret_cast<const unsigned*>(q1) : 0u;
       qa[ks][2] = ok0 ? *reinterpret_cast<const unsigned*>(q0 + 8) : 0u;
@@ -1198,10 +1199,10 @@ __global__ void __launch_bounds__(kPfWarps * 32) chunk_attn_mma_kernel(AttnGeo a
   for (int jd = 0; jd < DT; ++jd) {
     const int c0 = jd * 8 + 2 * t4;
     if (ok0)
-      *reinterpret_cast<__nv_bfloat162*>(out + (((size_t)b * a.H + h) * a.T + tr0) * D + c0) =
+      *reinterpret_cast<__nv_bfloat162*>(out + (((size_t)b * a.H + h) * a.QS + tr0) * D + c0) =
           __floats2bfloat162_rn(o[jd][0] * inv0, o[jd][1] * inv0);
     if (ok1)
-      *reinterpret_cast<__nv_bfloat162*>(out + (((size_t)b * a.H + h) * a.T + tr1) * D + c0) =
+      *reinterpret_cast<__nv_bfloat162*>(out + (((size_t)b * a.H + h) * a.QS + tr1) * D + c0) =
           __floats2bfloat162_rn(o[jd][2] * inv1, o[jd][3] * inv1);
   }
 }
@@ -1383,7 +1384,7 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
       const int tok = tq_of(t) + m % QT, h = g * a.rf + m / QT;
       unsigned char* dst = base + S::OFF_Q + t * S::Q1_BYTES + (c >> 3) * (kTcRows * 128) + m * 128 +
                            (((c & 7) ^ (m & 7)) << 4);
-      if (tok < a.qoff + a.TQ) cp_async16(dst, q + (((size_t)b * a.H + h) * a.T + tok) * D + c * 8);
+      if (tok < a.qoff + a.TQ) cp_async16(dst, q + (((size_t)b * a.H + h) * a.QS + tok) * D + c * 8);
       else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
     }
     tc::mbar_arrive_cp_async(&q_full);
@@ -1590,7 +1591,7 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
       const int hh = row / QT;
       const bool in = row_t < a.qoff + a.TQ;
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* orow = out + (((size_t)b * a.H + g * a.rf + hh) * a.T + row_t) * D;
+      __nv_bfloat16* orow = out + (((size_t)b * a.H + g * a.rf + hh) * a.QS + row_t) * D;
 #pragma unroll 1
       for (int c0 = 0; c0 < D; c0 += 32) {
         uint32_t r32[32];
@@ -1946,8 +1947,10 @@ LOGKV_API int logkv_attention(const logkv_layout_t* layout, const logkv_state_t*
   if (rc) return rc;
   if (!state || !prefix || !args || !args->q || !args->out || !prefix->length) return LOGKV_E_POINTER;
   const int G = layout->groups, H = args->heads, T = args->tokens, TQ = args->q_tokens;
+  const int QS = args->q_stride ? args->q_stride : T;
   if (H < G || H % G || T < 1 || TQ < 1 || args->q_offset < 0 || args->q_offset + TQ > T ||
-      args->recent_count < 0 || args->recent_count > layout->recent_capacity)
+      args->q_offset + TQ > QS || QS > T || (QS != T && args->causal) || args->recent_count < 0 ||
+      args->recent_count > layout->recent_capacity)
     return LOGKV_E_SHAPE;
   if (!args->k_new || !args->v_new) return LOGKV_E_POINTER;
   const int nq = H / G * TQ;
@@ -1962,6 +1965,7 @@ LOGKV_API int logkv_attention(const logkv_layout_t* layout, const logkv_state_t*
   ag.G = G;
   ag.H = H;
   ag.T = T;
+  ag.QS = QS;
   ag.rf = H / G;
   ag.TQ = TQ;
   ag.qoff = args->q_offset;
