@@ -378,6 +378,66 @@ struct AttnShape {
   static_assert(NQ >= 1 && NQ <= 32 && 32 % NQ == 0, "query rows per lane must divide 32");
 };
 
+template <typename T, int NQ>
+static size_t AttnShapeFor(int D) {
+  switch (D) {
+    case 16: return AttnShape<T, 16, NQ>::smem;
+    case 32: return AttnShape<T, 32, NQ>::smem;
+    case 64: return AttnShape<T, 64, NQ>::smem;
+    case 128: return AttnShape<T, 128, NQ>::smem;
+    default: return 0;
+  }
+}
+
+// Last-CTA combine of a lane's split partials ([m, l, o[D]] per split and query row): every
+// row's maximum over the splits and each split's weight exp2(m_s - max) go to shared memory
+// `wsh` ([nsplit][NQ] weights, [nsplit][NQ] sums, [NQ] row sums); then every output column's
+// weighted sum over the splits, its loads unrolled.  Same operations in the same split order as
+// one pass over the splits per output, so the result is the same.
+template <typename T, int D, int NQ>
+__device__ void combine_splits(const AttnGeo& a, const float* part, T* out, int ln, int b, int g, float* wsh) {
+  const int tid = threadIdx.x, nt = blockDim.x, ns = a.nsplit;
+  const size_t pstride = (size_t)D + 2;
+  float* wgt = wsh;                 // [ns][NQ]
+  float* lsp = wsh + ns * NQ;       // [ns][NQ]
+  float* rl = lsp + ns * NQ;        // [NQ] row sums, -1 marks a row without any finite score
+  for (int x = tid; x < ns * NQ; x += nt) {
+    const float* pp = part + ((size_t)ln * ns * NQ + x) * pstride;   // split x / NQ, row x % NQ
+    wgt[x] = __ldcg(pp);
+    lsp[x] = __ldcg(pp + 1);
+  }
+  __syncthreads();
+  if (tid < NQ) {
+    const int r = tid;
+    float mx = -INFINITY;
+    for (int sidx = 0; sidx < ns; ++sidx) mx = fmaxf(mx, wgt[sidx * NQ + r]);
+    float l = 0.f;
+    if (mx != -INFINITY) {
+      for (int sidx = 0; sidx < ns; ++sidx) {
+        const float f = exp2f(wgt[sidx * NQ + r] - mx);
+        l += lsp[sidx * NQ + r] * f;
+        wgt[sidx * NQ + r] = f;
+      }
+      rl[r] = l;
+    } else {
+      rl[r] = -1.f;
+    }
+  }
+  __syncthreads();
+  for (int x = tid; x < NQ * D; x += nt) {
+    const int r = x / D, d = x % D;
+    const float l = rl[r];
+    float o = 0.f;
+    if (l >= 0.f) {
+      const float* pp = part + ((size_t)ln * ns * NQ + r) * pstride + 2 + d;
+#pragma unroll 8
+      for (int sidx = 0; sidx < ns; ++sidx) o += __ldcg(pp + (size_t)sidx * NQ * pstride) * wgt[sidx * NQ + r];
+    }
+    const int h = g * a.rf + r / a.TQ, t = a.qoff + r % a.TQ;
+    Elem<T>::store(out + (((size_t)b * a.H + h) * a.QS + t) * D + d, l > 0.f ? o / l : 0.f);
+  }
+}
+
 template <typename T, int D, int NQ>
 __global__ void __launch_bounds__(kAttnWarps * 32) slot_attn_kernel(AttnGeo a, logkv_prefix_t pre, const T* rk,
                                                                    const T* rv, const T* kn, const T* vn, const T* q,
@@ -605,23 +665,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) slot_attn_kernel(AttnGeo a, l
   __syncthreads();
   if (!sh_last) return;
   __threadfence();
-  for (int x = tid; x < NQ * D; x += blockDim.x) {
-    const int r = x / D, d = x % D;
-    float mx = -INFINITY;
-    for (int sidx = 0; sidx < a.nsplit; ++sidx)
-      mx = fmaxf(mx, __ldcg(part + ((size_t)(ln * a.nsplit + sidx) * NQ + r) * pstride));
-    float l = 0.f, o = 0.f;
-    if (mx != -INFINITY) {
-      for (int sidx = 0; sidx < a.nsplit; ++sidx) {
-        const float* pp = part + ((size_t)(ln * a.nsplit + sidx) * NQ + r) * pstride;
-        const float f = exp2f(__ldcg(pp) - mx);
-        l += __ldcg(pp + 1) * f;
-        o += __ldcg(pp + 2 + d) * f;
-      }
-    }
-    const int h = g * a.rf + r / a.TQ, t = a.qoff + r % a.TQ;
-    Elem<T>::store(out + (((size_t)b * a.H + h) * a.QS + t) * D + d, l > 0.f ? o / l : 0.f);
-  }
+  combine_splits<T, D, NQ>(a, part, out, ln, b, g, reinterpret_cast<float*>(smem4));
   if (tid == 0) ticket[ln] = 0;
 }
 
@@ -946,23 +990,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) slot_attn_mma_kernel(AttnG
   __syncthreads();
   if (!sh_last) return;
   __threadfence();
-  for (int x = tid; x < NQ * D; x += blockDim.x) {
-    const int r = x / D, d = x % D;
-    float mx = -INFINITY;
-    for (int sidx = 0; sidx < a.nsplit; ++sidx)
-      mx = fmaxf(mx, __ldcg(part + ((size_t)(ln * a.nsplit + sidx) * NQ + r) * pstride));
-    float l = 0.f, ov = 0.f;
-    if (mx != -INFINITY) {
-      for (int sidx = 0; sidx < a.nsplit; ++sidx) {
-        const float* pp = part + ((size_t)(ln * a.nsplit + sidx) * NQ + r) * pstride;
-        const float f = exp2f(__ldcg(pp) - mx);
-        l += __ldcg(pp + 1) * f;
-        ov += __ldcg(pp + 2 + d) * f;
-      }
-    }
-    const int h = g * a.rf + r / a.TQ, t = a.qoff + r % a.TQ;
-    out[(((size_t)b * a.H + h) * a.QS + t) * D + d] = __float2bfloat16_rn(l > 0.f ? ov / l : 0.f);
-  }
+  combine_splits<__nv_bfloat16, D, NQ>(a, part, out, ln, b, g, reinterpret_cast<float*>(smem4));
   if (tid == 0) ticket[ln] = 0;
 }
 
@@ -1869,6 +1897,32 @@ static int launch_attn(int dtype, int D, int nq, const AttnGeo& ag, const logkv_
   }
 }
 
+// Dynamic shared memory of the decode kernel launch_attn picks (the last CTA's split combine
+// reuses it: 2 * nsplit * nq + nq floats).
+static size_t decode_smem(int dtype, int D, int nq) {
+  auto pick = [&](auto tag) -> size_t {
+    using T = decltype(tag);
+    switch (nq) {
+      case 1: return AttnShapeFor<T, 1>(D);
+      case 2: return AttnShapeFor<T, 2>(D);
+      case 4: return AttnShapeFor<T, 4>(D);
+      case 8: return AttnShapeFor<T, 8>(D);
+      default: return 0;
+    }
+  };
+  if (dtype == LOGKV_DTYPE_BF16) {
+    switch (D) {
+      case 16: return MmaShape<16>::smem;
+      case 32: return MmaShape<32>::smem;
+      case 64: return MmaShape<64>::smem;
+      case 128: return MmaShape<128>::smem;
+      case 256: return MmaShape<256>::smem;
+      default: return 0;
+    }
+  }
+  return pick(float{});
+}
+
 }  // namespace logkv
 
 using namespace logkv;
@@ -1956,7 +2010,10 @@ LOGKV_API int logkv_attention(const logkv_layout_t* layout, const logkv_state_t*
   const int nq = H / G * TQ;
   const size_t need = logkv_attention_workspace_bytes(layout, H, TQ, prefix->capacity);
   if (!workspace || workspace_bytes < need) return LOGKV_E_WORKSPACE;
-  const int nsplit = attn_splits(*layout, prefix->capacity);
+  // Splits: attn_splits, at most as many as the last CTA's combine can weigh in shared memory.
+  const size_t dsm = decode_smem(layout->dtype, layout->dim, nq);
+  const int ncap = dsm > (size_t)(4 * nq) ? (int)((dsm - 4 * (size_t)nq) / (8 * (size_t)nq)) : 1;
+  const int nsplit = std::max(1, std::min(attn_splits(*layout, prefix->capacity), ncap));
   const size_t lanes = (size_t)layout->batch * G;
   int* ticket = reinterpret_cast<int*>(static_cast<char*>(workspace) + 256);
   float* part = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256 + ((lanes * sizeof(int) + 255) / 256) * 256);
