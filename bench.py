@@ -213,6 +213,7 @@ def bench_ours(args, rank, world, local_rank):
     caches = make_caches(torch, cfg, device, cos, sin)
     flushes_per_step = cfg["layers"] * (cfg["tokens"] // cfg["chunk"] - cfg["recent"] // cfg["chunk"])
     stream = torch.cuda.Stream(device)
+    torch.cuda.synchronize()   # inputs were written on the default stream
     streams = [torch.cuda.Stream(device) for _ in range(args.streams)] if args.streams > 1 else None
     # Warm-up (eager), then one CUDA graph per step.
     with torch.cuda.stream(stream):
@@ -305,6 +306,7 @@ def bench_ours(args, rank, world, local_rank):
     nslot = 2 * max(1, args.streams)
     dev_buf = [tuple(torch.empty_like(t, device=device) for t in host[0][0]) for _ in range(nslot)]
     copy_stream = torch.cuda.Stream(device)
+    torch.cuda.synchronize()   # inputs were written on the default stream
     filled = [torch.cuda.Event() for _ in range(nslot)]
     consumed = [torch.cuda.Event() for _ in range(nslot)]
     h2d_per_step = sum(t.numel() * t.element_size() for t in host[0][0]) * len(layers) * len(layers[0])
@@ -392,6 +394,7 @@ def bench_flush_attend(args, rank, world, local_rank, inputs):
     out = torch.empty_like(q)
     scale = D ** -0.5
     stream = torch.cuda.Stream(device)
+    torch.cuda.synchronize()   # inputs were written on the default stream
     lstreams = [torch.cuda.Stream(device) for _ in caches]
     n_chunks = len(layers[0])
 
@@ -493,6 +496,7 @@ def bench_unified(args, rank, world, local_rank):
     old_mu = torch.randn(L, K, D, generator=gen, device=device) * 2.0
     limits = torch.full((L,), 1.2 * 0.35 * D ** 0.5, device=device)
     stream = torch.cuda.Stream(device)
+    torch.cuda.synchronize()   # inputs were written on the default stream
     prec = torch.get_float32_matmul_precision()
     torch.set_float32_matmul_precision("highest")
 
@@ -594,13 +598,16 @@ def bench_kv_sharded(args, rank, world, local_rank):
     H_local, D, T = 16 // cfg["groups"] * (hi - lo), cfg["head_dim"], cfg["chunk"]
     gen = torch.Generator(device=device).manual_seed(99 + rank)
     q = torch.randn(1, H_local, T, D, generator=gen, device=device).to(torch.bfloat16)
-    out = torch.empty_like(q)
+    outs = [torch.empty_like(q) for _ in caches]
     stream = torch.cuda.Stream(device)
+    torch.cuda.synchronize()   # inputs were written on the default stream
+    comm = torch.cuda.Stream(device)          # every collective, in one order on every rank
     lstreams = [torch.cuda.Stream(device) for _ in caches]
+    gathered = [torch.cuda.Event() for _ in caches]   # layer i's output all-gather has read outs[i]
 
     def step(attend):
         main = torch.cuda.current_stream()
-        for st in lstreams:
+        for st in lstreams + [comm]:
             st.wait_stream(main)
         for cache, st in zip(caches, lstreams):
             with torch.cuda.stream(st):
@@ -610,12 +617,18 @@ def bench_kv_sharded(args, rank, world, local_rank):
                 k, kr, v = layers[i][c]
                 if attend:
                     main.wait_stream(lstreams[i])          # the layer's previous commit
-                    log_kv_chunk_attention(cache, q, k, v, D ** -0.5, 0.0, out=out)
-                    if world > 1:
-                        gather_heads(out, group)
+                    if world > 1 and c > 0:
+                        main.wait_event(gathered[i])       # the previous chunk's gather of outs[i]
+                    log_kv_chunk_attention(cache, q, k, v, D ** -0.5, 0.0, out=outs[i])
+                    if world > 1:                          # the outputs' all-gather, beside the next layers
+                        comm.wait_stream(main)
+                        with torch.cuda.stream(comm):
+                            gather_heads(outs[i], group)
+                            gathered[i].record(comm)
                 batch.begin(i, dict(k=k, v=v, k_raw=kr, span_ends=ends_host, span_ends_device=ends_dev), lstreams[i])
-            batch.finish()
-        for st in lstreams:
+            with torch.cuda.stream(comm):
+                batch.finish()
+        for st in lstreams + [comm]:
             main.wait_stream(st)
 
     res = {}
@@ -653,7 +666,7 @@ def bench_kv_sharded(args, rank, world, local_rank):
                                        "attention of the rank's heads + output all-gather + add_recent)",
                              "unit": "us", "value": round(res["flush_attend"] / (cfg["layers"] * n_chunks), 2),
                              "heads_per_rank": H_local,
-                             "gather_bytes_per_layer_chunk": out.numel() * out.element_size() * world},
+                             "gather_bytes_per_layer_chunk": q.numel() * q.element_size() * world},
             "timing": "CUDA-graph steps, layer flushes on per-layer streams, one span-part all-gather per chunk, "
                       "max over ranks",
             "config": {k: cfg[k] for k in ("workload", "layers", "groups", "head_dim", "clusters", "B", "recent",
@@ -737,6 +750,7 @@ def bench_decode(args, rank, world, local_rank):
     outs = [torch.empty(batch, H, 1, D, dtype=torch.bfloat16, device=device) for _ in range(cfg["layers"])]
     scale = D ** -0.5
     stream = torch.cuda.Stream(device)
+    torch.cuda.synchronize()   # inputs were written on the default stream
 
     def step():
         for layer in range(cfg["layers"]):
@@ -931,6 +945,7 @@ def bench_prefill(args, rank, world, local_rank):
     out = torch.empty(1, H, T, D, dtype=torch.bfloat16, device=device)
     scale = D ** -0.5
     stream = torch.cuda.Stream(device)
+    torch.cuda.synchronize()   # inputs were written on the default stream
     reps = max(4, args.decode_steps // 2)
     with torch.no_grad(), torch.cuda.stream(stream):
         for _ in range(3):
@@ -1105,7 +1120,9 @@ def main():
     if rank == 0 and not os.path.exists(os.path.join(ROOT, "logkv_b200", "liblogkv_b200.so")):
         _build.build()
     if world > 1:
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+        import datetime
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank),
+                                timeout=datetime.timedelta(seconds=180))
     res = bench_ours(args, rank, world, local_rank)
     inputs = res.pop("inputs")
     fa = bench_flush_attend(args, rank, world, local_rank, inputs) if args.flush_attend else None

@@ -355,10 +355,12 @@ struct AttnGeo {
   int TQ, qoff;  // query tokens of this call and the first one's index among the T new tokens
   int causal;
   int nsplit, pcap, rcap, rcount;
+  int nsmin;     // splits a lane of the tensor-core decode kernel uses at least (fills every SM)
   float scale_log2, qx;
 };
 
 constexpr int kAttnWarps = 4;
+constexpr int kUnitsPerSplit = 128;   // 16-row tiles per split of the tensor-core decode kernel
 constexpr int kAttnStages = 3;
 // The tensor-core decode kernel keeps two tiles per warp in flight and fits three CTAs (12 warps)
 // per SM, so more warps overlap one tile's math with the next tiles' loads.
@@ -395,14 +397,15 @@ static size_t AttnShapeFor(int D) {
 // weighted sum over the splits, its loads unrolled.  Same operations in the same split order as
 // one pass over the splits per output, so the result is the same.
 template <typename T, int D, int NQ>
-__device__ void combine_splits(const AttnGeo& a, const float* part, T* out, int ln, int b, int g, float* wsh) {
-  const int tid = threadIdx.x, nt = blockDim.x, ns = a.nsplit;
+__device__ void combine_splits(const AttnGeo& a, const float* part, T* out, int ln, int b, int g, float* wsh,
+                               int ns) {
+  const int tid = threadIdx.x, nt = blockDim.x;
   const size_t pstride = (size_t)D + 2;
   float* wgt = wsh;                 // [ns][NQ]
   float* lsp = wsh + ns * NQ;       // [ns][NQ]
   float* rl = lsp + ns * NQ;        // [NQ] row sums, -1 marks a row without any finite score
   for (int x = tid; x < ns * NQ; x += nt) {
-    const float* pp = part + ((size_t)ln * ns * NQ + x) * pstride;   // split x / NQ, row x % NQ
+    const float* pp = part + ((size_t)ln * a.nsplit * NQ + x) * pstride;   // split x / NQ, row x % NQ
     wgt[x] = __ldcg(pp);
     lsp[x] = __ldcg(pp + 1);
   }
@@ -429,7 +432,7 @@ __device__ void combine_splits(const AttnGeo& a, const float* part, T* out, int 
     const float l = rl[r];
     float o = 0.f;
     if (l >= 0.f) {
-      const float* pp = part + ((size_t)ln * ns * NQ + r) * pstride + 2 + d;
+      const float* pp = part + ((size_t)ln * a.nsplit * NQ + r) * pstride + 2 + d;
 #pragma unroll 8
       for (int sidx = 0; sidx < ns; ++sidx) o += __ldcg(pp + (size_t)sidx * NQ * pstride) * wgt[sidx * NQ + r];
     }
@@ -457,7 +460,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) slot_attn_kernel(AttnGeo a, l
                  warp * kAttnStages * TS;
   const T* PK = static_cast<const T*>(pre.k);
   const T* PV = static_cast<const T*>(pre.v);
-  const int Lp = pre.length[ln], R = a.rcount, Stot = Lp + R + a.T;
+  const int Lp = min(max(pre.length[ln], 0), pre.capacity), R = a.rcount, Stot = Lp + R + a.T;
   int per = (Stot + a.nsplit - 1) / a.nsplit;
   per = (per + TS - 1) / TS * TS;
   const int s0 = min(Stot, split * per), s1 = min(Stot, s0 + per);
@@ -502,6 +505,10 @@ __global__ void __launch_bounds__(kAttnWarps * 32) slot_attn_kernel(AttnGeo a, l
           }
           cp_async16(dk + ts * D + u * VN, sk + u * VN);
           cp_async16(dv + ts * D + u * VN, sv + u * VN);
+        } else {
+          // Past the split's last slot: zeros, so the masked products (probability 0) stay 0.
+          *reinterpret_cast<uint4*>(dk + ts * D + u * VN) = make_uint4(0, 0, 0, 0);
+          *reinterpret_cast<uint4*>(dv + ts * D + u * VN) = make_uint4(0, 0, 0, 0);
         }
       }
     }
@@ -665,7 +672,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32) slot_attn_kernel(AttnGeo a, l
   __syncthreads();
   if (!sh_last) return;
   __threadfence();
-  combine_splits<T, D, NQ>(a, part, out, ln, b, g, reinterpret_cast<float*>(smem4));
+  combine_splits<T, D, NQ>(a, part, out, ln, b, g, reinterpret_cast<float*>(smem4), a.nsplit);
   if (tid == 0) ticket[ln] = 0;
 }
 
@@ -733,16 +740,20 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) slot_attn_mma_kernel(AttnG
   __shared__ int sh_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int g8 = lane >> 2, t4 = lane & 3;  // fragment row group and column pair
-  const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z, ln = b * a.G + g;
+  const int ln = blockIdx.x, split = blockIdx.y, g = ln % a.G, b = ln / a.G;
   unsigned char* wbase = reinterpret_cast<unsigned char*>(smem4) + (size_t)warp * kMmaStages * S::STAGE_BYTES;
   const unsigned wbase_s = (unsigned)__cvta_generic_to_shared(wbase);
   const __nv_bfloat16* PK = static_cast<const __nv_bfloat16*>(pre.k);
   const __nv_bfloat16* PV = static_cast<const __nv_bfloat16*>(pre.v);
   // Work units: tiles of 16 rows inside each segment.
-  const int Lp = pre.length[ln], R = a.rcount, Tn = a.T;
+  const int Lp = min(max(pre.length[ln], 0), pre.capacity), R = a.rcount, Tn = a.T;
   const int up = (Lp + TS - 1) / TS, ur = (R + TS - 1) / TS, uc = (Tn + TS - 1) / TS;
   const int U = up + ur + uc;
-  const int u0 = (int)((long long)U * split / a.nsplit), u1 = (int)((long long)U * (split + 1) / a.nsplit);
+  // This lane's splits: about kUnitsPerSplit tiles each (long streams per warp), at least
+  // a.nsmin (every SM busy at small batch); the grid's further splits return at once.
+  const int ns = min(a.nsplit, max(a.nsmin, U / kUnitsPerSplit));
+  if (split >= ns) return;
+  const int u0 = (int)((long long)U * split / ns), u1 = (int)((long long)U * (split + 1) / ns);
   const int mine = (u1 - u0) > warp ? (u1 - u0 - warp + kAttnWarps - 1) / kAttnWarps : 0;
 
   // Query A fragments (rows g8 and g8 + 8 of the 16, zero past NQ), loop invariant.
@@ -971,7 +982,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) slot_attn_mma_kernel(AttnG
                                              (size_t)w * kMmaStages * S::STAGE_BYTES)[r * D + d] * f;
       }
     }
-    if (a.nsplit == 1) {
+    if (ns == 1) {
       const int h = g * a.rf + r / a.TQ, t = a.qoff + r % a.TQ;
       out[(((size_t)b * a.H + h) * a.QS + t) * D + d] = __float2bfloat16_rn(l > 0.f ? ov / l : 0.f);
     } else {
@@ -983,14 +994,14 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) slot_attn_mma_kernel(AttnG
       pp[2 + d] = ov;
     }
   }
-  if (a.nsplit == 1) return;
+  if (ns == 1) return;
   __threadfence();
   __syncthreads();
-  if (tid == 0) sh_last = atomicAdd(ticket + ln, 1) == a.nsplit - 1;
+  if (tid == 0) sh_last = atomicAdd(ticket + ln, 1) == ns - 1;
   __syncthreads();
   if (!sh_last) return;
   __threadfence();
-  combine_splits<__nv_bfloat16, D, NQ>(a, part, out, ln, b, g, reinterpret_cast<float*>(smem4));
+  combine_splits<__nv_bfloat16, D, NQ>(a, part, out, ln, b, g, reinterpret_cast<float*>(smem4), ns);
   if (tid == 0) ticket[ln] = 0;
 }
 
@@ -1037,7 +1048,7 @@ __global__ void __launch_bounds__(kPfWarps * 32) chunk_attn_mma_kernel(AttnGeo a
   const int tlast = min(a.qoff + a.TQ, tq0 + QT) - 1;  // CTA's last query token
   const __nv_bfloat16* PK = static_cast<const __nv_bfloat16*>(pre.k);
   const __nv_bfloat16* PV = static_cast<const __nv_bfloat16*>(pre.v);
-  const int Lp = pre.length[ln], R = a.rcount;
+  const int Lp = min(max(pre.length[ln], 0), pre.capacity), R = a.rcount;
   const int Tvis = a.causal ? min(a.T, tlast + 1) : a.T;   // new tokens any row of the CTA can see
   const int up = (Lp + TS - 1) / TS, ur = (R + TS - 1) / TS, uc = (Tvis + TS - 1) / TS;
   const int U = up + ur + uc;
@@ -1324,7 +1335,7 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
   };
   const __nv_bfloat16* PK = static_cast<const __nv_bfloat16*>(pre.k);
   const __nv_bfloat16* PV = static_cast<const __nv_bfloat16*>(pre.v);
-  const int Lp = pre.length[ln], R = a.rcount;
+  const int Lp = min(max(pre.length[ln], 0), pre.capacity), R = a.rcount;
   const int up = (Lp + TS - 1) / TS, ur = (R + TS - 1) / TS;
   // Units (64-slot K/V tiles) each query tile attends to: prefix, window, then the new tokens up
   // to its last token (causal); the CTA streams the longest tile's units.
@@ -1706,14 +1717,17 @@ static void launch_pack_mid(const PlanGeo& pg, const logkv_state_t& s, const log
                                                     static_cast<T*>(ov), status);
 }
 
-// Splits per lane: about sixteen waves of two CTAs per SM over the grid (short tails), but
-// at least eight 16-row tiles per warp of a split.
-static int attn_splits(const logkv_layout_t& l, int prefix_capacity) {
+// Splits per lane of the grid: kUnitsPerSplit 16-row tiles each at full prefix capacity, and
+// at least one CTA per SM over all lanes (attn_min_splits).  The tensor-core kernel sizes each
+// lane's splits again from its actual lengths (slot_attn_mma_kernel), at most this many.
+static int attn_min_splits(const logkv_layout_t& l) {
   const int lanes = l.batch * l.groups;
+  return std::max(1, std::min((148 + lanes - 1) / lanes, 256));
+}
+
+static int attn_splits(const logkv_layout_t& l, int prefix_capacity) {
   const int units = (prefix_capacity + l.recent_capacity) / 16 + 1;
-  int n = (16 * 2 * 148 + lanes - 1) / lanes;
-  n = std::min(n, std::max(1, units / (kAttnWarps * 8)));
-  return std::max(1, std::min(n, 256));
+  return std::max(1, std::min(std::max(units / kUnitsPerSplit, attn_min_splits(l)), 256));
 }
 
 static size_t attn_part_bytes(const logkv_layout_t& l, int nq, int nsplit) {
@@ -1753,7 +1767,8 @@ static int launch_mma_dq(const AttnGeo& ag, const logkv_prefix_t& pre, const log
   auto kern = slot_attn_mma_kernel<D, NQ>;
   if (S::smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::smem);
   using B16 = __nv_bfloat16;
-  kern<<<dim3(ag.nsplit, ag.G, ag.B), kAttnWarps * 32, S::smem, st>>>(
+  // Lanes along x, splits along y: a lane's unused splits are the last CTAs dispatched.
+  kern<<<dim3(ag.G * ag.B, ag.nsplit), kAttnWarps * 32, S::smem, st>>>(
       ag, pre, static_cast<const B16*>(s.recent_k), static_cast<const B16*>(s.recent_v),
       static_cast<const B16*>(x.k_new), static_cast<const B16*>(x.v_new), static_cast<const B16*>(x.q),
       static_cast<B16*>(x.out), part, ticket);
@@ -2028,6 +2043,7 @@ LOGKV_API int logkv_attention(const logkv_layout_t* layout, const logkv_state_t*
   ag.qoff = args->q_offset;
   ag.causal = args->causal ? 1 : 0;
   ag.nsplit = nsplit;
+  ag.nsmin = std::min(attn_min_splits(*layout), nsplit);
   ag.pcap = prefix->capacity;
   ag.rcap = layout->recent_capacity;
   ag.rcount = args->recent_count;
