@@ -77,14 +77,15 @@ __device__ __forceinline__ void load_run(const T* p, float* out) {
 // (m the weighted mean, W the side's mass): a side's loss from the pairwise squared
 // distances D_ab of its rows (pairs 01, 02, 12, 13, 23 cover every side of the three cuts;
 // single-row sides lose nothing).  Every term is non-negative, so the result is within a
-// relative (D / 16 + 30) u of the exact cost (u = 2^-24: (D / 32 + 7) u for a distance or a
-// row energy summed per lane and across lanes, 7 u for a side's products, sums and division,
-// 5 u more for the energy, 4 u for the cost's sum).  The canonical evaluation is within
-// (2 D + 25) u relative of the exact cost
+// relative (D / 16 + 39) u of the exact cost (u = 2^-24: (D / 32 + 7) u for a distance or a
+// row energy summed per lane and across lanes, 10 u for a side's products, sums and division,
+// 11 u more for the energy and its reciprocal, 4 u for the cost's sum; the three divisions on
+// a term's path are __fdividef, within 2 ulp = 4 u each, for denominators in [1e-12, 1e30]).
+// The canonical evaluation is within (2 D + 25) u relative of the exact cost
 // at its rounded means, and a mean rounded by delta changes a side's loss by only
 // W |delta|^2 <= 36 u^2 W sum_i E_i (the mean minimises the loss).  So the returned cut is the
 // canonical one whenever runner-up minus best exceeds 2 rel * runner-up with
-// rel = (4 D + 128) u >= the sum of both relative bounds, plus twice
+// rel = (4 D + 128) u >= (2.0625 D + 64) u, the sum of both relative bounds, plus twice
 // B = sum over components of 40 u^2 (sum w)(sum_i E_i) / energy, plus a floor for subnormal
 // rounding.  Otherwise (a near tie), when a side's mass lies in (0, 1e-12) (the canonical
 // clamp), or when a row energy exceeds 1e30 (no overflow anywhere below that), -1 asks for
@@ -158,13 +159,15 @@ __device__ int beta_cut_warp(const T* tk, const T* tv, const Meta* tm, int start
     const float P13 = comp == 0 ? v[7] : x2[0], P23 = comp == 0 ? v[8] : x2[1];
     const float esum = E0 + E1 + E2 + E3;
     ok = ok && esum <= 1e30f;  // also false for NaN
-    const float energy = fmaxf(fdiv(fadd(fadd(fadd(fmul(E0, w0), fmul(E1, w1)), fmul(E2, w2)), fmul(E3, w3)), tot),
+    // Denominators: tot, the side masses >= 1e-12 and energy in [1e-12, 1e30] (ok below).
+    const float energy = fmaxf(__fdividef(fadd(fadd(fadd(fmul(E0, w0), fmul(E1, w1)), fmul(E2, w2)), fmul(E3, w3)),
+                                          tot),
                                1e-12f);
-    const float inv_e = fdiv(1.f, energy);
-    const float l2 = fdiv(fmul(w01, P01), fmaxf(m01, 1e-12f));
-    const float r2 = fdiv(fmul(w23, P23), fmaxf(m23, 1e-12f));
-    const float r1 = fdiv(fadd(fadd(fmul(w12, P12), fmul(w13, P13)), fmul(w23, P23)), fmaxf(m123, 1e-12f));
-    const float l3 = fdiv(fadd(fadd(fmul(w01, P01), fmul(w02, P02)), fmul(w12, P12)), fmaxf(m012, 1e-12f));
+    const float inv_e = __fdividef(1.f, energy);
+    const float l2 = __fdividef(fmul(w01, P01), fmaxf(m01, 1e-12f));
+    const float r2 = __fdividef(fmul(w23, P23), fmaxf(m23, 1e-12f));
+    const float r1 = __fdividef(fadd(fadd(fmul(w12, P12), fmul(w13, P13)), fmul(w23, P23)), fmaxf(m123, 1e-12f));
+    const float l3 = __fdividef(fadd(fadd(fmul(w01, P01), fmul(w02, P02)), fmul(w12, P12)), fmaxf(m012, 1e-12f));
     costs[0] = fadd(costs[0], fmul(fadd(l2, r2), inv_e));  // cut 2: rows 0,1 | 2,3
     costs[1] = fadd(costs[1], fmul(r1, inv_e));            // cut 1: row 0 | 1,2,3
     costs[2] = fadd(costs[2], fmul(l3, inv_e));            // cut 3: rows 0,1,2 | 3
@@ -172,15 +175,20 @@ __device__ int beta_cut_warp(const T* tk, const T* tv, const Meta* tm, int start
   }
   if (!ok) return -1;
   int best = 0;
-  if (costs[1] < costs[best]) best = 1;
-  if (costs[2] < costs[best]) best = 2;
-  float second = INFINITY;
-#pragma unroll
-  for (int j = 0; j < 3; ++j)
-    if (j != best) second = fminf(second, costs[j]);
+  float bc = costs[0];
+  if (costs[1] < bc) {
+    best = 1;
+    bc = costs[1];
+  }
+  if (costs[2] < bc) {
+    best = 2;
+    bc = costs[2];
+  }
+  const float second = best == 0 ? fminf(costs[1], costs[2]) : (best == 1 ? fminf(costs[0], costs[2])
+                                                                          : fminf(costs[0], costs[1]));
   const float rel = (4.f * D + 128.f) * 5.9604645e-8f;
   const float margin = 2.f * rel * second + 2.f * bound + 1e-25f * (1.f + wsum);
-  if (!(second - costs[best] > margin)) return -1;  // near tie (or NaN): canonical evaluation
+  if (!(second - bc > margin)) return -1;  // near tie (or NaN): canonical evaluation
   return best == 0 ? 2 : (best == 1 ? 1 : 3);
 }
 
