@@ -192,6 +192,42 @@ LOGKV_API int logkv_window_append(const logkv_layout_t* layout, const logkv_stat
                                   const int64_t* pos_strides, int64_t pos0, const uint8_t* ends, int32_t n,
                                   int32_t recent_count, void* stream);
 
+/* A chunk of n window rows as logkv_window_append takes them (same meaning and rules). */
+typedef struct logkv_chunk {
+  const void* k;
+  int64_t k_strides[3];
+  const void* k_raw;
+  int64_t k_raw_strides[3];
+  const void* v;
+  int64_t v_strides[3];
+  const int64_t* positions;   /* [B, n] int64, or NULL: pos0, pos0 + 1, ... */
+  int64_t pos_strides[2];
+  int64_t pos0;
+  const uint8_t* ends;        /* [B, n] uint8, contiguous */
+  int32_t n;
+} logkv_chunk_t;
+
+/*
+ * _semantic_add_recent of a chunk whose append overflows the window by exactly one flush of
+ * the flush_tokens oldest rows (log_kv_cache.py:5668-5718 with one pass of the flush loop),
+ * when those rows are all rows already in the window: recent_count (the fill before the
+ * chunk) in [flush_tokens, 2 * flush_tokens], recent_count + chunk->n <= recent_capacity.
+ * The flush runs on the window as it is, and its final kernel writes the kept old rows and
+ * the chunk's rows once, straight to their places after the shift (no separate append, no
+ * second copy of the chunk).  The state afterwards is the state that
+ * logkv_window_append(chunk, recent_count) followed by logkv_flush(flush_tokens,
+ * recent_count + n) leaves; the workspace is logkv_flush's.  Other cases: LOGKV_E_SHAPE,
+ * nothing launched.  logkv_flush_chunk_profiled adds logkv_flush_profiled's events (its last
+ * stage is this window write).
+ */
+LOGKV_API int logkv_flush_chunk(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                int32_t recent_count, const logkv_chunk_t* chunk, void* workspace,
+                                size_t workspace_bytes, void* stream);
+LOGKV_API int logkv_flush_chunk_profiled(const logkv_layout_t* layout, const logkv_state_t* state,
+                                         int32_t flush_tokens, int32_t recent_count, const logkv_chunk_t* chunk,
+                                         void* workspace, size_t workspace_bytes, void* stream, void** events,
+                                         int32_t n_events);
+
 /*
  * KV-head sharding of one sequence (no reference counterpart: the reference runs a
  * layer's cache on one device).  Each rank's layout and state hold its own block of
@@ -298,7 +334,8 @@ LOGKV_API int logkv_read_status(const void* workspace, int32_t* out, void* strea
  * cudaEvent_t as void*) before the first and after each of the
  * LOGKV_FLUSH_STAGES kernel stages: snapshot, span cut, span scores with attach
  * decisions, choose, seed + plan, prepare, cascade (merge and move kernels), pool
- * rewrite, window shift.  (Events between the kernels end their programmatic
+ * rewrite, window shift (logkv_flush_chunk: the window write of the kept rows and the
+ * chunk).  (Events between the kernels end their programmatic
  * overlap, so a profiled flush is slower than a plain one.)
  */
 #define LOGKV_FLUSH_STAGES 9

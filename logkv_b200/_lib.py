@@ -70,6 +70,14 @@ class Prefix(ctypes.Structure):
                 ("length", ctypes.c_void_p), ("capacity", ctypes.c_int32)]
 
 
+class Chunk(ctypes.Structure):
+    """logkv_chunk_t: a chunk of window rows (include/logkv_b200.h)."""
+    _fields_ = [("k", ctypes.c_void_p), ("k_strides", ctypes.c_int64 * 3), ("k_raw", ctypes.c_void_p),
+                ("k_raw_strides", ctypes.c_int64 * 3), ("v", ctypes.c_void_p), ("v_strides", ctypes.c_int64 * 3),
+                ("positions", ctypes.c_void_p), ("pos_strides", ctypes.c_int64 * 2), ("pos0", ctypes.c_int64),
+                ("ends", ctypes.c_void_p), ("n", ctypes.c_int32)]
+
+
 class AttentionArgs(ctypes.Structure):
     _fields_ = [("q", ctypes.c_void_p), ("k_new", ctypes.c_void_p), ("v_new", ctypes.c_void_p),
                 ("out", ctypes.c_void_p), ("heads", ctypes.c_int32), ("tokens", ctypes.c_int32),
@@ -110,6 +118,13 @@ def lib() -> ctypes.CDLL:
         handle.logkv_window_append.argtypes = [P(Layout), P(State), ctypes.c_void_p, I64, ctypes.c_void_p, I64,
                                                ctypes.c_void_p, I64, ctypes.c_void_p, I64, ctypes.c_int64,
                                                ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p]
+        handle.logkv_flush_chunk.restype = ctypes.c_int
+        handle.logkv_flush_chunk.argtypes = [P(Layout), P(State), ctypes.c_int32, ctypes.c_int32, P(Chunk),
+                                             ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+        handle.logkv_flush_chunk_profiled.restype = ctypes.c_int
+        handle.logkv_flush_chunk_profiled.argtypes = [P(Layout), P(State), ctypes.c_int32, ctypes.c_int32, P(Chunk),
+                                                      ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                                                      ctypes.POINTER(ctypes.c_void_p), ctypes.c_int32]
         handle.logkv_read_ties.restype = ctypes.c_int
         handle.logkv_read_ties.argtypes = [ctypes.c_void_p, P(Tie), ctypes.c_int32, P(ctypes.c_int64), ctypes.c_int32,
                                            ctypes.c_void_p]

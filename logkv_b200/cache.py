@@ -513,7 +513,17 @@ class LogStructuredKVCache(nn.Module):
         if self._active_updates is None and replaying:
             raise NotImplementedError("op-log replay outside an update tape context is not implemented by "
                                       "logkv_b200 (replay a recorded update tape instead)")
-        self._append_chunk(k, v, k_raw, input_pos, span_ends, span_ends_device)
+        chunk = self._check_chunk(k, v, k_raw, input_pos, span_ends, span_ends_device)
+        take = self._chunk_flush_take(chunk[-1])
+        if take is not None:
+            # The one flush this chunk triggers, with the chunk written once after the shift.
+            self._flush_chunk(chunk, take)
+            if record_op_log:
+                self._append_op_log(take)
+            self._finish_flush(take)
+            return
+        self._append_window(*chunk)
+        self.recent_count += chunk[-1]
         for take in self._pending_flushes():
             if self._active_updates is not None:
                 self._flush_with_updates(take, record_op_log, replaying or self._replaying_updates)
@@ -566,6 +576,42 @@ class LogStructuredKVCache(nn.Module):
 
     def _append_chunk(self, k, v, k_raw, input_pos, span_ends, span_ends_device) -> None:
         """Validation and the window write of add_recent (log_kv_cache.py:5668-5707)."""
+        chunk = self._check_chunk(k, v, k_raw, input_pos, span_ends, span_ends_device)
+        self._append_window(*chunk)
+        self.recent_count += chunk[-1]
+
+    def _chunk_flush_take(self, n: int):
+        """The flush size when this chunk's add_recent is one flush of rows already in the window
+        (logkv_flush_chunk's case: recent_count in [take, 2 take]), on the plain device path (no
+        update tape, KV-head sharding or route overlap); else None."""
+        if self._active_updates is not None or self.kv_shard_group is not None or self._route_overlap:
+            return None
+        c0, gran = self.recent_count, self.semantic_flush_granularity
+        overflow = c0 + n - self.recent_size
+        if overflow <= 0 or overflow > gran:
+            return None
+        return gran if gran <= c0 <= 2 * gran else None
+
+    def _flush_chunk(self, chunk, take: int) -> None:
+        """logkv_flush_chunk: the flush of the ``take`` oldest rows, then the kept rows and the
+        chunk written to their places (same state as _append_window + flush_device)."""
+        k, k_raw, v, positions, ends, n = chunk
+        self._ladder_epoch += 1
+        st, keep = self._chunk_struct(k, k_raw, v, positions, ends, n)
+        args = self._flush_args(take)
+        lib = _lib.lib()
+        if self.profile_events is None:
+            _lib.check(lib.logkv_flush_chunk(*args[:4], ctypes.byref(st), *args[4:]), "logkv_flush_chunk")
+        else:
+            events = (ctypes.c_void_p * len(self.profile_events))(*[e.cuda_event for e in self.profile_events])
+            _lib.check(lib.logkv_flush_chunk_profiled(*args[:4], ctypes.byref(st), *args[4:], events,
+                                                      len(self.profile_events)), "logkv_flush_chunk_profiled")
+        del keep
+        self.recent_count += n
+
+    def _check_chunk(self, k, v, k_raw, input_pos, span_ends, span_ends_device):
+        """Validation of add_recent (log_kv_cache.py:5668-5700): the chunk's rows, positions and
+        span-end flags on the device, as (k, k_raw, v, positions, ends, n); counts the tokens."""
         if k_raw is None:
             raise ValueError("semantic LogKV add_recent requires pre-RoPE k_raw")
         n = k.size(2)
@@ -589,8 +635,7 @@ class LogStructuredKVCache(nn.Module):
             host = torch.tensor(span_ends, dtype=torch.uint8)
             ends = self._ends_stage[:self.batch_size * n].view(self.batch_size, n)
             ends.copy_(host.pin_memory() if self.recent_pos.is_cuda else host, non_blocking=True)
-        self._append_window(k, k_raw, v, positions, ends, n)
-        self.recent_count += n
+        return k, k_raw, v, positions, ends, n
 
     def _pending_flushes(self):
         """Sizes of the flushes the window overflow needs (_semantic_add_recent :5708-5718)."""
@@ -613,10 +658,9 @@ class LogStructuredKVCache(nn.Module):
         self.recent_count -= take
         self._route_mark_ready()
 
-    def _append_window(self, k, k_raw, v, positions, ends, n: int) -> None:
-        """The chunk into window rows [recent_count, recent_count + n) with one kernel
-        (logkv_window_append).  Rows must be in the storage dtype, contiguous along the head dim
-        and 16-byte aligned; other inputs are made so first."""
+    def _chunk_struct(self, k, k_raw, v, positions, ends, n: int):
+        """(logkv_chunk_t, tensors it points into).  Rows must be in the storage dtype, contiguous
+        along the head dim and 16-byte aligned; other inputs are made so first."""
         dt, dev = self.recent_k.dtype, self.recent_k.device
         esize = self.recent_k.element_size()
 
@@ -624,20 +668,36 @@ class LogStructuredKVCache(nn.Module):
             if (t.dtype != dt or t.device != dev or t.stride(-1) != 1 or t.data_ptr() % 16
                     or any((st * esize) % 16 for st in t.stride()[:3])):
                 t = t.to(device=dev, dtype=dt).contiguous()
-            return t, (ctypes.c_int64 * 3)(*t.stride()[:3])
+            return t
 
-        (k, ks), (kr, krs), (v, vs) = rows(k), rows(k_raw), rows(v)
-        pos_ptr, ps = None, None
+        k, kr, v = rows(k), rows(k_raw), rows(v)
+        c = _lib.Chunk()
+        c.k, c.k_raw, c.v = k.data_ptr(), kr.data_ptr(), v.data_ptr()
+        c.k_strides[:] = k.stride()[:3]
+        c.k_raw_strides[:] = kr.stride()[:3]
+        c.v_strides[:] = v.stride()[:3]
         if positions is not None:
             if positions.dtype != torch.int64 or positions.device != dev:
                 positions = positions.to(device=dev, dtype=torch.int64)
-            pos_ptr, ps = ctypes.c_void_p(positions.data_ptr()), (ctypes.c_int64 * 2)(*positions.stride())
+            c.positions = positions.data_ptr()
+            c.pos_strides[:] = positions.stride()
+        c.pos0 = int(self.token_count - n)
+        c.ends = ends.data_ptr()
+        c.n = int(n)
+        return c, (k, kr, v, positions, ends)
+
+    def _append_window(self, k, k_raw, v, positions, ends, n: int) -> None:
+        """The chunk into window rows [recent_count, recent_count + n) with one kernel
+        (logkv_window_append)."""
+        c, keep = self._chunk_struct(k, k_raw, v, positions, ends, n)
         state = self._state_struct()
+        pos = ctypes.c_void_p(c.positions) if c.positions else None
         _lib.check(_lib.lib().logkv_window_append(
-            ctypes.byref(self._layout), ctypes.byref(state), ctypes.c_void_p(k.data_ptr()), ks,
-            ctypes.c_void_p(kr.data_ptr()), krs, ctypes.c_void_p(v.data_ptr()), vs, pos_ptr, ps,
-            int(self.token_count - n), ctypes.c_void_p(ends.data_ptr()), int(n), int(self.recent_count),
-            ctypes.c_void_p(_lib.stream_ptr(dev))), "logkv_window_append")
+            ctypes.byref(self._layout), ctypes.byref(state), ctypes.c_void_p(c.k), c.k_strides,
+            ctypes.c_void_p(c.k_raw), c.k_raw_strides, ctypes.c_void_p(c.v), c.v_strides, pos,
+            c.pos_strides if c.positions else None, c.pos0, ctypes.c_void_p(c.ends), c.n, int(self.recent_count),
+            ctypes.c_void_p(_lib.stream_ptr(self.recent_k.device))), "logkv_window_append")
+        del keep
 
     # ------------------------------------------------------------------ read side
     def _semantic_attention_plan(self):

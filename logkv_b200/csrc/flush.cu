@@ -288,22 +288,29 @@ struct AppendArgs {
   int n, recent_count;
 };
 
+// Chunk row t, 16-byte unit v of lane (b, grp) into window row `row` (K, pre-RoPE K, V).
+template <typename T>
+__device__ __forceinline__ void put_chunk_unit(const Geo& g, const logkv_state_t& s, const AppendArgs& a, int b,
+                                               int grp, int t, int v, int row) {
+  constexpr int VN = Vec<T>::N;
+  const size_t d = (((size_t)b * g.G + grp) * g.cap2R + row) * g.D + (size_t)v * VN;
+  const T* sk = static_cast<const T*>(a.k) + b * a.ks[0] + grp * a.ks[1] + t * a.ks[2] + v * VN;
+  const T* skr = static_cast<const T*>(a.k_raw) + b * a.krs[0] + grp * a.krs[1] + t * a.krs[2] + v * VN;
+  const T* sv = static_cast<const T*>(a.v) + b * a.vs[0] + grp * a.vs[1] + t * a.vs[2] + v * VN;
+  *reinterpret_cast<uint4*>(static_cast<T*>(s.recent_k) + d) = *reinterpret_cast<const uint4*>(sk);
+  *reinterpret_cast<uint4*>(static_cast<T*>(s.recent_k_raw) + d) = *reinterpret_cast<const uint4*>(skr);
+  *reinterpret_cast<uint4*>(static_cast<T*>(s.recent_v) + d) = *reinterpret_cast<const uint4*>(sv);
+}
+
 template <typename T>
 __global__ void window_append_kernel(Geo g, logkv_state_t s, AppendArgs a) {
   pdl_entry();
   constexpr int VN = Vec<T>::N;
   const int b = blockIdx.z, grp = blockIdx.y, DV = g.D / VN;
-  const size_t dst0 = (((size_t)b * g.G + grp) * g.cap2R + a.recent_count) * g.D;
-  const size_t units = (size_t)a.n * DV;
-  for (size_t u = blockIdx.x * (size_t)blockDim.x + threadIdx.x; u < units; u += (size_t)gridDim.x * blockDim.x) {
-    const size_t t = u / DV, v = u % DV;
-    const size_t d = dst0 + t * g.D + v * VN;
-    const T* sk = static_cast<const T*>(a.k) + b * a.ks[0] + grp * a.ks[1] + t * a.ks[2] + v * VN;
-    const T* skr = static_cast<const T*>(a.k_raw) + b * a.krs[0] + grp * a.krs[1] + t * a.krs[2] + v * VN;
-    const T* sv = static_cast<const T*>(a.v) + b * a.vs[0] + grp * a.vs[1] + t * a.vs[2] + v * VN;
-    *reinterpret_cast<uint4*>(static_cast<T*>(s.recent_k) + d) = *reinterpret_cast<const uint4*>(sk);
-    *reinterpret_cast<uint4*>(static_cast<T*>(s.recent_k_raw) + d) = *reinterpret_cast<const uint4*>(skr);
-    *reinterpret_cast<uint4*>(static_cast<T*>(s.recent_v) + d) = *reinterpret_cast<const uint4*>(sv);
+  const int units = a.n * DV;   // <= 8192 rows x 256 units
+  for (int u = blockIdx.x * blockDim.x + threadIdx.x; u < units; u += gridDim.x * blockDim.x) {
+    const int t = u / DV;
+    put_chunk_unit<T>(g, s, a, b, grp, t, u - t * DV, a.recent_count + t);
   }
   if (grp == 0 && blockIdx.x == 0)
     for (int t = threadIdx.x; t < a.n; t += blockDim.x) {
@@ -311,6 +318,61 @@ __global__ void window_append_kernel(Geo g, logkv_state_t s, AppendArgs a) {
       s.recent_pos[r] = a.pos ? a.pos[b * a.ps[0] + t * a.ps[1]] : a.pos0 + t;
       s.recent_ends[r] = a.ends[(size_t)b * a.n + t];
     }
+}
+
+// The window write of a flush whose chunk was not appended (logkv_flush_chunk): with c0 =
+// a.recent_count old rows, F = g.F flushed, rem0 = c0 - F <= F kept, the window becomes
+// [old rows F .. c0) ++ [chunk rows 0 .. n) ++ zeros.  Row r of [rem0, max(c0, rem0 + n)) is one
+// thread's: it reads old row r (r in [F, c0)) and writes it to r - F (below rem0, a row no
+// thread reads), then writes chunk row r - rem0 to r, or zeros (an old row left over).  Rows
+// at c0 and above are zero already (every shift zeroes what it vacates) unless a chunk row
+// lands there.
+template <typename T>
+__global__ void window_commit_kernel(Geo g, logkv_state_t s, AppendArgs a) {
+  pdl_entry();
+  constexpr int VN = Vec<T>::N;
+  const int b = blockIdx.z, grp = blockIdx.y, DV = g.D / VN;
+  const int c0 = a.recent_count, F = g.F, rem0 = c0 - F, hi = max(c0, rem0 + a.n);
+  uint4* rk = static_cast<uint4*>(s.recent_k);
+  uint4* rkr = static_cast<uint4*>(s.recent_k_raw);
+  uint4* rv = static_cast<uint4*>(s.recent_v);
+  const size_t base = ((size_t)b * g.G + grp) * g.cap2R * DV;
+  const uint4 zero = make_uint4(0u, 0u, 0u, 0u);
+  for (int u = rem0 * DV + blockIdx.x * blockDim.x + threadIdx.x; u < hi * DV; u += gridDim.x * blockDim.x) {
+    const int r = u / DV, v = u - r * DV;
+    if (r >= F && r < c0) {
+      const uint4 x0 = rk[base + u], x1 = rkr[base + u], x2 = rv[base + u];
+      rk[base + u - (size_t)F * DV] = x0;
+      rkr[base + u - (size_t)F * DV] = x1;
+      rv[base + u - (size_t)F * DV] = x2;
+    }
+    if (r - rem0 < a.n) {
+      put_chunk_unit<T>(g, s, a, b, grp, r - rem0, v, r);
+    } else {
+      rk[base + u] = zero;
+      rkr[base + u] = zero;
+      rv[base + u] = zero;
+    }
+  }
+  if (grp == 0 && blockIdx.x == 0) {
+    const size_t w0 = (size_t)b * g.cap2R;
+    for (int r = rem0 + threadIdx.x; r < hi; r += blockDim.x) {
+      if (r >= F && r < c0) {
+        const int64_t p = s.recent_pos[w0 + r];
+        const uint8_t e = s.recent_ends[w0 + r];
+        s.recent_pos[w0 + r - F] = p;
+        s.recent_ends[w0 + r - F] = e;
+      }
+      const int t = r - rem0;
+      if (t < a.n) {
+        s.recent_pos[w0 + r] = a.pos ? a.pos[b * a.ps[0] + t * a.ps[1]] : a.pos0 + t;
+        s.recent_ends[w0 + r] = a.ends[(size_t)b * a.n + t];
+      } else {
+        s.recent_pos[w0 + r] = 0;
+        s.recent_ends[w0 + r] = 0;
+      }
+    }
+  }
 }
 
 // ---------------------------------------------------------------- workspace
@@ -462,7 +524,7 @@ constexpr int kPhaseScores = 1, kPhaseRoute = 2, kPhaseApply = 4, kPhaseDecide =
 
 template <typename T>
 static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st, cudaEvent_t* ev,
-                        int phases = kPhaseAll, const TapeView* tape = nullptr) {
+                        int phases = kPhaseAll, const TapeView* tape = nullptr, const AppendArgs* chunk = nullptr) {
   int stage = 0;
   auto mark = [&]() {
     if (ev) cudaEventRecord(ev[stage], st);
@@ -521,11 +583,17 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   mark();
   launch_pdl(pool_rewrite_kernel<T>, dim3(per_bg, g.G, g.B), 256, 0, st, g, s, w);
   mark();
-  const int rem = g.recent_count - g.F;
-  const int per_win = std::max(1, std::min(128, (g.recent_count * g.D / (int)(16 / sizeof(T)) + 255) / 256));
-  const int staged = rem > g.F ? 1 : 0;
-  if (staged) launch_pdl(window_stage_kernel<T>, dim3(per_win, g.G, g.B), 256, 0, st, g, s, w, rem);
-  launch_pdl(window_shift_kernel<T>, dim3(per_win, g.G, g.B), 256, 0, st, g, s, w, rem, staged);
+  if (chunk) {
+    const int rem0 = chunk->recent_count - g.F, rows = std::max(chunk->recent_count, rem0 + chunk->n) - rem0;
+    const int per = std::max(1, std::min(128, (rows * g.D / (int)(16 / sizeof(T)) + 255) / 256));
+    launch_pdl(window_commit_kernel<T>, dim3(per, g.G, g.B), 256, 0, st, g, s, *chunk);
+  } else {
+    const int rem = g.recent_count - g.F;
+    const int per_win = std::max(1, std::min(128, (g.recent_count * g.D / (int)(16 / sizeof(T)) + 255) / 256));
+    const int staged = rem > g.F ? 1 : 0;
+    if (staged) launch_pdl(window_stage_kernel<T>, dim3(per_win, g.G, g.B), 256, 0, st, g, s, w, rem);
+    launch_pdl(window_shift_kernel<T>, dim3(per_win, g.G, g.B), 256, 0, st, g, s, w, rem, staged);
+  }
   mark();
   // Recording: the decisions (workspace) and the new span table (state) into the tape.
   if (tape) launch_pdl(tape_copy_kernel, dim3(2 * sm_count), 256, 0, st, tape_segments(g, s, w, *tape, true));
@@ -559,7 +627,7 @@ static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, i
                      int32_t recent_count, void* workspace, size_t workspace_bytes, void* stream, cudaEvent_t* ev,
                      int phases = kPhaseAll, const float* gpart_all = nullptr, int ranks = 1,
                      int tape_mode = kTapeNone, void* tape = nullptr, size_t tape_bytes = 0,
-                     long long rank_stride = 0) {
+                     long long rank_stride = 0, const AppendArgs* chunk = nullptr) {
   const int v = validate(layout, flush_tokens);
   if (v != LOGKV_OK) return v;
   if (!state || !workspace) return LOGKV_E_POINTER;
@@ -593,6 +661,7 @@ static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, i
     return LOGKV_E_SMEM;
   w.gpart_all = gpart_all;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (chunk && (tape_mode != kTapeNone || phases != kPhaseAll)) return LOGKV_E_SHAPE;
   if (tape_mode != kTapeNone) {
     TapeView t{};
     if (!tape || (reinterpret_cast<uintptr_t>(tape) & 15) != 0 || ranks != 1 || phases != kPhaseAll)
@@ -607,8 +676,8 @@ static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, i
     if (layout->dtype == LOGKV_DTYPE_BF16) return launch_flush<__nv_bfloat16>(g, *state, w, st, ev, phases, &t);
     return launch_flush<float>(g, *state, w, st, ev, phases, &t);
   }
-  if (layout->dtype == LOGKV_DTYPE_BF16) return launch_flush<__nv_bfloat16>(g, *state, w, st, ev, phases);
-  return launch_flush<float>(g, *state, w, st, ev, phases);
+  if (layout->dtype == LOGKV_DTYPE_BF16) return launch_flush<__nv_bfloat16>(g, *state, w, st, ev, phases, nullptr, chunk);
+  return launch_flush<float>(g, *state, w, st, ev, phases, nullptr, chunk);
 }
 
 }  // namespace logkv
@@ -660,13 +729,12 @@ extern "C" int logkv_flush_replay(const logkv_layout_t* layout, const logkv_stat
                    kPhaseAll, nullptr, 1, kTapeReplay, const_cast<void*>(tape), tape_bytes);
 }
 
-extern "C" int logkv_window_append(const logkv_layout_t* layout, const logkv_state_t* state, const void* k,
-                                   const int64_t* k_strides, const void* k_raw, const int64_t* k_raw_strides,
-                                   const void* v, const int64_t* v_strides, const int64_t* positions,
-                                   const int64_t* pos_strides, int64_t pos0, const uint8_t* ends, int32_t n,
-                                   int32_t recent_count, void* stream) {
-  const int val = validate(layout, 1);
-  if (val != LOGKV_OK) return val;
+// Chunk arguments: checks (LOGKV_E_POINTER for a missing or misaligned row, LOGKV_E_SHAPE for
+// rows past the window) and the kernel's view.
+static int make_append(const logkv_layout_t* layout, const logkv_state_t* state, const void* k,
+                       const int64_t* k_strides, const void* k_raw, const int64_t* k_raw_strides, const void* v,
+                       const int64_t* v_strides, const int64_t* positions, const int64_t* pos_strides, int64_t pos0,
+                       const uint8_t* ends, int32_t n, int32_t recent_count, AppendArgs* out) {
   if (!state || !k || !k_raw || !v || !ends || !k_strides || !k_raw_strides || !v_strides ||
       (positions && !pos_strides))
     return LOGKV_E_POINTER;
@@ -695,6 +763,22 @@ extern "C" int logkv_window_append(const logkv_layout_t* layout, const logkv_sta
   if (!a16(k) || !a16(k_raw) || !a16(v) || !a16(state->recent_k) || !a16(state->recent_k_raw) ||
       !a16(state->recent_v) || !state->recent_pos || !state->recent_ends)
     return LOGKV_E_POINTER;
+  *out = a;
+  return LOGKV_OK;
+}
+
+extern "C" int logkv_window_append(const logkv_layout_t* layout, const logkv_state_t* state, const void* k,
+                                   const int64_t* k_strides, const void* k_raw, const int64_t* k_raw_strides,
+                                   const void* v, const int64_t* v_strides, const int64_t* positions,
+                                   const int64_t* pos_strides, int64_t pos0, const uint8_t* ends, int32_t n,
+                                   int32_t recent_count, void* stream) {
+  const int val = validate(layout, 1);
+  if (val != LOGKV_OK) return val;
+  AppendArgs a{};
+  const int rc = make_append(layout, state, k, k_strides, k_raw, k_raw_strides, v, v_strides, positions, pos_strides,
+                             pos0, ends, n, recent_count, &a);
+  if (rc != LOGKV_OK) return rc;
+  const size_t esize = layout->dtype == LOGKV_DTYPE_BF16 ? 2 : 4;
   const Geo g = make_geo(*layout, 1, recent_count);
   const int per = std::max(1, std::min(64, (int)(((size_t)n * g.D / (16 / esize) + 255) / 256)));
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -703,6 +787,36 @@ extern "C" int logkv_window_append(const logkv_layout_t* layout, const logkv_sta
   else
     launch_pdl(window_append_kernel<float>, dim3(per, g.G, g.B), 256, 0, st, g, *state, a);
   return (int)cudaGetLastError();
+}
+
+static int flush_chunk(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                       int32_t recent_count, const logkv_chunk_t* c, void* workspace, size_t workspace_bytes,
+                       void* stream, cudaEvent_t* ev) {
+  const int val = validate(layout, flush_tokens);
+  if (val != LOGKV_OK) return val;
+  if (!c) return LOGKV_E_POINTER;
+  if (recent_count < flush_tokens || recent_count > 2 * flush_tokens) return LOGKV_E_SHAPE;
+  AppendArgs a{};
+  const int rc = make_append(layout, state, c->k, c->k_strides, c->k_raw, c->k_raw_strides, c->v, c->v_strides,
+                             c->positions, c->pos_strides, c->pos0, c->ends, c->n, recent_count, &a);
+  if (rc != LOGKV_OK) return rc;
+  return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream, ev, kPhaseAll,
+                   nullptr, 1, kTapeNone, nullptr, 0, 0, &a);
+}
+
+extern "C" int logkv_flush_chunk(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
+                                 int32_t recent_count, const logkv_chunk_t* chunk, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  return flush_chunk(layout, state, flush_tokens, recent_count, chunk, workspace, workspace_bytes, stream, nullptr);
+}
+
+extern "C" int logkv_flush_chunk_profiled(const logkv_layout_t* layout, const logkv_state_t* state,
+                                          int32_t flush_tokens, int32_t recent_count, const logkv_chunk_t* chunk,
+                                          void* workspace, size_t workspace_bytes, void* stream, void** events,
+                                          int32_t n_events) {
+  if (!events || n_events < LOGKV_FLUSH_STAGES + 1) return LOGKV_E_POINTER;
+  return flush_chunk(layout, state, flush_tokens, recent_count, chunk, workspace, workspace_bytes, stream,
+                     reinterpret_cast<cudaEvent_t*>(events));
 }
 
 extern "C" int logkv_flush_oplog_append(const logkv_layout_t* layout, int32_t flush_tokens, void* workspace,
