@@ -51,18 +51,21 @@ ROW_BYTES = 256 + 256 + 4 + 4 * 8 + 1   # one bf16 ladder entry (13 fields, firs
 # and move) in the one-launch ncu capture of this build at this layer shape (the
 # profiling command is in the cascade profile summary).  Written rows mostly stay in L2 within the
 # launch, so the figure is below the algorithmic bytes.
-CASCADE_TRAFFIC = 35_741_952
+CASCADE_TRAFFIC = 15_832_832 + 0 + 20_753_408 + 2_816
+# The same for one chunk attention launch (chunk_attn_tc_kernel, the prefill leg's shape).
+PREFILL_TRAFFIC = 51_040_512 + 721_664
 FLUSH_KERNELS = 12                      # kernel launches per flushing layer-chunk (the last writes the chunk)
 METRIC = "flush us per 2048-tok chunk/layer"
 
 
-def measured_peaks():
+def measured_peaks(key: str = "hbm_gbs"):
+    """(peak, "measured" | "fallback"): HBM copy GB/s or burst bf16 GEMM TFLOP/s of this pool's B200s."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
         with open(path) as fh:
             d = json.load(fh)
-        return float(d["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+        return float(d[key]), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}[key], "fallback"
 
 
 class ClockSampler:
@@ -973,16 +976,12 @@ def bench_prefill(args, rank, world, local_rank):
     Lp = int(caches[0]._read.length[0].float().mean().item())
     R = cfg["recent"]
     flops = 4.0 * D * H * (T * (Lp + R) + T * (T + 1) / 2)   # QK^T and PV over the visible slots
-    peak = 1649.1
-    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
-    if os.path.exists(path):
-        with open(path) as fh:
-            peak = float(json.load(fh)["bf16_tflops"])
+    peak, peak_kind = measured_peaks("bf16_tflops")
     tflops = flops / (us * 1e-6) / 1e12
     return {"metric": "chunk attention us per 2048-token chunk/layer", "value": round(us, 2), "unit": "us",
             "roofline": {"bound": "tensor", "kernel": "chunk_attn_tc_kernel", "achieved": round(tflops, 1),
-                         "peak": peak, "unit": "TFLOP/s", "frac": round(tflops / peak, 4), "traffic": None,
-                         "flops_per_launch": flops},
+                         "peak": peak, "peak_kind": peak_kind, "unit": "TFLOP/s", "frac": round(tflops / peak, 4),
+                         "traffic": PREFILL_TRAFFIC, "flops_per_launch": flops},
             "config": {"heads": H, "groups": G, "head_dim": D, "chunk": T, "prefix_slots": Lp, "recent": R,
                        "layers": cfg["layers"], "distinct_layer_caches": 2}}
 
