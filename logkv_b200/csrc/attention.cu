@@ -14,6 +14,7 @@
 //                            softmax in the log2 domain, CTA and cross-CTA combines
 //                            in a fixed order (the last CTA of a lane combines).
 #include <algorithm>
+#include <type_traits>
 #include <cstring>
 
 #include <cuda.h>
@@ -356,11 +357,18 @@ struct AttnGeo {
   int causal;
   int nsplit, pcap, rcap, rcount;
   int nsmin;     // splits a lane of the tensor-core decode kernel uses at least (fills every SM)
+  int ups;       // 16-row tiles per split of the tensor-core decode kernel (attn_units_per_split)
   float scale_log2, qx;
 };
 
 constexpr int kAttnWarps = 4;
-constexpr int kUnitsPerSplit = 128;   // 16-row tiles per split of the tensor-core decode kernel
+// Tensor-core decode: up to 256 lanes (batch x groups) take three cp.async stages per warp at two
+// CTAs per SM and splits of 64 tiles (up to 64 lanes) or 128; more lanes two stages at three CTAs
+// per SM (measured on B200 at 8305 slots per lane: 0.69 / 0.79 / 0.84 / 0.90 of HBM at batch 8 /
+// 16 / 32 / 64 with 8 groups, against 0.60 / 0.61 / 0.79 / 0.90 with two stages everywhere).
+constexpr int kDeepLanes = 256;
+static int attn_stages(int lanes) { return lanes <= kDeepLanes ? 3 : 2; }
+static int attn_units_per_split(int lanes) { return lanes <= 64 ? 64 : 128; }
 constexpr int kAttnStages = 3;
 // The tensor-core decode kernel keeps two tiles per warp in flight and fits three CTAs (12 warps)
 // per SM, so more warps overlap one tile's math with the next tiles' loads.
@@ -706,14 +714,14 @@ __device__ __forceinline__ unsigned pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const unsigned*>(&v);
 }
 
-template <int D>
+template <int D, int ST = kMmaStages>
 struct MmaShape {
   static constexpr int TS = 16;             // slots per tile (two n8 score tiles, one k16 PV step)
   static constexpr int CPR = D / 8;         // 16-byte chunks per row
   static constexpr int KS = D / 16;         // k16 steps of QK^T
   static constexpr int DT = D / 8;          // n8 output tiles of PV
   static constexpr int STAGE_BYTES = 2 * TS * D * 2 + TS * 4;   // K, V (bf16) and the mass column
-  static constexpr size_t smem = (size_t)kAttnWarps * kMmaStages * STAGE_BYTES;
+  static constexpr size_t smem = (size_t)kAttnWarps * ST * STAGE_BYTES;   // ST stages per warp
   static_assert(D % 16 == 0 && D >= 16 && D <= 256, "head dim must be a multiple of 16 up to 256");
   // Physical 16-byte chunk of logical chunk c in row r: rows of 8 consecutive ldmatrix
   // addresses land in 8 distinct 16-byte bank groups.
@@ -723,15 +731,15 @@ struct MmaShape {
   }
 };
 
-template <int D, int NQ>
-__global__ void __launch_bounds__(kAttnWarps * 32, 3) slot_attn_mma_kernel(AttnGeo a, logkv_prefix_t pre,
+template <int D, int NQ, int ST>
+__global__ void __launch_bounds__(kAttnWarps * 32, ST == 2 ? 3 : 2) slot_attn_mma_kernel(AttnGeo a, logkv_prefix_t pre,
                                                                        const __nv_bfloat16* rk,
                                                                        const __nv_bfloat16* rv,
                                                                        const __nv_bfloat16* kn,
                                                                        const __nv_bfloat16* vn,
                                                                        const __nv_bfloat16* q, __nv_bfloat16* out,
                                                                        float* part, int* ticket) {
-  using S = MmaShape<D>;
+  using S = MmaShape<D, ST>;
   constexpr int TS = S::TS, CPR = S::CPR, KS = S::KS, DT = S::DT;
   static_assert(NQ >= 1 && NQ <= 16, "at most 16 query rows per lane");
   extern __shared__ uint4 smem4[];
@@ -741,7 +749,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) slot_attn_mma_kernel(AttnG
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int g8 = lane >> 2, t4 = lane & 3;  // fragment row group and column pair
   const int ln = blockIdx.x, split = blockIdx.y, g = ln % a.G, b = ln / a.G;
-  unsigned char* wbase = reinterpret_cast<unsigned char*>(smem4) + (size_t)warp * kMmaStages * S::STAGE_BYTES;
+  unsigned char* wbase = reinterpret_cast<unsigned char*>(smem4) + (size_t)warp * ST * S::STAGE_BYTES;
   const unsigned wbase_s = (unsigned)__cvta_generic_to_shared(wbase);
   const __nv_bfloat16* PK = static_cast<const __nv_bfloat16*>(pre.k);
   const __nv_bfloat16* PV = static_cast<const __nv_bfloat16*>(pre.v);
@@ -749,9 +757,9 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) slot_attn_mma_kernel(AttnG
   const int Lp = min(max(pre.length[ln], 0), pre.capacity), R = a.rcount, Tn = a.T;
   const int up = (Lp + TS - 1) / TS, ur = (R + TS - 1) / TS, uc = (Tn + TS - 1) / TS;
   const int U = up + ur + uc;
-  // This lane's splits: about kUnitsPerSplit tiles each (long streams per warp), at least
+  // This lane's splits: about a.ups tiles each (long streams per warp), at least
   // a.nsmin (every SM busy at small batch); the grid's further splits return at once.
-  const int ns = min(a.nsplit, max(a.nsmin, U / kUnitsPerSplit));
+  const int ns = min(a.nsplit, max(a.nsmin, U / a.ups));
   if (split >= ns) return;
   const int u0 = (int)((long long)U * split / ns), u1 = (int)((long long)U * (split + 1) / ns);
   const int mine = (u1 - u0) > warp ? (u1 - u0 - warp + kAttnWarps - 1) / kAttnWarps : 0;
@@ -848,12 +856,12 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) slot_attn_mma_kernel(AttnG
   const int rq0 = g8 % a.TQ, rq1 = (g8 + 8) % a.TQ;         // query token of each row
 
 #pragma unroll
-  for (int k = 0; k < kMmaStages - 1; ++k) issue(k, k);
+  for (int k = 0; k < ST - 1; ++k) issue(k, k);
   for (int k = 0; k < mine; ++k) {
-    issue(k + kMmaStages - 1, (k + kMmaStages - 1) % kMmaStages);
-    cp_async_wait<kMmaStages - 1>();
+    issue(k + ST - 1, (k + ST - 1) % ST);
+    cp_async_wait<ST - 1>();
     __syncwarp();
-    const int stage = k % kMmaStages;
+    const int stage = k % ST;
     const __nv_bfloat16 *kb_, *vb_;
     const float* mb_;
     int rows, cls, first;
@@ -979,7 +987,7 @@ __global__ void __launch_bounds__(kAttnWarps * 32, 3) slot_attn_mma_kernel(AttnG
         const float f = exp2f(wm_[w][r] - mx);
         l += wl_[w][r] * f;
         ov += reinterpret_cast<const float*>(reinterpret_cast<unsigned char*>(smem4) +
-                                             (size_t)w * kMmaStages * S::STAGE_BYTES)[r * D + d] * f;
+                                             (size_t)w * ST * S::STAGE_BYTES)[r * D + d] * f;
       }
     }
     if (ns == 1) {
@@ -1717,7 +1725,7 @@ static void launch_pack_mid(const PlanGeo& pg, const logkv_state_t& s, const log
                                                     static_cast<T*>(ov), status);
 }
 
-// Splits per lane of the grid: kUnitsPerSplit 16-row tiles each at full prefix capacity, and
+// Splits per lane of the grid: attn_units_per_split 16-row tiles each at full prefix capacity, and
 // at least one CTA per SM over all lanes (attn_min_splits).  The tensor-core kernel sizes each
 // lane's splits again from its actual lengths (slot_attn_mma_kernel), at most this many.
 static int attn_min_splits(const logkv_layout_t& l) {
@@ -1727,7 +1735,8 @@ static int attn_min_splits(const logkv_layout_t& l) {
 
 static int attn_splits(const logkv_layout_t& l, int prefix_capacity) {
   const int units = (prefix_capacity + l.recent_capacity) / 16 + 1;
-  return std::max(1, std::min(std::max(units / kUnitsPerSplit, attn_min_splits(l)), 256));
+  const int ups = attn_units_per_split(l.batch * l.groups);
+  return std::max(1, std::min(std::max(units / ups, attn_min_splits(l)), 256));
 }
 
 static size_t attn_part_bytes(const logkv_layout_t& l, int nq, int nsplit) {
@@ -1762,17 +1771,22 @@ static int launch_attn_d(int nq, const AttnGeo& ag, const logkv_prefix_t& pre, c
 template <int D, int NQ>
 static int launch_mma_dq(const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
                          const logkv_attention_args_t& x, float* part, int* ticket, cudaStream_t st) {
-  using S = MmaShape<D>;
-  if (S::smem > 227 * 1024) return LOGKV_E_SMEM;
-  auto kern = slot_attn_mma_kernel<D, NQ>;
-  if (S::smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::smem);
-  using B16 = __nv_bfloat16;
-  // Lanes along x, splits along y: a lane's unused splits are the last CTAs dispatched.
-  kern<<<dim3(ag.G * ag.B, ag.nsplit), kAttnWarps * 32, S::smem, st>>>(
-      ag, pre, static_cast<const B16*>(s.recent_k), static_cast<const B16*>(s.recent_v),
-      static_cast<const B16*>(x.k_new), static_cast<const B16*>(x.v_new), static_cast<const B16*>(x.q),
-      static_cast<B16*>(x.out), part, ticket);
-  return launch_status();
+  auto go = [&](auto stages) {
+    constexpr int ST = decltype(stages)::value;
+    using S = MmaShape<D, ST>;
+    if (S::smem > 227 * 1024) return (int)LOGKV_E_SMEM;
+    auto kern = slot_attn_mma_kernel<D, NQ, ST>;
+    if (S::smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::smem);
+    using B16 = __nv_bfloat16;
+    // Lanes along x, splits along y: a lane's unused splits are the last CTAs dispatched.
+    kern<<<dim3(ag.G * ag.B, ag.nsplit), kAttnWarps * 32, S::smem, st>>>(
+        ag, pre, static_cast<const B16*>(s.recent_k), static_cast<const B16*>(s.recent_v),
+        static_cast<const B16*>(x.k_new), static_cast<const B16*>(x.v_new), static_cast<const B16*>(x.q),
+        static_cast<B16*>(x.out), part, ticket);
+    return launch_status();
+  };
+  if (attn_stages(ag.G * ag.B) == 3) return go(std::integral_constant<int, 3>{});
+  return go(std::integral_constant<int, 2>{});
 }
 
 template <int D>
@@ -1914,7 +1928,7 @@ static int launch_attn(int dtype, int D, int nq, const AttnGeo& ag, const logkv_
 
 // Dynamic shared memory of the decode kernel launch_attn picks (the last CTA's split combine
 // reuses it: 2 * nsplit * nq + nq floats).
-static size_t decode_smem(int dtype, int D, int nq) {
+static size_t decode_smem(int dtype, int D, int nq, int lanes) {
   auto pick = [&](auto tag) -> size_t {
     using T = decltype(tag);
     switch (nq) {
@@ -1926,12 +1940,13 @@ static size_t decode_smem(int dtype, int D, int nq) {
     }
   };
   if (dtype == LOGKV_DTYPE_BF16) {
+    const int st = attn_stages(lanes);
     switch (D) {
-      case 16: return MmaShape<16>::smem;
-      case 32: return MmaShape<32>::smem;
-      case 64: return MmaShape<64>::smem;
-      case 128: return MmaShape<128>::smem;
-      case 256: return MmaShape<256>::smem;
+      case 16: return st == 3 ? MmaShape<16, 3>::smem : MmaShape<16, 2>::smem;
+      case 32: return st == 3 ? MmaShape<32, 3>::smem : MmaShape<32, 2>::smem;
+      case 64: return st == 3 ? MmaShape<64, 3>::smem : MmaShape<64, 2>::smem;
+      case 128: return st == 3 ? MmaShape<128, 3>::smem : MmaShape<128, 2>::smem;
+      case 256: return st == 3 ? MmaShape<256, 3>::smem : MmaShape<256, 2>::smem;
       default: return 0;
     }
   }
@@ -2026,7 +2041,7 @@ LOGKV_API int logkv_attention(const logkv_layout_t* layout, const logkv_state_t*
   const size_t need = logkv_attention_workspace_bytes(layout, H, TQ, prefix->capacity);
   if (!workspace || workspace_bytes < need) return LOGKV_E_WORKSPACE;
   // Splits: attn_splits, at most as many as the last CTA's combine can weigh in shared memory.
-  const size_t dsm = decode_smem(layout->dtype, layout->dim, nq);
+  const size_t dsm = decode_smem(layout->dtype, layout->dim, nq, layout->batch * G);
   const int ncap = dsm > (size_t)(4 * nq) ? (int)((dsm - 4 * (size_t)nq) / (8 * (size_t)nq)) : 1;
   const int nsplit = std::max(1, std::min(attn_splits(*layout, prefix->capacity), ncap));
   const size_t lanes = (size_t)layout->batch * G;
@@ -2044,6 +2059,7 @@ LOGKV_API int logkv_attention(const logkv_layout_t* layout, const logkv_state_t*
   ag.causal = args->causal ? 1 : 0;
   ag.nsplit = nsplit;
   ag.nsmin = std::min(attn_min_splits(*layout), nsplit);
+  ag.ups = attn_units_per_split(layout->batch * G);
   ag.pcap = prefix->capacity;
   ag.rcap = layout->recent_capacity;
   ag.rcount = args->recent_count;
