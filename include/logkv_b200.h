@@ -289,7 +289,10 @@ LOGKV_API int logkv_flush_partials(const logkv_layout_t* layout, int32_t flush_t
  * state the recorded flush started from: the recorded rows replace the window's flushed rows,
  * nothing is routed, scored or chosen, and the cache ends exactly as the recorded flush left
  * it (buffers bit for bit).  The order of replays is the caller's to keep (the Python cache
- * checks it).  Neither runs KV-head sharded.
+ * checks it).  A KV-head-sharded rank records with logkv_flush_commit_record, the commit half of
+ * its flush (logkv_flush_commit_strided's arguments; rank_stride 0 = the parts' own count) that
+ * also writes its record; logkv_flush_replay of that record needs no exchange, since the record
+ * holds the span choice the ranks made together.
  */
 /*
  * Route op-log (replaces the op-log rows of _record_ops, litgpt/log_kv_cache.py:2043-2071,
@@ -309,6 +312,10 @@ LOGKV_API size_t logkv_tape_bytes(const logkv_layout_t* layout, int32_t flush_to
 LOGKV_API int logkv_flush_record(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
                                  int32_t recent_count, void* workspace, size_t workspace_bytes, void* tape,
                                  size_t tape_bytes, void* stream);
+LOGKV_API int logkv_flush_commit_record(const logkv_layout_t* layout, const logkv_state_t* state,
+                                        int32_t flush_tokens, int32_t recent_count, void* workspace,
+                                        size_t workspace_bytes, const float* partials_all, int32_t ranks,
+                                        int64_t rank_stride, void* tape, size_t tape_bytes, void* stream);
 LOGKV_API int logkv_flush_replay(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,
                                  int32_t recent_count, void* workspace, size_t workspace_bytes, const void* tape,
                                  size_t tape_bytes, void* stream);

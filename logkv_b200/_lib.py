@@ -149,6 +149,10 @@ def lib() -> ctypes.CDLL:
         handle.logkv_tape_bytes.argtypes = [P(Layout), ctypes.c_int32]
         handle.logkv_flush_record.restype = ctypes.c_int
         handle.logkv_flush_record.argtypes = flush_args + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+        handle.logkv_flush_commit_record.restype = ctypes.c_int
+        handle.logkv_flush_commit_record.argtypes = flush_args[:6] + [ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
+                                                                      ctypes.c_void_p, ctypes.c_size_t,
+                                                                      ctypes.c_void_p]
         handle.logkv_flush_replay.restype = ctypes.c_int
         handle.logkv_flush_replay.argtypes = flush_args + [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
         handle.logkv_attention_plan.restype = ctypes.c_int

@@ -317,16 +317,24 @@ class LogStructuredKVCache(nn.Module):
             raise RuntimeError("duplicate or incorrectly bound semantic update recording")
         if not record_op_log:
             raise RuntimeError("semantic update recording requires record_op_log=True")
-        if self.kv_shard_group is not None:
-            raise NotImplementedError("update recording is not implemented for KV-head-sharded caches")
         nbytes = lib.logkv_tape_bytes(ctypes.byref(self._layout), int(take))
         tape = torch.empty(nbytes, dtype=torch.uint8, device=dev)
         self._ladder_epoch += 1
         state = self._state_struct()
-        _lib.check(lib.logkv_flush_record(
-            ctypes.byref(self._layout), ctypes.byref(state), int(take), int(self.recent_count),
-            ctypes.c_void_p(self._workspace.data_ptr()), self._workspace.numel(), ctypes.c_void_p(tape.data_ptr()),
-            tape.numel(), ctypes.c_void_p(_lib.stream_ptr(dev))), "logkv_flush_record")
+        if self.kv_shard_group is not None:
+            # The scores of this rank's groups, the span-part exchange, then the commit with the
+            # record (which holds the ranks' common span choice: its replay needs no exchange).
+            args = self._flush_args(take)
+            world = self._gather_parts(args, take)
+            _lib.check(lib.logkv_flush_commit_record(
+                *args[:6], ctypes.c_void_p(self._span_gather.data_ptr()), world, 0, ctypes.c_void_p(tape.data_ptr()),
+                tape.numel(), args[6]), "logkv_flush_commit_record")
+        else:
+            _lib.check(lib.logkv_flush_record(
+                ctypes.byref(self._layout), ctypes.byref(state), int(take), int(self.recent_count),
+                ctypes.c_void_p(self._workspace.data_ptr()), self._workspace.numel(),
+                ctypes.c_void_p(tape.data_ptr()), tape.numel(), ctypes.c_void_p(_lib.stream_ptr(dev))),
+                "logkv_flush_record")
         ready = torch.cuda.Event()
         ready.record(torch.cuda.current_stream(dev))
         index = updates.save(tape, owned=True)
@@ -432,19 +440,24 @@ class LogStructuredKVCache(nn.Module):
         events = (ctypes.c_void_p * len(self.profile_events))(*[e.cuda_event for e in self.profile_events])
         _lib.check(_lib.lib().logkv_flush_profiled(*args, events, len(self.profile_events)), "logkv_flush_profiled")
 
-    def _sharded_flush(self, args, take: int) -> None:
-        """Scores of this rank's groups, all-gather of every rank's span parts, then the commit."""
+    def _gather_parts(self, args, take: int) -> int:
+        """Scores of this rank's groups and the all-gather of every rank's span parts into
+        ``self._span_gather``; returns the rank count."""
         import torch.distributed as dist
         from .sharding import gather_span_parts
-        lib = _lib.lib()
-        _lib.check(lib.logkv_flush_scores(*args), "logkv_flush_scores")
+        _lib.check(_lib.lib().logkv_flush_scores(*args), "logkv_flush_scores")
         local = self._local_parts(take)
         world = dist.get_world_size(self.kv_shard_group)
         if self._span_gather is None or self._span_gather.numel() != world * local.numel():
             self._span_gather = torch.empty(world * local.numel(), dtype=torch.float32, device=self._workspace.device)
         gather_span_parts(local, self.kv_shard_group, out=self._span_gather)
-        _lib.check(lib.logkv_flush_commit(*args[:6], ctypes.c_void_p(self._span_gather.data_ptr()), world, args[6]),
-                   "logkv_flush_commit")
+        return world
+
+    def _sharded_flush(self, args, take: int) -> None:
+        """Scores of this rank's groups, all-gather of every rank's span parts, then the commit."""
+        world = self._gather_parts(args, take)
+        _lib.check(_lib.lib().logkv_flush_commit(*args[:6], ctypes.c_void_p(self._span_gather.data_ptr()), world,
+                                                 args[6]), "logkv_flush_commit")
 
     def read_counters(self) -> dict:
         """Row counters accumulated by every flush of this cache (synchronizes)."""
@@ -510,11 +523,8 @@ class LogStructuredKVCache(nn.Module):
         copy and can be captured in a CUDA graph.
         """
         replaying = any(v_ is not None for v_ in replay.values())
-        if self._active_updates is None and replaying:
-            raise NotImplementedError("op-log replay outside an update tape context is not implemented by "
-                                      "logkv_b200 (replay a recorded update tape instead)")
         chunk = self._check_chunk(k, v, k_raw, input_pos, span_ends, span_ends_device)
-        take = self._chunk_flush_take(chunk[-1])
+        take = None if replaying else self._chunk_flush_take(chunk[-1])
         if take is not None:
             # The one flush this chunk triggers, with the chunk written once after the shift.
             self._flush_chunk(chunk, take)
@@ -525,6 +535,10 @@ class LogStructuredKVCache(nn.Module):
         self._append_window(*chunk)
         self.recent_count += chunk[-1]
         for take in self._pending_flushes():
+            if self._active_updates is None and replaying:
+                # As the reference's Alpha flush (log_kv_cache.py:5060-5061): an op-log alone cannot
+                # replay an Alpha flush; the update tape can.
+                raise RuntimeError("AlphaLogKV replay requires semantic_replay_updates; reranking is not allowed")
             if self._active_updates is not None:
                 self._flush_with_updates(take, record_op_log, replaying or self._replaying_updates)
             else:

@@ -664,8 +664,11 @@ static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, i
   if (chunk && (tape_mode != kTapeNone || phases != kPhaseAll)) return LOGKV_E_SHAPE;
   if (tape_mode != kTapeNone) {
     TapeView t{};
-    if (!tape || (reinterpret_cast<uintptr_t>(tape) & 15) != 0 || ranks != 1 || phases != kPhaseAll)
-      return LOGKV_E_POINTER;
+    // A whole unsharded flush, or the commit half of a sharded one when recording (the record
+    // holds the span choice, so its replay needs no exchange).
+    const bool whole = phases == kPhaseAll && ranks == 1;
+    const bool commit_record = phases == kPhaseCommit && tape_mode == kTapeRecord;
+    if (!tape || (reinterpret_cast<uintptr_t>(tape) & 15) != 0 || !(whole || commit_record)) return LOGKV_E_POINTER;
     if (tape_bytes < tape_carve(g, esize, static_cast<char*>(tape), &t)) return LOGKV_E_WORKSPACE;
     g.tape = tape_mode;
     w.tape_cuts = t.cuts;
@@ -720,6 +723,15 @@ extern "C" int logkv_flush_record(const logkv_layout_t* layout, const logkv_stat
                                   size_t tape_bytes, void* stream) {
   return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream, nullptr,
                    kPhaseAll, nullptr, 1, kTapeRecord, tape, tape_bytes);
+}
+
+extern "C" int logkv_flush_commit_record(const logkv_layout_t* layout, const logkv_state_t* state,
+                                         int32_t flush_tokens, int32_t recent_count, void* workspace,
+                                         size_t workspace_bytes, const float* partials_all, int32_t ranks,
+                                         int64_t rank_stride, void* tape, size_t tape_bytes, void* stream) {
+  if (rank_stride < 0) return LOGKV_E_SHAPE;
+  return run_flush(layout, state, flush_tokens, recent_count, workspace, workspace_bytes, stream, nullptr,
+                   kPhaseCommit, partials_all, ranks, kTapeRecord, tape, tape_bytes, rank_stride);
 }
 
 extern "C" int logkv_flush_replay(const logkv_layout_t* layout, const logkv_state_t* state, int32_t flush_tokens,

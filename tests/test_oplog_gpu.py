@@ -63,3 +63,30 @@ def test_op_log_overflow_raises():
             cache.add_recent(k, v, k_raw=kr, input_pos=pos, span_ends=chunk["span_ends"].tolist(),
                              record_op_log=True)
             cache.take_op_log()
+
+
+def test_op_log_replay_of_an_alpha_flush_raises_as_the_reference():
+    """Outside an update-tape context the reference cannot replay an Alpha flush from an op-log
+    (log_kv_cache.py:5060-5061): the chunk is appended, the flush raises, the window keeps the
+    chunk.  Chunks that flush nothing pass."""
+    cfg = config(CONFIGS[0]["name"])
+    stream = make_stream(cfg)
+    cache = make_cache(cfg, stream)
+    log = torch.zeros(cfg["batch"], cfg["groups"], 4, 4, dtype=torch.int32, device="cuda")
+    length = torch.zeros(cfg["batch"], cfg["groups"], dtype=torch.int32, device="cuda")
+    dt = cache.level_k.dtype
+    raised = False
+    for chunk in stream["chunks"][:3]:
+        k = torch.from_numpy(chunk["k"]).to("cuda", dt)
+        kr = torch.from_numpy(chunk["k_raw"]).to("cuda", dt)
+        v = torch.from_numpy(chunk["v"]).to("cuda", dt)
+        before = cache.recent_count
+        try:
+            cache.add_recent(k, v, k_raw=kr, span_ends=chunk["span_ends"].tolist(), replay_op_log=log,
+                             replay_op_log_len=length)
+        except RuntimeError as exc:
+            assert "AlphaLogKV replay requires semantic_replay_updates" in str(exc)
+            assert cache.recent_count == before + k.size(2)
+            raised = True
+            break
+    assert raised

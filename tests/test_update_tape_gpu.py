@@ -124,11 +124,13 @@ def test_replay_errors_and_prefilled_cache():
             pytest.raises(RuntimeError, match="missing"):
         for chunk in chunks:
             push(fresh, cfg, chunk)
-    # Recording needs record_op_log=True; outside a context, replay arguments are refused.
+    # Recording needs record_op_log=True; outside a context, an op-log cannot replay an Alpha flush
+    # (the reference's error, log_kv_cache.py:5060-5061, raised when the chunk flushes).
     fresh.reset_parameters()
     with fresh._semantic_update_context(_SemanticReplayUpdates()), pytest.raises(RuntimeError, match="record_op_log"):
         for chunk in chunks:
             push(fresh, cfg, chunk)
     fresh.reset_parameters()
-    with pytest.raises(NotImplementedError):
-        push(fresh, cfg, chunks[0], replay_op_log=torch.zeros(1))
+    with pytest.raises(RuntimeError, match="AlphaLogKV replay requires semantic_replay_updates"):
+        for chunk in chunks:
+            push(fresh, cfg, chunk, replay_op_log=torch.zeros(1))
