@@ -1262,12 +1262,15 @@ __global__ void __launch_bounds__(kPfWarps * 32) chunk_attn_mma_kernel(AttnGeo a
 //                   S(t,u), add the mass term, mask, online softmax (lazy rescaling: the running
 //                   max moves only when a tile exceeds it by more than 2^8), write P(t,u) as bf16
 //                   over S(t,u)'s first 32 columns;
-//   warp 4NQ        one thread issues S(t,u+1) = Q_t K^T for every tile t while the softmax of
-//                   tile u runs, then O_t += P(t,u) V (P from tensor memory, V an MN-major
-//                   shared-memory operand); with NQ = 2 the tensor core alternates between the
-//                   two query tiles, so one warpgroup's softmax hides behind the other's products;
-//   next 3 warps    cp.async loaders of the 64-slot K/V tiles (two stages, 128-byte swizzled
-//                   canonical layouts, chunk ^ (row & 7)).
+//   warps 4NQ..5NQ-1  one MMA-issuing thread per query tile t: S(t,u+1) = Q_t K^T while the
+//                   softmax of unit u runs, then O_t += P(t,u) V (P from tensor memory, V an
+//                   MN-major shared-memory operand).  Each tile's chain waits only on its own
+//                   softmax, so a slow step of one tile does not hold back the other's products
+//                   (the tensor core takes both issuers' instructions); a K/V stage is free once
+//                   both issuers have released it (after their PV, or at once for a unit past a
+//                   tile's causal range);
+//   next 3 warps    loaders of the 64-slot K/V tiles (TMA for full tiles, cp.async for partial
+//                   ones; 128-byte swizzled canonical layouts, chunk ^ (row & 7)).
 // Tensor memory: tile t's S in columns [64t, 64t+64), released as soon as the softmax has loaded it
 // (so S(t,u+1) is computed while the softmax of tile u runs); its P double-buffered as bf16 in
 // [64NQ + 64t + 32b, +32) (b = u & 1); its O at [128NQ + tD, 128NQ + (t+1)D).  Stages and buffers
@@ -1284,9 +1287,9 @@ template <int NQ>
 struct TcRoles {
   static constexpr int STAGES = NQ == 1 ? 2 : 4;   // K/V stages in shared memory
   static constexpr int SOFTMAX_WARPS = 4 * NQ;
-  static constexpr int MMA_WARP = 4 * NQ;
-  static constexpr int LOADER_WARP0 = 4 * NQ + 1;
-  static constexpr int WARPS = 4 * NQ + 4;
+  static constexpr int MMA_WARP0 = 4 * NQ;         // one issuer warp per query tile
+  static constexpr int LOADER_WARP0 = 5 * NQ;
+  static constexpr int WARPS = 5 * NQ + 3;
   static constexpr uint32_t COLS = NQ == 1 ? 256u : 512u;
 };
 
@@ -1364,7 +1367,7 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
     tc::mbar_init(&q_full, 2 * kTcLoaders);
     for (int i = 0; i < ST; ++i) {
       tc::mbar_init(&kv_full[i], 2 * kTcLoaders + 1);   // + the TMA issuer's (expect-tx) arrival
-      tc::mbar_init(&kv_empty[i], 1);
+      tc::mbar_init(&kv_empty[i], NQ);   // one release per query tile's issuer
     }
     for (int t = 0; t < NQ; ++t) {
       tc::mbar_init(&s_full[t], 1);
@@ -1480,30 +1483,32 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
       tc::mbar_arrive_cp_async(&kv_full[st]);   // when this thread's copies land
       tc::mbar_arrive(&kv_full[st]);            // releases its plain zero stores
     }
-  } else if (warp == RL::MMA_WARP) {
-    // ------------------------------------------------ MMA issuer
+  } else if (warp >= RL::MMA_WARP0) {
+    // ------------------------------------------------ MMA issuer of query tile t
+    const int t = warp - RL::MMA_WARP0;
     if ((tid & 31) == 0) {
       constexpr uint32_t idesc_s = tc::f16_idesc(kTcRows, TS, 0, 0);
       constexpr uint32_t idesc_o = tc::f16_idesc(kTcRows, D, 0, 1);
+      const int Uq = Ut[t];
+      const uint32_t qa = base_s + S::OFF_Q + t * S::Q1_BYTES;
       bool ok = tc::mbar_wait(&q_full, 0, kTcWaitBudget);
       for (int u = 0; ok && u <= U; ++u) {
         if (u < U) {
+          // Every unit's arrival is awaited (also past this tile's range) so that this issuer's
+          // releases of a stage stay in the stage's phase order.
           const int st = u % ST;
           ok = tc::mbar_wait(&kv_full[st], (u / ST) & 1, kTcWaitBudget);
           if (!ok) break;
-          tc::fence_proxy_async();
-          tc::fence_after();
-          const uint32_t kbs = base_s + S::OFF_K + st * S::KV_BYTES;
-#pragma unroll
-          for (int t = 0; t < NQ; ++t) {
-            if (u >= Ut[t]) continue;   // tile t's causal range ends before unit u
+          if (u < Uq) {
+            tc::fence_proxy_async();
+            tc::fence_after();
             // S(t) is free once the softmax has loaded S(t, u-1) into registers.
             if (u >= 1 && !tc::mbar_wait(&s_free[t], (u - 1) & 1, kTcWaitBudget)) {
               ok = false;
               break;
             }
             tc::fence_after();
-            const uint32_t qa = base_s + S::OFF_Q + t * S::Q1_BYTES;
+            const uint32_t kbs = base_s + S::OFF_K + st * S::KV_BYTES;
 #pragma unroll
             for (int ks = 0; ks < D / 16; ++ks) {
               const uint64_t da = tc::sw128_desc(qa + (ks >> 2) * (kTcRows * 128) + (ks & 3) * 32, 16, 1024);
@@ -1512,25 +1517,24 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
             }
             tc::umma_commit(&s_full[t]);
           }
-          if (!ok) break;
         }
         if (u >= 1) {
           const int v = u - 1, bp = v & 1, vs = v % ST;
-          const uint32_t vbs = base_s + S::OFF_V + vs * S::KV_BYTES;
-          for (int t = 0; t < NQ; ++t) {
-            if (v >= Ut[t]) continue;
+          if (v < Uq) {
             ok = tc::mbar_wait(&p_full[t][bp], (v >> 1) & 1, kTcWaitBudget);
             if (!ok) break;
             tc::fence_after();
+            const uint32_t vbs = base_s + S::OFF_V + vs * S::KV_BYTES;
 #pragma unroll
             for (int ks = 0; ks < TS / 16; ++ks) {
               const uint64_t db = tc::sw128_desc(vbs + ks * 16 * 128, TS * 128, 1024);
               tc::umma_f16_ts(t_o(t), t_p(t, bp) + ks * 8, db, idesc_o, (v > 0 || ks > 0) ? 1u : 0u);
             }
             tc::umma_commit(&pv_done[t][bp]);
+            tc::umma_commit(&kv_empty[vs]);
+          } else {
+            tc::mbar_arrive(&kv_empty[vs]);   // unit v lies past this tile's causal range
           }
-          if (!ok) break;
-          tc::umma_commit(&kv_empty[vs]);
         }
       }
       if (!ok) fail();
