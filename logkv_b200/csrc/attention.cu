@@ -1321,7 +1321,7 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
     chunk_attn_tc_kernel(AttnGeo a, logkv_prefix_t pre, const __nv_bfloat16* rk, const __nv_bfloat16* rv,
                          const __nv_bfloat16* kn, const __nv_bfloat16* vn, const __nv_bfloat16* q,
                          __nv_bfloat16* out, int32_t* status, const __grid_constant__ TcMaps maps,
-                         int tma_mask) {
+                         int tma_mask, int nsplit, float* part) {
   using S = TcShape<D, NQ>;
   using RL = TcRoles<NQ>;
   constexpr int CPR = D / 8, TS = kTcTS, ST = RL::STAGES;
@@ -1335,13 +1335,15 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
   const uint32_t base_s = tc::smem_u32(base);
   const int g = blockIdx.y, b = blockIdx.z, ln = b * a.G + g;
   const int QT = kTcRows / a.rf;
+  // CTA x = split * npairs + pair: split `split` of the key range of query tile pair `pair`.
+  const int npairs = (int)gridDim.x / nsplit, pair = (int)blockIdx.x % npairs, split = (int)blockIdx.x / npairs;
   // Query tiles of this CTA.  With two tiles and an even tile count, CTA x takes tiles x and
   // ntiles - 1 - x, so every CTA sees the same number of causal chunk units in total (adjacent
   // tiles would leave the last CTA with the two longest); otherwise tiles NQ x .. NQ x + NQ - 1.
   const int ntiles = (a.TQ + QT - 1) / QT;
   const bool mirror = NQ == 2 && (ntiles & 1) == 0;
   auto tq_of = [&](int t) {
-    const int tile = mirror ? (t == 0 ? (int)blockIdx.x : ntiles - 1 - (int)blockIdx.x) : (int)blockIdx.x * NQ + t;
+    const int tile = mirror ? (t == 0 ? pair : ntiles - 1 - pair) : pair * NQ + t;
     return a.qoff + tile * QT;
   };
   const __nv_bfloat16* PK = static_cast<const __nv_bfloat16*>(pre.k);
@@ -1361,7 +1363,11 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
   }
   const int Tvis = a.causal ? min(a.T, tlast + 1) : a.T;
   const int uc = (Tvis + TS - 1) / TS;
-  const int U = up + ur + uc;
+  // This split's units [ub, U) of the CTA's range; a tile's own units end at min(Ut[t], U).
+  const int Uall = up + ur + uc;
+  const int ub = (int)((long long)Uall * split / nsplit), U = (int)((long long)Uall * (split + 1) / nsplit);
+#pragma unroll
+  for (int t = 0; t < NQ; ++t) Ut[t] = max(min(Ut[t], U), ub);
 
   if (tid == 0) {
     tc::mbar_init(&q_full, 2 * kTcLoaders);
@@ -1439,9 +1445,9 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
     }
     tc::mbar_arrive_cp_async(&q_full);
     tc::mbar_arrive(&q_full);
-    for (int u = 0; u < U; ++u) {
-      const int st = u % ST;
-      if (u >= ST && !tc::mbar_wait(&kv_empty[st], ((u - ST) / ST) & 1, kTcWaitBudget)) {
+    for (int u = ub; u < U; ++u) {
+      const int r = u - ub, st = r % ST;
+      if (r >= ST && !tc::mbar_wait(&kv_empty[st], ((r - ST) / ST) & 1, kTcWaitBudget)) {
         fail();
         break;
       }
@@ -1492,18 +1498,19 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
       const int Uq = Ut[t];
       const uint32_t qa = base_s + S::OFF_Q + t * S::Q1_BYTES;
       bool ok = tc::mbar_wait(&q_full, 0, kTcWaitBudget);
-      for (int u = 0; ok && u <= U; ++u) {
+      for (int u = ub; ok && u <= U; ++u) {
+        const int r = u - ub;
         if (u < U) {
           // Every unit's arrival is awaited (also past this tile's range) so that this issuer's
           // releases of a stage stay in the stage's phase order.
-          const int st = u % ST;
-          ok = tc::mbar_wait(&kv_full[st], (u / ST) & 1, kTcWaitBudget);
+          const int st = r % ST;
+          ok = tc::mbar_wait(&kv_full[st], (r / ST) & 1, kTcWaitBudget);
           if (!ok) break;
           if (u < Uq) {
             tc::fence_proxy_async();
             tc::fence_after();
             // S(t) is free once the softmax has loaded S(t, u-1) into registers.
-            if (u >= 1 && !tc::mbar_wait(&s_free[t], (u - 1) & 1, kTcWaitBudget)) {
+            if (r >= 1 && !tc::mbar_wait(&s_free[t], (r - 1) & 1, kTcWaitBudget)) {
               ok = false;
               break;
             }
@@ -1518,17 +1525,17 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
             tc::umma_commit(&s_full[t]);
           }
         }
-        if (u >= 1) {
-          const int v = u - 1, bp = v & 1, vs = v % ST;
+        if (r >= 1) {
+          const int v = u - 1, rv_ = r - 1, bp = rv_ & 1, vs = rv_ % ST;
           if (v < Uq) {
-            ok = tc::mbar_wait(&p_full[t][bp], (v >> 1) & 1, kTcWaitBudget);
+            ok = tc::mbar_wait(&p_full[t][bp], (rv_ >> 1) & 1, kTcWaitBudget);
             if (!ok) break;
             tc::fence_after();
             const uint32_t vbs = base_s + S::OFF_V + vs * S::KV_BYTES;
 #pragma unroll
             for (int ks = 0; ks < TS / 16; ++ks) {
               const uint64_t db = tc::sw128_desc(vbs + ks * 16 * 128, TS * 128, 1024);
-              tc::umma_f16_ts(t_o(t), t_p(t, bp) + ks * 8, db, idesc_o, (v > 0 || ks > 0) ? 1u : 0u);
+              tc::umma_f16_ts(t_o(t), t_p(t, bp) + ks * 8, db, idesc_o, (rv_ > 0 || ks > 0) ? 1u : 0u);
             }
             tc::umma_commit(&pv_done[t][bp]);
             tc::umma_commit(&kv_empty[vs]);
@@ -1545,13 +1552,13 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
     const int row = tid - qt * kTcRows;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const int row_t = tq_of(qt) + (row % QT);
-    const int Uq = Ut[qt];
+    const int Uq = Ut[qt], nq_ = Uq - ub;   // this tile's units of the split: [ub, Uq)
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int u = 0; u < Uq; ++u) {
-      const int st = u & 1, ks_ = u % ST;
-      ok = __all_sync(0xffffffffu, tc::mbar_wait(&kv_full[ks_], (u / ST) & 1, kTcWaitBudget) &&
-                                       tc::mbar_wait(&s_full[qt], u & 1, kTcWaitBudget));
+    for (int u = ub; u < Uq; ++u) {
+      const int r = u - ub, st = r & 1, ks_ = r % ST;
+      ok = __all_sync(0xffffffffu, tc::mbar_wait(&kv_full[ks_], (r / ST) & 1, kTcWaitBudget) &&
+                                       tc::mbar_wait(&s_full[qt], r & 1, kTcWaitBudget));
       if (!ok) break;
       tc::fence_after();
       const __nv_bfloat16 *kb_, *vb_;
@@ -1608,15 +1615,15 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
       tc::f2unpack(ps2, ps0, ps1);
       const float ps = ps0 + ps1;
       l = l * alpha + ps;
-      if (u >= 2) {
+      if (r >= 2) {
         // P buffer st still feeds PV(u-2) until that product completes.
-        ok = __all_sync(0xffffffffu, tc::mbar_wait(&pv_done[qt][st], ((u - 2) >> 1) & 1, kTcWaitBudget));
+        ok = __all_sync(0xffffffffu, tc::mbar_wait(&pv_done[qt][st], ((r - 2) >> 1) & 1, kTcWaitBudget));
         if (!ok) break;
       }
-      if (u > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+      if (r > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
         // O must hold PV(u-1) before it is rescaled.
         ok = __all_sync(0xffffffffu,
-                        tc::mbar_wait(&pv_done[qt][(u - 1) & 1], ((u - 1) >> 1) & 1, kTcWaitBudget));
+                        tc::mbar_wait(&pv_done[qt][(r - 1) & 1], ((r - 1) >> 1) & 1, kTcWaitBudget));
         if (!ok) break;
         tc::fence_after();
 #pragma unroll 1
@@ -1632,12 +1639,43 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
       tc::fence_before();
       tc::mbar_arrive(&p_full[qt][st]);
     }
-    if (ok && Uq > 0)
+    if (ok && nq_ > 0)
       ok = __all_sync(0xffffffffu,
-                      tc::mbar_wait(&pv_done[qt][(Uq - 1) & 1], ((Uq - 1) >> 1) & 1, kTcWaitBudget));
+                      tc::mbar_wait(&pv_done[qt][(nq_ - 1) & 1], ((nq_ - 1) >> 1) & 1, kTcWaitBudget));
     if (!ok) {
       if ((tid & 31) == 0) fail();
-    } else if (Uq > 0) {
+    } else if (nsplit > 1) {
+      // Split partial [m, l, -, -, O[D]] of this row (O unnormalised, relative to 2^m; a tile
+      // without units in this split writes m = -inf, l = 0, O = 0) for chunk_combine_kernel.
+      // The tensor-memory loads are warp-wide: every lane issues them, rows past the chunk (a
+      // partial last tile) only skip the stores.
+      tc::fence_after();
+      const int hh = row / QT;
+      const bool in = row_t < a.qoff + a.TQ;
+      const size_t prow = ((size_t)b * a.H + g * a.rf + hh) * a.TQ + (in ? row_t - a.qoff : 0);
+      float* pp = part + ((size_t)split * a.B * a.H * a.TQ + prow) * (D + 4);
+      if (in) {
+        pp[0] = m_used;
+        pp[1] = l;
+      }
+#pragma unroll 1
+      for (int c0 = 0; c0 < D; c0 += 32) {
+        uint32_t r32[32];
+        if (nq_ > 0) {   // uniform over the warpgroup (one query tile)
+          tc::tmem_ld32(t_o(qt) + lane_off + c0, r32);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r32[j] = 0u;
+        }
+        if (in) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(pp + 4 + c0 + j) =
+                make_float4(__uint_as_float(r32[j]), __uint_as_float(r32[j + 1]), __uint_as_float(r32[j + 2]),
+                            __uint_as_float(r32[j + 3]));
+        }
+      }
+    } else if (nq_ > 0) {
       tc::fence_after();
       const int hh = row / QT;
       const bool in = row_t < a.qoff + a.TQ;
@@ -1813,6 +1851,7 @@ static bool use_chunk_kernel(const logkv_layout_t& l, int heads, int q_tokens) {
          (rf == 1 || rf == 2 || rf == 4 || rf == 8);
 }
 
+
 template <int D>
 static int launch_chunk_d(const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
                           const logkv_attention_args_t& x, cudaStream_t st) {
@@ -1857,9 +1896,57 @@ static bool encode_rows_map(CUtensorMap* m, const void* base, size_t rows, int D
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Combine of the chunk kernel's key-range splits: one warp per output row (b, h, token), the
+// partials [m, l, -, -, O[D]] weighted by 2^(m_s - max m) in split order.
+template <int D>
+__global__ void __launch_bounds__(256) chunk_combine_kernel(AttnGeo a, const float* part, int nsplit,
+                                                            __nv_bfloat16* out) {
+  constexpr int PER = D / 32;
+  const int lane = threadIdx.x & 31;
+  const size_t rows = (size_t)a.B * a.H * a.TQ;
+  const size_t row = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const size_t stride = rows * (D + 4);
+  const float* p0 = part + row * (D + 4);
+  float mx = -INFINITY;
+  for (int sp = 0; sp < nsplit; ++sp) mx = fmaxf(mx, p0[sp * stride]);
+  float L = 0.f, o[PER];
+#pragma unroll
+  for (int k = 0; k < PER; ++k) o[k] = 0.f;
+  for (int sp = 0; sp < nsplit; ++sp) {
+    const float* pp = p0 + sp * stride;
+    const float m = pp[0];
+    const float w = (m == -INFINITY || mx == -INFINITY) ? 0.f : exp2f(m - mx);
+    L += pp[1] * w;
+#pragma unroll
+    for (int k = 0; k < PER; ++k) o[k] += pp[4 + lane + 32 * k] * w;
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  const size_t bh = row / a.TQ;
+  const int t = (int)(row % a.TQ);
+  __nv_bfloat16* orow = out + (bh * a.QS + a.qoff + t) * D;
+#pragma unroll
+  for (int k = 0; k < PER; ++k) orow[lane + 32 * k] = __float2bfloat16_rn(o[k] * inv);
+}
+
+// Key-range splits of the chunk kernel: enough CTAs (query tile pairs x splits) to fill the SMs
+// when the chunk has few heads (a KV-head-sharded rank's share), at least 16 64-slot units per
+// split, at most 8.
+static int chunk_tc_nq(int tiles) { return tiles >= 2 ? 2 : 1; }
+static int chunk_tc_splits(int B, int G, int tiles, int units) {
+  const int ctas = (tiles + chunk_tc_nq(tiles) - 1) / chunk_tc_nq(tiles) * G * B;
+  int n = std::max(1, 148 / std::max(1, ctas));
+  n = std::min(n, std::max(1, units / 16));
+  return std::max(1, std::min(n, 8));
+}
+static size_t chunk_part_bytes(int B, int H, int TQ, int D, int nsplit) {
+  return nsplit > 1 ? (size_t)nsplit * B * H * TQ * (D + 4) * sizeof(float) : 0;
+}
+
 template <int D, int NQ>
 static int launch_chunk_tc(const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
-                           const logkv_attention_args_t& x, int32_t* status, cudaStream_t st) {
+                           const logkv_attention_args_t& x, int32_t* status, int nsplit, float* part,
+                           cudaStream_t st) {
   using S = TcShape<D, NQ>;
   auto kern = chunk_attn_tc_kernel<D, NQ>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::smem);
@@ -1878,31 +1965,48 @@ static int launch_chunk_tc(const AttnGeo& ag, const logkv_prefix_t& pre, const l
     mask |= 2;
   if (encode_rows_map(&maps.k[2], x.k_new, lanes * ag.T, D) && encode_rows_map(&maps.v[2], x.v_new, lanes * ag.T, D))
     mask |= 4;
-  kern<<<dim3((tiles + NQ - 1) / NQ, ag.G, ag.B), TcRoles<NQ>::WARPS * 32, S::smem, st>>>(
+  kern<<<dim3((tiles + NQ - 1) / NQ * nsplit, ag.G, ag.B), TcRoles<NQ>::WARPS * 32, S::smem, st>>>(
       ag, pre, static_cast<const B16*>(s.recent_k), static_cast<const B16*>(s.recent_v),
       static_cast<const B16*>(x.k_new), static_cast<const B16*>(x.v_new), static_cast<const B16*>(x.q),
-      static_cast<B16*>(x.out), status, maps, mask);
+      static_cast<B16*>(x.out), status, maps, mask, nsplit, part);
+  if (nsplit > 1) {
+    const size_t rows = (size_t)ag.B * ag.H * ag.TQ;
+    chunk_combine_kernel<D><<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(ag, part, nsplit, static_cast<B16*>(x.out));
+  }
   return launch_status();
 }
 
-// Two query tiles per CTA once there are enough tiles to give every SM a pair.
+// Two query tiles per CTA (a ping-pong pair) whenever there are two; the key range split
+// over CTAs when the pairs alone do not fill the SMs (chunk_tc_splits).
 template <int D>
 static int launch_chunk_tc_auto(const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
-                                const logkv_attention_args_t& x, int32_t* status, cudaStream_t st) {
+                                const logkv_attention_args_t& x, int32_t* status, int nsplit, float* part,
+                                cudaStream_t st) {
   const int QT = kTcRows / ag.rf;
   const int tiles = (ag.TQ + QT - 1) / QT;
-  if ((size_t)tiles * ag.G * ag.B >= 148) return launch_chunk_tc<D, 2>(ag, pre, s, x, status, st);
-  return launch_chunk_tc<D, 1>(ag, pre, s, x, status, st);
+  if (chunk_tc_nq(tiles) == 2) return launch_chunk_tc<D, 2>(ag, pre, s, x, status, nsplit, part, st);
+  return launch_chunk_tc<D, 1>(ag, pre, s, x, status, nsplit, part, st);
+}
+
+// Key-range splits of the tcgen05 chunk kernel for this call shape (1 for the mma.sync one);
+// the unit estimate uses the prefix capacity, since the actual length is on the device.
+static int chunk_splits_for(const logkv_layout_t& l, int heads, int q_tokens, int prefix_capacity) {
+  if (l.dim != 64 && l.dim != 128) return 1;
+  const int rf = heads / l.groups, QT = kTcRows / rf;
+  const int tiles = (q_tokens + QT - 1) / QT;
+  const int units = (prefix_capacity + l.recent_capacity + q_tokens) / kTcTS;
+  return chunk_tc_splits(l.batch, l.groups, tiles, units);
 }
 
 // Head dims 64 and 128 run on tcgen05 (tensor memory accumulators); 16 and 32 on mma.sync.
 static int launch_chunk(int D, const AttnGeo& ag, const logkv_prefix_t& pre, const logkv_state_t& s,
-                        const logkv_attention_args_t& x, int32_t* status, cudaStream_t st) {
+                        const logkv_attention_args_t& x, int32_t* status, int nsplit, float* part,
+                        cudaStream_t st) {
   switch (D) {
     case 16: return launch_chunk_d<16>(ag, pre, s, x, st);
     case 32: return launch_chunk_d<32>(ag, pre, s, x, st);
-    case 64: return launch_chunk_tc_auto<64>(ag, pre, s, x, status, st);
-    case 128: return launch_chunk_tc_auto<128>(ag, pre, s, x, status, st);
+    case 64: return launch_chunk_tc_auto<64>(ag, pre, s, x, status, nsplit, part, st);
+    case 128: return launch_chunk_tc_auto<128>(ag, pre, s, x, status, nsplit, part, st);
     default: return LOGKV_E_SHAPE;
   }
 }
@@ -2021,7 +2125,9 @@ LOGKV_API int logkv_pack_mid(const logkv_layout_t* layout, const logkv_state_t* 
 LOGKV_API size_t logkv_attention_workspace_bytes(const logkv_layout_t* layout, int32_t heads, int32_t q_tokens,
                                                  int32_t prefix_capacity) {
   if (check_layout(layout) || heads < layout->groups || heads % layout->groups || q_tokens < 1) return 0;
-  if (use_chunk_kernel(*layout, heads, q_tokens)) return 256;
+  if (use_chunk_kernel(*layout, heads, q_tokens))
+    return 256 + chunk_part_bytes(layout->batch, heads, q_tokens, layout->dim,
+                                  chunk_splits_for(*layout, heads, q_tokens, prefix_capacity));
   const int nq = heads / layout->groups * q_tokens;
   const int nsplit = attn_splits(*layout, prefix_capacity);
   const size_t lanes = (size_t)layout->batch * layout->groups;
@@ -2070,8 +2176,11 @@ LOGKV_API int logkv_attention(const logkv_layout_t* layout, const logkv_state_t*
   ag.scale_log2 = args->scale * 1.4426950408889634f;
   ag.qx = args->qx;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (use_chunk_kernel(*layout, H, TQ))
-    return launch_chunk(layout->dim, ag, *prefix, *state, *args, static_cast<int32_t*>(workspace), st);
+  if (use_chunk_kernel(*layout, H, TQ)) {
+    const int ns = chunk_splits_for(*layout, H, TQ, prefix->capacity);
+    float* cpart = reinterpret_cast<float*>(static_cast<char*>(workspace) + 256);
+    return launch_chunk(layout->dim, ag, *prefix, *state, *args, static_cast<int32_t*>(workspace), ns, cpart, st);
+  }
   return launch_attn(layout->dtype, layout->dim, nq, ag, *prefix, *state, *args, part, ticket, st);
 }
 

@@ -87,11 +87,14 @@ def test_d128_attention_matches_oracle(T):
         assert int(ws[:4].view(torch.int32).item()) == 0
 
 
-def test_two_tile_chunk_kernel_matches_fp32_reference():
-    """A 2048-token chunk over 8 groups (256 query tiles: the two-tile tcgen05 kernel) against
-    a PyTorch float32 softmax over the same packed K/V (the oracle's packer)."""
+@pytest.mark.parametrize("G", [8, 4, 2])
+def test_two_tile_chunk_kernel_matches_fp32_reference(G):
+    """A 2048-token chunk (the two-tile tcgen05 kernel) against a PyTorch float32 softmax over
+    the same packed K/V (the oracle's packer): 8 groups (128 query-tile pairs, one CTA each), and
+    4 or 2 groups (a KV-head-sharded rank's share: the key range is split over 2 or 4 CTAs per
+    pair and the splits combined)."""
     from logkv_b200 import log_kv_chunk_attention
-    G, H, T, D = 8, 16, 2048, 128
+    H, T, D = 2 * G, 2048, 128
     cache, cos, sin = make_state(seed=7, G=G, recent=512, R=300, max_seq=8192)
     gen = torch.Generator(device="cuda").manual_seed(77)
     q = torch.randn(1, H, T, D, generator=gen, device="cuda").bfloat16()
