@@ -13,6 +13,8 @@ no segments, and restates its commit path:
   ordinary joins         _semantic_commit_joins_unsegmented :4116-4175, _semantic_apply_join_plan :4225-4361
   late (delayed) joins   _alpha_commit_joins :3690-3788
   ladder append          oracle.ladder (== _semantic_append_entries_batched :1756-1929)
+  unified route          _semantic_route_unified :3589-3688 (oracle.unified), Ward merges of old
+                         clusters _semantic_ward_merge_batch :2517-2593
 
 Storage-dtype values are float32 arrays holding exact bf16 values when the
 cache dtype is bf16.
@@ -26,6 +28,7 @@ import numpy as np
 from . import alpha as A
 from .attach import attach_decide
 from .ladder import Ladder, Rows
+from . import unified as U
 from .numerics import F32, seq_sum, to_storage
 
 
@@ -48,8 +51,9 @@ def ladder_geometry(batch, groups, max_seq, dk, dv, B, clusters, exact, element_
 
 class OracleCache:
     def __init__(self, *, batch, groups, max_seq, dim, B, recent, clusters, granularity, exact, span_cap,
-                 beta, dtype="fp32", s_h=None, eta=1.0, g0=2048.0, lam=1.0):
+                 beta, dtype="fp32", s_h=None, eta=1.0, g0=2048.0, lam=1.0, unified=False, merge_passes=1):
         self.batch, self.groups, self.dim, self.K = batch, groups, dim, clusters
+        self.unified, self.merge_passes = bool(unified), int(merge_passes)
         self.dtype = dtype
         self.max_seq = max_seq
         self.recent_size, self.granularity = recent, granularity
@@ -169,7 +173,10 @@ class OracleCache:
             ap[b, :n] = pos[b, arch]
         if not counts.any():
             return
-        self.route_attach(ak, av, ap, counts)
+        if self.unified:
+            self.route_unified(ak, av, ap, counts)
+        else:
+            self.route_attach(ak, av, ap, counts)
 
     # ------------------------------------------------------------------ route
     def route_attach(self, ak, av, ap, counts):
@@ -192,6 +199,11 @@ class OracleCache:
                         toks = toks[1:]
                     if len(toks):
                         jobs.append((b, g, c, [int(t) for t in toks]))
+        self._commit(new_jobs, jobs, ak, av, ap)
+
+    def _commit(self, new_jobs, jobs, ak, av, ap):
+        """New clusters, then joins by (b, g, cluster), delayed when a token precedes p_hi
+        (_semantic_new_clusters :2268-2298, _alpha_commit_joins :3690-3788)."""
         for b, g, c, t in new_jobs:
             self._new_cluster(b, g, c, ak[b, g, t], av[b, g, t], int(ap[b, t]))
         for b, g, c, toks in sorted(jobs, key=lambda j: j[:3]):
@@ -200,6 +212,108 @@ class OracleCache:
                 self._late_join(b, g, c, ak[b, g, toks], av[b, g, toks], tpos)
             else:
                 self._join(b, g, c, ak[b, g, toks], av[b, g, toks], tpos)
+
+    def route_unified(self, ak, av, ap, counts):
+        """_semantic_route_unified (log_kv_cache.py:3589-3688): per lane a radius-limited candidate
+        pass over the flushed tokens, then a global pass over [live centroids, candidates] down to
+        K clusters; merges of two old clusters rebuild the keep cluster's ladder (Ward merges, in
+        trace order), candidates joined to an old root join that cluster, the others open new
+        clusters in the free slots."""
+        B, G, D, K = self.batch, self.groups, self.dim, self.K
+        lanes = [(b, g) for b in range(B) for g in range(G) if counts[b]]
+        if not lanes:
+            return
+        tile = U.route_tile(len(lanes), int(max(counts)))
+        position_order = [np.argsort(ap[b, :counts[b]], kind="stable") for b in range(B)]
+        routes, merge_jobs, decisions = [], [], {}
+        for start in range(0, len(lanes), tile):
+            part = lanes[start:start + tile]
+            ccounts = [int(counts[b]) for b, _ in part]
+            tokens = max(ccounts)
+            mu = np.zeros((len(part), tokens, D), F32)
+            for i, (b, g) in enumerate(part):
+                mu[i, :ccounts[i]] = ak[b, g, :ccounts[i]].astype(F32)
+            cweights = (np.arange(tokens)[None, :] < np.asarray(ccounts)[:, None]).astype(F32)
+            limits = [float(np.float32(math.sqrt(self.lam * float(self.s_h[b, g])))) for b, g in part]
+            candidates, ctraces = U.reduce_lanes(mu, ccounts, cweights, target=1, radius_limits=limits)
+            live = [np.flatnonzero(self.alive[b, g]).astype(np.int64) for b, g in part]
+            labels = U.labels_batch(ccounts, candidates, ctraces)
+            weights = [np.concatenate((self.n_total[b, g, old].astype(F32),
+                                       np.bincount(lab, minlength=len(roots)).astype(F32)))
+                       for (b, g), old, roots, lab in zip(part, live, candidates, labels)]
+            gcounts = [len(w) for w in weights]
+            size = max(gcounts)
+            centers = np.zeros((len(part), size, D), F32)
+            padded = np.zeros((len(part), size), F32)
+            for i, ((b, g), old, roots) in enumerate(zip(part, live, candidates)):
+                centers[i, :len(old)] = self.centroid[b, g, old]
+                centers[i, len(old):gcounts[i]] = mu[i, roots]
+                padded[i, :gcounts[i]] = weights[i]
+            groots, gtraces = U.reduce_lanes(centers, gcounts, padded, target=K, strict=True,
+                                             passes=self.merge_passes)
+            merged = U.labels_batch(gcounts, groots, gtraces)
+            for (b, g), old, clab, roots, trace, lab in zip(part, live, labels, groots, gtraces, merged):
+                old_trace = trace[trace[:, 1] < len(old)] if len(trace) else trace
+                merge_jobs.append((b, g, [tuple(int(x) for x in pair) for pair in old[old_trace]]))
+                routes.append((b, g, old, lab[len(old) + clab], roots))
+                decisions[(b, g)] = dict(candidates=len(candidates[part.index((b, g))]), ctrace=ctraces[
+                    part.index((b, g))], gtrace=trace, assign=lab[len(old) + clab])
+        self.trace[-1].update(unified=decisions)
+        for step in range(max((len(p) for _, _, p in merge_jobs), default=0)):
+            for b, g, pairs in merge_jobs:
+                if step < len(pairs):
+                    self._ward_merge(b, g, *pairs[step])
+        new_jobs, jobs = [], []
+        for b, g, old, assignment, roots in routes:
+            free = iter(np.flatnonzero(~self.alive[b, g]).tolist())
+            order = position_order[b]
+            by_cluster = assignment[order]
+            perm = np.argsort(by_cluster, kind="stable")
+            grouped = order[perm]
+            bounds = np.searchsorted(by_cluster[perm], np.arange(len(roots) + 1))
+            for cluster, root in enumerate(roots):
+                offsets = grouped[bounds[cluster]:bounds[cluster + 1]]
+                if not len(offsets):
+                    continue
+                if root < len(old):
+                    target = int(old[root])
+                else:
+                    target = next(free)
+                    new_jobs.append((b, g, target, int(offsets[0])))
+                    offsets = offsets[1:]
+                if len(offsets):
+                    jobs.append((b, g, target, [int(t) for t in offsets]))
+        self._commit(new_jobs, jobs, ak, av, ap)
+
+    def _ward_merge(self, b, g, keep, free):
+        """One Ward merge of two old clusters (_semantic_ward_merge_batch :2517-2593): the keep
+        and free entries in ward_entry_index order are re-appended to the cleared keep cluster
+        with orders 0..n-1; centroid the count-weighted mean."""
+        ek, ef = self.ladder.entries(b, g, keep), self.ladder.entries(b, g, free)
+        rows = Rows.cat(ek, ef)
+        idx = U.ward_entry_index(rows.order, rows.lo, rows.w > 0, len(ek))
+        rows = rows.take(idx)
+        rows.order = np.arange(len(rows), dtype=np.int64)
+        nk, nf = F32(self.n_total[b, g, keep]), F32(self.n_total[b, g, free])
+        mu = ((((nk * self.centroid[b, g, keep]).astype(F32) + (nf * self.centroid[b, g, free]).astype(F32))
+               .astype(F32)) / max(F32(nk + nf), F32(1))).astype(F32)
+        ne = F32(self.n_eff[b, g, keep] + self.n_eff[b, g, free])
+        total = int(self.n_total[b, g, keep] + self.n_total[b, g, free])
+        hi = max(int(self.p_hi_c[b, g, keep]), int(self.p_hi_c[b, g, free]))
+        for c in (keep, free):
+            self.ladder.clear_lane(b, g, c)
+            self.alive[b, g, c] = False
+            self.n_total[b, g, c] = 0
+            self.p_hi_c[b, g, c] = -1
+            self.level0_phase[b, g, c] = 0
+        self.centroid[b, g, keep] = mu
+        self.n_eff[b, g, keep] = ne
+        self.n_eff[b, g, free] = 0
+        self.alive[b, g, keep] = True
+        self.n_total[b, g, keep] = total
+        self.p_hi_c[b, g, keep] = hi
+        self.level0_phase[b, g, keep] = len(rows)
+        self.ladder.append(b, g, keep, rows, self.beta)
 
     def _new_cluster(self, b, g, c, k, v, pos):
         self.ladder.clear_lane(b, g, c)

@@ -6,7 +6,16 @@ distances / mirror of ``log_kv_route_triton.py:546-607``.  Every operation is fl
 rounded as the reference writes it (one rounding per product, quotient, sum); the one sum over
 features (the exact squared distance of a candidate pair, ``(diff * diff).sum(-1)`` in the
 reference, whose order torch leaves to its vectorised CPU kernel) runs left to right here, and
-the CUDA operators use the same order.  Frozen-centre sweeps (``passes > 1``) are not restated.
+the CUDA operators use the same order.
+
+Flush level (``_semantic_route_unified``, log_kv_cache.py:3589-3688): ``pair_matrix``
+(``_semantic_unified_pair_matrix`` :3185-3221, its two forms), ``reduce_lanes``
+(``_semantic_unified_reduce_device`` :3246-3299 with the host loop of
+``_semantic_unified_reduce_incremental`` :3301-3376), ``labels_batch``
+(``_semantic_unified_labels_batch`` :3544-3568), ``route_tile`` (``_semantic_unified_tile``
+:3578-3587) and ``ward_entry_index`` (``_semantic_ward_entry_index`` :2450-2474).  The Gram
+products and the exact-difference sums of the pair matrix run left to right over the features
+(the reference leaves that order to its BLAS / vectorised CPU kernels).
 """
 from __future__ import annotations
 
@@ -72,7 +81,8 @@ class UnifiedReduce:
     stuck [L]).  Arrays are updated in place.
     """
 
-    def __init__(self, dist, mu, mass, count, limits, target):
+    def __init__(self, dist, mu, mass, count, limits, target, passes=1):
+        self.passes = max(1, int(passes))
         self.dist = np.array(dist, F32)
         self.mu = np.array(mu, F32)
         self.mass = np.array(mass, F32)
@@ -91,11 +101,38 @@ class UnifiedReduce:
             for row in np.flatnonzero(self.alive[lane]):
                 self.packed[lane, row] = self._scan(lane, row)
 
-    def _scan(self, lane, row):
+    def _scan(self, lane, row, excluded=None):
         lim = None if self.limits is None else self.limits[lane]
-        cost, _ = pair_cost(self.dist[lane, row], self.mass[lane, row], self.mass[lane], self.radius[lane, row],
+        mass = self.mass[lane] if excluded is None else np.where(excluded, F32(0), self.mass[lane]).astype(F32)
+        cost, _ = pair_cost(self.dist[lane, row], self.mass[lane, row], mass, self.radius[lane, row],
                             self.radius[lane], lim, self.ids != row)
         return pack(cost, np.int64(row) ^ self.ids).min()
+
+    def _sweeps(self, lane, valid, best, pair_c):
+        """Frozen-centre sweeps of one lane (``_UnifiedReduceTorch._sweeps``, :564-588)."""
+        M, ids = self.M, self.ids
+        alive = self.alive[lane]
+        matched = np.zeros(M, bool)
+        rows = np.flatnonzero(valid)
+        matched[rows] = True
+        matched[best[rows]] = True
+        restricted = self.packed[lane].copy()
+        mate, extra = best.copy(), 0
+        for _ in range(self.passes - 1):
+            partner = np.clip((restricted & np.int64(0xFFFFFFFF)) ^ ids, 0, M - 1)
+            for row in np.flatnonzero(alive & ~matched & matched[partner]):
+                restricted[row] = self._scan(lane, row, excluded=matched)
+            partner = np.clip((restricted & np.int64(0xFFFFFFFF)) ^ ids, 0, M - 1)
+            cost = (restricted >> np.int64(32)).astype(np.int32).view(np.float32)
+            more = (alive & ~matched & (ids < partner) & (partner[partner] == ids) & (cost < np.inf)
+                    & ~matched[partner])
+            extra += int(more.sum())
+            rows = np.flatnonzero(more)
+            matched[rows] = True
+            matched[partner[rows]] = True
+            mate = np.where(more, partner, mate)
+            pair_c = np.where(more, cost, pair_c).astype(F32)
+        return mate, pair_c, extra
 
     def step(self):
         M, ids = self.M, self.ids
@@ -126,11 +163,15 @@ class UnifiedReduce:
                         valid[row] = False
                     bound[row] = verified
             pair_c = np.where(valid, cost, F32(np.inf)).astype(F32)
+            mate = best
+            if self.passes > 1:
+                mate, pair_c, extra = self._sweeps(lane, valid, best, pair_c)
+                nprop += extra
             order = np.argsort(pair_c, kind="stable")[:M // 2]
             ok = pair_c[order] < np.inf
             ok &= np.cumsum(ok) <= (self.count[lane] - self.target)
             a = order[ok]
-            b = best[a]
+            b = mate[a]
             keep = np.zeros(M, bool)
             merged = np.zeros(M, bool)
             if len(a):
@@ -206,3 +247,124 @@ class UnifiedReduce:
     def finish(self):
         traces = [np.asarray(t, np.int64).reshape(-1, 2) for t in self.traces]
         return traces, self.alive.copy(), self.stuck.copy()
+
+
+# ------------------------------------------------------------------------------ flush level
+ROUTE_TILE_BYTES = 64 << 20   # the CPU reference's distance budget per lane tile (log_kv_cache.py:3575)
+
+
+def route_tile(lanes: int, tokens: int, budget: int = ROUTE_TILE_BYTES) -> int:
+    """Lanes per tile: the largest balanced tile whose [M, M] float32 matrices fit `budget`
+    (``_semantic_unified_tile``, log_kv_cache.py:3578-3587)."""
+    widest = max(1, budget // max(1, 4 * tokens * tokens))
+    tiles = -(-lanes // widest)
+    return max(1, -(-lanes // max(tiles, 1)))
+
+
+def _lr_sum(terms) -> np.ndarray:
+    """Left-to-right float32 sum over the last axis (one rounding per addition)."""
+    acc = np.zeros(terms.shape[:-1], F32)
+    for d in range(terms.shape[-1]):
+        acc = (acc + terms[..., d]).astype(F32)
+    return acc
+
+
+def pair_matrix(mu: np.ndarray) -> np.ndarray:
+    """Squared centre distances [L, M, M] (``_semantic_unified_pair_matrix``, :3185-3221).
+
+    M <= 32: exact differences, ``cdist(...).square()`` (the root rounded, then squared).
+    Otherwise centred on each lane's first row: norm n_i = sum_d c_id^2, Gram G_ij = sum_d
+    c_id c_jd, d_ij = max((n_i + n_j) - 2 G_ij, 0), upper triangle mirrored.
+    """
+    mu = np.asarray(mu, F32)
+    L, M, D = mu.shape
+    if M <= 32:
+        acc = np.zeros((L, M, M), F32)
+        for d in range(D):
+            diff = (mu[:, :, None, d] - mu[:, None, :, d]).astype(F32)
+            acc = (acc + (diff * diff).astype(F32)).astype(F32)
+        root = np.sqrt(acc).astype(F32)
+        return mirror((root * root).astype(F32))
+    c = (mu - mu[:, :1]).astype(F32)
+    norm = _lr_sum((c * c).astype(F32))
+    gram = np.zeros((L, M, M), F32)
+    for d in range(D):
+        gram = (gram + (c[:, :, None, d] * c[:, None, :, d]).astype(F32)).astype(F32)
+    return pair_distances(gram, norm)
+
+
+def reduce_lanes(mu, counts, weights, *, target, radius_limits=None, strict=False, passes=1):
+    """Mutual-nearest Ward rounds on a padded float32 [L, M, D] buffer, updated in place
+    (``_semantic_unified_reduce_device`` :3246-3299 and the round loop of
+    ``_semantic_unified_reduce_incremental`` :3301-3376).  Returns per-lane surviving rows
+    (ascending) and merge pairs (left, right) in round, then (cost, left) order."""
+    lanes = len(counts)
+    active = [i for i, n in enumerate(counts) if n > target]
+    survivors = [np.arange(n, dtype=np.int64) for n in counts]
+    traces = [np.empty((0, 2), np.int64) for _ in counts]
+    if not active:
+        return survivors, traces
+    if len(active) < lanes:
+        size = max(counts[i] for i in active)
+    else:
+        size = mu.shape[1]
+    sub = np.array(mu[active, :size], F32)
+    w = np.asarray(weights, F32)[active, :size]
+    limits = None if radius_limits is None else np.asarray([radius_limits[i] for i in active], F32)
+    # Frozen-centre sweeps only for the uncapped global pass (radius limits keep one sweep).
+    red = UnifiedReduce(pair_matrix(sub), sub, w, [counts[i] for i in active], limits, target,
+                        passes if radius_limits is None else 1)
+    last_round = 2 * size + 7
+    for _ in range(last_round):
+        if not red.step().any():
+            break
+    lane_traces, alive, stuck = red.finish()
+    if strict and stuck.any():
+        raise RuntimeError("unified routing has no finite merge cost to satisfy the cluster budget")
+    mu[active, :size] = red.mu
+    for j, i in enumerate(active):
+        survivors[i] = np.flatnonzero(alive[j]).astype(np.int64)
+        traces[i] = lane_traces[j]
+    return survivors, traces
+
+
+def labels_batch(sizes, survivors, traces):
+    """Leaf -> compact surviving row, by pointer jumping over the merge forest
+    (``_semantic_unified_labels_batch``, :3544-3568)."""
+    sizes = np.asarray(sizes, np.int64)
+    offsets = np.cumsum(sizes) - sizes
+    parent = np.arange(int(sizes.sum()), dtype=np.int64)
+    pairs = [np.asarray(t, np.int64) + off for t, off in zip(traces, offsets.tolist()) if len(t)]
+    if pairs:
+        pairs = np.concatenate(pairs)
+        parent[pairs[:, 1]] = pairs[:, 0]
+        while True:
+            grand = parent[parent]
+            if np.array_equal(parent, grand):
+                break
+            parent = grand
+    compact = np.empty(len(parent), np.int64)
+    compact[np.concatenate([np.asarray(r, np.int64) + off for r, off in zip(survivors, offsets.tolist())])] = \
+        np.concatenate([np.arange(len(r), dtype=np.int64) for r in survivors])
+    return np.split(compact[parent], offsets[1:])
+
+
+def ward_entry_index(order, lo, has_mass, split):
+    """Merged entry order of one Ward merge (``_semantic_ward_entry_index``, :2450-2474, for one
+    keep side [0, split) and free side [split, n)): each side stably sorted by level order; an
+    entry's key is the p_lo of the next entry with mass at or after it on its side (else its
+    own order); the sides merge by their running maxima of that key, keep side first on ties."""
+    order = np.asarray(order, np.int64)
+    lo = np.asarray(lo, np.int64)
+    has_mass = np.asarray(has_mass, bool)
+    n = len(order)
+    segment = (np.arange(n) >= split).astype(np.int64)
+    perm = np.argsort((segment << 32) + order, kind="stable")
+    o, l, h = order[perm], lo[perm], has_mass[perm]
+    seg_end = np.where(segment == 0, split, n)
+    ids = np.arange(n)
+    following = np.minimum.accumulate(np.where(h, ids, n)[::-1])[::-1]
+    effective = np.where(following < seg_end, l[np.minimum(following, n - 1)], o)
+    running = np.maximum.accumulate((segment << 32) + effective) - (segment << 32)
+    merge = np.argsort(running, kind="stable")
+    return perm[merge]

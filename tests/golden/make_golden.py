@@ -33,7 +33,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
-from streams import CONFIGS, make_stream  # noqa: E402
+from streams import CONFIGS, UNIFIED_CONFIGS, make_stream  # noqa: E402
 
 
 def install_shim(reference: str) -> None:
@@ -123,6 +123,7 @@ def run_config(cfg: dict, outdir: str) -> str:
         alpha_exact_tokens=cfg["exact"], alpha_span_max_tokens=cfg["span_cap"],
         beta_novelty=cfg["beta"], beta_adaptive_merge=cfg["beta"],
         semantic_s_h=cfg.get("s_h"), cos_cache=cos, sin_cache=sin, rope_n_elem=cfg["dim"],
+        semantic_unified_route=cfg.get("unified", False), semantic_merge_passes=cfg.get("merge_passes", 1),
     )
     out: dict = {}
     for step, chunk in enumerate(stream["chunks"]):
@@ -163,13 +164,17 @@ def main() -> None:
         raise SystemExit("pass --reference <reference checkout> or set LOGKV_REFERENCE")
     install_shim(args.reference)
     index = {}
-    for cfg in CONFIGS:
+    index_path = os.path.join(args.out, "index.json")
+    if os.path.exists(index_path):
+        with open(index_path) as fh:
+            index = json.load(fh)
+    for cfg in CONFIGS + UNIFIED_CONFIGS:
         if args.only and cfg["name"] != args.only:
             continue
         path = run_config(cfg, args.out)
         index[cfg["name"]] = os.path.basename(path)
         print("wrote", path, os.path.getsize(path))
-    with open(os.path.join(args.out, "index.json"), "w") as fh:
+    with open(index_path, "w") as fh:
         json.dump(index, fh, indent=1, sort_keys=True)
 
 

@@ -31,6 +31,25 @@ CONFIGS = [
 ]
 
 
+# Unified (Ward / radius) route variants: the same miniature streams with
+# semantic_unified_route=True.  The default radius (s_h = 1) lets nearby tokens
+# form candidates; s_h = 3 widens it; merge_passes = 2 adds frozen-centre sweeps
+# to the global pass.
+UNIFIED_CONFIGS = [
+    dict(BASE, name="fp32_unified", unified=True, seed=6),
+    dict(BASE, name="bf16_unified", dtype="bf16", unified=True, seed=7),
+    dict(BASE, name="fp32_unified_sh", unified=True, s_h=3.0, seed=8, jumps=True),
+    dict(BASE, name="fp32_unified_passes2", unified=True, merge_passes=2, seed=9),
+    dict(BASE, name="bf16_unified_nobeta", dtype="bf16", unified=True, beta=False, merge_passes=3, seed=10,
+         clusters=6, slots=12),
+    # Wider flushes (96 tokens, head dim 32): the candidate and global passes take the Gram form.
+    dict(BASE, name="fp32_unified_wide", unified=True, recent=96, granularity=96, chunk=96, steps=9,
+         max_seq=1024, dim=32, clusters=6, exact=16, span_cap=8, seed=11),
+    dict(BASE, name="bf16_unified_wide", dtype="bf16", unified=True, recent=96, granularity=96, chunk=96,
+         steps=9, max_seq=1024, dim=32, clusters=6, exact=16, span_cap=8, s_h=2.0, merge_passes=2, seed=12),
+]
+
+
 def make_stream(cfg: dict) -> dict:
     rng = np.random.default_rng(cfg["seed"])
     Bt, G, D, T = cfg["batch"], cfg["groups"], cfg["dim"], cfg["chunk"]
