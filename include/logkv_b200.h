@@ -41,6 +41,11 @@ extern "C" {
 #define LOGKV_DTYPE_F32 0
 #define LOGKV_DTYPE_BF16 1
 
+/* Routing of the archived tokens (logkv_layout_t.route). */
+#define LOGKV_ROUTE_ATTACH 0    /* frozen-centre attach route (_alpha_route_flush :3984-3988)          */
+#define LOGKV_ROUTE_UNIFIED 1   /* semantic_unified_route=True: _semantic_route_unified :3589-3688     */
+#define LOGKV_UNIFIED_MAX_ROWS 4096  /* unified route: exact + flush tokens + clusters per lane, at most */
+
 /* Static geometry of one layer's cache (LogStructuredKVCache.__init__, log_kv_cache.py:681-1133). */
 typedef struct logkv_layout {
   int32_t batch;           /* B  : batch rows                                  */
@@ -57,6 +62,8 @@ typedef struct logkv_layout {
   float eta;               /* seg_eta                                          */
   float g0;                /* seg_g0                                           */
   float lam;               /* cluster_lambda_rel                               */
+  int32_t route;           /* LOGKV_ROUTE_*                                    */
+  int32_t merge_passes;    /* semantic_merge_passes (>= 1; unified route)      */
 } logkv_layout_t;
 
 /*

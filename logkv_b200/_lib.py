@@ -29,12 +29,16 @@ TIE_KINDS = {1: "attach_cost", 2: "direct", 3: "nearest", 4: "seed_pick", 5: "se
              7: "alpha_order", 8: "alpha_swap"}
 
 
+ROUTE_ATTACH, ROUTE_UNIFIED = 0, 1   # logkv_layout_t.route (LOGKV_ROUTE_*)
+
+
 class Layout(ctypes.Structure):
     _fields_ = [("batch", ctypes.c_int32), ("groups", ctypes.c_int32), ("dim", ctypes.c_int32),
                 ("clusters", ctypes.c_int32), ("levels", ctypes.c_int32), ("slots", ctypes.c_int32),
                 ("recent_capacity", ctypes.c_int32), ("exact", ctypes.c_int32), ("span_cap", ctypes.c_int32),
                 ("beta", ctypes.c_int32), ("dtype", ctypes.c_int32), ("eta", ctypes.c_float),
-                ("g0", ctypes.c_float), ("lam", ctypes.c_float)]
+                ("g0", ctypes.c_float), ("lam", ctypes.c_float), ("route", ctypes.c_int32),
+                ("merge_passes", ctypes.c_int32)]
 
 
 STATE_FIELDS = ["level_k", "level_v", "level_w", "level_p_lo", "level_p_hi", "level_sum_wp", "level_order",

@@ -23,7 +23,7 @@ import torch.nn as nn
 
 from . import _lib
 
-UNSUPPORTED = "logkv_b200 implements the attach + Alpha (+ Beta) mid-anchor flush path only"
+UNSUPPORTED = "logkv_b200 implements the attach or unified route + Alpha (+ Beta) mid-anchor flush path only"
 
 
 def ladder_geometry(max_seq_length: int, k_dim: int, v_dim: int, n_groups: int, B: int, clusters: int,
@@ -110,8 +110,14 @@ class LogStructuredKVCache(nn.Module):
             raise ValueError(f"storage dtype {dtype} is not supported (float32 or bfloat16)")
         if not semantic_clusters or semantic_anchor_mode != "mid" or allocate_second_order:
             raise NotImplementedError(UNSUPPORTED)
-        if semantic_unified_route or semantic_legacy_route or semantic_cluster_chunk_size:
-            raise NotImplementedError(UNSUPPORTED + " (attach route)")
+        if int(semantic_merge_passes) < 1:
+            raise ValueError("semantic_merge_passes must be >= 1")
+        if semantic_unified_route and (semantic_legacy_route or semantic_cluster_chunk_size):
+            raise ValueError("unified routing requires semantic clusters and excludes legacy/chunk-tree routing")
+        if semantic_unified_route and semantic_capacity_beta != 0.0:
+            raise ValueError("unified routing uses Ward costs; semantic_capacity_beta must be 0")
+        if semantic_legacy_route or semantic_cluster_chunk_size:
+            raise NotImplementedError(UNSUPPORTED + " (attach or unified route)")
         if semantic_capacity_hard_cap_mult or semantic_capacity_beta or importance_pooling:
             raise NotImplementedError(UNSUPPORTED + " (no capacity terms)")
         if (seg_gap_max is not None and math.isfinite(seg_gap_max)) or seg_block_level:
@@ -144,6 +150,8 @@ class LogStructuredKVCache(nn.Module):
         self.semantic_pack_backend = semantic_pack_backend
         self.semantic_centroid_backend = semantic_centroid_backend
         self.semantic_replay_updates = bool(semantic_replay_updates)
+        self.semantic_unified_route = bool(semantic_unified_route)
+        self.semantic_merge_passes = int(semantic_merge_passes)
         self.K_max = int(cluster_k_max)
         self.cluster_lambda_rel, self.seg_eta, self.seg_g0 = float(cluster_lambda_rel), float(seg_eta), float(seg_g0)
         self.seg_forget = float(seg_forget)
@@ -157,6 +165,8 @@ class LogStructuredKVCache(nn.Module):
         # is not proportional to the group count).
         geo_groups = groups
         if kv_shard_group is not None:
+            if semantic_unified_route:
+                raise NotImplementedError(UNSUPPORTED + " (KV-head sharding of the attach route only)")
             import torch.distributed as dist
             geo_groups = groups * dist.get_world_size(kv_shard_group)
         self.B_prime, self.L_alloc = ladder_geometry(max_seq, k_dim, v_dim, geo_groups, B, self.K_max,
@@ -227,7 +237,9 @@ class LogStructuredKVCache(nn.Module):
         self.op_log_len = None
         self._layout = _lib.Layout(batch, groups, k_dim, K, L, Bs, R, P, self.alpha_span_max_tokens,
                                    int(self.beta_adaptive_merge), _lib.DTYPE_CODES[dtype], self.seg_eta,
-                                   self.seg_g0, self.cluster_lambda_rel)
+                                   self.seg_g0, self.cluster_lambda_rel,
+                                   _lib.ROUTE_UNIFIED if self.semantic_unified_route else _lib.ROUTE_ATTACH,
+                                   self.semantic_merge_passes)
         nbytes = _lib.lib().logkv_flush_workspace_bytes(ctypes.byref(self._layout), self.semantic_flush_granularity)
         if not nbytes:
             raise ValueError("cache geometry is outside the supported range of the flush kernels")
@@ -289,6 +301,8 @@ class LogStructuredKVCache(nn.Module):
 
     def _flush_with_updates(self, take: int, record_op_log: bool, replay: bool) -> None:
         """One flush under an update context: record it, or replay its record without routing."""
+        if self.semantic_unified_route:
+            raise NotImplementedError(UNSUPPORTED + " (update tapes of the attach route only)")
         updates = self._active_updates
         key = (self._flush_cursor, int(take), int(self.recent_count))
         lib = _lib.lib()
@@ -380,6 +394,7 @@ class LogStructuredKVCache(nn.Module):
         """
         dev = self.level_k.device
         if (not self._route_overlap or dev.type != "cuda" or self._route_ready is None
+                or self.semantic_unified_route
                 or self.kv_shard_group is not None or self.profile_events is not None
                 or take > self._route_ready_rows
                 or self._route_ready_capture != _lib.capture_id(dev)):
@@ -523,6 +538,8 @@ class LogStructuredKVCache(nn.Module):
         copy and can be captured in a CUDA graph.
         """
         replaying = any(v_ is not None for v_ in replay.values())
+        if record_op_log and self.semantic_unified_route:
+            raise NotImplementedError(UNSUPPORTED + " (op-logs of the attach route only)")
         chunk = self._check_chunk(k, v, k_raw, input_pos, span_ends, span_ends_device)
         take = None if replaying else self._chunk_flush_take(chunk[-1])
         if take is not None:

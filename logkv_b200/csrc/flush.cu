@@ -23,6 +23,7 @@
 #include "flush_ladder.cuh"
 #include "flush_route.cuh"
 #include "flush_tape.cuh"
+#include "flush_unified.cuh"
 
 namespace logkv {
 
@@ -416,6 +417,9 @@ static Geo make_geo(const logkv_layout_t& L, int F, int recent_count) {
   g.g0 = L.g0;
   g.lam = L.lam;
   g.shard_ranks = 1;
+  g.route = L.route;
+  g.passes = L.merge_passes < 1 ? 1 : L.merge_passes;
+  g.Mg = g.NW + g.K;
   return g;
 }
 
@@ -473,6 +477,26 @@ static size_t carve(const Geo& g, size_t esize, char* base, Work* w) {
   w->wv = c.take<char>(B * G * R * D, esize);
   w->wpos = c.take<int64_t>(B * R, 8);
   w->wends = c.take<uint8_t>(B * R, 1);
+  if (g.route == LOGKV_ROUTE_UNIFIED) {
+    const size_t lanes = B * G, Mg = g.Mg;
+    UWork& u = w->u;
+    u.dist = c.take<float>(lanes * Mg * Mg, 4);
+    u.mu_c = c.take<float>(lanes * NW * D, 4);
+    u.mu_g = c.take<float>(lanes * Mg * D, 4);
+    u.mass = c.take<float>(lanes * Mg, 4);
+    u.radius = c.take<float>(lanes * Mg, 4);
+    u.packed = c.take<long long>(lanes * Mg, 8);
+    u.restr = c.take<long long>(lanes * Mg, 8);
+    u.trace_c = c.take<int32_t>(lanes * NW * 2, 4);
+    u.trace_g = c.take<int32_t>(lanes * Mg * 2, 4);
+    u.label = c.take<int32_t>(lanes * NW, 4);
+    u.words = c.take<int32_t>(lanes * kULaneWords, 4);
+    u.limit = c.take<float>(lanes, 4);
+    u.old = c.take<int32_t>(lanes * K, 4);
+    u.ward = c.take<int32_t>(lanes * K * 2, 4);
+    u.alive = c.take<uint8_t>(lanes * Mg, 1);
+    u.stuck = c.take<uint8_t>(lanes * 2, 1);
+  }
   return (c.off + 255) & ~size_t(255);
 }
 
@@ -485,6 +509,10 @@ static int validate(const logkv_layout_t* L, int F) {
   if (L->slots < 2 || L->exact < 1 || L->span_cap < 1 || L->span_cap > L->exact) return LOGKV_E_SHAPE;
   if (F < 1 || F > L->recent_capacity || L->exact + F > 8192) return LOGKV_E_SHAPE;
   if (L->levels * L->slots + L->exact + F > (1 << 14)) return LOGKV_E_SHAPE;
+  if (L->route != LOGKV_ROUTE_ATTACH && L->route != LOGKV_ROUTE_UNIFIED) return LOGKV_E_SHAPE;
+  if (L->route == LOGKV_ROUTE_UNIFIED &&
+      (L->merge_passes < 1 || L->exact + F + L->clusters > LOGKV_UNIFIED_MAX_ROWS || L->dim % 4))
+    return LOGKV_E_SHAPE;
   return LOGKV_OK;
 }
 
@@ -513,6 +541,70 @@ static TapeSegs tape_segments(const Geo& g, const logkv_state_t& s, const Work& 
   add(w.plan_scr, t.plan_scr, B * G * K * 4);
   add(w.plan_base, t.plan_base, B * G * K * 8);
   return segs;
+}
+
+// ---------------------------------------------------------------- unified route launches
+static size_t unified_gram_smem(const Geo& g) { return 2 * (size_t)g.D * kGramTile * 4 + 2 * (size_t)kGramTile * 4; }
+static size_t unified_round_smem(const Geo& g) {
+  return logkv_ward::round_smem_bytes(g.Mg, logkv_ward::sort_width(g.Mg));
+}
+static int unified_sort_cap(const Geo& g) {
+  int p = 2;
+  while (p < 2 * g.L * g.Bs) p <<= 1;
+  return p;
+}
+static size_t unified_walk_bytes(const Geo& g, size_t esize) { return (walk_smem(g, esize, kTileRows) + 15) & ~size_t(15); }
+static size_t unified_ward_smem(const Geo& g, size_t esize) {
+  return unified_walk_bytes(g, esize) + 2 * (size_t)unified_sort_cap(g) * 8;
+}
+static bool unified_fits(const Geo& g, size_t esize) {
+  const size_t lim = 227 * 1024;
+  return unified_gram_smem(g) <= lim && unified_round_smem(g) <= lim && unified_ward_smem(g, esize) <= lim &&
+         3 * (size_t)g.NW * 4 <= lim && 3 * (size_t)g.Mg * 4 <= lim && (size_t)g.B * 4 <= lim &&
+         (size_t)g.B * g.G <= 65535;
+}
+
+template <typename T, bool BETA, int DC>
+static void launch_ward(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st) {
+  const size_t smem = unified_ward_smem(g, sizeof(T));
+  smem_limit(unified_ward_kernel<T, BETA, DC>, smem);
+  launch_pdl(unified_ward_kernel<T, BETA, DC>, dim3(g.G, g.B), kCascadeThreads, smem, st, g, s, w,
+             unified_sort_cap(g), unified_walk_bytes(g, sizeof(T)));
+}
+
+// The unified route between the span choice and the per-cluster plan: candidate pass, labels,
+// global pass, route, Ward merges (11 launches, no host synchronisation).
+template <typename T>
+static void launch_unified(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st) {
+  const int lanes = g.B * g.G, tiles = (g.Mg + kGramTile - 1) / kGramTile;
+  const int S = logkv_ward::sort_width(g.Mg);
+  const size_t gram = unified_gram_smem(g), round = unified_round_smem(g);
+  const size_t lab = 3 * (size_t)g.NW * 4, rte = 3 * (size_t)g.Mg * 4, tile = (size_t)g.B * 4;
+  smem_limit(unified_dist_kernel, gram);
+  smem_limit(unified_reduce_kernel, round);
+  smem_limit(unified_labels_kernel, lab);
+  smem_limit(unified_route_kernel, rte);
+  smem_limit(unified_tile_kernel, tile);
+  const int per = std::max(1, std::min(64, (g.NW * g.D + 255) / 256));
+  for (int pass = 0; pass < 2; ++pass) {
+    // The load kernel clears the lane words, so the candidate pass's tile flags follow it.
+    if (pass == 0) launch_pdl(unified_load_kernel<T>, dim3(per, g.G, g.B), 256, 0, st, g, s, w);
+    launch_pdl(unified_tile_kernel, dim3(1), 1024, tile, st, g, w, pass);
+    launch_pdl(unified_dist_kernel, dim3(tiles, tiles, lanes), 256, gram, st, g, w, pass);
+    launch_pdl(unified_reduce_kernel, dim3(lanes * logkv_ward::kUCluster), logkv_ward::kUThreads, round, st, g, w,
+               pass, S);
+    if (pass == 0) launch_pdl(unified_labels_kernel, dim3(g.G, g.B), 1024, lab, st, g, s, w);
+  }
+  launch_pdl(unified_route_kernel, dim3(g.G, g.B), 1024, rte, st, g, s, w);
+  if (g.beta) {
+    if (g.D == 128) launch_ward<T, true, 128>(g, s, w, st);
+    else if (g.D == 64) launch_ward<T, true, 64>(g, s, w, st);
+    else launch_ward<T, true, 0>(g, s, w, st);
+  } else {
+    if (g.D == 128) launch_ward<T, false, 128>(g, s, w, st);
+    else if (g.D == 64) launch_ward<T, false, 64>(g, s, w, st);
+    else launch_ward<T, false, 0>(g, s, w, st);
+  }
 }
 
 // Phases: kPhaseScores = snapshot, span cut, span scores (the group parts of this rank) and
@@ -548,11 +640,13 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   if (g.D == 128) launch_score<T, 128>(g, s, w, score_smem, score_blocks, st);
   else if (g.D == 64) launch_score<T, 64>(g, s, w, score_smem, score_blocks, st);
   else launch_score<T, 0>(g, s, w, score_smem, score_blocks, st);
-  const size_t attach_smem = attach_smem_bytes(g);
-  const int attach_x = (g.NW + kAttachTokens - 1) / kAttachTokens;
-  if (g.D == 128) launch_attach<T, 128>(g, s, w, attach_smem, attach_x, st);
-  else if (g.D == 64) launch_attach<T, 64>(g, s, w, attach_smem, attach_x, st);
-  else launch_attach<T, 0>(g, s, w, attach_smem, attach_x, st);
+  if (g.route != LOGKV_ROUTE_UNIFIED) {
+    const size_t attach_smem = attach_smem_bytes(g);
+    const int attach_x = (g.NW + kAttachTokens - 1) / kAttachTokens;
+    if (g.D == 128) launch_attach<T, 128>(g, s, w, attach_smem, attach_x, st);
+    else if (g.D == 64) launch_attach<T, 64>(g, s, w, attach_smem, attach_x, st);
+    else launch_attach<T, 0>(g, s, w, attach_smem, attach_x, st);
+  }
   }
   if (phases & kPhaseRoute) {
   mark();
@@ -561,7 +655,9 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
     cudaFuncSetAttribute(alpha_choose_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)choose_smem);
   launch_pdl(alpha_choose_kernel, g.B, 1024, choose_smem, st, g, s, w);
   mark();
-  {
+  if (g.route == LOGKV_ROUTE_UNIFIED) {
+    launch_unified<T>(g, s, w, st);
+  } else {
     // Seeding: one 8-CTA cluster per lane; rows staged in shared memory when they fit.
     Geo gs = g;
     const size_t chunk = (size_t)(g.NW + kSeedCluster - 1) / kSeedCluster;
@@ -659,9 +755,15 @@ static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, i
   if (cascade_smem(g, esize) > 227 * 1024 || prep_smem_bytes(g, esize) > 227 * 1024 ||
       choose_smem_bytes(g) > 227 * 1024 || score_smem_bytes(g, esize) > 227 * 1024 || attach_smem_bytes(g) > 227 * 1024)
     return LOGKV_E_SMEM;
+  if (g.route == LOGKV_ROUTE_UNIFIED && !unified_fits(g, esize)) return LOGKV_E_SMEM;
   w.gpart_all = gpart_all;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (chunk && (tape_mode != kTapeNone || phases != kPhaseAll)) return LOGKV_E_SHAPE;
+  // The unified route's Ward merges rewrite ladders before the per-cluster plan, so its route
+  // phase runs only together with the apply phase, and it keeps no update tape.
+  if (layout->route == LOGKV_ROUTE_UNIFIED &&
+      (tape_mode != kTapeNone || ((phases & kPhaseRoute) && !(phases & kPhaseApply))))
+    return LOGKV_E_SHAPE;
   if (tape_mode != kTapeNone) {
     TapeView t{};
     // A whole unsharded flush, or the commit half of a sharded one when recording (the record

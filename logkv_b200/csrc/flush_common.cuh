@@ -24,7 +24,38 @@ struct Geo {
   int shard_ranks;        // KV-head sharding: ranks holding G groups each (1 = unsharded)
   long long gpart_stride; // KV-head sharding: floats between two ranks' span parts in gpart_all
   int tape;               // update tape: kTapeNone, kTapeRecord (save Beta cuts), kTapeReplay (use them)
+  int route;              // LOGKV_ROUTE_ATTACH or LOGKV_ROUTE_UNIFIED
+  int passes;             // unified route: semantic_merge_passes of the global pass
+  int Mg;                 // unified route: rows per lane of its matrices (NW + K)
   float eta, g0, lam;
+};
+
+// Unified-route workspace (flush_unified.cuh), per (batch, group) lane; null for the attach route.
+constexpr int kULaneWords = 16;
+enum ULaneWord : int {
+  kUCountC = 0, kUActiveC = 1, kUMergesC = 2,   // candidate pass: live count, active, merges
+  kUCountG = 4, kUActiveG = 5, kUMergesG = 6,   // global pass
+  kUGCount = 8, kUOld = 9, kUCand = 10,         // global rows, old clusters, candidates
+  kUCdistC = 11, kUCdistG = 12,                 // the pass takes the exact-difference form (tile size <= 32)
+  kUWard = 13,                                  // Ward merges of old clusters
+};
+struct UWork {
+  float* dist;          // [B*G, Mg, Mg] squared centre distances
+  float* mu_c;          // [B*G, NW, D] candidate pass centres (archived tokens, then candidates)
+  float* mu_g;          // [B*G, Mg, D] global pass centres (live centroids, then candidates)
+  float* mass;          // [B*G, Mg]
+  float* radius;        // [B*G, Mg]
+  uint8_t* alive;       // [B*G, Mg]
+  uint8_t* stuck;       // [B*G, 2]
+  long long* packed;    // [B*G, Mg]
+  long long* restr;     // [B*G, Mg] frozen-centre sweep scratch
+  int32_t* trace_c;     // [B*G, NW, 2]
+  int32_t* trace_g;     // [B*G, Mg, 2]
+  int32_t* label;       // [B*G, NW] candidate (compact) of every archived token
+  int32_t* words;       // [B*G, kULaneWords]
+  float* limit;         // [B*G] candidate pass radius limit
+  int32_t* old;         // [B*G, K] live clusters before the flush, ascending
+  int32_t* ward;        // [B*G, K, 2] Ward merges (keep, free) in trace order
 };
 
 // 16-byte asynchronous global -> shared copies (both addresses 16-byte aligned).
@@ -169,6 +200,7 @@ struct Work {
   void* wv;
   int64_t* wpos;
   uint8_t* wends;
+  UWork u;                 // unified route only
 };
 
 // Relative gap of two values: |a - b| / max(|a|, |b|) (0 when both are 0; NaN-safe: NaN gives

@@ -10,112 +10,20 @@
 // the reference writes it (this file is compiled without fused multiply-adds); the exact squared
 // distance of a candidate pair sums the features left to right.
 //
-// A thread-block cluster of kCluster CTAs runs one round of one lane (the leader selects the pairs,
-// all CTAs share the centre, Lance-Williams and rescan work); within a round every merge writes
-// only its own row and column, which no other merge of the round reads.
-#include <cooperative_groups.h>
+// The round itself (one thread-block cluster of kUCluster CTAs per lane) is unified_core.cuh's,
+// shared with the flush-level route; here each launch runs one round of every lane.
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include "../../include/logkv_unified.h"
-
-namespace cg = cooperative_groups;
+#include "unified_core.cuh"
 
 namespace {
 
-constexpr int kThreads = 1024;
-constexpr int kCluster = 8;         // CTAs per lane (one thread-block cluster)
-constexpr int kMaxSize = 4096;      // rows per lane (the sort runs in shared memory)
-constexpr long long kInfKey = 0x7F80000000000000LL;
-
-__device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
-__device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
-__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
-__device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b); }
-
-// (cost bits << 32) | key, with -0.0 written as +0.0 (_unified_pack, log_kv_cache.py:431-434).
-__device__ __forceinline__ long long pack_key(float cost, long long key) {
-  if (cost == 0.f) cost = 0.f;
-  return ((long long)__float_as_int(cost) << 32) | key;
-}
-
-// Ward cost of joining clusters i and j, +inf when the pair is not allowed
-// (_unified_pair_cost, log_kv_cache.py:437-445).
-__device__ __forceinline__ float pair_cost(float d2, float mi, float mj, float ri, float rj, const float* limit,
-                                           bool valid) {
-  const float denom = fmaxf(fadd(mi, mj), 1.f);
-  valid = valid && mi > 0.f && mj > 0.f;
-  if (limit) {
-    // Exact early out: with radii >= 0 and mi + mj >= 1, every rounding above leaves
-    // max(b1, b2) >= sqrt(d2) (1 - 5u) / 2 (u = 2^-24), so d2 > 4.0001 limit^2 proves the pair
-    // invalid without its divisions (an infinite or NaN limit never takes this branch).
-    if (denom == fadd(mi, mj) && d2 > fmul(fmul(4.0001f, *limit), *limit)) return __int_as_float(0x7F800000);
-    const float distance = __fsqrt_rn(d2);
-    const float b1 = fadd(ri, fmul(fdiv(mj, denom), distance));
-    const float b2 = fadd(rj, fmul(fdiv(mi, denom), distance));
-    valid = valid && fmaxf(b1, b2) <= *limit;
-  }
-  return valid ? fmul(d2, fdiv(fmul(mi, mj), denom)) : __int_as_float(0x7F800000);
-}
-
-struct Lane {
-  float* dist;       // [M, M]
-  float* mu;         // [M, D]
-  float* mass;       // [M]
-  float* radius;     // [M]
-  uint8_t* alive;    // [M]
-  long long* packed; // [M]
-  const float* limit;
-};
-
-__device__ Lane lane_of(const logkv_unified_t& u, int lane) {
-  const size_t M = u.size;
-  Lane l;
-  l.dist = u.dist + lane * M * M;
-  l.mu = u.mu + lane * M * (size_t)u.dim;
-  l.mass = u.mass + lane * M;
-  l.radius = u.radius + lane * M;
-  l.alive = u.alive + lane * M;
-  l.packed = reinterpret_cast<long long*>(u.packed) + lane * M;
-  l.limit = u.limits ? u.limits + lane : nullptr;
-  return l;
-}
-
-// packed[r] = min over columns of the row's packed keys; one warp per row.  Only live columns
-// (`cols`, or [0, ncols) when cols is null) are visited: any other column's key is +inf with
-// r ^ c > 0, never below the key of the row's own column, (+inf, 0), which starts the minimum.
-__device__ void scan_rows(const Lane& l, int M, const int* rows, int nrows, const int* cols, int ncols) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-  constexpr int kBatch = 4;   // columns per lane whose loads are in flight together
-  for (int i = warp; i < nrows; i += nwarps) {
-    const int r = rows[i];
-    const float* drow = l.dist + (size_t)r * M;
-    const float mr = l.mass[r], rr = l.radius[r];
-    long long best = kInfKey;
-    for (int kb = lane; kb < ncols; kb += 32 * kBatch) {
-      int cv[kBatch];
-      float dv[kBatch], mv[kBatch], rv[kBatch];
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        const int k = kb + 32 * j;
-        cv[j] = k < ncols ? (cols ? cols[k] : k) : -1;
-        const int c = cv[j] < 0 ? r : cv[j];
-        dv[j] = drow[c];
-        mv[j] = l.mass[c];
-        rv[j] = l.radius[c];
-      }
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        if (cv[j] < 0) continue;
-        const float cost = pair_cost(dv[j], mr, mv[j], rr, rv[j], l.limit, cv[j] != r);
-        best = min(best, pack_key(cost, (long long)(r ^ cv[j])));
-      }
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, off));
-    if (lane == 0) l.packed[r] = best;
-  }
-}
+using namespace logkv_ward;
+constexpr int kThreads = kUThreads;
+constexpr int kCluster = kUCluster;
+constexpr int kMaxSize = kUMaxSize;
 
 __global__ void __launch_bounds__(kThreads) pair_distances_kernel(float* gram, const float* norm, int M) {
   const int lane = blockIdx.z;
@@ -137,409 +45,56 @@ __global__ void __launch_bounds__(kThreads) mirror_kernel(float* dist, int M) {
   d[(size_t)i * M + j] = d[(size_t)j * M + i];
 }
 
+// One lane of the operator-level state.
+__device__ RunLane lane_of(const logkv_unified_t& u, int lane) {
+  const size_t M = u.size;
+  RunLane l;
+  l.dist = u.dist + lane * M * M;
+  l.mu = u.mu + lane * M * (size_t)u.dim;
+  l.mass = u.mass + lane * M;
+  l.radius = u.radius + lane * M;
+  l.alive = u.alive + lane * M;
+  l.packed = reinterpret_cast<long long*>(u.packed) + lane * M;
+  l.restricted = nullptr;
+  l.limit = u.limits ? u.limits + lane : nullptr;
+  l.count = u.status + u.lanes + lane;
+  l.active = u.status + lane;
+  l.merges = u.merges + lane;
+  l.stuck = u.stuck + lane;
+  l.trace = u.trace + (size_t)lane * M * 2;
+  l.M = (int)M;
+  l.D = u.dim;
+  l.target = u.target;
+  l.passes = 1;
+  return l;
+}
+
 // Every live row's minimum; the lane's rows are split over kCluster CTAs (row r goes to r % kCluster).
 __global__ void __launch_bounds__(kThreads) init_kernel(logkv_unified_t u) {
   extern __shared__ int rows[];
-  const int lane = blockIdx.x / kCluster, part = blockIdx.x % kCluster, M = u.size;
-  Lane l = lane_of(u, lane);
-  const int count = u.status[u.lanes + lane];
   __shared__ int n;
-  if (threadIdx.x == 0) {
-    n = 0;
-    if (part == 0) {
-      u.status[lane] = 0;
-      u.merges[lane] = 0;
-      u.stuck[lane] = 0;
-    }
+  const int lane = blockIdx.x / kCluster, part = blockIdx.x % kCluster;
+  const RunLane l = lane_of(u, lane);
+  if (part == 0 && threadIdx.x == 0) {
+    *l.active = 0;
+    *l.merges = 0;
+    *l.stuck = 0;
   }
-  __syncthreads();
-  for (int r = part + kCluster * (int)threadIdx.x; r < M; r += kCluster * blockDim.x) {
-    const bool live = r < count;
-    l.alive[r] = live;
-    l.radius[r] = 0.f;
-    l.packed[r] = kInfKey;
-    if (live) rows[atomicAdd(&n, 1)] = r;
-  }
-  __syncthreads();
-  scan_rows(l, M, rows, n, nullptr, count < M ? count : M);
+  init_lane(l, part, rows, &n);
 }
 
-// Shared memory of one round (the same layout in every CTA of a lane's cluster).
-struct RoundSmem {
-  unsigned long long* sk;  // [S] sort keys (leader)
-  long long* rowmin;       // [M/2 + 1] this CTA's row minima of the merged rows
-  long long* colmin;       // [CW] this CTA's column minima
-  int* best;               // [M]
-  int* partner;            // [M]
-  int* rows;               // [M] dirty rows of this CTA
-  int* pairs;              // [M/2 + 1] kept row of merge m, in merge order
-  int* cols;               // [M] live columns after the merges, ascending
-  float* bound;            // [M]
-  float* pma;              // [M] masses of a merge's rows, at its kept row
-  float* pmb;              // [M]
-  float* alpha;            // [M] ma / total, mb / total and alpha * beta * d_ab of a merge, at its kept row
-  float* beta;             // [M]
-  float* shift;            // [M]
-  uint8_t* flags;          // [M] 1 valid, 2 rejected, 4 keep, 8 merged
-};
-
-__host__ __device__ inline int column_width(int M) { return ((M + kCluster - 1) / kCluster + 31) / 32 * 32; }
-
-__host__ __device__ inline size_t round_smem_bytes(int M, int S) {
-  const size_t half = (size_t)M / 2 + 1;
-  return (size_t)S * 8 + half * 8 + (size_t)column_width(M) * 8 + (size_t)M * 4 * 3 + half * 4 +
-         (size_t)M * 4 * 7 + (size_t)M + 16;
-}
-
-__device__ RoundSmem carve_round(void* base, int M, int S) {
-  RoundSmem r;
-  char* p = static_cast<char*>(base);
-  const size_t half = (size_t)M / 2 + 1;
-  r.sk = reinterpret_cast<unsigned long long*>(p);
-  p += (size_t)S * 8;
-  r.rowmin = reinterpret_cast<long long*>(p);
-  p += half * 8;
-  r.colmin = reinterpret_cast<long long*>(p);
-  p += (size_t)column_width(M) * 8;
-  r.best = reinterpret_cast<int*>(p);
-  p += (size_t)M * 4;
-  r.partner = reinterpret_cast<int*>(p);
-  p += (size_t)M * 4;
-  r.rows = reinterpret_cast<int*>(p);
-  p += (size_t)M * 4;
-  r.pairs = reinterpret_cast<int*>(p);
-  p += half * 4;
-  r.cols = reinterpret_cast<int*>(p);
-  p += (size_t)M * 4;
-  r.bound = reinterpret_cast<float*>(p);
-  p += (size_t)M * 4;
-  r.pma = reinterpret_cast<float*>(p);
-  p += (size_t)M * 4;
-  r.pmb = reinterpret_cast<float*>(p);
-  p += (size_t)M * 4;
-  r.alpha = reinterpret_cast<float*>(p);
-  p += (size_t)M * 4;
-  r.beta = reinterpret_cast<float*>(p);
-  p += (size_t)M * 4;
-  r.shift = reinterpret_cast<float*>(p);
-  p += (size_t)M * 4;
-  r.flags = reinterpret_cast<uint8_t*>(p);
-  return r;
-}
-
-// Leader CTA: proposals, exact radius checks, the pairs' cost order and budget, and the
-// merged clusters' masses, liveness and radii; the trace and the lane's status.
-__device__ void select_pairs(const logkv_unified_t& u, const Lane& l, int lane, const RoundSmem& sm, int* n_ok_out,
-                             int* nprop_out) {
-  const int M = u.size, D = u.dim, tid = threadIdx.x, nt = blockDim.x;
-  __shared__ int nprop, nvalid, nok;
-  if (tid == 0) {
-    nprop = 0;
-    nvalid = 0;
-  }
-  const unsigned inf_bits = 0x7F800000u;
-  for (int r = tid; r < M; r += nt) {
-    const long long p = l.packed[r];
-    int b = (int)(((p & 0xFFFFFFFFLL) ^ (long long)r));
-    b = b < 0 ? 0 : (b > M - 1 ? M - 1 : b);
-    sm.best[r] = b;
-    sm.partner[r] = 0;
-    sm.pma[r] = 1.f;
-    sm.pmb[r] = 0.f;
-    sm.bound[r] = 0.f;
-  }
-  __syncthreads();
-  for (int r = tid; r < M; r += nt) {
-    const long long p = l.packed[r];
-    const float cost = __int_as_float((int)(p >> 32));
-    const int b = sm.best[r];
-    const bool v = l.alive[r] && r < b && sm.best[b] == r && cost < __int_as_float(inf_bits);
-    sm.flags[r] = v ? 1 : 0;
-    if (v) atomicAdd(&nprop, 1);
-  }
-  __syncthreads();
-  if (l.limit) {
-    for (int r = tid; r < M; r += nt) {
-      if (!(sm.flags[r] & 1)) continue;
-      const int o = sm.best[r];
-      const float* xa = l.mu + (size_t)r * D;
-      const float* xb = l.mu + (size_t)o * D;
-      float exact2 = 0.f;
-#pragma unroll 8
-      for (int d = 0; d < D; ++d) {
-        const float df = fsub(xa[d], xb[d]);
-        exact2 = fadd(exact2, fmul(df, df));
-      }
-      const float exact = __fsqrt_rn(exact2);
-      const float ma = l.mass[r], mb = l.mass[o];
-      const float denom = fmaxf(fadd(ma, mb), 1.f);
-      const float verified =
-          fmaxf(fadd(l.radius[r], fmul(fdiv(mb, denom), exact)), fadd(l.radius[o], fmul(fdiv(ma, denom), exact)));
-      if (verified > *l.limit) {
-        l.dist[(size_t)r * M + o] = exact2;
-        l.dist[(size_t)o * M + r] = exact2;
-        sm.flags[r] = 2;          // rejected, no longer valid
-        sm.flags[o] |= 2;
-      }
-      sm.bound[r] = verified;
-    }
-  }
-  __syncthreads();
-  // Valid pairs (a row each, below its partner; finite costs), compacted, then a bitonic sort of
-  // (cost bits << 32 | row): the reference's stable argsort by cost.
-  for (int r = tid; r < M; r += nt)
-    if (sm.flags[r] & 1) sm.sk[atomicAdd(&nvalid, 1)] = ((unsigned long long)(l.packed[r] >> 32) << 32) | (unsigned)r;
-  __syncthreads();
-  const int nv = nvalid;
-  int S = 1;
-  while (S < nv) S <<= 1;
-  for (int i = nv + tid; i < S; i += nt) sm.sk[i] = ~0ull;
-  __syncthreads();
-  for (int k = 2; k <= S; k <<= 1) {
-    for (int j = k >> 1; j > 0; j >>= 1) {
-      for (int i = tid; i < S; i += nt) {
-        const int ixj = i ^ j;
-        if (ixj > i) {
-          const unsigned long long x = sm.sk[i], y = sm.sk[ixj];
-          const bool up = (i & k) == 0;
-          if ((x > y) == up) {
-            sm.sk[i] = y;
-            sm.sk[ixj] = x;
-          }
-        }
-      }
-      __syncthreads();
-    }
-  }
-  // Budget: the first min(valid, count - target, M / 2) pairs merge.
-  const int count = u.status[u.lanes + lane];
-  if (tid == 0) {
-    int n = min(nv, M / 2);
-    n = min(n, max(count - u.target, 0));
-    nok = n;
-  }
-  __syncthreads();
-  const int n_ok = nok;
-  const int trace0 = u.merges[lane];
-  for (int m = tid; m < n_ok; m += nt) {
-    const int a = (int)(sm.sk[m] & 0xFFFFFFFFull), b = sm.best[a];
-    sm.pairs[m] = a;
-    sm.flags[a] |= 4 | 8;
-    sm.flags[b] |= 8;
-    sm.partner[a] = b;
-    const float ma = l.mass[a], mb = l.mass[b];
-    const float total = fadd(ma, mb);
-    const float al = fdiv(ma, total), be = fdiv(mb, total);
-    sm.pma[a] = ma;
-    sm.pmb[a] = mb;
-    sm.alpha[a] = al;
-    sm.beta[a] = be;
-    sm.shift[a] = fmul(fmul(al, be), l.dist[(size_t)a * M + b]);
-    u.trace[((size_t)lane * M + trace0 + m) * 2] = a;
-    u.trace[((size_t)lane * M + trace0 + m) * 2 + 1] = b;
-  }
-  __syncthreads();
-  for (int m = tid; m < n_ok; m += nt) {
-    const int a = sm.pairs[m], b = sm.best[a];
-    l.mass[a] = fadd(sm.pma[a], sm.pmb[a]);
-    l.mass[b] = 0.f;
-    l.alive[b] = 0;
-    if (l.limit) l.radius[a] = sm.bound[a];
-  }
-  if (tid == 0) {
-    const int left = count - n_ok;
-    u.status[u.lanes + lane] = left;
-    u.merges[lane] = trace0 + n_ok;
-    const bool remaining = left > u.target;
-    if (remaining && nprop == 0) u.stuck[lane] = 1;
-    u.status[lane] = remaining && nprop > 0;
-  }
-  *n_ok_out = n_ok;
-  *nprop_out = nprop;
-}
-
-// One round of one lane on a cluster of kCluster CTAs.  The leader selects the pairs; every CTA
-// copies the round's tables from the leader's shared memory, updates a share of the merged
-// centres, the Lance-Williams values of its columns of every merged row, and rescans its dirty
-// rows.  Within the round every merge writes only its own row and column, which no other merge
-// reads, and the phases are separated by cluster barriers (which also order the global writes).
+// One round of one lane on a cluster of kCluster CTAs.
 __global__ void __launch_bounds__(kThreads) round_kernel(logkv_unified_t u, int S) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ int act[2];
   cg::cluster_group cluster = cg::this_cluster();
-  const int part = (int)cluster.block_rank();
-  const int lane = blockIdx.x / kCluster, M = u.size, D = u.dim, tid = threadIdx.x, nt = blockDim.x;
-  Lane l = lane_of(u, lane);
-  const RoundSmem sm = carve_round(smem_raw, M, S);
-  __shared__ int n_ok_s, ndirty;
-  if (part == 0) {
-    int n_ok, nprop;
-    select_pairs(u, l, lane, sm, &n_ok, &nprop);
-    if (tid == 0) n_ok_s = n_ok;
-  }
-  cluster.sync();
-  // ---- the round's tables, from the leader
-  if (part != 0) {
-    const RoundSmem lead = carve_round(cluster.map_shared_rank(smem_raw, 0), M, S);
-    if (tid == 0) n_ok_s = *cluster.map_shared_rank(&n_ok_s, 0);
-    for (int r = tid; r < M; r += nt) {
-      sm.best[r] = lead.best[r];
-      sm.partner[r] = lead.partner[r];
-      sm.pma[r] = lead.pma[r];
-      sm.pmb[r] = lead.pmb[r];
-      sm.alpha[r] = lead.alpha[r];
-      sm.beta[r] = lead.beta[r];
-      sm.shift[r] = lead.shift[r];
-      sm.flags[r] = lead.flags[r];
-    }
-    __syncthreads();
-    for (int m = tid; m < n_ok_s; m += nt) sm.pairs[m] = lead.pairs[m];
-  }
-  if (tid == 0) ndirty = 0;
-  __syncthreads();
-  const int n_ok = n_ok_s;
-  // ---- merged centres: merge m goes to CTA m % kCluster
-  for (int item = tid; item < ((n_ok - part + kCluster - 1) / kCluster) * D; item += nt) {
-    const int m = part + kCluster * (item / D), d = item % D;
-    const int a = sm.pairs[m], b = sm.best[a];
-    const float ma = sm.pma[a], mb = sm.pmb[a];
-    const float total = fadd(ma, mb);
-    float* ra = l.mu + (size_t)a * D;
-    const float* rb = l.mu + (size_t)b * D;
-    ra[d] = fdiv(fadd(fmul(ma, ra[d]), fmul(mb, rb[d])), fmaxf(total, 1.f));
-  }
-  // ---- live columns after the merges (ascending): a block scan of the alive flags
-  __shared__ int wsum[kThreads / 32], ncols_s;
-  {
-    const int per = (M + nt - 1) / nt, lo = tid * per, hi = min(M, lo + per);
-    int cnt = 0;
-    for (int c = lo; c < hi; ++c) cnt += l.alive[c] != 0;
-    int incl = cnt;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, off);
-      if ((tid & 31) >= off) incl += v;
-    }
-    if ((tid & 31) == 31) wsum[tid >> 5] = incl;
-    __syncthreads();
-    if (tid < 32) {
-      int w = tid < nt / 32 ? wsum[tid] : 0;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, w, off);
-        if (tid >= off) w += v;
-      }
-      if (tid < nt / 32) wsum[tid] = w;
-      if (tid == 31) ncols_s = w;
-    }
-    __syncthreads();
-    int at = incl - cnt + ((tid >> 5) ? wsum[(tid >> 5) - 1] : 0);
-    for (int c = lo; c < hi; ++c)
-      if (l.alive[c]) sm.cols[at++] = c;
-  }
-  __syncthreads();
-  const int ncols = ncols_s;
-  // ---- Lance-Williams: this CTA's share [k0, k0 + CW) of the live columns, every merged row,
-  // as warp tasks of (merge, 32 columns); a merge's scalars were computed once by the leader.
-  const int CW = column_width(ncols), k0 = part * CW;
-  for (int i = tid; i < n_ok; i += nt) sm.rowmin[i] = kInfKey;
-  for (int i = tid; i < CW; i += nt) sm.colmin[i] = 0x7FFFFFFFFFFFFFFFLL;
-  __syncthreads();
-  constexpr int kChunks = 4;   // 32-column chunks per warp task, their loads in flight together
-  const int lanew = tid & 31, nchunk = CW / 32, ngrp = (nchunk + kChunks - 1) / kChunks;
-  const int ntask = k0 < ncols ? n_ok * ngrp : 0;
-  for (int task = tid >> 5; task < ntask; task += nt >> 5) {
-    const int m = task / ngrp, g0 = (task - m * ngrp) * kChunks;
-    const int a = sm.pairs[m], b = sm.best[a];
-    const float alpha = sm.alpha[a], beta = sm.beta[a], shift = sm.shift[a];
-    const float total = fadd(sm.pma[a], sm.pmb[a]), ra = l.radius[a];
-    const float* rowa = l.dist + (size_t)a * M;
-    const float* rowb = l.dist + (size_t)b * M;
-    int cv[kChunks];
-    float xaa[kChunks], xba[kChunks], mc[kChunks], rc[kChunks];
-#pragma unroll
-    for (int j = 0; j < kChunks; ++j) {
-      const int k = k0 + (g0 + j) * 32 + lanew;
-      cv[j] = (g0 + j < nchunk && k < ncols) ? sm.cols[k] : -1;
-      const int c = cv[j] < 0 ? a : cv[j];
-      xaa[j] = rowa[c];
-      xba[j] = rowb[c];
-      mc[j] = l.mass[c];
-      rc[j] = l.radius[c];
-    }
-    long long rkey = kInfKey;
-#pragma unroll
-    for (int j = 0; j < kChunks; ++j) {
-      const int c = cv[j];
-      if (c < 0) continue;
-      const float x_aa = xaa[j], x_ba = xba[j];
-      float nv = fsub(fadd(fmul(alpha, x_aa), fmul(beta, x_ba)), shift);
-      const bool keep_c = sm.flags[c] & 4;
-      if (keep_c) {
-        // Both clusters merged this round: the lower keep index's order, so both owners agree.
-        const int q = sm.partner[c];
-        const float x_ab = rowa[q], x_bb = rowb[q];
-        const float qal = sm.alpha[c], qbe = sm.beta[c], qsh = sm.shift[c];
-        float v;
-        if (a < c) {
-          const float inner = fsub(fadd(fmul(alpha, x_ab), fmul(beta, x_bb)), shift);
-          v = fsub(fadd(fmul(qal, nv), fmul(qbe, inner)), qsh);
-        } else {
-          const float t1 = fsub(fadd(fmul(qal, x_aa), fmul(qbe, x_ab)), qsh);
-          const float t2 = fsub(fadd(fmul(qal, x_ba), fmul(qbe, x_bb)), qsh);
-          v = fsub(fadd(fmul(alpha, t1), fmul(beta, t2)), shift);
-        }
-        nv = v;
-      }
-      nv = fmaxf(nv, 0.f);
-      if (c == a) nv = 0.f;
-      if (!keep_c) l.dist[(size_t)c * M + a] = nv;
-      l.dist[(size_t)a * M + c] = nv;
-      const float cost = pair_cost(nv, total, mc[j], ra, rc[j], l.limit, c != a);
-      const long long key = pack_key(cost, (long long)(a ^ c));
-      if (cost < __int_as_float(0x7F800000) && !keep_c) atomicMin(&sm.colmin[(g0 + j) * 32 + lanew], key);
-      rkey = min(rkey, key);
-    }
-    // A warp task covers columns of one merge only: one row-minimum atomic per task.
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) rkey = min(rkey, __shfl_xor_sync(0xffffffffu, rkey, off));
-    if (lanew == 0) atomicMin(&sm.rowmin[m], rkey);
-  }
-  __syncthreads();
-  // Columns this CTA owns take their new minima (non-merged columns only; an invalid key never lowers).
-  for (int kl = tid; kl < CW && k0 + kl < ncols; kl += nt) {
-    const int c = sm.cols[k0 + kl];
-    if (!(sm.flags[c] & 4) && sm.colmin[kl] < l.packed[c]) l.packed[c] = sm.colmin[kl];
-  }
-  cluster.sync();
-  // ---- merged rows: minimum over every CTA's columns (merge m on CTA m % kCluster)
-  for (int m = part + kCluster * tid; m < n_ok; m += kCluster * nt) {
-    long long v = sm.rowmin[m];
-    for (int r = 1; r < kCluster; ++r)
-      v = min(v, cluster.map_shared_rank(sm.rowmin, (part + r) % kCluster)[m]);
-    l.packed[sm.pairs[m]] = v;
-  }
-  // ---- rows whose best partner merged (or that were rejected) rescan; row r on CTA r % kCluster
-  for (int r = part + kCluster * tid; r < M; r += kCluster * nt) {
-    const uint8_t f = sm.flags[r];
-    if (l.alive[r] && !(f & 4) && ((sm.flags[sm.best[r]] & 8) || (f & 2))) sm.rows[atomicAdd(&ndirty, 1)] = r;
-  }
-  __syncthreads();
-  scan_rows(l, M, sm.rows, ndirty, sm.cols, ncols);
-  cluster.sync();   // no CTA leaves while another may still read its row minima
+  const RunLane l = lane_of(u, blockIdx.x / kCluster);
+  run_round(cluster, l, smem_raw, S, act, 0);
 }
 
 }  // namespace
 
-namespace {
 
-int next_pow2(int v) {
-  int p = 2;
-  while (p < v) p <<= 1;
-  return p;
-}
-
-
-}  // namespace
 
 extern "C" int logkv_pair_distances(float* gram, const float* norm, int32_t lanes, int32_t size, void* stream) {
   if (!gram || !norm) return LOGKV_UNIFIED_E_POINTER;
@@ -579,7 +134,7 @@ extern "C" int logkv_unified_init(const logkv_unified_t* u, void* stream) {
 extern "C" int logkv_unified_step(const logkv_unified_t* u, void* stream) {
   const int v = check_unified(u);
   if (v) return v;
-  const int S = next_pow2(u->size / 2);   // at most size / 2 disjoint pairs are sorted
+  const int S = sort_width(u->size);   // at most size / 2 disjoint pairs are sorted
   const size_t smem = round_smem_bytes(u->size, S);
   if (smem > 227 * 1024) return LOGKV_UNIFIED_E_SHAPE;
   if (smem > 48 * 1024) cudaFuncSetAttribute(round_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
