@@ -313,7 +313,9 @@ __device__ inline int uforest(int n, const int32_t* trace, int merges, const uin
   __syncthreads();
   for (int m = tid; m < merges; m += nt) parent[trace[2 * m + 1]] = trace[2 * m];
   __syncthreads();
-  for (;;) {
+  // Every retired row's parent is a smaller row, so depths halve per step: 32 steps cover any
+  // forest of fewer than 2^32 rows (the bound only guards against a malformed trace).
+  for (int step = 0; step < 32; ++step) {
     if (tid == 0) changed = 0;
     __syncthreads();
     for (int r = tid; r < n; r += nt) {
