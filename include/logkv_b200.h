@@ -371,6 +371,18 @@ LOGKV_API int logkv_flush_profiled(const logkv_layout_t* layout, const logkv_sta
 LOGKV_API int logkv_read_counters(const void* workspace, uint64_t* out, int32_t n, void* stream);
 
 /*
+ * Unified route only: copy the per-(batch, group) lane words of the last flush made with this
+ * workspace (16 int32 per lane, lane-major; up to n words) and synchronize `stream`.  Word 0..3:
+ * candidate pass live count, active flag, merges, rounds; 4..7 the same for the global pass;
+ * 8 global rows (live clusters + candidates), 9 live clusters before the flush, 10 candidates,
+ * 11/12 exact-difference pair matrices in the candidate / global pass, 13 Ward merges.  No
+ * reference counterpart: these are the host-side values the reference's route keeps in Python
+ * (_semantic_route_unified, log_kv_cache.py:3589-3688), read here for diagnostics and tests.
+ */
+LOGKV_API int logkv_read_unified(const logkv_layout_t* layout, int32_t flush_tokens, const void* workspace,
+                                 int32_t* out, int32_t n, void* stream);
+
+/*
  * Copy the near-tie log to out (up to cap entries, in logging order) and the number of entries
  * requested since the log was last cleared to *total (entries beyond the log's 4096-entry
  * capacity are counted but not kept); with clear != 0 the log is emptied after the copy.

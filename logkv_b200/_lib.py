@@ -30,6 +30,10 @@ TIE_KINDS = {1: "attach_cost", 2: "direct", 3: "nearest", 4: "seed_pick", 5: "se
 
 
 ROUTE_ATTACH, ROUTE_UNIFIED = 0, 1   # logkv_layout_t.route (LOGKV_ROUTE_*)
+# Per-lane words of the unified route (logkv_read_unified).
+UNIFIED_WORDS = ("cand_live", "cand_active", "cand_merges", "cand_rounds", "glob_live", "glob_active", "glob_merges",
+                 "glob_rounds", "glob_rows", "old_clusters", "candidates", "cand_exact_form", "glob_exact_form",
+                 "ward_merges", "unused14", "unused15")
 
 
 class Layout(ctypes.Structure):
@@ -116,6 +120,9 @@ def lib() -> ctypes.CDLL:
         handle.logkv_read_counters.restype = ctypes.c_int
         handle.logkv_read_counters.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int32,
                                                ctypes.c_void_p]
+        handle.logkv_read_unified.restype = ctypes.c_int
+        handle.logkv_read_unified.argtypes = [ctypes.POINTER(Layout), ctypes.c_int32, ctypes.c_void_p,
+                                              ctypes.POINTER(ctypes.c_int32), ctypes.c_int32, ctypes.c_void_p]
         P = ctypes.POINTER
         I64 = P(ctypes.c_int64)
         handle.logkv_window_append.restype = ctypes.c_int

@@ -18,6 +18,7 @@ import ctypes
 import math
 import os
 
+import numpy as np
 import torch
 import torch.nn as nn
 
@@ -482,6 +483,20 @@ class LogStructuredKVCache(nn.Module):
                                                   ctypes.c_void_p(_lib.stream_ptr(self.level_k.device))),
                    "logkv_read_counters")
         return dict(zip(_lib.COUNTERS, (int(x) for x in out)))
+
+    def read_unified(self) -> dict:
+        """Unified route: per-(batch, group) lane figures of the last flush (synchronizes): rounds,
+        merges and live counts of the candidate and global passes, candidates, Ward merges."""
+        if not self.semantic_unified_route:
+            raise RuntimeError("read_unified applies to caches with semantic_unified_route=True")
+        n = self.batch_size * self.n_groups * len(_lib.UNIFIED_WORDS)
+        out = (ctypes.c_int32 * n)()
+        _lib.check(_lib.lib().logkv_read_unified(ctypes.byref(self._layout), self.semantic_flush_granularity,
+                                                 ctypes.c_void_p(self._workspace.data_ptr()), out, n,
+                                                 ctypes.c_void_p(_lib.stream_ptr(self.level_k.device))),
+                   "logkv_read_unified")
+        words = np.frombuffer(out, dtype=np.int32).reshape(self.batch_size, self.n_groups, len(_lib.UNIFIED_WORDS))
+        return {name: words[..., i].copy() for i, name in enumerate(_lib.UNIFIED_WORDS) if not name.startswith("unused")}
 
     def read_ties(self, clear: bool = True) -> list[dict]:
         """Near-tie log of this cache's flushes since the last clear (synchronizes).

@@ -1140,6 +1140,23 @@ extern "C" int logkv_read_ties(void* workspace, logkv_tie_t* out, int32_t cap, i
   return (int)e;
 }
 
+extern "C" int logkv_read_unified(const logkv_layout_t* layout, int32_t flush_tokens, const void* workspace,
+                                  int32_t* out, int32_t n, void* stream) {
+  const int v = validate(layout, flush_tokens);
+  if (v != LOGKV_OK) return v;
+  if (!workspace || !out || n < 1) return LOGKV_E_POINTER;
+  if (layout->route != LOGKV_ROUTE_UNIFIED) return LOGKV_E_SHAPE;
+  const Geo g = make_geo(*layout, flush_tokens, layout->recent_capacity);
+  Work w{};
+  carve(g, layout->dtype == LOGKV_DTYPE_BF16 ? 2 : 4, static_cast<char*>(const_cast<void*>(workspace)), &w);
+  const size_t words = (size_t)g.B * g.G * kULaneWords;
+  const size_t m = (size_t)n < words ? (size_t)n : words;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(out, w.u.words, m * sizeof(int32_t), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  return (int)e;
+}
+
 extern "C" int logkv_read_counters(const void* workspace, uint64_t* out, int32_t n, void* stream) {
   if (!out || n < 1) return LOGKV_E_POINTER;
   if (!workspace) {

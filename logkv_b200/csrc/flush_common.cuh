@@ -33,8 +33,8 @@ struct Geo {
 // Unified-route workspace (flush_unified.cuh), per (batch, group) lane; null for the attach route.
 constexpr int kULaneWords = 16;
 enum ULaneWord : int {
-  kUCountC = 0, kUActiveC = 1, kUMergesC = 2,   // candidate pass: live count, active, merges
-  kUCountG = 4, kUActiveG = 5, kUMergesG = 6,   // global pass
+  kUCountC = 0, kUActiveC = 1, kUMergesC = 2, kURoundsC = 3,   // candidate pass: live count, active, merges, rounds
+  kUCountG = 4, kUActiveG = 5, kUMergesG = 6, kURoundsG = 7,   // global pass
   kUGCount = 8, kUOld = 9, kUCand = 10,         // global rows, old clusters, candidates
   kUCdistC = 11, kUCdistG = 12,                 // the pass takes the exact-difference form (tile size <= 32)
   kUWard = 13,                                  // Ward merges of old clusters

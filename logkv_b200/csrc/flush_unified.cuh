@@ -266,9 +266,12 @@ __global__ void __cluster_dims__(logkv_ward::kUCluster, 1, 1) __launch_bounds__(
   logkv_ward::init_lane(l, part, logkv_ward::carve_round(usm, l.M, S).rows, &n_sh);
   cluster.sync();
   const int rounds = 2 * l.M + 7;   // every round but the last merges or pins a pair (a guard)
-  for (int r = 0; r < rounds; ++r)
-    if (!logkv_ward::run_round(cluster, l, usm, S, act, r & 1)) break;
-  if (part == 0 && threadIdx.x == 0 && pass == 1 && *l.stuck) set_status(w.status, kStatusBadCluster);
+  int r = 0;
+  while (r < rounds && logkv_ward::run_round(cluster, l, usm, S, act, r & 1)) ++r;
+  if (part == 0 && threadIdx.x == 0) {
+    uwords(w, bg)[pass ? kURoundsG : kURoundsC] = min(r + 1, rounds);
+    if (pass == 1 && *l.stuck) set_status(w.status, kStatusBadCluster);
+  }
   cluster.sync();   // the leader's flags stay readable until every CTA has read them
 }
 

@@ -53,6 +53,21 @@ def test_workspace_size_and_argument_checks(lib):
     assert lib.logkv_flush(ctypes.byref(layout), None, 2048, 4096, None, 0, None) == -4
 
 
+def test_unified_layout_checks(lib):
+    from logkv_b200 import _lib
+    layout = _lib.Layout(1, 8, 128, 12, 7, 125, 4096, 256, 64, 1, 1, 1.0, 2048.0, 1.0, _lib.ROUTE_UNIFIED, 1)
+    attach = _lib.Layout(1, 8, 128, 12, 7, 125, 4096, 256, 64, 1, 1, 1.0, 2048.0, 1.0)
+    n = lib.logkv_flush_workspace_bytes(ctypes.byref(layout), 2048)
+    # The unified workspace holds each lane's (P + F + K)^2 float32 distances.
+    assert n > lib.logkv_flush_workspace_bytes(ctypes.byref(attach), 2048) + 8 * (256 + 2048 + 12) ** 2 * 4
+    for bad in (_lib.Layout(1, 8, 128, 12, 7, 125, 4096, 256, 64, 1, 1, 1.0, 2048.0, 1.0, 2, 1),   # unknown route
+                _lib.Layout(1, 8, 128, 12, 7, 125, 4096, 256, 64, 1, 1, 1.0, 2048.0, 1.0, 1, 0),   # passes < 1
+                _lib.Layout(1, 8, 128, 12, 7, 125, 8192, 256, 64, 1, 1, 1.0, 2048.0, 1.0, 1, 1)):  # rows > 4096
+        assert lib.logkv_flush_workspace_bytes(ctypes.byref(bad), 4096 if bad.recent_capacity == 8192 else 2048) == 0
+    out = (ctypes.c_int32 * 16)()
+    assert lib.logkv_read_unified(ctypes.byref(attach), 2048, None, out, 16, None) == -4
+
+
 def test_attention_argument_checks(lib):
     from logkv_b200 import _lib
     layout = _lib.Layout(1, 8, 128, 12, 7, 125, 4096, 256, 64, 1, 1, 1.0, 2048.0, 1.0)
