@@ -545,8 +545,42 @@ static TapeSegs tape_segments(const Geo& g, const logkv_state_t& s, const Work& 
 
 // ---------------------------------------------------------------- unified route launches
 static size_t unified_gram_smem(const Geo& g) { return 2 * (size_t)g.D * kGramTile * 4 + 2 * (size_t)kGramTile * 4; }
+// Every CTA of a reduction cluster holds the round's tables; sized for the smallest cluster (2).
 static size_t unified_round_smem(const Geo& g) {
-  return logkv_ward::round_smem_bytes(g.Mg, logkv_ward::sort_width(g.Mg));
+  return logkv_ward::round_smem_bytes(g.Mg, logkv_ward::sort_width(g.Mg), 2);
+}
+// CTAs per lane of the reductions: one lane per cluster and one CTA per SM (the round's shared
+// memory), so larger clusters shorten a lane's rounds while smaller ones fit more lanes at once:
+// 8 while the lanes fit on the SMs in one wave of 8-CTA clusters (15 lanes), else 4 (measured at
+// 32 lanes and D = 128: 10.5 ms per pass pair with 8, 7.0 with 4, 9.0 with 2).
+static int unified_cluster(const Geo& g) {
+  const int lanes = g.B * g.G;
+  const char* env = getenv("LOGKV_UNIFIED_CLUSTER");
+  if (env) {
+    const int v = atoi(env);
+    if (v == 2 || v == 4 || v == 8) return v;
+  }
+  return lanes <= 15 ? 8 : 4;
+}
+// A cluster launch that also carries the programmatic dependency on the previous kernel.
+template <typename... KArgs, typename... Args>
+static void launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                               int cluster_x, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  cudaLaunchKernelEx(&cfg, kern, args...);
 }
 static int unified_sort_cap(const Geo& g) {
   int p = 2;
@@ -577,7 +611,7 @@ static void launch_ward(const Geo& g, const logkv_state_t& s, const Work& w, cud
 template <typename T>
 static void launch_unified(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st) {
   const int lanes = g.B * g.G, tiles = (g.Mg + kGramTile - 1) / kGramTile;
-  const int S = logkv_ward::sort_width(g.Mg);
+  const int S = logkv_ward::sort_width(g.Mg), CL = unified_cluster(g);
   const size_t gram = unified_gram_smem(g), round = unified_round_smem(g);
   const size_t lab = 3 * (size_t)g.NW * 4, rte = 3 * (size_t)g.Mg * 4, tile = (size_t)g.B * 4;
   smem_limit(unified_dist_kernel, gram);
@@ -591,8 +625,7 @@ static void launch_unified(const Geo& g, const logkv_state_t& s, const Work& w, 
     if (pass == 0) launch_pdl(unified_load_kernel<T>, dim3(per, g.G, g.B), 256, 0, st, g, s, w);
     launch_pdl(unified_tile_kernel, dim3(1), 1024, tile, st, g, w, pass);
     launch_pdl(unified_dist_kernel, dim3(tiles, tiles, lanes), 256, gram, st, g, w, pass);
-    launch_pdl(unified_reduce_kernel, dim3(lanes * logkv_ward::kUCluster), logkv_ward::kUThreads, round, st, g, w,
-               pass, S);
+    launch_pdl_cluster(unified_reduce_kernel, dim3(lanes * CL), logkv_ward::kUThreads, round, st, CL, g, w, pass, S);
     if (pass == 0) launch_pdl(unified_labels_kernel, dim3(g.G, g.B), 1024, lab, st, g, s, w);
   }
   launch_pdl(unified_route_kernel, dim3(g.G, g.B), 1024, rte, st, g, s, w);

@@ -60,6 +60,7 @@ __device__ inline logkv_ward::RunLane urun(const Geo& g, const Work& w, size_t b
   l.D = g.D;
   l.target = pass ? g.K : 1;
   l.passes = pass ? g.passes : 1;
+  l.cost_order = 0;
   return l;
 }
 
@@ -241,17 +242,17 @@ __global__ void __launch_bounds__(256) unified_dist_kernel(Geo g, Work w, int pa
 }
 
 // ---------------------------------------------------------------- U3: the rounds of one pass
-// Every round of one lane in one launch, on a cluster of kUCluster CTAs (unified_core.cuh), until
-// the lane has no proposal left or reaches its target.  Grid (B*G * kUCluster) x 1024.
-__global__ void __cluster_dims__(logkv_ward::kUCluster, 1, 1) __launch_bounds__(logkv_ward::kUThreads)
-    unified_reduce_kernel(Geo g, Work w, int pass, int S) {
+// Every round of one lane in one launch, on a cluster of CL CTAs (unified_core.cuh; the cluster
+// size is the launch's), until the lane has no proposal left or reaches its target.
+// Grid (B*G * CL) x 1024.
+__global__ void __launch_bounds__(logkv_ward::kUThreads) unified_reduce_kernel(Geo g, Work w, int pass, int S) {
   pdl_entry();
   namespace cg = cooperative_groups;
   extern __shared__ __align__(16) unsigned char usm[];
   __shared__ int act[2], n_sh;
   cg::cluster_group cluster = cg::this_cluster();
-  const int part = (int)cluster.block_rank();
-  const size_t bg = blockIdx.x / logkv_ward::kUCluster;
+  const int part = (int)cluster.block_rank(), CL = (int)cluster.num_blocks();
+  const size_t bg = blockIdx.x / CL;
   const int b = (int)(bg / g.G);
   const int n = upass_rows(g, w, bg, b, pass);
   const logkv_ward::RunLane l = urun(g, w, bg, pass);
@@ -263,7 +264,7 @@ __global__ void __cluster_dims__(logkv_ward::kUCluster, 1, 1) __launch_bounds__(
     *l.stuck = 0;
   }
   cluster.sync();
-  logkv_ward::init_lane(l, part, logkv_ward::carve_round(usm, l.M, S).rows, &n_sh);
+  logkv_ward::init_lane(l, part, CL, logkv_ward::carve_round(usm, l.M, S, CL).rows, &n_sh);
   cluster.sync();
   const int rounds = 2 * l.M + 7;   // every round but the last merges or pins a pair (a guard)
   int r = 0;

@@ -66,6 +66,7 @@ __device__ RunLane lane_of(const logkv_unified_t& u, int lane) {
   l.D = u.dim;
   l.target = u.target;
   l.passes = 1;
+  l.cost_order = 1;
   return l;
 }
 
@@ -80,7 +81,7 @@ __global__ void __launch_bounds__(kThreads) init_kernel(logkv_unified_t u) {
     *l.merges = 0;
     *l.stuck = 0;
   }
-  init_lane(l, part, rows, &n);
+  init_lane(l, part, kCluster, rows, &n);
 }
 
 // One round of one lane on a cluster of kCluster CTAs.
@@ -135,7 +136,7 @@ extern "C" int logkv_unified_step(const logkv_unified_t* u, void* stream) {
   const int v = check_unified(u);
   if (v) return v;
   const int S = sort_width(u->size);   // at most size / 2 disjoint pairs are sorted
-  const size_t smem = round_smem_bytes(u->size, S);
+  const size_t smem = round_smem_bytes(u->size, S, kCluster);
   if (smem > 227 * 1024) return LOGKV_UNIFIED_E_SHAPE;
   if (smem > 48 * 1024) cudaFuncSetAttribute(round_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   cudaLaunchConfig_t cfg = {};

@@ -11,7 +11,7 @@
 // reference writes it (the including translation units are compiled without fused
 // multiply-adds); the exact squared distance of a candidate pair sums the features left to right.
 //
-// A cluster of kUCluster CTAs runs one round of one lane: the leader selects the pairs, all CTAs
+// A cluster of 2 to kUCluster CTAs runs one round of one lane: the leader selects the pairs, all CTAs
 // share the centre, Lance-Williams and rescan work; within a round every merge writes only its
 // own row and column, which no other merge of the round reads.
 #pragma once
@@ -25,7 +25,7 @@ namespace logkv_ward {
 namespace cg = cooperative_groups;
 
 constexpr int kUThreads = 1024;
-constexpr int kUCluster = 8;        // CTAs per lane (one thread-block cluster)
+constexpr int kUCluster = 8;        // most CTAs per lane (one thread-block cluster)
 constexpr int kUMaxSize = 4096;     // rows per lane (the pair sort runs in shared memory)
 constexpr long long kInfKey = 0x7F800000LL << 32;
 
@@ -59,6 +59,17 @@ __device__ __forceinline__ float pair_cost(float d2, float mi, float mj, float r
   return valid ? fmul(d2, fdiv(fmul(mi, mj), denom)) : __int_as_float(0x7F800000);
 }
 
+// A lower bound of pair_cost's finite value from a fast division: __fdividef is within 2 ulp of
+// the quotient (denominators here lie in [1, 2^126]), so the bound is below the exact cost by at
+// most ~4 ulp, and 2^-18 of slack covers it; tiny costs are never bounded (0 returned).  A pair
+// whose bound exceeds a known key's cost cannot have the smaller key (keys order by cost bits
+// first), so its exact evaluation can be skipped.
+__device__ __forceinline__ float cost_lower_bound(float d2, float mi, float mj) {
+  const float approx = __fmul_rn(d2, __fdividef(__fmul_rn(mi, mj), fmaxf(__fadd_rn(mi, mj), 1.f)));
+  return approx > 1e-30f ? __fmul_rn(approx, 0.999996f) : 0.f;
+}
+__device__ __forceinline__ float key_cost(long long key) { return __int_as_float((int)(key >> 32)); }
+
 // One lane's device state.  Rows are [0, M); the live count, merge count, flags and trace are
 // this lane's own words.
 struct RunLane {
@@ -74,8 +85,10 @@ struct RunLane {
   int* active;           // lane still active after the last round
   int* merges;           // merges so far (= trace rows)
   uint8_t* stuck;        // a round had no proposal while above target
-  int* trace;            // [M, 2] merge pairs in round then (cost, left) order
+  int* trace;            // [M, 2] merge pairs in round order; within a round in (cost, left) order,
+                         // or in row order when `cost_order` is 0 and the budget takes every pair
   int M, D, target, passes;
+  int cost_order;        // sort every round's pairs by cost (the operator API's trace contract)
 };
 
 // out[r] = min over columns of the row's packed keys; one warp per row.  Only live columns
@@ -106,7 +119,7 @@ __device__ inline void scan_rows(const RunLane& l, const int* rows, int nrows, c
       }
 #pragma unroll
       for (int j = 0; j < kBatch; ++j) {
-        if (cv[j] < 0) continue;
+        if (cv[j] < 0 || cost_lower_bound(dv[j], mr, mv[j]) > key_cost(best)) continue;
         const float cost = pair_cost(dv[j], mr, mv[j], rr, rv[j], l.limit, cv[j] != r);
         best = min(best, pack_key(cost, (long long)(r ^ cv[j])));
       }
@@ -118,13 +131,13 @@ __device__ inline void scan_rows(const RunLane& l, const int* rows, int nrows, c
 }
 
 // Every live row's minimum, at the lane's start; the rows are split over the cluster's CTAs
-// (row r on CTA r % kUCluster).  `rows` is an [M] int scratch of this CTA, n_sh a shared int.
-__device__ inline void init_lane(const RunLane& l, int part, int* rows, int* n_sh) {
+// (row r on CTA r % CL).  `rows` is an [M] int scratch of this CTA, n_sh a shared int.
+__device__ inline void init_lane(const RunLane& l, int part, int CL, int* rows, int* n_sh) {
   const int M = l.M;
   const int count = *l.count;
   if (threadIdx.x == 0) *n_sh = 0;
   __syncthreads();
-  for (int r = part + kUCluster * (int)threadIdx.x; r < M; r += kUCluster * blockDim.x) {
+  for (int r = part + CL * (int)threadIdx.x; r < M; r += CL * blockDim.x) {
     const bool live = r < count;
     l.alive[r] = live;
     l.radius[r] = 0.f;
@@ -154,11 +167,12 @@ struct RoundSmem {
   uint8_t* flags;          // [M] 1 valid, 2 rejected, 4 keep, 8 merged, 16 matched (sweeps), 32 sweep pair
 };
 
-__host__ __device__ inline int column_width(int M) { return ((M + kUCluster - 1) / kUCluster + 31) / 32 * 32; }
+// Live columns per CTA of a cluster of CL, in whole warps.
+__host__ __device__ inline int column_width(int M, int CL) { return ((M + CL - 1) / CL + 31) / 32 * 32; }
 
-__host__ __device__ inline size_t round_smem_bytes(int M, int S) {
+__host__ __device__ inline size_t round_smem_bytes(int M, int S, int CL) {
   const size_t half = (size_t)M / 2 + 1;
-  return (size_t)S * 8 + half * 8 + (size_t)column_width(M) * 8 + (size_t)M * 4 * 3 + half * 4 +
+  return (size_t)S * 8 + half * 8 + (size_t)column_width(M, CL) * 8 + (size_t)M * 4 * 3 + half * 4 +
          (size_t)M * 4 * 7 + (size_t)M + 16;
 }
 
@@ -169,7 +183,7 @@ __host__ __device__ inline int sort_width(int M) {
   return p;
 }
 
-__device__ inline RoundSmem carve_round(void* base, int M, int S) {
+__device__ inline RoundSmem carve_round(void* base, int M, int S, int CL) {
   RoundSmem r;
   char* p = static_cast<char*>(base);
   const size_t half = (size_t)M / 2 + 1;
@@ -178,7 +192,7 @@ __device__ inline RoundSmem carve_round(void* base, int M, int S) {
   r.rowmin = reinterpret_cast<long long*>(p);
   p += half * 8;
   r.colmin = reinterpret_cast<long long*>(p);
-  p += (size_t)column_width(M) * 8;
+  p += (size_t)column_width(M, CL) * 8;
   r.best = reinterpret_cast<int*>(p);
   p += (size_t)M * 4;
   r.partner = reinterpret_cast<int*>(p);
@@ -325,18 +339,46 @@ __device__ inline bool select_pairs(const RunLane& l, const RoundSmem& sm, int* 
   int extra = 0;
   const bool swept = l.passes > 1 && l.restricted;
   if (swept) extra = sweeps(l, sm);
-  // Valid pairs (a row each, below its partner; finite costs), compacted, then a bitonic sort of
-  // (cost bits << 32 | row): the reference's stable argsort by cost.  A sweep pair sorts by its
-  // restricted cost.
-  for (int r = tid; r < M; r += nt) {
-    const uint8_t f = sm.flags[r];
-    if (f & 1) sm.sk[atomicAdd(&nvalid, 1)] = ((unsigned long long)(l.packed[r] >> 32) << 32) | (unsigned)r;
-    else if (f & 32) sm.sk[atomicAdd(&nvalid, 1)] = ((unsigned long long)(l.restricted[r] >> 32) << 32) | (unsigned)r;
+  // Valid pairs (a row each, below its partner; finite costs) as (cost bits << 32 | row), in row
+  // order; a sweep pair carries its restricted cost.  The reference takes them in stable cost
+  // order up to the budget; when the budget takes them all, the order within the round changes
+  // nothing (the round's pairs are disjoint), so the sort runs only when the budget cuts.
+  {
+    const int per = (M + nt - 1) / nt, lo = min(M, tid * per), hi = min(M, lo + per);
+    int cnt = 0;
+    for (int r = lo; r < hi; ++r) cnt += (sm.flags[r] & (1 | 32)) != 0;
+    __shared__ int ws[kUThreads / 32];
+    int incl = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, off);
+      if ((tid & 31) >= off) incl += v;
+    }
+    if ((tid & 31) == 31) ws[tid >> 5] = incl;
+    __syncthreads();
+    if (tid < 32) {
+      int w = tid < nt / 32 ? ws[tid] : 0;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, w, off);
+        if (tid >= off) w += v;
+      }
+      if (tid < nt / 32) ws[tid] = w;
+      if (tid == 31) nvalid = w;
+    }
+    __syncthreads();
+    int at = incl - cnt + ((tid >> 5) ? ws[(tid >> 5) - 1] : 0);
+    for (int r = lo; r < hi; ++r) {
+      const uint8_t f = sm.flags[r];
+      if (f & 1) sm.sk[at++] = ((unsigned long long)(l.packed[r] >> 32) << 32) | (unsigned)r;
+      else if (f & 32) sm.sk[at++] = ((unsigned long long)(l.restricted[r] >> 32) << 32) | (unsigned)r;
+    }
   }
   __syncthreads();
   const int nv = nvalid;
+  const bool cut = l.cost_order || nv > M / 2 || nv > *l.count - l.target;
   int S = 1;
-  while (S < nv) S <<= 1;
+  while (cut && S < nv) S <<= 1;
   for (int i = nv + tid; i < S; i += nt) sm.sk[i] = ~0ull;
   __syncthreads();
   for (int k = 2; k <= S; k <<= 1) {
@@ -412,9 +454,9 @@ __device__ inline bool select_pairs(const RunLane& l, const RoundSmem& sm, int* 
 // `act`, which the next round's other word keeps from being overwritten before every CTA read it.
 __device__ inline bool run_round(cg::cluster_group& cluster, const RunLane& l, void* smem_raw, int S, int* act,
                                  int parity) {
-  const int part = (int)cluster.block_rank();
+  const int part = (int)cluster.block_rank(), CL = (int)cluster.num_blocks();
   const int M = l.M, D = l.D, tid = threadIdx.x, nt = blockDim.x;
-  const RoundSmem sm = carve_round(smem_raw, M, S);
+  const RoundSmem sm = carve_round(smem_raw, M, S, CL);
   __shared__ int n_ok_s, ndirty;
   if (part == 0) {
     int n_ok;
@@ -427,7 +469,7 @@ __device__ inline bool run_round(cg::cluster_group& cluster, const RunLane& l, v
   cluster.sync();
   // ---- the round's tables, from the leader
   if (part != 0) {
-    const RoundSmem lead = carve_round(cluster.map_shared_rank(smem_raw, 0), M, S);
+    const RoundSmem lead = carve_round(cluster.map_shared_rank(smem_raw, 0), M, S, CL);
     if (tid == 0) n_ok_s = *cluster.map_shared_rank(&n_ok_s, 0);
     for (int r = tid; r < M; r += nt) {
       sm.best[r] = lead.best[r];
@@ -445,9 +487,9 @@ __device__ inline bool run_round(cg::cluster_group& cluster, const RunLane& l, v
   if (tid == 0) ndirty = 0;
   __syncthreads();
   const int n_ok = n_ok_s;
-  // ---- merged centres: merge m goes to CTA m % kUCluster
-  for (int item = tid; item < ((n_ok - part + kUCluster - 1) / kUCluster) * D; item += nt) {
-    const int m = part + kUCluster * (item / D), d = item % D;
+  // ---- merged centres: merge m goes to CTA m % CL
+  for (int item = tid; item < ((n_ok - part + CL - 1) / CL) * D; item += nt) {
+    const int m = part + CL * (item / D), d = item % D;
     const int a = sm.pairs[m], b = sm.partner[a];
     const float ma = sm.pma[a], mb = sm.pmb[a];
     const float total = fadd(ma, mb);
@@ -488,7 +530,7 @@ __device__ inline bool run_round(cg::cluster_group& cluster, const RunLane& l, v
   const int ncols = ncols_s;
   // ---- Lance-Williams: this CTA's share [k0, k0 + CW) of the live columns, every merged row,
   // as warp tasks of (merge, 32 columns); a merge's scalars were computed once by the leader.
-  const int CW = column_width(ncols), k0 = part * CW;
+  const int CW = column_width(ncols, CL), k0 = part * CW;
   for (int i = tid; i < n_ok; i += nt) sm.rowmin[i] = kInfKey;
   for (int i = tid; i < CW; i += nt) sm.colmin[i] = 0x7FFFFFFFFFFFFFFFLL;
   __syncthreads();
@@ -503,7 +545,7 @@ __device__ inline bool run_round(cg::cluster_group& cluster, const RunLane& l, v
     const float* rowa = l.dist + (size_t)a * M;
     const float* rowb = l.dist + (size_t)b * M;
     int cv[kChunks];
-    float xaa[kChunks], xba[kChunks], mc[kChunks], rc[kChunks];
+    float xaa[kChunks], xba[kChunks], mc[kChunks], rc[kChunks], pc[kChunks];
 #pragma unroll
     for (int j = 0; j < kChunks; ++j) {
       const int k = k0 + (g0 + j) * 32 + lanew;
@@ -513,6 +555,7 @@ __device__ inline bool run_round(cg::cluster_group& cluster, const RunLane& l, v
       xba[j] = rowb[c];
       mc[j] = l.mass[c];
       rc[j] = l.radius[c];
+      pc[j] = key_cost(l.packed[c]);
     }
     long long rkey = kInfKey;
 #pragma unroll
@@ -542,6 +585,10 @@ __device__ inline bool run_round(cg::cluster_group& cluster, const RunLane& l, v
       if (c == a) nv = 0.f;
       if (!keep_c) l.dist[(size_t)c * M + a] = nv;
       l.dist[(size_t)a * M + c] = nv;
+      // The key matters only if it can lower the row's minimum or (a column that is not a merged
+      // row) the column's current one; a column whose minimum went stale is rescanned anyway.
+      const float lb = cost_lower_bound(nv, total, mc[j]);
+      if (lb > key_cost(rkey) && (keep_c || lb > pc[j])) continue;
       const float cost = pair_cost(nv, total, mc[j], ra, rc[j], l.limit, c != a);
       const long long key = pack_key(cost, (long long)(a ^ c));
       if (cost < __int_as_float(0x7F800000) && !keep_c) atomicMin(&sm.colmin[(g0 + j) * 32 + lanew], key);
@@ -559,15 +606,15 @@ __device__ inline bool run_round(cg::cluster_group& cluster, const RunLane& l, v
     if (!(sm.flags[c] & 4) && sm.colmin[kl] < l.packed[c]) l.packed[c] = sm.colmin[kl];
   }
   cluster.sync();
-  // ---- merged rows: minimum over every CTA's columns (merge m on CTA m % kUCluster)
-  for (int m = part + kUCluster * tid; m < n_ok; m += kUCluster * nt) {
+  // ---- merged rows: minimum over every CTA's columns (merge m on CTA m % CL)
+  for (int m = part + CL * tid; m < n_ok; m += CL * nt) {
     long long v = sm.rowmin[m];
-    for (int r = 1; r < kUCluster; ++r)
-      v = min(v, cluster.map_shared_rank(sm.rowmin, (part + r) % kUCluster)[m]);
+    for (int r = 1; r < CL; ++r)
+      v = min(v, cluster.map_shared_rank(sm.rowmin, (part + r) % CL)[m]);
     l.packed[sm.pairs[m]] = v;
   }
-  // ---- rows whose best partner merged (or that were rejected) rescan; row r on CTA r % kUCluster
-  for (int r = part + kUCluster * tid; r < M; r += kUCluster * nt) {
+  // ---- rows whose best partner merged (or that were rejected) rescan; row r on CTA r % CL
+  for (int r = part + CL * tid; r < M; r += CL * nt) {
     const uint8_t f = sm.flags[r];
     if (l.alive[r] && !(f & 4) && ((sm.flags[sm.best[r]] & 8) || (f & 2))) sm.rows[atomicAdd(&ndirty, 1)] = r;
   }
