@@ -461,101 +461,129 @@ def bench_flush_attend(args, rank, world, local_rank, inputs):
 
 
 # ---------------------------------------------------------------------------------------------- unified route
-UNIFIED = dict(workload="unified (Ward) route passes, BASELINE configs[4] shapes: 16 lanes of one flush tile, "
-                        "2060 points each (2048 flushed + exact pool remainder + centres), 48-component mixture",
-               lanes=16, points=2060, head_dim=128, components=48, orphan_frac=0.10, target=12)
+UNIFIED = dict(workload="unified (Ward / radius) route flush, BASELINE configs[4]: 256 streams of 65536 tokens "
+                        "batch-sharded over 8 ranks (32 per rank), 8 KV groups, head dim 128, bf16 K/V, K=12, B=128, "
+                        "recent 2048 flushed 2048 at a time, exact pool 256 (span cap 64), Beta on; keys from a "
+                        "48-component mixture per stream and group (sigma ~ U[0.1, 0.6], 10% orphans)",
+               streams_per_rank=32, groups=8, head_dim=128, clusters=12, B=128, recent=2048, granularity=2048,
+               exact=256, span_cap=64, max_seq=65536, components=48, orphan_frac=0.10)
 
 
-def unified_points(torch, cfg, device, seed):
-    """[lanes, points, D] float32 keys: a 48-component mixture (sigma_j ~ U[0.1, 0.6]) with 10 % orphans."""
-    L, M, D, C = cfg["lanes"], cfg["points"], cfg["head_dim"], cfg["components"]
-    gen = torch.Generator(device=device).manual_seed(seed)
-    centres = torch.randn(L, C, D, generator=gen, device=device) * 2.0
-    sigma = torch.rand(L, C, generator=gen, device=device) * 0.5 + 0.1
-    z = torch.randint(0, C, (L, M), generator=gen, device=device)
-    lane = torch.arange(L, device=device)[:, None]
-    x = centres[lane, z] + sigma[lane, z][..., None] * torch.randn(L, M, D, generator=gen, device=device)
-    orphan = torch.rand(L, M, generator=gen, device=device) < cfg["orphan_frac"]
-    u = torch.randn(L, M, D, generator=gen, device=device)
-    u = u / u.norm(dim=-1, keepdim=True) * (4 * 0.35 * D ** 0.5)
-    return torch.where(orphan[..., None], centres[lane, z] + u, x).contiguous()
+def unified_reference_timing():
+    """The reference's own CPU unified flush at this shape, timed in the build container
+    (tests/golden/time_unified_reference.py writes tests/golden/unified_timing.json)."""
+    path = os.path.join(ROOT, "tests", "golden", "unified_timing.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as fh:
+        t = json.load(fh)
+    return {"s_per_stream_flush": round(statistics.median(t["flush_s"]), 3), "threads": t["threads"],
+            "flushes": len(t["flush_s"]), "where": "build container CPU (the reference is not on the GPU box)",
+            "kind": "reference"}
 
 
 def bench_unified(args, rank, world, local_rank):
-    """The unified route's two reductions per flush tile, as the reference runs them
-    (log_kv_cache.py:3185-3376, :3589-3688): FP32 Gram (cuBLAS, highest precision) + fused pair
-    distances, then UnifiedReduce rounds with the host polling (active, live) every four rounds.
-    First the radius-limited candidate pass over the tile's points (to one cluster per radius),
-    then the global pass to K = 12 over each lane's 12 old centres (weight 128) followed by the
-    candidate centres (weights = their merged masses), padded to the widest lane."""
+    """Unified-route flushes of this rank's streams (batch-sharded: no collective).
+    Chunk 0 fills each stream's window, --warmup flushes run untimed, then --steps flushes are timed
+    with CUDA events around add_recent (inputs already on the device; each chunk is 2048 fresh
+    tokens per stream).  Per-lane pass figures come from cache.read_unified()."""
     import torch
     import torch.distributed as dist
-    from logkv_b200.plugin import UnifiedReduce, pair_distances
-    device = torch.device("cuda", local_rank)
+    from logkv_b200._lib import FLUSH_STAGES
+    from logkv_b200.cache import LogStructuredKVCache
+    from logkv_b200.workload import rope_tables
     cfg = UNIFIED
-    L, M, D, K = cfg["lanes"], cfg["points"], cfg["head_dim"], cfg["target"]
-    mu0 = unified_points(torch, cfg, device, seed=900 + rank)
-    gen = torch.Generator(device=device).manual_seed(950 + rank)
-    old_mu = torch.randn(L, K, D, generator=gen, device=device) * 2.0
-    limits = torch.full((L,), 1.2 * 0.35 * D ** 0.5, device=device)
-    stream = torch.cuda.Stream(device)
-    torch.cuda.synchronize()   # inputs were written on the default stream
-    prec = torch.get_float32_matmul_precision()
-    torch.set_float32_matmul_precision("highest")
+    S, G, D, T = cfg["streams_per_rank"], cfg["groups"], cfg["head_dim"], cfg["granularity"]
+    device = torch.device("cuda", local_rank)
+    cos, sin = rope_tables(cfg["max_seq"] + 64, D)
+    cache = LogStructuredKVCache(
+        (S, G, cfg["max_seq"], D), (S, G, cfg["max_seq"], D), B=cfg["B"], recent_size=cfg["recent"], device=device,
+        dtype=torch.bfloat16, semantic_clusters=True, cluster_k_max=cfg["clusters"], semantic_anchor_mode="mid",
+        semantic_flush_granularity=T, allocate_second_order=False, alpha_exact_tokens=cfg["exact"],
+        alpha_span_max_tokens=cfg["span_cap"], beta_novelty=True, beta_adaptive_merge=True,
+        cos_cache=torch.from_numpy(cos), sin_cache=torch.from_numpy(sin), rope_n_elem=D, semantic_unified_route=True)
+    gen = torch.Generator(device=device).manual_seed(7000 + rank)
+    C = cfg["components"]
+    centres = torch.randn(S, G, C, D, generator=gen, device=device)
+    sigma = torch.rand(S, G, C, generator=gen, device=device) * 0.5 + 0.1
+    si = torch.arange(S, device=device)[:, None, None]
+    gi = torch.arange(G, device=device)[None, :, None]
+    cos_d, sin_d = torch.from_numpy(cos).to(device), torch.from_numpy(sin).to(device)
+    ends = (torch.arange(T) % 23 == 22).expand(S, T)
+    ends_dev = ends.to(device, torch.uint8).contiguous()
+    ends_host = ends.tolist()
 
-    def one_pass(mu, mass, count, lim, target):
-        centred = mu - mu[:, :1]
-        norm = centred.square().sum(-1)
-        dist_ = pair_distances(torch.bmm(centred, centred.transpose(1, 2)), norm)
-        red = UnifiedReduce(dist_, mu, mass, count, lim, target)
-        rounds = 0
-        for r in range(1, 2 * mu.size(1) + 8):
-            red.step(r)
-            rounds = r
-            if r % 4 == 0 and not bool(red.status[0].any()):
-                break
-        traces, alive, stuck = red.finish()
-        return rounds, alive
+    def chunk(c):
+        z = torch.randint(0, C, (S, G, T), generator=gen, device=device)
+        base, sig = centres[si, gi, z], sigma[si, gi, z][..., None]
+        x = base + sig * torch.randn(S, G, T, D, generator=gen, device=device)
+        u = torch.randn(S, G, T, D, generator=gen, device=device)
+        u = u / u.norm(dim=-1, keepdim=True)
+        orphan = torch.rand(S, G, T, generator=gen, device=device) < cfg["orphan_frac"]
+        kr = torch.where(orphan[..., None], base + u * (4.0 * sig * D ** 0.5), x)
+        pos = torch.arange(c * T, (c + 1) * T, device=device)
+        half = D // 2
+        rot = torch.cat([-kr[..., half:], kr[..., :half]], dim=-1)
+        k = kr * cos_d[pos] + rot * sin_d[pos]
+        v = torch.randn(S, G, T, D, generator=gen, device=device)
+        return k.to(torch.bfloat16), kr.to(torch.bfloat16), v.to(torch.bfloat16)
 
-    def route():
-        mu = mu0.clone()
-        mass = torch.ones(L, M, device=device)
-        count = torch.full((L,), M, dtype=torch.int64, device=device)
-        e = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
-        e[0].record(stream)
-        r1, alive = one_pass(mu, mass, count, limits, 1)
-        e[1].record(stream)
-        # Global pass input: old centres, then the candidate centres of each lane, padded.
-        keep = torch.from_numpy(alive).to(device)
-        n_new = keep.sum(1)
-        size = K + int(n_new.max())
-        order = torch.argsort((~keep).to(torch.int8), dim=1, stable=True)[:, :size - K]
-        mu2 = torch.zeros(L, size, D, device=device)
-        mass2 = torch.zeros(L, size, device=device)
-        mu2[:, :K] = old_mu
-        mass2[:, :K] = 128.0
-        mu2[:, K:] = torch.gather(mu, 1, order[..., None].expand(-1, -1, D))
-        valid = torch.arange(size - K, device=device)[None, :] < n_new[:, None]
-        mass2[:, K:] = torch.where(valid, torch.gather(mass, 1, order), 0.0)
-        r2, _ = one_pass(mu2, mass2, K + n_new, None, K)
-        e[2].record(stream)
+    nstage = len(FLUSH_STAGES)
+    stage_ms = [0.0] * nstage
+    total_ms, figures = [], []
+    warm = max(1, args.warmup)
+    for c in range(1 + warm + args.steps):
+        k, kr, v = chunk(c)
+        timed = c > warm
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(nstage + 1)] if timed else None
+        for e in evs or []:
+            e.record()
         torch.cuda.synchronize()
-        return e[0].elapsed_time(e[1]), e[1].elapsed_time(e[2]), r1, r2, size
-
-    with torch.no_grad(), torch.cuda.stream(stream):
-        runs = [route() for _ in range(max(3, args.warmup) + max(3, args.steps))][max(3, args.warmup):]
-    torch.set_float32_matmul_precision(prec)
-    t = torch.tensor([statistics.median(r[0] for r in runs), statistics.median(r[1] for r in runs)], device=device)
+        cache.profile_events = evs
+        cache.add_recent(k, v, k_raw=kr, span_ends=ends_host, span_ends_device=ends_dev)
+        cache.profile_events = None
+        torch.cuda.synchronize()
+        if timed:
+            total_ms.append(evs[0].elapsed_time(evs[-1]))
+            for i in range(nstage):
+                stage_ms[i] += evs[i].elapsed_time(evs[i + 1])
+            figures.append(cache.read_unified())
+    status = cache.read_status()
+    t = torch.tensor([sum(total_ms) / len(total_ms)], device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    c_us, g_us = t[0].item() * 1000.0, t[1].item() * 1000.0
-    _, _, r1, r2, size = runs[-1]
-    return {"metric": "unified route us per flush tile (16 lanes x 2060 points, both passes)", "unit": "us",
-            "value": round(c_us + g_us, 1),
-            "passes": {"candidate_pass": {"us": round(c_us, 1), "rounds": r1, "points": M},
-                       "global_pass": {"us": round(g_us, 1), "rounds": r2, "points": size}},
-            "config": {k: v for k, v in cfg.items()} | {"radius_limit": round(float(limits[0]), 3),
-                                                        "l2": "16 x 2060^2 float32 distances = 272 MB > L2"}}
+    ms = float(t.item())
+    n = len(total_ms)
+    route_ms = stage_ms[FLUSH_STAGES.index("seed_plan")] / n
+    lanes = S * G
+    mean = lambda key: round(float(sum(f[key].mean() for f in figures) / n), 1)  # noqa: E731
+    rows_c = sum(float((f["cand_live"] + f["cand_merges"]).astype("float64").mean()) for f in figures) / n
+    rows_g = mean("glob_rows")
+    # Pair-matrix work per flush: every lane's two passes (upper-triangle Gram products, 2 flops each).
+    gram_flop = lanes * D * (rows_c * (rows_c + 1) + rows_g * (rows_g + 1))
+    dist_bytes = lanes * 4 * 2 * (rows_c ** 2 + rows_g ** 2)   # each matrix written once, read once by the first scan
+    peak, kind = measured_peaks()
+    ref = unified_reference_timing()
+    out = {"metric": "unified-route flush ms per 2048-token chunk of this rank's streams (32 streams x 8 groups)",
+           "unit": "ms", "value": round(ms, 3), "higher_is_better": False, "scaling": "weak",
+           "tokens_per_s": round(S * world * T / (ms * 1e-3), 1),
+           "us_per_lane_flush": round(ms * 1000.0 / lanes, 2), "status": status,
+           "stages_ms": {name: round(stage_ms[i] / n, 3) for i, name in enumerate(FLUSH_STAGES)},
+           "route_ms": round(route_ms, 3),
+           "passes": {"candidate_rows": round(rows_c, 1), "candidate_rounds": mean("cand_rounds"),
+                      "candidates": mean("candidates"), "global_rows": rows_g, "global_rounds": mean("glob_rounds"),
+                      "ward_merges_per_flush": round(sum(float(f["ward_merges"].sum()) for f in figures) / n, 2)},
+           "pair_matrix": {"gram_gflop_per_flush": round(gram_flop / 1e9, 2),
+                           "dist_bytes_per_flush": int(dist_bytes),
+                           "route_stage_dist_gbs": round(dist_bytes / (route_ms * 1e-3) / 1e9, 1),
+                           "route_stage_dist_frac": round(dist_bytes / (route_ms * 1e-3) / 1e9 / peak, 4),
+                           "peak_gbs": peak, "peak_kind": kind},
+           "config": {k: v for k, v in cfg.items()} | {"flushes_timed": n, "ranks": world, "lanes_per_rank": lanes}}
+    if ref is not None:
+        out["cpu_reference"] = ref | {"ratio_per_stream": round(ref["s_per_stream_flush"] * 1000.0 / (ms / S), 1)}
+    del cache
+    torch.cuda.empty_cache()
+    return out
 
 
 # ---------------------------------------------------------------------------------------------- KV-head sharded

@@ -72,3 +72,31 @@ def boundary_pattern(rng: np.random.Generator, rows: int, tokens: int, kind: str
         row = (np.arange(tokens) % 3) == 2
         return np.broadcast_to(row, (rows, tokens)).copy()
     return rng.random((rows, tokens)) < 0.2
+
+
+class StressMixture:
+    """Keys of the unified-route stress workload: per (stream, group) a ``components``-centre
+    Gaussian mixture (centres ~ N(0, I)) with per-component sigma ~ U[0.1, 0.6] and a fraction of
+    orphan tokens placed 4 sigma sqrt(D) from their centre in a random direction."""
+
+    def __init__(self, rng: np.random.Generator, streams: int, groups: int, dim: int, components: int = 48,
+                 orphan_frac: float = 0.10):
+        self.rng = rng
+        self.shape = (streams, groups, dim)
+        self.orphan_frac = orphan_frac
+        self.centres = rng.standard_normal((streams, groups, components, dim)).astype(np.float32)
+        self.sigma = rng.uniform(0.1, 0.6, (streams, groups, components)).astype(np.float32)
+
+    def draw(self, tokens: int) -> np.ndarray:
+        rng = self.rng
+        S, G, D = self.shape
+        z = rng.integers(0, self.centres.shape[2], size=(S, G, tokens))
+        si, gi = np.arange(S)[:, None, None], np.arange(G)[None, :, None]
+        base = self.centres[si, gi, z]
+        sig = self.sigma[si, gi, z][..., None]
+        x = base + sig * rng.standard_normal((S, G, tokens, D)).astype(np.float32)
+        u = rng.standard_normal((S, G, tokens, D)).astype(np.float32)
+        u /= np.linalg.norm(u, axis=-1, keepdims=True)
+        far = base + u * (4.0 * sig * np.float32(np.sqrt(D)))
+        orphan = rng.random((S, G, tokens)) < self.orphan_frac
+        return np.where(orphan[..., None], far, x).astype(np.float32)
