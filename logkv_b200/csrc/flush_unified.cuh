@@ -22,8 +22,9 @@
 // exact differences, rooted and squared (cdist), when the widest active lane of the lane's tile
 // has at most 32 rows, else a Gram product of the centres centred on each lane's first row.  The
 // tile is the reference's CPU tile (_semantic_unified_tile :3578-3587, 64 MiB of float32 distances
-// per tile).  Gram products and difference sums run left to right over the features, in float32
-// without fused multiply-adds (this file is compiled with -fmad=false).
+// per tile).  Gram products (one fused multiply-add per feature) and difference sums run left to
+// right over the features in float32; nothing else contracts (this file is compiled with
+// -fmad=false).
 #pragma once
 
 #include "flush_cascade.cuh"
@@ -33,7 +34,8 @@
 namespace logkv {
 
 constexpr long long kUTileBytes = 64ll << 20;   // the CPU reference's distance budget per lane tile
-constexpr int kGramTile = 64;                   // Gram output tile (rows x columns) per CTA
+constexpr int kGramTile = 128;                  // Gram output tile (rows x columns) per CTA
+constexpr int kGramChunk = 32;                  // features staged per pass of the Gram tile
 
 __device__ __forceinline__ size_t ulane(const Geo& g, int b, int grp) { return (size_t)b * g.G + grp; }
 __device__ __forceinline__ int32_t* uwords(const Work& w, size_t bg) { return w.u.words + bg * kULaneWords; }
@@ -142,9 +144,12 @@ __global__ void __launch_bounds__(256) unified_load_kernel(Geo g, logkv_state_t 
 }
 
 // ---------------------------------------------------------------- U2: pair matrix
-// Upper-triangle output tiles of kGramTile x kGramTile, both centre panels staged transposed
-// ([D][64], features of 4 consecutive rows in one 16-byte shared load); each thread owns a 4 x 4
-// block of outputs and accumulates it over the features in order.  Grid (tiles, tiles, B*G) x 256.
+// Upper-triangle output tiles of kGramTile x kGramTile (128 x 128) per CTA of 256 threads; the
+// two centre panels are staged transposed ([kGramChunk][128] per feature chunk, c = x - x_0) and
+// each thread owns 8 x 8 outputs (rows ty*4 + {0..3, 64..67}, columns tx*4 + {0..3, 64..67}, so a
+// warp's 16-byte shared loads are conflict-free), accumulated over the features in order with one
+// fused multiply-add each.  Norms n_i = sum_d c_id^2 run left to right across the chunks.
+// Grid (tiles, tiles, B*G) x 256.
 __global__ void __launch_bounds__(256) unified_dist_kernel(Geo g, Work w, int pass) {
   pdl_entry();
   const size_t bg = blockIdx.z;
@@ -176,65 +181,69 @@ __global__ void __launch_bounds__(256) unified_dist_kernel(Geo g, Work w, int pa
     return;
   }
   // Gram form: c = x - x_0, n_i = sum_d c_id^2, d_ij = max((n_i + n_j) - 2 G_ij, 0).
-  extern __shared__ float4 gsm4[];
-  float* at = reinterpret_cast<float*>(gsm4);      // [D][64] rows i0..
-  float* bt = at + (size_t)D * kGramTile;           // [D][64] rows j0..
-  float* ni = bt + (size_t)D * kGramTile;           // [64]
-  float* nj = ni + kGramTile;                       // [64]
-  // Staged as c = x - x_0, four features per 16-byte global load; consecutive threads take
-  // consecutive rows, so the transposed shared stores fall in distinct banks.
+  __shared__ __align__(16) float at[kGramChunk][kGramTile];   // rows i0.., chunk features
+  __shared__ __align__(16) float bt[kGramChunk][kGramTile];   // rows j0..
+  __shared__ float nrm[2][kGramTile];
   const float4* x0 = reinterpret_cast<const float4*>(mu);
-  const int D4 = D / 4;
-  for (int item = tid; item < kGramTile * D4; item += blockDim.x) {
-    const int r = item % kGramTile, d4 = item / kGramTile;
-    const int ri = i0 + r, rj = j0 + r;
-    const float4 o = x0[d4];
-    const float4 a = ri < n ? reinterpret_cast<const float4*>(mu + (size_t)ri * D)[d4] : o;
-    const float4 c = rj < n ? reinterpret_cast<const float4*>(mu + (size_t)rj * D)[d4] : o;
-    at[(4 * d4 + 0) * kGramTile + r] = fsub(a.x, o.x);
-    at[(4 * d4 + 1) * kGramTile + r] = fsub(a.y, o.y);
-    at[(4 * d4 + 2) * kGramTile + r] = fsub(a.z, o.z);
-    at[(4 * d4 + 3) * kGramTile + r] = fsub(a.w, o.w);
-    bt[(4 * d4 + 0) * kGramTile + r] = fsub(c.x, o.x);
-    bt[(4 * d4 + 1) * kGramTile + r] = fsub(c.y, o.y);
-    bt[(4 * d4 + 2) * kGramTile + r] = fsub(c.z, o.z);
-    bt[(4 * d4 + 3) * kGramTile + r] = fsub(c.w, o.w);
-  }
-  __syncthreads();
-  if (tid < 2 * kGramTile) {
-    const float* p = tid < kGramTile ? at + tid : bt + (tid - kGramTile);
-    float acc = 0.f;
-    for (int d = 0; d < D; ++d) {
-      const float c = p[d * kGramTile];
-      acc = fadd(acc, fmul(c, c));
+  const int tx = tid & 15, ty = tid >> 4;
+  float acc[8][8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r)
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[r][c] = 0.f;
+  float nacc = 0.f;   // thread t: the norm of row i0 + t (t < 128) or j0 + t - 128
+  for (int d0 = 0; d0 < D; d0 += kGramChunk) {
+    const int dn = min(kGramChunk, D - d0);   // a multiple of 4 (D % 4 == 0)
+    // Stage: consecutive threads take consecutive rows (conflict-free transposed stores).
+    for (int item = tid; item < kGramTile * (dn / 4); item += blockDim.x) {
+      const int r = item % kGramTile, q = item / kGramTile;
+      const int ri = i0 + r, rj = j0 + r;
+      const float4 o = x0[d0 / 4 + q];
+      const float4 a = ri < n ? reinterpret_cast<const float4*>(mu + (size_t)ri * D + d0)[q] : o;
+      const float4 c = rj < n ? reinterpret_cast<const float4*>(mu + (size_t)rj * D + d0)[q] : o;
+      at[4 * q + 0][r] = fsub(a.x, o.x);
+      at[4 * q + 1][r] = fsub(a.y, o.y);
+      at[4 * q + 2][r] = fsub(a.z, o.z);
+      at[4 * q + 3][r] = fsub(a.w, o.w);
+      bt[4 * q + 0][r] = fsub(c.x, o.x);
+      bt[4 * q + 1][r] = fsub(c.y, o.y);
+      bt[4 * q + 2][r] = fsub(c.z, o.z);
+      bt[4 * q + 3][r] = fsub(c.w, o.w);
     }
-    (tid < kGramTile ? ni : nj)[tid % kGramTile] = acc;
+    __syncthreads();
+    {
+      const float* col = tid < kGramTile ? &at[0][tid] : &bt[0][tid - kGramTile];
+      for (int d = 0; d < dn; ++d) {
+        const float v = col[d * kGramTile];
+        nacc = fadd(nacc, fmul(v, v));
+      }
+    }
+#pragma unroll 4
+    for (int d = 0; d < dn; ++d) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&at[d][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&at[d][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&bt[d][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&bt[d][64 + tx * 4]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[r][c] = __fmaf_rn(av[r], bv[c], acc[r][c]);
+    }
+    __syncthreads();
   }
-  const int tx = tid & 15, ty = tid >> 4;   // columns j0 + 4 tx .., rows i0 + 4 ty ..
-  float acc[4][4];
-#pragma unroll
-  for (int r = 0; r < 4; ++r)
-#pragma unroll
-    for (int c = 0; c < 4; ++c) acc[r][c] = 0.f;
-  for (int d = 0; d < D; ++d) {
-    const float4 a = reinterpret_cast<const float4*>(at + d * kGramTile)[ty];
-    const float4 bb = reinterpret_cast<const float4*>(bt + d * kGramTile)[tx];
-    const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {bb.x, bb.y, bb.z, bb.w};
-#pragma unroll
-    for (int r = 0; r < 4; ++r)
-#pragma unroll
-      for (int c = 0; c < 4; ++c) acc[r][c] = fadd(acc[r][c], fmul(av[r], bv[c]));
-  }
+  nrm[tid >> 7][tid & 127] = nacc;
   __syncthreads();
 #pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    const int i = i0 + 4 * ty + r;
+  for (int r = 0; r < 8; ++r) {
+    const int il = (r < 4 ? 0 : 64) + ty * 4 + (r & 3), i = i0 + il;
     if (i >= n) continue;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const int j = j0 + 4 * tx + c;
+    for (int c = 0; c < 8; ++c) {
+      const int jl = (c < 4 ? 0 : 64) + tx * 4 + (c & 3), j = j0 + jl;
       if (j >= n || j < i) continue;
-      const float v = fmaxf(fsub(fadd(ni[4 * ty + r], nj[4 * tx + c]), fmul(2.f, acc[r][c])), 0.f);
+      const float v = fmaxf(fsub(fadd(nrm[0][il], nrm[1][jl]), fmul(2.f, acc[r][c])), 0.f);
       dist[(size_t)i * Mg + j] = v;
       dist[(size_t)j * Mg + i] = v;
     }

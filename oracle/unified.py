@@ -14,8 +14,9 @@ Flush level (``_semantic_route_unified``, log_kv_cache.py:3589-3688): ``pair_mat
 ``_semantic_unified_reduce_incremental`` :3301-3376), ``labels_batch``
 (``_semantic_unified_labels_batch`` :3544-3568), ``route_tile`` (``_semantic_unified_tile``
 :3578-3587) and ``ward_entry_index`` (``_semantic_ward_entry_index`` :2450-2474).  The Gram
-products and the exact-difference sums of the pair matrix run left to right over the features
-(the reference leaves that order to its BLAS / vectorised CPU kernels).
+products (one fused multiply-add per feature) and the exact-difference sums of the pair matrix run
+left to right over the features (the reference leaves that order to its BLAS / vectorised CPU
+kernels).
 """
 from __future__ import annotations
 
@@ -269,12 +270,30 @@ def _lr_sum(terms) -> np.ndarray:
     return acc
 
 
+def fma32(a, b, c) -> np.ndarray:
+    """float32 fused multiply-add a * b + c with one rounding (as CUDA's fmaf): the product and
+    the sum are exact in float64 up to the sum's rounding, whose error TwoSum recovers; only a
+    float64 sum lying exactly on a float32 midpoint with a nonzero error rounds differently, and is
+    nudged one float64 ulp toward the error first."""
+    p = np.asarray(a, np.float64) * np.asarray(b, np.float64)
+    cc = np.asarray(c, np.float64)
+    s = p + cc
+    bb = s - p
+    e = (p - (s - bb)) + (cc - bb)
+    low = s.view(np.uint64) & np.uint64((1 << 29) - 1)
+    fix = (low == np.uint64(1 << 28)) & (e != 0)
+    if fix.any():
+        s = np.where(fix, np.nextafter(s, np.where(e > 0, np.inf, -np.inf)), s)
+    return s.astype(F32)
+
+
 def pair_matrix(mu: np.ndarray) -> np.ndarray:
     """Squared centre distances [L, M, M] (``_semantic_unified_pair_matrix``, :3185-3221).
 
     M <= 32: exact differences, ``cdist(...).square()`` (the root rounded, then squared).
     Otherwise centred on each lane's first row: norm n_i = sum_d c_id^2, Gram G_ij = sum_d
-    c_id c_jd, d_ij = max((n_i + n_j) - 2 G_ij, 0), upper triangle mirrored.
+    c_id c_jd (a fused multiply-add per feature, in order), d_ij = max((n_i + n_j) - 2 G_ij, 0),
+    upper triangle mirrored.
     """
     mu = np.asarray(mu, F32)
     L, M, D = mu.shape
@@ -289,7 +308,7 @@ def pair_matrix(mu: np.ndarray) -> np.ndarray:
     norm = _lr_sum((c * c).astype(F32))
     gram = np.zeros((L, M, M), F32)
     for d in range(D):
-        gram = (gram + (c[:, :, None, d] * c[:, None, :, d]).astype(F32)).astype(F32)
+        gram = fma32(c[:, :, None, d], c[:, None, :, d], gram)
     return pair_distances(gram, norm)
 
 
