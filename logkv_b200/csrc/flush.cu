@@ -544,7 +544,8 @@ static TapeSegs tape_segments(const Geo& g, const logkv_state_t& s, const Work& 
 }
 
 // ---------------------------------------------------------------- unified route launches
-static size_t unified_gram_smem(const Geo&) { return 0; }   // the Gram tile's panels are static shared memory
+// The Gram tile's output staging (its panels are static shared memory).
+static size_t unified_gram_smem(const Geo&) { return (size_t)kGramTile * (kGramTile + 1) * 4; }
 // Every CTA of a reduction cluster holds the round's tables; sized for the smallest cluster (2).
 static size_t unified_round_smem(const Geo& g) {
   return logkv_ward::round_smem_bytes(g.Mg, logkv_ward::sort_width(g.Mg), 2);
@@ -614,6 +615,7 @@ static void launch_unified(const Geo& g, const logkv_state_t& s, const Work& w, 
   const int S = logkv_ward::sort_width(g.Mg), CL = unified_cluster(g);
   const size_t gram = unified_gram_smem(g), round = unified_round_smem(g);
   const size_t lab = 3 * (size_t)g.NW * 4, rte = 3 * (size_t)g.Mg * 4, tile = (size_t)g.B * 4;
+  smem_limit(unified_dist_kernel, gram);
   smem_limit(unified_reduce_kernel, round);
   smem_limit(unified_labels_kernel, lab);
   smem_limit(unified_route_kernel, rte);

@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(256) unified_load_kernel(Geo g, logkv_state_t 
 // each thread owns 8 x 8 outputs (rows ty*4 + {0..3, 64..67}, columns tx*4 + {0..3, 64..67}, so a
 // warp's 16-byte shared loads are conflict-free), accumulated over the features in order with one
 // fused multiply-add each.  Norms n_i = sum_d c_id^2 run left to right across the chunks.
-// Grid (tiles, tiles, B*G) x 256.
+// Grid (tiles, tiles, B*G) x 256; dynamic shared memory: the output tile, 128 x 129 floats.
 __global__ void __launch_bounds__(256) unified_dist_kernel(Geo g, Work w, int pass) {
   pdl_entry();
   const size_t bg = blockIdx.z;
@@ -235,18 +235,32 @@ __global__ void __launch_bounds__(256) unified_dist_kernel(Geo g, Work w, int pa
   }
   nrm[tid >> 7][tid & 127] = nacc;
   __syncthreads();
+  // The finished tile through shared memory (row stride kGramTile + 1: a column read is
+  // conflict-free), then both halves written with coalesced stores: rows i of columns j >= i, and
+  // the mirror, rows j of columns i < j (the upper triangle's values, as the reference mirrors).
+  extern __shared__ float tile[];   // [kGramTile][kGramTile + 1]
+  constexpr int TS = kGramTile + 1;
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
-    const int il = (r < 4 ? 0 : 64) + ty * 4 + (r & 3), i = i0 + il;
-    if (i >= n) continue;
+    const int il = (r < 4 ? 0 : 64) + ty * 4 + (r & 3);
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
-      const int jl = (c < 4 ? 0 : 64) + tx * 4 + (c & 3), j = j0 + jl;
-      if (j >= n || j < i) continue;
-      const float v = fmaxf(fsub(fadd(nrm[0][il], nrm[1][jl]), fmul(2.f, acc[r][c])), 0.f);
-      dist[(size_t)i * Mg + j] = v;
-      dist[(size_t)j * Mg + i] = v;
+      const int jl = (c < 4 ? 0 : 64) + tx * 4 + (c & 3);
+      tile[il * TS + jl] = fmaxf(fsub(fadd(nrm[0][il], nrm[1][jl]), fmul(2.f, acc[r][c])), 0.f);
     }
+  }
+  __syncthreads();
+  const int warp = tid >> 5, lane = tid & 31;
+  const int ni = min(kGramTile, n - i0), nj = min(kGramTile, n - j0);
+  for (int il = warp; il < ni; il += 8) {
+    const int i = i0 + il;
+    for (int jl = lane; jl < nj; jl += 32)
+      if (j0 + jl >= i) dist[(size_t)i * Mg + j0 + jl] = tile[il * TS + jl];
+  }
+  for (int jl = warp; jl < nj; jl += 8) {
+    const int j = j0 + jl;
+    for (int il = lane; il < ni; il += 32)
+      if (i0 + il < j) dist[(size_t)j * Mg + i0 + il] = tile[il * TS + jl];
   }
 }
 
