@@ -482,6 +482,22 @@ def unified_reference_timing():
             "kind": "reference"}
 
 
+def configs0_reference_timing():
+    """the reference's own CPU Torch flush (single layer, B=1, G=8, D=128, K=12,
+    one 2048-token flush, planted spans; s_h = 1 / 12 / 32 and the 8-alive seeding case, fp32 and
+    bf16), timed in the build container by tests/golden/make_fullshape.py (fullshape_timing.json)."""
+    path = os.path.join(ROOT, "tests", "golden", "fullshape_timing.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as fh:
+        t = json.load(fh)
+    per_case = {name: round(statistics.median(v["flush_s"]) * 1000.0, 1) for name, v in sorted(t.items())}
+    return {"ms_per_flush_median_by_case": per_case,
+            "ms_per_flush_median": round(statistics.median(per_case.values()), 1),
+            "threads": next(iter(t.values()))["threads"], "kind": "reference",
+            "where": "build container CPU (the reference is not on the GPU box)"}
+
+
 def bench_unified(args, rank, world, local_rank):
     """Unified-route flushes of this rank's streams (batch-sharded: no collective).
     Chunk 0 fills each stream's window, --warmup flushes run untimed, then --steps flushes are timed
@@ -1180,7 +1196,7 @@ def main():
                     rows_per_flush={k: round(v / res["flushes_per_step"], 1) for k, v in res["counters"].items()
                                     if k != "flushes"},
                     decode=dec, prefill=pre, flush_attend=fa, kv_sharded=kvs,
-                    unified=uni)
+                    unified=uni, configs0_reference=configs0_reference_timing())
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
