@@ -553,8 +553,6 @@ class LogStructuredKVCache(nn.Module):
         copy and can be captured in a CUDA graph.
         """
         replaying = any(v_ is not None for v_ in replay.values())
-        if record_op_log and self.semantic_unified_route:
-            raise NotImplementedError(UNSUPPORTED + " (op-logs of the attach route only)")
         chunk = self._check_chunk(k, v, k_raw, input_pos, span_ends, span_ends_device)
         take = None if replaying else self._chunk_flush_take(chunk[-1])
         if take is not None:

@@ -567,7 +567,8 @@ __global__ void lane_plan_kernel(Geo g, logkv_state_t s, Work w) {
 
 // ---------------------------------------------------------------- op-log append
 // The route log rows of the last flush (_record_ops, litgpt/log_kv_cache.py:2043-2071), per
-// (batch, group) lane in the reference's order: a NEW_CLUSTER row (op 0, cluster, 0, position of
+// (batch, group) lane in the reference's order: for the unified route first a WARD_MERGE row
+// (op 3, keep, free, -1) per Ward merge of two old clusters, in merge order; a NEW_CLUSTER row (op 0, cluster, 0, position of
 // the opening token) for every cluster the flush opened, in cluster order (_semantic_new_clusters
 // :2276-2298); then JOIN rows (op 2, cluster, 0, position) for the joined tokens of every
 // ordinary or newly opened cluster, cluster by cluster, positions ascending
@@ -582,9 +583,13 @@ __global__ void __launch_bounds__(256) oplog_append_kernel(Geo g, Work w, int32_
   const int K = g.K;
   const size_t bg = (size_t)b * g.G + grp, row0 = bg * K;
   __shared__ int off_new[kMaxClusters], off_join[kMaxClusters], off_late[kMaxClusters];
-  __shared__ int sh_total, sh_new, sh_join, sh_len;
+  __shared__ int sh_total, sh_new, sh_join, sh_len, sh_ward;
   if (tid == 0) {
     int nn = 0, nj = 0, nl = 0;
+    // Unified route: the lane's Ward merges come first (_semantic_ward_merge_batch records them
+    // before the new clusters and joins, log_kv_cache.py:2580).
+    const int nw = (g.route == LOGKV_ROUTE_UNIFIED && w.narch[b] > 0) ? w.u.words[bg * kULaneWords + kUWard] : 0;
+    sh_ward = nw;
     for (int c = 0; c < K; ++c) {
       const int type = w.plan_type[row0 + c], n = w.plan_n[row0 + c];
       off_new[c] = nn;
@@ -601,7 +606,7 @@ __global__ void __launch_bounds__(256) oplog_append_kernel(Geo g, Work w, int32_
     }
     sh_new = nn;
     sh_join = nj;
-    sh_total = nn + nj + nl;
+    sh_total = nw + nn + nj + nl;
     sh_len = op_len[bg];
     if (sh_len > cap || sh_len + sh_total > cap) {
       op_len[bg] = cap + 1;
@@ -610,7 +615,11 @@ __global__ void __launch_bounds__(256) oplog_append_kernel(Geo g, Work w, int32_
   }
   __syncthreads();
   if (sh_total < 0) return;
-  const int len0 = sh_len;
+  for (int i = tid; i < sh_ward; i += nt) {
+    int4* wl = reinterpret_cast<int4*>(op_log) + bg * (size_t)cap;
+    wl[sh_len + i] = make_int4(3, w.u.ward[(bg * K + i) * 2], w.u.ward[(bg * K + i) * 2 + 1], -1);
+  }
+  const int len0 = sh_len + sh_ward;
   const int* arch = w.arch_idx + (size_t)b * g.NW;
   const int* toks = w.tok_list + bg * g.NW;
   const int64_t* pos = w.tok_pos + (size_t)b * g.NW;
@@ -638,7 +647,7 @@ __global__ void __launch_bounds__(256) oplog_append_kernel(Geo g, Work w, int32_
     }
   }
   __syncthreads();
-  if (tid == 0) op_len[bg] = len0 + sh_total;
+  if (tid == 0) op_len[bg] = sh_len + sh_total;
 }
 
 }  // namespace logkv

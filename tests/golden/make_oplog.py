@@ -21,7 +21,7 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 from make_golden import install_shim, to_np  # noqa: E402
-from streams import CONFIGS, make_stream  # noqa: E402
+from streams import CONFIGS, UNIFIED_CONFIGS, make_stream  # noqa: E402
 
 
 def run_config(cfg: dict, outdir: str) -> str:
@@ -44,6 +44,7 @@ def run_config(cfg: dict, outdir: str) -> str:
         alpha_exact_tokens=cfg["exact"], alpha_span_max_tokens=cfg["span_cap"],
         beta_novelty=cfg["beta"], beta_adaptive_merge=cfg["beta"],
         semantic_s_h=cfg.get("s_h"), cos_cache=cos, sin_cache=sin, rope_n_elem=cfg["dim"],
+        semantic_unified_route=cfg.get("unified", False), semantic_merge_passes=cfg.get("merge_passes", 1),
     )
     cache.begin_op_log()
     out: dict = {}
@@ -71,7 +72,7 @@ def main() -> None:
     if not args.reference:
         raise SystemExit("pass --reference <reference checkout> or set LOGKV_REFERENCE")
     install_shim(args.reference)
-    for cfg in CONFIGS:
+    for cfg in CONFIGS + UNIFIED_CONFIGS:
         if args.only and cfg["name"] != args.only:
             continue
         path = run_config(cfg, args.out)

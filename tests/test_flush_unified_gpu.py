@@ -60,11 +60,42 @@ def test_device_unified_flush_matches_reference_stream(name):
                                           err_msg=f"step {step} {mirror}")
 
 
+@pytest.mark.parametrize("name", [c["name"] for c in UNIFIED_CONFIGS])
+def test_unified_op_log_matches_reference(name):
+    """WARD_MERGE, NEW_CLUSTER and JOIN rows after every step equal the reference's op-log
+    (tests/golden/oplog_<name>.npz from make_oplog.py), and recording leaves the flush unchanged."""
+    import os
+    cfg = unified_config(name)
+    stream = make_stream(cfg)
+    ref = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", f"oplog_{name}.npz"))
+    cache = make_unified_cache(cfg, stream)
+    cache.begin_op_log()
+    for step, chunk in enumerate(stream["chunks"]):
+        dt = cache.level_k.dtype
+        k = torch.from_numpy(chunk["k"]).to("cuda", dt)
+        kr = torch.from_numpy(chunk["k_raw"]).to("cuda", dt)
+        v = torch.from_numpy(chunk["v"]).to("cuda", dt)
+        pos = torch.from_numpy(chunk["pos"]).cuda() if chunk.get("pos") is not None else None
+        cache.add_recent(k, v, k_raw=kr, input_pos=pos, span_ends=chunk["span_ends"].tolist(), record_op_log=True)
+        log, lengths = cache.take_op_log()
+        want_len = ref[f"step{step}/op_log_len"]
+        np.testing.assert_array_equal(lengths.cpu().numpy(), want_len, err_msg=f"step {step} lengths")
+        want, got = ref[f"step{step}/op_log"], log.cpu().numpy()
+        for b in range(want.shape[0]):
+            for g in range(want.shape[1]):
+                n = int(want_len[b, g])
+                np.testing.assert_array_equal(got[b, g, :n], want[b, g, :n], err_msg=f"step {step} lane {(b, g)}")
+        np.testing.assert_array_equal(cache.level_count.cpu().numpy(), ref[f"step{step}/level_count"])
+
+
 def test_unified_route_rejects_what_it_does_not_build():
+    from logkv_b200 import _SemanticReplayUpdates
     cfg = unified_config("fp32_unified")
     stream = make_stream(cfg)
     cache = make_unified_cache(cfg, stream)
-    chunk = stream["chunks"][0]
-    k = torch.from_numpy(chunk["k"]).to("cuda", torch_dtype(cfg))
-    with pytest.raises(NotImplementedError):
-        cache.add_recent(k, k, k_raw=k, record_op_log=True, span_ends=chunk["span_ends"].tolist())
+    dt = torch_dtype(cfg)
+    with torch.no_grad(), cache._semantic_update_context(_SemanticReplayUpdates()), \
+            pytest.raises(NotImplementedError):
+        for chunk in stream["chunks"][:3]:
+            k = torch.from_numpy(chunk["k"]).to("cuda", dt)
+            cache.add_recent(k, k, k_raw=k, span_ends=chunk["span_ends"].tolist(), record_op_log=True)
