@@ -124,7 +124,13 @@ typedef struct logkv_state {
  *   ALPHA_ORDER   two span candidates of one batch row with near-equal densities
  *                 (alpha_log_kv.py:177-226 sorts by density): first / second = candidates;
  *   ALPHA_SWAP    the greedy's replacement test density * length > evicted loss: first =
- *                 candidate, second = 1 if the span was taken.
+ *                 candidate, second = 1 if the span was taken;
+ *   WARD_MIN      unified route: a row's minimum Ward cost and the next cost of that row
+ *                 (_UnifiedReduceTorch._scan, log_kv_cache.py:480-494, found by a full scan of the
+ *                 row): cluster = pass (0 candidate, 1 global), index = row, first / second =
+ *                 columns, value = the minimum cost;
+ *   WARD_BUDGET   unified route: the last pair the round's budget takes and the first it leaves
+ *                 (the stable cost order, :525-527): cluster = pass, first / second = their rows.
  * `flush` = flushes of this workspace before the logging one (0-based).
  */
 #define LOGKV_TIE_ATTACH_COST 1
@@ -135,6 +141,8 @@ typedef struct logkv_state {
 #define LOGKV_TIE_BETA_CUT 6
 #define LOGKV_TIE_ALPHA_ORDER 7
 #define LOGKV_TIE_ALPHA_SWAP 8
+#define LOGKV_TIE_WARD_MIN 9
+#define LOGKV_TIE_WARD_BUDGET 10
 typedef struct logkv_tie {
   int32_t kind, flush, batch, group, cluster, index, first, second;
   float gap;    /* relative gap of the two values */

@@ -26,7 +26,7 @@ FLUSH_STAGES = ("snapshot", "span_cut", "score_attach", "choose", "seed_plan", "
 COUNTERS = ("storage_read", "stage_read", "survivor", "fill", "clear", "carry", "gather", "flushes", "exact_cuts",
             "ties", "seq_lanes")
 TIE_KINDS = {1: "attach_cost", 2: "direct", 3: "nearest", 4: "seed_pick", 5: "seed_nearest", 6: "beta_cut",
-             7: "alpha_order", 8: "alpha_swap"}
+             7: "alpha_order", 8: "alpha_swap", 9: "ward_min", 10: "ward_budget"}
 
 
 ROUTE_ATTACH, ROUTE_UNIFIED = 0, 1   # logkv_layout_t.route (LOGKV_ROUTE_*)

@@ -63,6 +63,9 @@ __device__ inline logkv_ward::RunLane urun(const Geo& g, const Work& w, size_t b
   l.target = pass ? g.K : 1;
   l.passes = pass ? g.passes : 1;
   l.cost_order = 0;
+  l.pass = pass;
+  l.ties = logkv_ward::TieSink{&w.counters[kCntTies], reinterpret_cast<logkv_tie_t*>(w.ties), &w.counters[kCntFlushes],
+                               kTieCap, (int)(bg / g.G), (int)(bg % g.G)};
   return l;
 }
 

@@ -67,6 +67,8 @@ __device__ RunLane lane_of(const logkv_unified_t& u, int lane) {
   l.target = u.target;
   l.passes = 1;
   l.cost_order = 1;
+  l.pass = 0;
+  l.ties = TieSink{nullptr, nullptr, nullptr, 0, 0, 0};
   return l;
 }
 

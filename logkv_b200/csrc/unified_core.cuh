@@ -20,6 +20,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/logkv_b200.h"
+
 namespace logkv_ward {
 
 namespace cg = cooperative_groups;
@@ -70,6 +72,31 @@ __device__ __forceinline__ float cost_lower_bound(float d2, float mi, float mj) 
 }
 __device__ __forceinline__ float key_cost(long long key) { return __int_as_float((int)(key >> 32)); }
 
+// Where a lane's near ties go (the flush workspace's tie log), or nowhere (count null): a
+// decision whose best and runner-up costs lie within a relative 1e-6 of each other, which the
+// reference's own summation order could decide the other way.
+struct TieSink {
+  unsigned long long* count;          // entries requested (entries beyond cap are counted only)
+  logkv_tie_t* log;
+  const unsigned long long* flushes;  // flushes so far (the entry's flush index is this - 1)
+  int cap, b, g;
+};
+
+__device__ __forceinline__ bool near_tie_cost(float a, float b) {
+  return fabsf(fsub(a, b)) < fmul(1e-6f, fmaxf(fabsf(a), fabsf(b)));
+}
+
+__device__ inline void log_ward_tie(const TieSink& t, int kind, int pass, int index, int first, int second, float a,
+                                    float b) {
+  if (!t.count) return;
+  const unsigned long long slot = atomicAdd(t.count, 1ull);
+  if (slot >= (unsigned long long)t.cap) return;
+  const float den = fmaxf(fabsf(a), fabsf(b));
+  const float gap = den > 0.f ? fdiv(fabsf(fsub(a, b)), den) : 0.f;
+  const unsigned long long f = *reinterpret_cast<const volatile unsigned long long*>(t.flushes);
+  t.log[slot] = logkv_tie_t{kind, (int32_t)f - 1, t.b, t.g, pass, index, first, second, gap, a};
+}
+
 // One lane's device state.  Rows are [0, M); the live count, merge count, flags and trace are
 // this lane's own words.
 struct RunLane {
@@ -89,6 +116,8 @@ struct RunLane {
                          // or in row order when `cost_order` is 0 and the budget takes every pair
   int M, D, target, passes;
   int cost_order;        // sort every round's pairs by cost (the operator API's trace contract)
+  int pass;              // 0 candidate pass, 1 global pass (tie log entries)
+  TieSink ties;          // near-tie log of the row minima and the budget cut
 };
 
 // out[r] = min over columns of the row's packed keys; one warp per row.  Only live columns
@@ -104,7 +133,8 @@ __device__ inline void scan_rows(const RunLane& l, const int* rows, int nrows, c
     const int r = rows[i];
     const float* drow = l.dist + (size_t)r * M;
     const float mr = l.mass[r], rr = l.radius[r];
-    long long best = kInfKey;
+    long long best = kInfKey, second = kInfKey;   // the row's minimum key and the next one
+    const bool tie_log = l.ties.count != nullptr;
     for (int kb = lane; kb < ncols; kb += 32 * kBatch) {
       int cv[kBatch];
       float dv[kBatch], mv[kBatch], rv[kBatch];
@@ -119,14 +149,34 @@ __device__ inline void scan_rows(const RunLane& l, const int* rows, int nrows, c
       }
 #pragma unroll
       for (int j = 0; j < kBatch; ++j) {
-        if (cv[j] < 0 || cost_lower_bound(dv[j], mr, mv[j]) > key_cost(best)) continue;
+        if (cv[j] < 0) continue;
+        // With the tie log on, the runner-up is kept exactly while it lies within 4e-6 of the
+        // minimum (beyond that it cannot be a near tie, and the bound skips it).
+        const float bound = tie_log ? fminf(key_cost(second), fmul(key_cost(best), 1.000004f)) : key_cost(best);
+        if (cost_lower_bound(dv[j], mr, mv[j]) > bound) continue;
         const float cost = pair_cost(dv[j], mr, mv[j], rr, rv[j], l.limit, cv[j] != r);
-        best = min(best, pack_key(cost, (long long)(r ^ cv[j])));
+        const long long key = pack_key(cost, (long long)(r ^ cv[j]));
+        if (key < best) {
+          second = best;
+          best = key;
+        } else if (key < second) {
+          second = key;
+        }
       }
     }
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) best = min(best, __shfl_xor_sync(0xffffffffu, best, off));
-    if (lane == 0) out[r] = best;
+    for (int off = 16; off > 0; off >>= 1) {
+      const long long ob = __shfl_xor_sync(0xffffffffu, best, off), os = __shfl_xor_sync(0xffffffffu, second, off);
+      second = min(min(second, os), max(best, ob));
+      best = min(best, ob);
+    }
+    if (lane == 0) {
+      out[r] = best;
+      const float bc = key_cost(best), sc = key_cost(second);
+      if (tie_log && bc < __int_as_float(0x7F800000) && sc < __int_as_float(0x7F800000) && near_tie_cost(bc, sc))
+        log_ward_tie(l.ties, LOGKV_TIE_WARD_MIN, l.pass, r, (int)((best & 0xFFFFFFFFLL) ^ r),
+                     (int)((second & 0xFFFFFFFFLL) ^ r), bc, sc);
+    }
   }
 }
 
@@ -403,6 +453,12 @@ __device__ inline bool select_pairs(const RunLane& l, const RoundSmem& sm, int* 
     int n = min(nv, M / 2);
     n = min(n, max(count - l.target, 0));
     nok = n;
+    if (cut && n > 0 && n < nv) {
+      const float a = __int_as_float((int)(sm.sk[n - 1] >> 32)), b = __int_as_float((int)(sm.sk[n] >> 32));
+      if (near_tie_cost(a, b))
+        log_ward_tie(l.ties, LOGKV_TIE_WARD_BUDGET, l.pass, n - 1, (int)(sm.sk[n - 1] & 0xFFFFFFFFull),
+                     (int)(sm.sk[n] & 0xFFFFFFFFull), a, b);
+    }
   }
   __syncthreads();
   const int n_ok = nok;
