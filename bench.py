@@ -491,7 +491,8 @@ def configs0_reference_timing():
         return None
     with open(path) as fh:
         t = json.load(fh)
-    per_case = {name: round(statistics.median(v["flush_s"]) * 1000.0, 1) for name, v in sorted(t.items())}
+    per_case = {name: round(statistics.median(v["flush_s"]) * 1000.0, 1) for name, v in sorted(t.items())
+                if "unified" not in name}
     return {"ms_per_flush_median_by_case": per_case,
             "ms_per_flush_median": round(statistics.median(per_case.values()), 1),
             "threads": next(iter(t.values()))["threads"], "kind": "reference",

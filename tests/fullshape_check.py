@@ -4,7 +4,8 @@ Decisions and layout fields must equal the reference's.  The only waiver is a lo
 when a per-token decision (the cluster a token joined, read from the route op-log), the exact
 pool's kept positions, or a lane's ladder layout differs, every differing item must be covered by
 a near-tie log entry of that flush (same token position and lane for attach / seed decisions,
-same batch row for Alpha, same lane for Beta cuts); the lanes it affects are then excluded from the
+same batch row for Alpha, same lane for Beta cuts and for the unified route's Ward decisions); the
+lanes it affects are then excluded from the
 exact comparison of that flush and every later one, and the waiver is printed.  Without waivers
 every field is compared exactly, the level K/V and exact-pool rows through their bit hashes
 (with the float64 projections as a second, tolerance-based view when a hash differs).
@@ -58,6 +59,8 @@ class Checker:
         seed_lanes = {(t["batch"], t["group"]) for t in ties if t["kind"] == "seed_pick"}
         beta_lanes = {(t["batch"], t["group"]) for t in ties if t["kind"] == "beta_cut"}
         alpha_rows = {t["batch"] for t in ties if t["kind"] in ("alpha_order", "alpha_swap")}
+        # Unified route: a Ward near tie (a row minimum or a budget cut) can move any token of its lane.
+        seed_lanes |= {(t["batch"], t["group"]) for t in ties if t["kind"] in ("ward_min", "ward_budget")}
         # Exact pool: kept positions per batch row.
         for b in range(B):
             if b in self.waived_rows:

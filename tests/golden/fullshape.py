@@ -44,8 +44,18 @@ CASES = [
 ]
 
 
+# The unified (Ward / radius) route at the same shape: radius sqrt(s_h) = 1 (few candidates
+# merge: the global pass reduces ~2300 rows), sqrt(32) (candidates absorb most tokens), and
+# frozen-centre sweeps in the global pass.
+UNIFIED_CASES = [
+    dict(GEOM, name="f32_unified", dtype="fp32", s_h=1.0, alive=12, seed=20, unified=True),
+    dict(GEOM, name="bf16_unified_sh32", dtype="bf16", s_h=32.0, alive=8, seed=21, unified=True),
+    dict(GEOM, name="f32_unified_passes2", dtype="fp32", s_h=4.0, alive=12, seed=22, unified=True, merge_passes=2),
+]
+
+
 def case(name: str) -> dict:
-    return next(c for c in CASES if c["name"] == name)
+    return next(c for c in CASES + UNIFIED_CASES if c["name"] == name)
 
 
 def make_case(cfg: dict) -> dict:

@@ -27,7 +27,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
-from fullshape import CASES, bit_hash, make_case, prestate, projections  # noqa: E402
+from fullshape import CASES, UNIFIED_CASES, bit_hash, make_case, prestate, projections  # noqa: E402
 from make_golden import install_shim, to_np  # noqa: E402
 
 THREADS = 8
@@ -58,7 +58,8 @@ def run_case(cfg: dict, outdir: str) -> tuple[str, list]:
         semantic_replay_updates=True, allocate_second_order=False, alpha_exact_tokens=cfg["exact"],
         alpha_span_max_tokens=cfg["span_cap"], beta_novelty=cfg["beta"], beta_adaptive_merge=cfg["beta"],
         semantic_s_h=cfg["s_h"], cos_cache=torch.from_numpy(inputs["cos"]),
-        sin_cache=torch.from_numpy(inputs["sin"]), rope_n_elem=D)
+        sin_cache=torch.from_numpy(inputs["sin"]), rope_n_elem=D,
+        semantic_unified_route=cfg.get("unified", False), semantic_merge_passes=cfg.get("merge_passes", 1))
 
     def push(chunk, record):
         k = torch.from_numpy(chunk["k"]).to(dtype)
@@ -120,7 +121,7 @@ def main() -> None:
     install_shim(args.reference)
     timing_path = os.path.join(args.out, "fullshape_timing.json")
     timing = json.load(open(timing_path)) if os.path.exists(timing_path) else {}
-    for cfg in CASES:
+    for cfg in CASES + UNIFIED_CASES:
         if args.only and cfg["name"] != args.only:
             continue
         path, times = run_case(cfg, args.out)

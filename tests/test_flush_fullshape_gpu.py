@@ -1,7 +1,8 @@
 """Device flush against the reference at the production shape, with the near-tie log.
 
 Each case of ``tests/golden/fullshape.py`` (G=8, D=128, K=12, B'=125, three 2048-token flushes,
-fp32 / bf16, s_h = 1 / 12 / 32, farthest-point seeding) runs through ``add_recent`` with the op-log
+fp32 / bf16, s_h = 1 / 12 / 32, farthest-point seeding; and the unified route with s_h = 1 / 32 and
+frozen-centre sweeps) runs through ``add_recent`` with the op-log
 bound, and after every flush the cache is compared with the fixture the unmodified reference wrote
 (``tests/golden/make_fullshape.py``): per-token cluster decisions (op-log rows), the exact pool,
 every layout field, the cluster table and the level / pool K-V bits.  Decisions may differ only
@@ -19,7 +20,7 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(HERE, "golden"))
-from fullshape import CASES, case, make_case, prestate  # noqa: E402
+from fullshape import CASES, UNIFIED_CASES, case, make_case, prestate  # noqa: E402
 from fullshape_check import CLUSTER, LAYOUT, Checker  # noqa: E402
 
 pytestmark = pytest.mark.gpu
@@ -35,7 +36,8 @@ def build_cache(cfg, inputs):
         semantic_centroid_backend="sequential", semantic_replay_updates=True, allocate_second_order=False,
         alpha_exact_tokens=cfg["exact"], alpha_span_max_tokens=cfg["span_cap"], beta_novelty=cfg["beta"],
         beta_adaptive_merge=cfg["beta"], semantic_s_h=cfg["s_h"], cos_cache=torch.from_numpy(inputs["cos"]),
-        sin_cache=torch.from_numpy(inputs["sin"]), rope_n_elem=cfg["dim"])
+        sin_cache=torch.from_numpy(inputs["sin"]), rope_n_elem=cfg["dim"],
+        semantic_unified_route=cfg.get("unified", False), semantic_merge_passes=cfg.get("merge_passes", 1))
 
 
 def push(cache, chunk, record):
@@ -54,7 +56,7 @@ def bits_and_values(t: torch.Tensor):
     return v.view(np.uint32), v
 
 
-@pytest.mark.parametrize("name", [c["name"] for c in CASES])
+@pytest.mark.parametrize("name", [c["name"] for c in CASES + UNIFIED_CASES])
 def test_fullshape_flush_matches_reference(name, cascade_path):
     cfg = case(name)
     inputs = make_case(cfg)
