@@ -298,12 +298,10 @@ class LogStructuredKVCache(nn.Module):
     def _update_signature(self, take: int):
         L = self._layout
         return (L.batch, L.groups, L.dim, L.clusters, L.levels, L.slots, L.recent_capacity, L.exact, L.span_cap,
-                L.beta, L.dtype, L.eta, L.g0, L.lam, int(take), int(self.recent_count))
+                L.beta, L.dtype, L.eta, L.g0, L.lam, L.route, L.merge_passes, int(take), int(self.recent_count))
 
     def _flush_with_updates(self, take: int, record_op_log: bool, replay: bool) -> None:
         """One flush under an update context: record it, or replay its record without routing."""
-        if self.semantic_unified_route:
-            raise NotImplementedError(UNSUPPORTED + " (update tapes of the attach route only)")
         updates = self._active_updates
         key = (self._flush_cursor, int(take), int(self.recent_count))
         lib = _lib.lib()

@@ -426,6 +426,7 @@ static Geo make_geo(const logkv_layout_t& L, int F, int recent_count) {
 static size_t carve(const Geo& g, size_t esize, char* base, Work* w) {
   Carver c{base};
   const size_t B = g.B, G = g.G, D = g.D, K = g.K, P = g.P, NC = g.NC, NW = g.NW, S = g.S;
+  w->tape_cut_lane = -1;
   w->status = c.take<int32_t>(1, 4);
   w->counters = c.take<unsigned long long>(kNumCounters, 8);
   w->ties = c.take<TieEntry>(kTieCap, sizeof(TieEntry));  // lands at kTieOffset (checked below)
@@ -540,6 +541,10 @@ static TapeSegs tape_segments(const Geo& g, const logkv_state_t& s, const Work& 
   add(w.plan_m0, t.plan_m0, B * G * K * 4);
   add(w.plan_scr, t.plan_scr, B * G * K * 4);
   add(w.plan_base, t.plan_base, B * G * K * 8);
+  if (g.route == LOGKV_ROUTE_UNIFIED) {
+    add(w.u.words, t.uwords, B * G * kULaneWords * 4);
+    add(w.u.ward, t.ward, B * G * K * 2 * 4);
+  }
   return segs;
 }
 
@@ -600,17 +605,31 @@ static bool unified_fits(const Geo& g, size_t esize) {
 }
 
 template <typename T, bool BETA, int DC>
-static void launch_ward(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st) {
+static void launch_ward(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st, uint8_t* ward_cuts) {
   const size_t smem = unified_ward_smem(g, sizeof(T));
   smem_limit(unified_ward_kernel<T, BETA, DC>, smem);
   launch_pdl(unified_ward_kernel<T, BETA, DC>, dim3(g.G, g.B), kCascadeThreads, smem, st, g, s, w,
-             unified_sort_cap(g), unified_walk_bytes(g, sizeof(T)));
+             unified_sort_cap(g), unified_walk_bytes(g, sizeof(T)), ward_cuts);
+}
+
+// The Ward merges of a flush (recorded jobs when replaying an update tape).
+template <typename T>
+static void launch_ward_all(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st, uint8_t* ward_cuts) {
+  if (g.beta) {
+    if (g.D == 128) launch_ward<T, true, 128>(g, s, w, st, ward_cuts);
+    else if (g.D == 64) launch_ward<T, true, 64>(g, s, w, st, ward_cuts);
+    else launch_ward<T, true, 0>(g, s, w, st, ward_cuts);
+  } else {
+    if (g.D == 128) launch_ward<T, false, 128>(g, s, w, st, ward_cuts);
+    else if (g.D == 64) launch_ward<T, false, 64>(g, s, w, st, ward_cuts);
+    else launch_ward<T, false, 0>(g, s, w, st, ward_cuts);
+  }
 }
 
 // The unified route between the span choice and the per-cluster plan: candidate pass, labels,
 // global pass, route, Ward merges (11 launches, no host synchronisation).
 template <typename T>
-static void launch_unified(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st) {
+static void launch_unified(const Geo& g, const logkv_state_t& s, const Work& w, cudaStream_t st, uint8_t* ward_cuts) {
   const int lanes = g.B * g.G, tiles = (g.Mg + kGramTile - 1) / kGramTile;
   const int S = logkv_ward::sort_width(g.Mg), CL = unified_cluster(g);
   const size_t gram = unified_gram_smem(g), round = unified_round_smem(g);
@@ -630,15 +649,7 @@ static void launch_unified(const Geo& g, const logkv_state_t& s, const Work& w, 
     if (pass == 0) launch_pdl(unified_labels_kernel, dim3(g.G, g.B), 1024, lab, st, g, s, w);
   }
   launch_pdl(unified_route_kernel, dim3(g.G, g.B), 1024, rte, st, g, s, w);
-  if (g.beta) {
-    if (g.D == 128) launch_ward<T, true, 128>(g, s, w, st);
-    else if (g.D == 64) launch_ward<T, true, 64>(g, s, w, st);
-    else launch_ward<T, true, 0>(g, s, w, st);
-  } else {
-    if (g.D == 128) launch_ward<T, false, 128>(g, s, w, st);
-    else if (g.D == 64) launch_ward<T, false, 64>(g, s, w, st);
-    else launch_ward<T, false, 0>(g, s, w, st);
-  }
+  launch_ward_all<T>(g, s, w, st, ward_cuts);
 }
 
 // Phases: kPhaseScores = snapshot, span cut, span scores (the group parts of this rank) and
@@ -690,7 +701,7 @@ static int launch_flush(const Geo& g, const logkv_state_t& s, const Work& w, cud
   launch_pdl(alpha_choose_kernel, g.B, 1024, choose_smem, st, g, s, w);
   mark();
   if (g.route == LOGKV_ROUTE_UNIFIED) {
-    launch_unified<T>(g, s, w, st);
+    launch_unified<T>(g, s, w, st, tape ? tape->ward_cuts : nullptr);
   } else {
     // Seeding: one 8-CTA cluster per lane; rows staged in shared memory when they fit.
     Geo gs = g;
@@ -741,6 +752,12 @@ static int launch_replay(const Geo& g, const logkv_state_t& s, const Work& w, co
   launch_pdl(snapshot_kernel<T>, dim3(per_bg, g.G, g.B), 256, 0, st, g, s, w);
   launch_pdl(tape_payload_kernel<T>, dim3(per_pay, g.G, g.B), 256, 0, st, g, s, tape, 0);
   launch_pdl(tape_copy_kernel, dim3(2 * sm_count), 256, 0, st, tape_segments(g, s, w, tape, false));
+  if (g.route == LOGKV_ROUTE_UNIFIED) {
+    // The recorded Ward merges (with their recorded cuts) before the per-cluster plan; they use the
+    // plan fields of the lanes they rebuild, so the recorded plan is copied back after them.
+    launch_ward_all<T>(g, s, w, st, tape.ward_cuts);
+    launch_pdl(tape_copy_kernel, dim3(2 * sm_count), 256, 0, st, tape_segments(g, s, w, tape, false));
+  }
   launch_pdl(lane_plan_kernel, dim3(g.G, g.B), 32 * ((g.K + 31) / 32), 0, st, g, s, w);
   launch_prepare<T>(g, s, w, st);
   launch_cascade_all<T>(g, s, w, st);
@@ -794,9 +811,10 @@ static int run_flush(const logkv_layout_t* layout, const logkv_state_t* state, i
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (chunk && (tape_mode != kTapeNone || phases != kPhaseAll)) return LOGKV_E_SHAPE;
   // The unified route's Ward merges rewrite ladders before the per-cluster plan, so its route
-  // phase runs only together with the apply phase, and it keeps no update tape.
+  // phase runs only together with the apply phase, and only whole flushes keep update tapes.
   if (layout->route == LOGKV_ROUTE_UNIFIED &&
-      (tape_mode != kTapeNone || ((phases & kPhaseRoute) && !(phases & kPhaseApply))))
+      (((phases & kPhaseRoute) && !(phases & kPhaseApply)) ||
+       (tape_mode != kTapeNone && (phases != kPhaseAll || ranks != 1))))
     return LOGKV_E_SHAPE;
   if (tape_mode != kTapeNone) {
     TapeView t{};

@@ -226,7 +226,7 @@ __device__ void merge_tile(const LaneCtx<T>& x, const Geo& g, const Work& w, con
       const int qn = (mend - t0 + 3) / 4;  // groups of this tile (tile rows 4q..4q+3)
       // Recorded cuts of this (lane, level, tile): written when recording, read when replaying.
       uint8_t* tcut = g.tape != kTapeNone
-                          ? w.tape_cuts + ((size_t)x.lane * g.L + ell) * tape_cut_stride(g) + t0 / 4
+                          ? w.tape_cuts + ((size_t)(w.tape_cut_lane >= 0 ? w.tape_cut_lane : (long long)x.lane) * g.L + ell) * tape_cut_stride(g) + t0 / 4
                           : nullptr;
       if (g.tape == kTapeReplay) {
         for (int q = tid; q < qn; q += nt) bcut[q] = tcut[q];
@@ -829,7 +829,7 @@ __device__ void merge_group_warp(const LaneCtx<T>& x, const Geo& g, const Work& 
   int cut = 1;
   bool finite = false;   // the certified warp cut saw every row finite (energies <= 1e30)
   uint8_t* tcut = g.tape != kTapeNone
-                      ? w.tape_cuts + ((size_t)x.lane * g.L + ell) * tape_cut_stride(g) + r0 / 4
+                      ? w.tape_cuts + ((size_t)(w.tape_cut_lane >= 0 ? w.tape_cut_lane : (long long)x.lane) * g.L + ell) * tape_cut_stride(g) + r0 / 4
                       : nullptr;
   if (two) {
     if (g.tape == kTapeReplay) {

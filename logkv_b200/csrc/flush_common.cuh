@@ -175,6 +175,7 @@ struct Work {
   float* s_winner;         // [B,G,NW] token index order
   float* cnorm;            // [B,G,K] sum_d mu_d^2 of every centre (left to right), before the flush
   uint8_t* tape_cuts;      // update tape's Beta cuts [B,G,K,L,cut stride] (record / replay), else null
+  long long tape_cut_lane; // >= 0: the cut slot a sequential walk uses instead of its lane (Ward merges)
   int64_t* tok_pos;        // [B,NW] position of every token of the flush's index space (written by K0)
   int32_t* tok_list;       // [B,G,NW] archive ranks grouped by cluster (stable)
   int32_t* plan_off;       // [B,G,K] offset into tok_list

@@ -11,6 +11,7 @@
 //             flags, span count); the row counts and alpha_count follow from the kept counts
 //   plan      per-cluster jobs (token lists, offsets, counts, kinds, scratch ranges, base orders)
 //   cuts      the Beta cut of every 4-row group the cascade merged, per (lane, level, group)
+//   unified route: the Ward merge jobs and counts, and the Beta cuts of their ladder rebuilds
 #pragma once
 
 #include "flush_common.cuh"
@@ -35,6 +36,11 @@ struct TapeView {
   int32_t* plan_scr;
   int64_t* plan_base;      // [B,G,K]
   uint8_t* cuts;           // [B,G,K,L,cut_stride]
+  // Unified route only: the lane words (Ward merge counts), the Ward merge jobs and the Beta cuts
+  // of the Ward merges' ladder rebuilds, per (b, g, merge).
+  int32_t* uwords;         // [B,G,kULaneWords]
+  int32_t* ward;           // [B,G,K,2]
+  uint8_t* ward_cuts;      // [B,G,K,L,cut_stride]
 };
 
 // Beta groups a level can merge: its pool holds at most Bs stored rows plus its incoming rows,
@@ -68,6 +74,14 @@ inline size_t tape_carve(const Geo& g, size_t esize, char* base, TapeView* t) {
   t->plan_scr = static_cast<int32_t*>(take(B * G * K * 4));
   t->plan_base = static_cast<int64_t*>(take(B * G * K * 8));
   t->cuts = static_cast<uint8_t*>(take(B * G * K * (size_t)g.L * tape_cut_stride(g)));
+  t->uwords = nullptr;
+  t->ward = nullptr;
+  t->ward_cuts = nullptr;
+  if (g.route == LOGKV_ROUTE_UNIFIED) {
+    t->uwords = static_cast<int32_t*>(take(B * G * kULaneWords * 4));
+    t->ward = static_cast<int32_t*>(take(B * G * K * 2 * 4));
+    t->ward_cuts = static_cast<uint8_t*>(take(B * G * K * (size_t)g.L * tape_cut_stride(g)));
+  }
   return (off + 255) & ~size_t(255);
 }
 

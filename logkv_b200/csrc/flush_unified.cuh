@@ -510,7 +510,7 @@ __global__ void __launch_bounds__(1024) unified_route_kernel(Geo g, logkv_state_
 // walk.  Dynamic shared memory: the walk's (walk_bytes), then two sort arrays of cap entries.
 template <typename T, bool BETA, int DC>
 __global__ void __launch_bounds__(kCascadeThreads) unified_ward_kernel(Geo g, logkv_state_t s, Work w, int cap,
-                                                                        size_t walk_bytes) {
+                                                                        size_t walk_bytes, uint8_t* ward_cuts) {
   pdl_entry();
   const int b = blockIdx.y, grp = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
   const size_t bg = ulane(g, b, grp);
@@ -659,9 +659,15 @@ __global__ void __launch_bounds__(kCascadeThreads) unified_ward_kernel(Geo g, lo
       for (int l = tid; l < L; l += nt) s.level_count[(side ? lf : lk) * L + l] = 0;
     }
     __syncthreads();
-    // 7. Append the staged entries to the empty keep ladder.
+    // 7. Append the staged entries to the empty keep ladder (an update tape keeps this rebuild's
+    // Beta cuts in its own slot, merge j of lane (b, g)).
     const LaneCtx<T> x = make_ctx_at<T>(g, s, w, keep, grp, b);
-    cascade_walk<T, BETA, DC, kTileRows>(x, g, s, w);
+    Work wj = w;
+    if (g.tape != kTapeNone) {
+      wj.tape_cuts = ward_cuts;
+      wj.tape_cut_lane = (long long)(bg * K + j);
+    }
+    cascade_walk<T, BETA, DC, kTileRows>(x, g, s, wj);
     __syncthreads();
   }
 }

@@ -95,17 +95,40 @@ def test_unified_op_log_matches_reference(name):
         np.testing.assert_array_equal(cache.level_count.cpu().numpy(), ref[f"step{step}/level_count"])
 
 
-def test_unified_route_rejects_what_it_does_not_build():
+@pytest.mark.parametrize("name", ["bf16_unified_nobeta", "fp32_unified_passes2", "fp32_unified_sh"])
+def test_unified_update_tape_replays_without_routing(name):
+    """Record every flush of a unified stream on an update tape (Ward merges and their Beta cuts
+    included), reset the cache, and replay: no flush reroutes, and every buffer equals the recorded
+    run after every step, twice."""
+    from unittest.mock import patch
     from logkv_b200 import _SemanticReplayUpdates
-    cfg = unified_config("fp32_unified")
+    from test_update_tape_gpu import assert_state, state
+    cfg = unified_config(name)
     stream = make_stream(cfg)
     cache = make_unified_cache(cfg, stream)
+    tape = _SemanticReplayUpdates()
+    expected = []
     dt = torch_dtype(cfg)
-    with torch.no_grad(), cache._semantic_update_context(_SemanticReplayUpdates()), \
-            pytest.raises(NotImplementedError):
-        for chunk in stream["chunks"][:3]:
-            k = torch.from_numpy(chunk["k"]).to("cuda", dt)
-            cache.add_recent(k, k, k_raw=k, span_ends=chunk["span_ends"].tolist(), record_op_log=True)
+
+    def push(chunk, **kw):
+        k = torch.from_numpy(chunk["k"]).to("cuda", dt)
+        kr = torch.from_numpy(chunk["k_raw"]).to("cuda", dt)
+        v = torch.from_numpy(chunk["v"]).to("cuda", dt)
+        pos = torch.from_numpy(chunk["pos"]).cuda() if chunk.get("pos") is not None else None
+        cache.add_recent(k, v, k_raw=kr, input_pos=pos, span_ends=chunk["span_ends"].tolist(), **kw)
+
+    with torch.no_grad(), cache._semantic_update_context(tape):
+        for chunk in stream["chunks"]:
+            push(chunk, record_op_log=True)
+            expected.append(state(cache))
+    for _ in range(2):
+        cache.reset_parameters()
+        with patch.object(cache, "flush_device", side_effect=AssertionError("rerouted")):
+            for chunk, want in zip(stream["chunks"], expected):
+                with torch.no_grad(), cache._semantic_update_context(tape, replay=True):
+                    push(chunk)
+                assert cache.read_status() == 0
+                assert_state(cache, want)
 
 
 def test_unified_ward_ties_are_logged():
