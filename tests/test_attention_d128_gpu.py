@@ -41,7 +41,7 @@ def make_state(seed=0, B=1, G=2, D=128, K=4, levels=3, recent=512, R=300, P=64, 
     cache.level_sum_wp[lv] = w.long() * m
     cache.level_count[:, :, :, :levels] = Bs
     cache.level_count[0, 0, 1, 2] = Bs // 3          # ragged lanes
-    cache.level_w[0, 1, 0, 0, 5] = 0.0               # an occupied slot with zero weight (invalid)
+    cache.level_w[0, min(1, G - 1), 0, 0, 5] = 0.0   # an occupied slot with zero weight (invalid)
     cache.alpha_k_raw.normal_(generator=gen)
     cache.alpha_v.normal_(generator=gen)
     cache.alpha_pos.copy_(torch.randint(0, max_seq, cache.alpha_pos.shape, generator=gen, device="cuda"))
@@ -87,12 +87,12 @@ def test_d128_attention_matches_oracle(T):
         assert int(ws[:4].view(torch.int32).item()) == 0
 
 
-@pytest.mark.parametrize("G", [8, 4, 2])
+@pytest.mark.parametrize("G", [8, 4, 2, 1])
 def test_two_tile_chunk_kernel_matches_fp32_reference(G):
     """A 2048-token chunk (the two-tile tcgen05 kernel) against a PyTorch float32 softmax over
     the same packed K/V (the oracle's packer): 8 groups (128 query-tile pairs, one CTA each), and
-    4 or 2 groups (a KV-head-sharded rank's share: the key range is split over 2 or 4 CTAs per
-    pair and the splits combined)."""
+    4, 2 or 1 groups (a KV-head-sharded rank's share at 2, 4 or 8 ranks: the key range is split
+    over several CTAs per pair and the splits combined)."""
     from logkv_b200 import log_kv_chunk_attention
     H, T, D = 2 * G, 2048, 128
     cache, cos, sin = make_state(seed=7, G=G, recent=512, R=300, max_seq=8192)
