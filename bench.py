@@ -23,6 +23,11 @@ roofline  = the ladder cascade kernel (the dominant flush stage): algorithmic
             bytes of its rows (549 B per bf16 row: K and V 256 B each, w 4 B,
             p_lo/p_hi/sum_wp/order 8 B each, pad 1 B) over its CUDA-event time,
             against the measured HBM copy bandwidth.
+Other legs on the same line: decode (configs[3], with and without committing
+generated tokens), prefill chunk attention, flush-and-attend, kv_sharded
+(configs[2]), unified (configs[4]: unified-route flushes of 32 streams x 8 groups
+per rank), and the reference's own CPU timings of configs[0] and of the unified
+flush, recorded in the build container (tests/golden/*_timing.json).
 --impl reference times the CPU oracle port (a numpy restatement of the
 reference's flush) on every host core: one worker process per layer, --warmup
 untimed and --steps timed steps, a step being one flush in every worker.
