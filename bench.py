@@ -514,7 +514,7 @@ def bench_unified(args, rank, world, local_rank):
     from logkv_b200._lib import FLUSH_STAGES
     from logkv_b200.cache import LogStructuredKVCache
     from logkv_b200.workload import rope_tables
-    cfg = UNIFIED
+    cfg = UNIFIED | {"streams_per_rank": args.unified_streams}
     S, G, D, T = cfg["streams_per_rank"], cfg["groups"], cfg["head_dim"], cfg["granularity"]
     device = torch.device("cuda", local_rank)
     cos, sin = rope_tables(cfg["max_seq"] + 64, D)
@@ -586,7 +586,7 @@ def bench_unified(args, rank, world, local_rank):
     dist_bytes = lanes * 4 * 2 * (rows_c ** 2 + rows_g ** 2)   # each matrix written once, read once by the first scan
     peak, kind = measured_peaks()
     ref = unified_reference_timing()
-    out = {"metric": "unified-route flush ms per 2048-token chunk of this rank's streams (32 streams x 8 groups)",
+    out = {"metric": f"unified-route flush ms per 2048-token chunk of this rank's streams ({S} streams x {G} groups)",
            "unit": "ms", "value": round(ms, 3), "higher_is_better": False, "scaling": "weak",
            "tokens_per_s": round(S * world * T / (ms * 1e-3), 1),
            "us_per_lane_flush": round(ms * 1000.0 / lanes, 2), "status": status,
@@ -1136,6 +1136,8 @@ def main():
     ap.add_argument("--streams", type=int, default=28, help="streams the layers' flushes are spread over")
     ap.add_argument("--flush-attend", type=int, default=1, help="run the flush-and-attend prefill leg (0: skip)")
     ap.add_argument("--unified", type=int, default=1, help="run the unified-route leg (0: skip)")
+    ap.add_argument("--unified-streams", type=int, default=UNIFIED["streams_per_rank"],
+                    help="streams per rank of the unified-route leg (profiling runs only)")
     ap.add_argument("--kv-layers", type=int, default=28,
                     help="layers of the KV-head-sharded leg (BASELINE configs[2]; 0 skips it)")
     args = ap.parse_args()
