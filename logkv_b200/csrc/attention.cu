@@ -1326,7 +1326,7 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
   using RL = TcRoles<NQ>;
   constexpr int CPR = D / 8, TS = kTcTS, ST = RL::STAGES;
   extern __shared__ uint4 smem4[];
-  __shared__ uint64_t q_full, kv_full[ST], kv_empty[ST], s_full[NQ], s_free[NQ], p_full[NQ][2], pv_done[NQ][2];
+  __shared__ uint64_t q_full, kv_full[ST], kv_empty[ST], s_full[NQ][2], p_full[NQ][2], pv_done[NQ][2];
   __shared__ uint32_t sh_tmem;
   __shared__ int sh_abort;
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -1376,9 +1376,8 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
       tc::mbar_init(&kv_empty[i], NQ);   // one release per query tile's issuer
     }
     for (int t = 0; t < NQ; ++t) {
-      tc::mbar_init(&s_full[t], 1);
-      tc::mbar_init(&s_free[t], kTcRows);
       for (int i = 0; i < 2; ++i) {
+        tc::mbar_init(&s_full[t][i], 1);
         tc::mbar_init(&p_full[t][i], kTcRows);
         tc::mbar_init(&pv_done[t][i], 1);
       }
@@ -1394,8 +1393,10 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = sh_tmem;
-  auto t_s = [&](int t) { return tmem + 64u * t; };
-  auto t_p = [&](int t, int buf) { return tmem + 64u * NQ + 64u * t + 32u * buf; };
+  // Per query tile: two 64-column S buffers (unit r's scores in buffer r & 1, then its P as bf16
+  // pairs over the buffer's first 32 columns) and O.  QK^T of unit r + 1 overlaps the softmax's
+  // read of unit r's scores.
+  auto t_s = [&](int t, int buf) { return tmem + 128u * t + 64u * buf; };
   auto t_o = [&](int t) { return tmem + 128u * NQ + (uint32_t)(t * D); };
   auto unit_info = [&](int u, const __nv_bfloat16*& kb, const __nv_bfloat16*& vb, const float*& mb, int& rows,
                        int& cls, int& first) {
@@ -1509,8 +1510,9 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
           if (u < Uq) {
             tc::fence_proxy_async();
             tc::fence_after();
-            // S(t) is free once the softmax has loaded S(t, u-1) into registers.
-            if (r >= 1 && !tc::mbar_wait(&s_free[t], (r - 1) & 1, kTcWaitBudget)) {
+            // S buffer r & 1 is free once PV of unit r - 2 has read its P (the softmax loaded
+            // that unit's scores before writing the P).
+            if (r >= 2 && !tc::mbar_wait(&pv_done[t][r & 1], ((r - 2) >> 1) & 1, kTcWaitBudget)) {
               ok = false;
               break;
             }
@@ -1520,9 +1522,9 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
             for (int ks = 0; ks < D / 16; ++ks) {
               const uint64_t da = tc::sw128_desc(qa + (ks >> 2) * (kTcRows * 128) + (ks & 3) * 32, 16, 1024);
               const uint64_t db = tc::sw128_desc(kbs + (ks >> 2) * (TS * 128) + (ks & 3) * 32, 16, 1024);
-              tc::umma_f16(t_s(t), da, db, idesc_s, ks > 0 ? 1u : 0u);
+              tc::umma_f16(t_s(t, r & 1), da, db, idesc_s, ks > 0 ? 1u : 0u);
             }
-            tc::umma_commit(&s_full[t]);
+            tc::umma_commit(&s_full[t][r & 1]);
           }
         }
         if (r >= 1) {
@@ -1535,7 +1537,7 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
 #pragma unroll
             for (int ks = 0; ks < TS / 16; ++ks) {
               const uint64_t db = tc::sw128_desc(vbs + ks * 16 * 128, TS * 128, 1024);
-              tc::umma_f16_ts(t_o(t), t_p(t, bp) + ks * 8, db, idesc_o, (rv_ > 0 || ks > 0) ? 1u : 0u);
+              tc::umma_f16_ts(t_o(t), t_s(t, bp) + ks * 8, db, idesc_o, (rv_ > 0 || ks > 0) ? 1u : 0u);
             }
             tc::umma_commit(&pv_done[t][bp]);
             tc::umma_commit(&kv_empty[vs]);
@@ -1558,7 +1560,7 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
     for (int u = ub; u < Uq; ++u) {
       const int r = u - ub, st = r & 1, ks_ = r % ST;
       ok = __all_sync(0xffffffffu, tc::mbar_wait(&kv_full[ks_], (r / ST) & 1, kTcWaitBudget) &&
-                                       tc::mbar_wait(&s_full[qt], r & 1, kTcWaitBudget));
+                                       tc::mbar_wait(&s_full[qt][st], (r >> 1) & 1, kTcWaitBudget));
       if (!ok) break;
       tc::fence_after();
       const __nv_bfloat16 *kb_, *vb_;
@@ -1569,12 +1571,10 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
       float sv[TS];
       {
         uint32_t r64[64];
-        tc::tmem_ld64(t_s(qt) + lane_off, r64);
+        tc::tmem_ld64(t_s(qt, st) + lane_off, r64);
 #pragma unroll
         for (int j = 0; j < TS; ++j) sv[j] = __uint_as_float(r64[j]);
       }
-      tc::fence_before();
-      tc::mbar_arrive(&s_free[qt]);   // S(qt) may now take the next tile's scores
       float mt = -INFINITY;
       const bool full = rows == TS && (cls != 2 || !a.causal || first + TS - 1 <= row_t);
       if (full) {
@@ -1615,11 +1615,6 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
       tc::f2unpack(ps2, ps0, ps1);
       const float ps = ps0 + ps1;
       l = l * alpha + ps;
-      if (r >= 2) {
-        // P buffer st still feeds PV(u-2) until that product completes.
-        ok = __all_sync(0xffffffffu, tc::mbar_wait(&pv_done[qt][st], ((r - 2) >> 1) & 1, kTcWaitBudget));
-        if (!ok) break;
-      }
       if (r > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
         // O must hold PV(u-1) before it is rescaled.
         ok = __all_sync(0xffffffffu,
@@ -1635,7 +1630,7 @@ __global__ void __launch_bounds__(TcRoles<NQ>::WARPS * 32, 1)
           tc::tmem_st32(t_o(qt) + lane_off + c0, r32);
         }
       }
-      tc::tmem_st32(t_p(qt, st) + lane_off, pk);
+      tc::tmem_st32(t_s(qt, st) + lane_off, pk);   // P over this unit's own (loaded) scores
       tc::fence_before();
       tc::mbar_arrive(&p_full[qt][st]);
     }
