@@ -58,7 +58,7 @@ ROW_BYTES = 256 + 256 + 4 + 4 * 8 + 1   # one bf16 ladder entry (13 fields, firs
 # launch, so the figure is below the algorithmic bytes.
 CASCADE_TRAFFIC = 15_832_832 + 0 + 20_753_408 + 2_816
 # The same for one chunk attention launch (chunk_attn_tc_kernel, the prefill leg's shape).
-PREFILL_TRAFFIC = 51_043_584 + 1_107_456
+PREFILL_TRAFFIC = 51_042_816 + 705_536
 FLUSH_KERNELS = 12                      # kernel launches per flushing layer-chunk (the last writes the chunk)
 METRIC = "flush us per 2048-tok chunk/layer"
 
