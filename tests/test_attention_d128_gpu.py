@@ -128,3 +128,44 @@ def test_two_tile_chunk_kernel_matches_fp32_reference(G):
         ref = torch.softmax(sc, dim=-1) @ vt[0, hh // rf]
         worst = max(worst, (out[0, hh].float() - ref).abs().max().item())
     assert worst <= TOL, worst
+
+
+@pytest.mark.parametrize("G", [8, 2])
+def test_chunk_kernel_running_max_rescales(G):
+    """Keys of the new chunk grow with their position (x (1 + t / 256)), so the running maximum of
+    every query row rises unit after unit and the softmax rescales O many times while the next
+    units' scores are already in flight; 8 groups (one CTA per query-tile pair) and 2 (the key
+    range split over CTAs), against a PyTorch float32 softmax over the same packed K/V."""
+    from logkv_b200 import log_kv_chunk_attention
+    H, T, D = 2 * G, 2048, 128
+    cache, cos, sin = make_state(seed=11, G=G, recent=512, R=300, max_seq=8192)
+    gen = torch.Generator(device="cuda").manual_seed(78)
+    q = torch.randn(1, H, T, D, generator=gen, device="cuda").bfloat16()
+    grow = (1.0 + torch.arange(T, device="cuda", dtype=torch.float32) / 256.0)[None, None, :, None]
+    k = (torch.randn(1, G, T, D, generator=gen, device="cuda") * grow).bfloat16()
+    v = torch.randn(1, G, T, D, generator=gen, device="cuda").bfloat16()
+    scale = D ** -0.5
+    with torch.no_grad():
+        out = log_kv_chunk_attention(cache, q, k, v, scale, 0.0)
+    torch.cuda.synchronize()
+    assert int(cache._read.status.item()) == 0
+    assert int(cache._read.workspaces[(H, T)][:4].view(torch.int32).item()) == 0
+    h = lambda t: t.detach().float().cpu().numpy() if t.dtype == torch.bfloat16 else t.detach().cpu().numpy()  # noqa
+    plan = A.mid_plan(h(cache.level_count), h(cache.level_w), h(cache.level_sum_wp))
+    ka, va = A.pack_mid(h(cache.level_k), h(cache.level_v), h(cache.level_w), plan, h(cache.alpha_k_raw),
+                        h(cache.alpha_v), h(cache.alpha_pos), h(cache.alpha_valid), cache.alpha_count,
+                        h(cache.recent_k), h(cache.recent_v), cache.recent_count, h(k), h(v), cos, sin, D,
+                        ((D + 8) // 8) * 8, "bf16", "fp32")
+    kt = torch.from_numpy(np.asarray(ka, np.float32)).cuda()
+    vt = torch.from_numpy(np.asarray(va, np.float32))[..., :D].cuda()
+    qa = torch.zeros(1, H, T, kt.shape[-1], device="cuda")
+    qa[..., :D] = q.float()
+    qa[..., D] = float(A.query_extra(scale, "bf16"))
+    S = kt.shape[2]
+    blocked = torch.arange(S, device="cuda")[None, :] > (S - T) + torch.arange(T, device="cuda")[:, None]
+    worst = 0.0
+    for hh in range(H):
+        sc = scale * (qa[0, hh] @ kt[0, hh // 2].T)
+        ref = torch.softmax(sc.masked_fill(blocked, float("-inf")), dim=-1) @ vt[0, hh // 2]
+        worst = max(worst, (out[0, hh].float() - ref).abs().max().item())
+    assert worst <= TOL, worst
